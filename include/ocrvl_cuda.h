@@ -1,0 +1,174 @@
+/*
+ * ocrvl_cuda.h -- C ABI of the B200 (sm_100a) decode path for the ERNIE text
+ * decoder of RapidAI/RapidOCRvl (Go module paddleocrvl-go).
+ *
+ * The ABI is what a cgo shim behind the reference's backend interface binds:
+ * plain pointers and sizes, no CUDA or torch types.  Each entry point names
+ * the reference interface it replaces (paths relative to the reference root).
+ *
+ * Conventions
+ *   - Every function returns OCRVL_OK (0) or a negative OCRVL_E_* code;
+ *     ocrvl_last_error() then describes the failure (thread-local string).
+ *   - Host pointers are only read or written during the call; nothing is
+ *     retained (cgo pointer rules).
+ *   - A model handle may be used from several threads; calls on it are
+ *     serialised internally.  There is no CPU fallback: every compute entry
+ *     point fails when the GPU path cannot run.
+ *   - Tensor types: 0 = F32, 1000 = Q8_ROW, 1001 = Q4_ROW, 1002 = Q6_ROW
+ *     (internal/gguf/gguf.go:19-22).  Quantized tensors are passed exactly
+ *     as stored in the repo's GGUF files: rows f32 scales, then rows packed
+ *     rows (internal/gguf/gguf.go:435-569).
+ */
+#ifndef OCRVL_CUDA_H
+#define OCRVL_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define OCRVL_OK 0
+#define OCRVL_E_INVALID (-1)  /* bad argument, shape or state */
+#define OCRVL_E_CUDA (-2)     /* CUDA runtime error or no device */
+#define OCRVL_E_NOMEM (-3)    /* device memory or KV pages exhausted */
+#define OCRVL_E_TIMEOUT (-4)  /* a bounded device-side wait gave up */
+
+#define OCRVL_F32 0
+#define OCRVL_Q8_ROW 1000
+#define OCRVL_Q4_ROW 1001
+#define OCRVL_Q6_ROW 1002
+
+typedef struct ocrvl_model ocrvl_model;
+typedef struct ocrvl_seq ocrvl_seq;
+
+/* Decoder shape, mirroring internal/config/config.go:31-49 after Load's
+ * defaults.  kv_pool_bytes: device memory for paged f32 KV (0 = 4 GiB).
+ * max_position: largest RoPE position + 1 (0 = 32768). */
+typedef struct ocrvl_model_desc {
+  int32_t vocab_size;
+  int32_t hidden_size;
+  int32_t intermediate_size;
+  int32_t num_layers;
+  int32_t num_heads;
+  int32_t num_kv_heads;
+  int32_t head_dim;
+  float rms_norm_eps;
+  double rope_theta;
+  int32_t mrope_section[3];
+  int32_t max_position;
+  int64_t kv_pool_bytes;
+} ocrvl_model_desc;
+
+/* Last error message of the calling thread ("" if none). */
+const char *ocrvl_last_error(void);
+
+/* Number of visible CUDA devices (internal/backend/backend.go:85-111 gains a
+ * "cuda" choice; this is its probe).  Returns >= 0 or OCRVL_E_CUDA. */
+int ocrvl_device_count(void);
+
+/* Creates an empty model on `device`.  Replaces the Runtime construction in
+ * model.LoadWithOptions (internal/model/model.go:546-605). */
+int ocrvl_init(int device, const ocrvl_model_desc *desc, ocrvl_model **out);
+
+/* Uploads one tensor.  Replaces preloadTextWeights' per-tensor load
+ * (internal/model/model.go:2861-2945): `scales` is NULL for F32, `data` the
+ * packed rows (or f32 values).  Names other than the decoder's are ignored. */
+int ocrvl_load_tensor(ocrvl_model *m, const char *name, int type, int64_t rows, int64_t cols,
+                      const float *scales, const void *data);
+
+/* Loads every decoder tensor of a GGUF file (gguf.Open + Q*Row / Float32,
+ * internal/gguf/gguf.go:111-569) through ocrvl_load_tensor. */
+int ocrvl_load_gguf(ocrvl_model *m, const char *path);
+
+/* Checks that all decoder tensors are present and prepares the device state
+ * (row sums, RoPE tables, work buffers).  Required before any step. */
+int ocrvl_finalize(ocrvl_model *m);
+
+/* Quantization type of the loaded linear weights (OCRVL_Q*_ROW) or < 0. */
+int ocrvl_quant_type(const ocrvl_model *m);
+
+/* Step trace (no reference counterpart; the reference only has load-phase
+ * timings, internal/model/model.go:503-509).  With OCRVL_TRACE set at
+ * ocrvl_finalize, the step kernel records per phase [start, prologue end,
+ * end (max over blocks), barrier exit] as %globaltimer ns; this copies up to
+ * cap values of the last step and clears them.  Returns the count (0 when
+ * tracing is off). */
+int ocrvl_trace_read(ocrvl_model *m, uint64_t *out, int cap);
+
+void ocrvl_free(ocrvl_model *m);
+
+/* A decode sequence owning paged KV for up to max_tokens positions.
+ * Replaces getKVCaches/putKVCaches (internal/model/model.go:3286-3344). */
+int ocrvl_seq_create(ocrvl_model *m, int max_tokens, ocrvl_seq **out);
+int ocrvl_seq_reset(ocrvl_seq *s);
+void ocrvl_seq_free(ocrvl_seq *s);
+int ocrvl_seq_len(const ocrvl_seq *s);
+
+/* Copies layer `layer`'s cached K and V ([len][kv_heads*head_dim] f32 each,
+ * the contiguous kvCache layout of model.go:373-379) to host memory,
+ * gathering through the sequence's block table. */
+int ocrvl_seq_read_kv(ocrvl_seq *s, int layer, float *k, float *v);
+
+/* One decode step for n sequences (1 <= n <= 8) of the same model: the
+ * batched form of Runtime.forwardEmbeddingForSampling
+ * (internal/model/model.go:3475-3643).
+ *   ids       n token ids (embedding rows), or NULL when embeds is given
+ *   embeds    n*hidden_size f32 input embeddings, or NULL
+ *   pos_thw   n*3 M-RoPE positions, or NULL for (len, len, len)
+ *   need_logits  0: prompt token (K/V only in the last layer), 1: full step
+ *   out_ids   n greedy ids (lm_head argmax, ties -> lowest id), may be NULL
+ *   out_logits  n*vocab_size f32 logits, may be NULL                      */
+int ocrvl_step(ocrvl_model *m, ocrvl_seq *const *seqs, int n, const int32_t *ids, const float *embeds,
+               const int32_t *pos_thw, int need_logits, int32_t *out_ids, float *out_logits);
+
+/* Greedy generation (Runtime.GenerateWithOptions with temperature 0,
+ * internal/model/model.go:1492-1572): prompt tokens one at a time, then up to
+ * max_new tokens, stopping after an EOS id (eos NULL -> {2}).  out receives
+ * prompt + generated ids; *n_out their count. */
+int ocrvl_generate_greedy(ocrvl_model *m, const int32_t *ids, int n_ids, int max_new, const int32_t *eos,
+                          int n_eos, int32_t *out, int out_cap, int *n_out);
+
+/* ---- op level: device pointers, optional cudaStream_t as void* --------
+ * Kernel-level entry points for parity tests and for callers that hold
+ * their own device buffers; each names the internal/tensor function whose
+ * result it reproduces.  Quantized matrices: w = packed rows (rows x
+ * packed_row_bytes), scale = rows f32, rowsum = rows int32 from
+ * ocrvl_op_rowsum.  m = number of input vectors (1..8). */
+
+/* Per-row sum of the unpacked int8 weights (UnpackQ4Matrix / UnpackQ6Matrix
+ * RowSum, internal/tensor/quant.go:2325-2368, 2605-2656). */
+int ocrvl_op_rowsum(int type, int rows, int cols, const void *w, int32_t *rowsum, void *stream);
+
+/* out[m][rows] = W x[m]  (tensor.MatVecQ8/Q4/Q6, quant.go:443-561).
+ * norm_w != NULL first applies RMSNorm(x, norm_w, eps) (ops.go:1015-1037). */
+int ocrvl_op_matvec(int type, int rows, int cols, const void *w, const float *scale,
+                    const int32_t *rowsum, int m, const float *x, const float *norm_w, float eps,
+                    float *out, void *stream);
+
+/* v = residual + W x; residual = v when in_place; norm_out = RMSNorm of v with
+ * the fused sum-of-squares order (tensor.MatVec*AddRMSNorm[OutOnly],
+ * internal/tensor/fused_matvec2.go). */
+int ocrvl_op_matvec_add_rmsnorm(int type, int rows, int cols, const void *w, const float *scale,
+                                const int32_t *rowsum, int m, const float *x, float *residual,
+                                int in_place, const float *norm_w, float eps, float *v_out,
+                                float *norm_out, void *stream);
+
+/* out = silu(Wg x) * (Wu x)  (tensor.SwiGLUGateUp*Scratch, quant.go:757-1000). */
+int ocrvl_op_swiglu(int type, int rows, int cols, const void *wg, const float *sg, const int32_t *rsg,
+                    const void *wu, const float *su, const int32_t *rsu, int m, const float *x,
+                    float *out, void *stream);
+
+/* ids[m] = argmax_r (W x[m])_r, first maximum (tensor.MatVecArgmaxQ*,
+ * internal/tensor/argmax_quant.go). */
+int ocrvl_op_argmax(int type, int rows, int cols, const void *w, const float *scale,
+                    const int32_t *rowsum, int m, const float *x, int32_t *ids, void *stream);
+
+/* out = RMSNorm(x, w, eps) for m vectors of n (tensor.RMSNorm). */
+int ocrvl_op_rmsnorm(int n, int m, const float *x, const float *w, float eps, float *out, void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* OCRVL_CUDA_H */

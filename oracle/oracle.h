@@ -1,0 +1,104 @@
+/*
+ * CPU oracle for the ERNIE text-decoder decode step of RapidAI/RapidOCRvl.
+ *
+ * TEST INFRASTRUCTURE ONLY.  This library is a C++ restatement of the
+ * reference's Go CPU path (internal/model/model.go + internal/tensor +
+ * internal/gguf).  Only tests/, __graft_entry__.smoke() and bench.py's CPU
+ * baseline leg may load it, and only as the checker / CPU baseline.  The CUDA
+ * product path never calls into it.
+ *
+ * Numerics follow the reference as compiled for amd64 with AVX-512 VNNI
+ * (int8-activation dots for Q4/Q6, fp32 FMA dots for Q8 loaded from GGUF),
+ * with one canonical float summation order per operation; each function in
+ * oracle.cpp cites the reference file:line it restates.
+ */
+#ifndef OCRVL_ORACLE_H
+#define OCRVL_ORACLE_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct orc_config {
+  int vocab_size;
+  int hidden_size;
+  int intermediate_size;
+  int num_layers;
+  int num_heads;
+  int num_kv_heads;
+  int head_dim;
+  float rms_norm_eps;
+  double rope_theta;
+  int mrope_section[3];
+} orc_config;
+
+/* Tensor types as stored in the repo's GGUF files (internal/gguf/gguf.go:19-22). */
+enum { ORC_F32 = 0, ORC_Q8 = 1000, ORC_Q4 = 1001, ORC_Q6 = 1002 };
+
+/* ---- model / sequence --------------------------------------------------- */
+void *orc_load(const char *gguf_path, const orc_config *cfg, char *err, int errlen);
+void orc_free(void *model);
+int orc_quant_type(void *model);
+void *orc_seq_new(void *model, int max_tokens);
+void orc_seq_free(void *seq);
+int orc_seq_len(void *seq);
+/* Copies layer `layer`'s K and V caches ([len][kv_heads*head_dim] f32). */
+int orc_seq_kv(void *seq, int layer, float *k, float *v);
+
+/* One decode step (Runtime.forwardEmbeddingForSampling, model.go:3475-3643).
+ * emb: hidden_size f32.  pos: (T,H,W).  If need_logits, writes the argmax id to
+ * *token (ties -> lowest id) and, if logits != NULL, the full logits.
+ * final_norm (nullable) receives the lm_head input vector. */
+int orc_forward(void *model, void *seq, const float *emb, int pT, int pH, int pW,
+                int need_logits, int *token, float *logits, float *final_norm);
+
+/* Greedy generation (Runtime.GenerateWithOptions, model.go:1492-1572) with
+ * temperature 0.  out receives prompt + generated ids; returns count or <0. */
+int orc_generate(void *model, const int *ids, int n_ids, int max_new,
+                 const int *eos, int n_eos, int *out, int out_cap);
+
+/* Decode-only timing helper for the CPU baseline: runs `steps` greedy decode
+ * steps on `seq` starting from token `tok` at position `pos`; returns the
+ * last token. */
+int orc_decode_steps(void *model, void *seq, int tok, int pos, int steps);
+
+/* Embedding row gather (tokenEmbeddingInto, model.go:3251-3258). */
+int orc_embed(void *model, int id, float *out);
+
+/* ---- op level ----------------------------------------------------------- */
+/* Row quantizers used by the GGUF converter (quant.go:96-137, 201-384). */
+float orc_quantize_row(int type, const float *w, int cols, uint8_t *packed);
+/* Unpack one packed row to int8 (quant.go:2325-2368, 2605-2656). */
+void orc_unpack_row(int type, const uint8_t *packed, int cols, int8_t *out);
+/* quantizeXForVNNI (quant.go:2087-2115, dot_vnni_amd64.s:434-500). */
+float orc_quantize_x(const float *x, int n, uint8_t *xq);
+/* matVecMaybeQuant semantics per type: Q4/Q6 via int8 activations, Q8 via
+ * fp32 FMA dots.  data = packed rows as stored in GGUF. */
+void orc_matvec(int type, int rows, int cols, const float *scales, const void *data,
+                const float *x, float *out);
+/* Fused matvec + residual + RMSNorm (fused_matvec2.go).  in_place=1 updates
+ * residual (MatVec*AddRMSNorm), 0 leaves it (…OutOnly). */
+void orc_matvec_add_rmsnorm(int type, int rows, int cols, const float *scales,
+                            const void *data, const float *x, float *residual,
+                            const float *norm_w, float eps, int in_place, float *norm_out);
+/* SwiGLU gate/up (quant.go:757-1000 + ops.go:1125-1138). */
+void orc_swiglu(int type, int rows, int cols, const float *gs, const void *gd,
+                const float *us, const void *ud, const float *x, float *out);
+void orc_rmsnorm(const float *x, const float *w, int n, float eps, float *out);
+float orc_fast_rsqrt(float x);
+float orc_fast_exp(float x);
+void orc_rope(float *x, int heads, int dim, const float *cos_t, const float *sin_t);
+void orc_rope_table(const orc_config *cfg, int pT, int pH, int pW, float *cos_t, float *sin_t);
+void orc_softmax(float *x, int n);
+/* Decode attention over a contiguous cache ([n][kv_heads*dim]) for all heads. */
+void orc_attention(const float *q, const float *kc, const float *vc, int n, int heads,
+                   int kv_heads, int dim, float *head_out);
+int orc_argmax_matvec(int type, int rows, int cols, const float *scales, const void *data,
+                      const float *x, float *best_score);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

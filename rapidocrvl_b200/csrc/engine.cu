@@ -1,0 +1,1159 @@
+// Host engine and C ABI (include/ocrvl_cuda.h) of the B200 decode path.
+//
+// A decode step runs as ONE persistent cooperative kernel (k_step): every
+// block walks the phases of decoder.cuh for all layers, separated by a grid
+// barrier whose waits are bounded (a timed-out wait sets an error word and
+// every block returns).  OCRVL_STEP_MODE=phases runs the same phases as
+// separate launches instead (used to cross-check the barrier path).
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <atomic>
+#include <cmath>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "../../include/ocrvl_cuda.h"
+#include "decoder.cuh"
+
+using namespace ocrvl;
+
+namespace {
+
+thread_local std::string g_err;
+
+int fail(int code, const std::string &msg) {
+  g_err = msg;
+  return code;
+}
+
+#define CK(call)                                                                         \
+  do {                                                                                   \
+    cudaError_t e_ = (call);                                                             \
+    if (e_ != cudaSuccess) return fail(OCRVL_E_CUDA, std::string(#call) + ": " + cudaGetErrorString(e_)); \
+  } while (0)
+
+int packed_row_bytes(int type, int cols) {
+  switch (type) {
+    case OCRVL_Q8_ROW: return cols;
+    case OCRVL_Q4_ROW: return (cols + 1) / 2;
+    case OCRVL_Q6_ROW: return (cols * 6 + 7) / 8;
+  }
+  return -1;
+}
+
+}  // namespace
+
+// ---------------------------------------------------------------------------
+// Kernels
+// ---------------------------------------------------------------------------
+namespace ocrvl {
+
+__device__ __forceinline__ unsigned ld_acquire(const unsigned *p) {
+  unsigned v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Grid barrier for the cooperative step kernel: one arrival counter
+// (atom.acq_rel) and a generation word (red.release / ld.acquire).  Waits are
+// bounded: after kBarrierSpins polls the waiting block records an error and
+// leaves; waiting blocks also leave once any block has recorded one.
+// Returns false on error.
+constexpr unsigned long long kBarrierSpins = 1ull << 22;
+__device__ __forceinline__ unsigned atom_add_acqrel(unsigned *p, unsigned v) {
+  unsigned old;
+  asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+  return old;
+}
+__device__ __forceinline__ void red_add_release(unsigned *p, unsigned v) {
+  asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ void st_relaxed(unsigned *p, unsigned v) {
+  asm volatile("st.relaxed.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ bool grid_sync(const Ctx &c) {
+  __shared__ int ok;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    ok = 1;
+    unsigned gen = ld_acquire(c.bar_gen);
+    unsigned arrived = atom_add_acqrel(c.bar_count, 1u);
+    if (arrived == gridDim.x - 1) {
+      st_relaxed(c.bar_count, 0u);
+      red_add_release(c.bar_gen, 1u);
+    } else {
+      unsigned long long spins = 0;
+      while (ld_acquire(c.bar_gen) == gen) {
+        ++spins;
+        if (spins > kBarrierSpins || ((spins & 1023) == 0 && *(volatile int *)c.err)) {
+          atomicExch(c.err, 1);
+          ok = 0;
+          break;
+        }
+      }
+    }
+  }
+  __syncthreads();
+  return ok != 0;
+}
+
+__device__ GemvArgs gemv_args(const DMat &A, int rb, int re, const float *src, int ld, int mode,
+                              const float *nw, int epi, float *out, int ldo) {
+  GemvArgs a;
+  memset(&a, 0, sizeof(a));
+  a.A = A;
+  a.row_begin = rb;
+  a.row_end = re;
+  a.src = src;
+  a.ld = ld;
+  a.mode = mode;
+  a.norm_w = nw;
+  a.epi = epi;
+  a.out = out;
+  a.ldo = ldo;
+  return a;
+}
+
+// L2 prefetch (cp.async.bulk.prefetch.L2) of this block's weight slabs of
+// layer l (same row split as the GEMV phases) and of this block's share of
+// the sequences' KV pages of layer l.  Issued by one thread, never waited on.
+__device__ void prefetch_layer(const Ctx &c, int l, int M) {
+  if (threadIdx.x != 0 || l < 0 || l >= c.L) return;
+  const LayerW &L = c.layers[l];
+  const int b = blockIdx.x, nb = gridDim.x;
+  prefetch_gemv_slab(L.qkv, 0, L.qkv.rows, b, nb);
+  prefetch_gemv_slab(L.o, 0, L.o.rows, b, nb);
+  prefetch_gemv_slab(L.gate, 0, L.gate.rows, b, nb);
+  prefetch_gemv_slab(L.up, 0, L.up.rows, b, nb);
+  prefetch_gemv_slab(L.down, 0, L.down.rows, b, nb);
+  const StepParams &sp = *c.sp;
+  const size_t layer_off = (size_t)l * 2 * c.KVH * kPageTokens * c.D;
+  const size_t layer_bytes = (size_t)2 * c.KVH * kPageTokens * c.D * 4;
+  int idx = 0;
+  for (int m = 0; m < M; m++) {
+    int np = (sp.len[m] + kPageTokens - 1) / kPageTokens;
+    for (int p = 0; p < np; p++, idx++)
+      if (idx % nb == b) prefetch_l2(c.kv_pool + (size_t)sp.bt[m][p] * c.page_floats + layer_off, layer_bytes);
+  }
+}
+
+// Phase bodies shared by the persistent kernel and the per-phase launches.
+__device__ void run_phase_body(const Ctx &c, int phase, int layer, int M, int any_logits, float *smem,
+                               unsigned long long *tslot);
+__device__ void run_phase(const Ctx &c, int phase, int layer, int M, int any_logits, float *smem, int tidx) {
+  unsigned long long *tslot = c.trace ? c.trace + 4 * tidx : nullptr;
+  if (tslot && blockIdx.x == 0 && threadIdx.x == 0) tslot[0] = gtimer();
+  run_phase_body(c, phase, layer, M, any_logits, smem, tslot);
+  if (tslot && threadIdx.x == 0) atomicMax(tslot + 2, gtimer());
+}
+
+__device__ void run_phase_body(const Ctx &c, int phase, int layer, int M, int any_logits, float *smem,
+                               unsigned long long *tslot) {
+  const LayerW &L = c.layers[layer];
+  const int qkvld = (c.QH + 2 * c.KVH) * c.D;
+  const bool last = layer == c.L - 1;
+  switch (phase) {
+    case 0: {  // QKV projection with the input RMSNorm as prologue
+      prefetch_layer(c, layer + 1, M);
+      if (last && any_logits && threadIdx.x == 0)
+        prefetch_gemv_slab(c.lm_head, 0, c.lm_head.rows, blockIdx.x, gridDim.x);
+      int rb = (last && !any_logits) ? c.QH * c.D : 0;
+      GemvArgs a = gemv_args(L.qkv, rb, L.qkv.rows, c.h, c.H, PRO_RMSNORM, L.ln1, EPI_STORE, c.qkv, qkvld);
+      a.tslot = tslot;
+      phase_gemv(c, a, M, smem);
+      break;
+    }
+    case 1:
+      phase_scores(c, layer, last && !any_logits, smem);
+      break;
+    case 2:
+      phase_pv(c, layer, smem);
+      break;
+    case 3: {  // o projection + residual
+      GemvArgs a = gemv_args(L.o, 0, L.o.rows, c.head, c.QH * c.D, PRO_PLAIN, nullptr, EPI_RESID, nullptr, c.H);
+      a.resid = c.h;
+      a.vout = c.vbuf;
+      a.resid_mode = RESID_ATTN;
+      a.tslot = tslot;
+      phase_gemv(c, a, M, smem);
+      break;
+    }
+    case 4: {  // gate/up with the post-attention AddRMSNorm as prologue
+      GemvArgs a = gemv_args(L.gate, 0, L.gate.rows, c.vbuf, c.H, PRO_ADDNORM, L.ln2, EPI_SWIGLU, c.g, c.I);
+      a.B = L.up;
+      a.tslot = tslot;
+      phase_gemv(c, a, M, smem);
+      break;
+    }
+    case 5: {  // down projection + residual (last layer: out-only)
+      GemvArgs a = gemv_args(L.down, 0, L.down.rows, c.g, c.I, PRO_PLAIN, nullptr, EPI_RESID, nullptr, c.H);
+      a.resid = c.h;
+      a.vout = c.vbuf;
+      a.resid_mode = last ? RESID_NEVER : RESID_ALWAYS;
+      a.tslot = tslot;
+      phase_gemv(c, a, M, smem);
+      break;
+    }
+    case 6: {  // lm_head argmax with the final AddRMSNorm as prologue
+      GemvArgs a = gemv_args(c.lm_head, 0, c.lm_head.rows, c.vbuf, c.H, PRO_ADDNORM, c.final_norm, EPI_ARGMAX,
+                             nullptr, c.V);
+      a.argkey = c.argkey;
+      a.logits = c.logits;
+      a.tslot = tslot;
+      phase_gemv(c, a, M, smem);
+      break;
+    }
+    case 7:
+      phase_argmax_finish(c);
+      break;
+  }
+}
+
+constexpr int kLayerPhases = 6;  // qkv, scores, pv, o, gate/up, down
+
+__device__ __forceinline__ bool traced_sync(const Ctx &c, int tidx) {
+  bool ok = grid_sync(c);
+  if (c.trace && blockIdx.x == 0 && threadIdx.x == 0) c.trace[4 * tidx + 3] = gtimer();
+  return ok;
+}
+
+__global__ void __launch_bounds__(kThreads) k_step(Ctx c, int M, int any_logits, int do_embed) {
+  extern __shared__ float4 smem4[];
+  float *smem = (float *)smem4;
+  prefetch_layer(c, 0, M);
+  if (do_embed) {
+    phase_embed(c);
+    if (!grid_sync(c)) return;
+  }
+  int t = 0;
+  for (int l = 0; l < c.L; l++) {
+    bool kv_only = l == c.L - 1 && !any_logits;
+    for (int ph = 0; ph < kLayerPhases; ph++, t++) {
+      run_phase(c, ph, l, M, any_logits, smem, t);
+      if (!traced_sync(c, t)) return;
+      if (kv_only && ph == 1) return;
+    }
+  }
+  if (any_logits) {
+    run_phase(c, kLayerPhases, c.L - 1, M, any_logits, smem, t);
+    if (!traced_sync(c, t)) return;
+    t++;
+    run_phase(c, kLayerPhases + 1, c.L - 1, M, any_logits, smem, t);
+  }
+}
+
+__global__ void __launch_bounds__(kThreads) k_phase(Ctx c, int phase, int layer, int M, int any_logits) {
+  extern __shared__ float4 smem4[];
+  c.trace = nullptr;
+  run_phase(c, phase, layer, M, any_logits, (float *)smem4, 0);
+}
+
+__global__ void __launch_bounds__(kThreads) k_embed(Ctx c) { phase_embed(c); }
+
+__global__ void __launch_bounds__(kThreads) k_gemv(Ctx c, GemvArgs a, int M) {
+  extern __shared__ float4 smem4[];
+  phase_gemv(c, a, M, (float *)smem4);
+}
+
+__global__ void __launch_bounds__(kThreads) k_addnorm_out(Ctx c, const float *v, int n, int M, const float *w,
+                                                          float *out) {
+  extern __shared__ float4 smem4[];
+  phase_addnorm_out(c, v, n, M, w, out, (float *)smem4);
+}
+
+__global__ void __launch_bounds__(kThreads) k_rmsnorm_out(Ctx c, const float *x, int n, int M, const float *w,
+                                                          float *out) {
+  extern __shared__ float4 smem4[];
+  phase_rmsnorm_out(c, x, n, M, w, out, (float *)smem4);
+}
+
+__global__ void k_argmax_ids(const unsigned long long *keys, int M, int *ids) {
+  int m = threadIdx.x;
+  if (m < M) ids[m] = argmax_key_row(keys[m]);
+}
+
+// Per-row sum of unpacked int8 weights; one warp per row.
+__global__ void k_rowsum(int type, const uint8_t *w, int rows, int cols, int pitch, int32_t *out) {
+  int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+  if (warp >= rows) return;
+  const uint8_t *r = w + (size_t)warp * pitch;
+  int s = 0;
+  for (int cidx = lane; cidx < cols; cidx += 32) {
+    int v;
+    if (type == QT_Q8) {
+      v = (int8_t)r[cidx];
+    } else if (type == QT_Q4) {
+      uint8_t b = r[cidx >> 1];
+      v = ((cidx & 1) ? (b >> 4) : (b & 0x0F)) - 8;
+    } else {
+      int bit = cidx * 6, idx = bit >> 3, sh = bit & 7;
+      uint32_t x = r[idx];
+      if (idx + 1 < pitch) x |= (uint32_t)r[idx + 1] << 8;
+      v = (int)((x >> sh) & 0x3F) - 32;
+    }
+    s += v;
+  }
+  for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+  if (lane == 0) out[warp] = s;
+}
+
+}  // namespace ocrvl
+
+// ---------------------------------------------------------------------------
+// Host state
+// ---------------------------------------------------------------------------
+struct ocrvl_model {
+  int device = 0;
+  ocrvl_model_desc desc{};
+  int qtype = 0;
+  bool finalized = false;
+  cudaStream_t stream = nullptr;
+  std::mutex mu;
+  std::vector<void *> allocs;
+  // weights
+  float *embed = nullptr, *final_norm = nullptr;
+  DMat lm_head{};
+  std::vector<LayerW> layers;
+  LayerW *layers_d = nullptr;
+  std::vector<uint32_t> have;  // bitmask of loaded tensors per layer (+ globals at index L)
+  // rope
+  float *rope_cos = nullptr, *rope_sin = nullptr;
+  int *sec_axis = nullptr;
+  // kv
+  float *kv_pool = nullptr;
+  long long page_floats = 0;
+  int num_pages = 0;
+  std::vector<int> free_pages;
+  // work
+  Ctx ctx{};
+  StepParams *sp_h = nullptr, *sp_d = nullptr;
+  int *out_h = nullptr;  // [kMaxBatch tokens][err]
+  int *bt_stage = nullptr;
+  int grid = 0;
+  size_t smem = 0;
+  bool persistent = true;
+  int sms = 0;
+
+  template <typename T>
+  T *dalloc(size_t n) {
+    void *p = nullptr;
+    if (cudaMalloc(&p, n * sizeof(T) + 16) != cudaSuccess) return nullptr;
+    allocs.push_back(p);
+    return (T *)p;
+  }
+};
+
+struct ocrvl_seq {
+  ocrvl_model *m = nullptr;
+  int max_tokens = 0, len = 0;
+  std::vector<int> pages;
+  int *bt_d = nullptr;
+};
+
+namespace {
+
+enum {
+  T_LN1 = 0, T_LN2, T_Q, T_K, T_V, T_O, T_GATE, T_UP, T_DOWN, T_NLAYER,
+  G_EMBED = 0, G_NORM, G_LM, G_N
+};
+
+int set_device(ocrvl_model *m) {
+  CK(cudaSetDevice(m->device));
+  return OCRVL_OK;
+}
+
+bool parse_layer(const std::string &name, int &layer, std::string &suffix) {
+  const std::string pre = "model.layers.";
+  if (name.compare(0, pre.size(), pre) != 0) return false;
+  size_t dot = name.find('.', pre.size());
+  if (dot == std::string::npos) return false;
+  std::string num = name.substr(pre.size(), dot - pre.size());
+  if (num.empty() || num.size() > 6) return false;
+  for (char ch : num)
+    if (ch < '0' || ch > '9') return false;
+  layer = std::atoi(num.c_str());
+  suffix = name.substr(dot + 1);
+  return true;
+}
+
+int upload_matrix(ocrvl_model *m, DMat &dst, int type, int64_t rows, int64_t cols, const float *scales,
+                  const void *data, int row_offset, int total_rows) {
+  int pb = packed_row_bytes(type, (int)cols);
+  if (!dst.w) {
+    uint8_t *w = m->dalloc<uint8_t>((size_t)total_rows * pb);
+    float *s = m->dalloc<float>((size_t)total_rows);
+    int32_t *rs = m->dalloc<int32_t>((size_t)total_rows);
+    if (!w || !s || !rs) return fail(OCRVL_E_NOMEM, "cudaMalloc failed for weights");
+    dst.w = w;
+    dst.scale = s;
+    dst.rowsum = rs;
+    dst.rows = total_rows;
+    dst.cols = (int)cols;
+    dst.pitch = pb;
+  }
+  CK(cudaMemcpy((void *)(dst.w + (size_t)row_offset * pb), data, (size_t)rows * pb, cudaMemcpyHostToDevice));
+  CK(cudaMemcpy((void *)(dst.scale + row_offset), scales, (size_t)rows * 4, cudaMemcpyHostToDevice));
+  k_rowsum<<<(unsigned)((rows * 32 + 255) / 256), 256, 0, m->stream>>>(
+      type, dst.w + (size_t)row_offset * pb, (int)rows, (int)cols, pb, (int32_t *)dst.rowsum + row_offset);
+  CK(cudaGetLastError());
+  CK(cudaStreamSynchronize(m->stream));
+  return OCRVL_OK;
+}
+
+int upload_f32(ocrvl_model *m, float *&dst, int64_t n, const void *data) {
+  if (!dst) dst = m->dalloc<float>((size_t)n);
+  if (!dst) return fail(OCRVL_E_NOMEM, "cudaMalloc failed");
+  CK(cudaMemcpy(dst, data, (size_t)n * 4, cudaMemcpyHostToDevice));
+  return OCRVL_OK;
+}
+
+size_t smem_bytes(const ocrvl_model_desc &d, int qtype) {
+  int nmax = std::max(std::max(d.hidden_size, d.intermediate_size), d.num_heads * d.head_dim);
+  size_t area = qtype == QT_Q8 ? (size_t)kMaxBatch * nmax * 4 : (size_t)kMaxBatch * nmax;
+  size_t gemv = (320 + (size_t)nmax) * 4 + area;
+  int G = d.num_heads / d.num_kv_heads;
+  size_t scores = ((size_t)G * d.head_dim + (size_t)kScoreChunk * (d.head_dim + 1)) * 4;
+  size_t pv = (32 + 8 * kPVChunk + (size_t)kPVChunk * d.head_dim) * 4;
+  return std::max(std::max(gemv, scores), pv) + 64;
+}
+
+int launch_step(ocrvl_model *m, int M, int any_logits, int do_embed) {
+  Ctx c = m->ctx;
+  if (m->persistent) {
+    void *args[] = {&c, &M, &any_logits, &do_embed};
+    CK(cudaLaunchCooperativeKernel((void *)k_step, dim3(m->grid), dim3(kThreads), args, m->smem, m->stream));
+    return OCRVL_OK;
+  }
+  if (do_embed) k_embed<<<m->grid, kThreads, 0, m->stream>>>(c);
+  for (int l = 0; l < m->desc.num_layers; l++) {
+    bool kv_only = l == m->desc.num_layers - 1 && !any_logits;
+    for (int ph = 0; ph < kLayerPhases; ph++) {
+      k_phase<<<m->grid, kThreads, m->smem, m->stream>>>(c, ph, l, M, any_logits);
+      if (kv_only && ph == 1) break;
+    }
+  }
+  if (any_logits) {
+    k_phase<<<m->grid, kThreads, m->smem, m->stream>>>(c, kLayerPhases, m->desc.num_layers - 1, M, any_logits);
+    k_phase<<<1, kThreads, m->smem, m->stream>>>(c, kLayerPhases + 1, m->desc.num_layers - 1, M, any_logits);
+  }
+  CK(cudaGetLastError());
+  return OCRVL_OK;
+}
+
+}  // namespace
+
+// ---------------------------------------------------------------------------
+// C ABI
+// ---------------------------------------------------------------------------
+extern "C" {
+
+const char *ocrvl_last_error(void) { return g_err.c_str(); }
+
+int ocrvl_device_count(void) {
+  int n = 0;
+  cudaError_t e = cudaGetDeviceCount(&n);
+  if (e != cudaSuccess) return fail(OCRVL_E_CUDA, std::string("cudaGetDeviceCount: ") + cudaGetErrorString(e));
+  return n;
+}
+
+int ocrvl_init(int device, const ocrvl_model_desc *desc, ocrvl_model **out) {
+  if (!desc || !out) return fail(OCRVL_E_INVALID, "null argument");
+  const ocrvl_model_desc &d = *desc;
+  if (d.num_layers <= 0 || d.hidden_size <= 0 || d.vocab_size <= 0 || d.num_heads <= 0 || d.num_kv_heads <= 0 ||
+      d.intermediate_size <= 0)
+    return fail(OCRVL_E_INVALID, "model dimensions must be positive");
+  if (d.head_dim != kHeadDim) return fail(OCRVL_E_INVALID, "head_dim must be 128");
+  if (d.num_heads % d.num_kv_heads != 0 || d.num_heads / d.num_kv_heads > 8)
+    return fail(OCRVL_E_INVALID, "num_heads must be 1..8 x num_kv_heads");
+  int qrows = d.num_heads * d.head_dim;
+  if (d.hidden_size % 128 || d.intermediate_size % 128 || qrows % 128)
+    return fail(OCRVL_E_INVALID, "hidden, intermediate and heads*head_dim must be multiples of 128");
+  // The fused AddRMSNorm sums split hidden_size rows over 8 workers; the
+  // reference's vector finalize needs each chunk < 16 rows or a multiple of 16.
+  int chunk = (d.hidden_size + kFusedWorkers - 1) / kFusedWorkers;
+  if (chunk >= 16 && chunk % 16) return fail(OCRVL_E_INVALID, "hidden_size/8 must be a multiple of 16");
+  int secsum = d.mrope_section[0] + d.mrope_section[1] + d.mrope_section[2];
+  if (secsum <= 0) return fail(OCRVL_E_INVALID, "mrope_section must be positive");
+  ocrvl_model *m = new ocrvl_model();
+  m->device = device;
+  m->desc = d;
+  if (m->desc.max_position <= 0) m->desc.max_position = 32768;
+  if (m->desc.kv_pool_bytes <= 0) m->desc.kv_pool_bytes = 4ll << 30;
+  cudaError_t e = cudaSetDevice(device);
+  if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&m->stream, cudaStreamNonBlocking);
+  if (e != cudaSuccess) {
+    delete m;
+    return fail(OCRVL_E_CUDA, std::string("device init: ") + cudaGetErrorString(e));
+  }
+  m->layers.assign(d.num_layers, LayerW{});
+  m->have.assign(d.num_layers + 1, 0);
+  *out = m;
+  return OCRVL_OK;
+}
+
+int ocrvl_load_tensor(ocrvl_model *m, const char *cname, int type, int64_t rows, int64_t cols,
+                      const float *scales, const void *data) {
+  if (!m || !cname || !data) return fail(OCRVL_E_INVALID, "null argument");
+  std::lock_guard<std::mutex> lk(m->mu);
+  if (m->finalized) return fail(OCRVL_E_INVALID, "model already finalized");
+  if (int rc = set_device(m)) return rc;
+  const ocrvl_model_desc &d = m->desc;
+  std::string name(cname);
+  int H = d.hidden_size, I = d.intermediate_size, qr = d.num_heads * d.head_dim, kvr = d.num_kv_heads * d.head_dim;
+  auto want_q = [&](int64_t r, int64_t c) -> int {
+    if (type != OCRVL_Q8_ROW && type != OCRVL_Q4_ROW && type != OCRVL_Q6_ROW)
+      return fail(OCRVL_E_INVALID, name + ": expected a row-quantized tensor (1000/1001/1002)");
+    if (!scales) return fail(OCRVL_E_INVALID, name + ": missing scales");
+    if (rows != r || cols != c) return fail(OCRVL_E_INVALID, name + ": unexpected shape");
+    if (m->qtype == 0) m->qtype = type;
+    if (m->qtype != type) return fail(OCRVL_E_INVALID, name + ": mixed quantization types");
+    return OCRVL_OK;
+  };
+  auto want_f32 = [&](int64_t n) -> int {
+    if (type != OCRVL_F32) return fail(OCRVL_E_INVALID, name + ": expected F32");
+    if (rows * std::max<int64_t>(cols, 1) != n) return fail(OCRVL_E_INVALID, name + ": unexpected shape");
+    return OCRVL_OK;
+  };
+  int rc;
+  if (name == "model.embed_tokens.weight") {
+    if ((rc = want_f32((int64_t)d.vocab_size * H))) return rc;
+    if ((rc = upload_f32(m, m->embed, (int64_t)d.vocab_size * H, data))) return rc;
+    m->have[d.num_layers] |= 1u << G_EMBED;
+    return OCRVL_OK;
+  }
+  if (name == "model.norm.weight") {
+    if ((rc = want_f32(H))) return rc;
+    if ((rc = upload_f32(m, m->final_norm, H, data))) return rc;
+    m->have[d.num_layers] |= 1u << G_NORM;
+    return OCRVL_OK;
+  }
+  if (name == "lm_head.weight") {
+    if ((rc = want_q(d.vocab_size, H))) return rc;
+    if ((rc = upload_matrix(m, m->lm_head, type, rows, cols, scales, data, 0, (int)rows))) return rc;
+    m->have[d.num_layers] |= 1u << G_LM;
+    return OCRVL_OK;
+  }
+  int layer;
+  std::string suf;
+  if (!parse_layer(name, layer, suf) || layer >= d.num_layers) return OCRVL_OK;  // not a decoder tensor
+  LayerW &L = m->layers[layer];
+  uint32_t &have = m->have[layer];
+  float *tmp = nullptr;
+  if (suf == "input_layernorm.weight" || suf == "post_attention_layernorm.weight") {
+    if ((rc = want_f32(H))) return rc;
+    bool first = suf[0] == 'i';
+    tmp = first ? (float *)L.ln1 : (float *)L.ln2;
+    if ((rc = upload_f32(m, tmp, H, data))) return rc;
+    if (first) { L.ln1 = tmp; have |= 1u << T_LN1; } else { L.ln2 = tmp; have |= 1u << T_LN2; }
+    return OCRVL_OK;
+  }
+  struct Slot { const char *s; int bit; int rows, cols, off, total; DMat *dst; };
+  Slot slots[] = {
+      {"self_attn.q_proj.weight", T_Q, qr, H, 0, qr + 2 * kvr, &L.qkv},
+      {"self_attn.k_proj.weight", T_K, kvr, H, qr, qr + 2 * kvr, &L.qkv},
+      {"self_attn.v_proj.weight", T_V, kvr, H, qr + kvr, qr + 2 * kvr, &L.qkv},
+      {"self_attn.o_proj.weight", T_O, H, qr, 0, H, &L.o},
+      {"mlp.gate_proj.weight", T_GATE, I, H, 0, I, &L.gate},
+      {"mlp.up_proj.weight", T_UP, I, H, 0, I, &L.up},
+      {"mlp.down_proj.weight", T_DOWN, H, I, 0, H, &L.down},
+  };
+  for (auto &s : slots) {
+    if (suf != s.s) continue;
+    if ((rc = want_q(s.rows, s.cols))) return rc;
+    if ((rc = upload_matrix(m, *s.dst, type, rows, cols, scales, data, s.off, s.total))) return rc;
+    have |= 1u << s.bit;
+    return OCRVL_OK;
+  }
+  return OCRVL_OK;
+}
+
+int ocrvl_finalize(ocrvl_model *m) {
+  if (!m) return fail(OCRVL_E_INVALID, "null model");
+  std::lock_guard<std::mutex> lk(m->mu);
+  if (m->finalized) return OCRVL_OK;
+  if (int rc = set_device(m)) return rc;
+  const ocrvl_model_desc &d = m->desc;
+  if (m->have[d.num_layers] != (1u << G_N) - 1) return fail(OCRVL_E_INVALID, "missing embed/norm/lm_head tensor");
+  for (int l = 0; l < d.num_layers; l++)
+    if (m->have[l] != (1u << T_NLAYER) - 1)
+      return fail(OCRVL_E_INVALID, "missing tensor(s) of layer " + std::to_string(l));
+  int half = d.head_dim / 2;
+  // RoPE tables (initTextRoPE + buildMRoPETable, model.go:877-902, 7318-7357):
+  // freq in float64, angle p*freq in float64, cos/sin rounded to f32.
+  {
+    std::vector<double> freq(half);
+    std::vector<int> axis(half);
+    int sec[3] = {d.mrope_section[0], d.mrope_section[1], d.mrope_section[2]};
+    int end = sec[0], ax = 0;
+    for (int i = 0; i < half; i++) {
+      while (ax + 1 < 3 && i >= end) { ax++; end += sec[ax]; }
+      axis[i] = std::min(ax, 2);
+      freq[i] = std::pow(d.rope_theta, -(double)(2 * i) / (double)d.head_dim);
+    }
+    size_t n = (size_t)d.max_position * half;
+    std::vector<float> cs(n), sn(n);
+    for (int p = 0; p < d.max_position; p++)
+      for (int i = 0; i < half; i++) {
+        double ang = (double)p * freq[i];
+        cs[(size_t)p * half + i] = (float)std::cos(ang);
+        sn[(size_t)p * half + i] = (float)std::sin(ang);
+      }
+    m->rope_cos = m->dalloc<float>(n);
+    m->rope_sin = m->dalloc<float>(n);
+    m->sec_axis = m->dalloc<int>(half);
+    if (!m->rope_cos || !m->rope_sin || !m->sec_axis) return fail(OCRVL_E_NOMEM, "rope tables");
+    CK(cudaMemcpy(m->rope_cos, cs.data(), n * 4, cudaMemcpyHostToDevice));
+    CK(cudaMemcpy(m->rope_sin, sn.data(), n * 4, cudaMemcpyHostToDevice));
+    CK(cudaMemcpy(m->sec_axis, axis.data(), half * 4, cudaMemcpyHostToDevice));
+  }
+  // layers
+  m->layers_d = m->dalloc<LayerW>(d.num_layers);
+  if (!m->layers_d) return fail(OCRVL_E_NOMEM, "layers");
+  CK(cudaMemcpy(m->layers_d, m->layers.data(), sizeof(LayerW) * d.num_layers, cudaMemcpyHostToDevice));
+  // KV pool
+  m->page_floats = (long long)d.num_layers * 2 * d.num_kv_heads * kPageTokens * d.head_dim;
+  m->num_pages = (int)std::min<long long>(d.kv_pool_bytes / (m->page_floats * 4), 1 << 24);
+  if (m->num_pages <= 0) return fail(OCRVL_E_INVALID, "kv_pool_bytes too small for one page");
+  m->kv_pool = m->dalloc<float>((size_t)m->num_pages * m->page_floats);
+  if (!m->kv_pool) return fail(OCRVL_E_NOMEM, "kv pool allocation failed");
+  m->free_pages.resize(m->num_pages);
+  for (int i = 0; i < m->num_pages; i++) m->free_pages[i] = m->num_pages - 1 - i;
+  // work buffers
+  Ctx &c = m->ctx;
+  c.qtype = m->qtype;
+  c.H = d.hidden_size;
+  c.I = d.intermediate_size;
+  c.L = d.num_layers;
+  c.QH = d.num_heads;
+  c.KVH = d.num_kv_heads;
+  c.D = d.head_dim;
+  c.V = d.vocab_size;
+  c.eps = d.rms_norm_eps;
+  c.attn_scale = (float)(1.0 / std::sqrt((double)d.head_dim));
+  c.embed = m->embed;
+  c.final_norm = m->final_norm;
+  c.layers = m->layers_d;
+  c.lm_head = m->lm_head;
+  c.rope_cos = m->rope_cos;
+  c.rope_sin = m->rope_sin;
+  c.rope_max = d.max_position;
+  c.sec_axis = m->sec_axis;
+  c.kv_pool = m->kv_pool;
+  c.page_floats = m->page_floats;
+  c.max_ctx = d.max_position;
+  c.max_chunks = (c.max_ctx + kPVChunk - 1) / kPVChunk;
+  int qkvld = (c.QH + 2 * c.KVH) * c.D;
+  size_t B = kMaxBatch;
+  c.h = m->dalloc<float>(B * c.H);
+  c.vbuf = m->dalloc<float>(B * c.H);
+  c.qkv = m->dalloc<float>(B * qkvld);
+  c.head = m->dalloc<float>(B * c.QH * c.D);
+  c.g = m->dalloc<float>(B * c.I);
+  c.scores = m->dalloc<float>(B * c.QH * (size_t)c.max_ctx);
+  c.partial = m->dalloc<float>(B * c.QH * (size_t)c.max_chunks * c.D);
+  c.logits = m->dalloc<float>(B * (size_t)c.V);
+  c.argkey = m->dalloc<unsigned long long>(B);
+  c.tok_out = m->dalloc<int>(B + 1);
+  c.bar_count = m->dalloc<unsigned>(2 + B * c.KVH);
+  c.bar_gen = c.bar_count + 1;
+  c.pv_count = c.bar_count + 2;
+  StepParams *spd = m->dalloc<StepParams>(1);
+  if (!c.h || !c.vbuf || !c.qkv || !c.head || !c.g || !c.scores || !c.partial || !c.logits || !c.argkey ||
+      !c.tok_out || !c.bar_count || !spd)
+    return fail(OCRVL_E_NOMEM, "work buffer allocation failed");
+  c.err = c.tok_out + B;
+  c.sp = spd;
+  m->sp_d = spd;
+  CK(cudaMemset(c.argkey, 0, B * 8));
+  CK(cudaMemset(c.tok_out, 0, (B + 1) * 4));
+  CK(cudaMemset(c.bar_count, 0, (2 + B * c.KVH) * 4));
+  CK(cudaHostAlloc((void **)&m->sp_h, sizeof(StepParams), cudaHostAllocDefault));
+  CK(cudaHostAlloc((void **)&m->out_h, (B + 1) * 4, cudaHostAllocDefault));
+  CK(cudaHostAlloc((void **)&m->bt_stage, B * 4, cudaHostAllocDefault));
+  // launch geometry
+  m->smem = smem_bytes(d, m->qtype);
+  CK(cudaFuncSetAttribute(k_step, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)m->smem));
+  CK(cudaFuncSetAttribute(k_phase, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)m->smem));
+  CK(cudaDeviceGetAttribute(&m->sms, cudaDevAttrMultiProcessorCount, m->device));
+  int per_sm = 0;
+  CK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_step, kThreads, m->smem));
+  if (per_sm <= 0) return fail(OCRVL_E_CUDA, "step kernel does not fit on an SM");
+  int want = 1;
+  if (const char *e = getenv("OCRVL_BLOCKS_PER_SM")) want = std::max(1, std::atoi(e));
+  m->grid = m->sms * std::min(per_sm, want);
+  if (getenv("OCRVL_TRACE")) {
+    c.trace = m->dalloc<unsigned long long>(4 * 256);
+    if (!c.trace) return fail(OCRVL_E_NOMEM, "trace buffer");
+    CK(cudaMemset(c.trace, 0, 4 * 256 * 8));
+  }
+  const char *mode = getenv("OCRVL_STEP_MODE");
+  m->persistent = !(mode && std::string(mode) == "phases");
+  CK(cudaStreamSynchronize(m->stream));
+  m->finalized = true;
+  return OCRVL_OK;
+}
+
+int ocrvl_quant_type(const ocrvl_model *m) { return m ? m->qtype : OCRVL_E_INVALID; }
+
+int ocrvl_trace_read(ocrvl_model *m, uint64_t *out, int cap) {
+  if (!m || !out) return fail(OCRVL_E_INVALID, "null argument");
+  if (!m->ctx.trace) return 0;
+  std::lock_guard<std::mutex> lk(m->mu);
+  if (int rc = set_device(m)) return rc;
+  int n = std::min(cap, 4 * 256);
+  CK(cudaStreamSynchronize(m->stream));
+  CK(cudaMemcpy(out, m->ctx.trace, (size_t)n * 8, cudaMemcpyDeviceToHost));
+  CK(cudaMemset(m->ctx.trace, 0, 4 * 256 * 8));
+  return n;
+}
+
+void ocrvl_free(ocrvl_model *m) {
+  if (!m) return;
+  cudaSetDevice(m->device);
+  if (m->stream) cudaStreamSynchronize(m->stream);
+  for (void *p : m->allocs) cudaFree(p);
+  if (m->sp_h) cudaFreeHost(m->sp_h);
+  if (m->out_h) cudaFreeHost(m->out_h);
+  if (m->bt_stage) cudaFreeHost(m->bt_stage);
+  if (m->stream) cudaStreamDestroy(m->stream);
+  delete m;
+}
+
+int ocrvl_seq_create(ocrvl_model *m, int max_tokens, ocrvl_seq **out) {
+  if (!m || !out || max_tokens <= 0) return fail(OCRVL_E_INVALID, "bad arguments");
+  std::lock_guard<std::mutex> lk(m->mu);
+  if (!m->finalized) return fail(OCRVL_E_INVALID, "model not finalized");
+  if (max_tokens > m->desc.max_position) return fail(OCRVL_E_INVALID, "max_tokens exceeds max_position");
+  if (int rc = set_device(m)) return rc;
+  ocrvl_seq *s = new ocrvl_seq();
+  s->m = m;
+  s->max_tokens = max_tokens;
+  int np = (max_tokens + kPageTokens - 1) / kPageTokens;
+  if (cudaMalloc(&s->bt_d, (size_t)np * 4) != cudaSuccess) {
+    delete s;
+    return fail(OCRVL_E_NOMEM, "block table allocation failed");
+  }
+  cudaMemset(s->bt_d, 0, (size_t)np * 4);
+  *out = s;
+  return OCRVL_OK;
+}
+
+int ocrvl_seq_reset(ocrvl_seq *s) {
+  if (!s) return fail(OCRVL_E_INVALID, "null seq");
+  std::lock_guard<std::mutex> lk(s->m->mu);
+  for (int p : s->pages) s->m->free_pages.push_back(p);
+  s->pages.clear();
+  s->len = 0;
+  return OCRVL_OK;
+}
+
+void ocrvl_seq_free(ocrvl_seq *s) {
+  if (!s) return;
+  ocrvl_seq_reset(s);
+  cudaSetDevice(s->m->device);
+  cudaFree(s->bt_d);
+  delete s;
+}
+
+int ocrvl_seq_len(const ocrvl_seq *s) { return s ? s->len : OCRVL_E_INVALID; }
+
+int ocrvl_seq_read_kv(ocrvl_seq *s, int layer, float *k, float *v) {
+  if (!s || !k || !v) return fail(OCRVL_E_INVALID, "null argument");
+  ocrvl_model *m = s->m;
+  std::lock_guard<std::mutex> lk(m->mu);
+  const ocrvl_model_desc &d = m->desc;
+  if (layer < 0 || layer >= d.num_layers) return fail(OCRVL_E_INVALID, "layer out of range");
+  if (int rc = set_device(m)) return rc;
+  CK(cudaStreamSynchronize(m->stream));
+  int kvd = d.num_kv_heads * d.head_dim;
+  for (int t = 0; t < s->len; t++) {
+    int page = s->pages[t / kPageTokens];
+    for (int kind = 0; kind < 2; kind++)
+      for (int g = 0; g < d.num_kv_heads; g++) {
+        size_t off = (size_t)page * m->page_floats +
+                     ((((size_t)layer * 2 + kind) * d.num_kv_heads + g) * kPageTokens + t % kPageTokens) * d.head_dim;
+        float *dst = (kind == 0 ? k : v) + (size_t)t * kvd + (size_t)g * d.head_dim;
+        CK(cudaMemcpy(dst, m->kv_pool + off, d.head_dim * 4, cudaMemcpyDeviceToHost));
+      }
+  }
+  return s->len;
+}
+
+int ocrvl_step(ocrvl_model *m, ocrvl_seq *const *seqs, int n, const int32_t *ids, const float *embeds,
+               const int32_t *pos_thw, int need_logits, int32_t *out_ids, float *out_logits) {
+  if (!m || !seqs) return fail(OCRVL_E_INVALID, "null argument");
+  if (n < 1 || n > kMaxBatch) return fail(OCRVL_E_INVALID, "batch must be 1..8 sequences");
+  if (!ids && !embeds) return fail(OCRVL_E_INVALID, "ids or embeds required");
+  std::lock_guard<std::mutex> lk(m->mu);
+  if (!m->finalized) return fail(OCRVL_E_INVALID, "model not finalized");
+  if (int rc = set_device(m)) return rc;
+  const ocrvl_model_desc &d = m->desc;
+  StepParams &sp = *m->sp_h;
+  memset(&sp, 0, sizeof(sp));
+  sp.M = n;
+  sp.any_logits = need_logits ? 1 : 0;
+  int max_n = 0;
+  for (int i = 0; i < n; i++) {
+    ocrvl_seq *s = seqs[i];
+    if (!s || s->m != m) return fail(OCRVL_E_INVALID, "sequence belongs to another model");
+    for (int j = 0; j < i; j++)
+      if (seqs[j] == s) return fail(OCRVL_E_INVALID, "sequence repeated in one step");
+    if (s->len >= s->max_tokens) return fail(OCRVL_E_INVALID, "sequence is full (max_tokens reached)");
+    if (ids && (ids[i] < 0 || ids[i] >= d.vocab_size))
+      return fail(OCRVL_E_INVALID, "token id " + std::to_string(ids ? ids[i] : 0) + " outside vocab");
+    int p[3] = {s->len, s->len, s->len};
+    if (pos_thw)
+      for (int a = 0; a < 3; a++) p[a] = pos_thw[3 * i + a];
+    for (int a = 0; a < 3; a++)
+      if (p[a] < 0 || p[a] >= d.max_position) return fail(OCRVL_E_INVALID, "position outside RoPE table");
+    sp.tok[i] = ids ? ids[i] : 0;
+    sp.len[i] = s->len;
+    for (int a = 0; a < 3; a++) sp.pos[i][a] = p[a];
+    sp.need[i] = need_logits ? 1 : 0;
+    sp.bt[i] = s->bt_d;
+    max_n = std::max(max_n, s->len + 1);
+  }
+  sp.max_n = max_n;
+  // pages for the positions appended this step
+  for (int i = 0; i < n; i++) {
+    ocrvl_seq *s = seqs[i];
+    if (s->len % kPageTokens == 0 && (int)s->pages.size() <= s->len / kPageTokens) {
+      if (m->free_pages.empty()) return fail(OCRVL_E_NOMEM, "KV page pool exhausted");
+      int pg = m->free_pages.back();
+      m->free_pages.pop_back();
+      s->pages.push_back(pg);
+      m->bt_stage[i] = pg;
+      CK(cudaMemcpyAsync(s->bt_d + s->len / kPageTokens, &m->bt_stage[i], 4, cudaMemcpyHostToDevice, m->stream));
+    }
+  }
+  CK(cudaMemcpyAsync(m->sp_d, &sp, sizeof(StepParams), cudaMemcpyHostToDevice, m->stream));
+  if (embeds) CK(cudaMemcpyAsync(m->ctx.h, embeds, (size_t)n * d.hidden_size * 4, cudaMemcpyHostToDevice, m->stream));
+  if (int rc = launch_step(m, n, sp.any_logits, embeds ? 0 : 1)) return rc;
+  CK(cudaMemcpyAsync(m->out_h, m->ctx.tok_out, (kMaxBatch + 1) * 4, cudaMemcpyDeviceToHost, m->stream));
+  if (out_logits && need_logits)
+    CK(cudaMemcpyAsync(out_logits, m->ctx.logits, (size_t)n * d.vocab_size * 4, cudaMemcpyDeviceToHost, m->stream));
+  CK(cudaStreamSynchronize(m->stream));
+  if (m->out_h[kMaxBatch]) {
+    int zero = 0;
+    cudaMemcpy(m->ctx.err, &zero, 4, cudaMemcpyHostToDevice);
+    cudaMemset(m->ctx.bar_count, 0, (2 + kMaxBatch * m->ctx.KVH) * 4);
+    return fail(OCRVL_E_TIMEOUT, "device grid barrier timed out");
+  }
+  for (int i = 0; i < n; i++) {
+    seqs[i]->len++;
+    if (out_ids) out_ids[i] = need_logits ? m->out_h[i] : -1;
+  }
+  return OCRVL_OK;
+}
+
+int ocrvl_generate_greedy(ocrvl_model *m, const int32_t *ids, int n_ids, int max_new, const int32_t *eos,
+                          int n_eos, int32_t *out, int out_cap, int *n_out) {
+  if (!m || !out || !n_out || (n_ids > 0 && !ids)) return fail(OCRVL_E_INVALID, "null argument");
+  if (max_new < 0) return fail(OCRVL_E_INVALID, "max_new_tokens must be >= 0");
+  for (int i = 0; i < n_ids; i++)
+    if (ids[i] < 0) return fail(OCRVL_E_INVALID, "input tokens must not contain negative ids");
+  if (max_new > 0 && n_ids == 0) return fail(OCRVL_E_INVALID, "input tokens must not be empty when max_new_tokens > 0");
+  if (out_cap < n_ids + max_new) return fail(OCRVL_E_INVALID, "output buffer too small");
+  static const int32_t kDefaultEOS[1] = {2};
+  if (!eos) { eos = kDefaultEOS; n_eos = 1; }
+  for (int i = 0; i < n_ids; i++) out[i] = ids[i];
+  *n_out = n_ids;
+  if (max_new == 0) return OCRVL_OK;
+  ocrvl_seq *s = nullptr;
+  int rc = ocrvl_seq_create(m, n_ids + max_new, &s);
+  if (rc) return rc;
+  int32_t tok = -1;
+  for (int p = 0; p < n_ids && rc == 0; p++) rc = ocrvl_step(m, &s, 1, &ids[p], nullptr, nullptr, p == n_ids - 1, &tok, nullptr);
+  int n = n_ids;
+  for (int i = 0; rc == 0 && i < max_new; i++) {
+    out[n++] = tok;
+    bool stop = false;
+    for (int j = 0; j < n_eos; j++) stop |= tok == eos[j];
+    if (stop || i + 1 >= max_new) break;
+    int32_t cur = tok;
+    rc = ocrvl_step(m, &s, 1, &cur, nullptr, nullptr, 1, &tok, nullptr);
+  }
+  ocrvl_seq_free(s);
+  *n_out = n;
+  return rc;
+}
+
+}  // extern "C"
+
+// ---------------------------------------------------------------------------
+// GGUF file loading (gguf.Open, internal/gguf/gguf.go:111-251, and the row
+// loaders 313-569): header parsed here, tensor bytes handed to
+// ocrvl_load_tensor straight from a read-only mapping of the file.
+// ---------------------------------------------------------------------------
+#include <fcntl.h>
+#include <sys/mman.h>
+#include <sys/stat.h>
+#include <unistd.h>
+
+namespace {
+
+struct Reader {
+  const uint8_t *p;
+  size_t n, pos = 0;
+  bool ok = true;
+  template <typename T>
+  T get() {
+    T v{};
+    if (pos + sizeof(T) > n) { ok = false; return v; }
+    memcpy(&v, p + pos, sizeof(T));
+    pos += sizeof(T);
+    return v;
+  }
+  std::string str() {
+    uint64_t len = get<uint64_t>();
+    if (!ok || len > (16u << 20) || pos + len > n) { ok = false; return ""; }
+    std::string s((const char *)p + pos, len);
+    pos += len;
+    return s;
+  }
+};
+
+}  // namespace
+
+extern "C" int ocrvl_load_gguf(ocrvl_model *m, const char *path) {
+  if (!m || !path) return fail(OCRVL_E_INVALID, "null argument");
+  int fd = open(path, O_RDONLY);
+  if (fd < 0) return fail(OCRVL_E_INVALID, std::string("cannot open ") + path);
+  struct stat st;
+  if (fstat(fd, &st) != 0 || st.st_size < 24) {
+    close(fd);
+    return fail(OCRVL_E_INVALID, "bad GGUF file");
+  }
+  size_t size = (size_t)st.st_size;
+  void *map = mmap(nullptr, size, PROT_READ, MAP_PRIVATE, fd, 0);
+  close(fd);
+  if (map == MAP_FAILED) return fail(OCRVL_E_INVALID, "mmap failed");
+  struct Unmap { void *p; size_t n; ~Unmap() { munmap(p, n); } } um{map, size};
+  Reader r{(const uint8_t *)map, size};
+  uint32_t magic = r.get<uint32_t>();
+  if (magic != 0x46554747u) return fail(OCRVL_E_INVALID, "bad GGUF magic");
+  if (r.get<uint32_t>() != 3u) return fail(OCRVL_E_INVALID, "unsupported GGUF version");
+  uint64_t nt = r.get<uint64_t>(), nkv = r.get<uint64_t>();
+  if (nt > (1u << 20) || nkv > (1u << 20)) return fail(OCRVL_E_INVALID, "GGUF counts too large");
+  for (uint64_t i = 0; i < nkv && r.ok; i++) {
+    r.str();
+    uint32_t t = r.get<uint32_t>();
+    if (t == 4) r.get<uint32_t>();
+    else if (t == 10) r.get<uint64_t>();
+    else if (t == 8) r.str();
+    else return fail(OCRVL_E_INVALID, "unsupported GGUF metadata type");
+  }
+  struct TI { std::string name; std::vector<uint64_t> shape; uint32_t type; uint64_t off; };
+  std::vector<TI> infos;
+  for (uint64_t i = 0; i < nt && r.ok; i++) {
+    TI t;
+    t.name = r.str();
+    uint32_t nd = r.get<uint32_t>();
+    if (nd > 8) return fail(OCRVL_E_INVALID, "GGUF tensor has too many dimensions");
+    for (uint32_t j = 0; j < nd; j++) t.shape.push_back(r.get<uint64_t>());
+    t.type = r.get<uint32_t>();
+    t.off = r.get<uint64_t>();
+    infos.push_back(t);
+  }
+  if (!r.ok) return fail(OCRVL_E_INVALID, "truncated GGUF header");
+  size_t data_start = (r.pos + 31) / 32 * 32;
+  for (auto &t : infos) {
+    int64_t rows = t.shape.empty() ? 1 : (int64_t)t.shape[0];
+    int64_t cols = t.shape.size() >= 2 ? (int64_t)t.shape[1] : 1;
+    size_t bytes;
+    if (t.type == OCRVL_F32) {
+      bytes = 4;
+      for (auto dsz : t.shape) bytes *= dsz;
+    } else {
+      int pb = packed_row_bytes((int)t.type, (int)cols);
+      if (pb < 0 || t.shape.size() != 2) return fail(OCRVL_E_INVALID, "unsupported GGUF tensor " + t.name);
+      bytes = (size_t)rows * (4 + pb);
+    }
+    if (data_start + t.off + bytes > size) return fail(OCRVL_E_INVALID, "GGUF tensor " + t.name + " exceeds file size");
+    const uint8_t *base = (const uint8_t *)map + data_start + t.off;
+    int rc;
+    if (t.type == OCRVL_F32)
+      rc = ocrvl_load_tensor(m, t.name.c_str(), 0, rows, t.shape.size() >= 2 ? cols : 1, nullptr, base);
+    else
+      rc = ocrvl_load_tensor(m, t.name.c_str(), (int)t.type, rows, cols, (const float *)base, base + rows * 4);
+    if (rc) return rc;
+  }
+  return OCRVL_OK;
+}
+
+// ---------------------------------------------------------------------------
+// Op-level entry points (device pointers)
+// ---------------------------------------------------------------------------
+namespace {
+
+Ctx op_ctx(int type, float eps) {
+  Ctx c;
+  memset(&c, 0, sizeof(c));
+  c.qtype = type;
+  c.eps = eps;
+  return c;
+}
+
+DMat op_mat(int type, int rows, int cols, const void *w, const float *scale, const int32_t *rowsum) {
+  DMat a;
+  a.w = (const uint8_t *)w;
+  a.scale = scale;
+  a.rowsum = rowsum;
+  a.rows = rows;
+  a.cols = cols;
+  a.pitch = packed_row_bytes(type, cols);
+  return a;
+}
+
+int op_check(int type, int rows, int cols, int m) {
+  if (type != OCRVL_Q8_ROW && type != OCRVL_Q4_ROW && type != OCRVL_Q6_ROW)
+    return fail(OCRVL_E_INVALID, "type must be 1000, 1001 or 1002");
+  if (rows <= 0 || cols <= 0 || cols % 128) return fail(OCRVL_E_INVALID, "cols must be a positive multiple of 128");
+  if (m < 1 || m > kMaxBatch) return fail(OCRVL_E_INVALID, "m must be 1..8");
+  return OCRVL_OK;
+}
+
+int op_grid(int rows) {
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  return std::max(1, std::min(sms * 2, (rows + 7) / 8));
+}
+
+int op_gemv(const Ctx &c, const GemvArgs &a, int m, cudaStream_t st) {
+  size_t smem = (320 + (size_t)a.A.cols) * 4 + (c.qtype == QT_Q8 ? (size_t)m * a.A.cols * 4 : (size_t)m * a.A.cols) + 64;
+  CK(cudaFuncSetAttribute(k_gemv, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  k_gemv<<<op_grid(a.A.rows), kThreads, smem, st>>>(c, a, m);
+  CK(cudaGetLastError());
+  return OCRVL_OK;
+}
+
+std::mutex g_scratch_mu;
+unsigned long long *g_keys[64];
+
+}  // namespace
+
+extern "C" {
+
+int ocrvl_op_rowsum(int type, int rows, int cols, const void *w, int32_t *rowsum, void *stream) {
+  if (int rc = op_check(type, rows, cols, 1)) return rc;
+  k_rowsum<<<(unsigned)(((int64_t)rows * 32 + 255) / 256), 256, 0, (cudaStream_t)stream>>>(
+      type, (const uint8_t *)w, rows, cols, packed_row_bytes(type, cols), rowsum);
+  CK(cudaGetLastError());
+  return OCRVL_OK;
+}
+
+int ocrvl_op_matvec(int type, int rows, int cols, const void *w, const float *scale, const int32_t *rowsum, int m,
+                    const float *x, const float *norm_w, float eps, float *out, void *stream) {
+  if (int rc = op_check(type, rows, cols, m)) return rc;
+  Ctx c = op_ctx(type, eps);
+  GemvArgs a;
+  memset(&a, 0, sizeof(a));
+  a.A = op_mat(type, rows, cols, w, scale, rowsum);
+  a.row_end = rows;
+  a.src = x;
+  a.ld = cols;
+  a.mode = norm_w ? PRO_RMSNORM : PRO_PLAIN;
+  a.norm_w = norm_w;
+  a.epi = EPI_STORE;
+  a.out = out;
+  a.ldo = rows;
+  return op_gemv(c, a, m, (cudaStream_t)stream);
+}
+
+int ocrvl_op_matvec_add_rmsnorm(int type, int rows, int cols, const void *w, const float *scale,
+                                const int32_t *rowsum, int m, const float *x, float *residual, int in_place,
+                                const float *norm_w, float eps, float *v_out, float *norm_out, void *stream) {
+  if (int rc = op_check(type, rows, cols, m)) return rc;
+  int chunk = (rows + kFusedWorkers - 1) / kFusedWorkers;
+  if (type != OCRVL_Q8_ROW && chunk >= 16 && chunk % 16)
+    return fail(OCRVL_E_INVALID, "rows/8 must be < 16 or a multiple of 16");
+  Ctx c = op_ctx(type, eps);
+  GemvArgs a;
+  memset(&a, 0, sizeof(a));
+  a.A = op_mat(type, rows, cols, w, scale, rowsum);
+  a.row_end = rows;
+  a.src = x;
+  a.ld = cols;
+  a.mode = PRO_PLAIN;
+  a.epi = EPI_RESID;
+  a.ldo = rows;
+  a.resid = residual;
+  a.vout = v_out;
+  a.resid_mode = RESID_MASK;
+  a.in_place_mask = in_place ? 0xFF : 0;
+  cudaStream_t st = (cudaStream_t)stream;
+  if (int rc = op_gemv(c, a, m, st)) return rc;
+  size_t smem = (320 + (size_t)rows) * 4 + 64;
+  CK(cudaFuncSetAttribute(k_addnorm_out, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  k_addnorm_out<<<m, kThreads, smem, st>>>(c, v_out, rows, m, norm_w, norm_out);
+  CK(cudaGetLastError());
+  return OCRVL_OK;
+}
+
+int ocrvl_op_swiglu(int type, int rows, int cols, const void *wg, const float *sg, const int32_t *rsg,
+                    const void *wu, const float *su, const int32_t *rsu, int m, const float *x, float *out,
+                    void *stream) {
+  if (int rc = op_check(type, rows, cols, m)) return rc;
+  Ctx c = op_ctx(type, 0.0f);
+  GemvArgs a;
+  memset(&a, 0, sizeof(a));
+  a.A = op_mat(type, rows, cols, wg, sg, rsg);
+  a.B = op_mat(type, rows, cols, wu, su, rsu);
+  a.row_end = rows;
+  a.src = x;
+  a.ld = cols;
+  a.mode = PRO_PLAIN;
+  a.epi = EPI_SWIGLU;
+  a.out = out;
+  a.ldo = rows;
+  return op_gemv(c, a, m, (cudaStream_t)stream);
+}
+
+int ocrvl_op_argmax(int type, int rows, int cols, const void *w, const float *scale, const int32_t *rowsum, int m,
+                    const float *x, int32_t *ids, void *stream) {
+  if (int rc = op_check(type, rows, cols, m)) return rc;
+  int dev = 0;
+  CK(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= 64) return fail(OCRVL_E_INVALID, "device index out of range");
+  cudaStream_t st = (cudaStream_t)stream;
+  unsigned long long *keys;
+  {
+    std::lock_guard<std::mutex> lk(g_scratch_mu);
+    if (!g_keys[dev]) CK(cudaMalloc(&g_keys[dev], kMaxBatch * 8));
+    keys = g_keys[dev];
+  }
+  CK(cudaMemsetAsync(keys, 0, kMaxBatch * 8, st));
+  Ctx c = op_ctx(type, 0.0f);
+  GemvArgs a;
+  memset(&a, 0, sizeof(a));
+  a.A = op_mat(type, rows, cols, w, scale, rowsum);
+  a.row_end = rows;
+  a.src = x;
+  a.ld = cols;
+  a.mode = PRO_PLAIN;
+  a.epi = EPI_ARGMAX;
+  a.ldo = rows;
+  a.argkey = keys;
+  if (int rc = op_gemv(c, a, m, st)) return rc;
+  k_argmax_ids<<<1, 32, 0, st>>>(keys, m, ids);
+  CK(cudaGetLastError());
+  return OCRVL_OK;
+}
+
+int ocrvl_op_rmsnorm(int n, int m, const float *x, const float *w, float eps, float *out, void *stream) {
+  if (n <= 0 || n % 128 || m < 1) return fail(OCRVL_E_INVALID, "n must be a positive multiple of 128, m >= 1");
+  Ctx c = op_ctx(OCRVL_Q8_ROW, eps);
+  size_t smem = (320 + (size_t)n) * 4 + 64;
+  CK(cudaFuncSetAttribute(k_rmsnorm_out, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  k_rmsnorm_out<<<std::min(m, 1024), kThreads, smem, (cudaStream_t)stream>>>(c, x, n, m, w, out);
+  CK(cudaGetLastError());
+  return OCRVL_OK;
+}
+
+}  // extern "C"

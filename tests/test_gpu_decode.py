@@ -1,0 +1,180 @@
+"""Decode-step parity of the CUDA engine against the CPU oracle on seeded
+synthetic decoders (tolerance from the spec: logits within 2e-2 absolute or
+1e-2 relative; greedy ids equal; KV append bit-exact)."""
+import os
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+from rapidocrvl_b200 import GenerateOptions, LoadOptions, Runtime, config, synth  # noqa: E402
+
+LOGIT_ATOL = 2e-2
+LOGIT_RTOL = 1e-2
+
+
+def _need_gpu():
+    import torch
+
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+
+
+def _pair(model_dir, q):
+    import pyoracle
+
+    cfg = config.load(model_dir)
+    rt = Runtime.load(model_dir, LoadOptions(quantization=q, max_position=4096, kv_pool_bytes=1 << 28))
+    orc = pyoracle.OracleModel(os.path.join(model_dir, f"model-{q}.gguf"), cfg)
+    return cfg, rt, orc
+
+
+@pytest.mark.parametrize("q", ["q8", "q6", "q4"])
+def test_greedy_ids_match_oracle(tiny_models, q):
+    _need_gpu()
+    cfg, rt, orc = _pair(tiny_models[q], q)
+    ids = synth.random_prompt(12, cfg.vocab_size, 0)
+    got = rt.generate_with_options(ids, GenerateOptions(max_new_tokens=70, eos_token_ids=[]))
+    want = orc.generate(ids, 70, eos=[])
+    assert got.prompt_tokens == 12
+    assert got.tokens == want
+
+
+@pytest.mark.parametrize("q", ["q8", "q4"])
+def test_stepwise_logits_and_kv(tiny_models, q):
+    """Token-by-token: logits within tolerance, argmax equal, KV compared."""
+    _need_gpu()
+    cfg, rt, orc = _pair(tiny_models[q], q)
+    seq = rt.new_sequence(128)
+    oseq = orc.new_seq(128)
+    tok = 5
+    worst = 0.0
+    for p in range(80):  # crosses n = 6/7, 16 (softmax tail rule), 64 (two value chunks) and page edges
+        ids, logits = rt.step([seq], ids=[tok], need_logits=True, return_logits=True)
+        otok, ologits, _ = oseq.forward(orc.embed(tok), p, need_logits=True, want_logits=True)
+        err = np.abs(logits[0] - ologits)
+        worst = max(worst, float(err.max()))
+        assert np.all(err <= LOGIT_ATOL + LOGIT_RTOL * np.abs(ologits)), f"pos {p}: max err {err.max()}"
+        assert int(ids[0]) == otok, f"pos {p}: argmax {ids[0]} vs {otok}"
+        if p == 0:
+            for layer in range(cfg.num_hidden_layers):
+                k, v = seq.read_kv(layer)
+                ok, ov = oseq.kv(layer)
+                assert np.array_equal(k, ok) and np.array_equal(v, ov), "first append must be bit-exact"
+        tok = int(ids[0])
+    assert len(seq) == 80
+    for layer in range(cfg.num_hidden_layers):
+        k, v = seq.read_kv(layer)
+        ok, ov = oseq.kv(layer)
+        assert k.shape == ok.shape
+        np.testing.assert_allclose(k, ok, rtol=1e-3, atol=1e-4)
+        np.testing.assert_allclose(v, ov, rtol=1e-3, atol=1e-4)
+
+
+def test_prompt_steps_without_logits(tiny_models):
+    _need_gpu()
+    cfg, rt, orc = _pair(tiny_models["q4"], "q4")
+    seq = rt.new_sequence(64)
+    oseq = orc.new_seq(64)
+    prompt = synth.random_prompt(20, cfg.vocab_size, 3)
+    for p, t in enumerate(prompt):
+        last = p == len(prompt) - 1
+        ids, _ = rt.step([seq], ids=[t], need_logits=last)
+        otok, _, _ = oseq.forward(orc.embed(t), p, need_logits=last)
+        if not last:
+            assert int(ids[0]) == -1
+    assert int(ids[0]) == otok
+
+
+def test_batched_step_equals_single(tiny_models):
+    """Sequences stepped together give the same bits as stepped alone."""
+    _need_gpu()
+    cfg, rt, _ = _pair(tiny_models["q8"], "q8")
+    prompts = [synth.random_prompt(n, cfg.vocab_size, n) for n in (3, 9, 21)]
+
+    def run(batched):
+        seqs = [rt.new_sequence(64) for _ in prompts]
+        outs = [[] for _ in prompts]
+        steps = max(len(p) for p in prompts) + 10
+        toks = [p[0] for p in prompts]
+        for i in range(steps):
+            live = [j for j in range(len(prompts))]
+            if batched:
+                ids, logits = rt.step([seqs[j] for j in live], ids=[toks[j] for j in live], return_logits=True)
+            else:
+                res = [rt.step([seqs[j]], ids=[toks[j]], return_logits=True) for j in live]
+                ids = np.array([r[0][0] for r in res])
+                logits = np.stack([r[1][0] for r in res])
+            for j in live:
+                outs[j].append(logits[j])
+                nxt = i + 1
+                toks[j] = prompts[j][nxt] if nxt < len(prompts[j]) else int(ids[j])
+        return outs
+
+    a, b = run(True), run(False)
+    for j in range(len(prompts)):
+        for x, y in zip(a[j], b[j]):
+            assert np.array_equal(x, y)
+
+
+def test_embeds_and_mrope_positions(tiny_models):
+    """Embedding input and distinct (T,H,W) positions (image-token prefill)."""
+    _need_gpu()
+    cfg, rt, orc = _pair(tiny_models["q6"], "q6")
+    seq = rt.new_sequence(32)
+    oseq = orc.new_seq(32)
+    rng = np.random.default_rng(0)
+    for p in range(10):
+        emb = (rng.standard_normal(cfg.hidden_size) * 0.02).astype(np.float32)
+        pos = (p, 3 + p // 3, 5 + p % 3) if p < 8 else (p, p, p)
+        ids, logits = rt.step([seq], embeds=emb[None], positions=[pos], return_logits=True)
+        otok, ologits, _ = oseq.forward(emb, pos, need_logits=True, want_logits=True)
+        assert np.all(np.abs(logits[0] - ologits) <= LOGIT_ATOL + LOGIT_RTOL * np.abs(ologits))
+        assert int(ids[0]) == otok
+
+
+def test_eos_and_edge_lengths(tiny_models):
+    _need_gpu()
+    cfg, rt, orc = _pair(tiny_models["q4"], "q4")
+    ids = synth.random_prompt(4, cfg.vocab_size, 11)
+    full = orc.generate(ids, 12, eos=[])
+    eos = full[4 + 5]
+    got = rt.generate_with_options(ids, GenerateOptions(max_new_tokens=12, eos_token_ids=[eos]))
+    assert got.tokens == orc.generate(ids, 12, eos=[eos])
+    assert rt.generate(ids, 0) == ids
+    assert rt.generate(ids[:1], 1) == orc.generate(ids[:1], 1, eos=[])
+    with pytest.raises(ValueError):
+        rt.generate([], 3)
+    with pytest.raises(ValueError):
+        rt.generate([cfg.vocab_size], 3)
+
+
+def test_step_errors_leave_state_unchanged(tiny_models):
+    _need_gpu()
+    from rapidocrvl_b200 import _lib
+
+    cfg, rt, _ = _pair(tiny_models["q8"], "q8")
+    seq = rt.new_sequence(2)
+    rt.step([seq], ids=[1])
+    rt.step([seq], ids=[2])
+    with pytest.raises(_lib.OcrvlError):
+        rt.step([seq], ids=[3])  # full
+    assert len(seq) == 2
+    seq2 = rt.new_sequence(4)
+    with pytest.raises(_lib.OcrvlError):
+        rt.step([seq2], ids=[cfg.vocab_size + 5])
+    assert len(seq2) == 0
+
+
+@pytest.mark.slow
+@pytest.mark.parametrize("q", ["q4", "q8"])
+def test_bench_model_greedy_32(q):
+    """Benchmark-size decoder: 32 greedy ids after a 512-token prompt match."""
+    _need_gpu()
+    d = synth.ensure("bench", q)
+    cfg, rt, orc = _pair(d, q)
+    ids = synth.random_prompt(512, cfg.vocab_size, 0)
+    got = rt.generate_with_options(ids, GenerateOptions(max_new_tokens=32, eos_token_ids=[]))
+    want = orc.generate(ids, 32, eos=[])
+    assert got.tokens == want
