@@ -130,6 +130,24 @@ int ocrvl_step(ocrvl_model *m, ocrvl_seq *const *seqs, int n, const int32_t *ids
 int ocrvl_generate_greedy(ocrvl_model *m, const int32_t *ids, int n_ids, int max_new, const int32_t *eos,
                           int n_eos, int32_t *out, int out_cap, int *n_out);
 
+/* Greedy decode of `steps` tokens for n sequences with the token feedback
+ * kept on the device (the decode loop of GenerateWithOptions,
+ * internal/model/model.go:1538-1568, without the per-token EOS check): the
+ * step kernel writes each argmax id and advances its own parameters, so no
+ * host round trip happens between tokens.  first_ids: the n ids to feed
+ * first; out_ids: steps*n generated ids (step-major).  KV pages for all
+ * steps are reserved before the first launch. */
+int ocrvl_decode_greedy_device(ocrvl_model *m, ocrvl_seq *const *seqs, int n, const int32_t *first_ids, int steps,
+                               int32_t *out_ids);
+
+/* The model's CUDA stream (a cudaStream_t) for callers that time or order
+ * work against the engine's launches; no reference counterpart. */
+void *ocrvl_model_stream(ocrvl_model *m);
+
+/* Host<->device bytes one ocrvl_step call of n sequences moves besides
+ * embeddings and logits (step parameters in, ids and status out). */
+int ocrvl_step_io_bytes(const ocrvl_model *m, int n, int64_t *h2d, int64_t *d2h);
+
 /* ---- op level: device pointers, optional cudaStream_t as void* --------
  * Kernel-level entry points for parity tests and for callers that hold
  * their own device buffers; each names the internal/tensor function whose

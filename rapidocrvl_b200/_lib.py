@@ -63,6 +63,9 @@ SIGNATURES = {
     "ocrvl_seq_read_kv": (I, [P, I, P, P]),
     "ocrvl_step": (I, [P, P, I, P, P, P, I, P, P]),
     "ocrvl_generate_greedy": (I, [P, P, I, I, P, I, P, I, C.POINTER(I)]),
+    "ocrvl_decode_greedy_device": (I, [P, P, I, P, I, P]),
+    "ocrvl_model_stream": (P, [P]),
+    "ocrvl_step_io_bytes": (I, [P, I, C.POINTER(I64), C.POINTER(I64)]),
     "ocrvl_op_rowsum": (I, [I, I, I, P, P, P]),
     "ocrvl_op_matvec": (I, [I, I, I, P, P, P, I, P, P, F, P, P]),
     "ocrvl_op_matvec_add_rmsnorm": (I, [I, I, I, P, P, P, I, P, P, I, P, F, P, P, P]),

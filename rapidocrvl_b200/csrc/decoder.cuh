@@ -3,8 +3,10 @@
 //
 // Every stage is a __device__ "phase" that walks its work items with a
 // grid-stride loop, so the same code runs as a standalone kernel (op tests,
-// CUDA-graph step) or inside the persistent step kernel (engine.cu), where
-// phases are separated by grid barriers.
+// per-phase launches) or inside the persistent step kernel (engine.cu), where
+// phases are separated by grid barriers.  Phases read the model/step context
+// through a pointer to a Ctx in global memory and keep their arguments in
+// shared memory, so no large per-thread stack frames exist.
 #pragma once
 #include <cuda_runtime.h>
 #include <stdint.h>
@@ -16,9 +18,9 @@ namespace ocrvl {
 constexpr int kMaxBatch = 8;      // sequences per GEMV step
 constexpr int kThreads = 256;     // threads per block, every phase
 constexpr int kPageTokens = 16;   // tokens per KV page
-constexpr int kScoreChunk = 32;   // tokens per score work item
-constexpr int kPVChunk = 64;      // tokens per softmax/value work item
-constexpr int kHeadDim = 128;     // head size the attention phases support
+constexpr int kAttnChunk = 32;    // tokens per attention work item
+constexpr int kHeadDim = 128;     // head size the attention phase supports
+constexpr int kMaxGroup = 8;      // q heads per kv head
 constexpr int kFusedWorkers = 8;  // reference GOMAXPROCS partition for fused sums
 
 enum QType { QT_Q8 = 1000, QT_Q4 = 1001, QT_Q6 = 1002 };
@@ -62,14 +64,19 @@ struct Ctx {
   float *kv_pool;                    // pages of [L][2][KVH][16][D] f32
   long long page_floats;
   // step work buffers
-  float *h, *vbuf, *qkv, *head, *g, *scores, *partial, *logits;
-  unsigned long long *argkey;
-  int *tok_out;
+  float *h, *vbuf, *qkv, *head, *g, *logits;
+  float *part_o;                     // [B][QH][max_chunks][D] attention chunk sums
+  float *part_ml;                    // [B][QH][max_chunks][2] chunk max / sum
+  float *part_t;                     // [B][QH][D] raw-score tail sums
+  unsigned long long *argkey;        // [B]
+  int *tok_out;                      // [B] ids, then the error word
   int max_ctx, max_chunks;
-  const StepParams *sp;
-  unsigned *pv_count;                // [kMaxBatch][KVH] chunk arrivals
-  // persistent-kernel barrier state
-  unsigned *bar_count, *bar_gen;
+  StepParams *sp;
+  unsigned *attn_count;              // [B][KVH] chunk arrivals
+  unsigned *lm_count;                // lm_head block arrivals
+  int *hist, *hist_pos;              // device-side greedy loop: ids [steps][M], write index
+  // persistent-kernel barrier: monotonic arrival counter and error word
+  unsigned *bar_count;
   int *err;
   // optional step trace: per phase [start, prologue end, phase end (max over
   // blocks), barrier exit] in %globaltimer ns
@@ -81,7 +88,6 @@ __device__ __forceinline__ unsigned long long gtimer() {
   asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
   return t;
 }
-
 // ---------------------------------------------------------------------------
 // Small block-level helpers
 // ---------------------------------------------------------------------------
@@ -125,6 +131,7 @@ __device__ __forceinline__ int block_sum_int(int v, int *red) {
 __device__ float ss_rmsnorm(const float *x, int n, float *red) {
   if (threadIdx.x < 64) {
     float a = 0.0f;
+#pragma unroll 1
     for (int c = threadIdx.x; c < n; c += 64) a = __fmaf_rn(x[c], x[c], a);
     red[threadIdx.x] = a;
   }
@@ -207,11 +214,12 @@ enum { PRO_PLAIN = 0, PRO_RMSNORM = 1, PRO_ADDNORM = 2 };
 
 struct XIn {
   // VNNI types: xq (uint8, offset 128) per sequence; Q4 stores even columns
-  // then odd columns.  Q8: xf fp32 per sequence.
+  // then odd columns.  Q8: xf fp32 per sequence.  sx / sumq: per-sequence
+  // activation scale and sum of xq (shared memory).
   uint8_t *xq;
   float *xf;
-  float sx[kMaxBatch];
-  int sumq[kMaxBatch];
+  const float *sx;
+  const int *sumq;
 };
 
 // Copies n floats (n % 4 == 0, 16-byte aligned) global -> shared; every
@@ -263,18 +271,20 @@ __device__ __forceinline__ void norm_apply(float *x, const float *w, int n, floa
   }
 }
 
-// Shared-memory layout of the prologue: [red 320 f32][tmp n f32][x area].
-__device__ void gemv_prologue(int qt, int M, const float *src, int ld, int n, int mode,
-                              const float *w, float eps, float *smem, XIn &xin) {
+// Shared-memory layout of the prologue: [red 320 f32 (sx at 304.., sumq at
+// 312..)][tmp n f32][x area].  Out of line: every GEMV phase shares one copy.
+__device__ __noinline__ void gemv_prologue(int qt, int M, const float *src, int ld, const int *tok, int n,
+                                           int mode, const float *w, float eps, float *smem) {
   float *red = smem;
+  float *sxs = smem + 304;
+  int *sqs = (int *)(smem + 312);
   float *tmp = smem + 320;
   uint8_t *area = (uint8_t *)(tmp + n);
-  bool vnni = qt != QT_Q8;
-  xin.xq = area;
-  xin.xf = (float *)area;
+  const bool vnni = qt != QT_Q8;
+#pragma unroll 1
   for (int m = 0; m < M; m++) {
-    const float *s = src + (size_t)m * ld;
-    float *dst = vnni ? tmp : xin.xf + (size_t)m * n;
+    const float *s = src + (size_t)(tok ? tok[m] : m) * ld;
+    float *dst = vnni ? tmp : (float *)area + (size_t)m * n;
     g2s_f32(dst, s, n);
     __syncthreads();
     if (mode != PRO_PLAIN) {
@@ -285,6 +295,7 @@ __device__ void gemv_prologue(int qt, int M, const float *src, int ld, int n, in
     }
     if (vnni) {
       float mx = 0.0f;
+#pragma unroll 1
       for (int i = threadIdx.x; i < n; i += kThreads) mx = fmaxf(mx, fabsf(dst[i]));
       mx = block_max(mx, red);
       float sx = 1.0f, inv = 0.0f;
@@ -292,76 +303,117 @@ __device__ void gemv_prologue(int qt, int M, const float *src, int ld, int n, in
         sx = __fdiv_rn(mx, 127.0f);
         inv = __fdiv_rn(1.0f, sx);
       }
-      uint8_t *q = xin.xq + (size_t)m * n;
+      uint8_t *q = area + (size_t)m * n;
+      const int half = qt == QT_Q4 ? n / 2 : 0;
       int acc = 0;
+#pragma unroll 1
       for (int i = threadIdx.x; i < n; i += kThreads) {
-        int v = 128;
-        if (mx != 0.0f) {
-          float f = __fadd_rn(rintf(__fmul_rn(dst[i], inv)), 128.0f);
-          f = fminf(fmaxf(f, 0.0f), 255.0f);
-          v = (int)f;
-        }
+        float f = __fadd_rn(rintf(__fmul_rn(dst[i], inv)), 128.0f);
+        int v = mx != 0.0f ? (int)fminf(fmaxf(f, 0.0f), 255.0f) : 128;
         acc += v;
-        if (qt == QT_Q4)
-          q[(i & 1) * (n / 2) + (i >> 1)] = (uint8_t)v;  // even | odd halves
-        else
-          q[i] = (uint8_t)v;
+        q[half ? (i & 1) * half + (i >> 1) : i] = (uint8_t)v;  // Q4: even | odd halves
       }
       acc = block_sum_int(acc, (int *)red);
-      xin.sx[m] = sx;
-      xin.sumq[m] = acc;
+      if (threadIdx.x == 0) {
+        sxs[m] = sx;
+        sqs[m] = acc;
+      }
       __syncthreads();
     }
   }
   __syncthreads();
 }
 
+__device__ __forceinline__ XIn gemv_inputs(int n, float *smem) {
+  XIn x;
+  x.xq = (uint8_t *)(smem + 320 + n);
+  x.xf = (float *)x.xq;
+  x.sx = smem + 304;
+  x.sumq = (const int *)(smem + 312);
+  return x;
+}
+
 __device__ __forceinline__ size_t gemv_smem_bytes(int qt, int M, int n) {
   size_t area = qt == QT_Q8 ? (size_t)M * n * 4 : (size_t)M * n;
   return (320 + (size_t)n) * 4 + area;
 }
+// ---------------------------------------------------------------------------
+// Bulk copies (TMA, cp.async.bulk) and mbarriers
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t smem_u32(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_fence_init() { asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory"); }
+__device__ __forceinline__ void mbar_expect_tx(uint64_t *bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
+}
+// global -> shared bulk copy; src and dst 16-byte aligned, bytes % 16 == 0
+__device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   smem_u32(dst)),
+               "l"(src), "r"(bytes), "r"(smem_u32(bar))
+               : "memory");
+}
+// Bounded wait for phase `parity` of an mbarrier.  On timeout the error word
+// is set and false returned.
+constexpr long long kMbarSpins = 1ll << 24;
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, int *err) {
+  uint32_t done = 0;
+  long long spins = 0;
+  while (true) {
+    asm volatile("{ .reg .pred p; mbarrier.try_wait.parity.shared.b64 p, [%1], %2; selp.u32 %0, 1, 0, p; }"
+                 : "=r"(done)
+                 : "r"(smem_u32(bar)), "r"(parity)
+                 : "memory");
+    if (done) return true;
+    if (++spins > kMbarSpins) {
+      if (err) atomicExch(err, 1);
+      return false;
+    }
+  }
+}
+
+__device__ __forceinline__ uint4 lds16(const void *p) {
+  uint4 v;
+  asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(smem_u32(p)));
+  return v;
+}
+__device__ __forceinline__ uint32_t lds4(const void *p) {
+  uint32_t v;
+  asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(smem_u32(p)));
+  return v;
+}
 
 // ---------------------------------------------------------------------------
-// Row dot products over a batch of RB rows.  All RB rows' weight loads of a
-// chunk are issued before any arithmetic so that each lane keeps RB 16-byte
-// loads in flight.  Results: out[r][m] = finished row value (per-type
+// Row dot products over a batch of RB rows whose packed weights are staged in
+// shared memory (rp[r] = row start).  out[r][m] = finished row value (per-type
 // epilogue arithmetic applied), valid on the lane with (lane % lpr) == 0.
 // ---------------------------------------------------------------------------
-
-__device__ __forceinline__ uint4 ld_stream16(const void *p) {
-  uint4 v;
-  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
-               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
-               : "l"(p));
-  return v;
-}
-__device__ __forceinline__ uint32_t ld_stream4(const void *p) {
-  uint32_t v;
-  asm volatile("ld.global.nc.L1::no_allocate.u32 %0, [%1];" : "=r"(v) : "l"(p));
-  return v;
-}
 
 // Q4 (int8-activation mode): per 16-byte chunk, low nibbles hold even columns
 // and high nibbles odd columns; dp4a of the unsigned nibbles against the even /
 // odd halves of xq gives sum((q+8)*xq), corrected by 8*sum(xq).
 template <int M_, int RB>
-__device__ __forceinline__ void dot_q4(const DMat &A, const int *rows, int M, const XIn &x, int li, int lpr,
-                                       float (*out)[M_]) {
-  const int P = A.pitch, CH = P >> 4, n = A.cols;
+__device__ __forceinline__ void dot_q4(const DMat &A, const uint8_t *const *rp, const int *rows, int M, const XIn &x,
+                                       int li, int lpr, float (*out)[M_]) {
+  const int CH = A.pitch >> 4, n = A.cols;
   uint32_t acc[RB][M_];
 #pragma unroll
   for (int r = 0; r < RB; r++)
 #pragma unroll
     for (int m = 0; m < M_; m++) acc[r][m] = 0;
+#pragma unroll 1
   for (int k = li; k < CH; k += lpr) {
     uint4 wv[RB];
 #pragma unroll
-    for (int r = 0; r < RB; r++) wv[r] = ld_stream16(A.w + (size_t)rows[r] * P + 16 * k);
+    for (int r = 0; r < RB; r++) wv[r] = lds16(rp[r] + 16 * k);
 #pragma unroll
     for (int m = 0; m < M_; m++) {
       if (m >= M) break;
-      const uint4 xe = *(const uint4 *)(x.xq + (size_t)m * n + 16 * k);
-      const uint4 xo = *(const uint4 *)(x.xq + (size_t)m * n + n / 2 + 16 * k);
+      const uint4 xe = lds16(x.xq + (size_t)m * n + 16 * k);
+      const uint4 xo = lds16(x.xq + (size_t)m * n + n / 2 + 16 * k);
       const uint32_t e4[4] = {xe.x, xe.y, xe.z, xe.w}, o4[4] = {xo.x, xo.y, xo.z, xo.w};
 #pragma unroll
       for (int r = 0; r < RB; r++) {
@@ -376,14 +428,23 @@ __device__ __forceinline__ void dot_q4(const DMat &A, const int *rows, int M, co
   }
 #pragma unroll
   for (int r = 0; r < RB; r++) {
-    const int32_t rs = A.rowsum[rows[r]];
-    const float sw = A.scale[rows[r]];
 #pragma unroll
     for (int m = 0; m < M_; m++) {
       if (m >= M) break;
       uint32_t a = acc[r][m];
       for (int o = lpr >> 1; o > 0; o >>= 1) a += __shfl_xor_sync(0xffffffffu, a, o);
-      out[r][m] = vnni_finalize((int32_t)a - 8 * x.sumq[m], rs, x.sx[m], sw);
+      acc[r][m] = a;
+    }
+  }
+  if ((li) != 0) return;
+#pragma unroll
+  for (int r = 0; r < RB; r++) {
+    const int32_t rs = __ldg(A.rowsum + rows[r]);
+    const float sw = __ldg(A.scale + rows[r]);
+#pragma unroll
+    for (int m = 0; m < M_; m++) {
+      if (m >= M) break;
+      out[r][m] = vnni_finalize((int32_t)acc[r][m] - 8 * x.sumq[m], rs, x.sx[m], sw);
     }
   }
 }
@@ -394,58 +455,56 @@ __device__ __forceinline__ uint32_t q6_spread(uint32_t g) {
   return (g & 0x3Fu) | ((g << 2) & 0x3F00u) | ((g << 4) & 0x3F0000u) | ((g << 6) & 0x3F000000u);
 }
 template <int M_, int RB>
-__device__ __forceinline__ void dot_q6(const DMat &A, const int *rows, int M, const XIn &x, int li, int lpr,
-                                       float (*out)[M_]) {
-  const int P = A.pitch, CH = P / 48, n = A.cols;
+__device__ __forceinline__ void dot_q6(const DMat &A, const uint8_t *const *rp, const int *rows, int M, const XIn &x,
+                                       int li, int lpr, float (*out)[M_]) {
+  const int CH = A.pitch / 48, n = A.cols;
   uint32_t acc[RB][M_];
 #pragma unroll
   for (int r = 0; r < RB; r++)
 #pragma unroll
     for (int m = 0; m < M_; m++) acc[r][m] = 0;
+#pragma unroll 1
   for (int k = li; k < CH; k += lpr) {
-    uint4 wv[RB][3];
-#pragma unroll
-    for (int r = 0; r < RB; r++)
-#pragma unroll
-      for (int q = 0; q < 3; q++) wv[r][q] = ld_stream16(A.w + (size_t)rows[r] * P + 48 * k + 16 * q);
 #pragma unroll
     for (int r = 0; r < RB; r++) {
-      const uint32_t w[12] = {wv[r][0].x, wv[r][0].y, wv[r][0].z, wv[r][0].w, wv[r][1].x, wv[r][1].y,
-                              wv[r][1].z, wv[r][1].w, wv[r][2].x, wv[r][2].y, wv[r][2].z, wv[r][2].w};
-      uint32_t f[16];
+      const uint4 wa = lds16(rp[r] + 48 * k), wb = lds16(rp[r] + 48 * k + 16), wc = lds16(rp[r] + 48 * k + 32);
+      const uint32_t w[12] = {wa.x, wa.y, wa.z, wa.w, wb.x, wb.y, wb.z, wb.w, wc.x, wc.y, wc.z, wc.w};
 #pragma unroll
       for (int t = 0; t < 4; t++) {
-        uint32_t w0 = w[3 * t], w1 = w[3 * t + 1], w2 = w[3 * t + 2];
-        f[4 * t + 0] = q6_spread(w0 & 0xFFFFFFu);
-        f[4 * t + 1] = q6_spread(__funnelshift_r(w0, w1, 24) & 0xFFFFFFu);
-        f[4 * t + 2] = q6_spread(__funnelshift_r(w1, w2, 16) & 0xFFFFFFu);
-        f[4 * t + 3] = q6_spread(w2 >> 8);
-      }
+        const uint32_t w0 = w[3 * t], w1 = w[3 * t + 1], w2 = w[3 * t + 2];
+        const uint32_t f0 = q6_spread(w0 & 0xFFFFFFu), f1 = q6_spread(__funnelshift_r(w0, w1, 24) & 0xFFFFFFu);
+        const uint32_t f2 = q6_spread(__funnelshift_r(w1, w2, 16) & 0xFFFFFFu), f3 = q6_spread(w2 >> 8);
 #pragma unroll
-      for (int m = 0; m < M_; m++) {
-        if (m >= M) break;
-        const uint4 *xv = (const uint4 *)(x.xq + (size_t)m * n + 64 * k);
-#pragma unroll
-        for (int q = 0; q < 4; q++) {
-          uint4 xx = xv[q];
-          acc[r][m] = __dp4a(f[4 * q + 0], xx.x, acc[r][m]);
-          acc[r][m] = __dp4a(f[4 * q + 1], xx.y, acc[r][m]);
-          acc[r][m] = __dp4a(f[4 * q + 2], xx.z, acc[r][m]);
-          acc[r][m] = __dp4a(f[4 * q + 3], xx.w, acc[r][m]);
+        for (int m = 0; m < M_; m++) {
+          if (m >= M) break;
+          const uint4 xx = lds16(x.xq + (size_t)m * n + 64 * k + 16 * t);
+          acc[r][m] = __dp4a(f0, xx.x, acc[r][m]);
+          acc[r][m] = __dp4a(f1, xx.y, acc[r][m]);
+          acc[r][m] = __dp4a(f2, xx.z, acc[r][m]);
+          acc[r][m] = __dp4a(f3, xx.w, acc[r][m]);
         }
       }
     }
   }
 #pragma unroll
   for (int r = 0; r < RB; r++) {
-    const int32_t rs = A.rowsum[rows[r]];
-    const float sw = A.scale[rows[r]];
 #pragma unroll
     for (int m = 0; m < M_; m++) {
       if (m >= M) break;
       uint32_t a = acc[r][m];
       for (int o = lpr >> 1; o > 0; o >>= 1) a += __shfl_xor_sync(0xffffffffu, a, o);
-      out[r][m] = vnni_finalize((int32_t)a - 32 * x.sumq[m], rs, x.sx[m], sw);
+      acc[r][m] = a;
+    }
+  }
+  if (li != 0) return;
+#pragma unroll
+  for (int r = 0; r < RB; r++) {
+    const int32_t rs = __ldg(A.rowsum + rows[r]);
+    const float sw = __ldg(A.scale + rows[r]);
+#pragma unroll
+    for (int m = 0; m < M_; m++) {
+      if (m >= M) break;
+      out[r][m] = vnni_finalize((int32_t)acc[r][m] - 32 * x.sumq[m], rs, x.sx[m], sw);
     }
   }
 }
@@ -455,9 +514,8 @@ __device__ __forceinline__ void dot_q6(const DMat &A, const int *rows, int M, co
 // block (accumulator t/4, ZMM lanes 4(t%4)..+3); the accumulator pairs are
 // reduced with xor-4/8/16 shuffles and the 16-lane tree with xor-2/1.
 template <int M_, int RB>
-__device__ __forceinline__ void dot_q8(const DMat &A, const int *rows, int M, const XIn &x, int lane,
-                                       float (*out)[M_]) {
-  constexpr int JB = 4;
+__device__ __forceinline__ void dot_q8(const DMat &A, const uint8_t *const *rp, const int *rows, int M, const XIn &x,
+                                       int lane, float (*out)[M_]) {
   const int n = A.cols, NB = n >> 7;
   float acc[RB][M_][4];
 #pragma unroll
@@ -466,34 +524,30 @@ __device__ __forceinline__ void dot_q8(const DMat &A, const int *rows, int M, co
     for (int m = 0; m < M_; m++)
 #pragma unroll
       for (int i = 0; i < 4; i++) acc[r][m][i] = 0.0f;
-  for (int j0 = 0; j0 < NB; j0 += JB) {
-    uint32_t wv[RB][JB];
+#pragma unroll 1
+  for (int j = 0; j < NB; j++) {
+    uint32_t wv[RB];
 #pragma unroll
-    for (int r = 0; r < RB; r++)
+    for (int r = 0; r < RB; r++) wv[r] = lds4(rp[r] + 128 * j + 4 * lane);
 #pragma unroll
-      for (int jj = 0; jj < JB; jj++)
-        wv[r][jj] = (j0 + jj < NB) ? ld_stream4(A.w + (size_t)rows[r] * A.pitch + 128 * (j0 + jj) + 4 * lane) : 0u;
+    for (int m = 0; m < M_; m++) {
+      if (m >= M) break;
+      const uint4 xb = lds16(x.xf + (size_t)m * n + 128 * j + 4 * lane);
+      const float x0 = __uint_as_float(xb.x), x1 = __uint_as_float(xb.y);
+      const float x2 = __uint_as_float(xb.z), x3 = __uint_as_float(xb.w);
 #pragma unroll
-    for (int jj = 0; jj < JB; jj++) {
-      if (j0 + jj >= NB) break;
-#pragma unroll
-      for (int m = 0; m < M_; m++) {
-        if (m >= M) break;
-        const float4 xv = *(const float4 *)(x.xf + (size_t)m * n + 128 * (j0 + jj) + 4 * lane);
-#pragma unroll
-        for (int r = 0; r < RB; r++) {
-          const uint32_t w = wv[r][jj];
-          acc[r][m][0] = __fmaf_rn((float)(int8_t)(w & 0xFF), xv.x, acc[r][m][0]);
-          acc[r][m][1] = __fmaf_rn((float)(int8_t)((w >> 8) & 0xFF), xv.y, acc[r][m][1]);
-          acc[r][m][2] = __fmaf_rn((float)(int8_t)((w >> 16) & 0xFF), xv.z, acc[r][m][2]);
-          acc[r][m][3] = __fmaf_rn((float)(int8_t)(w >> 24), xv.w, acc[r][m][3]);
-        }
+      for (int r = 0; r < RB; r++) {
+        const uint32_t w = wv[r];
+        acc[r][m][0] = __fmaf_rn((float)(int8_t)(w & 0xFF), x0, acc[r][m][0]);
+        acc[r][m][1] = __fmaf_rn((float)(int8_t)((w >> 8) & 0xFF), x1, acc[r][m][1]);
+        acc[r][m][2] = __fmaf_rn((float)(int8_t)((w >> 16) & 0xFF), x2, acc[r][m][2]);
+        acc[r][m][3] = __fmaf_rn((float)(int8_t)(w >> 24), x3, acc[r][m][3]);
       }
     }
   }
 #pragma unroll
   for (int r = 0; r < RB; r++) {
-    const float sw = A.scale[rows[r]];
+    const float sw = __ldg(A.scale + rows[r]);
 #pragma unroll
     for (int m = 0; m < M_; m++) {
       if (m >= M) break;
@@ -524,14 +578,14 @@ __device__ __forceinline__ int lanes_per_row(int qt, const DMat &A) {
 }
 
 template <int QT, int M_, int RB>
-__device__ __forceinline__ void rows_dot(const DMat &A, const int *rows, int M, const XIn &x, int lane, int lpr,
-                                         float (*out)[M_]) {
+__device__ __forceinline__ void rows_dot(const DMat &A, const uint8_t *const *rp, const int *rows, int M,
+                                         const XIn &x, int lane, int lpr, float (*out)[M_]) {
   if (QT == QT_Q4)
-    dot_q4<M_, RB>(A, rows, M, x, lane % lpr, lpr, out);
+    dot_q4<M_, RB>(A, rp, rows, M, x, lane % lpr, lpr, out);
   else if (QT == QT_Q6)
-    dot_q6<M_, RB>(A, rows, M, x, lane % lpr, lpr, out);
+    dot_q6<M_, RB>(A, rp, rows, M, x, lane % lpr, lpr, out);
   else
-    dot_q8<M_, RB>(A, rows, M, x, lane, out);
+    dot_q8<M_, RB>(A, rp, rows, M, x, lane, out);
 }
 
 // ---------------------------------------------------------------------------
@@ -540,22 +594,26 @@ __device__ __forceinline__ void rows_dot(const DMat &A, const int *rows, int M, 
 enum { EPI_STORE = 0, EPI_RESID = 1, EPI_SWIGLU = 2, EPI_ARGMAX = 3 };
 enum { RESID_ALWAYS = 0, RESID_ATTN = 1, RESID_NEVER = 2, RESID_MASK = 3 };
 
+// Arguments of one GEMV phase; built in shared memory by the caller.
 struct GemvArgs {
   DMat A, B;                // B: up matrix for EPI_SWIGLU
   int row_begin, row_end;   // rows of A to compute
-  const float *src;         // input vectors [M][ld]
-  int ld;
+  const float *src;         // input vectors [M][ld] (or rows tok[m] when src_tok)
+  int ld, src_tok;
+  float *copy_src;          // when set, block 0 stores the prologue's input rows here ([M][ld])
   int mode;                 // PRO_*
   const float *norm_w;
   int epi;
   float *out;               // EPI_STORE / EPI_SWIGLU: [M][ldo]
   int ldo;
-  float *resid;             // EPI_RESID: residual [M][ldo] (updated when in_place[m])
+  float *resid;             // EPI_RESID: residual [M][ldo] (updated when in place)
   float *vout;              // EPI_RESID: v = resid + out, [M][ldo]
   int resid_mode;           // EPI_RESID: RESID_*
   int in_place_mask;        // RESID_MASK: bit m set -> update resid
   unsigned long long *argkey;  // EPI_ARGMAX: [M]
   float *logits;            // EPI_ARGMAX: optional full scores [M][ldo]
+  int argmax_finish;        // EPI_ARGMAX: last block turns keys into ids
+  int feed;                 // EPI_ARGMAX finish: advance the step parameters
   unsigned long long *tslot;   // optional trace slot of this phase
 };
 
@@ -587,11 +645,89 @@ __device__ __forceinline__ void prefetch_gemv_slab(const DMat &A, int row_begin,
   prefetch_l2(A.rowsum + lo, (size_t)(hi - lo) * 4);
 }
 
+// Weight staging: each block streams its slab of packed rows through a ring
+// of kStages shared-memory stages with TMA bulk copies; the copies of the
+// first stages are issued before the input prologue so weight transfer
+// overlaps the normalisation / quantisation of the input.
+constexpr int kStageBytes = 32768;
+constexpr int kStagesM1 = 3;   // stages for the single-sequence form
+constexpr int kStagesMB = 2;   // stages for the batched form
+
+__host__ __device__ __forceinline__ size_t gemv_prologue_bytes(int qt, int nvec, int n) {
+  size_t area = qt == QT_Q8 ? (size_t)nvec * n * 4 : (size_t)nvec * n;
+  return ((320 + (size_t)n) * 4 + area + 127) / 128 * 128;
+}
+__host__ __device__ __forceinline__ size_t gemv_smem_total(int qt, int nvec, int n, int stages) {
+  return gemv_prologue_bytes(qt, nvec, n) + (size_t)stages * kStageBytes;
+}
+
+// Last block of the lm_head phase: keys -> ids (ties -> lowest id), key and
+// counter reset, and (device-side greedy loop) the next step's parameters:
+// tok = argmax, len + 1, position (len, len, len).
+__device__ void argmax_finish(const Ctx &c, int M, int feed) {
+  StepParams &sp = *c.sp;
+  if (threadIdx.x < M) {
+    const int m = threadIdx.x;
+    unsigned long long k = __ldcg(c.argkey + m);
+    int id = sp.need[m] ? argmax_key_row(k) : -1;
+    c.tok_out[m] = id;
+    c.argkey[m] = 0ull;
+    if (feed) {
+      int step = *c.hist_pos;
+      c.hist[(size_t)step * M + m] = id;
+      int len = sp.len[m] + 1;
+      sp.tok[m] = id;
+      sp.len[m] = len;
+      sp.pos[m][0] = sp.pos[m][1] = sp.pos[m][2] = len;
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    if (feed) {
+      *c.hist_pos += 1;
+      sp.max_n += 1;
+    }
+    *c.lm_count = 0u;
+  }
+}
+
 template <int QT, int M_, int RB>
-__device__ void phase_gemv_t(const Ctx &c, const GemvArgs &a, int M, float *smem) {
+__device__ __noinline__ void phase_gemv_t(const Ctx *cp, const GemvArgs *ap, int M, float *smem) {
+  const Ctx &c = *cp;
+  const GemvArgs &a = *ap;
+  constexpr int kSt = M_ == 1 ? kStagesM1 : kStagesMB;
+  __shared__ __align__(8) uint64_t full[kSt];
   const int qt = QT;
-  XIn x;
-  gemv_prologue(qt, M, a.src, a.ld, a.A.cols, a.mode, a.norm_w, c.eps, smem, x);
+  const int P = a.A.pitch;
+  const bool two = a.epi == EPI_SWIGLU;
+  int lo, hi;
+  gemv_slab(a.row_begin, a.row_end, blockIdx.x, gridDim.x, lo, hi);
+  uint8_t *stage = (uint8_t *)smem + gemv_prologue_bytes(qt, M_ == 1 ? 1 : kMaxBatch, a.A.cols);
+  const int srows = kStageBytes / (P * (two ? 2 : 1));  // rows per stage
+  const int nst = (hi - lo + srows - 1) / srows;
+  auto issue = [&](int st) {
+    const int r0 = lo + st * srows, nr = min(srows, hi - r0);
+    uint8_t *buf = stage + (size_t)(st % kSt) * kStageBytes;
+    const uint32_t bytes = (uint32_t)nr * P;
+    mbar_expect_tx(&full[st % kSt], two ? 2 * bytes : bytes);
+    bulk_g2s(buf, a.A.w + (size_t)r0 * P, bytes, &full[st % kSt]);
+    if (two) bulk_g2s(buf + (size_t)srows * P, a.B.w + (size_t)r0 * P, bytes, &full[st % kSt]);
+  };
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < kSt; i++) mbar_init(&full[i], 1);
+    mbar_fence_init();
+    for (int st = 0; st < nst && st < kSt; st++) issue(st);
+  }
+  gemv_prologue(qt, M, a.src, a.ld, a.src_tok ? c.sp->tok : nullptr, a.A.cols, a.mode, a.norm_w, c.eps, smem);
+  const XIn x = gemv_inputs(a.A.cols, smem);
+  if (a.copy_src && blockIdx.x == 0) {
+    // layer 0: the embedding rows the prologue gathered become the residual
+    for (int m = 0; m < M; m++) {
+      const float4 *s4 = (const float4 *)(a.src + (size_t)c.sp->tok[m] * a.ld);
+      float4 *d4 = (float4 *)(a.copy_src + (size_t)m * a.ld);
+      for (int i = threadIdx.x; i < a.ld / 4; i += kThreads) d4[i] = __ldg(s4 + i);
+    }
+  }
   if (a.tslot && blockIdx.x == 0 && threadIdx.x == 0) a.tslot[1] = gtimer();
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int lpr = lanes_per_row(qt, a.A);
@@ -617,50 +753,61 @@ __device__ void phase_gemv_t(const Ctx &c, const GemvArgs &a, int M, float *smem
       in_place |= (ip ? 1 : 0) << m;
     }
   }
-  int blo, bhi, lo, hi;
-  gemv_slab(a.row_begin, a.row_end, blockIdx.x, gridDim.x, blo, bhi);
-  gemv_slab(blo, bhi, warp, kThreads / 32, lo, hi);  // this warp's contiguous rows
-  const int per_group = rpw * RB;
-  const int ngroups = (hi - lo + per_group - 1) / per_group;
   unsigned long long best[M_];
 #pragma unroll
   for (int m = 0; m < M_; m++) best[m] = 0ull;
-  for (int gi = 0; gi < ngroups; gi++) {
-    int rows[RB];
-    bool valid[RB];
+  const int per_group = rpw * RB;
+  bool ok = true;
+#pragma unroll 1
+  for (int st = 0; st < nst; st++) {
+    const int r0 = lo + st * srows, nr = min(srows, hi - r0);
+    const uint8_t *buf = stage + (size_t)(st % kSt) * kStageBytes;
+    if (!mbar_wait(&full[st % kSt], (uint32_t)((st / kSt) & 1), c.err)) ok = false;
+    const int ngroups = (nr + per_group - 1) / per_group;
+#pragma unroll 1
+    for (int gi = warp; ok && gi < ngroups; gi += kThreads / 32) {
+      int rows[RB];
+      const uint8_t *rpa[RB], *rpb[RB];
+      bool valid[RB];
 #pragma unroll
-    for (int r = 0; r < RB; r++) {
-      int row = lo + gi * per_group + r * rpw + sub;
-      valid[r] = row < hi;
-      rows[r] = valid[r] ? row : hi - 1;
-    }
-    float v[RB][M_], u[RB][M_];
-    rows_dot<QT, M_, RB>(a.A, rows, M, x, lane, lpr, v);
-    if (a.epi == EPI_SWIGLU) rows_dot<QT, M_, RB>(a.B, rows, M, x, lane, lpr, u);
-    if ((lane % lpr) != 0) continue;
+      for (int r = 0; r < RB; r++) {
+        int lr = gi * per_group + r * rpw + sub;
+        valid[r] = lr < nr;
+        lr = valid[r] ? lr : nr - 1;
+        rows[r] = r0 + lr;
+        rpa[r] = buf + (size_t)lr * P;
+        rpb[r] = buf + (size_t)(srows + lr) * P;
+      }
+      float v[RB][M_], u[RB][M_];
+      rows_dot<QT, M_, RB>(a.A, rpa, rows, M, x, lane, lpr, v);
+      if (two) rows_dot<QT, M_, RB>(a.B, rpb, rows, M, x, lane, lpr, u);
+      if ((lane % lpr) != 0) continue;
 #pragma unroll
-    for (int r = 0; r < RB; r++) {
-      if (!valid[r]) continue;
-      const int row = rows[r];
+      for (int r = 0; r < RB; r++) {
+        if (!valid[r]) continue;
+        const int row = rows[r];
 #pragma unroll
-      for (int m = 0; m < M_; m++) {
-        if (m >= M) break;
-        size_t o = (size_t)m * a.ldo + row;
-        if (a.epi == EPI_STORE) {
-          a.out[o] = v[r][m];
-        } else if (a.epi == EPI_RESID) {
-          float t = __fadd_rn(__ldcg(a.resid + o), v[r][m]);
-          a.vout[o] = t;
-          if ((in_place >> m) & 1) a.resid[o] = t;
-        } else if (a.epi == EPI_SWIGLU) {
-          a.out[o] = silu_mul(v[r][m], u[r][m]);
-        } else {
-          if (a.logits) a.logits[o] = v[r][m];
-          unsigned long long k = argmax_key(v[r][m], row);
-          best[m] = k > best[m] ? k : best[m];
+        for (int m = 0; m < M_; m++) {
+          if (m >= M) break;
+          size_t o = (size_t)m * a.ldo + row;
+          if (a.epi == EPI_STORE) {
+            a.out[o] = v[r][m];
+          } else if (a.epi == EPI_RESID) {
+            float t = __fadd_rn(__ldcg(a.resid + o), v[r][m]);
+            a.vout[o] = t;
+            if ((in_place >> m) & 1) a.resid[o] = t;
+          } else if (a.epi == EPI_SWIGLU) {
+            a.out[o] = silu_mul(v[r][m], u[r][m]);
+          } else {
+            if (a.logits) a.logits[o] = v[r][m];
+            unsigned long long k = argmax_key(v[r][m], row);
+            best[m] = k > best[m] ? k : best[m];
+          }
         }
       }
     }
+    __syncthreads();  // stage buffer free
+    if (threadIdx.x == 0 && st + kSt < nst) issue(st + kSt);
   }
   if (a.epi == EPI_ARGMAX) {
 #pragma unroll
@@ -673,46 +820,43 @@ __device__ void phase_gemv_t(const Ctx &c, const GemvArgs &a, int M, float *smem
       }
       if (lane == 0 && k) atomicMax(a.argkey + m, k);
     }
+    if (a.argmax_finish) {
+      __shared__ int is_last;
+      __threadfence();
+      __syncthreads();
+      if (threadIdx.x == 0) is_last = atomicAdd(c.lm_count, 1u) == gridDim.x - 1;
+      __syncthreads();
+      if (is_last) {
+        __threadfence();
+        argmax_finish(c, M, a.feed);
+      }
+    }
   }
   __syncthreads();
 }
 
-// Rows per warp batch: enough 16-byte loads in flight per lane at M = 1,
-// fewer as the per-row accumulator count grows with M.
+// Rows per warp batch: enough 16-byte loads in flight per lane at M = 1; one
+// row per batch for the batched (M > 1) form.
 template <int QT>
-__device__ void phase_gemv_q(const Ctx &c, const GemvArgs &a, int M, float *smem) {
-  constexpr int R1 = QT == QT_Q4 ? 8 : 4;
+__device__ __forceinline__ void phase_gemv_q(const Ctx *c, const GemvArgs *a, int M, float *smem) {
+  constexpr int R1 = 2;
   if (M <= 1)
     phase_gemv_t<QT, 1, R1>(c, a, M, smem);
-  else if (M <= 2)
-    phase_gemv_t<QT, 2, R1 / 2>(c, a, M, smem);
-  else if (M <= 4)
-    phase_gemv_t<QT, 4, (R1 / 4 > 0 ? R1 / 4 : 1)>(c, a, M, smem);
   else
-    phase_gemv_t<QT, 8, 1>(c, a, M, smem);
+    phase_gemv_t<QT, kMaxBatch, 1>(c, a, M, smem);
 }
 
-__device__ void phase_gemv(const Ctx &c, const GemvArgs &a, int M, float *smem) {
-  if (c.qtype == QT_Q4)
+__device__ __forceinline__ void phase_gemv(const Ctx *c, const GemvArgs *a, int M, float *smem) {
+  if (c->qtype == QT_Q4)
     phase_gemv_q<QT_Q4>(c, a, M, smem);
-  else if (c.qtype == QT_Q6)
+  else if (c->qtype == QT_Q6)
     phase_gemv_q<QT_Q6>(c, a, M, smem);
   else
     phase_gemv_q<QT_Q8>(c, a, M, smem);
 }
-
 // ---------------------------------------------------------------------------
-// Embedding gather (tokenEmbeddingInto, model.go:3251-3258)
+// KV cache and RoPE helpers
 // ---------------------------------------------------------------------------
-__device__ void phase_embed(const Ctx &c) {
-  const StepParams &sp = *c.sp;
-  size_t total = (size_t)sp.M * c.H;
-  for (size_t i = (size_t)blockIdx.x * kThreads + threadIdx.x; i < total; i += (size_t)gridDim.x * kThreads) {
-    int m = (int)(i / c.H), j = (int)(i % c.H);
-    c.h[i] = c.embed[(size_t)sp.tok[m] * c.H + j];
-  }
-}
-
 __device__ __forceinline__ float *kv_ptr(const Ctx &c, const int *bt, int layer, int kind, int kvh, int t) {
   int page = bt[t / kPageTokens];
   return c.kv_pool + (size_t)page * c.page_floats +
@@ -728,14 +872,6 @@ __device__ __forceinline__ void rope_pair(float &a, float &b, float cs, float sn
   b = nb;
 }
 
-// ---------------------------------------------------------------------------
-// Attention phase 1: RoPE of q/k, KV append, scores.
-// Items: (sequence, kv head, chunk of kScoreChunk tokens).  The item whose
-// chunk holds the new token appends its rotated k and its v to the paged
-// cache (kvCache.append, model.go:5593-5612).  Scores restate
-// cacheAttentionScores (model.go:4623-4795): (q.k)*1/sqrt(D), the dot in
-// the 8x16-slot order of the reference's 128-wide dot kernels.
-// ---------------------------------------------------------------------------
 __device__ __forceinline__ void rope4(float4 &a, float4 &b, const float *cs, const float *sn) {
   float ax[4] = {a.x, a.y, a.z, a.w}, bx[4] = {b.x, b.y, b.z, b.w};
 #pragma unroll
@@ -744,138 +880,34 @@ __device__ __forceinline__ void rope4(float4 &a, float4 &b, const float *cs, con
   b = make_float4(bx[0], bx[1], bx[2], bx[3]);
 }
 
-// cos/sin of frequencies i4*4 .. i4*4+3 for the M-RoPE position triple.
+// cos/sin of frequencies 4*i4 .. 4*i4+3 for the M-RoPE position triple.
 __device__ __forceinline__ void rope_cs4(const Ctx &c, const int *pos, int i4, float *cs, float *sn) {
   const int half = c.D / 2;
 #pragma unroll
   for (int j = 0; j < 4; j++) {
     int i = i4 * 4 + j;
     int p = pos[c.sec_axis[i]];
-    cs[j] = c.rope_cos[(size_t)p * half + i];
-    sn[j] = c.rope_sin[(size_t)p * half + i];
+    cs[j] = __ldg(c.rope_cos + (size_t)p * half + i);
+    sn[j] = __ldg(c.rope_sin + (size_t)p * half + i);
   }
 }
 
-__device__ void phase_scores(const Ctx &c, int layer, bool append_only, float *smem) {
-  const StepParams &sp = *c.sp;
-  const int G = c.QH / c.KVH, D = c.D, H4 = D / 8;  // H4: float4 per half head
-  const int qkvld = (c.QH + 2 * c.KVH) * D;
-  const int nchunk = (sp.max_n + kScoreChunk - 1) / kScoreChunk;
-  const int items = sp.M * c.KVH * nchunk;
-  float *qs = smem;                       // [G][D]
-  float *ks = smem + G * D;               // [kScoreChunk][D+1]
-  for (int it = blockIdx.x; it < items; it += gridDim.x) {
-    int m = it / (c.KVH * nchunk), rem = it % (c.KVH * nchunk);
-    int g = rem / nchunk, ch = rem % nchunk;
-    int len = sp.len[m], n = len + 1;
-    int t0 = ch * kScoreChunk;
-    if (t0 >= n) continue;
-    int t1 = min(n, t0 + kScoreChunk);
-    if (append_only && len >= t1) continue;
-    const int *pos = sp.pos[m];
-    const bool has_rope = pos[0] != 0 || pos[1] != 0 || pos[2] != 0;
-    const float *qkv = c.qkv + (size_t)m * qkvld;
-    // q heads of this group, rotated: task = (head, float4 index of the first half)
-    if (!append_only) {
-      for (int p = threadIdx.x; p < G * H4; p += kThreads) {
-        int hh = p / H4, i4 = p % H4;
-        const float4 *qh = (const float4 *)(qkv + (size_t)(g * G + hh) * D);
-        float4 a = __ldcg(qh + i4), b = __ldcg(qh + i4 + H4);
-        if (has_rope) {
-          float cs[4], sn[4];
-          rope_cs4(c, pos, i4, cs, sn);
-          rope4(a, b, cs, sn);
-        }
-        ((float4 *)(qs + hh * D))[i4] = a;
-        ((float4 *)(qs + hh * D))[i4 + H4] = b;
-      }
-    }
-    // keys of the chunk (2 tasks per thread, loads first); the new token's
-    // key comes from the projection output and is appended with its value
-    {
-      const int ntask = (t1 - t0) * H4;
-      constexpr int U = 2;
-      for (int base = threadIdx.x; base < ntask; base += kThreads * U) {
-        float4 ka[U], kb[U];
-        int tt[U], i4s[U];
-#pragma unroll
-        for (int u = 0; u < U; u++) {
-          int p = base + u * kThreads;
-          tt[u] = -1;
-          if (p < ntask) {
-            tt[u] = p / H4;
-            i4s[u] = p % H4;
-            int t = t0 + tt[u];
-            const float4 *src = (t == len) ? (const float4 *)(qkv + (size_t)(c.QH + g) * D)
-                                           : (const float4 *)kv_ptr(c, sp.bt[m], layer, 0, g, t);
-            ka[u] = __ldcg(src + i4s[u]);
-            kb[u] = __ldcg(src + i4s[u] + H4);
-          }
-        }
-#pragma unroll
-        for (int u = 0; u < U; u++) {
-          if (tt[u] < 0) continue;
-          int t = t0 + tt[u], i4 = i4s[u];
-          if (t == len) {
-            if (has_rope) {
-              float cs[4], sn[4];
-              rope_cs4(c, pos, i4, cs, sn);
-              rope4(ka[u], kb[u], cs, sn);
-            }
-            float4 *kd = (float4 *)kv_ptr(c, sp.bt[m], layer, 0, g, t);
-            kd[i4] = ka[u];
-            kd[i4 + H4] = kb[u];
-            const float4 *vh = (const float4 *)(qkv + (size_t)(c.QH + c.KVH + g) * D);
-            float4 *vd = (float4 *)kv_ptr(c, sp.bt[m], layer, 1, g, t);
-            vd[i4] = __ldcg(vh + i4);
-            vd[i4 + H4] = __ldcg(vh + i4 + H4);
-          }
-          float *kr = ks + tt[u] * (D + 1) + i4 * 4;
-          kr[0] = ka[u].x; kr[1] = ka[u].y; kr[2] = ka[u].z; kr[3] = ka[u].w;
-          float *kr2 = kr + D / 2;
-          kr2[0] = kb[u].x; kr2[1] = kb[u].y; kr2[2] = kb[u].z; kr2[3] = kb[u].w;
-        }
-      }
-    }
-    __syncthreads();
-    if (!append_only) {
-      for (int p = threadIdx.x; p < G * kScoreChunk; p += kThreads) {
-        int hh = p / kScoreChunk, tt = p % kScoreChunk, t = t0 + tt;
-        if (t >= t1) continue;
-        const float *q = qs + hh * D;
-        const float *k = ks + tt * (D + 1);
-        float r[16];
-#pragma unroll
-        for (int l = 0; l < 16; l++) {
-          float p0 = __fmul_rn(q[l], k[l]), p1 = __fmul_rn(q[16 + l], k[16 + l]);
-          float p2 = __fmul_rn(q[32 + l], k[32 + l]), p3 = __fmul_rn(q[48 + l], k[48 + l]);
-          float p4 = __fmul_rn(q[64 + l], k[64 + l]), p5 = __fmul_rn(q[80 + l], k[80 + l]);
-          float p6 = __fmul_rn(q[96 + l], k[96 + l]), p7 = __fmul_rn(q[112 + l], k[112 + l]);
-          r[l] = __fadd_rn(__fadd_rn(__fadd_rn(p0, p1), __fadd_rn(p2, p3)),
-                           __fadd_rn(__fadd_rn(p4, p5), __fadd_rn(p6, p7)));
-        }
-        float sc = __fmul_rn(tree16(r), c.attn_scale);
-        c.scores[((size_t)m * c.QH + g * G + hh) * c.max_ctx + t] = sc;
-      }
-    }
-    __syncthreads();
-  }
-}
-
-// Softmax statistics of one head (SoftmaxInPlace, ops.go:1199-1363, and the
-// cacheAttentionLen2..6 paths of model.go:4797-5081).  `mode` tells how a
-// score becomes its weight:
+// ---------------------------------------------------------------------------
+// Softmax of one head over <= 32 scores held in shared memory, restating
+// SoftmaxInPlace (ops.go:1199-1363) and the cacheAttentionLen2..6 paths
+// (model.go:4797-5081).  `mode` says how a score becomes its weight:
 //   0: fast_exp(s-m)*inv, 1: exp_fma(s-m)*inv for t < nv, raw s*inv above,
 //   2: n == 2 special form, 3: n == 1 (weight 1).
+// ---------------------------------------------------------------------------
 struct SMStats {
   float m, inv;
   int mode, nv;
 };
 
-__device__ __forceinline__ float sm_weight(const SMStats &st, const float *s, int t, int n) {
+__device__ __forceinline__ float sm_weight(const SMStats &st, const float *s, int t) {
   if (st.mode == 3) return 1.0f;
   if (st.mode == 2) {
-    float a = __ldcg(s), b = __ldcg(s + 1);
+    float a = s[0], b = s[1];
     if (a >= b) {
       float e = fast_exp(__fsub_rn(b, a));
       float inv = __fdiv_rn(1.0f, __fadd_rn(1.0f, e));
@@ -885,51 +917,28 @@ __device__ __forceinline__ float sm_weight(const SMStats &st, const float *s, in
     float inv = __fdiv_rn(1.0f, __fadd_rn(1.0f, e));
     return t == 0 ? __fmul_rn(e, inv) : inv;
   }
-  const float v = __ldcg(s + t);
+  const float v = s[t];
   if (st.mode == 0) return __fmul_rn(fast_exp(__fsub_rn(v, st.m)), st.inv);
   if (t < st.nv) return __fmul_rn(exp_fma(__fsub_rn(v, st.m)), st.inv);
   return __fmul_rn(v, st.inv);
 }
 
-// Statistics of one head computed by one warp.  For n >= 16 the 16 lane
-// chains of expF32VecFMA are kept exactly: lane l < 16 adds the exponentials
-// of tokens l, l+16, l+32, ... in order (two per 32-token step).
-__device__ SMStats warp_softmax_stats(const float *s, int n) {
+// One warp, n <= 32 scores.  For n >= 16 the 16 lane chains of
+// expF32VecFMA are kept exactly: lane l adds the exponential of token l, then
+// of token l+16 (when below the 16-aligned prefix nv).
+__device__ SMStats warp_softmax_small(const float *s, int n) {
   const int lane = threadIdx.x & 31;
-  float mx = -INFINITY;
-  for (int t0 = 0; t0 < n; t0 += 128) {
-    float v[4];
-#pragma unroll
-    for (int u = 0; u < 4; u++) {
-      int t = t0 + 32 * u + lane;
-      v[u] = t < n ? __ldcg(s + t) : -INFINITY;
-    }
-#pragma unroll
-    for (int u = 0; u < 4; u++) mx = fmaxf(mx, v[u]);
-  }
+  float mx = lane < n ? s[lane] : -INFINITY;
   for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
   SMStats st;
   st.m = mx;
   st.nv = 0;
   if (n >= 16) {
     const int nv = n & ~15;
-    float acc = 0.0f;
-    for (int t0 = 0; t0 < nv; t0 += 128) {
-      float e[4];
-#pragma unroll
-      for (int u = 0; u < 4; u++) {
-        int t = t0 + 32 * u + lane;
-        e[u] = t < nv ? exp_fma(__fsub_rn(__ldcg(s + t), mx)) : 0.0f;
-      }
-#pragma unroll
-      for (int u = 0; u < 4; u++) {
-        float hi = __shfl_down_sync(0xffffffffu, e[u], 16);
-        if (t0 + 32 * u < nv) {
-          acc = __fadd_rn(acc, e[u]);
-          if (t0 + 32 * u + 16 < nv) acc = __fadd_rn(acc, hi);
-        }
-      }
-    }
+    float e = lane < nv ? exp_fma(__fsub_rn(s[lane], mx)) : 0.0f;
+    float hi = __shfl_down_sync(0xffffffffu, e, 16);
+    float acc = __fadd_rn(0.0f, e);
+    if (16 < nv) acc = __fadd_rn(acc, hi);
     float lanes[16];
 #pragma unroll
     for (int l = 0; l < 16; l++) lanes[l] = __shfl_sync(0xffffffffu, acc, l);
@@ -948,27 +957,28 @@ __device__ SMStats warp_softmax_stats(const float *s, int n) {
     st.inv = 1.0f;
     return st;
   }
-  float e[15];
-  for (int t = 0; t < n; t++) e[t] = fast_exp(__fsub_rn(__ldcg(s + t), mx));
+  // 3 <= n <= 15: one exponential per lane, then the reference's sum order
+  const float e = lane < n ? fast_exp(__fsub_rn(s[lane], mx)) : 0.0f;
   float sum;
   if (n <= 8) {
-    float p01 = __fadd_rn(e[0], e[1]);
+    float e8[8];
+#pragma unroll
+    for (int t = 0; t < 8; t++) e8[t] = __shfl_sync(0xffffffffu, e, t);
+    float p01 = __fadd_rn(e8[0], e8[1]), p23 = __fadd_rn(e8[2], e8[3]);
+    float p45 = __fadd_rn(e8[4], e8[5]), p67 = __fadd_rn(e8[6], e8[7]);
+    float q4 = __fadd_rn(p01, p23);
     switch (n) {
-      case 3: sum = __fadd_rn(p01, e[2]); break;
-      case 4: sum = __fadd_rn(p01, __fadd_rn(e[2], e[3])); break;
-      case 5: sum = __fadd_rn(__fadd_rn(p01, __fadd_rn(e[2], e[3])), e[4]); break;
-      case 6: sum = __fadd_rn(__fadd_rn(p01, __fadd_rn(e[2], e[3])), __fadd_rn(e[4], e[5])); break;
-      case 7:
-        sum = __fadd_rn(__fadd_rn(__fadd_rn(p01, __fadd_rn(e[2], e[3])), __fadd_rn(e[4], e[5])), e[6]);
-        break;
-      default:
-        sum = __fadd_rn(__fadd_rn(__fadd_rn(p01, __fadd_rn(e[2], e[3])), __fadd_rn(e[4], e[5])),
-                        __fadd_rn(e[6], e[7]));
-        break;
+      case 3: sum = __fadd_rn(p01, e8[2]); break;
+      case 4: sum = q4; break;
+      case 5: sum = __fadd_rn(q4, e8[4]); break;
+      case 6: sum = __fadd_rn(q4, p45); break;
+      case 7: sum = __fadd_rn(__fadd_rn(q4, p45), e8[6]); break;
+      default: sum = __fadd_rn(__fadd_rn(q4, p45), p67); break;
     }
   } else {
     sum = 0.0f;
-    for (int t = 0; t < n; t++) sum = __fadd_rn(sum, e[t]);
+#pragma unroll 1
+    for (int t = 0; t < n; t++) sum = __fadd_rn(sum, __shfl_sync(0xffffffffu, e, t));
   }
   st.inv = __fdiv_rn(1.0f, sum);
   st.mode = 0;
@@ -976,89 +986,259 @@ __device__ SMStats warp_softmax_stats(const float *s, int n) {
 }
 
 // ---------------------------------------------------------------------------
-// Attention phase 2: softmax weights, value partial sums and head outputs.
-// Items: (sequence, kv head, chunk of kPVChunk tokens).  Each item derives
-// the softmax statistics of its G heads from all scores (one warp per head),
-// writes partial[m][h][chunk][d] = sum over its tokens of w_t * v_t[d] (token
-// order), and the last item to finish a (sequence, kv head) adds the partials
-// of its heads in chunk order into the head output.
+// Attention phase: RoPE, KV append, scores, softmax and value sums.
+// Items: (sequence, kv head, chunk of kAttnChunk tokens); each item serves the
+// G = QH/KVH query heads of its kv head (GQA).  The item whose chunk holds the
+// new token appends its rotated k and its v to the paged cache
+// (kvCache.append, model.go:5593-5612).  Scores restate cacheAttentionScores
+// (model.go:4623-4795): (q.k)*1/sqrt(D), the dot in the 8x16-slot order of
+// the reference's 128-wide dot kernels.
+//   * n <= kAttnChunk: one item per (sequence, kv head) holds every score and
+//     applies the reference softmax exactly (including its small-n forms) and
+//     the token-order value sum; the head output is written directly.
+//   * longer caches: each chunk keeps its own max m_c, the sum l_c of
+//     exp(s - m_c) and o_c = sum exp(s - m_c) v over the 16-aligned prefix
+//     nv = 16*floor(n/16); tokens at or above nv carry their raw score as
+//     weight (the reference's expF32VecFMA leaves them unexponentiated,
+//     dot_amd64.s:6131-6168).  The last chunk item to finish merges:
+//     head = (sum_c exp(m_c - M) o_c + T) / sum_c exp(m_c - M) l_c, with
+//     M the max over all scores and T the raw-weighted tail sum.
 // ---------------------------------------------------------------------------
-__device__ void phase_pv(const Ctx &c, int layer, float *smem) {
+__device__ __noinline__ void phase_attn(const Ctx *cp, int layer, int append_only, float *smem) {
+  const Ctx &c = *cp;
   const StepParams &sp = *c.sp;
-  const int G = c.QH / c.KVH, D = c.D;
-  const int nchunk = (sp.max_n + kPVChunk - 1) / kPVChunk;
+  const int G = c.QH / c.KVH, D = c.D, H4 = D / 8, D4 = D / 4;
+  const int qkvld = (c.QH + 2 * c.KVH) * D;
+  const int nchunk = (sp.max_n + kAttnChunk - 1) / kAttnChunk;
   const int items = sp.M * c.KVH * nchunk;
-  SMStats *st = (SMStats *)smem;                      // 8 entries
-  float *wts = smem + 32;                             // [G][kPVChunk]
-  float *vs = wts + 8 * kPVChunk;                     // [kPVChunk][D]
-  __shared__ int last_flag;
-  const int warp = threadIdx.x >> 5;
+  float *qs = smem;                               // [kMaxGroup][D]
+  float *ks = qs + kMaxGroup * D;                 // [kAttnChunk][D+1]
+  float *vs = ks + kAttnChunk * (D + 1);          // [kAttnChunk][D]
+  float *sc = vs + kAttnChunk * D;                // [kMaxGroup][kAttnChunk]
+  float *wt = sc + kMaxGroup * kAttnChunk;        // [kMaxGroup][kAttnChunk]
+  float *scl = wt + kMaxGroup * kAttnChunk;       // [kMaxGroup][max_chunks] merge scales
+  __shared__ SMStats st[kMaxGroup];
+  __shared__ float mloc[kMaxGroup], lloc[kMaxGroup], dinv[kMaxGroup];
+  __shared__ int is_last;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   for (int it = blockIdx.x; it < items; it += gridDim.x) {
-    int m = it / (c.KVH * nchunk), rem = it % (c.KVH * nchunk);
-    int g = rem / nchunk, ch = rem % nchunk;
-    int n = sp.len[m] + 1;
-    int nch = (n + kPVChunk - 1) / kPVChunk;
-    int t0 = ch * kPVChunk;
+    const int m = it / (c.KVH * nchunk), rem = it % (c.KVH * nchunk);
+    const int g = rem / nchunk, ch = rem % nchunk;
+    const int len = sp.len[m], n = len + 1;
+    const int t0 = ch * kAttnChunk;
     if (t0 >= n) continue;
-    int t1 = min(n, t0 + kPVChunk), cnt = t1 - t0;
-    const float *sc = c.scores + ((size_t)m * c.QH + g * G) * c.max_ctx;
-    // value rows of the chunk (loads issued first)
+    const int t1 = min(n, t0 + kAttnChunk), cnt = t1 - t0;
+    if (append_only && len >= t1) continue;
+    const int nch = (n + kAttnChunk - 1) / kAttnChunk;
+    const int *pos = sp.pos[m];
+    const int *bt = sp.bt[m];
+    const bool has_rope = pos[0] != 0 || pos[1] != 0 || pos[2] != 0;
+    const float *qkv = c.qkv + (size_t)m * qkvld;
+    // ---- loads: q pairs, k pairs, v rows; each thread issues a batch of
+    // loads before its first shared-memory store
     {
-      constexpr int U = 8;
-      const int ntask = cnt * (D / 4);
+      const int nq = append_only ? 0 : G * H4, nk = cnt * H4, nv4 = cnt * D4;
+      const int ntask = nq + nk + nv4;
+      constexpr int U = 2;
+#pragma unroll 1
       for (int base = threadIdx.x; base < ntask; base += kThreads * U) {
-        float4 v[U];
+        float4 ra[U], rb[U];
 #pragma unroll
         for (int u = 0; u < U; u++) {
           int p = base + u * kThreads;
-          if (p < ntask) v[u] = __ldcg((const float4 *)kv_ptr(c, sp.bt[m], layer, 1, g, t0 + p / (D / 4)) + p % (D / 4));
+          if (p >= ntask) continue;
+          if (p < nq) {
+            const float4 *qh = (const float4 *)(qkv + (size_t)(g * G + p / H4) * D);
+            ra[u] = __ldcg(qh + p % H4);
+            rb[u] = __ldcg(qh + p % H4 + H4);
+          } else if (p < nq + nk) {
+            int q = p - nq, t = t0 + q / H4, i4 = q % H4;
+            const float4 *src = (t == len) ? (const float4 *)(qkv + (size_t)(c.QH + g) * D)
+                                           : (const float4 *)kv_ptr(c, bt, layer, 0, g, t);
+            ra[u] = __ldcg(src + i4);
+            rb[u] = __ldcg(src + i4 + H4);
+          } else {
+            int q = p - nq - nk, t = t0 + q / D4, i4 = q % D4;
+            const float4 *src = (t == len) ? (const float4 *)(qkv + (size_t)(c.QH + c.KVH + g) * D)
+                                           : (const float4 *)kv_ptr(c, bt, layer, 1, g, t);
+            ra[u] = __ldcg(src + i4);
+          }
         }
 #pragma unroll
         for (int u = 0; u < U; u++) {
           int p = base + u * kThreads;
-          if (p < ntask) ((float4 *)vs)[p] = v[u];
+          if (p >= ntask) continue;
+          if (p < nq) {
+            int hh = p / H4, i4 = p % H4;
+            if (has_rope) {
+              float cs[4], sn[4];
+              rope_cs4(c, pos, i4, cs, sn);
+              rope4(ra[u], rb[u], cs, sn);
+            }
+            ((float4 *)(qs + hh * D))[i4] = ra[u];
+            ((float4 *)(qs + hh * D))[i4 + H4] = rb[u];
+          } else if (p < nq + nk) {
+            int q = p - nq, tt = q / H4, i4 = q % H4, t = t0 + tt;
+            if (t == len) {
+              if (has_rope) {
+                float cs[4], sn[4];
+                rope_cs4(c, pos, i4, cs, sn);
+                rope4(ra[u], rb[u], cs, sn);
+              }
+              float4 *kd = (float4 *)kv_ptr(c, bt, layer, 0, g, t);
+              kd[i4] = ra[u];
+              kd[i4 + H4] = rb[u];
+            }
+            float *kr = ks + tt * (D + 1) + i4 * 4;
+            kr[0] = ra[u].x; kr[1] = ra[u].y; kr[2] = ra[u].z; kr[3] = ra[u].w;
+            kr += D / 2;
+            kr[0] = rb[u].x; kr[1] = rb[u].y; kr[2] = rb[u].z; kr[3] = rb[u].w;
+          } else {
+            int q = p - nq - nk, tt = q / D4, i4 = q % D4, t = t0 + tt;
+            if (t == len) ((float4 *)kv_ptr(c, bt, layer, 1, g, t))[i4] = ra[u];
+            ((float4 *)(vs + tt * D))[i4] = ra[u];
+          }
         }
       }
     }
+    if (append_only) {
+      __syncthreads();
+      continue;
+    }
+    __syncthreads();
+    // ---- scores: one (head, token) per thread
+#pragma unroll 1
+    for (int p = threadIdx.x; p < G * kAttnChunk; p += kThreads) {
+      int hh = p / kAttnChunk, tt = p % kAttnChunk;
+      if (tt >= cnt) continue;
+      const float *q = qs + hh * D;
+      const float *k = ks + tt * (D + 1);
+      float r[16];
+#pragma unroll 4
+      for (int l = 0; l < 16; l++) {
+        float p0 = __fmul_rn(q[l], k[l]), p1 = __fmul_rn(q[16 + l], k[16 + l]);
+        float p2 = __fmul_rn(q[32 + l], k[32 + l]), p3 = __fmul_rn(q[48 + l], k[48 + l]);
+        float p4 = __fmul_rn(q[64 + l], k[64 + l]), p5 = __fmul_rn(q[80 + l], k[80 + l]);
+        float p6 = __fmul_rn(q[96 + l], k[96 + l]), p7 = __fmul_rn(q[112 + l], k[112 + l]);
+        r[l] = __fadd_rn(__fadd_rn(__fadd_rn(p0, p1), __fadd_rn(p2, p3)),
+                         __fadd_rn(__fadd_rn(p4, p5), __fadd_rn(p6, p7)));
+      }
+      sc[hh * kAttnChunk + tt] = __fmul_rn(tree16(r), c.attn_scale);
+    }
+    __syncthreads();
+    const size_t hbase = (size_t)m * c.QH + g * G;  // first query head of the group
+    if (nch == 1) {
+      // ---- exact reference softmax and token-order value sum
+      if (warp < G) {
+        SMStats s = warp_softmax_small(sc + warp * kAttnChunk, n);
+        if (lane < n) wt[warp * kAttnChunk + lane] = sm_weight(s, sc + warp * kAttnChunk, lane);
+      }
+      __syncthreads();
+#pragma unroll 1
+      for (int p = threadIdx.x; p < G * D; p += kThreads) {
+        int hh = p / D, d = p % D;
+        const float *w = wt + hh * kAttnChunk;
+        float acc = __fmul_rn(w[0], vs[d]);
+#pragma unroll 4
+        for (int tt = 1; tt < cnt; tt++) acc = __fmaf_rn(w[tt], vs[tt * D + d], acc);
+        c.head[(hbase + hh) * D + d] = acc;
+      }
+      __syncthreads();
+      continue;
+    }
+    // ---- chunk of a longer cache: local max, exponentials, sums
+    const int nv = n & ~15;
     if (warp < G) {
-      SMStats s = warp_softmax_stats(sc + (size_t)warp * c.max_ctx, n);
-      if ((threadIdx.x & 31) == 0) st[warp] = s;
+      const float *s = sc + warp * kAttnChunk;
+      float v = lane < cnt ? s[lane] : -INFINITY;
+      float mx = v;
+      for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+      int t = t0 + lane;
+      float e = 0.0f, w = 0.0f;
+      if (lane < cnt) {
+        if (t < nv) {
+          e = exp_fma(__fsub_rn(v, mx));
+          w = e;
+        } else {
+          w = v;  // raw score
+        }
+      }
+      float l = e;
+      for (int o = 16; o > 0; o >>= 1) l = __fadd_rn(l, __shfl_xor_sync(0xffffffffu, l, o));
+      wt[warp * kAttnChunk + lane] = w;
+      if (lane == 0) {
+        mloc[warp] = mx;
+        lloc[warp] = l;
+      }
     }
     __syncthreads();
-    for (int p = threadIdx.x; p < G * cnt; p += kThreads) {
-      int hh = p / cnt, tt = p % cnt;
-      wts[hh * kPVChunk + tt] = sm_weight(st[hh], sc + (size_t)hh * c.max_ctx, t0 + tt, n);
-    }
-    __syncthreads();
+    const bool has_tail = t1 > nv;
+#pragma unroll 1
     for (int p = threadIdx.x; p < G * D; p += kThreads) {
       int hh = p / D, d = p % D;
-      const float *w = wts + hh * kPVChunk;
-      float acc = __fmul_rn(w[0], vs[d]);
-      for (int tt = 1; tt < cnt; tt++) acc = __fmaf_rn(w[tt], vs[tt * D + d], acc);
-      c.partial[(((size_t)m * c.QH + g * G + hh) * c.max_chunks + ch) * D + d] = acc;
+      const float *w = wt + hh * kAttnChunk;
+      float acc = 0.0f, tail = 0.0f;
+#pragma unroll 4
+      for (int tt = 0; tt < cnt; tt++) {
+        if (t0 + tt < nv)
+          acc = __fmaf_rn(w[tt], vs[tt * D + d], acc);
+        else
+          tail = __fmaf_rn(w[tt], vs[tt * D + d], tail);
+      }
+      size_t hc = (hbase + hh) * c.max_chunks + ch;
+      c.part_o[hc * D + d] = acc;
+      if (ch == nch - 1) c.part_t[(hbase + hh) * D + d] = has_tail ? tail : 0.0f;
+      if (d == 0) {
+        c.part_ml[hc * 2] = mloc[hh];
+        c.part_ml[hc * 2 + 1] = lloc[hh];
+      }
     }
-    // last chunk item of (m, g) to finish reduces the partials
+    // ---- the last chunk item of (m, g) merges the chunks
     __threadfence();
     __syncthreads();
     if (threadIdx.x == 0) {
-      unsigned *cnt_p = c.pv_count + m * c.KVH + g;
-      unsigned done = atomicAdd(cnt_p, 1u);
-      last_flag = done == (unsigned)(nch - 1);
-      if (last_flag) atomicExch(cnt_p, 0u);
+      unsigned *cntp = c.attn_count + m * c.KVH + g;
+      is_last = atomicAdd(cntp, 1u) == (unsigned)(nch - 1);
+      if (is_last) *cntp = 0u;
     }
     __syncthreads();
-    if (last_flag) {
+    if (is_last) {
       __threadfence();
+      if (warp < G) {
+        const float *ml = c.part_ml + ((hbase + warp) * c.max_chunks) * 2;
+        float mx = -INFINITY;
+#pragma unroll 1
+        for (int k = lane; k < nch; k += 32) mx = fmaxf(mx, __ldcg(ml + 2 * k));
+        for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+        float den = 0.0f;
+#pragma unroll 1
+        for (int k = lane; k < nch; k += 32) {
+          float s = exp_fma(__fsub_rn(__ldcg(ml + 2 * k), mx));
+          scl[warp * c.max_chunks + k] = s;
+          den = __fmaf_rn(s, __ldcg(ml + 2 * k + 1), den);
+        }
+        for (int o = 16; o > 0; o >>= 1) den = __fadd_rn(den, __shfl_xor_sync(0xffffffffu, den, o));
+        if (lane == 0) dinv[warp] = __fdiv_rn(1.0f, den);
+      }
+      __syncthreads();
+#pragma unroll 1
       for (int p = threadIdx.x; p < G * D; p += kThreads) {
         int hh = p / D, d = p % D;
-        const float *pp = c.partial + (((size_t)m * c.QH + g * G + hh) * c.max_chunks) * D + d;
-        float acc = __ldcg(pp);
-        for (int k = 1; k < nch; k++) acc = __fadd_rn(acc, __ldcg(pp + (size_t)k * D));
-        c.head[((size_t)m * c.QH + g * G + hh) * D + d] = acc;
+        const float *po = c.part_o + ((hbase + hh) * c.max_chunks) * D + d;
+        const float *s = scl + hh * c.max_chunks;
+        float acc = __ldcg(c.part_t + (hbase + hh) * D + d);
+#pragma unroll 4
+        for (int k = 0; k < nch; k++) acc = __fmaf_rn(s[k], __ldcg(po + (size_t)k * D), acc);
+        c.head[(hbase + hh) * D + d] = __fmul_rn(acc, dinv[hh]);
       }
     }
     __syncthreads();
   }
+}
+
+__host__ __device__ __forceinline__ size_t attn_smem_floats(int max_chunks) {
+  return (size_t)kMaxGroup * kHeadDim + (size_t)kAttnChunk * (kHeadDim + 1) + (size_t)kAttnChunk * kHeadDim +
+         2 * (size_t)kMaxGroup * kAttnChunk + (size_t)kMaxGroup * max_chunks;
 }
 
 // Normalised output of a fused AddRMSNorm (the normOut vector of
@@ -1087,16 +1267,6 @@ __device__ void phase_rmsnorm_out(const Ctx &c, const float *x, int n, int M, co
     float scale = fast_rsqrt(__fadd_rn(__fdiv_rn(ss, (float)n), c.eps));
     for (int i = threadIdx.x; i < n; i += kThreads) out[(size_t)m * n + i] = __fmul_rn(__fmul_rn(tmp[i], w[i]), scale);
     __syncthreads();
-  }
-}
-
-// lm_head argmax result -> token ids (and reset of the keys for the next step).
-__device__ void phase_argmax_finish(const Ctx &c) {
-  const StepParams &sp = *c.sp;
-  if (blockIdx.x == 0 && threadIdx.x < sp.M) {
-    unsigned long long k = c.argkey[threadIdx.x];
-    c.tok_out[threadIdx.x] = sp.need[threadIdx.x] ? argmax_key_row(k) : -1;
-    c.argkey[threadIdx.x] = 0ull;
   }
 }
 

@@ -58,43 +58,30 @@ __device__ __forceinline__ unsigned ld_acquire(const unsigned *p) {
   asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
   return v;
 }
-
-// Grid barrier for the cooperative step kernel: one arrival counter
-// (atom.acq_rel) and a generation word (red.release / ld.acquire).  Waits are
-// bounded: after kBarrierSpins polls the waiting block records an error and
-// leaves; waiting blocks also leave once any block has recorded one.
-// Returns false on error.
-constexpr unsigned long long kBarrierSpins = 1ull << 22;
-__device__ __forceinline__ unsigned atom_add_acqrel(unsigned *p, unsigned v) {
-  unsigned old;
-  asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
-  return old;
-}
 __device__ __forceinline__ void red_add_release(unsigned *p, unsigned v) {
   asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
-__device__ __forceinline__ void st_relaxed(unsigned *p, unsigned v) {
-  asm volatile("st.relaxed.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-__device__ bool grid_sync(const Ctx &c) {
+
+// Grid barrier of the cooperative step kernel: every block adds 1 to a
+// monotonic counter with a non-returning release reduction and polls it with
+// acquire loads until it reaches `target` (the host tracks the counter's value
+// across launches).  Waits are bounded: after kBarrierSpins polls the block
+// records an error and leaves; waiting blocks also leave once any block has
+// recorded one.  Returns false on error.
+constexpr unsigned long long kBarrierSpins = 1ull << 22;
+__device__ bool grid_sync(const Ctx &c, unsigned target) {
   __shared__ int ok;
   __syncthreads();
   if (threadIdx.x == 0) {
     ok = 1;
-    unsigned gen = ld_acquire(c.bar_gen);
-    unsigned arrived = atom_add_acqrel(c.bar_count, 1u);
-    if (arrived == gridDim.x - 1) {
-      st_relaxed(c.bar_count, 0u);
-      red_add_release(c.bar_gen, 1u);
-    } else {
-      unsigned long long spins = 0;
-      while (ld_acquire(c.bar_gen) == gen) {
-        ++spins;
-        if (spins > kBarrierSpins || ((spins & 1023) == 0 && *(volatile int *)c.err)) {
-          atomicExch(c.err, 1);
-          ok = 0;
-          break;
-        }
+    red_add_release(c.bar_count, 1u);
+    unsigned long long spins = 0;
+    while ((int)(ld_acquire(c.bar_count) - target) < 0) {
+      ++spins;
+      if (spins > kBarrierSpins || ((spins & 1023) == 0 && *(volatile int *)c.err)) {
+        atomicExch(c.err, 1);
+        ok = 0;
+        break;
       }
     }
   }
@@ -102,162 +89,152 @@ __device__ bool grid_sync(const Ctx &c) {
   return ok != 0;
 }
 
-__device__ GemvArgs gemv_args(const DMat &A, int rb, int re, const float *src, int ld, int mode,
-                              const float *nw, int epi, float *out, int ldo) {
-  GemvArgs a;
-  memset(&a, 0, sizeof(a));
-  a.A = A;
-  a.row_begin = rb;
-  a.row_end = re;
-  a.src = src;
-  a.ld = ld;
-  a.mode = mode;
-  a.norm_w = nw;
-  a.epi = epi;
-  a.out = out;
-  a.ldo = ldo;
-  return a;
+constexpr int kLayerPhases = 5;  // qkv, attention, o, gate/up, down
+constexpr int kPhaseLM = 5;      // lm_head argmax (after the last layer)
+
+__host__ __device__ __forceinline__ unsigned barriers_per_step(int L, int any_logits) {
+  return any_logits ? (unsigned)(kLayerPhases * L) : (unsigned)(kLayerPhases * (L - 1) + 1);
 }
 
-// L2 prefetch (cp.async.bulk.prefetch.L2) of this block's weight slabs of
-// layer l (same row split as the GEMV phases) and of this block's share of
-// the sequences' KV pages of layer l.  Issued by one thread, never waited on.
-__device__ void prefetch_layer(const Ctx &c, int l, int M) {
-  if (threadIdx.x != 0 || l < 0 || l >= c.L) return;
-  const LayerW &L = c.layers[l];
-  const int b = blockIdx.x, nb = gridDim.x;
-  prefetch_gemv_slab(L.qkv, 0, L.qkv.rows, b, nb);
-  prefetch_gemv_slab(L.o, 0, L.o.rows, b, nb);
-  prefetch_gemv_slab(L.gate, 0, L.gate.rows, b, nb);
-  prefetch_gemv_slab(L.up, 0, L.up.rows, b, nb);
-  prefetch_gemv_slab(L.down, 0, L.down.rows, b, nb);
-  const StepParams &sp = *c.sp;
-  const size_t layer_off = (size_t)l * 2 * c.KVH * kPageTokens * c.D;
-  const size_t layer_bytes = (size_t)2 * c.KVH * kPageTokens * c.D * 4;
-  int idx = 0;
-  for (int m = 0; m < M; m++) {
-    int np = (sp.len[m] + kPageTokens - 1) / kPageTokens;
-    for (int p = 0; p < np; p++, idx++)
-      if (idx % nb == b) prefetch_l2(c.kv_pool + (size_t)sp.bt[m][p] * c.page_floats + layer_off, layer_bytes);
-  }
-}
-
-// Phase bodies shared by the persistent kernel and the per-phase launches.
-__device__ void run_phase_body(const Ctx &c, int phase, int layer, int M, int any_logits, float *smem,
-                               unsigned long long *tslot);
-__device__ void run_phase(const Ctx &c, int phase, int layer, int M, int any_logits, float *smem, int tidx) {
+// One phase of layer `layer`.  GEMV arguments are built by thread 0 in
+// shared memory.
+template <int QT>
+__device__ void run_phase(const Ctx &c, int phase, int layer, int M, int any_logits, int do_embed, int feed,
+                          float *smem, int tidx) {
+  __shared__ GemvArgs sa;
   unsigned long long *tslot = c.trace ? c.trace + 4 * tidx : nullptr;
   if (tslot && blockIdx.x == 0 && threadIdx.x == 0) tslot[0] = gtimer();
-  run_phase_body(c, phase, layer, M, any_logits, smem, tslot);
+  const LayerW &L = c.layers[layer < c.L ? layer : c.L - 1];
+  const bool last = layer == c.L - 1;
+  if (phase == 1) {
+    phase_attn(&c, layer, last && !any_logits, smem);
+  } else {
+    if (threadIdx.x == 0) {
+      memset(&sa, 0, sizeof(sa));
+      sa.tslot = tslot;
+      switch (phase) {
+        case 0:  // QKV with the input RMSNorm (layer 0: embedding gather) as prologue
+          sa.A = L.qkv;
+          sa.row_begin = (last && !any_logits) ? c.QH * c.D : 0;
+          sa.row_end = L.qkv.rows;
+          sa.ld = c.H;
+          if (layer == 0 && do_embed) {
+            sa.src = c.embed;
+            sa.src_tok = 1;
+            sa.copy_src = c.h;
+          } else {
+            sa.src = c.h;
+          }
+          sa.mode = PRO_RMSNORM;
+          sa.norm_w = L.ln1;
+          sa.epi = EPI_STORE;
+          sa.out = c.qkv;
+          sa.ldo = (c.QH + 2 * c.KVH) * c.D;
+          break;
+        case 2:  // o projection + residual
+          sa.A = L.o;
+          sa.row_end = L.o.rows;
+          sa.src = c.head;
+          sa.ld = c.QH * c.D;
+          sa.mode = PRO_PLAIN;
+          sa.epi = EPI_RESID;
+          sa.ldo = c.H;
+          sa.resid = c.h;
+          sa.vout = c.vbuf;
+          sa.resid_mode = RESID_ATTN;
+          break;
+        case 3:  // gate/up with the post-attention AddRMSNorm as prologue
+          sa.A = L.gate;
+          sa.B = L.up;
+          sa.row_end = L.gate.rows;
+          sa.src = c.vbuf;
+          sa.ld = c.H;
+          sa.mode = PRO_ADDNORM;
+          sa.norm_w = L.ln2;
+          sa.epi = EPI_SWIGLU;
+          sa.out = c.g;
+          sa.ldo = c.I;
+          break;
+        case 4:  // down projection + residual (last layer: out-only)
+          sa.A = L.down;
+          sa.row_end = L.down.rows;
+          sa.src = c.g;
+          sa.ld = c.I;
+          sa.mode = PRO_PLAIN;
+          sa.epi = EPI_RESID;
+          sa.ldo = c.H;
+          sa.resid = c.h;
+          sa.vout = c.vbuf;
+          sa.resid_mode = last ? RESID_NEVER : RESID_ALWAYS;
+          break;
+        default:  // lm_head argmax with the final AddRMSNorm as prologue
+          sa.A = c.lm_head;
+          sa.row_end = c.lm_head.rows;
+          sa.src = c.vbuf;
+          sa.ld = c.H;
+          sa.mode = PRO_ADDNORM;
+          sa.norm_w = c.final_norm;
+          sa.epi = EPI_ARGMAX;
+          sa.ldo = c.V;
+          sa.argkey = c.argkey;
+          sa.logits = c.logits;
+          sa.argmax_finish = 1;
+          sa.feed = feed;
+          break;
+      }
+    }
+    __syncthreads();
+    phase_gemv_q<QT>(&c, &sa, M, smem);
+  }
   if (tslot && threadIdx.x == 0) atomicMax(tslot + 2, gtimer());
 }
 
-__device__ void run_phase_body(const Ctx &c, int phase, int layer, int M, int any_logits, float *smem,
-                               unsigned long long *tslot) {
-  const LayerW &L = c.layers[layer];
-  const int qkvld = (c.QH + 2 * c.KVH) * c.D;
-  const bool last = layer == c.L - 1;
-  switch (phase) {
-    case 0: {  // QKV projection with the input RMSNorm as prologue
-      prefetch_layer(c, layer + 1, M);
-      if (last && any_logits && threadIdx.x == 0)
-        prefetch_gemv_slab(c.lm_head, 0, c.lm_head.rows, blockIdx.x, gridDim.x);
-      int rb = (last && !any_logits) ? c.QH * c.D : 0;
-      GemvArgs a = gemv_args(L.qkv, rb, L.qkv.rows, c.h, c.H, PRO_RMSNORM, L.ln1, EPI_STORE, c.qkv, qkvld);
-      a.tslot = tslot;
-      phase_gemv(c, a, M, smem);
-      break;
-    }
-    case 1:
-      phase_scores(c, layer, last && !any_logits, smem);
-      break;
-    case 2:
-      phase_pv(c, layer, smem);
-      break;
-    case 3: {  // o projection + residual
-      GemvArgs a = gemv_args(L.o, 0, L.o.rows, c.head, c.QH * c.D, PRO_PLAIN, nullptr, EPI_RESID, nullptr, c.H);
-      a.resid = c.h;
-      a.vout = c.vbuf;
-      a.resid_mode = RESID_ATTN;
-      a.tslot = tslot;
-      phase_gemv(c, a, M, smem);
-      break;
-    }
-    case 4: {  // gate/up with the post-attention AddRMSNorm as prologue
-      GemvArgs a = gemv_args(L.gate, 0, L.gate.rows, c.vbuf, c.H, PRO_ADDNORM, L.ln2, EPI_SWIGLU, c.g, c.I);
-      a.B = L.up;
-      a.tslot = tslot;
-      phase_gemv(c, a, M, smem);
-      break;
-    }
-    case 5: {  // down projection + residual (last layer: out-only)
-      GemvArgs a = gemv_args(L.down, 0, L.down.rows, c.g, c.I, PRO_PLAIN, nullptr, EPI_RESID, nullptr, c.H);
-      a.resid = c.h;
-      a.vout = c.vbuf;
-      a.resid_mode = last ? RESID_NEVER : RESID_ALWAYS;
-      a.tslot = tslot;
-      phase_gemv(c, a, M, smem);
-      break;
-    }
-    case 6: {  // lm_head argmax with the final AddRMSNorm as prologue
-      GemvArgs a = gemv_args(c.lm_head, 0, c.lm_head.rows, c.vbuf, c.H, PRO_ADDNORM, c.final_norm, EPI_ARGMAX,
-                             nullptr, c.V);
-      a.argkey = c.argkey;
-      a.logits = c.logits;
-      a.tslot = tslot;
-      phase_gemv(c, a, M, smem);
-      break;
-    }
-    case 7:
-      phase_argmax_finish(c);
-      break;
-  }
-}
+// Ctx is copied into shared memory once per launch; phases read it there.
+#define OCRVL_CTX_TO_SMEM(cv)                       \
+  __shared__ Ctx sctx;                              \
+  if (threadIdx.x == 0) sctx = cv;                  \
+  __syncthreads();                                  \
+  const Ctx &c = sctx;
 
-constexpr int kLayerPhases = 6;  // qkv, scores, pv, o, gate/up, down
-
-__device__ __forceinline__ bool traced_sync(const Ctx &c, int tidx) {
-  bool ok = grid_sync(c);
-  if (c.trace && blockIdx.x == 0 && threadIdx.x == 0) c.trace[4 * tidx + 3] = gtimer();
-  return ok;
-}
-
-__global__ void __launch_bounds__(kThreads) k_step(Ctx c, int M, int any_logits, int do_embed) {
+template <int QT>
+__global__ void __launch_bounds__(kThreads, 1)
+    k_step(Ctx cv, int M, int any_logits, int do_embed, int feed, unsigned bar_base) {
   extern __shared__ float4 smem4[];
   float *smem = (float *)smem4;
-  prefetch_layer(c, 0, M);
-  if (do_embed) {
-    phase_embed(c);
-    if (!grid_sync(c)) return;
-  }
+  OCRVL_CTX_TO_SMEM(cv);
+  unsigned k = 0;
   int t = 0;
   for (int l = 0; l < c.L; l++) {
-    bool kv_only = l == c.L - 1 && !any_logits;
+    const bool kv_only = l == c.L - 1 && !any_logits;
     for (int ph = 0; ph < kLayerPhases; ph++, t++) {
-      run_phase(c, ph, l, M, any_logits, smem, t);
-      if (!traced_sync(c, t)) return;
+      run_phase<QT>(c, ph, l, M, any_logits, do_embed, feed, smem, t);
       if (kv_only && ph == 1) return;
+      if (!grid_sync(c, bar_base + (++k) * gridDim.x)) return;
+      if (c.trace && blockIdx.x == 0 && threadIdx.x == 0) c.trace[4 * t + 3] = gtimer();
     }
   }
-  if (any_logits) {
-    run_phase(c, kLayerPhases, c.L - 1, M, any_logits, smem, t);
-    if (!traced_sync(c, t)) return;
-    t++;
-    run_phase(c, kLayerPhases + 1, c.L - 1, M, any_logits, smem, t);
-  }
+  if (any_logits) run_phase<QT>(c, kPhaseLM, c.L, M, any_logits, do_embed, feed, smem, t);
 }
 
-__global__ void __launch_bounds__(kThreads) k_phase(Ctx c, int phase, int layer, int M, int any_logits) {
+template <int QT>
+__global__ void __launch_bounds__(kThreads, 1)
+    k_phase(Ctx cv, int phase, int layer, int M, int any_logits, int do_embed, int feed) {
   extern __shared__ float4 smem4[];
-  c.trace = nullptr;
-  run_phase(c, phase, layer, M, any_logits, (float *)smem4, 0);
+  OCRVL_CTX_TO_SMEM(cv);
+  Ctx &cm = sctx;
+  if (threadIdx.x == 0) cm.trace = nullptr;
+  __syncthreads();
+  run_phase<QT>(c, phase, layer, M, any_logits, do_embed, feed, (float *)smem4, 0);
 }
 
-__global__ void __launch_bounds__(kThreads) k_embed(Ctx c) { phase_embed(c); }
-
-__global__ void __launch_bounds__(kThreads) k_gemv(Ctx c, GemvArgs a, int M) {
+template <int QT>
+__global__ void __launch_bounds__(kThreads) k_gemv(Ctx cv, GemvArgs av, int M) {
   extern __shared__ float4 smem4[];
-  phase_gemv(c, a, M, (float *)smem4);
+  OCRVL_CTX_TO_SMEM(cv);
+  __shared__ GemvArgs sa;
+  if (threadIdx.x == 0) sa = av;
+  __syncthreads();
+  phase_gemv_q<QT>(&c, &sa, M, (float *)smem4);
 }
 
 __global__ void __launch_bounds__(kThreads) k_addnorm_out(Ctx c, const float *v, int n, int M, const float *w,
@@ -337,6 +314,7 @@ struct ocrvl_model {
   int grid = 0;
   size_t smem = 0;
   bool persistent = true;
+  unsigned bar_base = 0;  // value of the barrier counter before the next launch
   int sms = 0;
 
   template <typename T>
@@ -412,37 +390,64 @@ int upload_f32(ocrvl_model *m, float *&dst, int64_t n, const void *data) {
   return OCRVL_OK;
 }
 
-size_t smem_bytes(const ocrvl_model_desc &d, int qtype) {
+size_t smem_bytes(const ocrvl_model_desc &d, int qtype, int max_chunks) {
   int nmax = std::max(std::max(d.hidden_size, d.intermediate_size), d.num_heads * d.head_dim);
-  size_t area = qtype == QT_Q8 ? (size_t)kMaxBatch * nmax * 4 : (size_t)kMaxBatch * nmax;
-  size_t gemv = (320 + (size_t)nmax) * 4 + area;
-  int G = d.num_heads / d.num_kv_heads;
-  size_t scores = ((size_t)G * d.head_dim + (size_t)kScoreChunk * (d.head_dim + 1)) * 4;
-  size_t pv = (32 + 8 * kPVChunk + (size_t)kPVChunk * d.head_dim) * 4;
-  return std::max(std::max(gemv, scores), pv) + 64;
+  size_t g1 = gemv_smem_total(qtype, 1, nmax, kStagesM1);
+  size_t gb = gemv_smem_total(qtype, kMaxBatch, nmax, kStagesMB);
+  size_t attn = attn_smem_floats(max_chunks) * 4;
+  return std::max(std::max(g1, gb), attn) + 64;
 }
 
-int launch_step(ocrvl_model *m, int M, int any_logits, int do_embed) {
+template <int QT>
+int launch_step_q(ocrvl_model *m, int M, int any_logits, int do_embed, int feed) {
   Ctx c = m->ctx;
   if (m->persistent) {
-    void *args[] = {&c, &M, &any_logits, &do_embed};
-    CK(cudaLaunchCooperativeKernel((void *)k_step, dim3(m->grid), dim3(kThreads), args, m->smem, m->stream));
+    unsigned base = m->bar_base;
+    void *args[] = {&c, &M, &any_logits, &do_embed, &feed, &base};
+    CK(cudaLaunchCooperativeKernel((void *)k_step<QT>, dim3(m->grid), dim3(kThreads), args, m->smem, m->stream));
+    m->bar_base += barriers_per_step(m->desc.num_layers, any_logits) * (unsigned)m->grid;
     return OCRVL_OK;
   }
-  if (do_embed) k_embed<<<m->grid, kThreads, 0, m->stream>>>(c);
   for (int l = 0; l < m->desc.num_layers; l++) {
     bool kv_only = l == m->desc.num_layers - 1 && !any_logits;
     for (int ph = 0; ph < kLayerPhases; ph++) {
-      k_phase<<<m->grid, kThreads, m->smem, m->stream>>>(c, ph, l, M, any_logits);
+      k_phase<QT><<<m->grid, kThreads, m->smem, m->stream>>>(c, ph, l, M, any_logits, do_embed, feed);
       if (kv_only && ph == 1) break;
     }
   }
-  if (any_logits) {
-    k_phase<<<m->grid, kThreads, m->smem, m->stream>>>(c, kLayerPhases, m->desc.num_layers - 1, M, any_logits);
-    k_phase<<<1, kThreads, m->smem, m->stream>>>(c, kLayerPhases + 1, m->desc.num_layers - 1, M, any_logits);
-  }
+  if (any_logits) k_phase<QT><<<m->grid, kThreads, m->smem, m->stream>>>(c, kPhaseLM, m->desc.num_layers, M, any_logits, do_embed, feed);
   CK(cudaGetLastError());
   return OCRVL_OK;
+}
+
+int launch_step(ocrvl_model *m, int M, int any_logits, int do_embed, int feed = 0) {
+  if (m->qtype == QT_Q4) return launch_step_q<QT_Q4>(m, M, any_logits, do_embed, feed);
+  if (m->qtype == QT_Q6) return launch_step_q<QT_Q6>(m, M, any_logits, do_embed, feed);
+  return launch_step_q<QT_Q8>(m, M, any_logits, do_embed, feed);
+}
+
+template <int QT>
+int set_kernel_attrs(ocrvl_model *m) {
+  CK(cudaFuncSetAttribute(k_step<QT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)m->smem));
+  CK(cudaFuncSetAttribute(k_phase<QT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)m->smem));
+  int per_sm = 0;
+  CK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_step<QT>, kThreads, m->smem));
+  if (per_sm <= 0) return fail(OCRVL_E_CUDA, "step kernel does not fit on an SM");
+  int want = 1;
+  if (const char *e = getenv("OCRVL_BLOCKS_PER_SM")) want = std::max(1, std::atoi(e));
+  m->grid = m->sms * std::min(per_sm, want);
+  return OCRVL_OK;
+}
+
+// Clears the barrier counter and error word after a timed-out step.
+void reset_after_timeout(ocrvl_model *m) {
+  int zero = 0;
+  cudaMemcpy(m->ctx.err, &zero, 4, cudaMemcpyHostToDevice);
+  cudaMemset(m->ctx.bar_count, 0, 4);
+  cudaMemset(m->ctx.attn_count, 0, (size_t)kMaxBatch * m->ctx.KVH * 4);
+  cudaMemset(m->ctx.lm_count, 0, 4);
+  cudaMemset(m->ctx.argkey, 0, kMaxBatch * 8);
+  m->bar_base = 0;
 }
 
 }  // namespace
@@ -646,7 +651,7 @@ int ocrvl_finalize(ocrvl_model *m) {
   c.kv_pool = m->kv_pool;
   c.page_floats = m->page_floats;
   c.max_ctx = d.max_position;
-  c.max_chunks = (c.max_ctx + kPVChunk - 1) / kPVChunk;
+  c.max_chunks = (c.max_ctx + kAttnChunk - 1) / kAttnChunk;
   int qkvld = (c.QH + 2 * c.KVH) * c.D;
   size_t B = kMaxBatch;
   c.h = m->dalloc<float>(B * c.H);
@@ -654,16 +659,19 @@ int ocrvl_finalize(ocrvl_model *m) {
   c.qkv = m->dalloc<float>(B * qkvld);
   c.head = m->dalloc<float>(B * c.QH * c.D);
   c.g = m->dalloc<float>(B * c.I);
-  c.scores = m->dalloc<float>(B * c.QH * (size_t)c.max_ctx);
-  c.partial = m->dalloc<float>(B * c.QH * (size_t)c.max_chunks * c.D);
+  c.part_o = m->dalloc<float>(B * c.QH * (size_t)c.max_chunks * c.D);
+  c.part_ml = m->dalloc<float>(B * c.QH * (size_t)c.max_chunks * 2);
+  c.part_t = m->dalloc<float>(B * c.QH * (size_t)c.D);
   c.logits = m->dalloc<float>(B * (size_t)c.V);
   c.argkey = m->dalloc<unsigned long long>(B);
   c.tok_out = m->dalloc<int>(B + 1);
   c.bar_count = m->dalloc<unsigned>(2 + B * c.KVH);
-  c.bar_gen = c.bar_count + 1;
-  c.pv_count = c.bar_count + 2;
+  c.lm_count = c.bar_count + 1;
+  c.attn_count = c.bar_count + 2;
+  c.hist_pos = m->dalloc<int>(1);
+  if (!c.hist_pos) return fail(OCRVL_E_NOMEM, "history counter");
   StepParams *spd = m->dalloc<StepParams>(1);
-  if (!c.h || !c.vbuf || !c.qkv || !c.head || !c.g || !c.scores || !c.partial || !c.logits || !c.argkey ||
+  if (!c.h || !c.vbuf || !c.qkv || !c.head || !c.g || !c.part_o || !c.part_ml || !c.part_t || !c.logits || !c.argkey ||
       !c.tok_out || !c.bar_count || !spd)
     return fail(OCRVL_E_NOMEM, "work buffer allocation failed");
   c.err = c.tok_out + B;
@@ -676,16 +684,13 @@ int ocrvl_finalize(ocrvl_model *m) {
   CK(cudaHostAlloc((void **)&m->out_h, (B + 1) * 4, cudaHostAllocDefault));
   CK(cudaHostAlloc((void **)&m->bt_stage, B * 4, cudaHostAllocDefault));
   // launch geometry
-  m->smem = smem_bytes(d, m->qtype);
-  CK(cudaFuncSetAttribute(k_step, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)m->smem));
-  CK(cudaFuncSetAttribute(k_phase, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)m->smem));
+  m->smem = smem_bytes(d, m->qtype, c.max_chunks);
   CK(cudaDeviceGetAttribute(&m->sms, cudaDevAttrMultiProcessorCount, m->device));
-  int per_sm = 0;
-  CK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_step, kThreads, m->smem));
-  if (per_sm <= 0) return fail(OCRVL_E_CUDA, "step kernel does not fit on an SM");
-  int want = 1;
-  if (const char *e = getenv("OCRVL_BLOCKS_PER_SM")) want = std::max(1, std::atoi(e));
-  m->grid = m->sms * std::min(per_sm, want);
+  {
+    int rc = m->qtype == QT_Q4 ? set_kernel_attrs<QT_Q4>(m)
+             : m->qtype == QT_Q6 ? set_kernel_attrs<QT_Q6>(m) : set_kernel_attrs<QT_Q8>(m);
+    if (rc) return rc;
+  }
   if (getenv("OCRVL_TRACE")) {
     c.trace = m->dalloc<unsigned long long>(4 * 256);
     if (!c.trace) return fail(OCRVL_E_NOMEM, "trace buffer");
@@ -839,15 +844,91 @@ int ocrvl_step(ocrvl_model *m, ocrvl_seq *const *seqs, int n, const int32_t *ids
     CK(cudaMemcpyAsync(out_logits, m->ctx.logits, (size_t)n * d.vocab_size * 4, cudaMemcpyDeviceToHost, m->stream));
   CK(cudaStreamSynchronize(m->stream));
   if (m->out_h[kMaxBatch]) {
-    int zero = 0;
-    cudaMemcpy(m->ctx.err, &zero, 4, cudaMemcpyHostToDevice);
-    cudaMemset(m->ctx.bar_count, 0, (2 + kMaxBatch * m->ctx.KVH) * 4);
+    reset_after_timeout(m);
     return fail(OCRVL_E_TIMEOUT, "device grid barrier timed out");
   }
   for (int i = 0; i < n; i++) {
     seqs[i]->len++;
     if (out_ids) out_ids[i] = need_logits ? m->out_h[i] : -1;
   }
+  return OCRVL_OK;
+}
+
+void *ocrvl_model_stream(ocrvl_model *m) { return m ? (void *)m->stream : nullptr; }
+
+int ocrvl_step_io_bytes(const ocrvl_model *m, int n, int64_t *h2d, int64_t *d2h) {
+  if (!m || !h2d || !d2h || n < 1 || n > kMaxBatch) return fail(OCRVL_E_INVALID, "bad arguments");
+  *h2d = (int64_t)sizeof(StepParams);               // step parameters (ids, lengths, positions)
+  *d2h = (int64_t)(kMaxBatch + 1) * 4;              // ids + error word
+  return OCRVL_OK;
+}
+
+int ocrvl_decode_greedy_device(ocrvl_model *m, ocrvl_seq *const *seqs, int n, const int32_t *first_ids, int steps,
+                               int32_t *out_ids) {
+  if (!m || !seqs || !first_ids || !out_ids) return fail(OCRVL_E_INVALID, "null argument");
+  if (n < 1 || n > kMaxBatch || steps < 1) return fail(OCRVL_E_INVALID, "batch must be 1..8, steps >= 1");
+  std::lock_guard<std::mutex> lk(m->mu);
+  if (!m->finalized) return fail(OCRVL_E_INVALID, "model not finalized");
+  if (int rc = set_device(m)) return rc;
+  const ocrvl_model_desc &d = m->desc;
+  StepParams &sp = *m->sp_h;
+  memset(&sp, 0, sizeof(sp));
+  sp.M = n;
+  sp.any_logits = 1;
+  int max_n = 0;
+  for (int i = 0; i < n; i++) {
+    ocrvl_seq *s = seqs[i];
+    if (!s || s->m != m) return fail(OCRVL_E_INVALID, "sequence belongs to another model");
+    for (int j = 0; j < i; j++)
+      if (seqs[j] == s) return fail(OCRVL_E_INVALID, "sequence repeated in one step");
+    if (s->len + steps > s->max_tokens) return fail(OCRVL_E_INVALID, "steps exceed the sequence's max_tokens");
+    if (s->len + steps > d.max_position) return fail(OCRVL_E_INVALID, "positions exceed the RoPE table");
+    if (first_ids[i] < 0 || first_ids[i] >= d.vocab_size) return fail(OCRVL_E_INVALID, "token id outside vocab");
+    sp.tok[i] = first_ids[i];
+    sp.len[i] = s->len;
+    sp.pos[i][0] = sp.pos[i][1] = sp.pos[i][2] = s->len;
+    sp.need[i] = 1;
+    sp.bt[i] = s->bt_d;
+    max_n = std::max(max_n, s->len + 1);
+  }
+  sp.max_n = max_n;
+  // every page the loop will touch is allocated up front
+  for (int i = 0; i < n; i++) {
+    ocrvl_seq *s = seqs[i];
+    int need_pages = (s->len + steps + kPageTokens - 1) / kPageTokens;
+    int first_new = (int)s->pages.size();
+    if (need_pages - first_new > (int)m->free_pages.size()) return fail(OCRVL_E_NOMEM, "KV page pool exhausted");
+    std::vector<int> ids;
+    while ((int)s->pages.size() < need_pages) {
+      int pg = m->free_pages.back();
+      m->free_pages.pop_back();
+      s->pages.push_back(pg);
+    }
+    if (need_pages > first_new)
+      CK(cudaMemcpy(s->bt_d + first_new, s->pages.data() + first_new, (size_t)(need_pages - first_new) * 4,
+                    cudaMemcpyHostToDevice));
+  }
+  int *hist = nullptr;
+  CK(cudaMallocAsync((void **)&hist, (size_t)steps * n * 4, m->stream));
+  m->ctx.hist = hist;
+  CK(cudaMemsetAsync(m->ctx.hist_pos, 0, 4, m->stream));
+  CK(cudaMemcpyAsync(m->sp_d, &sp, sizeof(StepParams), cudaMemcpyHostToDevice, m->stream));
+  int rc = OCRVL_OK;
+  for (int st = 0; st < steps && rc == OCRVL_OK; st++) rc = launch_step(m, n, 1, 1, 1);
+  m->ctx.hist = nullptr;
+  if (rc == OCRVL_OK) {
+    cudaError_t e1 = cudaMemcpyAsync(out_ids, hist, (size_t)steps * n * 4, cudaMemcpyDeviceToHost, m->stream);
+    cudaError_t e2 = cudaMemcpyAsync(m->out_h, m->ctx.tok_out, (kMaxBatch + 1) * 4, cudaMemcpyDeviceToHost, m->stream);
+    if (e1 != cudaSuccess || e2 != cudaSuccess) rc = fail(OCRVL_E_CUDA, "copy of decoded ids failed");
+  }
+  cudaFreeAsync(hist, m->stream);
+  CK(cudaStreamSynchronize(m->stream));
+  if (rc) return rc;
+  if (m->out_h[kMaxBatch]) {
+    reset_after_timeout(m);
+    return fail(OCRVL_E_TIMEOUT, "device grid barrier timed out");
+  }
+  for (int i = 0; i < n; i++) seqs[i]->len += steps;
   return OCRVL_OK;
 }
 
@@ -1025,12 +1106,21 @@ int op_grid(int rows) {
   return std::max(1, std::min(sms * 2, (rows + 7) / 8));
 }
 
-int op_gemv(const Ctx &c, const GemvArgs &a, int m, cudaStream_t st) {
-  size_t smem = (320 + (size_t)a.A.cols) * 4 + (c.qtype == QT_Q8 ? (size_t)m * a.A.cols * 4 : (size_t)m * a.A.cols) + 64;
-  CK(cudaFuncSetAttribute(k_gemv, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-  k_gemv<<<op_grid(a.A.rows), kThreads, smem, st>>>(c, a, m);
+template <int QT>
+int op_gemv_q(const Ctx &c, const GemvArgs &a, int m, cudaStream_t st) {
+  // the batched form (m > 1) keeps kMaxBatch input vectors in shared memory
+  size_t smem = (m > 1 ? gemv_smem_total(QT, kMaxBatch, a.A.cols, kStagesMB)
+                       : gemv_smem_total(QT, 1, a.A.cols, kStagesM1)) + 64;
+  CK(cudaFuncSetAttribute(k_gemv<QT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  k_gemv<QT><<<op_grid(a.A.rows), kThreads, smem, st>>>(c, a, m);
   CK(cudaGetLastError());
   return OCRVL_OK;
+}
+
+int op_gemv(const Ctx &c, const GemvArgs &a, int m, cudaStream_t st) {
+  if (c.qtype == QT_Q4) return op_gemv_q<QT_Q4>(c, a, m, st);
+  if (c.qtype == QT_Q6) return op_gemv_q<QT_Q6>(c, a, m, st);
+  return op_gemv_q<QT_Q8>(c, a, m, st);
 }
 
 std::mutex g_scratch_mu;

@@ -246,6 +246,25 @@ class Runtime:
                                       _ptr(out), _ptr(logits)))
         return out, logits
 
+    def decode_device(self, seqs, first_ids, steps: int) -> np.ndarray:
+        """Greedy decode of ``steps`` tokens per sequence with device-side
+        token feedback (no host round trip per token).  Returns [steps, n] ids."""
+        n = len(seqs)
+        arr = (C.c_void_p * n)(*[s._h for s in seqs])
+        first = _i32(first_ids)
+        out = np.zeros((steps, n), np.int32)
+        _lib.check(self._L.ocrvl_decode_greedy_device(self._h, arr, n, _ptr(first), int(steps), _ptr(out)))
+        return out
+
+    @property
+    def stream_handle(self) -> int:
+        return int(self._L.ocrvl_model_stream(self._h) or 0)
+
+    def step_io_bytes(self, n: int):
+        h2d, d2h = C.c_int64(), C.c_int64()
+        _lib.check(self._L.ocrvl_step_io_bytes(self._h, int(n), C.byref(h2d), C.byref(d2h)))
+        return h2d.value, d2h.value
+
     def generate(self, ids: Sequence[int], max_new: int) -> List[int]:
         return self.generate_with_options(ids, GenerateOptions(max_new_tokens=max_new)).tokens
 
