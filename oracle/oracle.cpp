@@ -922,6 +922,11 @@ float orc_quantize_row(int type, const float *w, int cols, uint8_t *data) {
 
 void orc_unpack_row(int type, const uint8_t *p, int cols, int8_t *out) { unpack_row(type, p, cols, out); }
 float orc_quantize_x(const float *x, int n, uint8_t *xq) { return quantize_x(x, n, xq); }
+int32_t orc_dot_u8s8(const int8_t *w, const uint8_t *xq, int n) { return dot_u8s8(w, xq, n); }
+float orc_vnni_finalize(int32_t dot, int32_t rowsum, float scale_x, float scale_w) {
+  return vnni_finalize(dot, rowsum, scale_x, scale_w);
+}
+float orc_dot_q8_f32(const int8_t *w, const float *x, int n) { return dot_q8_f32(w, x, n); }
 
 static QMat make_qmat(int type, int rows, int cols, const float *scales, const void *data) {
   QMat m;

@@ -74,6 +74,12 @@ float orc_quantize_row(int type, const float *w, int cols, uint8_t *packed);
 void orc_unpack_row(int type, const uint8_t *packed, int cols, int8_t *out);
 /* quantizeXForVNNI (quant.go:2087-2115, dot_vnni_amd64.s:434-500). */
 float orc_quantize_x(const float *x, int n, uint8_t *xq);
+/* dotQ8VNNICore (dot_vnni_amd64.s): sum of w[i] * xq[i] in int32. */
+int32_t orc_dot_u8s8(const int8_t *w, const uint8_t *xq, int n);
+/* finalizeDotQ8VNNI lane (dot_vnni_amd64.s:1043-1090). */
+float orc_vnni_finalize(int32_t dot, int32_t rowsum, float scale_x, float scale_w);
+/* dotQ8 fp32 FMA order (quant.go:2062-2198), unscaled. */
+float orc_dot_q8_f32(const int8_t *w, const float *x, int n);
 /* matVecMaybeQuant semantics per type: Q4/Q6 via int8 activations, Q8 via
  * fp32 FMA dots.  data = packed rows as stored in GGUF. */
 void orc_matvec(int type, int rows, int cols, const float *scales, const void *data,

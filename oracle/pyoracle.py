@@ -61,6 +61,12 @@ def lib():
         L.orc_unpack_row.argtypes = [I, P, I, P]
         L.orc_quantize_x.restype = F
         L.orc_quantize_x.argtypes = [P, I, P]
+        L.orc_dot_u8s8.restype = C.c_int32
+        L.orc_dot_u8s8.argtypes = [P, P, I]
+        L.orc_vnni_finalize.restype = F
+        L.orc_vnni_finalize.argtypes = [C.c_int32, C.c_int32, F, F]
+        L.orc_dot_q8_f32.restype = F
+        L.orc_dot_q8_f32.argtypes = [P, P, I]
         L.orc_matvec.argtypes = [I, I, I, P, P, P, P]
         L.orc_matvec_add_rmsnorm.argtypes = [I, I, I, P, P, P, P, P, F, I, P]
         L.orc_swiglu.argtypes = [I, I, I, P, P, P, P, P, P]

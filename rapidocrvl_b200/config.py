@@ -27,6 +27,7 @@ class Config:
     rope_theta: float = 0.0
     mrope_section: list = field(default_factory=lambda: [16, 24, 24])
     vision_num_hidden_layers: int = 0
+    spatial_merge_size: int = 0
     image_token_id: int = 0
 
     @property
@@ -50,7 +51,8 @@ class Config:
             "rope_theta": self.rope_theta,
             "rope_scaling": {"mrope_section": list(self.mrope_section), "type": "mrope"},
             "image_token_id": self.image_token_id,
-            "vision_config": {"num_hidden_layers": self.vision_num_hidden_layers},
+            "vision_config": {"num_hidden_layers": self.vision_num_hidden_layers,
+                              "spatial_merge_size": self.spatial_merge_size},
         }
 
 
@@ -82,6 +84,7 @@ def loads(text: str) -> Config:
         c.mrope_section = [int(v) for v in rs["mrope_section"]]
     vc = raw.get("vision_config") or {}
     c.vision_num_hidden_layers = int(vc.get("num_hidden_layers", 0))
+    c.spatial_merge_size = int(vc.get("spatial_merge_size", 0))
     if c.head_dim == 0 and c.num_attention_heads != 0:
         c.head_dim = c.hidden_size // c.num_attention_heads
     if c.num_key_value_heads == 0:

@@ -122,13 +122,7 @@ def quantize_rows(typ: int, w: np.ndarray):
     if typ == Q6_ROW:
         scale, inv, zero = _row_scales(w, 31.0)
         v = (np.clip(_round_half_away(w * inv[:, None]), -31, 31) + 32).astype(np.uint32)
-        pad = (-cols) % 4
-        if pad:
-            v = np.concatenate([v, np.zeros((rows, pad), np.uint32)], axis=1)
-        g = v.reshape(rows, -1, 4)
-        word = g[:, :, 0] | (g[:, :, 1] << 6) | (g[:, :, 2] << 12) | (g[:, :, 3] << 18)
-        b = np.stack([word & 0xFF, (word >> 8) & 0xFF, (word >> 16) & 0xFF], axis=2).astype(np.uint8)
-        packed = b.reshape(rows, -1)[:, : packed_row_bytes(Q6_ROW, cols)].copy()
+        packed = pack_q6_fields(v)
         packed[zero] = 0
         return scale, packed
     raise ValueError(f"unsupported quantized type {typ}")
@@ -148,14 +142,34 @@ def unpack_rows(typ: int, packed: np.ndarray, cols: int) -> np.ndarray:
         out[:, 1::2] = hi
         return out[:, :cols].astype(np.int8)
     if typ == Q6_ROW:
-        nb = packed.shape[1]
-        padded = np.zeros((rows, (nb + 2) // 3 * 3), np.uint32)
-        padded[:, :nb] = packed
-        g = padded.reshape(rows, -1, 3)
-        word = g[:, :, 0] | (g[:, :, 1] << 8) | (g[:, :, 2] << 16)
-        vals = np.stack([(word >> s) & 0x3F for s in (0, 6, 12, 18)], axis=2).reshape(rows, -1)
-        return (vals[:, :cols].astype(np.int16) - 32).astype(np.int8)
+        return (q6_fields(packed, cols).astype(np.int16) - 32).astype(np.int8)
     raise ValueError(f"unsupported quantized type {typ}")
+
+
+def pack_q6_fields(v: np.ndarray) -> np.ndarray:
+    """Pack [rows, cols] 6-bit fields, four per three bytes little endian
+    (putQ6, quant.go:2886-2895); a partial last group leaves its unused bits 0."""
+    v = np.asarray(v, dtype=np.uint32) & 0x3F
+    rows, cols = v.shape
+    pad = (-cols) % 4
+    if pad:
+        v = np.concatenate([v, np.zeros((rows, pad), np.uint32)], axis=1)
+    g = v.reshape(rows, -1, 4)
+    word = g[:, :, 0] | (g[:, :, 1] << 6) | (g[:, :, 2] << 12) | (g[:, :, 3] << 18)
+    b = np.stack([word & 0xFF, (word >> 8) & 0xFF, (word >> 16) & 0xFF], axis=2).astype(np.uint8)
+    return b.reshape(rows, -1)[:, : packed_row_bytes(Q6_ROW, cols)].copy()
+
+
+def q6_fields(packed: np.ndarray, cols: int) -> np.ndarray:
+    """The [rows, cols] 6-bit fields of packed Q6 rows (getQ6, quant.go:2897-2906)."""
+    packed = np.ascontiguousarray(packed, dtype=np.uint8)
+    rows, nb = packed.shape
+    padded = np.zeros((rows, (nb + 2) // 3 * 3), np.uint32)
+    padded[:, :nb] = packed
+    g = padded.reshape(rows, -1, 3)
+    word = g[:, :, 0] | (g[:, :, 1] << 8) | (g[:, :, 2] << 16)
+    vals = np.stack([(word >> s) & 0x3F for s in (0, 6, 12, 18)], axis=2).reshape(rows, -1)
+    return vals[:, :cols].astype(np.uint8)
 
 
 # ---------------------------------------------------------------------------

@@ -76,6 +76,57 @@ def validate_generation_input(ids: Sequence[int], opts: GenerateOptions) -> None
         raise ValueError("input tokens must not be empty when max_new_tokens > 0")
 
 
+def expand_single_image_placeholder(ids: Sequence[int], n: int, image_token_id: int) -> List[int]:
+    """expandSingleImagePlaceholderInto (model.go:2834-2859): a prompt holding
+    exactly one image placeholder gets it repeated once per image embedding."""
+    ids = list(ids)
+    if sum(1 for t in ids if t == image_token_id) != 1 or n <= 1:
+        return ids
+    out: List[int] = []
+    for t in ids:
+        out.extend([t] * n if t == image_token_id else [t])
+    return out
+
+
+def multimodal_positions(ids: Sequence[int], image_grid, image_token_id: int, spatial_merge_size: int):
+    """multimodalPositionsInto (model.go:1717-1783): M-RoPE (t, h, w) positions
+    for a prompt whose image placeholders each stand for one merged patch of a
+    (grid_t, grid_h, grid_w) image, and the rope delta for generated tokens
+    (position = len(out) - 1 + delta)."""
+    ids = list(ids)
+    pos: List[tuple] = []
+    st = 0
+    next_pos = 0
+    while True:
+        try:
+            ed = ids.index(image_token_id, st)
+        except ValueError:
+            break
+        st_idx = next_pos
+        text_len = ed - st
+        pos.extend((st_idx + i,) * 3 for i in range(text_len))
+        if spatial_merge_size <= 0:
+            raise ValueError("config: vision_config.spatial_merge_size must be positive for image prompts")
+        gt = int(image_grid[0])
+        gh = int(image_grid[1]) // spatial_merge_size
+        gw = int(image_grid[2]) // spatial_merge_size
+        max_pos = st_idx + text_len - 1
+        base = text_len + st_idx
+        for t in range(gt):
+            for h in range(gh):
+                for w in range(gw):
+                    pos.append((base + t, base + h, base + w))
+                    max_pos = max(max_pos, base + t, base + h, base + w)
+        next_pos = max_pos + 1
+        st = ed + gt * gh * gw
+    if st < len(ids):
+        pos.extend((next_pos + i,) * 3 for i in range(len(ids) - st))
+        next_pos = next_pos + len(ids) - st
+    if not pos:
+        return pos, 0
+    return pos, next_pos - len(ids)
+
+
 def normalize_quantization(q: str) -> str:
     q = (q or "").strip().lower()
     return q or "f32"
@@ -288,3 +339,49 @@ class Runtime:
                                                  _ptr(eos_a), len(eos), _ptr(out),
                                                  len(out), C.byref(n)))
         return GenerateResult(tokens=out[: n.value].tolist(), prompt_tokens=len(ids_a))
+
+    def generate_with_image_embeds(self, ids: Sequence[int], image_embeds, image_grid,
+                                   opts: GenerateOptions) -> GenerateResult:
+        """GenerateWithImageEmbeds (model.go:1582-1707) with temperature 0:
+        image placeholders take the given embeddings (one row each, in order),
+        M-RoPE positions come from :func:`multimodal_positions`, and generated
+        tokens sit at len(out) - 1 + rope delta.  One ``ocrvl_step`` per token."""
+        validate_generate_options(opts)
+        validate_generation_input(ids, opts)
+        if opts.temperature > 0:
+            raise NotImplementedError("sampled generation (temperature > 0) is not on the CUDA path yet")
+        if opts.max_new_tokens == 0:
+            return GenerateResult(tokens=list(ids), prompt_tokens=len(ids))
+        c = self.cfg
+        emb = np.ascontiguousarray(np.asarray(image_embeds, dtype=np.float32).reshape(-1, c.hidden_size))
+        eos = DEFAULT_EOS_TOKEN_IDS if opts.eos_token_ids is None else list(opts.eos_token_ids)
+        inp = expand_single_image_placeholder(ids, len(emb), c.image_token_id)
+        positions, delta = multimodal_positions(inp, image_grid, c.image_token_id, c.spatial_merge_size)
+        n_img = sum(1 for t in inp if t == c.image_token_id)
+        if n_img > len(emb):
+            raise ValueError(f"too many image placeholder tokens: need {len(emb)}")
+        if n_img < len(emb):
+            raise ValueError(f"not enough image placeholder tokens: got {n_img} need {len(emb)}")
+        seq = self.new_sequence(len(inp) + opts.max_new_tokens)
+        try:
+            cursor = 0
+            nxt = -1
+            for i, t in enumerate(inp):
+                last = i == len(inp) - 1
+                if t == c.image_token_id:
+                    r, _ = self.step([seq], embeds=emb[cursor:cursor + 1], positions=[positions[i]], need_logits=last)
+                    cursor += 1
+                else:
+                    r, _ = self.step([seq], ids=[t], positions=[positions[i]], need_logits=last)
+                nxt = int(r[0])
+            out = list(inp)
+            for i in range(opts.max_new_tokens):
+                out.append(nxt)
+                if nxt in eos or i + 1 >= opts.max_new_tokens:
+                    break
+                p = len(out) - 1 + delta
+                r, _ = self.step([seq], ids=[nxt], positions=[(p, p, p)], need_logits=True)
+                nxt = int(r[0])
+            return GenerateResult(tokens=out, prompt_tokens=len(inp))
+        finally:
+            seq.close()
