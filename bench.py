@@ -301,7 +301,12 @@ def run_cuda(args):
         with open(traffic_path) as f:
             tj = json.load(f)
         if tj.get("quant") == args.quant:
-            line["roofline"]["traffic"] = tj.get("dram_bytes_per_step")
+            # one ncu capture at a fixed context, moved to this run's mean
+            # context by the K/V bytes per position (traffic grows with it)
+            mean_ctx = ctx0 + (args.steps + 1) / 2
+            line["roofline"]["traffic"] = (tj["dram_bytes_per_step"]
+                                           + (mean_ctx - tj["context"]) * tj["kv_bytes_per_position"])
+            line["roofline"]["traffic_source"] = tj.get("source")
     if rank == 0 and world == 1 and os.environ.get("OCRVL_BENCH_NO_CPU") is None:
         steps, dt, t_pre = cpu_reference_decode(d, args.quant, cfg, prompt, args.steps, 0, budget_s=15.0)
         line["cpu_baseline"] = {

@@ -1039,7 +1039,7 @@ __device__ __noinline__ void phase_attn(const Ctx *cp, int layer, int append_onl
     {
       const int nq = append_only ? 0 : G * H4, nk = cnt * H4, nv4 = cnt * D4;
       const int ntask = nq + nk + nv4;
-      constexpr int U = 2;
+      constexpr int U = 4;
 #pragma unroll 1
       for (int base = threadIdx.x; base < ntask; base += kThreads * U) {
         float4 ra[U], rb[U];
@@ -1221,15 +1221,40 @@ __device__ __noinline__ void phase_attn(const Ctx *cp, int layer, int append_onl
         if (lane == 0) dinv[warp] = __fdiv_rn(1.0f, den);
       }
       __syncthreads();
+      // one float4 of one head per thread; the chunk partials are fetched
+      // kMergeBatch at a time so that their L2 round trips overlap, and
+      // accumulated in chunk order
+      constexpr int kMergeBatch = 8;
 #pragma unroll 1
-      for (int p = threadIdx.x; p < G * D; p += kThreads) {
-        int hh = p / D, d = p % D;
-        const float *po = c.part_o + ((hbase + hh) * c.max_chunks) * D + d;
+      for (int p = threadIdx.x; p < G * D4; p += kThreads) {
+        const int hh = p / D4, d4 = p % D4;
+        const float4 *po = (const float4 *)(c.part_o + ((hbase + hh) * c.max_chunks) * D) + d4;
         const float *s = scl + hh * c.max_chunks;
-        float acc = __ldcg(c.part_t + (hbase + hh) * D + d);
-#pragma unroll 4
-        for (int k = 0; k < nch; k++) acc = __fmaf_rn(s[k], __ldcg(po + (size_t)k * D), acc);
-        c.head[(hbase + hh) * D + d] = __fmul_rn(acc, dinv[hh]);
+        float4 acc = __ldcg((const float4 *)(c.part_t + (hbase + hh) * D) + d4);
+#pragma unroll 1
+        for (int k0 = 0; k0 < nch; k0 += kMergeBatch) {
+          float4 v[kMergeBatch];
+#pragma unroll
+          for (int u = 0; u < kMergeBatch; u++)
+            if (k0 + u < nch) v[u] = __ldcg(po + (size_t)(k0 + u) * D4);
+#pragma unroll
+          for (int u = 0; u < kMergeBatch; u++) {
+            if (k0 + u < nch) {
+              const float w = s[k0 + u];
+              acc.x = __fmaf_rn(w, v[u].x, acc.x);
+              acc.y = __fmaf_rn(w, v[u].y, acc.y);
+              acc.z = __fmaf_rn(w, v[u].z, acc.z);
+              acc.w = __fmaf_rn(w, v[u].w, acc.w);
+            }
+          }
+        }
+        const float di = dinv[hh];
+        float4 o;
+        o.x = __fmul_rn(acc.x, di);
+        o.y = __fmul_rn(acc.y, di);
+        o.z = __fmul_rn(acc.z, di);
+        o.w = __fmul_rn(acc.w, di);
+        ((float4 *)(c.head + (hbase + hh) * D))[d4] = o;
       }
     }
     __syncthreads();
