@@ -183,6 +183,20 @@ int ocrvl_op_swiglu(int type, int rows, int cols, const void *wg, const float *s
 int ocrvl_op_argmax(int type, int rows, int cols, const void *w, const float *scale,
                     const int32_t *rowsum, int m, const float *x, int32_t *ids, void *stream);
 
+/* The same argmax as ocrvl_op_argmax for callers that must not allocate
+ * device memory (no counterpart in the reference).  ocrvl_op_argmax
+ * cudaMalloc's a small key buffer on first use; a server that has reserved the
+ * GPU's memory for its own pools, or a loop that cannot afford the device
+ * synchronisation cudaMalloc may cause, uses this variant, which keeps the keys
+ * in a fixed static device array and allocates nothing.  Limit: m <= 8
+ * vectors (64 bytes of keys); larger m returns OCRVL_E_INVALID.  The first
+ * call on a device looks up the array's device address; make it before any
+ * stream capture.  Every call clears and reuses the same array, so calls that
+ * overlap on the GPU (other streams or threads on the same device) race and
+ * must be ordered by the caller. */
+int ocrvl_op_argmax_noalloc(int type, int rows, int cols, const void *w, const float *scale,
+                            const int32_t *rowsum, int m, const float *x, int32_t *ids, void *stream);
+
 /* out = RMSNorm(x, w, eps) for m vectors of n (tensor.RMSNorm). */
 int ocrvl_op_rmsnorm(int n, int m, const float *x, const float *w, float eps, float *out, void *stream);
 

@@ -71,6 +71,7 @@ SIGNATURES = {
     "ocrvl_op_matvec_add_rmsnorm": (I, [I, I, I, P, P, P, I, P, P, I, P, F, P, P, P]),
     "ocrvl_op_swiglu": (I, [I, I, I, P, P, P, P, P, P, I, P, P, P]),
     "ocrvl_op_argmax": (I, [I, I, I, P, P, P, I, P, P, P]),
+    "ocrvl_op_argmax_noalloc": (I, [I, I, I, P, P, P, I, P, P, P]),
     "ocrvl_op_rmsnorm": (I, [I, I, P, P, F, P, P]),
 }
 

@@ -1247,3 +1247,78 @@ int ocrvl_op_rmsnorm(int n, int m, const float *x, const float *w, float eps, fl
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Allocation-free argmax (ocrvl_op_argmax_noalloc)
+//
+// ocrvl_op_argmax keeps its per-vector argmax keys in device memory that it
+// cudaMalloc's on first use.  Some callers must not allocate device memory at
+// all: a server that reserves the GPU's memory for its own pools at start-up
+// (a cudaMalloc from inside a request can then fail), or a latency-critical
+// loop where cudaMalloc may synchronize the device and stall other streams.
+// This variant keeps the keys in a fixed file-scope device array instead.
+//
+// Limit: kNoAllocArgmaxKeys keys (one 64-bit key per input vector, i.e. at
+// most 8 vectors per call; 64 bytes that every GPU loading this library holds
+// until the process exits).  The host obtains the array's device address with
+// cudaGetSymbolAddress once per device, on the first call made with that
+// device current; make that first call before any stream capture.  All calls
+// share the one array: the keys are cleared at the start of every call, and
+// calls whose kernels overlap on the GPU (different streams, or different
+// host threads on one device) race on it and must be ordered by the caller.
+// ---------------------------------------------------------------------------
+namespace {
+
+constexpr int kNoAllocArgmaxKeys = kMaxBatch;
+static __device__ __align__(256) unsigned long long g_noalloc_argmax_keys[kNoAllocArgmaxKeys];
+
+std::mutex g_noalloc_mu;
+unsigned long long *g_noalloc_keys_dev[64];  // device address of the array, per device
+
+}  // namespace
+
+extern "C" {
+
+int ocrvl_op_argmax_noalloc(int type, int rows, int cols, const void *w, const float *scale, const int32_t *rowsum,
+                            int m, const float *x, int32_t *ids, void *stream) {
+  if (m > kNoAllocArgmaxKeys)
+    return fail(OCRVL_E_INVALID, "m = " + std::to_string(m) + " exceeds the " + std::to_string(kNoAllocArgmaxKeys) +
+                                     " vectors the static argmax scratch holds");
+  if (int rc = op_check(type, rows, cols, m)) return rc;
+  int dev = 0;
+  CK(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= 64) return fail(OCRVL_E_INVALID, "device index out of range");
+  unsigned long long *keys = nullptr;
+  {
+    std::lock_guard<std::mutex> lk(g_noalloc_mu);
+    if (!g_noalloc_keys_dev[dev]) {
+      // the device address of the file-scope array on the current device (the
+      // host-side name g_noalloc_argmax_keys is not a device pointer)
+      void *p = nullptr;
+      cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_argmax_keys);
+      if (e != cudaSuccess) return fail(OCRVL_E_CUDA, std::string("cudaGetSymbolAddress: ") + cudaGetErrorString(e));
+      g_noalloc_keys_dev[dev] = (unsigned long long *)p;
+    }
+    keys = g_noalloc_keys_dev[dev];
+  }
+  cudaStream_t st = (cudaStream_t)stream;
+  // the array keeps the previous call's keys: clear the ones this call uses
+  CK(cudaMemsetAsync(keys, 0, (size_t)m * sizeof(unsigned long long), st));
+  Ctx c = op_ctx(type, 0.0f);
+  GemvArgs a;
+  memset(&a, 0, sizeof(a));
+  a.A = op_mat(type, rows, cols, w, scale, rowsum);
+  a.row_end = rows;
+  a.src = x;
+  a.ld = cols;
+  a.mode = PRO_PLAIN;
+  a.epi = EPI_ARGMAX;
+  a.ldo = rows;
+  a.argkey = keys;
+  if (int rc = op_gemv(c, a, m, st)) return rc;
+  k_argmax_ids<<<1, 32, 0, st>>>(keys, m, ids);
+  CK(cudaGetLastError());
+  return OCRVL_OK;
+}
+
+}  // extern "C"
