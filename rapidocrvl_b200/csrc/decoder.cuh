@@ -91,37 +91,26 @@ __device__ __forceinline__ unsigned long long gtimer() {
 // ---------------------------------------------------------------------------
 // Small block-level helpers
 // ---------------------------------------------------------------------------
+// Block reductions with a single __syncthreads: warp partials go to red[0..7],
+// then every thread reduces the eight partials itself.  Callers give each
+// reduction its own red slots (no barrier protects them from the next write).
 __device__ __forceinline__ float block_max(float v, float *red) {
   for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
-  int w = threadIdx.x >> 5, l = threadIdx.x & 31;
-  __syncthreads();
-  if (l == 0) red[w] = v;
-  __syncthreads();
-  if (w == 0) {
-    v = l < (kThreads / 32) ? red[l] : -INFINITY;
-    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
-    if (l == 0) red[0] = v;
-  }
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
   __syncthreads();
   float r = red[0];
-  __syncthreads();
+#pragma unroll
+  for (int w = 1; w < kThreads / 32; w++) r = fmaxf(r, red[w]);
   return r;
 }
 
 __device__ __forceinline__ int block_sum_int(int v, int *red) {
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-  int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
   __syncthreads();
-  if (l == 0) red[w] = v;
-  __syncthreads();
-  if (w == 0) {
-    v = l < (kThreads / 32) ? red[l] : 0;
-    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-    if (l == 0) red[0] = v;
-  }
-  __syncthreads();
-  int r = red[0];
-  __syncthreads();
+  int r = 0;
+#pragma unroll
+  for (int w = 0; w < kThreads / 32; w++) r += red[w];
   return r;
 }
 
@@ -136,16 +125,11 @@ __device__ float ss_rmsnorm(const float *x, int n, float *red) {
     red[threadIdx.x] = a;
   }
   __syncthreads();
-  if (threadIdx.x == 0) {
-    float r[16];
-    for (int l = 0; l < 16; l++)
-      r[l] = __fadd_rn(__fadd_rn(red[l], red[16 + l]), __fadd_rn(red[32 + l], red[48 + l]));
-    red[64] = tree16(r);
-  }
-  __syncthreads();
-  float s = red[64];
-  __syncthreads();
-  return s;
+  // every thread folds the 64 slots the same way (no second barrier)
+  float r[16];
+#pragma unroll
+  for (int l = 0; l < 16; l++) r[l] = __fadd_rn(__fadd_rn(red[l], red[16 + l]), __fadd_rn(red[32 + l], red[48 + l]));
+  return tree16(r);
 }
 
 // Sum of squares of the fused matvec+AddRMSNorm kernels (fused_matvec2.go):
@@ -174,35 +158,32 @@ __device__ float ss_fused(const float *v, int n, bool vnni, float *red) {
     red[t] = a;
   }
   __syncthreads();
-  if (t == 0) {
-    float ss = 0.0f;
-    for (int wk = 0; wk < workers; wk++) {
-      int s = wk * chunk, e = min(n, s + chunk);
-      float part = 0.0f;
-      if (s < e) {
-        const float *r = red + wk * lanes;
-        if (vnni) {
-          if (e - s >= 16) {
-            part = tree16(r);
-          } else {
-            for (int i = s; i < e; i++) part = __fadd_rn(part, __fmul_rn(v[i], v[i]));
-          }
+  // every thread adds the worker partials in worker order (no second barrier)
+  float ss = 0.0f;
+  for (int wk = 0; wk < workers; wk++) {
+    int s = wk * chunk, e = min(n, s + chunk);
+    float part = 0.0f;
+    if (s < e) {
+      const float *r = red + wk * lanes;
+      if (vnni) {
+        if (e - s >= 16) {
+          part = tree16(r);
         } else {
-          part = __fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(r[0], r[1]), __fadd_rn(r[2], r[3])),
-                                     __fadd_rn(r[4], r[5])),
-                           __fadd_rn(r[6], r[7]));
-          int nb = (e - s) / 8 * 8;
-          for (int i = s + nb; i < e; i++) part = __fadd_rn(part, __fmul_rn(v[i], v[i]));
+          for (int i = s; i < e; i++) part = __fadd_rn(part, __fmul_rn(v[i], v[i]));
         }
+      } else {
+        part = __fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(r[0], r[1]), __fadd_rn(r[2], r[3])), __fadd_rn(r[4], r[5])),
+                         __fadd_rn(r[6], r[7]));
+        int nb = (e - s) / 8 * 8;
+        for (int i = s + nb; i < e; i++) part = __fadd_rn(part, __fmul_rn(v[i], v[i]));
       }
-      ss = __fadd_rn(ss, part);
     }
-    red[300] = ss;
+    ss = __fadd_rn(ss, part);
   }
-  __syncthreads();
-  float r = red[300];
-  __syncthreads();
-  return r;
+  // the tail terms above read v after the barrier: keep v unchanged until
+  // every thread has read it (uniform condition, depends on n only)
+  if ((vnni && chunk < 16) || (!vnni && chunk % 8 != 0)) __syncthreads();
+  return ss;
 }
 
 // ---------------------------------------------------------------------------
@@ -245,8 +226,9 @@ __device__ __forceinline__ void g2s_f32(float *dst, const float *src, int n) {
   }
 }
 
-// x = (x * w) * scale over shared x, w from global (mulScaleFMA order).
-__device__ __forceinline__ void norm_apply(float *x, const float *w, int n, float scale) {
+// x = (x * w) * scale over shared x (mulScaleFMA order); w in shared memory
+// (staged by the GEMV phase) or, when w_global, read from global memory.
+__device__ __forceinline__ void norm_apply(float *x, const float *w, bool w_global, int n, float scale) {
   constexpr int U = 4;
   const int n4 = n >> 2;
   for (int base = threadIdx.x; base < n4; base += kThreads * U) {
@@ -254,7 +236,7 @@ __device__ __forceinline__ void norm_apply(float *x, const float *w, int n, floa
 #pragma unroll
     for (int u = 0; u < U; u++) {
       int i = base + u * kThreads;
-      if (i < n4) wv[u] = __ldg((const float4 *)w + i);
+      if (i < n4) wv[u] = w_global ? __ldg((const float4 *)w + i) : ((const float4 *)w)[i];
     }
 #pragma unroll
     for (int u = 0; u < U; u++) {
@@ -271,10 +253,15 @@ __device__ __forceinline__ void norm_apply(float *x, const float *w, int n, floa
   }
 }
 
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+
 // Shared-memory layout of the prologue: [red 320 f32 (sx at 304.., sumq at
 // 312..)][tmp n f32][x area].  Out of line: every GEMV phase shares one copy.
+// The caller's cp.async copies (row scales, row sums, norm weights) are
+// complete and visible after the first barrier here.  Barriers: one after the
+// gather, one per reduction, one after the normalisation, one at the end.
 __device__ __noinline__ void gemv_prologue(int qt, int M, const float *src, int ld, const int *tok, int n,
-                                           int mode, const float *w, float eps, float *smem) {
+                                           int mode, const float *w, bool w_global, float eps, float *smem) {
   float *red = smem;
   float *sxs = smem + 304;
   int *sqs = (int *)(smem + 312);
@@ -286,18 +273,19 @@ __device__ __noinline__ void gemv_prologue(int qt, int M, const float *src, int 
     const float *s = src + (size_t)(tok ? tok[m] : m) * ld;
     float *dst = vnni ? tmp : (float *)area + (size_t)m * n;
     g2s_f32(dst, s, n);
+    cp_async_wait_all();
     __syncthreads();
     if (mode != PRO_PLAIN) {
       float ss = mode == PRO_RMSNORM ? ss_rmsnorm(dst, n, red) : ss_fused(dst, n, vnni, red);
       float scale = fast_rsqrt(__fadd_rn(__fdiv_rn(ss, (float)n), eps));
-      norm_apply(dst, w, n, scale);
+      norm_apply(dst, w, w_global, n, scale);
       __syncthreads();
     }
     if (vnni) {
       float mx = 0.0f;
 #pragma unroll 1
       for (int i = threadIdx.x; i < n; i += kThreads) mx = fmaxf(mx, fabsf(dst[i]));
-      mx = block_max(mx, red);
+      mx = block_max(mx, red + 160);
       float sx = 1.0f, inv = 0.0f;
       if (mx != 0.0f) {
         sx = __fdiv_rn(mx, 127.0f);
@@ -313,15 +301,15 @@ __device__ __noinline__ void gemv_prologue(int qt, int M, const float *src, int 
         acc += v;
         q[half ? (i & 1) * half + (i >> 1) : i] = (uint8_t)v;  // Q4: even | odd halves
       }
-      acc = block_sum_int(acc, (int *)red);
+      acc = block_sum_int(acc, (int *)(red + 176));
       if (threadIdx.x == 0) {
         sxs[m] = sx;
         sqs[m] = acc;
       }
-      __syncthreads();
     }
+    // tmp / red are rewritten by the next sequence
+    __syncthreads();
   }
-  __syncthreads();
 }
 
 __device__ __forceinline__ XIn gemv_inputs(int n, float *smem) {
@@ -341,6 +329,15 @@ __device__ __forceinline__ size_t gemv_smem_bytes(int qt, int M, int n) {
 // Bulk copies (TMA, cp.async.bulk) and mbarriers
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ uint32_t smem_u32(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+// Asynchronous global -> shared copies of read-only weights (row scales, row
+// sums, norm weights); completed by cp_async_wait_all in the GEMV prologue.
+__device__ __forceinline__ void cp_async4(void *dst, const void *src) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async16(void *dst, const void *src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
 
 __device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
   asm volatile("mbarrier.init.shared.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
@@ -397,7 +394,7 @@ __device__ __forceinline__ uint32_t lds4(const void *p) {
 // odd halves of xq gives sum((q+8)*xq), corrected by 8*sum(xq).
 template <int M_, int RB>
 __device__ __forceinline__ void dot_q4(const DMat &A, const uint8_t *const *rp, const int *rows, int M, const XIn &x,
-                                       int li, int lpr, float (*out)[M_]) {
+                                       const float *scl, const int32_t *rsm, int li, int lpr, float (*out)[M_]) {
   const int CH = A.pitch >> 4, n = A.cols;
   uint32_t acc[RB][M_];
 #pragma unroll
@@ -439,8 +436,8 @@ __device__ __forceinline__ void dot_q4(const DMat &A, const uint8_t *const *rp, 
   if ((li) != 0) return;
 #pragma unroll
   for (int r = 0; r < RB; r++) {
-    const int32_t rs = __ldg(A.rowsum + rows[r]);
-    const float sw = __ldg(A.scale + rows[r]);
+    const int32_t rs = rsm[r];
+    const float sw = scl[r];
 #pragma unroll
     for (int m = 0; m < M_; m++) {
       if (m >= M) break;
@@ -456,7 +453,7 @@ __device__ __forceinline__ uint32_t q6_spread(uint32_t g) {
 }
 template <int M_, int RB>
 __device__ __forceinline__ void dot_q6(const DMat &A, const uint8_t *const *rp, const int *rows, int M, const XIn &x,
-                                       int li, int lpr, float (*out)[M_]) {
+                                       const float *scl, const int32_t *rsm, int li, int lpr, float (*out)[M_]) {
   const int CH = A.pitch / 48, n = A.cols;
   uint32_t acc[RB][M_];
 #pragma unroll
@@ -499,8 +496,8 @@ __device__ __forceinline__ void dot_q6(const DMat &A, const uint8_t *const *rp, 
   if (li != 0) return;
 #pragma unroll
   for (int r = 0; r < RB; r++) {
-    const int32_t rs = __ldg(A.rowsum + rows[r]);
-    const float sw = __ldg(A.scale + rows[r]);
+    const int32_t rs = rsm[r];
+    const float sw = scl[r];
 #pragma unroll
     for (int m = 0; m < M_; m++) {
       if (m >= M) break;
@@ -515,7 +512,7 @@ __device__ __forceinline__ void dot_q6(const DMat &A, const uint8_t *const *rp, 
 // reduced with xor-4/8/16 shuffles and the 16-lane tree with xor-2/1.
 template <int M_, int RB>
 __device__ __forceinline__ void dot_q8(const DMat &A, const uint8_t *const *rp, const int *rows, int M, const XIn &x,
-                                       int lane, float (*out)[M_]) {
+                                       const float *scl, int lane, float (*out)[M_]) {
   const int n = A.cols, NB = n >> 7;
   float acc[RB][M_][4];
 #pragma unroll
@@ -547,7 +544,7 @@ __device__ __forceinline__ void dot_q8(const DMat &A, const uint8_t *const *rp, 
   }
 #pragma unroll
   for (int r = 0; r < RB; r++) {
-    const float sw = __ldg(A.scale + rows[r]);
+    const float sw = scl[r];
 #pragma unroll
     for (int m = 0; m < M_; m++) {
       if (m >= M) break;
@@ -577,15 +574,18 @@ __device__ __forceinline__ int lanes_per_row(int qt, const DMat &A) {
   return l;
 }
 
+// scl[r] / rsm[r]: scale and row sum of row r of the batch (loaded by the
+// caller before the dots so their latency overlaps the dot products).
 template <int QT, int M_, int RB>
 __device__ __forceinline__ void rows_dot(const DMat &A, const uint8_t *const *rp, const int *rows, int M,
-                                         const XIn &x, int lane, int lpr, float (*out)[M_]) {
+                                         const XIn &x, const float *scl, const int32_t *rsm, int lane, int lpr,
+                                         float (*out)[M_]) {
   if (QT == QT_Q4)
-    dot_q4<M_, RB>(A, rp, rows, M, x, lane % lpr, lpr, out);
+    dot_q4<M_, RB>(A, rp, rows, M, x, scl, rsm, lane % lpr, lpr, out);
   else if (QT == QT_Q6)
-    dot_q6<M_, RB>(A, rp, rows, M, x, lane % lpr, lpr, out);
+    dot_q6<M_, RB>(A, rp, rows, M, x, scl, rsm, lane % lpr, lpr, out);
   else
-    dot_q8<M_, RB>(A, rp, rows, M, x, lane, out);
+    dot_q8<M_, RB>(A, rp, rows, M, x, scl, lane, out);
 }
 
 // ---------------------------------------------------------------------------
@@ -617,32 +617,11 @@ struct GemvArgs {
   unsigned long long *tslot;   // optional trace slot of this phase
 };
 
-// Contiguous slab of rows [lo, hi) of a GEMV owned by block `b` of `nb`; the
-// same split drives the L2 prefetch of the slab.
+// Contiguous slab of rows [lo, hi) of a GEMV owned by block `b` of `nb`.
 __device__ __forceinline__ void gemv_slab(int row_begin, int row_end, int b, int nb, int &lo, int &hi) {
   long long n = row_end - row_begin;
   lo = row_begin + (int)(n * b / nb);
   hi = row_begin + (int)(n * (b + 1) / nb);
-}
-
-__device__ __forceinline__ void prefetch_l2(const void *p, size_t bytes) {
-  uintptr_t a = (uintptr_t)p & ~(uintptr_t)15;
-  uintptr_t e = ((uintptr_t)p + bytes + 15) & ~(uintptr_t)15;
-  for (uintptr_t o = a; o < e; o += 32768) {
-    uint32_t sz = (uint32_t)((e - o) < 32768 ? (e - o) : 32768);
-    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(o), "r"(sz) : "memory");
-  }
-}
-
-// Issues L2 prefetches of block b's slab of rows [row_begin, row_end) of A
-// (packed rows, scales, row sums).  Called by one thread.
-__device__ __forceinline__ void prefetch_gemv_slab(const DMat &A, int row_begin, int row_end, int b, int nb) {
-  int lo, hi;
-  gemv_slab(row_begin, row_end, b, nb, lo, hi);
-  if (hi <= lo) return;
-  prefetch_l2(A.w + (size_t)lo * A.pitch, (size_t)(hi - lo) * A.pitch);
-  prefetch_l2(A.scale + lo, (size_t)(hi - lo) * 4);
-  prefetch_l2(A.rowsum + lo, (size_t)(hi - lo) * 4);
 }
 
 // Weight staging: each block streams its slab of packed rows through a ring
@@ -650,15 +629,22 @@ __device__ __forceinline__ void prefetch_gemv_slab(const DMat &A, int row_begin,
 // first stages are issued before the input prologue so weight transfer
 // overlaps the normalisation / quantisation of the input.
 constexpr int kStageBytes = 32768;
-constexpr int kStagesM1 = 3;   // stages for the single-sequence form
+constexpr int kStagesM1 = 4;   // stages for the single-sequence form
 constexpr int kStagesMB = 2;   // stages for the batched form
+// Row scales and row sums of a block's slab (A and B matrices) and the norm
+// weights are staged in shared memory with cp.async at the start of the
+// phase, when the slab has at most kSlabRowsMax rows and the norm vector at
+// most kNormStageMax entries (otherwise they are read from global memory).
+constexpr int kSlabRowsMax = 1024;
+constexpr int kNormStageMax = 2048;
+constexpr size_t kGemvAuxBytes = (size_t)4 * kSlabRowsMax * 4 + (size_t)kNormStageMax * 4;
 
 __host__ __device__ __forceinline__ size_t gemv_prologue_bytes(int qt, int nvec, int n) {
   size_t area = qt == QT_Q8 ? (size_t)nvec * n * 4 : (size_t)nvec * n;
   return ((320 + (size_t)n) * 4 + area + 127) / 128 * 128;
 }
 __host__ __device__ __forceinline__ size_t gemv_smem_total(int qt, int nvec, int n, int stages) {
-  return gemv_prologue_bytes(qt, nvec, n) + (size_t)stages * kStageBytes;
+  return gemv_prologue_bytes(qt, nvec, n) + (size_t)stages * kStageBytes + kGemvAuxBytes;
 }
 
 // Last block of the lm_head phase: keys -> ids (ties -> lowest id), key and
@@ -718,7 +704,32 @@ __device__ __noinline__ void phase_gemv_t(const Ctx *cp, const GemvArgs *ap, int
     mbar_fence_init();
     for (int st = 0; st < nst && st < kSt; st++) issue(st);
   }
-  gemv_prologue(qt, M, a.src, a.ld, a.src_tok ? c.sp->tok : nullptr, a.A.cols, a.mode, a.norm_w, c.eps, smem);
+  // stage the slab's row scales / row sums and the norm weights (cp.async,
+  // waited for inside the prologue)
+  float *aux = (float *)(stage + (size_t)kSt * kStageBytes);
+  const int nrows = hi - lo;
+  const bool staged = nrows <= kSlabRowsMax;
+  const bool vnni = qt != QT_Q8;
+  if (staged) {
+    for (int i = threadIdx.x; i < nrows; i += kThreads) {
+      cp_async4(aux + i, a.A.scale + lo + i);
+      if (vnni) cp_async4(aux + kSlabRowsMax + i, a.A.rowsum + lo + i);
+      if (two) {
+        cp_async4(aux + 2 * kSlabRowsMax + i, a.B.scale + lo + i);
+        if (vnni) cp_async4(aux + 3 * kSlabRowsMax + i, a.B.rowsum + lo + i);
+      }
+    }
+  }
+  const float *scl_a = staged ? aux : a.A.scale + lo;
+  const int32_t *rsm_a = staged ? (const int32_t *)(aux + kSlabRowsMax) : a.A.rowsum + lo;
+  const float *scl_b = staged ? aux + 2 * kSlabRowsMax : a.B.scale + lo;
+  const int32_t *rsm_b = staged ? (const int32_t *)(aux + 3 * kSlabRowsMax) : a.B.rowsum + lo;
+  const bool nw_staged = a.mode != PRO_PLAIN && a.A.cols <= kNormStageMax;
+  float *nw_s = aux + 4 * kSlabRowsMax;
+  if (nw_staged)
+    for (int i = threadIdx.x; i < a.A.cols / 4; i += kThreads) cp_async16(nw_s + 4 * i, a.norm_w + 4 * i);
+  gemv_prologue(qt, M, a.src, a.ld, a.src_tok ? c.sp->tok : nullptr, a.A.cols, a.mode, nw_staged ? nw_s : a.norm_w,
+                !nw_staged, c.eps, smem);
   const XIn x = gemv_inputs(a.A.cols, smem);
   if (a.copy_src && blockIdx.x == 0) {
     // layer 0: the embedding rows the prologue gathered become the residual
@@ -778,9 +789,19 @@ __device__ __noinline__ void phase_gemv_t(const Ctx *cp, const GemvArgs *ap, int
         rpa[r] = buf + (size_t)lr * P;
         rpb[r] = buf + (size_t)(srows + lr) * P;
       }
+      float sa[RB], sb[RB];
+      int32_t ra[RB], rb[RB];
+#pragma unroll
+      for (int r = 0; r < RB; r++) {
+        const int i = rows[r] - lo;
+        sa[r] = scl_a[i];
+        ra[r] = vnni ? rsm_a[i] : 0;
+        sb[r] = two ? scl_b[i] : 0.0f;
+        rb[r] = two && vnni ? rsm_b[i] : 0;
+      }
       float v[RB][M_], u[RB][M_];
-      rows_dot<QT, M_, RB>(a.A, rpa, rows, M, x, lane, lpr, v);
-      if (two) rows_dot<QT, M_, RB>(a.B, rpb, rows, M, x, lane, lpr, u);
+      rows_dot<QT, M_, RB>(a.A, rpa, rows, M, x, sa, ra, lane, lpr, v);
+      if (two) rows_dot<QT, M_, RB>(a.B, rpb, rows, M, x, sb, rb, lane, lpr, u);
       if ((lane % lpr) != 0) continue;
 #pragma unroll
       for (int r = 0; r < RB; r++) {
@@ -835,15 +856,270 @@ __device__ __noinline__ void phase_gemv_t(const Ctx *cp, const GemvArgs *ap, int
   __syncthreads();
 }
 
-// Rows per warp batch: enough 16-byte loads in flight per lane at M = 1; one
-// row per batch for the batched (M > 1) form.
+// ---------------------------------------------------------------------------
+// Single-sequence GEMV for the int8-activation types (Q4, Q6): x-stationary.
+// A row is split over lpr lanes, each lane owning the same chunk positions
+// k = li + lpr*j (j < XMAX) of every row it visits, so the lane keeps those
+// chunks of the quantised input in registers for the whole phase and reads
+// only weights from the shared-memory stages.  Each thread works on RB rows
+// at once with two dp4a chains per row; the int32 sums are exact, so the split
+// does not change results.
+// ---------------------------------------------------------------------------
+template <int QT>
+struct XsTraits;
+template <>
+struct XsTraits<QT_Q4> {
+  static constexpr int CB = 16;    // packed bytes per chunk (32 columns)
+  static constexpr int XMAX = 4;   // chunks per lane kept in registers
+  static constexpr int XW = 2;     // uint4 of activations per chunk (even, odd halves)
+  static constexpr int OFF = 8;    // stored nibble = q + 8
+};
+template <>
+struct XsTraits<QT_Q6> {
+  static constexpr int CB = 48;    // 64 columns
+  static constexpr int XMAX = 2;
+  static constexpr int XW = 4;
+  static constexpr int OFF = 32;   // stored field = q + 32
+};
+
+__host__ __device__ __forceinline__ int xs_lanes_per_row(int chunks, int xmax) {
+  int l = 1;
+  while (l < 32 && (chunks + l - 1) / l > xmax) l <<= 1;
+  return l;
+}
+
+// True when the x-stationary path handles a matrix of this pitch.
+template <int QT>
+__device__ __forceinline__ bool xs_fits(int pitch) {
+  const int ch = pitch / XsTraits<QT>::CB;
+  return pitch % XsTraits<QT>::CB == 0 && (ch + 31) / 32 <= XsTraits<QT>::XMAX;
+}
+
+// Partial dot of one row: the lane's chunks of the row at `w` against its
+// register-held activations.
+template <int QT>
+__device__ __forceinline__ uint32_t xs_row_dot(const uint8_t *w, const uint4 (*xr)[XsTraits<QT>::XW], int li,
+                                               int lpr, int CH) {
+  using T = XsTraits<QT>;
+  uint32_t a0 = 0, a1 = 0;
+#pragma unroll
+  for (int j = 0; j < T::XMAX; j++) {
+    const int k = li + lpr * j;
+    if (k >= CH) break;
+    if (QT == QT_Q4) {
+      const uint4 wv = lds16(w + 16 * k);
+      const uint32_t wd[4] = {wv.x, wv.y, wv.z, wv.w};
+      const uint32_t e4[4] = {xr[j][0].x, xr[j][0].y, xr[j][0].z, xr[j][0].w};
+      const uint32_t o4[4] = {xr[j][1].x, xr[j][1].y, xr[j][1].z, xr[j][1].w};
+#pragma unroll
+      for (int q = 0; q < 4; q++) {
+        a0 = __dp4a(wd[q] & 0x0F0F0F0Fu, e4[q], a0);
+        a1 = __dp4a((wd[q] >> 4) & 0x0F0F0F0Fu, o4[q], a1);
+      }
+    } else {
+      const uint4 wa = lds16(w + 48 * k), wb = lds16(w + 48 * k + 16), wc = lds16(w + 48 * k + 32);
+      const uint32_t wd[12] = {wa.x, wa.y, wa.z, wa.w, wb.x, wb.y, wb.z, wb.w, wc.x, wc.y, wc.z, wc.w};
+#pragma unroll
+      for (int t = 0; t < 4; t++) {
+        const uint32_t w0 = wd[3 * t], w1 = wd[3 * t + 1], w2 = wd[3 * t + 2];
+        const uint32_t f0 = q6_spread(w0 & 0xFFFFFFu), f1 = q6_spread(__funnelshift_r(w0, w1, 24) & 0xFFFFFFu);
+        const uint32_t f2 = q6_spread(__funnelshift_r(w1, w2, 16) & 0xFFFFFFu), f3 = q6_spread(w2 >> 8);
+        const uint4 xx = xr[j][t];
+        a0 = __dp4a(f0, xx.x, a0);
+        a1 = __dp4a(f1, xx.y, a1);
+        a0 = __dp4a(f2, xx.z, a0);
+        a1 = __dp4a(f3, xx.w, a1);
+      }
+    }
+  }
+  return a0 + a1;
+}
+
+template <int QT>
+__device__ __noinline__ void phase_gemv_xs(const Ctx *cp, const GemvArgs *ap, float *smem) {
+  using T = XsTraits<QT>;
+  constexpr int RB = 2;
+  constexpr int kSt = kStagesM1;
+  const Ctx &c = *cp;
+  const GemvArgs &a = *ap;
+  __shared__ __align__(8) uint64_t full[kSt];
+  const int P = a.A.pitch, n = a.A.cols, CH = P / T::CB;
+  const bool two = a.epi == EPI_SWIGLU;
+  int lo, hi;
+  gemv_slab(a.row_begin, a.row_end, blockIdx.x, gridDim.x, lo, hi);
+  uint8_t *stage = (uint8_t *)smem + gemv_prologue_bytes(QT, 1, n);
+  const int srows = kStageBytes / (P * (two ? 2 : 1));
+  const int nst = (hi - lo + srows - 1) / srows;
+  auto issue = [&](int st) {
+    const int r0 = lo + st * srows, nr = min(srows, hi - r0);
+    uint8_t *buf = stage + (size_t)(st % kSt) * kStageBytes;
+    const uint32_t bytes = (uint32_t)nr * P;
+    mbar_expect_tx(&full[st % kSt], two ? 2 * bytes : bytes);
+    bulk_g2s(buf, a.A.w + (size_t)r0 * P, bytes, &full[st % kSt]);
+    if (two) bulk_g2s(buf + (size_t)srows * P, a.B.w + (size_t)r0 * P, bytes, &full[st % kSt]);
+  };
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < kSt; i++) mbar_init(&full[i], 1);
+    mbar_fence_init();
+    for (int st = 0; st < nst && st < kSt; st++) issue(st);
+  }
+  // row scales / row sums of the slab and the norm weights (cp.async)
+  float *aux = (float *)(stage + (size_t)kSt * kStageBytes);
+  const int nrows = hi - lo;
+  const bool staged = nrows <= kSlabRowsMax;
+  if (staged) {
+    for (int i = threadIdx.x; i < nrows; i += kThreads) {
+      cp_async4(aux + i, a.A.scale + lo + i);
+      cp_async4(aux + kSlabRowsMax + i, a.A.rowsum + lo + i);
+      if (two) {
+        cp_async4(aux + 2 * kSlabRowsMax + i, a.B.scale + lo + i);
+        cp_async4(aux + 3 * kSlabRowsMax + i, a.B.rowsum + lo + i);
+      }
+    }
+  }
+  const float *scl_a = staged ? aux : a.A.scale + lo;
+  const int32_t *rsm_a = staged ? (const int32_t *)(aux + kSlabRowsMax) : a.A.rowsum + lo;
+  const float *scl_b = staged ? aux + 2 * kSlabRowsMax : a.B.scale + lo;
+  const int32_t *rsm_b = staged ? (const int32_t *)(aux + 3 * kSlabRowsMax) : a.B.rowsum + lo;
+  const bool nw_staged = a.mode != PRO_PLAIN && n <= kNormStageMax;
+  float *nw_s = aux + 4 * kSlabRowsMax;
+  if (nw_staged)
+    for (int i = threadIdx.x; i < n / 4; i += kThreads) cp_async16(nw_s + 4 * i, a.norm_w + 4 * i);
+  gemv_prologue(QT, 1, a.src, a.ld, a.src_tok ? c.sp->tok : nullptr, n, a.mode, nw_staged ? nw_s : a.norm_w,
+                !nw_staged, c.eps, smem);
+  const XIn x = gemv_inputs(n, smem);
+  if (a.copy_src && blockIdx.x == 0) {
+    // layer 0: the embedding row the prologue gathered becomes the residual
+    const float4 *s4 = (const float4 *)(a.src + (size_t)c.sp->tok[0] * a.ld);
+    float4 *d4 = (float4 *)a.copy_src;
+    for (int i = threadIdx.x; i < a.ld / 4; i += kThreads) d4[i] = __ldg(s4 + i);
+  }
+  if (a.tslot && blockIdx.x == 0 && threadIdx.x == 0) a.tslot[1] = gtimer();
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int lpr = xs_lanes_per_row(CH, T::XMAX);
+  const int rpw = 32 / lpr, li = lane % lpr, sub = lane / lpr;
+  // this lane's activation chunks
+  uint4 xr[T::XMAX][T::XW];
+#pragma unroll
+  for (int j = 0; j < T::XMAX; j++) {
+    const int k = li + lpr * j;
+#pragma unroll
+    for (int t = 0; t < T::XW; t++) {
+      if (k < CH) {
+        xr[j][t] = QT == QT_Q4 ? lds16(x.xq + (size_t)t * (n / 2) + 16 * k) : lds16(x.xq + 64 * k + 16 * t);
+      } else {
+        xr[j][t] = make_uint4(0, 0, 0, 0);
+      }
+    }
+  }
+  const float sx = x.sx[0];
+  const int32_t corr = T::OFF * x.sumq[0];
+  bool in_place = false;
+  if (a.epi == EPI_RESID) {
+    if (a.resid_mode == RESID_ALWAYS) {
+      in_place = true;
+    } else if (a.resid_mode == RESID_MASK) {
+      in_place = a.in_place_mask & 1;
+    } else if (a.resid_mode == RESID_ATTN) {
+      // Q4/Q6 use the in-place form only for caches of 2..6 tokens
+      // (matVecOutAddRMSNormCPU), the ...OutOnly form otherwise
+      // (model.go:3896-3908, 3975-3992, 4043-4062)
+      const int len = c.sp->len[0];
+      in_place = len >= 1 && len + 1 <= 6;
+    }
+  }
+  unsigned long long best = 0ull;
+  bool ok = true;
+  const int pass = (kThreads / 32) * rpw;  // rows one pass of the block covers per RB slot
+#pragma unroll 1
+  for (int st = 0; st < nst; st++) {
+    const int r0 = lo + st * srows, nr = min(srows, hi - r0);
+    const uint8_t *buf = stage + (size_t)(st % kSt) * kStageBytes;
+    if (!mbar_wait(&full[st % kSt], (uint32_t)((st / kSt) & 1), c.err)) ok = false;
+#pragma unroll 1
+    for (int base = warp * rpw; ok && base < nr; base += pass * RB) {
+      int lr[RB];
+      bool valid[RB];
+      uint32_t da[RB], db[RB];
+#pragma unroll
+      for (int r = 0; r < RB; r++) {
+        const int l = base + sub + r * pass;
+        valid[r] = l < nr;
+        lr[r] = valid[r] ? l : nr - 1;
+        da[r] = xs_row_dot<QT>(buf + (size_t)lr[r] * P, xr, li, lpr, CH);
+        db[r] = two ? xs_row_dot<QT>(buf + (size_t)(srows + lr[r]) * P, xr, li, lpr, CH) : 0u;
+      }
+#pragma unroll
+      for (int r = 0; r < RB; r++) {
+        for (int o = lpr >> 1; o > 0; o >>= 1) {
+          da[r] += __shfl_xor_sync(0xffffffffu, da[r], o);
+          if (two) db[r] += __shfl_xor_sync(0xffffffffu, db[r], o);
+        }
+      }
+      if (li != 0) continue;
+#pragma unroll
+      for (int r = 0; r < RB; r++) {
+        if (!valid[r]) continue;
+        const int i = r0 - lo + lr[r];
+        const int row = r0 + lr[r];
+        const float v = vnni_finalize((int32_t)da[r] - corr, rsm_a[i], sx, scl_a[i]);
+        if (a.epi == EPI_STORE) {
+          a.out[row] = v;
+        } else if (a.epi == EPI_RESID) {
+          const float t = __fadd_rn(__ldcg(a.resid + row), v);
+          a.vout[row] = t;
+          if (in_place) a.resid[row] = t;
+        } else if (a.epi == EPI_SWIGLU) {
+          const float u = vnni_finalize((int32_t)db[r] - corr, rsm_b[i], sx, scl_b[i]);
+          a.out[row] = silu_mul(v, u);
+        } else {
+          if (a.logits) a.logits[row] = v;
+          const unsigned long long k = argmax_key(v, row);
+          best = k > best ? k : best;
+        }
+      }
+    }
+    __syncthreads();  // stage buffer free
+    if (threadIdx.x == 0 && st + kSt < nst) issue(st + kSt);
+  }
+  if (a.epi == EPI_ARGMAX) {
+    for (int o = 16; o > 0; o >>= 1) {
+      const unsigned long long t = __shfl_xor_sync(0xffffffffu, best, o);
+      best = t > best ? t : best;
+    }
+    if (lane == 0 && best) atomicMax(a.argkey, best);
+    if (a.argmax_finish) {
+      __shared__ int is_last;
+      __threadfence();
+      __syncthreads();
+      if (threadIdx.x == 0) is_last = atomicAdd(c.lm_count, 1u) == gridDim.x - 1;
+      __syncthreads();
+      if (is_last) {
+        __threadfence();
+        argmax_finish(c, 1, a.feed);
+      }
+    }
+  }
+  __syncthreads();
+}
+
+// Single sequence: the x-stationary path for Q4/Q6 (when the rows are narrow
+// enough for its registers), else warp-row batches; one row per batch for the
+// batched (M > 1) form.
 template <int QT>
 __device__ __forceinline__ void phase_gemv_q(const Ctx *c, const GemvArgs *a, int M, float *smem) {
   constexpr int R1 = 2;
-  if (M <= 1)
+  if (M <= 1) {
+    if constexpr (QT != QT_Q8) {
+      if (xs_fits<QT>(a->A.pitch)) {
+        phase_gemv_xs<QT>(c, a, smem);
+        return;
+      }
+    }
     phase_gemv_t<QT, 1, R1>(c, a, M, smem);
-  else
+  } else {
     phase_gemv_t<QT, kMaxBatch, 1>(c, a, M, smem);
+  }
 }
 
 __device__ __forceinline__ void phase_gemv(const Ctx *c, const GemvArgs *a, int M, float *smem) {
@@ -1017,7 +1293,6 @@ __device__ __noinline__ void phase_attn(const Ctx *cp, int layer, int append_onl
   float *sc = vs + kAttnChunk * D;                // [kMaxGroup][kAttnChunk]
   float *wt = sc + kMaxGroup * kAttnChunk;        // [kMaxGroup][kAttnChunk]
   float *scl = wt + kMaxGroup * kAttnChunk;       // [kMaxGroup][max_chunks] merge scales
-  __shared__ SMStats st[kMaxGroup];
   __shared__ float mloc[kMaxGroup], lloc[kMaxGroup], dinv[kMaxGroup];
   __shared__ int is_last;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;

@@ -316,6 +316,12 @@ struct ocrvl_model {
   bool persistent = true;
   unsigned bar_base = 0;  // value of the barrier counter before the next launch
   int sms = 0;
+  // device-fed decode loop: id history and pinned staging for block-table
+  // updates, grown on demand and kept (no allocation in the steady state)
+  int *hist_d = nullptr;
+  size_t hist_cap = 0;
+  int *pin_pages = nullptr;
+  size_t pin_cap = 0;
 
   template <typename T>
   T *dalloc(size_t n) {
@@ -725,6 +731,8 @@ void ocrvl_free(ocrvl_model *m) {
   if (m->sp_h) cudaFreeHost(m->sp_h);
   if (m->out_h) cudaFreeHost(m->out_h);
   if (m->bt_stage) cudaFreeHost(m->bt_stage);
+  if (m->hist_d) cudaFree(m->hist_d);
+  if (m->pin_pages) cudaFreeHost(m->pin_pages);
   if (m->stream) cudaStreamDestroy(m->stream);
   delete m;
 }
@@ -892,24 +900,54 @@ int ocrvl_decode_greedy_device(ocrvl_model *m, ocrvl_seq *const *seqs, int n, co
     max_n = std::max(max_n, s->len + 1);
   }
   sp.max_n = max_n;
+  // buffers sized for this call (grown once, then reused): the id history and
+  // pinned staging for the new block-table entries
+  size_t new_pages = 0;
+  for (int i = 0; i < n; i++) {
+    ocrvl_seq *s = seqs[i];
+    int need_pages = (s->len + steps + kPageTokens - 1) / kPageTokens;
+    new_pages += (size_t)std::max(0, need_pages - (int)s->pages.size());
+  }
+  if (new_pages > m->free_pages.size()) return fail(OCRVL_E_NOMEM, "KV page pool exhausted");
+  if ((size_t)steps * n > m->hist_cap) {
+    CK(cudaStreamSynchronize(m->stream));
+    if (m->hist_d) cudaFree(m->hist_d);
+    m->hist_d = nullptr;
+    m->hist_cap = 0;
+    size_t cap = std::max<size_t>((size_t)steps * n, 4096);
+    if (cudaMalloc(&m->hist_d, cap * 4) != cudaSuccess) return fail(OCRVL_E_NOMEM, "id history allocation failed");
+    m->hist_cap = cap;
+  }
+  if (new_pages > m->pin_cap) {
+    CK(cudaStreamSynchronize(m->stream));
+    if (m->pin_pages) cudaFreeHost(m->pin_pages);
+    m->pin_pages = nullptr;
+    m->pin_cap = 0;
+    size_t cap = std::max<size_t>(new_pages, 1024);
+    CK(cudaHostAlloc((void **)&m->pin_pages, cap * 4, cudaHostAllocDefault));
+    m->pin_cap = cap;
+  } else if (new_pages) {
+    CK(cudaStreamSynchronize(m->stream));  // the staging buffer may still feed an earlier copy
+  }
   // every page the loop will touch is allocated up front
+  size_t off = 0;
   for (int i = 0; i < n; i++) {
     ocrvl_seq *s = seqs[i];
     int need_pages = (s->len + steps + kPageTokens - 1) / kPageTokens;
     int first_new = (int)s->pages.size();
-    if (need_pages - first_new > (int)m->free_pages.size()) return fail(OCRVL_E_NOMEM, "KV page pool exhausted");
-    std::vector<int> ids;
     while ((int)s->pages.size() < need_pages) {
       int pg = m->free_pages.back();
       m->free_pages.pop_back();
       s->pages.push_back(pg);
+      m->pin_pages[off + s->pages.size() - 1 - first_new] = pg;
     }
-    if (need_pages > first_new)
-      CK(cudaMemcpy(s->bt_d + first_new, s->pages.data() + first_new, (size_t)(need_pages - first_new) * 4,
-                    cudaMemcpyHostToDevice));
+    if (need_pages > first_new) {
+      CK(cudaMemcpyAsync(s->bt_d + first_new, m->pin_pages + off, (size_t)(need_pages - first_new) * 4,
+                         cudaMemcpyHostToDevice, m->stream));
+      off += (size_t)(need_pages - first_new);
+    }
   }
-  int *hist = nullptr;
-  CK(cudaMallocAsync((void **)&hist, (size_t)steps * n * 4, m->stream));
+  int *hist = m->hist_d;
   m->ctx.hist = hist;
   CK(cudaMemsetAsync(m->ctx.hist_pos, 0, 4, m->stream));
   CK(cudaMemcpyAsync(m->sp_d, &sp, sizeof(StepParams), cudaMemcpyHostToDevice, m->stream));
@@ -921,7 +959,6 @@ int ocrvl_decode_greedy_device(ocrvl_model *m, ocrvl_seq *const *seqs, int n, co
     cudaError_t e2 = cudaMemcpyAsync(m->out_h, m->ctx.tok_out, (kMaxBatch + 1) * 4, cudaMemcpyDeviceToHost, m->stream);
     if (e1 != cudaSuccess || e2 != cudaSuccess) rc = fail(OCRVL_E_CUDA, "copy of decoded ids failed");
   }
-  cudaFreeAsync(hist, m->stream);
   CK(cudaStreamSynchronize(m->stream));
   if (rc) return rc;
   if (m->out_h[kMaxBatch]) {
