@@ -71,8 +71,13 @@ struct Ctx {
   unsigned long long *argkey;        // [B]
   int *tok_out;                      // [B] ids, then the error word
   int max_ctx, max_chunks;
-  StepParams *sp;
-  unsigned *attn_count;              // [B][KVH] chunk arrivals
+  // step parameters: `sp` is read (inside the step kernels it points to a
+  // shared-memory copy made at launch), `sp_w` is the global copy that the
+  // device-fed loop advances for the next launch
+  const StepParams *sp;
+  StepParams *sp_w;
+  int pro_cols;                      // widest GEMV input: fixes the stage-ring offset (0: per phase)
+  unsigned *attn_count;              // [B][KVH][2] chunk arrivals, finished mergers
   unsigned *lm_count;                // lm_head block arrivals
   int *hist, *hist_pos;              // device-side greedy loop: ids [steps][M], write index
   // persistent-kernel barrier: monotonic arrival counter and error word
@@ -651,7 +656,8 @@ __host__ __device__ __forceinline__ size_t gemv_smem_total(int qt, int nvec, int
 // counter reset, and (device-side greedy loop) the next step's parameters:
 // tok = argmax, len + 1, position (len, len, len).
 __device__ void argmax_finish(const Ctx &c, int M, int feed) {
-  StepParams &sp = *c.sp;
+  const StepParams &sp = *c.sp;
+  StepParams &spw = *c.sp_w;
   if (threadIdx.x < M) {
     const int m = threadIdx.x;
     unsigned long long k = __ldcg(c.argkey + m);
@@ -662,16 +668,16 @@ __device__ void argmax_finish(const Ctx &c, int M, int feed) {
       int step = *c.hist_pos;
       c.hist[(size_t)step * M + m] = id;
       int len = sp.len[m] + 1;
-      sp.tok[m] = id;
-      sp.len[m] = len;
-      sp.pos[m][0] = sp.pos[m][1] = sp.pos[m][2] = len;
+      spw.tok[m] = id;
+      spw.len[m] = len;
+      spw.pos[m][0] = spw.pos[m][1] = spw.pos[m][2] = len;
     }
   }
   __syncthreads();
   if (threadIdx.x == 0) {
     if (feed) {
       *c.hist_pos += 1;
-      sp.max_n += 1;
+      spw.max_n = sp.max_n + 1;
     }
     *c.lm_count = 0u;
   }
@@ -688,7 +694,7 @@ __device__ __noinline__ void phase_gemv_t(const Ctx *cp, const GemvArgs *ap, int
   const bool two = a.epi == EPI_SWIGLU;
   int lo, hi;
   gemv_slab(a.row_begin, a.row_end, blockIdx.x, gridDim.x, lo, hi);
-  uint8_t *stage = (uint8_t *)smem + gemv_prologue_bytes(qt, M_ == 1 ? 1 : kMaxBatch, a.A.cols);
+  uint8_t *stage = (uint8_t *)smem + gemv_prologue_bytes(qt, M_ == 1 ? 1 : kMaxBatch, c.pro_cols ? c.pro_cols : a.A.cols);
   const int srows = kStageBytes / (P * (two ? 2 : 1));  // rows per stage
   const int nst = (hi - lo + srows - 1) / srows;
   auto issue = [&](int st) {
@@ -843,14 +849,14 @@ __device__ __noinline__ void phase_gemv_t(const Ctx *cp, const GemvArgs *ap, int
     }
     if (a.argmax_finish) {
       __shared__ int is_last;
-      __threadfence();
       __syncthreads();
-      if (threadIdx.x == 0) is_last = atomicAdd(c.lm_count, 1u) == gridDim.x - 1;
-      __syncthreads();
-      if (is_last) {
+      if (threadIdx.x == 0) {
         __threadfence();
-        argmax_finish(c, M, a.feed);
+        is_last = atomicAdd(c.lm_count, 1u) == gridDim.x - 1;
+        if (is_last) __threadfence();
       }
+      __syncthreads();
+      if (is_last) argmax_finish(c, M, a.feed);
     }
   }
   __syncthreads();
@@ -947,7 +953,7 @@ __device__ __noinline__ void phase_gemv_xs(const Ctx *cp, const GemvArgs *ap, fl
   const bool two = a.epi == EPI_SWIGLU;
   int lo, hi;
   gemv_slab(a.row_begin, a.row_end, blockIdx.x, gridDim.x, lo, hi);
-  uint8_t *stage = (uint8_t *)smem + gemv_prologue_bytes(QT, 1, n);
+  uint8_t *stage = (uint8_t *)smem + gemv_prologue_bytes(QT, 1, c.pro_cols ? c.pro_cols : n);
   const int srows = kStageBytes / (P * (two ? 2 : 1));
   const int nst = (hi - lo + srows - 1) / srows;
   auto issue = [&](int st) {
@@ -1090,14 +1096,14 @@ __device__ __noinline__ void phase_gemv_xs(const Ctx *cp, const GemvArgs *ap, fl
     if (lane == 0 && best) atomicMax(a.argkey, best);
     if (a.argmax_finish) {
       __shared__ int is_last;
-      __threadfence();
       __syncthreads();
-      if (threadIdx.x == 0) is_last = atomicAdd(c.lm_count, 1u) == gridDim.x - 1;
-      __syncthreads();
-      if (is_last) {
+      if (threadIdx.x == 0) {
         __threadfence();
-        argmax_finish(c, 1, a.feed);
+        is_last = atomicAdd(c.lm_count, 1u) == gridDim.x - 1;
+        if (is_last) __threadfence();
       }
+      __syncthreads();
+      if (is_last) argmax_finish(c, 1, a.feed);
     }
   }
   __syncthreads();
@@ -1169,80 +1175,51 @@ __device__ __forceinline__ void rope_cs4(const Ctx &c, const int *pos, int i4, f
 }
 
 // ---------------------------------------------------------------------------
-// Softmax of one head over <= 32 scores held in shared memory, restating
-// SoftmaxInPlace (ops.go:1199-1363) and the cacheAttentionLen2..6 paths
-// (model.go:4797-5081).  `mode` says how a score becomes its weight:
-//   0: fast_exp(s-m)*inv, 1: exp_fma(s-m)*inv for t < nv, raw s*inv above,
-//   2: n == 2 special form, 3: n == 1 (weight 1).
+// Softmax of one head over n <= 32 scores, one score per lane (lane t holds
+// token t), restating SoftmaxInPlace (ops.go:1199-1363) and the
+// cacheAttentionLen2..6 paths (model.go:4797-5081).  Returns lane t's weight.
+//   n == 1: weight 1; n == 2: the two-score form; 3..8: FastExpF32 with the
+//   fixed sum trees; 9..15: FastExpF32 summed in order; >= 16: exp_fma over
+//   the 16-aligned prefix nv summed in 16 lane chains + tree16, tokens at or
+//   above nv keep their raw score (dot_amd64.s:6116-6210); all times 1/sum.
 // ---------------------------------------------------------------------------
-struct SMStats {
-  float m, inv;
-  int mode, nv;
-};
-
-__device__ __forceinline__ float sm_weight(const SMStats &st, const float *s, int t) {
-  if (st.mode == 3) return 1.0f;
-  if (st.mode == 2) {
-    float a = s[0], b = s[1];
-    if (a >= b) {
-      float e = fast_exp(__fsub_rn(b, a));
-      float inv = __fdiv_rn(1.0f, __fadd_rn(1.0f, e));
-      return t == 0 ? inv : __fmul_rn(e, inv);
-    }
-    float e = fast_exp(__fsub_rn(a, b));
-    float inv = __fdiv_rn(1.0f, __fadd_rn(1.0f, e));
-    return t == 0 ? __fmul_rn(e, inv) : inv;
-  }
-  const float v = s[t];
-  if (st.mode == 0) return __fmul_rn(fast_exp(__fsub_rn(v, st.m)), st.inv);
-  if (t < st.nv) return __fmul_rn(exp_fma(__fsub_rn(v, st.m)), st.inv);
-  return __fmul_rn(v, st.inv);
-}
-
-// One warp, n <= 32 scores.  For n >= 16 the 16 lane chains of
-// expF32VecFMA are kept exactly: lane l adds the exponential of token l, then
-// of token l+16 (when below the 16-aligned prefix nv).
-__device__ SMStats warp_softmax_small(const float *s, int n) {
+__device__ float warp_softmax_weight(float v, int n) {
   const int lane = threadIdx.x & 31;
-  float mx = lane < n ? s[lane] : -INFINITY;
+  if (n == 1) return 1.0f;
+  if (n == 2) {
+    const float a = __shfl_sync(0xffffffffu, v, 0), b = __shfl_sync(0xffffffffu, v, 1);
+    if (a >= b) {
+      const float e = fast_exp(__fsub_rn(b, a));
+      const float inv = __fdiv_rn(1.0f, __fadd_rn(1.0f, e));
+      return lane == 0 ? inv : __fmul_rn(e, inv);
+    }
+    const float e = fast_exp(__fsub_rn(a, b));
+    const float inv = __fdiv_rn(1.0f, __fadd_rn(1.0f, e));
+    return lane == 0 ? __fmul_rn(e, inv) : inv;
+  }
+  float mx = lane < n ? v : -INFINITY;
   for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-  SMStats st;
-  st.m = mx;
-  st.nv = 0;
   if (n >= 16) {
     const int nv = n & ~15;
-    float e = lane < nv ? exp_fma(__fsub_rn(s[lane], mx)) : 0.0f;
-    float hi = __shfl_down_sync(0xffffffffu, e, 16);
+    const float e = lane < nv ? exp_fma(__fsub_rn(v, mx)) : 0.0f;
+    const float hi = __shfl_down_sync(0xffffffffu, e, 16);
     float acc = __fadd_rn(0.0f, e);
     if (16 < nv) acc = __fadd_rn(acc, hi);
     float lanes[16];
 #pragma unroll
     for (int l = 0; l < 16; l++) lanes[l] = __shfl_sync(0xffffffffu, acc, l);
-    st.inv = __fdiv_rn(1.0f, tree16(lanes));
-    st.mode = 1;
-    st.nv = nv;
-    return st;
+    const float inv = __fdiv_rn(1.0f, tree16(lanes));
+    return lane < nv ? __fmul_rn(e, inv) : __fmul_rn(v, inv);
   }
-  if (n == 1) {
-    st.mode = 3;
-    st.inv = 1.0f;
-    return st;
-  }
-  if (n == 2) {
-    st.mode = 2;
-    st.inv = 1.0f;
-    return st;
-  }
-  // 3 <= n <= 15: one exponential per lane, then the reference's sum order
-  const float e = lane < n ? fast_exp(__fsub_rn(s[lane], mx)) : 0.0f;
+  const float e = lane < n ? fast_exp(__fsub_rn(v, mx)) : 0.0f;
   float sum;
   if (n <= 8) {
     float e8[8];
 #pragma unroll
     for (int t = 0; t < 8; t++) e8[t] = __shfl_sync(0xffffffffu, e, t);
-    float p01 = __fadd_rn(e8[0], e8[1]), p23 = __fadd_rn(e8[2], e8[3]);
-    float p45 = __fadd_rn(e8[4], e8[5]), p67 = __fadd_rn(e8[6], e8[7]);
-    float q4 = __fadd_rn(p01, p23);
+    const float p01 = __fadd_rn(e8[0], e8[1]), p23 = __fadd_rn(e8[2], e8[3]);
+    const float p45 = __fadd_rn(e8[4], e8[5]), p67 = __fadd_rn(e8[6], e8[7]);
+    const float q4 = __fadd_rn(p01, p23);
     switch (n) {
       case 3: sum = __fadd_rn(p01, e8[2]); break;
       case 4: sum = q4; break;
@@ -1256,289 +1233,452 @@ __device__ SMStats warp_softmax_small(const float *s, int n) {
 #pragma unroll 1
     for (int t = 0; t < n; t++) sum = __fadd_rn(sum, __shfl_sync(0xffffffffu, e, t));
   }
-  st.inv = __fdiv_rn(1.0f, sum);
-  st.mode = 0;
-  return st;
+  return __fmul_rn(e, __fdiv_rn(1.0f, sum));
 }
 
 // ---------------------------------------------------------------------------
 // Attention phase: RoPE, KV append, scores, softmax and value sums.
-// Items: (sequence, kv head, chunk of kAttnChunk tokens); each item serves the
-// G = QH/KVH query heads of its kv head (GQA).  The item whose chunk holds the
-// new token appends its rotated k and its v to the paged cache
-// (kvCache.append, model.go:5593-5612).  Scores restate cacheAttentionScores
-// (model.go:4623-4795): (q.k)*1/sqrt(D), the dot in the 8x16-slot order of
-// the reference's 128-wide dot kernels.
-//   * n <= kAttnChunk: one item per (sequence, kv head) holds every score and
-//     applies the reference softmax exactly (including its small-n forms) and
-//     the token-order value sum; the head output is written directly.
-//   * longer caches: each chunk keeps its own max m_c, the sum l_c of
-//     exp(s - m_c) and o_c = sum exp(s - m_c) v over the 16-aligned prefix
-//     nv = 16*floor(n/16); tokens at or above nv carry their raw score as
-//     weight (the reference's expF32VecFMA leaves them unexponentiated,
-//     dot_amd64.s:6131-6168).  The last chunk item to finish merges:
-//     head = (sum_c exp(m_c - M) o_c + T) / sum_c exp(m_c - M) l_c, with
-//     M the max over all scores and T the raw-weighted tail sum.
+//
+// Items: (sequence m, kv head g, chunk of tokens).  Caches of n <= 32
+// positions form one 32-token item per (m, g) that applies the reference
+// softmax exactly (incl. its small-n forms) and sums values in token order.
+// Longer caches are split into 16-token chunks (one KV page each): chunk c
+// keeps its max m_c, l_c = sum of exp_fma(s - m_c) and o_c = sum exp(...) v;
+// with nv = 16*floor(n/16) the last chunk holds the tokens at or above nv
+// (if n % 16 != 0), which the reference weights by their raw score
+// (expF32VecFMA leaves them unexponentiated, dot_amd64.s:6131-6168): that
+// chunk reports its max and the raw-weighted sum T instead.  Merge per query
+// head: head = (T + sum_c exp(m_c - M) o_c) / sum_c exp(m_c - M) l_c, M the
+// max over all scores.
+//
+// Each item serves the G = QH/KVH query heads of its kv head (GQA): warp h
+// computes head h's scores, one 128-wide dot per token split over the warp in
+// the reference's 16-slot order (lane = slot + 16*half, 4 products per lane,
+// xor-16 pair, then the tree16 pairs by xor 8/4/2/1), so lane t ends holding
+// token t's score.  K/V pages arrive by TMA bulk copy into shared memory,
+// issued before the grid barrier that precedes the phase when the block's
+// item is known (attn_prefetch); the item holding the new token takes its k
+// and v from the QKV output, rotates k and appends both to the page
+// (kvCache.append, model.go:5593-5612).
+//
+// Merge: each item raises its (m, g) arrival counter.  When every item has a
+// block of its own, the last G arrivals each wait for the counter to be
+// complete (bounded) and merge one query head in parallel; otherwise the last
+// arrival merges all G heads.
 // ---------------------------------------------------------------------------
-__device__ __noinline__ void phase_attn(const Ctx *cp, int layer, int append_only, float *smem) {
+constexpr int kChunkTok = 16;  // tokens per chunk of a long cache (one KV page)
+
+__device__ __forceinline__ unsigned ld_acquire_u32(const unsigned *p) {
+  unsigned v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+struct AttnItem {
+  int m, g, ch, t0, cnt, n, nch;
+  bool exact;
+};
+
+// Item `it` of the step; false when it is past the last item.
+__device__ __forceinline__ bool attn_item(const Ctx &c, const StepParams &sp, int it, AttnItem &I) {
+  for (int m = 0; m < sp.M; m++) {
+    const int n = sp.len[m] + 1;
+    const bool exact = n <= kAttnChunk;
+    const int ct = exact ? kAttnChunk : kChunkTok;
+    const int nch = (n + ct - 1) / ct;
+    const int cnt_items = c.KVH * nch;
+    if (it < cnt_items) {
+      I.m = m;
+      I.g = it / nch;
+      I.ch = it % nch;
+      I.t0 = I.ch * ct;
+      I.cnt = min(n, I.t0 + ct) - I.t0;
+      I.n = n;
+      I.nch = nch;
+      I.exact = exact;
+      return true;
+    }
+    it -= cnt_items;
+  }
+  return false;
+}
+
+__device__ __forceinline__ int attn_items_total(const Ctx &c, const StepParams &sp) {
+  int total = 0;
+  for (int m = 0; m < sp.M; m++) {
+    const int n = sp.len[m] + 1;
+    const int ct = n <= kAttnChunk ? kAttnChunk : kChunkTok;
+    total += c.KVH * ((n + ct - 1) / ct);
+  }
+  return total;
+}
+
+// Per-block state of the K/V page loads, kept across phases of one launch.
+__shared__ __align__(8) uint64_t s_kv_bar;
+__shared__ uint32_t s_kv_parity;
+__shared__ int s_kv_item;  // item whose pages are in flight / loaded, -1 none
+// cos / sin of every RoPE frequency at each sequence's position of this step
+__shared__ float s_rope_cs[kMaxBatch][kHeadDim / 2], s_rope_sn[kMaxBatch][kHeadDim / 2];
+__shared__ int s_rope_ready;
+
+// Shared-memory layout of the attention phase (floats):
+//   K [32][D] | V [32][D] | q [G][D] | wt [G][32] | red [8][D] | scl [max_chunks]
+__host__ __device__ __forceinline__ size_t attn_smem_floats(int max_chunks) {
+  return (size_t)2 * kAttnChunk * kHeadDim + (size_t)kMaxGroup * kHeadDim + (size_t)kMaxGroup * kAttnChunk +
+         (size_t)8 * kHeadDim + (size_t)max_chunks;
+}
+
+// Called by every thread at the start of a launch that runs attention phases.
+__device__ __forceinline__ void attn_block_init() {
+  if (threadIdx.x == 0) {
+    mbar_init(&s_kv_bar, 1);
+    mbar_fence_init();
+    s_kv_parity = 0;
+    s_kv_item = -1;
+    s_rope_ready = 0;
+  }
+  __syncthreads();
+}
+
+// Fills s_rope_cs / s_rope_sn for the step's sequences (all threads call;
+// positions are fixed for the whole launch).
+__device__ void attn_rope_tables(const Ctx &c) {
+  const StepParams &sp = *c.sp;
+  const int half = c.D / 2;
+  for (int p = threadIdx.x; p < sp.M * half; p += kThreads) {
+    const int m = p / half, i = p % half;
+    const int q = sp.pos[m][c.sec_axis[i]];
+    s_rope_cs[m][i] = __ldg(c.rope_cos + (size_t)q * half + i);
+    s_rope_sn[m][i] = __ldg(c.rope_sin + (size_t)q * half + i);
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) s_rope_ready = 1;
+}
+
+// Thread 0: bulk copies of item I's K and V page(s) into the K/V buffers.
+__device__ __forceinline__ void attn_issue_kv(const Ctx &c, int layer, const AttnItem &I, float *smem) {
+  const int *bt = c.sp->bt[I.m];
+  const int p0 = I.t0 / kPageTokens;
+  const int np = (I.cnt + kPageTokens - 1) / kPageTokens;
+  const uint32_t pbytes = (uint32_t)kPageTokens * c.D * 4;
+  // the buffers were last touched by ordinary loads/stores of this block
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  mbar_expect_tx(&s_kv_bar, 2u * np * pbytes);
+  for (int p = 0; p < np; p++) {
+    const float *kp = kv_ptr(c, bt, layer, 0, I.g, (p0 + p) * kPageTokens);
+    const float *vp = kv_ptr(c, bt, layer, 1, I.g, (p0 + p) * kPageTokens);
+    bulk_g2s(smem + (size_t)p * kPageTokens * c.D, kp, pbytes, &s_kv_bar);
+    bulk_g2s(smem + (size_t)kAttnChunk * c.D + (size_t)p * kPageTokens * c.D, vp, pbytes, &s_kv_bar);
+  }
+}
+
+// Issues this block's first attention item's K/V loads ahead of the phase
+// (all threads call; the block's shared memory must be free of other use).
+__device__ void attn_prefetch(const Ctx &c, int layer, float *smem) {
+  AttnItem I;
+  if (threadIdx.x == 0 && s_kv_item < 0 && attn_item(c, *c.sp, blockIdx.x, I)) {
+    attn_issue_kv(c, layer, I, smem);
+    s_kv_item = blockIdx.x;
+  }
+}
+
+// Waits for outstanding K/V loads (before the block leaves the kernel).
+__device__ void attn_drain(const Ctx &c) {
+  if (threadIdx.x == 0 && s_kv_item >= 0) {
+    mbar_wait(&s_kv_bar, s_kv_parity, c.err);
+    s_kv_parity ^= 1u;
+    s_kv_item = -1;
+  }
+  __syncthreads();
+}
+
+__device__ __noinline__ void phase_attn(const Ctx *cp, int layer, int append_only, int coop, float *smem) {
   const Ctx &c = *cp;
   const StepParams &sp = *c.sp;
-  const int G = c.QH / c.KVH, D = c.D, H4 = D / 8, D4 = D / 4;
+  const int G = c.QH / c.KVH, D = c.D, D4 = D / 4, H4 = D / 8;
   const int qkvld = (c.QH + 2 * c.KVH) * D;
-  const int nchunk = (sp.max_n + kAttnChunk - 1) / kAttnChunk;
-  const int items = sp.M * c.KVH * nchunk;
-  float *qs = smem;                               // [kMaxGroup][D]
-  float *ks = qs + kMaxGroup * D;                 // [kAttnChunk][D+1]
-  float *vs = ks + kAttnChunk * (D + 1);          // [kAttnChunk][D]
-  float *sc = vs + kAttnChunk * D;                // [kMaxGroup][kAttnChunk]
-  float *wt = sc + kMaxGroup * kAttnChunk;        // [kMaxGroup][kAttnChunk]
-  float *scl = wt + kMaxGroup * kAttnChunk;       // [kMaxGroup][max_chunks] merge scales
-  __shared__ float mloc[kMaxGroup], lloc[kMaxGroup], dinv[kMaxGroup];
-  __shared__ int is_last;
+  float *Ks = smem;                                // [32][D]
+  float *Vs = Ks + kAttnChunk * D;                 // [32][D]
+  float *qs = Vs + kAttnChunk * D;                 // [G][D]
+  float *wt = qs + kMaxGroup * D;                  // [G][32]
+  float *red = wt + kMaxGroup * kAttnChunk;        // [8][D]
+  float *scl = red + 8 * D;                        // [max_chunks]
+  __shared__ float rcs_l[kHeadDim / 2], rsn_l[kHeadDim / 2];
+  __shared__ int merge_head;
+  __shared__ float mloc[kMaxGroup], lloc[kMaxGroup], dinv_s;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int items = attn_items_total(c, sp);
+  const bool multi = coop && items <= (int)gridDim.x;
+  int tab_m = -1;  // sequence whose RoPE values rcs/rsn hold
   for (int it = blockIdx.x; it < items; it += gridDim.x) {
-    const int m = it / (c.KVH * nchunk), rem = it % (c.KVH * nchunk);
-    const int g = rem / nchunk, ch = rem % nchunk;
-    const int len = sp.len[m], n = len + 1;
-    const int t0 = ch * kAttnChunk;
-    if (t0 >= n) continue;
-    const int t1 = min(n, t0 + kAttnChunk), cnt = t1 - t0;
-    if (append_only && len >= t1) continue;
-    const int nch = (n + kAttnChunk - 1) / kAttnChunk;
-    const int *pos = sp.pos[m];
-    const int *bt = sp.bt[m];
+    AttnItem I;
+    attn_item(c, sp, it, I);
+    const int len = I.n - 1;
+    const bool has_new = I.t0 <= len && len < I.t0 + I.cnt;
+    if (append_only && !has_new) continue;
+    const int *pos = sp.pos[I.m];
     const bool has_rope = pos[0] != 0 || pos[1] != 0 || pos[2] != 0;
-    const float *qkv = c.qkv + (size_t)m * qkvld;
-    // ---- loads: q pairs, k pairs, v rows; each thread issues a batch of
-    // loads before its first shared-memory store
-    {
-      const int nq = append_only ? 0 : G * H4, nk = cnt * H4, nv4 = cnt * D4;
-      const int ntask = nq + nk + nv4;
-      constexpr int U = 4;
-#pragma unroll 1
-      for (int base = threadIdx.x; base < ntask; base += kThreads * U) {
-        float4 ra[U], rb[U];
-#pragma unroll
-        for (int u = 0; u < U; u++) {
-          int p = base + u * kThreads;
-          if (p >= ntask) continue;
-          if (p < nq) {
-            const float4 *qh = (const float4 *)(qkv + (size_t)(g * G + p / H4) * D);
-            ra[u] = __ldcg(qh + p % H4);
-            rb[u] = __ldcg(qh + p % H4 + H4);
-          } else if (p < nq + nk) {
-            int q = p - nq, t = t0 + q / H4, i4 = q % H4;
-            const float4 *src = (t == len) ? (const float4 *)(qkv + (size_t)(c.QH + g) * D)
-                                           : (const float4 *)kv_ptr(c, bt, layer, 0, g, t);
-            ra[u] = __ldcg(src + i4);
-            rb[u] = __ldcg(src + i4 + H4);
-          } else {
-            int q = p - nq - nk, t = t0 + q / D4, i4 = q % D4;
-            const float4 *src = (t == len) ? (const float4 *)(qkv + (size_t)(c.QH + c.KVH + g) * D)
-                                           : (const float4 *)kv_ptr(c, bt, layer, 1, g, t);
-            ra[u] = __ldcg(src + i4);
-          }
-        }
-#pragma unroll
-        for (int u = 0; u < U; u++) {
-          int p = base + u * kThreads;
-          if (p >= ntask) continue;
-          if (p < nq) {
-            int hh = p / H4, i4 = p % H4;
-            if (has_rope) {
-              float cs[4], sn[4];
-              rope_cs4(c, pos, i4, cs, sn);
-              rope4(ra[u], rb[u], cs, sn);
-            }
-            ((float4 *)(qs + hh * D))[i4] = ra[u];
-            ((float4 *)(qs + hh * D))[i4 + H4] = rb[u];
-          } else if (p < nq + nk) {
-            int q = p - nq, tt = q / H4, i4 = q % H4, t = t0 + tt;
-            if (t == len) {
-              if (has_rope) {
-                float cs[4], sn[4];
-                rope_cs4(c, pos, i4, cs, sn);
-                rope4(ra[u], rb[u], cs, sn);
-              }
-              float4 *kd = (float4 *)kv_ptr(c, bt, layer, 0, g, t);
-              kd[i4] = ra[u];
-              kd[i4 + H4] = rb[u];
-            }
-            float *kr = ks + tt * (D + 1) + i4 * 4;
-            kr[0] = ra[u].x; kr[1] = ra[u].y; kr[2] = ra[u].z; kr[3] = ra[u].w;
-            kr += D / 2;
-            kr[0] = rb[u].x; kr[1] = rb[u].y; kr[2] = rb[u].z; kr[3] = rb[u].w;
-          } else {
-            int q = p - nq - nk, tt = q / D4, i4 = q % D4, t = t0 + tt;
-            if (t == len) ((float4 *)kv_ptr(c, bt, layer, 1, g, t))[i4] = ra[u];
-            ((float4 *)(vs + tt * D))[i4] = ra[u];
-          }
-        }
+    const float *qkv = c.qkv + (size_t)I.m * qkvld;
+    // ---- K/V pages (unless prefetched for this item), RoPE table of the position
+    if (threadIdx.x == 0 && s_kv_item != it) {
+      attn_issue_kv(c, layer, I, smem);
+      s_kv_item = it;
+    }
+    const bool rope_pre = s_rope_ready != 0;
+    if (!rope_pre && threadIdx.x < D / 2 && I.m != tab_m) {
+      const int i = threadIdx.x;
+      const int p = pos[c.sec_axis[i]];
+      rcs_l[i] = __ldg(c.rope_cos + (size_t)p * (D / 2) + i);
+      rsn_l[i] = __ldg(c.rope_sin + (size_t)p * (D / 2) + i);
+    }
+    __syncthreads();
+    tab_m = I.m;
+    const float *rcs = rope_pre ? s_rope_cs[I.m] : rcs_l;
+    const float *rsn = rope_pre ? s_rope_sn[I.m] : rsn_l;
+    // ---- q (rotated) into shared memory; the new token's k (rotated) and v
+    // appended to the page and placed into the K/V buffers (after the copy)
+    if (!append_only) {
+      for (int p = threadIdx.x; p < G * H4; p += kThreads) {
+        const int hh = p / H4, i4 = p % H4;
+        const float4 *qh = (const float4 *)(qkv + (size_t)(I.g * G + hh) * D);
+        float4 ra = __ldcg(qh + i4), rb = __ldcg(qh + i4 + H4);
+        if (has_rope) rope4(ra, rb, rcs + 4 * i4, rsn + 4 * i4);
+        ((float4 *)(qs + hh * D))[i4] = ra;
+        ((float4 *)(qs + hh * D))[i4 + H4] = rb;
       }
+    }
+    float4 nk_a, nk_b, nv4;
+    const int tt_new = len - I.t0;
+    if (has_new && threadIdx.x < D4) {
+      if (threadIdx.x < H4) {
+        const float4 *kn = (const float4 *)(qkv + (size_t)(c.QH + I.g) * D);
+        nk_a = __ldcg(kn + threadIdx.x);
+        nk_b = __ldcg(kn + threadIdx.x + H4);
+        if (has_rope) rope4(nk_a, nk_b, rcs + 4 * threadIdx.x, rsn + 4 * threadIdx.x);
+        float4 *kd = (float4 *)kv_ptr(c, sp.bt[I.m], layer, 0, I.g, len);
+        kd[threadIdx.x] = nk_a;
+        kd[threadIdx.x + H4] = nk_b;
+      }
+      nv4 = __ldcg((const float4 *)(qkv + (size_t)(c.QH + c.KVH + I.g) * D) + threadIdx.x);
+      ((float4 *)kv_ptr(c, sp.bt[I.m], layer, 1, I.g, len))[threadIdx.x] = nv4;
+    }
+    if (threadIdx.x == 0) {
+      mbar_wait(&s_kv_bar, s_kv_parity, c.err);
+      s_kv_parity ^= 1u;
+      s_kv_item = -1;
+    }
+    __syncthreads();
+    if (has_new && threadIdx.x < D4) {
+      if (threadIdx.x < H4) {
+        ((float4 *)(Ks + (size_t)tt_new * D))[threadIdx.x] = nk_a;
+        ((float4 *)(Ks + (size_t)tt_new * D))[threadIdx.x + H4] = nk_b;
+      }
+      ((float4 *)(Vs + (size_t)tt_new * D))[threadIdx.x] = nv4;
     }
     if (append_only) {
       __syncthreads();
       continue;
     }
     __syncthreads();
-    // ---- scores: one (head, token) per thread
-#pragma unroll 1
-    for (int p = threadIdx.x; p < G * kAttnChunk; p += kThreads) {
-      int hh = p / kAttnChunk, tt = p % kAttnChunk;
-      if (tt >= cnt) continue;
-      const float *q = qs + hh * D;
-      const float *k = ks + tt * (D + 1);
-      float r[16];
+    // ---- scores (warp = head) and softmax / chunk statistics
+    const int slot = lane & 15, half = lane >> 4;
+    if (warp < G) {
+      const float *q = qs + warp * D;
+      float qv[4];
+#pragma unroll
+      for (int jj = 0; jj < 4; jj++) qv[jj] = q[16 * (4 * half + (jj ^ half)) + slot];
+      float mine = 0.0f;
 #pragma unroll 4
-      for (int l = 0; l < 16; l++) {
-        float p0 = __fmul_rn(q[l], k[l]), p1 = __fmul_rn(q[16 + l], k[16 + l]);
-        float p2 = __fmul_rn(q[32 + l], k[32 + l]), p3 = __fmul_rn(q[48 + l], k[48 + l]);
-        float p4 = __fmul_rn(q[64 + l], k[64 + l]), p5 = __fmul_rn(q[80 + l], k[80 + l]);
-        float p6 = __fmul_rn(q[96 + l], k[96 + l]), p7 = __fmul_rn(q[112 + l], k[112 + l]);
-        r[l] = __fadd_rn(__fadd_rn(__fadd_rn(p0, p1), __fadd_rn(p2, p3)),
-                         __fadd_rn(__fadd_rn(p4, p5), __fadd_rn(p6, p7)));
+      for (int tt = 0; tt < I.cnt; tt++) {
+        const float *k = Ks + (size_t)tt * D;
+        float pr[4];
+#pragma unroll
+        for (int jj = 0; jj < 4; jj++) pr[jj] = __fmul_rn(qv[jj], k[16 * (4 * half + (jj ^ half)) + slot]);
+        // products in j order: half 0 read j = 0,1,2,3; half 1 read j = 5,4,7,6
+        float s4 = half ? __fadd_rn(__fadd_rn(pr[1], pr[0]), __fadd_rn(pr[3], pr[2]))
+                        : __fadd_rn(__fadd_rn(pr[0], pr[1]), __fadd_rn(pr[2], pr[3]));
+        float r = __fadd_rn(s4, __shfl_xor_sync(0xffffffffu, s4, 16));  // slot sum (halves commute)
+        r = __fadd_rn(r, __shfl_xor_sync(0xffffffffu, r, 8));
+        r = __fadd_rn(r, __shfl_xor_sync(0xffffffffu, r, 4));
+        r = __fadd_rn(r, __shfl_xor_sync(0xffffffffu, r, 2));
+        r = __fadd_rn(r, __shfl_xor_sync(0xffffffffu, r, 1));
+        if (lane == tt) mine = __fmul_rn(r, c.attn_scale);
       }
-      sc[hh * kAttnChunk + tt] = __fmul_rn(tree16(r), c.attn_scale);
+      float w;
+      if (I.exact) {
+        w = warp_softmax_weight(mine, I.n);  // every lane takes part in the shuffles
+        if (lane >= I.cnt) w = 0.0f;
+      } else {
+        const int nv = I.n & ~15;
+        const bool tail = I.t0 >= nv;  // the whole chunk lies at or above nv
+        float mx = lane < I.cnt ? mine : -INFINITY;
+        for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+        float e = 0.0f;
+        if (lane < I.cnt) e = tail ? mine : exp_fma(__fsub_rn(mine, mx));
+        float l = tail ? 0.0f : e;
+        for (int o = 16; o > 0; o >>= 1) l = __fadd_rn(l, __shfl_xor_sync(0xffffffffu, l, o));
+        w = e;
+        if (lane == 0) {
+          mloc[warp] = mx;
+          lloc[warp] = l;
+        }
+      }
+      wt[warp * kAttnChunk + lane] = w;
     }
     __syncthreads();
-    const size_t hbase = (size_t)m * c.QH + g * G;  // first query head of the group
-    if (nch == 1) {
-      // ---- exact reference softmax and token-order value sum
-      if (warp < G) {
-        SMStats s = warp_softmax_small(sc + warp * kAttnChunk, n);
-        if (lane < n) wt[warp * kAttnChunk + lane] = sm_weight(s, sc + warp * kAttnChunk, lane);
+    // ---- value sums: thread = (head, 4 dims), token order
+    const size_t hbase = (size_t)I.m * c.QH + (size_t)I.g * G;
+    for (int p = threadIdx.x; p < G * D4; p += kThreads) {
+      const int hh = p / D4, d4 = p % D4;
+      const float *w = wt + hh * kAttnChunk;
+      float4 acc;
+      int t = 0;
+      if (I.exact) {
+        const float4 v0 = ((const float4 *)Vs)[d4];
+        acc = make_float4(__fmul_rn(w[0], v0.x), __fmul_rn(w[0], v0.y), __fmul_rn(w[0], v0.z), __fmul_rn(w[0], v0.w));
+        t = 1;
+      } else {
+        acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
       }
-      __syncthreads();
-#pragma unroll 1
-      for (int p = threadIdx.x; p < G * D; p += kThreads) {
-        int hh = p / D, d = p % D;
-        const float *w = wt + hh * kAttnChunk;
-        float acc = __fmul_rn(w[0], vs[d]);
 #pragma unroll 4
-        for (int tt = 1; tt < cnt; tt++) acc = __fmaf_rn(w[tt], vs[tt * D + d], acc);
-        c.head[(hbase + hh) * D + d] = acc;
+      for (; t < I.cnt; t++) {
+        const float4 v = ((const float4 *)(Vs + (size_t)t * D))[d4];
+        const float wv = w[t];
+        acc.x = __fmaf_rn(wv, v.x, acc.x);
+        acc.y = __fmaf_rn(wv, v.y, acc.y);
+        acc.z = __fmaf_rn(wv, v.z, acc.z);
+        acc.w = __fmaf_rn(wv, v.w, acc.w);
       }
+      if (I.exact) {
+        ((float4 *)(c.head + (hbase + hh) * D))[d4] = acc;
+      } else {
+        const bool tail = I.t0 >= (I.n & ~15);
+        if (tail) {
+          ((float4 *)(c.part_t + (hbase + hh) * D))[d4] = acc;
+        } else {
+          ((float4 *)(c.part_o + ((hbase + hh) * c.max_chunks + I.ch) * D))[d4] = acc;
+        }
+        if (d4 == 0) {
+          float *ml = c.part_ml + ((hbase + hh) * c.max_chunks + I.ch) * 2;
+          ml[0] = mloc[hh];
+          ml[1] = lloc[hh];
+        }
+      }
+    }
+    if (I.exact) {
       __syncthreads();
       continue;
     }
-    // ---- chunk of a longer cache: local max, exponentials, sums
-    const int nv = n & ~15;
-    if (warp < G) {
-      const float *s = sc + warp * kAttnChunk;
-      float v = lane < cnt ? s[lane] : -INFINITY;
-      float mx = v;
-      for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-      int t = t0 + lane;
-      float e = 0.0f, w = 0.0f;
-      if (lane < cnt) {
-        if (t < nv) {
-          e = exp_fma(__fsub_rn(v, mx));
-          w = e;
-        } else {
-          w = v;  // raw score
-        }
-      }
-      float l = e;
-      for (int o = 16; o > 0; o >>= 1) l = __fadd_rn(l, __shfl_xor_sync(0xffffffffu, l, o));
-      wt[warp * kAttnChunk + lane] = w;
-      if (lane == 0) {
-        mloc[warp] = mx;
-        lloc[warp] = l;
-      }
-    }
-    __syncthreads();
-    const bool has_tail = t1 > nv;
-#pragma unroll 1
-    for (int p = threadIdx.x; p < G * D; p += kThreads) {
-      int hh = p / D, d = p % D;
-      const float *w = wt + hh * kAttnChunk;
-      float acc = 0.0f, tail = 0.0f;
-#pragma unroll 4
-      for (int tt = 0; tt < cnt; tt++) {
-        if (t0 + tt < nv)
-          acc = __fmaf_rn(w[tt], vs[tt * D + d], acc);
-        else
-          tail = __fmaf_rn(w[tt], vs[tt * D + d], tail);
-      }
-      size_t hc = (hbase + hh) * c.max_chunks + ch;
-      c.part_o[hc * D + d] = acc;
-      if (ch == nch - 1) c.part_t[(hbase + hh) * D + d] = has_tail ? tail : 0.0f;
-      if (d == 0) {
-        c.part_ml[hc * 2] = mloc[hh];
-        c.part_ml[hc * 2 + 1] = lloc[hh];
-      }
-    }
-    // ---- the last chunk item of (m, g) merges the chunks
-    __threadfence();
+    // ---- arrival (the barrier orders the block's partial writes before
+    // thread 0's fence and count); pick the merge work of this block
     __syncthreads();
     if (threadIdx.x == 0) {
-      unsigned *cntp = c.attn_count + m * c.KVH + g;
-      is_last = atomicAdd(cntp, 1u) == (unsigned)(nch - 1);
-      if (is_last) *cntp = 0u;
+      __threadfence();
+      unsigned *cnt = c.attn_count + 2 * (I.m * c.KVH + I.g);
+      const unsigned v = atomicAdd(cnt, 1u);
+      const int nch = I.nch;
+      int mh = -1;
+      if (multi && nch >= G) {
+        if ((int)v >= nch - G) {
+          mh = (int)v - (nch - G);
+          // wait until every chunk of (m, g) has arrived (bounded)
+          unsigned long long spins = 0;
+          while (ld_acquire_u32(cnt) < (unsigned)nch) {
+            if (++spins > (1ull << 24) || *(volatile int *)c.err) {
+              atomicExch(c.err, 1);
+              mh = -2;
+              break;
+            }
+          }
+          if (mh >= 0 && atomicAdd(cnt + 1, 1u) == (unsigned)G - 1) {
+            // every merger has seen the complete count: reset for the next layer
+            cnt[1] = 0u;
+            cnt[0] = 0u;
+          }
+        }
+      } else if ((int)v == nch - 1) {
+        mh = G;  // all heads
+        cnt[0] = 0u;
+      }
+      if (mh >= 0) __threadfence();  // acquire side: the other blocks' partials
+      merge_head = mh;
     }
     __syncthreads();
-    if (is_last) {
-      __threadfence();
-      if (warp < G) {
-        const float *ml = c.part_ml + ((hbase + warp) * c.max_chunks) * 2;
-        float mx = -INFINITY;
+    const int mh = merge_head;
+    if (mh < 0) continue;
+    const int h0 = mh == G ? 0 : mh, h1 = mh == G ? G : mh + 1;
+    const bool has_tail = (I.n & 15) != 0;
+    const int nfull = has_tail ? I.nch - 1 : I.nch;  // chunks with exponentiated weights
 #pragma unroll 1
-        for (int k = lane; k < nch; k += 32) mx = fmaxf(mx, __ldcg(ml + 2 * k));
+    for (int hh = h0; hh < h1; hh++) {
+      const size_t hq = hbase + hh;
+      const float *ml = c.part_ml + hq * c.max_chunks * 2;
+      // this thread's first chunk partials, fetched while warp 0 works out
+      // the chunk scales
+      constexpr int kB = 4;
+      const int grp = threadIdx.x >> 5, d4 = threadIdx.x & 31;
+      const float4 *po = (const float4 *)(c.part_o + hq * c.max_chunks * D) + d4;
+      float4 v[kB];
+#pragma unroll
+      for (int u = 0; u < kB; u++)
+        if (grp + 8 * u < nfull && d4 < D4) v[u] = __ldcg(po + (size_t)(grp + 8 * u) * D4);
+      if (warp == 0) {
+        float mx = -INFINITY;
+        for (int k = lane; k < I.nch; k += 32) mx = fmaxf(mx, __ldcg(ml + 2 * k));
         for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
         float den = 0.0f;
-#pragma unroll 1
-        for (int k = lane; k < nch; k += 32) {
-          float s = exp_fma(__fsub_rn(__ldcg(ml + 2 * k), mx));
-          scl[warp * c.max_chunks + k] = s;
-          den = __fmaf_rn(s, __ldcg(ml + 2 * k + 1), den);
+        for (int k = lane; k < nfull; k += 32) {
+          const float sk = exp_fma(__fsub_rn(__ldcg(ml + 2 * k), mx));
+          scl[k] = sk;
+          den = __fmaf_rn(sk, __ldcg(ml + 2 * k + 1), den);
         }
         for (int o = 16; o > 0; o >>= 1) den = __fadd_rn(den, __shfl_xor_sync(0xffffffffu, den, o));
-        if (lane == 0) dinv[warp] = __fdiv_rn(1.0f, den);
+        if (lane == 0) dinv_s = __fdiv_rn(1.0f, den);
       }
       __syncthreads();
-      // one float4 of one head per thread; the chunk partials are fetched
-      // kMergeBatch at a time so that their L2 round trips overlap, and
-      // accumulated in chunk order
-      constexpr int kMergeBatch = 8;
+      // 8 chunk groups x 32 float4 of dims; group sums, then in group order
+      {
+        float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
 #pragma unroll 1
-      for (int p = threadIdx.x; p < G * D4; p += kThreads) {
-        const int hh = p / D4, d4 = p % D4;
-        const float4 *po = (const float4 *)(c.part_o + ((hbase + hh) * c.max_chunks) * D) + d4;
-        const float *s = scl + hh * c.max_chunks;
-        float4 acc = __ldcg((const float4 *)(c.part_t + (hbase + hh) * D) + d4);
-#pragma unroll 1
-        for (int k0 = 0; k0 < nch; k0 += kMergeBatch) {
-          float4 v[kMergeBatch];
+        for (int k0 = grp; k0 < nfull; k0 += 8 * kB) {
+          if (k0 != grp) {
 #pragma unroll
-          for (int u = 0; u < kMergeBatch; u++)
-            if (k0 + u < nch) v[u] = __ldcg(po + (size_t)(k0 + u) * D4);
+            for (int u = 0; u < kB; u++)
+              if (k0 + 8 * u < nfull && d4 < D4) v[u] = __ldcg(po + (size_t)(k0 + 8 * u) * D4);
+          }
 #pragma unroll
-          for (int u = 0; u < kMergeBatch; u++) {
-            if (k0 + u < nch) {
-              const float w = s[k0 + u];
-              acc.x = __fmaf_rn(w, v[u].x, acc.x);
-              acc.y = __fmaf_rn(w, v[u].y, acc.y);
-              acc.z = __fmaf_rn(w, v[u].z, acc.z);
-              acc.w = __fmaf_rn(w, v[u].w, acc.w);
+          for (int u = 0; u < kB; u++) {
+            if (k0 + 8 * u < nfull) {
+              const float sk = scl[k0 + 8 * u];
+              acc.x = __fmaf_rn(sk, v[u].x, acc.x);
+              acc.y = __fmaf_rn(sk, v[u].y, acc.y);
+              acc.z = __fmaf_rn(sk, v[u].z, acc.z);
+              acc.w = __fmaf_rn(sk, v[u].w, acc.w);
             }
           }
         }
-        const float di = dinv[hh];
-        float4 o;
-        o.x = __fmul_rn(acc.x, di);
-        o.y = __fmul_rn(acc.y, di);
-        o.z = __fmul_rn(acc.z, di);
-        o.w = __fmul_rn(acc.w, di);
-        ((float4 *)(c.head + (hbase + hh) * D))[d4] = o;
+        if (d4 < D4) ((float4 *)(red + grp * D))[d4] = acc;
       }
+      __syncthreads();
+      if (threadIdx.x < D4) {
+        const int d4 = threadIdx.x;
+        float4 acc = has_tail ? __ldcg((const float4 *)(c.part_t + hq * D) + d4) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+#pragma unroll
+        for (int gq = 0; gq < 8; gq++) {
+          const float4 v = ((const float4 *)(red + gq * D))[d4];
+          acc.x = __fadd_rn(acc.x, v.x);
+          acc.y = __fadd_rn(acc.y, v.y);
+          acc.z = __fadd_rn(acc.z, v.z);
+          acc.w = __fadd_rn(acc.w, v.w);
+        }
+        const float di = dinv_s;
+        ((float4 *)(c.head + hq * D))[d4] =
+            make_float4(__fmul_rn(acc.x, di), __fmul_rn(acc.y, di), __fmul_rn(acc.z, di), __fmul_rn(acc.w, di));
+      }
+      __syncthreads();
     }
-    __syncthreads();
   }
-}
-
-__host__ __device__ __forceinline__ size_t attn_smem_floats(int max_chunks) {
-  return (size_t)kMaxGroup * kHeadDim + (size_t)kAttnChunk * (kHeadDim + 1) + (size_t)kAttnChunk * kHeadDim +
-         2 * (size_t)kMaxGroup * kAttnChunk + (size_t)kMaxGroup * max_chunks;
+  attn_drain(c);
 }
 
 // Normalised output of a fused AddRMSNorm (the normOut vector of

@@ -69,12 +69,17 @@ __device__ __forceinline__ void red_add_release(unsigned *p, unsigned v) {
 // records an error and leaves; waiting blocks also leave once any block has
 // recorded one.  Returns false on error.
 constexpr unsigned long long kBarrierSpins = 1ull << 22;
-__device__ bool grid_sync(const Ctx &c, unsigned target) {
-  __shared__ int ok;
+__shared__ int s_grid_ok;
+// Arrival half: after the block's phase work (all threads), thread 0 adds 1.
+__device__ __forceinline__ void grid_arrive(const Ctx &c) {
   __syncthreads();
+  if (threadIdx.x == 0) red_add_release(c.bar_count, 1u);
+}
+// Waiting half: thread 0 polls until the counter reaches `target`; the block
+// may do work that does not depend on other blocks between the two halves.
+__device__ bool grid_wait(const Ctx &c, unsigned target) {
   if (threadIdx.x == 0) {
-    ok = 1;
-    red_add_release(c.bar_count, 1u);
+    int ok = 1;
     unsigned long long spins = 0;
     while ((int)(ld_acquire(c.bar_count) - target) < 0) {
       ++spins;
@@ -84,9 +89,14 @@ __device__ bool grid_sync(const Ctx &c, unsigned target) {
         break;
       }
     }
+    s_grid_ok = ok;
   }
   __syncthreads();
-  return ok != 0;
+  return s_grid_ok != 0;
+}
+__device__ bool grid_sync(const Ctx &c, unsigned target) {
+  grid_arrive(c);
+  return grid_wait(c, target);
 }
 
 constexpr int kLayerPhases = 5;  // qkv, attention, o, gate/up, down
@@ -100,14 +110,14 @@ __host__ __device__ __forceinline__ unsigned barriers_per_step(int L, int any_lo
 // shared memory.
 template <int QT>
 __device__ void run_phase(const Ctx &c, int phase, int layer, int M, int any_logits, int do_embed, int feed,
-                          float *smem, int tidx) {
+                          float *smem, int tidx, int coop) {
   __shared__ GemvArgs sa;
   unsigned long long *tslot = c.trace ? c.trace + 4 * tidx : nullptr;
   if (tslot && blockIdx.x == 0 && threadIdx.x == 0) tslot[0] = gtimer();
   const LayerW &L = c.layers[layer < c.L ? layer : c.L - 1];
   const bool last = layer == c.L - 1;
   if (phase == 1) {
-    phase_attn(&c, layer, last && !any_logits, smem);
+    phase_attn(&c, layer, last && !any_logits, coop, smem);
   } else {
     if (threadIdx.x == 0) {
       memset(&sa, 0, sizeof(sa));
@@ -189,11 +199,29 @@ __device__ void run_phase(const Ctx &c, int phase, int layer, int M, int any_log
   if (tslot && threadIdx.x == 0) atomicMax(tslot + 2, gtimer());
 }
 
-// Ctx is copied into shared memory once per launch; phases read it there.
-#define OCRVL_CTX_TO_SMEM(cv)                       \
-  __shared__ Ctx sctx;                              \
-  if (threadIdx.x == 0) sctx = cv;                  \
-  __syncthreads();                                  \
+// Ctx is copied into shared memory once per launch, and with it the step
+// parameters and (up to kSmemLayers layers) the layer descriptors, so phases
+// start without global-memory round trips for their arguments.
+constexpr int kSmemLayers = 32;
+__shared__ StepParams s_step_params;
+__shared__ LayerW s_layer_desc[kSmemLayers];
+
+__device__ __forceinline__ void copy_words(void *dst, const void *src, int bytes) {
+  for (int i = threadIdx.x; i < bytes / 4; i += kThreads) ((int *)dst)[i] = ((const int *)src)[i];
+}
+
+#define OCRVL_CTX_TO_SMEM(cv)                                                        \
+  __shared__ Ctx sctx;                                                               \
+  if (threadIdx.x == 0) sctx = cv;                                                   \
+  if (cv.sp) copy_words(&s_step_params, cv.sp, (int)sizeof(StepParams));             \
+  if (cv.layers && cv.L <= kSmemLayers)                                              \
+    copy_words(s_layer_desc, cv.layers, (int)sizeof(LayerW) * cv.L);                 \
+  __syncthreads();                                                                   \
+  if (threadIdx.x == 0) {                                                            \
+    if (cv.sp) sctx.sp = &s_step_params;                                             \
+    if (cv.layers && cv.L <= kSmemLayers) sctx.layers = s_layer_desc;                \
+  }                                                                                  \
+  __syncthreads();                                                                   \
   const Ctx &c = sctx;
 
 template <int QT>
@@ -202,18 +230,30 @@ __global__ void __launch_bounds__(kThreads, 1)
   extern __shared__ float4 smem4[];
   float *smem = (float *)smem4;
   OCRVL_CTX_TO_SMEM(cv);
+  attn_block_init();
   unsigned k = 0;
   int t = 0;
   for (int l = 0; l < c.L; l++) {
     const bool kv_only = l == c.L - 1 && !any_logits;
     for (int ph = 0; ph < kLayerPhases; ph++, t++) {
-      run_phase<QT>(c, ph, l, M, any_logits, do_embed, feed, smem, t);
+      run_phase<QT>(c, ph, l, M, any_logits, do_embed, feed, smem, t, 1);
       if (kv_only && ph == 1) return;
-      if (!grid_sync(c, bar_base + (++k) * gridDim.x)) return;
+      grid_arrive(c);
+      if (ph == 0) {
+        // work that needs nothing from other blocks, done while they finish:
+        // the attention item's K/V page copies, and (once per launch) the
+        // RoPE values of this step's positions
+        attn_prefetch(c, l, smem);
+        if (l == 0) attn_rope_tables(c);
+      }
+      if (!grid_wait(c, bar_base + (++k) * gridDim.x)) {
+        attn_drain(c);
+        return;
+      }
       if (c.trace && blockIdx.x == 0 && threadIdx.x == 0) c.trace[4 * t + 3] = gtimer();
     }
   }
-  if (any_logits) run_phase<QT>(c, kPhaseLM, c.L, M, any_logits, do_embed, feed, smem, t);
+  if (any_logits) run_phase<QT>(c, kPhaseLM, c.L, M, any_logits, do_embed, feed, smem, t, 1);
 }
 
 template <int QT>
@@ -224,7 +264,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   Ctx &cm = sctx;
   if (threadIdx.x == 0) cm.trace = nullptr;
   __syncthreads();
-  run_phase<QT>(c, phase, layer, M, any_logits, do_embed, feed, (float *)smem4, 0);
+  attn_block_init();
+  run_phase<QT>(c, phase, layer, M, any_logits, do_embed, feed, (float *)smem4, 0, 0);
 }
 
 template <int QT>
@@ -450,7 +491,7 @@ void reset_after_timeout(ocrvl_model *m) {
   int zero = 0;
   cudaMemcpy(m->ctx.err, &zero, 4, cudaMemcpyHostToDevice);
   cudaMemset(m->ctx.bar_count, 0, 4);
-  cudaMemset(m->ctx.attn_count, 0, (size_t)kMaxBatch * m->ctx.KVH * 4);
+  cudaMemset(m->ctx.attn_count, 0, (size_t)2 * kMaxBatch * m->ctx.KVH * 4);
   cudaMemset(m->ctx.lm_count, 0, 4);
   cudaMemset(m->ctx.argkey, 0, kMaxBatch * 8);
   m->bar_base = 0;
@@ -657,7 +698,7 @@ int ocrvl_finalize(ocrvl_model *m) {
   c.kv_pool = m->kv_pool;
   c.page_floats = m->page_floats;
   c.max_ctx = d.max_position;
-  c.max_chunks = (c.max_ctx + kAttnChunk - 1) / kAttnChunk;
+  c.max_chunks = (c.max_ctx + kChunkTok - 1) / kChunkTok;
   int qkvld = (c.QH + 2 * c.KVH) * c.D;
   size_t B = kMaxBatch;
   c.h = m->dalloc<float>(B * c.H);
@@ -671,7 +712,7 @@ int ocrvl_finalize(ocrvl_model *m) {
   c.logits = m->dalloc<float>(B * (size_t)c.V);
   c.argkey = m->dalloc<unsigned long long>(B);
   c.tok_out = m->dalloc<int>(B + 1);
-  c.bar_count = m->dalloc<unsigned>(2 + B * c.KVH);
+  c.bar_count = m->dalloc<unsigned>(2 + 2 * B * c.KVH);
   c.lm_count = c.bar_count + 1;
   c.attn_count = c.bar_count + 2;
   c.hist_pos = m->dalloc<int>(1);
@@ -682,10 +723,12 @@ int ocrvl_finalize(ocrvl_model *m) {
     return fail(OCRVL_E_NOMEM, "work buffer allocation failed");
   c.err = c.tok_out + B;
   c.sp = spd;
+  c.sp_w = spd;
   m->sp_d = spd;
+  c.pro_cols = std::max(std::max(d.hidden_size, d.intermediate_size), d.num_heads * d.head_dim);
   CK(cudaMemset(c.argkey, 0, B * 8));
   CK(cudaMemset(c.tok_out, 0, (B + 1) * 4));
-  CK(cudaMemset(c.bar_count, 0, (2 + B * c.KVH) * 4));
+  CK(cudaMemset(c.bar_count, 0, (2 + 2 * B * c.KVH) * 4));
   CK(cudaHostAlloc((void **)&m->sp_h, sizeof(StepParams), cudaHostAllocDefault));
   CK(cudaHostAlloc((void **)&m->out_h, (B + 1) * 4, cudaHostAllocDefault));
   CK(cudaHostAlloc((void **)&m->bt_stage, B * 4, cudaHostAllocDefault));
