@@ -624,9 +624,14 @@ struct GemvArgs {
 
 // Contiguous slab of rows [lo, hi) of a GEMV owned by block `b` of `nb`.
 __device__ __forceinline__ void gemv_slab(int row_begin, int row_end, int b, int nb, int &lo, int &hi) {
-  long long n = row_end - row_begin;
-  lo = row_begin + (int)(n * b / nb);
-  hi = row_begin + (int)(n * (b + 1) / nb);
+  const unsigned n = (unsigned)(row_end - row_begin);
+  if (n < (1u << 23)) {  // n * nb fits 32 bits for any grid of <= 512 blocks
+    lo = row_begin + (int)(n * (unsigned)b / (unsigned)nb);
+    hi = row_begin + (int)(n * (unsigned)(b + 1) / (unsigned)nb);
+  } else {
+    lo = row_begin + (int)((unsigned long long)n * b / nb);
+    hi = row_begin + (int)((unsigned long long)n * (b + 1) / nb);
+  }
 }
 
 // Weight staging: each block streams its slab of packed rows through a ring
@@ -634,15 +639,19 @@ __device__ __forceinline__ void gemv_slab(int row_begin, int row_end, int b, int
 // first stages are issued before the input prologue so weight transfer
 // overlaps the normalisation / quantisation of the input.
 constexpr int kStageBytes = 32768;
-constexpr int kStagesM1 = 4;   // stages for the single-sequence form
+constexpr int kStagesM1 = 5;   // stages for the single-sequence form
 constexpr int kStagesMB = 2;   // stages for the batched form
 // Row scales and row sums of a block's slab (A and B matrices) and the norm
 // weights are staged in shared memory with cp.async at the start of the
 // phase, when the slab has at most kSlabRowsMax rows and the norm vector at
 // most kNormStageMax entries (otherwise they are read from global memory).
-constexpr int kSlabRowsMax = 1024;
+constexpr int kSlabRowsMax = 1024;  // A matrix rows
+constexpr int kSlabRowsB = 128;     // B matrix (SwiGLU up) rows
 constexpr int kNormStageMax = 2048;
-constexpr size_t kGemvAuxBytes = (size_t)4 * kSlabRowsMax * 4 + (size_t)kNormStageMax * 4;
+// aux layout (floats): A scales | A row sums | B scales | B row sums | norm weights
+constexpr int kAuxRsA = kSlabRowsMax, kAuxScB = 2 * kSlabRowsMax, kAuxRsB = kAuxScB + kSlabRowsB;
+constexpr int kAuxNw = kAuxRsB + kSlabRowsB;
+constexpr size_t kGemvAuxBytes = (size_t)(kAuxNw + kNormStageMax) * 4;
 
 __host__ __device__ __forceinline__ size_t gemv_prologue_bytes(int qt, int nvec, int n) {
   size_t area = qt == QT_Q8 ? (size_t)nvec * n * 4 : (size_t)nvec * n;
@@ -650,6 +659,140 @@ __host__ __device__ __forceinline__ size_t gemv_prologue_bytes(int qt, int nvec,
 }
 __host__ __device__ __forceinline__ size_t gemv_smem_total(int qt, int nvec, int n, int stages) {
   return gemv_prologue_bytes(qt, nvec, n) + (size_t)stages * kStageBytes + kGemvAuxBytes;
+}
+
+// ---------------------------------------------------------------------------
+// Stage ring shared by the GEMV phases of one launch.  One mbarrier per ring
+// slot, initialised once per launch; s_ring_par bit i is the parity of slot
+// i's next completion and s_ring_busy bit i says a copy into slot i is in
+// flight.  A phase's first stages and its cp.async staging (row scales / row
+// sums, norm weights) can be issued ahead of the phase ("setup"), in the step
+// kernel while the block waits at the grid barrier before it; s_ring_setup
+// tells the phase that this was done.
+// ---------------------------------------------------------------------------
+constexpr int kMaxStages = kStagesM1 > kStagesMB ? kStagesM1 : kStagesMB;
+__shared__ __align__(8) uint64_t s_ring_bar[kMaxStages];
+__shared__ uint32_t s_ring_par, s_ring_busy;
+__shared__ int s_ring_setup;
+
+__device__ __forceinline__ void ring_init() {
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < kMaxStages; i++) mbar_init(&s_ring_bar[i], 1);
+    mbar_fence_init();
+    s_ring_par = 0;
+    s_ring_busy = 0;
+    s_ring_setup = 0;
+  }
+  __syncthreads();
+}
+
+// Where a GEMV phase keeps its stages and staged values, and how its slab of
+// rows splits into stages.  The ring follows the widest prologue the kernel
+// can run (Ctx::pro_cols), so its place does not move between phases.
+struct GemvGeo {
+  int lo, hi, P, srows, nst, kSt;
+  int lpr;  // lanes per row of the x-stationary form (Q4/Q6)
+  bool two, staged, nw_staged;
+  uint8_t *stage;
+  float *aux;
+};
+__shared__ GemvGeo s_geo;  // geometry of the phase that was set up ahead
+
+__device__ __forceinline__ GemvGeo gemv_geo(int qt, const Ctx &c, const GemvArgs &a, int M, float *smem) {
+  GemvGeo g;
+  gemv_slab(a.row_begin, a.row_end, blockIdx.x, gridDim.x, g.lo, g.hi);
+  g.P = a.A.pitch;
+  g.two = a.epi == EPI_SWIGLU;
+  g.kSt = M <= 1 ? kStagesM1 : kStagesMB;
+  g.stage = (uint8_t *)smem + gemv_prologue_bytes(qt, M <= 1 ? 1 : kMaxBatch, c.pro_cols ? c.pro_cols : a.A.cols);
+  g.srows = kStageBytes / (g.P * (g.two ? 2 : 1));
+  g.nst = (g.hi - g.lo + g.srows - 1) / g.srows;
+  g.aux = (float *)(g.stage + (size_t)g.kSt * kStageBytes);
+  g.staged = g.hi - g.lo <= kSlabRowsMax && (!g.two || g.hi - g.lo <= kSlabRowsB);
+  g.nw_staged = a.mode != PRO_PLAIN && a.A.cols <= kNormStageMax;
+  g.lpr = 32;
+  if (qt != QT_Q8) {
+    const int cb = qt == QT_Q4 ? 16 : 48, xmax = qt == QT_Q4 ? 4 : 2;
+    const int ch = g.P / cb;
+    int l = 1;
+    while (l < 32 && (ch + l - 1) / l > xmax) l <<= 1;
+    g.lpr = l;
+  }
+  return g;
+}
+
+// Thread 0: copy of stage `st` of the slab into its ring slot.
+__device__ __forceinline__ void gemv_issue(const GemvArgs &a, const GemvGeo &g, int st) {
+  const int slot = st % g.kSt;
+  const int r0 = g.lo + st * g.srows, nr = min(g.srows, g.hi - r0);
+  uint8_t *buf = g.stage + (size_t)slot * kStageBytes;
+  const uint32_t bytes = (uint32_t)nr * g.P;
+  mbar_expect_tx(&s_ring_bar[slot], g.two ? 2 * bytes : bytes);
+  bulk_g2s(buf, a.A.w + (size_t)r0 * g.P, bytes, &s_ring_bar[slot]);
+  if (g.two) bulk_g2s(buf + (size_t)g.srows * g.P, a.B.w + (size_t)r0 * g.P, bytes, &s_ring_bar[slot]);
+  s_ring_busy |= 1u << slot;
+}
+
+// Bounded wait for stage `st`; every thread calls it.
+__device__ __forceinline__ bool gemv_wait(const Ctx &c, const GemvGeo &g, int st) {
+  const int slot = st % g.kSt;
+  return mbar_wait(&s_ring_bar[slot], (s_ring_par >> slot) & 1u, c.err);
+}
+
+// After a stage's compute and a block barrier: thread 0 retires the slot and
+// refills it with stage st + kSt.
+__device__ __forceinline__ void gemv_retire(const GemvArgs &a, const GemvGeo &g, int st) {
+  if (threadIdx.x == 0) {
+    const int slot = st % g.kSt;
+    s_ring_par ^= 1u << slot;
+    s_ring_busy &= ~(1u << slot);
+    if (st + g.kSt < g.nst) gemv_issue(a, g, st + g.kSt);
+  }
+}
+
+// Issues the phase's first stages (thread `lead`) and the cp.async staging of
+// its row scales / row sums and norm weights (threads lead .. lead+nthr-1).
+__device__ void gemv_setup(int qt, const Ctx &c, const GemvArgs &a, int M, float *smem, int lead = 0,
+                           int nthr = kThreads) {
+  const GemvGeo g = gemv_geo(qt, c, a, M, smem);
+  const int tid = (int)threadIdx.x - lead;
+  if (tid == 0) {
+    s_geo = g;
+    for (int st = 0; st < g.nst && st < g.kSt; st++) gemv_issue(a, g, st);
+  }
+  const bool vnni = qt != QT_Q8;
+  if (g.nw_staged) {
+    float *nw_s = g.aux + kAuxNw;
+    for (int i = tid; i < a.A.cols / 4; i += nthr) cp_async16(nw_s + 4 * i, a.norm_w + 4 * i);
+  }
+  if (g.staged) {
+    const int nrows = g.hi - g.lo;
+    for (int i = tid; i < nrows; i += nthr) {
+      cp_async4(g.aux + i, a.A.scale + g.lo + i);
+      if (vnni) cp_async4(g.aux + kAuxRsA + i, a.A.rowsum + g.lo + i);
+      if (g.two) {
+        cp_async4(g.aux + kAuxScB + i, a.B.scale + g.lo + i);
+        if (vnni) cp_async4(g.aux + kAuxRsB + i, a.B.rowsum + g.lo + i);
+      }
+    }
+  }
+}
+
+// Waits for copies the block still has in flight (before leaving the kernel
+// early).  Every thread calls it.
+__device__ void gemv_drain(const Ctx &c) {
+  cp_async_wait_all();
+  if (threadIdx.x == 0) {
+    for (int slot = 0; slot < kMaxStages; slot++) {
+      if ((s_ring_busy >> slot) & 1u) {
+        mbar_wait(&s_ring_bar[slot], (s_ring_par >> slot) & 1u, c.err);
+        s_ring_par ^= 1u << slot;
+      }
+    }
+    s_ring_busy = 0;
+    s_ring_setup = 0;
+  }
+  __syncthreads();
 }
 
 // Last block of the lm_head phase: keys -> ids (ties -> lowest id), key and
@@ -687,53 +830,21 @@ template <int QT, int M_, int RB>
 __device__ __noinline__ void phase_gemv_t(const Ctx *cp, const GemvArgs *ap, int M, float *smem) {
   const Ctx &c = *cp;
   const GemvArgs &a = *ap;
-  constexpr int kSt = M_ == 1 ? kStagesM1 : kStagesMB;
-  __shared__ __align__(8) uint64_t full[kSt];
   const int qt = QT;
-  const int P = a.A.pitch;
-  const bool two = a.epi == EPI_SWIGLU;
-  int lo, hi;
-  gemv_slab(a.row_begin, a.row_end, blockIdx.x, gridDim.x, lo, hi);
-  uint8_t *stage = (uint8_t *)smem + gemv_prologue_bytes(qt, M_ == 1 ? 1 : kMaxBatch, c.pro_cols ? c.pro_cols : a.A.cols);
-  const int srows = kStageBytes / (P * (two ? 2 : 1));  // rows per stage
-  const int nst = (hi - lo + srows - 1) / srows;
-  auto issue = [&](int st) {
-    const int r0 = lo + st * srows, nr = min(srows, hi - r0);
-    uint8_t *buf = stage + (size_t)(st % kSt) * kStageBytes;
-    const uint32_t bytes = (uint32_t)nr * P;
-    mbar_expect_tx(&full[st % kSt], two ? 2 * bytes : bytes);
-    bulk_g2s(buf, a.A.w + (size_t)r0 * P, bytes, &full[st % kSt]);
-    if (two) bulk_g2s(buf + (size_t)srows * P, a.B.w + (size_t)r0 * P, bytes, &full[st % kSt]);
-  };
-  if (threadIdx.x == 0) {
-    for (int i = 0; i < kSt; i++) mbar_init(&full[i], 1);
-    mbar_fence_init();
-    for (int st = 0; st < nst && st < kSt; st++) issue(st);
-  }
-  // stage the slab's row scales / row sums and the norm weights (cp.async,
-  // waited for inside the prologue)
-  float *aux = (float *)(stage + (size_t)kSt * kStageBytes);
-  const int nrows = hi - lo;
-  const bool staged = nrows <= kSlabRowsMax;
+  const bool pre = s_ring_setup;
+  if (!pre) gemv_setup(qt, c, a, M_ == 1 ? 1 : kMaxBatch, smem);
+  const GemvGeo g = pre ? s_geo : gemv_geo(qt, c, a, M_ == 1 ? 1 : kMaxBatch, smem);
+  const int P = g.P, lo = g.lo, hi = g.hi, srows = g.srows, nst = g.nst;
+  const bool two = g.two;
+  float *aux = g.aux;
+  const bool staged = g.staged;
   const bool vnni = qt != QT_Q8;
-  if (staged) {
-    for (int i = threadIdx.x; i < nrows; i += kThreads) {
-      cp_async4(aux + i, a.A.scale + lo + i);
-      if (vnni) cp_async4(aux + kSlabRowsMax + i, a.A.rowsum + lo + i);
-      if (two) {
-        cp_async4(aux + 2 * kSlabRowsMax + i, a.B.scale + lo + i);
-        if (vnni) cp_async4(aux + 3 * kSlabRowsMax + i, a.B.rowsum + lo + i);
-      }
-    }
-  }
   const float *scl_a = staged ? aux : a.A.scale + lo;
-  const int32_t *rsm_a = staged ? (const int32_t *)(aux + kSlabRowsMax) : a.A.rowsum + lo;
-  const float *scl_b = staged ? aux + 2 * kSlabRowsMax : a.B.scale + lo;
-  const int32_t *rsm_b = staged ? (const int32_t *)(aux + 3 * kSlabRowsMax) : a.B.rowsum + lo;
-  const bool nw_staged = a.mode != PRO_PLAIN && a.A.cols <= kNormStageMax;
-  float *nw_s = aux + 4 * kSlabRowsMax;
-  if (nw_staged)
-    for (int i = threadIdx.x; i < a.A.cols / 4; i += kThreads) cp_async16(nw_s + 4 * i, a.norm_w + 4 * i);
+  const int32_t *rsm_a = staged ? (const int32_t *)(aux + kAuxRsA) : a.A.rowsum + lo;
+  const float *scl_b = staged ? aux + kAuxScB : a.B.scale + lo;
+  const int32_t *rsm_b = staged ? (const int32_t *)(aux + kAuxRsB) : a.B.rowsum + lo;
+  const bool nw_staged = g.nw_staged;
+  float *nw_s = aux + kAuxNw;
   gemv_prologue(qt, M, a.src, a.ld, a.src_tok ? c.sp->tok : nullptr, a.A.cols, a.mode, nw_staged ? nw_s : a.norm_w,
                 !nw_staged, c.eps, smem);
   const XIn x = gemv_inputs(a.A.cols, smem);
@@ -778,8 +889,8 @@ __device__ __noinline__ void phase_gemv_t(const Ctx *cp, const GemvArgs *ap, int
 #pragma unroll 1
   for (int st = 0; st < nst; st++) {
     const int r0 = lo + st * srows, nr = min(srows, hi - r0);
-    const uint8_t *buf = stage + (size_t)(st % kSt) * kStageBytes;
-    if (!mbar_wait(&full[st % kSt], (uint32_t)((st / kSt) & 1), c.err)) ok = false;
+    const uint8_t *buf = g.stage + (size_t)(st % g.kSt) * kStageBytes;
+    if (!gemv_wait(c, g, st)) ok = false;
     const int ngroups = (nr + per_group - 1) / per_group;
 #pragma unroll 1
     for (int gi = warp; ok && gi < ngroups; gi += kThreads / 32) {
@@ -834,8 +945,9 @@ __device__ __noinline__ void phase_gemv_t(const Ctx *cp, const GemvArgs *ap, int
       }
     }
     __syncthreads();  // stage buffer free
-    if (threadIdx.x == 0 && st + kSt < nst) issue(st + kSt);
+    gemv_retire(a, g, st);
   }
+  if (threadIdx.x == 0) s_ring_setup = 0;
   if (a.epi == EPI_ARGMAX) {
 #pragma unroll
     for (int m = 0; m < M_; m++) {
@@ -871,6 +983,128 @@ __device__ __noinline__ void phase_gemv_t(const Ctx *cp, const GemvArgs *ap, int
 // at once with two dp4a chains per row; the int32 sums are exact, so the split
 // does not change results.
 // ---------------------------------------------------------------------------
+// Input prologue of the single-sequence int8-activation GEMV (xs path), with
+// two block barriers: the gather, then the quantised vector.  Every warp
+// computes the norm's sum of squares in the reference order and the largest
+// |value| itself, so no barrier is spent on those reductions.
+//   PRO_RMSNORM: 64 FMA slot chains (sumSquaresF32FMA), lane L owning slots L
+//     and L+32; slots folded as (s[l]+s[l+16]) + (s[l+32]+s[l+48]) by xor-16
+//     shuffles, then tree16 by xor 8/4/2/1.
+//   PRO_ADDNORM: the fused kernels' 8 workers of n/8 rows, each 16 lanes of
+//     unfused square-adds + tree16 (VNNI finalize); lane L (l = L%16, h =
+//     L/16) runs workers h, h+2, h+4, h+6; worker partials added in order.
+//   The largest |normalised value| is fl(max|fl(x*w)| * scale), rounding
+//   being monotone and sign-symmetric.
+// Writes the uint8 activations (Q4: even columns then odd) to the x area and
+// returns the activation scale sx (the same value in every thread).
+__device__ __noinline__ float xs_prologue(int qt, const float *src, int n, int mode, const float *w, bool w_global,
+                                          float eps, float *smem) {
+  float *tmp = smem + 320;
+  uint8_t *q = (uint8_t *)(tmp + n);
+  g2s_f32(tmp, src, n);
+  cp_async_wait_all();
+  __syncthreads();
+  const int lane = threadIdx.x & 31;
+  auto wv = [&](int i) { return w_global ? __ldg(w + i) : w[i]; };
+  float ss = 0.0f, M = 0.0f;
+  // largest |x| (PLAIN) or |fl(x*w)| over the whole vector, float4 at a time
+  if (mode == PRO_PLAIN || !w_global) {
+#pragma unroll 4
+    for (int i = lane; i < n / 4; i += 32) {
+      const float4 x = ((const float4 *)tmp)[i];
+      if (mode == PRO_PLAIN) {
+        M = fmaxf(M, fmaxf(fmaxf(fabsf(x.x), fabsf(x.y)), fmaxf(fabsf(x.z), fabsf(x.w))));
+      } else {
+        const float4 ww = ((const float4 *)w)[i];
+        M = fmaxf(M, fmaxf(fmaxf(fabsf(__fmul_rn(x.x, ww.x)), fabsf(__fmul_rn(x.y, ww.y))),
+                           fmaxf(fabsf(__fmul_rn(x.z, ww.z)), fabsf(__fmul_rn(x.w, ww.w)))));
+      }
+    }
+  } else {
+    for (int i = lane; i < n; i += 32) M = fmaxf(M, fabsf(__fmul_rn(tmp[i], __ldg(w + i))));
+  }
+  if (mode == PRO_RMSNORM) {
+    // two slot chains per lane; loads batched ahead of the FMAs
+    float a0 = 0.0f, a1 = 0.0f;
+    constexpr int U = 8;
+#pragma unroll 1
+    for (int c0 = 0; c0 < n; c0 += 64 * U) {
+      float x0[U], x1[U];
+#pragma unroll
+      for (int u = 0; u < U; u++) {
+        const int c = c0 + 64 * u;
+        x0[u] = c < n ? tmp[c + lane] : 0.0f;
+        x1[u] = c < n ? tmp[c + 32 + lane] : 0.0f;
+      }
+#pragma unroll
+      for (int u = 0; u < U; u++) {
+        if (c0 + 64 * u < n) {
+          a0 = __fmaf_rn(x0[u], x0[u], a0);
+          a1 = __fmaf_rn(x1[u], x1[u], a1);
+        }
+      }
+    }
+    float r = __fadd_rn(__fadd_rn(a0, __shfl_xor_sync(0xffffffffu, a0, 16)),
+                        __fadd_rn(a1, __shfl_xor_sync(0xffffffffu, a1, 16)));
+    r = __fadd_rn(r, __shfl_xor_sync(0xffffffffu, r, 8));
+    r = __fadd_rn(r, __shfl_xor_sync(0xffffffffu, r, 4));
+    r = __fadd_rn(r, __shfl_xor_sync(0xffffffffu, r, 2));
+    ss = __fadd_rn(r, __shfl_xor_sync(0xffffffffu, r, 1));
+  } else if (mode == PRO_ADDNORM) {
+    // four worker chains per lane, interleaved; loads batched ahead
+    const int chunk = n / kFusedWorkers, l = lane & 15, h = lane >> 4;
+    float part[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+    constexpr int U = 4;
+#pragma unroll 1
+    for (int k0 = 0; k0 < chunk; k0 += 16 * U) {
+      float v[4][U];
+#pragma unroll
+      for (int j = 0; j < 4; j++)
+#pragma unroll
+        for (int u = 0; u < U; u++) {
+          const int k = k0 + 16 * u;
+          v[j][u] = k < chunk ? tmp[(h + 2 * j) * chunk + k + l] : 0.0f;
+        }
+#pragma unroll
+      for (int u = 0; u < U; u++)
+#pragma unroll
+        for (int j = 0; j < 4; j++)
+          if (k0 + 16 * u < chunk) part[j] = __fadd_rn(part[j], __fmul_rn(v[j][u], v[j][u]));
+    }
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+      float a = part[j];
+      a = __fadd_rn(a, __shfl_xor_sync(0xffffffffu, a, 8));
+      a = __fadd_rn(a, __shfl_xor_sync(0xffffffffu, a, 4));
+      a = __fadd_rn(a, __shfl_xor_sync(0xffffffffu, a, 2));
+      part[j] = __fadd_rn(a, __shfl_xor_sync(0xffffffffu, a, 1));
+    }
+#pragma unroll
+    for (int wk = 0; wk < kFusedWorkers; wk++) ss = __fadd_rn(ss, __shfl_sync(0xffffffffu, part[wk >> 1], (wk & 1) * 16));
+  }
+  for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+  float scale = 1.0f, mx = M;
+  if (mode != PRO_PLAIN) {
+    scale = fast_rsqrt(__fadd_rn(__fdiv_rn(ss, (float)n), eps));
+    mx = __fmul_rn(M, scale);
+  }
+  float sx = 1.0f, inv = 0.0f;
+  if (mx != 0.0f) {
+    sx = __fdiv_rn(mx, 127.0f);
+    inv = __fdiv_rn(1.0f, sx);
+  }
+  const int half = qt == QT_Q4 ? n / 2 : 0;
+  for (int i = threadIdx.x; i < n; i += kThreads) {
+    float v = tmp[i];
+    if (mode != PRO_PLAIN) v = __fmul_rn(__fmul_rn(v, wv(i)), scale);
+    const float f = __fadd_rn(rintf(__fmul_rn(v, inv)), 128.0f);
+    const int b = mx != 0.0f ? (int)fminf(fmaxf(f, 0.0f), 255.0f) : 128;
+    q[half ? (i & 1) * half + (i >> 1) : i] = (uint8_t)b;
+  }
+  __syncthreads();
+  return sx;
+}
+
 template <int QT>
 struct XsTraits;
 template <>
@@ -941,70 +1175,52 @@ __device__ __forceinline__ uint32_t xs_row_dot(const uint8_t *w, const uint4 (*x
   return a0 + a1;
 }
 
-template <int QT>
+template <int QT, int RB>
 __device__ __noinline__ void phase_gemv_xs(const Ctx *cp, const GemvArgs *ap, float *smem) {
   using T = XsTraits<QT>;
-  constexpr int RB = 2;
-  constexpr int kSt = kStagesM1;
   const Ctx &c = *cp;
   const GemvArgs &a = *ap;
-  __shared__ __align__(8) uint64_t full[kSt];
-  const int P = a.A.pitch, n = a.A.cols, CH = P / T::CB;
-  const bool two = a.epi == EPI_SWIGLU;
-  int lo, hi;
-  gemv_slab(a.row_begin, a.row_end, blockIdx.x, gridDim.x, lo, hi);
-  uint8_t *stage = (uint8_t *)smem + gemv_prologue_bytes(QT, 1, c.pro_cols ? c.pro_cols : n);
-  const int srows = kStageBytes / (P * (two ? 2 : 1));
-  const int nst = (hi - lo + srows - 1) / srows;
-  auto issue = [&](int st) {
-    const int r0 = lo + st * srows, nr = min(srows, hi - r0);
-    uint8_t *buf = stage + (size_t)(st % kSt) * kStageBytes;
-    const uint32_t bytes = (uint32_t)nr * P;
-    mbar_expect_tx(&full[st % kSt], two ? 2 * bytes : bytes);
-    bulk_g2s(buf, a.A.w + (size_t)r0 * P, bytes, &full[st % kSt]);
-    if (two) bulk_g2s(buf + (size_t)srows * P, a.B.w + (size_t)r0 * P, bytes, &full[st % kSt]);
-  };
-  if (threadIdx.x == 0) {
-    for (int i = 0; i < kSt; i++) mbar_init(&full[i], 1);
-    mbar_fence_init();
-    for (int st = 0; st < nst && st < kSt; st++) issue(st);
-  }
-  // row scales / row sums of the slab and the norm weights (cp.async)
-  float *aux = (float *)(stage + (size_t)kSt * kStageBytes);
-  const int nrows = hi - lo;
-  const bool staged = nrows <= kSlabRowsMax;
-  if (staged) {
-    for (int i = threadIdx.x; i < nrows; i += kThreads) {
-      cp_async4(aux + i, a.A.scale + lo + i);
-      cp_async4(aux + kSlabRowsMax + i, a.A.rowsum + lo + i);
-      if (two) {
-        cp_async4(aux + 2 * kSlabRowsMax + i, a.B.scale + lo + i);
-        cp_async4(aux + 3 * kSlabRowsMax + i, a.B.rowsum + lo + i);
-      }
+  const bool pre = s_ring_setup;
+  if (!pre) gemv_setup(QT, c, a, 1, smem);
+  const GemvGeo g = pre ? s_geo : gemv_geo(QT, c, a, 1, smem);
+  const int P = g.P, n = a.A.cols, CH = QT == QT_Q4 ? P >> 4 : P / 48;
+  const int lo = g.lo, hi = g.hi, srows = g.srows, nst = g.nst;
+  const bool two = g.two;
+  float *aux = g.aux;
+  const bool staged = g.staged;
+  const float *scl_a = staged ? aux : a.A.scale + lo;
+  const int32_t *rsm_a = staged ? (const int32_t *)(aux + kAuxRsA) : a.A.rowsum + lo;
+  const float *scl_b = staged ? aux + kAuxScB : a.B.scale + lo;
+  const int32_t *rsm_b = staged ? (const int32_t *)(aux + kAuxRsB) : a.B.rowsum + lo;
+  const bool nw_staged = g.nw_staged;
+  float *nw_s = aux + kAuxNw;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int lpr = g.lpr;
+  const int rpw = 32 / lpr, li = lane & (lpr - 1), sub = lane / lpr;
+  const int pass = (kThreads / 32) * rpw;  // rows one pass of the block covers per RB slot
+  // residual values of this lane's rows of a one-stage slab, fetched now so
+  // their latency hides behind the prologue
+  float rpre[RB];
+  const bool rpre_ok = a.epi == EPI_RESID && nst == 1 && li == 0;
+  if (rpre_ok) {
+#pragma unroll
+    for (int r = 0; r < RB; r++) {
+      const int l = warp * rpw + sub + r * pass;
+      rpre[r] = l < hi - lo ? __ldcg(a.resid + lo + l) : 0.0f;
     }
   }
-  const float *scl_a = staged ? aux : a.A.scale + lo;
-  const int32_t *rsm_a = staged ? (const int32_t *)(aux + kSlabRowsMax) : a.A.rowsum + lo;
-  const float *scl_b = staged ? aux + 2 * kSlabRowsMax : a.B.scale + lo;
-  const int32_t *rsm_b = staged ? (const int32_t *)(aux + 3 * kSlabRowsMax) : a.B.rowsum + lo;
-  const bool nw_staged = a.mode != PRO_PLAIN && n <= kNormStageMax;
-  float *nw_s = aux + 4 * kSlabRowsMax;
-  if (nw_staged)
-    for (int i = threadIdx.x; i < n / 4; i += kThreads) cp_async16(nw_s + 4 * i, a.norm_w + 4 * i);
-  gemv_prologue(QT, 1, a.src, a.ld, a.src_tok ? c.sp->tok : nullptr, n, a.mode, nw_staged ? nw_s : a.norm_w,
-                !nw_staged, c.eps, smem);
-  const XIn x = gemv_inputs(n, smem);
+  const float *src = a.src + (a.src_tok ? (size_t)c.sp->tok[0] * a.ld : 0);
+  const float sx = xs_prologue(QT, src, n, a.mode, nw_staged ? nw_s : a.norm_w, !nw_staged, c.eps, smem);
+  const uint8_t *xq = (const uint8_t *)(smem + 320 + n);
   if (a.copy_src && blockIdx.x == 0) {
     // layer 0: the embedding row the prologue gathered becomes the residual
-    const float4 *s4 = (const float4 *)(a.src + (size_t)c.sp->tok[0] * a.ld);
+    const float4 *s4 = (const float4 *)src;
     float4 *d4 = (float4 *)a.copy_src;
     for (int i = threadIdx.x; i < a.ld / 4; i += kThreads) d4[i] = __ldg(s4 + i);
   }
   if (a.tslot && blockIdx.x == 0 && threadIdx.x == 0) a.tslot[1] = gtimer();
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int lpr = xs_lanes_per_row(CH, T::XMAX);
-  const int rpw = 32 / lpr, li = lane % lpr, sub = lane / lpr;
-  // this lane's activation chunks
+  // this lane's activation chunks, and the sum of all activations (each warp
+  // adds the n bytes itself)
   uint4 xr[T::XMAX][T::XW];
 #pragma unroll
   for (int j = 0; j < T::XMAX; j++) {
@@ -1012,14 +1228,22 @@ __device__ __noinline__ void phase_gemv_xs(const Ctx *cp, const GemvArgs *ap, fl
 #pragma unroll
     for (int t = 0; t < T::XW; t++) {
       if (k < CH) {
-        xr[j][t] = QT == QT_Q4 ? lds16(x.xq + (size_t)t * (n / 2) + 16 * k) : lds16(x.xq + 64 * k + 16 * t);
+        xr[j][t] = QT == QT_Q4 ? lds16(xq + (size_t)t * (n / 2) + 16 * k) : lds16(xq + 64 * k + 16 * t);
       } else {
         xr[j][t] = make_uint4(0, 0, 0, 0);
       }
     }
   }
-  const float sx = x.sx[0];
-  const int32_t corr = T::OFF * x.sumq[0];
+  uint32_t qsum = 0;
+  for (int i = lane; i < n / 16; i += 32) {
+    const uint4 v = lds16(xq + 16 * i);
+    qsum = __dp4a(v.x, 0x01010101u, qsum);
+    qsum = __dp4a(v.y, 0x01010101u, qsum);
+    qsum = __dp4a(v.z, 0x01010101u, qsum);
+    qsum = __dp4a(v.w, 0x01010101u, qsum);
+  }
+  for (int o = 16; o > 0; o >>= 1) qsum += __shfl_xor_sync(0xffffffffu, qsum, o);
+  const int32_t corr = T::OFF * (int32_t)qsum;
   bool in_place = false;
   if (a.epi == EPI_RESID) {
     if (a.resid_mode == RESID_ALWAYS) {
@@ -1036,12 +1260,11 @@ __device__ __noinline__ void phase_gemv_xs(const Ctx *cp, const GemvArgs *ap, fl
   }
   unsigned long long best = 0ull;
   bool ok = true;
-  const int pass = (kThreads / 32) * rpw;  // rows one pass of the block covers per RB slot
 #pragma unroll 1
   for (int st = 0; st < nst; st++) {
     const int r0 = lo + st * srows, nr = min(srows, hi - r0);
-    const uint8_t *buf = stage + (size_t)(st % kSt) * kStageBytes;
-    if (!mbar_wait(&full[st % kSt], (uint32_t)((st / kSt) & 1), c.err)) ok = false;
+    const uint8_t *buf = g.stage + (size_t)(st % g.kSt) * kStageBytes;
+    if (!gemv_wait(c, g, st)) ok = false;
 #pragma unroll 1
     for (int base = warp * rpw; ok && base < nr; base += pass * RB) {
       int lr[RB];
@@ -1072,7 +1295,8 @@ __device__ __noinline__ void phase_gemv_xs(const Ctx *cp, const GemvArgs *ap, fl
         if (a.epi == EPI_STORE) {
           a.out[row] = v;
         } else if (a.epi == EPI_RESID) {
-          const float t = __fadd_rn(__ldcg(a.resid + row), v);
+          // rpre holds the rows of the first pass (base == warp * rpw)
+          const float t = __fadd_rn(rpre_ok && base == warp * rpw ? rpre[r] : __ldcg(a.resid + row), v);
           a.vout[row] = t;
           if (in_place) a.resid[row] = t;
         } else if (a.epi == EPI_SWIGLU) {
@@ -1086,8 +1310,9 @@ __device__ __noinline__ void phase_gemv_xs(const Ctx *cp, const GemvArgs *ap, fl
       }
     }
     __syncthreads();  // stage buffer free
-    if (threadIdx.x == 0 && st + kSt < nst) issue(st + kSt);
+    gemv_retire(a, g, st);
   }
+  if (threadIdx.x == 0) s_ring_setup = 0;
   if (a.epi == EPI_ARGMAX) {
     for (int o = 16; o > 0; o >>= 1) {
       const unsigned long long t = __shfl_xor_sync(0xffffffffu, best, o);
@@ -1118,7 +1343,7 @@ __device__ __forceinline__ void phase_gemv_q(const Ctx *c, const GemvArgs *a, in
   if (M <= 1) {
     if constexpr (QT != QT_Q8) {
       if (xs_fits<QT>(a->A.pitch)) {
-        phase_gemv_xs<QT>(c, a, smem);
+        phase_gemv_xs<QT, 2>(c, a, smem);
         return;
       }
     }
@@ -1321,11 +1546,19 @@ __shared__ int s_kv_item;  // item whose pages are in flight / loaded, -1 none
 __shared__ float s_rope_cs[kMaxBatch][kHeadDim / 2], s_rope_sn[kMaxBatch][kHeadDim / 2];
 __shared__ int s_rope_ready;
 
-// Shared-memory layout of the attention phase (floats):
-//   K [32][D] | V [32][D] | q [G][D] | wt [G][32] | red [8][D] | scl [max_chunks]
+// Shared-memory layout of the attention phase (floats), from the base:
+//   q [G][D] | wt [G][32] | red [8][D] | scl [max_chunks]
+// and the K/V page buffers K [32][D] | V [32][D] (32 KB) in the last slot of
+// the GEMV stage ring, which the QKV phase before attention leaves unused.
 __host__ __device__ __forceinline__ size_t attn_smem_floats(int max_chunks) {
-  return (size_t)2 * kAttnChunk * kHeadDim + (size_t)kMaxGroup * kHeadDim + (size_t)kMaxGroup * kAttnChunk +
-         (size_t)8 * kHeadDim + (size_t)max_chunks;
+  return (size_t)kMaxGroup * kHeadDim + (size_t)kMaxGroup * kAttnChunk + (size_t)8 * kHeadDim + (size_t)max_chunks;
+}
+static_assert(2 * kAttnChunk * kHeadDim * 4 <= kStageBytes, "K/V buffers fit one ring slot");
+
+__device__ __forceinline__ float *attn_kv_buf(const Ctx &c, int M, float *smem) {
+  const int kSt = M <= 1 ? kStagesM1 : kStagesMB;
+  return (float *)((uint8_t *)smem + gemv_prologue_bytes(c.qtype, M <= 1 ? 1 : kMaxBatch, c.pro_cols) +
+                   (size_t)(kSt - 1) * kStageBytes);
 }
 
 // Called by every thread at the start of a launch that runs attention phases.
@@ -1340,23 +1573,30 @@ __device__ __forceinline__ void attn_block_init() {
   __syncthreads();
 }
 
-// Fills s_rope_cs / s_rope_sn for the step's sequences (all threads call;
-// positions are fixed for the whole launch).
-__device__ void attn_rope_tables(const Ctx &c) {
+// Named barrier among the threads lead .. kThreads-1 (lead a multiple of 32),
+// used by work the block does while thread 0 waits at the grid barrier.
+__device__ __forceinline__ void helpers_sync(int lead) {
+  asm volatile("bar.sync 1, %0;" ::"r"(kThreads - lead) : "memory");
+}
+
+// Fills s_rope_cs / s_rope_sn for the step's sequences (threads lead..; the
+// values become visible to the block at its next __syncthreads; positions are
+// fixed for the whole launch).
+__device__ void attn_rope_tables(const Ctx &c, int lead) {
   const StepParams &sp = *c.sp;
   const int half = c.D / 2;
-  for (int p = threadIdx.x; p < sp.M * half; p += kThreads) {
+  for (int p = threadIdx.x - lead; p < sp.M * half; p += kThreads - lead) {
     const int m = p / half, i = p % half;
     const int q = sp.pos[m][c.sec_axis[i]];
     s_rope_cs[m][i] = __ldg(c.rope_cos + (size_t)q * half + i);
     s_rope_sn[m][i] = __ldg(c.rope_sin + (size_t)q * half + i);
   }
-  __syncthreads();
-  if (threadIdx.x == 0) s_rope_ready = 1;
+  if ((int)threadIdx.x == lead) s_rope_ready = 1;
 }
 
 // Thread 0: bulk copies of item I's K and V page(s) into the K/V buffers.
-__device__ __forceinline__ void attn_issue_kv(const Ctx &c, int layer, const AttnItem &I, float *smem) {
+__device__ __forceinline__ void attn_issue_kv(const Ctx &c, int layer, const AttnItem &I, float *kvbuf) {
+  float *smem = kvbuf;
   const int *bt = c.sp->bt[I.m];
   const int p0 = I.t0 / kPageTokens;
   const int np = (I.cnt + kPageTokens - 1) / kPageTokens;
@@ -1372,14 +1612,21 @@ __device__ __forceinline__ void attn_issue_kv(const Ctx &c, int layer, const Att
   }
 }
 
-// Issues this block's first attention item's K/V loads ahead of the phase
-// (all threads call; the block's shared memory must be free of other use).
-__device__ void attn_prefetch(const Ctx &c, int layer, float *smem) {
+// Issues this block's first attention item's K/V loads ahead of the phase,
+// before the QKV phase of the layer, when that phase's stages leave the last
+// ring slot free.  Thread 0 acts.
+__device__ void attn_prefetch(const Ctx &c, int layer, float *smem, int lead) {
   AttnItem I;
-  if (threadIdx.x == 0 && s_kv_item < 0 && attn_item(c, *c.sp, blockIdx.x, I)) {
-    attn_issue_kv(c, layer, I, smem);
-    s_kv_item = blockIdx.x;
-  }
+  if ((int)threadIdx.x != lead || s_kv_item >= 0 || !attn_item(c, *c.sp, blockIdx.x, I)) return;
+  const int M = c.sp->M;
+  const int kSt = M <= 1 ? kStagesM1 : kStagesMB;
+  const DMat &A = c.layers[layer].qkv;
+  int lo, hi;
+  gemv_slab(0, A.rows, blockIdx.x, gridDim.x, lo, hi);
+  const int srows = kStageBytes / A.pitch;
+  if ((hi - lo + srows - 1) / srows > kSt - 1) return;
+  attn_issue_kv(c, layer, I, attn_kv_buf(c, M, smem));
+  s_kv_item = blockIdx.x;
 }
 
 // Waits for outstanding K/V loads (before the block leaves the kernel).
@@ -1397,9 +1644,9 @@ __device__ __noinline__ void phase_attn(const Ctx *cp, int layer, int append_onl
   const StepParams &sp = *c.sp;
   const int G = c.QH / c.KVH, D = c.D, D4 = D / 4, H4 = D / 8;
   const int qkvld = (c.QH + 2 * c.KVH) * D;
-  float *Ks = smem;                                // [32][D]
+  float *Ks = attn_kv_buf(c, sp.M, smem);         // [32][D]
   float *Vs = Ks + kAttnChunk * D;                 // [32][D]
-  float *qs = Vs + kAttnChunk * D;                 // [G][D]
+  float *qs = smem;                                // [G][D]
   float *wt = qs + kMaxGroup * D;                  // [G][32]
   float *red = wt + kMaxGroup * kAttnChunk;        // [8][D]
   float *scl = red + 8 * D;                        // [max_chunks]
@@ -1421,7 +1668,7 @@ __device__ __noinline__ void phase_attn(const Ctx *cp, int layer, int append_onl
     const float *qkv = c.qkv + (size_t)I.m * qkvld;
     // ---- K/V pages (unless prefetched for this item), RoPE table of the position
     if (threadIdx.x == 0 && s_kv_item != it) {
-      attn_issue_kv(c, layer, I, smem);
+      attn_issue_kv(c, layer, I, Ks);
       s_kv_item = it;
     }
     const bool rope_pre = s_rope_ready != 0;

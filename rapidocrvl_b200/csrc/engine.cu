@@ -106,95 +106,121 @@ __host__ __device__ __forceinline__ unsigned barriers_per_step(int L, int any_lo
   return any_logits ? (unsigned)(kLayerPhases * L) : (unsigned)(kLayerPhases * (L - 1) + 1);
 }
 
-// One phase of layer `layer`.  GEMV arguments are built by thread 0 in
-// shared memory.
+// GEMV arguments of a phase, built by thread 0 in shared memory.
+__shared__ GemvArgs s_args;
+
+__device__ void build_args(const Ctx &c, int phase, int layer, int any_logits, int do_embed, int feed, int tidx) {
+  GemvArgs &sa = s_args;
+  const LayerW &L = c.layers[layer < c.L ? layer : c.L - 1];
+  const bool last = layer == c.L - 1;
+  memset(&sa, 0, sizeof(sa));
+  sa.tslot = c.trace ? c.trace + 4 * tidx : nullptr;
+    switch (phase) {
+      case 0:  // QKV with the input RMSNorm (layer 0: embedding gather) as prologue
+        sa.A = L.qkv;
+        sa.row_begin = (last && !any_logits) ? c.QH * c.D : 0;
+        sa.row_end = L.qkv.rows;
+        sa.ld = c.H;
+        if (layer == 0 && do_embed) {
+          sa.src = c.embed;
+          sa.src_tok = 1;
+          sa.copy_src = c.h;
+        } else {
+          sa.src = c.h;
+        }
+        sa.mode = PRO_RMSNORM;
+        sa.norm_w = L.ln1;
+        sa.epi = EPI_STORE;
+        sa.out = c.qkv;
+        sa.ldo = (c.QH + 2 * c.KVH) * c.D;
+        break;
+      case 2:  // o projection + residual
+        sa.A = L.o;
+        sa.row_end = L.o.rows;
+        sa.src = c.head;
+        sa.ld = c.QH * c.D;
+        sa.mode = PRO_PLAIN;
+        sa.epi = EPI_RESID;
+        sa.ldo = c.H;
+        sa.resid = c.h;
+        sa.vout = c.vbuf;
+        sa.resid_mode = RESID_ATTN;
+        break;
+      case 3:  // gate/up with the post-attention AddRMSNorm as prologue
+        sa.A = L.gate;
+        sa.B = L.up;
+        sa.row_end = L.gate.rows;
+        sa.src = c.vbuf;
+        sa.ld = c.H;
+        sa.mode = PRO_ADDNORM;
+        sa.norm_w = L.ln2;
+        sa.epi = EPI_SWIGLU;
+        sa.out = c.g;
+        sa.ldo = c.I;
+        break;
+      case 4:  // down projection + residual (last layer: out-only)
+        sa.A = L.down;
+        sa.row_end = L.down.rows;
+        sa.src = c.g;
+        sa.ld = c.I;
+        sa.mode = PRO_PLAIN;
+        sa.epi = EPI_RESID;
+        sa.ldo = c.H;
+        sa.resid = c.h;
+        sa.vout = c.vbuf;
+        sa.resid_mode = last ? RESID_NEVER : RESID_ALWAYS;
+        break;
+      default:  // lm_head argmax with the final AddRMSNorm as prologue
+        sa.A = c.lm_head;
+        sa.row_end = c.lm_head.rows;
+        sa.src = c.vbuf;
+        sa.ld = c.H;
+        sa.mode = PRO_ADDNORM;
+        sa.norm_w = c.final_norm;
+        sa.epi = EPI_ARGMAX;
+        sa.ldo = c.V;
+        sa.argkey = c.argkey;
+        sa.logits = c.logits;
+        sa.argmax_finish = 1;
+        sa.feed = feed;
+        break;
+    }
+}
+
+__device__ __forceinline__ bool is_gemv_phase(int phase) { return phase != 1; }
+
+// Work for phase (phase, layer) that needs nothing from other blocks, done by
+// threads kHelper.. while thread 0 waits at the grid barrier before it: the
+// GEMV arguments, the first weight stages and the staged scales / norm
+// weights; before a QKV phase also the K/V pages of the block's attention
+// item.  The block's next __syncthreads publishes the results.
+constexpr int kHelper = 32;
+template <int QT>
+__device__ void prepare_phase(const Ctx &c, int phase, int layer, int M, int any_logits, int do_embed, int feed,
+                              float *smem, int tidx) {
+  if (!is_gemv_phase(phase)) return;
+  if (threadIdx.x == kHelper) build_args(c, phase, layer, any_logits, do_embed, feed, tidx);
+  helpers_sync(kHelper);
+  gemv_setup(QT, c, s_args, M, smem, kHelper, kThreads - kHelper);
+  if (phase == 0) attn_prefetch(c, layer, smem, kHelper);
+  if (threadIdx.x == kHelper) s_ring_setup = 1;
+}
+
+// One phase of layer `layer`; `prepared`: prepare_phase ran for it.
 template <int QT>
 __device__ void run_phase(const Ctx &c, int phase, int layer, int M, int any_logits, int do_embed, int feed,
-                          float *smem, int tidx, int coop) {
-  __shared__ GemvArgs sa;
+                          float *smem, int tidx, int coop, bool prepared) {
   unsigned long long *tslot = c.trace ? c.trace + 4 * tidx : nullptr;
   if (tslot && blockIdx.x == 0 && threadIdx.x == 0) tslot[0] = gtimer();
-  const LayerW &L = c.layers[layer < c.L ? layer : c.L - 1];
   const bool last = layer == c.L - 1;
   if (phase == 1) {
     phase_attn(&c, layer, last && !any_logits, coop, smem);
   } else {
-    if (threadIdx.x == 0) {
-      memset(&sa, 0, sizeof(sa));
-      sa.tslot = tslot;
-      switch (phase) {
-        case 0:  // QKV with the input RMSNorm (layer 0: embedding gather) as prologue
-          sa.A = L.qkv;
-          sa.row_begin = (last && !any_logits) ? c.QH * c.D : 0;
-          sa.row_end = L.qkv.rows;
-          sa.ld = c.H;
-          if (layer == 0 && do_embed) {
-            sa.src = c.embed;
-            sa.src_tok = 1;
-            sa.copy_src = c.h;
-          } else {
-            sa.src = c.h;
-          }
-          sa.mode = PRO_RMSNORM;
-          sa.norm_w = L.ln1;
-          sa.epi = EPI_STORE;
-          sa.out = c.qkv;
-          sa.ldo = (c.QH + 2 * c.KVH) * c.D;
-          break;
-        case 2:  // o projection + residual
-          sa.A = L.o;
-          sa.row_end = L.o.rows;
-          sa.src = c.head;
-          sa.ld = c.QH * c.D;
-          sa.mode = PRO_PLAIN;
-          sa.epi = EPI_RESID;
-          sa.ldo = c.H;
-          sa.resid = c.h;
-          sa.vout = c.vbuf;
-          sa.resid_mode = RESID_ATTN;
-          break;
-        case 3:  // gate/up with the post-attention AddRMSNorm as prologue
-          sa.A = L.gate;
-          sa.B = L.up;
-          sa.row_end = L.gate.rows;
-          sa.src = c.vbuf;
-          sa.ld = c.H;
-          sa.mode = PRO_ADDNORM;
-          sa.norm_w = L.ln2;
-          sa.epi = EPI_SWIGLU;
-          sa.out = c.g;
-          sa.ldo = c.I;
-          break;
-        case 4:  // down projection + residual (last layer: out-only)
-          sa.A = L.down;
-          sa.row_end = L.down.rows;
-          sa.src = c.g;
-          sa.ld = c.I;
-          sa.mode = PRO_PLAIN;
-          sa.epi = EPI_RESID;
-          sa.ldo = c.H;
-          sa.resid = c.h;
-          sa.vout = c.vbuf;
-          sa.resid_mode = last ? RESID_NEVER : RESID_ALWAYS;
-          break;
-        default:  // lm_head argmax with the final AddRMSNorm as prologue
-          sa.A = c.lm_head;
-          sa.row_end = c.lm_head.rows;
-          sa.src = c.vbuf;
-          sa.ld = c.H;
-          sa.mode = PRO_ADDNORM;
-          sa.norm_w = c.final_norm;
-          sa.epi = EPI_ARGMAX;
-          sa.ldo = c.V;
-          sa.argkey = c.argkey;
-          sa.logits = c.logits;
-          sa.argmax_finish = 1;
-          sa.feed = feed;
-          break;
-      }
+    if (!prepared) {
+      if (threadIdx.x == 0) build_args(c, phase, layer, any_logits, do_embed, feed, tidx);
+      __syncthreads();
     }
-    __syncthreads();
-    phase_gemv_q<QT>(&c, &sa, M, smem);
+    phase_gemv_q<QT>(&c, &s_args, M, smem);
   }
   if (tslot && threadIdx.x == 0) atomicMax(tslot + 2, gtimer());
 }
@@ -231,29 +257,38 @@ __global__ void __launch_bounds__(kThreads, 1)
   float *smem = (float *)smem4;
   OCRVL_CTX_TO_SMEM(cv);
   attn_block_init();
+  ring_init();
   unsigned k = 0;
   int t = 0;
+  if (threadIdx.x >= kHelper) prepare_phase<QT>(c, 0, 0, M, any_logits, do_embed, feed, smem, 0);
+  __syncthreads();
   for (int l = 0; l < c.L; l++) {
     const bool kv_only = l == c.L - 1 && !any_logits;
     for (int ph = 0; ph < kLayerPhases; ph++, t++) {
-      run_phase<QT>(c, ph, l, M, any_logits, do_embed, feed, smem, t, 1);
+      run_phase<QT>(c, ph, l, M, any_logits, do_embed, feed, smem, t, 1, is_gemv_phase(ph));
       if (kv_only && ph == 1) return;
       grid_arrive(c);
-      if (ph == 0) {
-        // work that needs nothing from other blocks, done while they finish:
-        // the attention item's K/V page copies, and (once per launch) the
-        // RoPE values of this step's positions
-        attn_prefetch(c, l, smem);
-        if (l == 0) attn_rope_tables(c);
+      // while thread 0 waits for the other blocks, the helper threads set up
+      // the next phase and (once per launch) the RoPE values of this step
+      if (threadIdx.x >= kHelper) {
+        const bool more = ph + 1 < kLayerPhases || l + 1 < c.L || any_logits;
+        if (more) {
+          const int nph = ph + 1 < kLayerPhases ? ph + 1 : (l + 1 < c.L ? 0 : kPhaseLM);
+          const int nl = ph + 1 < kLayerPhases ? l : l + 1;
+          if (!(nl == c.L - 1 && !any_logits && nph > 1))
+            prepare_phase<QT>(c, nph, nl, M, any_logits, do_embed, feed, smem, t + 1);
+        }
+        if (l == 0 && ph == 0) attn_rope_tables(c, kHelper);
       }
       if (!grid_wait(c, bar_base + (++k) * gridDim.x)) {
         attn_drain(c);
+        gemv_drain(c);
         return;
       }
       if (c.trace && blockIdx.x == 0 && threadIdx.x == 0) c.trace[4 * t + 3] = gtimer();
     }
   }
-  if (any_logits) run_phase<QT>(c, kPhaseLM, c.L, M, any_logits, do_embed, feed, smem, t, 1);
+  if (any_logits) run_phase<QT>(c, kPhaseLM, c.L, M, any_logits, do_embed, feed, smem, t, 1, true);
 }
 
 template <int QT>
@@ -265,13 +300,15 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (threadIdx.x == 0) cm.trace = nullptr;
   __syncthreads();
   attn_block_init();
-  run_phase<QT>(c, phase, layer, M, any_logits, do_embed, feed, (float *)smem4, 0, 0);
+  ring_init();
+  run_phase<QT>(c, phase, layer, M, any_logits, do_embed, feed, (float *)smem4, 0, 0, false);
 }
 
 template <int QT>
 __global__ void __launch_bounds__(kThreads) k_gemv(Ctx cv, GemvArgs av, int M) {
   extern __shared__ float4 smem4[];
   OCRVL_CTX_TO_SMEM(cv);
+  ring_init();
   __shared__ GemvArgs sa;
   if (threadIdx.x == 0) sa = av;
   __syncthreads();
