@@ -1175,7 +1175,7 @@ __device__ __forceinline__ uint32_t xs_row_dot(const uint8_t *w, const uint4 (*x
   return a0 + a1;
 }
 
-template <int QT, int RB>
+template <int QT, int RB, int EPI>
 __device__ __noinline__ void phase_gemv_xs(const Ctx *cp, const GemvArgs *ap, float *smem) {
   using T = XsTraits<QT>;
   const Ctx &c = *cp;
@@ -1185,7 +1185,7 @@ __device__ __noinline__ void phase_gemv_xs(const Ctx *cp, const GemvArgs *ap, fl
   const GemvGeo g = pre ? s_geo : gemv_geo(QT, c, a, 1, smem);
   const int P = g.P, n = a.A.cols, CH = QT == QT_Q4 ? P >> 4 : P / 48;
   const int lo = g.lo, hi = g.hi, srows = g.srows, nst = g.nst;
-  const bool two = g.two;
+  constexpr bool two = EPI == EPI_SWIGLU;
   float *aux = g.aux;
   const bool staged = g.staged;
   const float *scl_a = staged ? aux : a.A.scale + lo;
@@ -1201,7 +1201,7 @@ __device__ __noinline__ void phase_gemv_xs(const Ctx *cp, const GemvArgs *ap, fl
   // residual values of this lane's rows of a one-stage slab, fetched now so
   // their latency hides behind the prologue
   float rpre[RB];
-  const bool rpre_ok = a.epi == EPI_RESID && nst == 1 && li == 0;
+  const bool rpre_ok = EPI == EPI_RESID && nst == 1 && li == 0;
   if (rpre_ok) {
 #pragma unroll
     for (int r = 0; r < RB; r++) {
@@ -1245,7 +1245,7 @@ __device__ __noinline__ void phase_gemv_xs(const Ctx *cp, const GemvArgs *ap, fl
   for (int o = 16; o > 0; o >>= 1) qsum += __shfl_xor_sync(0xffffffffu, qsum, o);
   const int32_t corr = T::OFF * (int32_t)qsum;
   bool in_place = false;
-  if (a.epi == EPI_RESID) {
+  if (EPI == EPI_RESID) {
     if (a.resid_mode == RESID_ALWAYS) {
       in_place = true;
     } else if (a.resid_mode == RESID_MASK) {
@@ -1276,13 +1276,14 @@ __device__ __noinline__ void phase_gemv_xs(const Ctx *cp, const GemvArgs *ap, fl
         valid[r] = l < nr;
         lr[r] = valid[r] ? l : nr - 1;
         da[r] = xs_row_dot<QT>(buf + (size_t)lr[r] * P, xr, li, lpr, CH);
-        db[r] = two ? xs_row_dot<QT>(buf + (size_t)(srows + lr[r]) * P, xr, li, lpr, CH) : 0u;
+        if constexpr (two) db[r] = xs_row_dot<QT>(buf + (size_t)(srows + lr[r]) * P, xr, li, lpr, CH);
+        else db[r] = 0u;
       }
 #pragma unroll
       for (int r = 0; r < RB; r++) {
         for (int o = lpr >> 1; o > 0; o >>= 1) {
           da[r] += __shfl_xor_sync(0xffffffffu, da[r], o);
-          if (two) db[r] += __shfl_xor_sync(0xffffffffu, db[r], o);
+          if constexpr (two) db[r] += __shfl_xor_sync(0xffffffffu, db[r], o);
         }
       }
       if (li != 0) continue;
@@ -1292,14 +1293,14 @@ __device__ __noinline__ void phase_gemv_xs(const Ctx *cp, const GemvArgs *ap, fl
         const int i = r0 - lo + lr[r];
         const int row = r0 + lr[r];
         const float v = vnni_finalize((int32_t)da[r] - corr, rsm_a[i], sx, scl_a[i]);
-        if (a.epi == EPI_STORE) {
+        if constexpr (EPI == EPI_STORE) {
           a.out[row] = v;
-        } else if (a.epi == EPI_RESID) {
+        } else if constexpr (EPI == EPI_RESID) {
           // rpre holds the rows of the first pass (base == warp * rpw)
           const float t = __fadd_rn(rpre_ok && base == warp * rpw ? rpre[r] : __ldcg(a.resid + row), v);
           a.vout[row] = t;
           if (in_place) a.resid[row] = t;
-        } else if (a.epi == EPI_SWIGLU) {
+        } else if constexpr (EPI == EPI_SWIGLU) {
           const float u = vnni_finalize((int32_t)db[r] - corr, rsm_b[i], sx, scl_b[i]);
           a.out[row] = silu_mul(v, u);
         } else {
@@ -1313,7 +1314,7 @@ __device__ __noinline__ void phase_gemv_xs(const Ctx *cp, const GemvArgs *ap, fl
     gemv_retire(a, g, st);
   }
   if (threadIdx.x == 0) s_ring_setup = 0;
-  if (a.epi == EPI_ARGMAX) {
+  if constexpr (EPI == EPI_ARGMAX) {
     for (int o = 16; o > 0; o >>= 1) {
       const unsigned long long t = __shfl_xor_sync(0xffffffffu, best, o);
       best = t > best ? t : best;
@@ -1343,7 +1344,13 @@ __device__ __forceinline__ void phase_gemv_q(const Ctx *c, const GemvArgs *a, in
   if (M <= 1) {
     if constexpr (QT != QT_Q8) {
       if (xs_fits<QT>(a->A.pitch)) {
-        phase_gemv_xs<QT, 2>(c, a, smem);
+        // one instance per epilogue keeps each stage loop's code small
+        switch (a->epi) {
+          case EPI_STORE: phase_gemv_xs<QT, 2, EPI_STORE>(c, a, smem); break;
+          case EPI_RESID: phase_gemv_xs<QT, 2, EPI_RESID>(c, a, smem); break;
+          case EPI_SWIGLU: phase_gemv_xs<QT, 2, EPI_SWIGLU>(c, a, smem); break;
+          default: phase_gemv_xs<QT, 2, EPI_ARGMAX>(c, a, smem); break;
+        }
         return;
       }
     }
@@ -1820,9 +1827,11 @@ __device__ __noinline__ void phase_attn(const Ctx *cp, int layer, int append_onl
     // thread 0's fence and count); pick the merge work of this block
     __syncthreads();
     if (threadIdx.x == 0) {
-      __threadfence();
       unsigned *cnt = c.attn_count + 2 * (I.m * c.KVH + I.g);
-      const unsigned v = atomicAdd(cnt, 1u);
+      // release: the block's partials (ordered before by the barrier) become
+      // visible with the count; acquire: a merger sees the others' partials
+      unsigned v;
+      asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(v) : "l"(cnt) : "memory");
       const int nch = I.nch;
       int mh = -1;
       if (multi && nch >= G) {
@@ -1847,7 +1856,6 @@ __device__ __noinline__ void phase_attn(const Ctx *cp, int layer, int append_onl
         mh = G;  // all heads
         cnt[0] = 0u;
       }
-      if (mh >= 0) __threadfence();  // acquire side: the other blocks' partials
       merge_head = mh;
     }
     __syncthreads();
