@@ -111,9 +111,11 @@ int ocrvl_seq_len(const ocrvl_seq *s);
  * gathering through the sequence's block table. */
 int ocrvl_seq_read_kv(ocrvl_seq *s, int layer, float *k, float *v);
 
-/* One decode step for n sequences (1 <= n <= 8) of the same model: the
+/* One decode step for n sequences (1 <= n <= 64) of the same model: the
  * batched form of Runtime.forwardEmbeddingForSampling
- * (internal/model/model.go:3475-3643).
+ * (internal/model/model.go:3475-3643).  Every sequence is validated before
+ * any state changes; the step then runs as one kernel launch per group of up
+ * to 8 sequences.
  *   ids       n token ids (embedding rows), or NULL when embeds is given
  *   embeds    n*hidden_size f32 input embeddings, or NULL
  *   pos_thw   n*3 M-RoPE positions, or NULL for (len, len, len)
@@ -135,8 +137,9 @@ int ocrvl_generate_greedy(ocrvl_model *m, const int32_t *ids, int n_ids, int max
  * internal/model/model.go:1538-1568, without the per-token EOS check): the
  * step kernel writes each argmax id and advances its own parameters, so no
  * host round trip happens between tokens.  first_ids: the n ids to feed
- * first; out_ids: steps*n generated ids (step-major).  KV pages for all
- * steps are reserved before the first launch. */
+ * first; out_ids: steps*n generated ids (step-major), 1 <= n <= 64 (groups
+ * of up to 8 sequences run one after another).  KV pages for all steps are
+ * reserved before the first launch. */
 int ocrvl_decode_greedy_device(ocrvl_model *m, ocrvl_seq *const *seqs, int n, const int32_t *first_ids, int steps,
                                int32_t *out_ids);
 
@@ -145,7 +148,7 @@ int ocrvl_decode_greedy_device(ocrvl_model *m, ocrvl_seq *const *seqs, int n, co
 void *ocrvl_model_stream(ocrvl_model *m);
 
 /* Host<->device bytes one ocrvl_step call of n sequences moves besides
- * embeddings and logits (step parameters in, ids and status out). */
+ * embeddings and logits (step parameters in, ids and status out; 1 <= n <= 64). */
 int ocrvl_step_io_bytes(const ocrvl_model *m, int n, int64_t *h2d, int64_t *d2h);
 
 /* ---- op level: device pointers, optional cudaStream_t as void* --------

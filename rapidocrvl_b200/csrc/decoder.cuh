@@ -15,7 +15,8 @@
 
 namespace ocrvl {
 
-constexpr int kMaxBatch = 8;      // sequences per GEMV step
+constexpr int kMaxBatch = 8;      // sequences the register-batched GEMV and the single-step kernel take
+constexpr int kMaxSeqs = 64;      // sequences per decode step (the batched step kernel above kMaxBatch)
 constexpr int kThreads = 256;     // threads per block, every phase
 constexpr int kPageTokens = 16;   // tokens per KV page
 constexpr int kAttnChunk = 32;    // tokens per attention work item
@@ -41,16 +42,24 @@ struct LayerW {
   DMat o, gate, up, down;
 };
 
+// Per-sequence step record (32 bytes), so a step's parameters are a header
+// plus its n records and only those bytes cross to the device.
+struct SeqParams {
+  int tok;                 // input token id (embedding row)
+  int len;                 // cache length before this step's append
+  int pos[3];              // M-RoPE (T, H, W) position
+  int need;                // sequence needs logits / argmax
+  const int *bt;           // block table (page ids)
+};
 struct StepParams {
   int M;                   // sequences in this step
   int any_logits;          // some sequence needs lm_head this step
   int max_n;               // max over sequences of len+1
-  int tok[kMaxBatch];      // input token ids (embedding rows)
-  int len[kMaxBatch];      // cache length before this step's append
-  int pos[kMaxBatch][3];   // M-RoPE (T, H, W) position
-  int need[kMaxBatch];     // sequence needs logits / argmax
-  const int *bt[kMaxBatch];// block table (page ids) of each sequence
+  int pad;
+  SeqParams seq[kMaxSeqs];
 };
+__host__ __device__ __forceinline__ size_t step_params_bytes(int n) { return 16 + (size_t)n * sizeof(SeqParams); }
+static_assert(sizeof(SeqParams) == 32, "SeqParams is 32 bytes");
 
 struct Ctx {
   int qtype, H, I, L, QH, KVH, D, V;
@@ -65,8 +74,8 @@ struct Ctx {
   long long page_floats;
   // step work buffers
   float *h, *vbuf, *qkv, *head, *g, *logits;
-  float *part_o;                     // [B][QH][max_chunks][D] attention chunk sums
-  float *part_ml;                    // [B][QH][max_chunks][2] chunk max / sum
+  float *part_o;                     // [item][G][D] attention chunk sums (item = (sequence, kv head, chunk))
+  float *part_ml;                    // [item][G][2] chunk max / sum
   float *part_t;                     // [B][QH][D] raw-score tail sums
   unsigned long long *argkey;        // [B]
   int *tok_out;                      // [B] ids, then the error word
@@ -265,7 +274,7 @@ __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wai
 // The caller's cp.async copies (row scales, row sums, norm weights) are
 // complete and visible after the first barrier here.  Barriers: one after the
 // gather, one per reduction, one after the normalisation, one at the end.
-__device__ __noinline__ void gemv_prologue(int qt, int M, const float *src, int ld, const int *tok, int n,
+__device__ __noinline__ void gemv_prologue(int qt, int M, const float *src, int ld, const StepParams *tok, int n,
                                            int mode, const float *w, bool w_global, float eps, float *smem) {
   float *red = smem;
   float *sxs = smem + 304;
@@ -275,7 +284,7 @@ __device__ __noinline__ void gemv_prologue(int qt, int M, const float *src, int 
   const bool vnni = qt != QT_Q8;
 #pragma unroll 1
   for (int m = 0; m < M; m++) {
-    const float *s = src + (size_t)(tok ? tok[m] : m) * ld;
+    const float *s = src + (size_t)(tok ? tok->seq[m].tok : m) * ld;
     float *dst = vnni ? tmp : (float *)area + (size_t)m * n;
     g2s_f32(dst, s, n);
     cp_async_wait_all();
@@ -804,16 +813,16 @@ __device__ void argmax_finish(const Ctx &c, int M, int feed) {
   if (threadIdx.x < M) {
     const int m = threadIdx.x;
     unsigned long long k = __ldcg(c.argkey + m);
-    int id = sp.need[m] ? argmax_key_row(k) : -1;
+    int id = sp.seq[m].need ? argmax_key_row(k) : -1;
     c.tok_out[m] = id;
     c.argkey[m] = 0ull;
     if (feed) {
       int step = *c.hist_pos;
       c.hist[(size_t)step * M + m] = id;
-      int len = sp.len[m] + 1;
-      spw.tok[m] = id;
-      spw.len[m] = len;
-      spw.pos[m][0] = spw.pos[m][1] = spw.pos[m][2] = len;
+      int len = sp.seq[m].len + 1;
+      spw.seq[m].tok = id;
+      spw.seq[m].len = len;
+      spw.seq[m].pos[0] = spw.seq[m].pos[1] = spw.seq[m].pos[2] = len;
     }
   }
   __syncthreads();
@@ -845,13 +854,13 @@ __device__ __noinline__ void phase_gemv_t(const Ctx *cp, const GemvArgs *ap, int
   const int32_t *rsm_b = staged ? (const int32_t *)(aux + kAuxRsB) : a.B.rowsum + lo;
   const bool nw_staged = g.nw_staged;
   float *nw_s = aux + kAuxNw;
-  gemv_prologue(qt, M, a.src, a.ld, a.src_tok ? c.sp->tok : nullptr, a.A.cols, a.mode, nw_staged ? nw_s : a.norm_w,
+  gemv_prologue(qt, M, a.src, a.ld, a.src_tok ? c.sp : nullptr, a.A.cols, a.mode, nw_staged ? nw_s : a.norm_w,
                 !nw_staged, c.eps, smem);
   const XIn x = gemv_inputs(a.A.cols, smem);
   if (a.copy_src && blockIdx.x == 0) {
     // layer 0: the embedding rows the prologue gathered become the residual
     for (int m = 0; m < M; m++) {
-      const float4 *s4 = (const float4 *)(a.src + (size_t)c.sp->tok[m] * a.ld);
+      const float4 *s4 = (const float4 *)(a.src + (size_t)c.sp->seq[m].tok * a.ld);
       float4 *d4 = (float4 *)(a.copy_src + (size_t)m * a.ld);
       for (int i = threadIdx.x; i < a.ld / 4; i += kThreads) d4[i] = __ldg(s4 + i);
     }
@@ -875,7 +884,7 @@ __device__ __noinline__ void phase_gemv_t(const Ctx *cp, const GemvArgs *ap, int
         // only for caches of 2..6 tokens (matVecOutAddRMSNormCPU) and the
         // ...OutOnly form for the first token and longer caches
         // (model.go:3896-3908, 3975-3992, 4043-4062).
-        int len = c.sp->len[m];
+        int len = c.sp->seq[m].len;
         ip = qt == QT_Q8 || (len >= 1 && len + 1 <= 6);
       }
       in_place |= (ip ? 1 : 0) << m;
@@ -1209,7 +1218,7 @@ __device__ __noinline__ void phase_gemv_xs(const Ctx *cp, const GemvArgs *ap, fl
       rpre[r] = l < hi - lo ? __ldcg(a.resid + lo + l) : 0.0f;
     }
   }
-  const float *src = a.src + (a.src_tok ? (size_t)c.sp->tok[0] * a.ld : 0);
+  const float *src = a.src + (a.src_tok ? (size_t)c.sp->seq[0].tok * a.ld : 0);
   const float sx = xs_prologue(QT, src, n, a.mode, nw_staged ? nw_s : a.norm_w, !nw_staged, c.eps, smem);
   const uint8_t *xq = (const uint8_t *)(smem + 320 + n);
   if (a.copy_src && blockIdx.x == 0) {
@@ -1254,7 +1263,7 @@ __device__ __noinline__ void phase_gemv_xs(const Ctx *cp, const GemvArgs *ap, fl
       // Q4/Q6 use the in-place form only for caches of 2..6 tokens
       // (matVecOutAddRMSNormCPU), the ...OutOnly form otherwise
       // (model.go:3896-3908, 3975-3992, 4043-4062)
-      const int len = c.sp->len[0];
+      const int len = c.sp->seq[0].len;
       in_place = len >= 1 && len + 1 <= 6;
     }
   }
@@ -1514,7 +1523,7 @@ struct AttnItem {
 // Item `it` of the step; false when it is past the last item.
 __device__ __forceinline__ bool attn_item(const Ctx &c, const StepParams &sp, int it, AttnItem &I) {
   for (int m = 0; m < sp.M; m++) {
-    const int n = sp.len[m] + 1;
+    const int n = sp.seq[m].len + 1;
     const bool exact = n <= kAttnChunk;
     const int ct = exact ? kAttnChunk : kChunkTok;
     const int nch = (n + ct - 1) / ct;
@@ -1538,7 +1547,7 @@ __device__ __forceinline__ bool attn_item(const Ctx &c, const StepParams &sp, in
 __device__ __forceinline__ int attn_items_total(const Ctx &c, const StepParams &sp) {
   int total = 0;
   for (int m = 0; m < sp.M; m++) {
-    const int n = sp.len[m] + 1;
+    const int n = sp.seq[m].len + 1;
     const int ct = n <= kAttnChunk ? kAttnChunk : kChunkTok;
     total += c.KVH * ((n + ct - 1) / ct);
   }
@@ -1594,7 +1603,7 @@ __device__ void attn_rope_tables(const Ctx &c, int lead) {
   const int half = c.D / 2;
   for (int p = threadIdx.x - lead; p < sp.M * half; p += kThreads - lead) {
     const int m = p / half, i = p % half;
-    const int q = sp.pos[m][c.sec_axis[i]];
+    const int q = sp.seq[m].pos[c.sec_axis[i]];
     s_rope_cs[m][i] = __ldg(c.rope_cos + (size_t)q * half + i);
     s_rope_sn[m][i] = __ldg(c.rope_sin + (size_t)q * half + i);
   }
@@ -1604,7 +1613,7 @@ __device__ void attn_rope_tables(const Ctx &c, int lead) {
 // Thread 0: bulk copies of item I's K and V page(s) into the K/V buffers.
 __device__ __forceinline__ void attn_issue_kv(const Ctx &c, int layer, const AttnItem &I, float *kvbuf) {
   float *smem = kvbuf;
-  const int *bt = c.sp->bt[I.m];
+  const int *bt = c.sp->seq[I.m].bt;
   const int p0 = I.t0 / kPageTokens;
   const int np = (I.cnt + kPageTokens - 1) / kPageTokens;
   const uint32_t pbytes = (uint32_t)kPageTokens * c.D * 4;
@@ -1670,7 +1679,7 @@ __device__ __noinline__ void phase_attn(const Ctx *cp, int layer, int append_onl
     const int len = I.n - 1;
     const bool has_new = I.t0 <= len && len < I.t0 + I.cnt;
     if (append_only && !has_new) continue;
-    const int *pos = sp.pos[I.m];
+    const int *pos = sp.seq[I.m].pos;
     const bool has_rope = pos[0] != 0 || pos[1] != 0 || pos[2] != 0;
     const float *qkv = c.qkv + (size_t)I.m * qkvld;
     // ---- K/V pages (unless prefetched for this item), RoPE table of the position
@@ -1709,12 +1718,12 @@ __device__ __noinline__ void phase_attn(const Ctx *cp, int layer, int append_onl
         nk_a = __ldcg(kn + threadIdx.x);
         nk_b = __ldcg(kn + threadIdx.x + H4);
         if (has_rope) rope4(nk_a, nk_b, rcs + 4 * threadIdx.x, rsn + 4 * threadIdx.x);
-        float4 *kd = (float4 *)kv_ptr(c, sp.bt[I.m], layer, 0, I.g, len);
+        float4 *kd = (float4 *)kv_ptr(c, sp.seq[I.m].bt, layer, 0, I.g, len);
         kd[threadIdx.x] = nk_a;
         kd[threadIdx.x + H4] = nk_b;
       }
       nv4 = __ldcg((const float4 *)(qkv + (size_t)(c.QH + c.KVH + I.g) * D) + threadIdx.x);
-      ((float4 *)kv_ptr(c, sp.bt[I.m], layer, 1, I.g, len))[threadIdx.x] = nv4;
+      ((float4 *)kv_ptr(c, sp.seq[I.m].bt, layer, 1, I.g, len))[threadIdx.x] = nv4;
     }
     if (threadIdx.x == 0) {
       mbar_wait(&s_kv_bar, s_kv_parity, c.err);
@@ -1810,10 +1819,10 @@ __device__ __noinline__ void phase_attn(const Ctx *cp, int layer, int append_onl
         if (tail) {
           ((float4 *)(c.part_t + (hbase + hh) * D))[d4] = acc;
         } else {
-          ((float4 *)(c.part_o + ((hbase + hh) * c.max_chunks + I.ch) * D))[d4] = acc;
+          ((float4 *)(c.part_o + ((size_t)it * G + hh) * D))[d4] = acc;
         }
         if (d4 == 0) {
-          float *ml = c.part_ml + ((hbase + hh) * c.max_chunks + I.ch) * 2;
+          float *ml = c.part_ml + ((size_t)it * G + hh) * 2;
           ml[0] = mloc[hh];
           ml[1] = lloc[hh];
         }
@@ -1867,25 +1876,28 @@ __device__ __noinline__ void phase_attn(const Ctx *cp, int layer, int append_onl
 #pragma unroll 1
     for (int hh = h0; hh < h1; hh++) {
       const size_t hq = hbase + hh;
-      const float *ml = c.part_ml + hq * c.max_chunks * 2;
+      // chunk k of (m, g) is item it0 + k; stride G heads per item
+      const size_t it0 = (size_t)(it - I.ch);
+      const float *ml = c.part_ml + (it0 * G + hh) * 2;
       // this thread's first chunk partials, fetched while warp 0 works out
       // the chunk scales
       constexpr int kB = 4;
       const int grp = threadIdx.x >> 5, d4 = threadIdx.x & 31;
-      const float4 *po = (const float4 *)(c.part_o + hq * c.max_chunks * D) + d4;
+      const float4 *po = (const float4 *)(c.part_o + (it0 * G + hh) * D) + d4;
+      const size_t pstride = (size_t)G * D4;  // float4 per chunk
       float4 v[kB];
 #pragma unroll
       for (int u = 0; u < kB; u++)
-        if (grp + 8 * u < nfull && d4 < D4) v[u] = __ldcg(po + (size_t)(grp + 8 * u) * D4);
+        if (grp + 8 * u < nfull && d4 < D4) v[u] = __ldcg(po + (size_t)(grp + 8 * u) * pstride);
       if (warp == 0) {
         float mx = -INFINITY;
-        for (int k = lane; k < I.nch; k += 32) mx = fmaxf(mx, __ldcg(ml + 2 * k));
+        for (int k = lane; k < I.nch; k += 32) mx = fmaxf(mx, __ldcg(ml + 2 * G * k));
         for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
         float den = 0.0f;
         for (int k = lane; k < nfull; k += 32) {
-          const float sk = exp_fma(__fsub_rn(__ldcg(ml + 2 * k), mx));
+          const float sk = exp_fma(__fsub_rn(__ldcg(ml + 2 * G * k), mx));
           scl[k] = sk;
-          den = __fmaf_rn(sk, __ldcg(ml + 2 * k + 1), den);
+          den = __fmaf_rn(sk, __ldcg(ml + 2 * G * k + 1), den);
         }
         for (int o = 16; o > 0; o >>= 1) den = __fadd_rn(den, __shfl_xor_sync(0xffffffffu, den, o));
         if (lane == 0) dinv_s = __fdiv_rn(1.0f, den);
@@ -1899,7 +1911,7 @@ __device__ __noinline__ void phase_attn(const Ctx *cp, int layer, int append_onl
           if (k0 != grp) {
 #pragma unroll
             for (int u = 0; u < kB; u++)
-              if (k0 + 8 * u < nfull && d4 < D4) v[u] = __ldcg(po + (size_t)(k0 + 8 * u) * D4);
+              if (k0 + 8 * u < nfull && d4 < D4) v[u] = __ldcg(po + (size_t)(k0 + 8 * u) * pstride);
           }
 #pragma unroll
           for (int u = 0; u < kB; u++) {

@@ -387,7 +387,7 @@ struct ocrvl_model {
   // work
   Ctx ctx{};
   StepParams *sp_h = nullptr, *sp_d = nullptr;
-  int *out_h = nullptr;  // [kMaxBatch tokens][err]
+  int *out_h = nullptr;  // [kMaxSeqs tokens][err]
   int *bt_stage = nullptr;
   int grid = 0;
   size_t smem = 0;
@@ -528,9 +528,9 @@ void reset_after_timeout(ocrvl_model *m) {
   int zero = 0;
   cudaMemcpy(m->ctx.err, &zero, 4, cudaMemcpyHostToDevice);
   cudaMemset(m->ctx.bar_count, 0, 4);
-  cudaMemset(m->ctx.attn_count, 0, (size_t)2 * kMaxBatch * m->ctx.KVH * 4);
+  cudaMemset(m->ctx.attn_count, 0, (size_t)2 * kMaxSeqs * m->ctx.KVH * 4);
   cudaMemset(m->ctx.lm_count, 0, 4);
-  cudaMemset(m->ctx.argkey, 0, kMaxBatch * 8);
+  cudaMemset(m->ctx.argkey, 0, kMaxSeqs * 8);
   m->bar_base = 0;
 }
 
@@ -737,14 +737,18 @@ int ocrvl_finalize(ocrvl_model *m) {
   c.max_ctx = d.max_position;
   c.max_chunks = (c.max_ctx + kChunkTok - 1) / kChunkTok;
   int qkvld = (c.QH + 2 * c.KVH) * c.D;
-  size_t B = kMaxBatch;
+  size_t B = kMaxSeqs;
   c.h = m->dalloc<float>(B * c.H);
   c.vbuf = m->dalloc<float>(B * c.H);
   c.qkv = m->dalloc<float>(B * qkvld);
   c.head = m->dalloc<float>(B * c.QH * c.D);
   c.g = m->dalloc<float>(B * c.I);
-  c.part_o = m->dalloc<float>(B * c.QH * (size_t)c.max_chunks * c.D);
-  c.part_ml = m->dalloc<float>(B * c.QH * (size_t)c.max_chunks * 2);
+  // attention chunk partials, one slot per item: a step has at most one item
+  // per (kv head, KV page), i.e. kv_heads * pages of the pool
+  const size_t max_items = (size_t)c.KVH * m->num_pages + (size_t)2 * kMaxSeqs * c.KVH;
+  const size_t G = (size_t)(c.QH / c.KVH);
+  c.part_o = m->dalloc<float>(max_items * G * c.D);
+  c.part_ml = m->dalloc<float>(max_items * G * 2);
   c.part_t = m->dalloc<float>(B * c.QH * (size_t)c.D);
   c.logits = m->dalloc<float>(B * (size_t)c.V);
   c.argkey = m->dalloc<unsigned long long>(B);
@@ -877,38 +881,31 @@ int ocrvl_seq_read_kv(ocrvl_seq *s, int layer, float *k, float *v) {
   return s->len;
 }
 
-int ocrvl_step(ocrvl_model *m, ocrvl_seq *const *seqs, int n, const int32_t *ids, const float *embeds,
+}  // extern "C"
+
+namespace {
+
+// One launch of the step kernel for n <= kMaxBatch sequences that ocrvl_step
+// has validated (model lock held): page allocation, parameter upload,
+// launch, results.
+int step_group(ocrvl_model *m, ocrvl_seq *const *seqs, int n, const int32_t *ids, const float *embeds,
                const int32_t *pos_thw, int need_logits, int32_t *out_ids, float *out_logits) {
-  if (!m || !seqs) return fail(OCRVL_E_INVALID, "null argument");
-  if (n < 1 || n > kMaxBatch) return fail(OCRVL_E_INVALID, "batch must be 1..8 sequences");
-  if (!ids && !embeds) return fail(OCRVL_E_INVALID, "ids or embeds required");
-  std::lock_guard<std::mutex> lk(m->mu);
-  if (!m->finalized) return fail(OCRVL_E_INVALID, "model not finalized");
-  if (int rc = set_device(m)) return rc;
   const ocrvl_model_desc &d = m->desc;
   StepParams &sp = *m->sp_h;
-  memset(&sp, 0, sizeof(sp));
   sp.M = n;
   sp.any_logits = need_logits ? 1 : 0;
+  sp.pad = 0;
   int max_n = 0;
   for (int i = 0; i < n; i++) {
     ocrvl_seq *s = seqs[i];
-    if (!s || s->m != m) return fail(OCRVL_E_INVALID, "sequence belongs to another model");
-    for (int j = 0; j < i; j++)
-      if (seqs[j] == s) return fail(OCRVL_E_INVALID, "sequence repeated in one step");
-    if (s->len >= s->max_tokens) return fail(OCRVL_E_INVALID, "sequence is full (max_tokens reached)");
-    if (ids && (ids[i] < 0 || ids[i] >= d.vocab_size))
-      return fail(OCRVL_E_INVALID, "token id " + std::to_string(ids ? ids[i] : 0) + " outside vocab");
     int p[3] = {s->len, s->len, s->len};
     if (pos_thw)
       for (int a = 0; a < 3; a++) p[a] = pos_thw[3 * i + a];
-    for (int a = 0; a < 3; a++)
-      if (p[a] < 0 || p[a] >= d.max_position) return fail(OCRVL_E_INVALID, "position outside RoPE table");
-    sp.tok[i] = ids ? ids[i] : 0;
-    sp.len[i] = s->len;
-    for (int a = 0; a < 3; a++) sp.pos[i][a] = p[a];
-    sp.need[i] = need_logits ? 1 : 0;
-    sp.bt[i] = s->bt_d;
+    sp.seq[i].tok = ids ? ids[i] : 0;
+    sp.seq[i].len = s->len;
+    for (int a = 0; a < 3; a++) sp.seq[i].pos[a] = p[a];
+    sp.seq[i].need = need_logits ? 1 : 0;
+    sp.seq[i].bt = s->bt_d;
     max_n = std::max(max_n, s->len + 1);
   }
   sp.max_n = max_n;
@@ -924,14 +921,15 @@ int ocrvl_step(ocrvl_model *m, ocrvl_seq *const *seqs, int n, const int32_t *ids
       CK(cudaMemcpyAsync(s->bt_d + s->len / kPageTokens, &m->bt_stage[i], 4, cudaMemcpyHostToDevice, m->stream));
     }
   }
-  CK(cudaMemcpyAsync(m->sp_d, &sp, sizeof(StepParams), cudaMemcpyHostToDevice, m->stream));
+  CK(cudaMemcpyAsync(m->sp_d, &sp, step_params_bytes(n), cudaMemcpyHostToDevice, m->stream));
   if (embeds) CK(cudaMemcpyAsync(m->ctx.h, embeds, (size_t)n * d.hidden_size * 4, cudaMemcpyHostToDevice, m->stream));
   if (int rc = launch_step(m, n, sp.any_logits, embeds ? 0 : 1)) return rc;
-  CK(cudaMemcpyAsync(m->out_h, m->ctx.tok_out, (kMaxBatch + 1) * 4, cudaMemcpyDeviceToHost, m->stream));
+  CK(cudaMemcpyAsync(m->out_h, m->ctx.tok_out, (size_t)n * 4, cudaMemcpyDeviceToHost, m->stream));
+  CK(cudaMemcpyAsync(m->out_h + kMaxSeqs, m->ctx.err, 4, cudaMemcpyDeviceToHost, m->stream));
   if (out_logits && need_logits)
     CK(cudaMemcpyAsync(out_logits, m->ctx.logits, (size_t)n * d.vocab_size * 4, cudaMemcpyDeviceToHost, m->stream));
   CK(cudaStreamSynchronize(m->stream));
-  if (m->out_h[kMaxBatch]) {
+  if (m->out_h[kMaxSeqs]) {
     reset_after_timeout(m);
     return fail(OCRVL_E_TIMEOUT, "device grid barrier timed out");
   }
@@ -942,26 +940,69 @@ int ocrvl_step(ocrvl_model *m, ocrvl_seq *const *seqs, int n, const int32_t *ids
   return OCRVL_OK;
 }
 
-void *ocrvl_model_stream(ocrvl_model *m) { return m ? (void *)m->stream : nullptr; }
+}  // namespace
 
-int ocrvl_step_io_bytes(const ocrvl_model *m, int n, int64_t *h2d, int64_t *d2h) {
-  if (!m || !h2d || !d2h || n < 1 || n > kMaxBatch) return fail(OCRVL_E_INVALID, "bad arguments");
-  *h2d = (int64_t)sizeof(StepParams);               // step parameters (ids, lengths, positions)
-  *d2h = (int64_t)(kMaxBatch + 1) * 4;              // ids + error word
-  return OCRVL_OK;
-}
+extern "C" {
 
-int ocrvl_decode_greedy_device(ocrvl_model *m, ocrvl_seq *const *seqs, int n, const int32_t *first_ids, int steps,
-                               int32_t *out_ids) {
-  if (!m || !seqs || !first_ids || !out_ids) return fail(OCRVL_E_INVALID, "null argument");
-  if (n < 1 || n > kMaxBatch || steps < 1) return fail(OCRVL_E_INVALID, "batch must be 1..8, steps >= 1");
+int ocrvl_step(ocrvl_model *m, ocrvl_seq *const *seqs, int n, const int32_t *ids, const float *embeds,
+               const int32_t *pos_thw, int need_logits, int32_t *out_ids, float *out_logits) {
+  if (!m || !seqs) return fail(OCRVL_E_INVALID, "null argument");
+  if (n < 1 || n > kMaxSeqs) return fail(OCRVL_E_INVALID, "batch must be 1..64 sequences");
+  if (!ids && !embeds) return fail(OCRVL_E_INVALID, "ids or embeds required");
   std::lock_guard<std::mutex> lk(m->mu);
   if (!m->finalized) return fail(OCRVL_E_INVALID, "model not finalized");
   if (int rc = set_device(m)) return rc;
   const ocrvl_model_desc &d = m->desc;
+  // validate every sequence before any state changes
+  size_t new_pages = 0;
+  for (int i = 0; i < n; i++) {
+    ocrvl_seq *s = seqs[i];
+    if (!s || s->m != m) return fail(OCRVL_E_INVALID, "sequence belongs to another model");
+    for (int j = 0; j < i; j++)
+      if (seqs[j] == s) return fail(OCRVL_E_INVALID, "sequence repeated in one step");
+    if (s->len >= s->max_tokens) return fail(OCRVL_E_INVALID, "sequence is full (max_tokens reached)");
+    if (ids && (ids[i] < 0 || ids[i] >= d.vocab_size))
+      return fail(OCRVL_E_INVALID, "token id " + std::to_string(ids ? ids[i] : 0) + " outside vocab");
+    if (pos_thw)
+      for (int a = 0; a < 3; a++)
+        if (pos_thw[3 * i + a] < 0 || pos_thw[3 * i + a] >= d.max_position)
+          return fail(OCRVL_E_INVALID, "position outside RoPE table");
+    if (!pos_thw && s->len >= d.max_position) return fail(OCRVL_E_INVALID, "position outside RoPE table");
+    if (s->len % kPageTokens == 0 && (int)s->pages.size() <= s->len / kPageTokens) new_pages++;
+  }
+  if (new_pages > m->free_pages.size()) return fail(OCRVL_E_NOMEM, "KV page pool exhausted");
+  // groups of kMaxBatch sequences, one launch each
+  for (int g0 = 0; g0 < n; g0 += kMaxBatch) {
+    const int gn = std::min(kMaxBatch, n - g0);
+    int rc = step_group(m, seqs + g0, gn, ids ? ids + g0 : nullptr, embeds ? embeds + (size_t)g0 * d.hidden_size : nullptr,
+                        pos_thw ? pos_thw + 3 * g0 : nullptr, need_logits, out_ids ? out_ids + g0 : nullptr,
+                        out_logits ? out_logits + (size_t)g0 * d.vocab_size : nullptr);
+    if (rc) return rc;
+  }
+  return OCRVL_OK;
+}
+
+void *ocrvl_model_stream(ocrvl_model *m) { return m ? (void *)m->stream : nullptr; }
+
+int ocrvl_step_io_bytes(const ocrvl_model *m, int n, int64_t *h2d, int64_t *d2h) {
+  if (!m || !h2d || !d2h || n < 1 || n > kMaxSeqs) return fail(OCRVL_E_INVALID, "bad arguments");
+  const int groups = (n + kMaxBatch - 1) / kMaxBatch;
+  *h2d = (int64_t)(step_params_bytes(kMaxBatch) * (groups - 1) + step_params_bytes(n - (groups - 1) * kMaxBatch));
+  *d2h = (int64_t)n * 4 + 4 * groups;  // ids + error word per launch
+  return OCRVL_OK;
+}
+
+}  // extern "C"
+
+namespace {
+
+// The device-fed loop for n <= kMaxBatch sequences (model lock held).
+int decode_group(ocrvl_model *m, ocrvl_seq *const *seqs, int n, const int32_t *first_ids, int steps,
+                 int32_t *out_ids) {
+  const ocrvl_model_desc &d = m->desc;
   StepParams &sp = *m->sp_h;
-  memset(&sp, 0, sizeof(sp));
   sp.M = n;
+  sp.pad = 0;
   sp.any_logits = 1;
   int max_n = 0;
   for (int i = 0; i < n; i++) {
@@ -972,11 +1013,11 @@ int ocrvl_decode_greedy_device(ocrvl_model *m, ocrvl_seq *const *seqs, int n, co
     if (s->len + steps > s->max_tokens) return fail(OCRVL_E_INVALID, "steps exceed the sequence's max_tokens");
     if (s->len + steps > d.max_position) return fail(OCRVL_E_INVALID, "positions exceed the RoPE table");
     if (first_ids[i] < 0 || first_ids[i] >= d.vocab_size) return fail(OCRVL_E_INVALID, "token id outside vocab");
-    sp.tok[i] = first_ids[i];
-    sp.len[i] = s->len;
-    sp.pos[i][0] = sp.pos[i][1] = sp.pos[i][2] = s->len;
-    sp.need[i] = 1;
-    sp.bt[i] = s->bt_d;
+    sp.seq[i].tok = first_ids[i];
+    sp.seq[i].len = s->len;
+    sp.seq[i].pos[0] = sp.seq[i].pos[1] = sp.seq[i].pos[2] = s->len;
+    sp.seq[i].need = 1;
+    sp.seq[i].bt = s->bt_d;
     max_n = std::max(max_n, s->len + 1);
   }
   sp.max_n = max_n;
@@ -1030,22 +1071,56 @@ int ocrvl_decode_greedy_device(ocrvl_model *m, ocrvl_seq *const *seqs, int n, co
   int *hist = m->hist_d;
   m->ctx.hist = hist;
   CK(cudaMemsetAsync(m->ctx.hist_pos, 0, 4, m->stream));
-  CK(cudaMemcpyAsync(m->sp_d, &sp, sizeof(StepParams), cudaMemcpyHostToDevice, m->stream));
+  CK(cudaMemcpyAsync(m->sp_d, &sp, step_params_bytes(n), cudaMemcpyHostToDevice, m->stream));
   int rc = OCRVL_OK;
   for (int st = 0; st < steps && rc == OCRVL_OK; st++) rc = launch_step(m, n, 1, 1, 1);
   m->ctx.hist = nullptr;
   if (rc == OCRVL_OK) {
     cudaError_t e1 = cudaMemcpyAsync(out_ids, hist, (size_t)steps * n * 4, cudaMemcpyDeviceToHost, m->stream);
-    cudaError_t e2 = cudaMemcpyAsync(m->out_h, m->ctx.tok_out, (kMaxBatch + 1) * 4, cudaMemcpyDeviceToHost, m->stream);
+    cudaError_t e2 = cudaMemcpyAsync(m->out_h + kMaxSeqs, m->ctx.err, 4, cudaMemcpyDeviceToHost, m->stream);
     if (e1 != cudaSuccess || e2 != cudaSuccess) rc = fail(OCRVL_E_CUDA, "copy of decoded ids failed");
   }
   CK(cudaStreamSynchronize(m->stream));
   if (rc) return rc;
-  if (m->out_h[kMaxBatch]) {
+  if (m->out_h[kMaxSeqs]) {
     reset_after_timeout(m);
     return fail(OCRVL_E_TIMEOUT, "device grid barrier timed out");
   }
   for (int i = 0; i < n; i++) seqs[i]->len += steps;
+  return OCRVL_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int ocrvl_decode_greedy_device(ocrvl_model *m, ocrvl_seq *const *seqs, int n, const int32_t *first_ids, int steps,
+                               int32_t *out_ids) {
+  if (!m || !seqs || !first_ids || !out_ids) return fail(OCRVL_E_INVALID, "null argument");
+  if (n < 1 || n > kMaxSeqs || steps < 1) return fail(OCRVL_E_INVALID, "batch must be 1..64, steps >= 1");
+  std::lock_guard<std::mutex> lk(m->mu);
+  if (!m->finalized) return fail(OCRVL_E_INVALID, "model not finalized");
+  if (int rc = set_device(m)) return rc;
+  if (n <= kMaxBatch) return decode_group(m, seqs, n, first_ids, steps, out_ids);
+  // groups of kMaxBatch sequences run one after another; pages for all of
+  // them are checked first so that no group starts when a later one cannot
+  size_t new_pages = 0;
+  for (int i = 0; i < n; i++) {
+    const ocrvl_seq *s = seqs[i];
+    if (!s || s->m != m) return fail(OCRVL_E_INVALID, "sequence belongs to another model");
+    for (int j = 0; j < i; j++)
+      if (seqs[j] == s) return fail(OCRVL_E_INVALID, "sequence repeated in one step");
+    int need_pages = (s->len + steps + kPageTokens - 1) / kPageTokens;
+    new_pages += (size_t)std::max(0, need_pages - (int)s->pages.size());
+  }
+  if (new_pages > m->free_pages.size()) return fail(OCRVL_E_NOMEM, "KV page pool exhausted");
+  std::vector<int32_t> part((size_t)steps * kMaxBatch);
+  for (int g0 = 0; g0 < n; g0 += kMaxBatch) {
+    const int gn = std::min(kMaxBatch, n - g0);
+    if (int rc = decode_group(m, seqs + g0, gn, first_ids + g0, steps, part.data())) return rc;
+    for (int st = 0; st < steps; st++)
+      for (int i = 0; i < gn; i++) out_ids[(size_t)st * n + g0 + i] = part[(size_t)st * gn + i];
+  }
   return OCRVL_OK;
 }
 

@@ -118,6 +118,39 @@ def test_batched_step_equals_single(tiny_models):
             assert np.array_equal(x, y)
 
 
+@pytest.mark.parametrize("q", ["q4", "q8"])
+def test_many_sequences_step_equals_single(tiny_models, q):
+    """A step over more sequences than one launch takes (20 here, 64 at most)
+    gives each sequence the same ids and logits, bit for bit, as stepping it
+    alone; the device-fed loop over 12 sequences matches too."""
+    _need_gpu()
+    cfg, rt, _ = _pair(tiny_models[q], q)
+    n = 20
+    prompts = [synth.random_prompt(4 + (j % 5), cfg.vocab_size, 100 + j) for j in range(n)]
+    seq_a = [rt.new_sequence(48) for _ in range(n)]
+    seq_b = [rt.new_sequence(48) for _ in range(n)]
+    # prefill each sequence alone (different lengths), then one joint step
+    last = []
+    for j in range(n):
+        for t in prompts[j][:-1]:
+            rt.step([seq_a[j]], ids=[t], need_logits=False)
+            rt.step([seq_b[j]], ids=[t], need_logits=False)
+        last.append(prompts[j][-1])
+    ids_joint, logits_joint = rt.step(seq_a, ids=last, return_logits=True)
+    for j in range(n):
+        ids1, logits1 = rt.step([seq_b[j]], ids=[last[j]], return_logits=True)
+        assert int(ids1[0]) == int(ids_joint[j])
+        assert np.array_equal(logits1[0], logits_joint[j])
+    # device-fed loop, 12 sequences at once vs one at a time
+    first = [int(i) for i in ids_joint[:12]]
+    dev_joint = rt.decode_device(seq_a[:12], first, 5)
+    for j in range(12):
+        dev1 = rt.decode_device([seq_b[j]], [first[j]], 5)
+        assert dev1[:, 0].tolist() == dev_joint[:, j].tolist()
+    with pytest.raises(Exception):
+        rt.step([rt.new_sequence(4) for _ in range(65)], ids=[1] * 65)
+
+
 def test_embeds_and_mrope_positions(tiny_models):
     """Embedding input and distinct (T,H,W) positions (image-token prefill)."""
     _need_gpu()
