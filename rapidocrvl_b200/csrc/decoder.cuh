@@ -1678,6 +1678,14 @@ __device__ __noinline__ void phase_attn(const Ctx *cp, int layer, int append_onl
     attn_item(c, sp, it, I);
     const int len = I.n - 1;
     const bool has_new = I.t0 <= len && len < I.t0 + I.cnt;
+    // one K/V copy in flight at a time: a copy started for another item (the
+    // one prefetched before the phase, when that item is skipped below or the
+    // block moves past it) completes before the buffers are reused
+    if (threadIdx.x == 0 && s_kv_item >= 0 && (s_kv_item != it || (append_only && !has_new))) {
+      mbar_wait(&s_kv_bar, s_kv_parity, c.err);
+      s_kv_parity ^= 1u;
+      s_kv_item = -1;
+    }
     if (append_only && !has_new) continue;
     const int *pos = sp.seq[I.m].pos;
     const bool has_rope = pos[0] != 0 || pos[1] != 0 || pos[2] != 0;

@@ -17,8 +17,11 @@
 #include <string>
 #include <vector>
 
+#include <cuda.h>
+
 #include "../../include/ocrvl_cuda.h"
 #include "decoder.cuh"
+#include "batched.cuh"
 
 using namespace ocrvl;
 
@@ -332,6 +335,146 @@ __global__ void k_argmax_ids(const unsigned long long *keys, int M, int *ids) {
   if (m < M) ids[m] = argmax_key_row(keys[m]);
 }
 
+// ---------------------------------------------------------------------------
+// Batched step kernel (kMaxBatch < M <= kMaxSeqs, Q4 / Q6): per layer the
+// input quantisation and tcgen05 int8 GEMM for QKV, o, gate/up and down, the
+// attention phase between QKV and o; grid barrier after each phase.
+// ---------------------------------------------------------------------------
+__host__ __device__ __forceinline__ int gemm_nt(int rows, int grid) {
+  const int per = (rows + grid - 1) / grid;
+  const int nt = (per + 15) & ~15;
+  return nt < 256 ? nt : 256;  // kMaxNT
+}
+__host__ __device__ __forceinline__ unsigned barriers_per_step_b(int L, int any_logits) {
+  return any_logits ? (unsigned)(9 * L + 1) : (unsigned)(9 * (L - 1) + 2);
+}
+
+template <int QT>
+__device__ void step_b_body(const Ctx &c, const BatchedW *bw, uint32_t tmem, int any_logits, int do_embed, int feed,
+                            unsigned bar_base, float *smem) {
+  __shared__ GemmArgs sg;
+  unsigned k = 0;
+  auto sync = [&]() { return grid_sync(c, bar_base + (++k) * gridDim.x); };
+  auto gemm = [&](const GemmArgs &g) {
+    if (threadIdx.x == 0) sg = g;
+    __syncthreads();
+    phase_gemm_b<QT>(&c, bw, &sg, tmem, smem);
+  };
+  const int qkvld = (c.QH + 2 * c.KVH) * c.D;
+  for (int l = 0; l < c.L; l++) {
+    const LayerW &L = c.layers[l];
+    const bool last = l == c.L - 1, kv_only = last && !any_logits, emb = l == 0 && do_embed;
+    phase_quant_b(&c, bw, emb ? c.embed : c.h, c.H, emb, c.H, PRO_RMSNORM, L.ln1, emb ? c.h : nullptr, smem);
+    if (!sync()) return;
+    {
+      GemmArgs g{};
+      g.mapA = bw_map(*bw, l, 0);
+      g.A = L.qkv;
+      g.row_begin = kv_only ? c.QH * c.D : 0;
+      g.row_end = L.qkv.rows;
+      g.K = c.H;
+      g.nt = gemm_nt(L.qkv.rows, gridDim.x);
+      g.epi = EPI_STORE;
+      g.out = c.qkv;
+      g.ldo = qkvld;
+      gemm(g);
+    }
+    if (!sync()) return;
+    phase_attn(&c, l, kv_only, 1, smem);
+    if (kv_only) return;
+    if (!sync()) return;
+    phase_quant_b(&c, bw, c.head, c.QH * c.D, 0, c.QH * c.D, PRO_PLAIN, nullptr, nullptr, smem);
+    if (!sync()) return;
+    {
+      GemmArgs g{};
+      g.mapA = bw_map(*bw, l, 1);
+      g.A = L.o;
+      g.row_end = L.o.rows;
+      g.K = c.QH * c.D;
+      g.nt = gemm_nt(L.o.rows, gridDim.x);
+      g.epi = EPI_RESID;
+      g.ldo = c.H;
+      g.resid = c.h;
+      g.vout = c.vbuf;
+      g.resid_mode = RESID_ATTN;
+      gemm(g);
+    }
+    if (!sync()) return;
+    phase_quant_b(&c, bw, c.vbuf, c.H, 0, c.H, PRO_ADDNORM, L.ln2, nullptr, smem);
+    if (!sync()) return;
+    {
+      GemmArgs g{};
+      g.mapA = bw_map(*bw, l, 2);
+      g.mapB = bw_map(*bw, l, 3);
+      g.A = L.gate;
+      g.B = L.up;
+      g.row_end = L.gate.rows;
+      g.K = c.H;
+      g.nt = gemm_nt(L.gate.rows, gridDim.x);
+      g.epi = EPI_SWIGLU;
+      g.out = c.g;
+      g.ldo = c.I;
+      gemm(g);
+    }
+    if (!sync()) return;
+    phase_quant_b(&c, bw, c.g, c.I, 0, c.I, PRO_PLAIN, nullptr, nullptr, smem);
+    if (!sync()) return;
+    {
+      GemmArgs g{};
+      g.mapA = bw_map(*bw, l, 4);
+      g.A = L.down;
+      g.row_end = L.down.rows;
+      g.K = c.I;
+      g.nt = gemm_nt(L.down.rows, gridDim.x);
+      g.epi = EPI_RESID;
+      g.ldo = c.H;
+      g.resid = c.h;
+      g.vout = c.vbuf;
+      g.resid_mode = last ? RESID_NEVER : RESID_ALWAYS;
+      gemm(g);
+    }
+    if (!sync()) return;
+  }
+  phase_quant_b(&c, bw, c.vbuf, c.H, 0, c.H, PRO_ADDNORM, c.final_norm, nullptr, smem);
+  if (!sync()) return;
+  GemmArgs g{};
+  g.mapA = bw_map(*bw, c.L, 0);
+  g.A = c.lm_head;
+  g.row_end = c.lm_head.rows;
+  g.K = c.H;
+  g.nt = gemm_nt(c.lm_head.rows, gridDim.x);
+  g.epi = EPI_ARGMAX;
+  g.ldo = c.V;
+  g.argkey = c.argkey;
+  g.logits = c.logits;
+  g.argmax_finish = 1;
+  g.feed = feed;
+  gemm(g);
+}
+
+template <int QT>
+__global__ void __launch_bounds__(kThreads, 1)
+    k_step_b(Ctx cv, BatchedW bwv, int any_logits, int do_embed, int feed, unsigned bar_base) {
+  extern __shared__ float4 smem4[];
+  float *smem = (float *)smem4;
+  OCRVL_CTX_TO_SMEM(cv);
+  __shared__ BatchedW sbw;
+  __shared__ uint32_t s_tmem;
+  if (threadIdx.x == 0) sbw = bwv;
+  attn_block_init();
+  ring_init();
+  if (threadIdx.x < 32) tmem_alloc(&s_tmem, kTmemCols);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  step_b_body<QT>(c, &sbw, s_tmem, any_logits, do_embed, feed, bar_base, smem);
+  // every exit path: no TMEM held when the block leaves
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (threadIdx.x < 32) tmem_dealloc(s_tmem, kTmemCols);
+}
+
 // Per-row sum of unpacked int8 weights; one warp per row.
 __global__ void k_rowsum(int type, const uint8_t *w, int rows, int cols, int pitch, int32_t *out) {
   int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
@@ -400,6 +543,10 @@ struct ocrvl_model {
   size_t hist_cap = 0;
   int *pin_pages = nullptr;
   size_t pin_cap = 0;
+  // batched step (Q4 / Q6, more than kMaxBatch sequences): weight tensor maps
+  // and the activation image
+  bool batched = false;
+  BatchedW bw{};
 
   template <typename T>
   T *dalloc(size_t n) {
@@ -479,7 +626,72 @@ size_t smem_bytes(const ocrvl_model_desc &d, int qtype, int max_chunks) {
   size_t g1 = gemv_smem_total(qtype, 1, nmax, kStagesM1);
   size_t gb = gemv_smem_total(qtype, kMaxBatch, nmax, kStagesMB);
   size_t attn = attn_smem_floats(max_chunks) * 4;
-  return std::max(std::max(g1, gb), attn) + 64;
+  size_t bgemm = qtype == QT_Q8 ? 0 : gemm_b_smem_bytes();
+  return std::max(std::max(std::max(g1, gb), attn), bgemm) + 64;
+}
+
+typedef CUresult (*PfnEncodeTiled)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
+                                   const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+// 2-D TMA map of a packed weight matrix: rows of `pitch` bytes; box = one
+// K tile of packed bytes x gemm_nt(rows, grid) rows (rows past the end read 0).
+bool make_weight_map(PfnEncodeTiled enc, const DMat &A, int qtype, int grid, TmapBytes *out) {
+  const int KP = qtype == QT_Q4 ? kKT / 2 : kKT * 3 / 4;
+  cuuint64_t dims[2] = {(cuuint64_t)A.pitch, (cuuint64_t)A.rows};
+  cuuint64_t strides[1] = {(cuuint64_t)A.pitch};
+  cuuint32_t box[2] = {(cuuint32_t)KP, (cuuint32_t)gemm_nt(A.rows, grid)};
+  cuuint32_t es[2] = {1, 1};
+  memset(out, 0, sizeof(*out));
+  return enc((CUtensorMap *)out, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, (void *)A.w, dims, strides, box, es,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// Sets up the batched step for Q4 / Q6 models: weight maps, activation image,
+// kernel attributes.  Leaves m->batched false (steps of more than kMaxBatch
+// sequences then run as groups) when any part is unavailable.
+template <int QT>
+void setup_batched(ocrvl_model *m) {
+  static_assert(sizeof(TmapBytes) == sizeof(CUtensorMap), "tensor map size");
+  void *fn = nullptr;
+  cudaDriverEntryPointQueryResult q;
+  if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) != cudaSuccess || !fn ||
+      q != cudaDriverEntryPointSuccess) {
+    cudaGetLastError();
+    return;
+  }
+  PfnEncodeTiled enc = (PfnEncodeTiled)fn;
+  const int L = m->desc.num_layers;
+  std::vector<TmapBytes> maps((size_t)L * 5 + 1);
+  for (int l = 0; l < L; l++) {
+    const LayerW &w = m->layers[l];
+    const DMat *mats[5] = {&w.qkv, &w.o, &w.gate, &w.up, &w.down};
+    for (int i = 0; i < 5; i++)
+      if (!make_weight_map(enc, *mats[i], QT, m->grid, &maps[(size_t)l * 5 + i])) return;
+  }
+  if (!make_weight_map(enc, m->lm_head, QT, m->grid, &maps[(size_t)L * 5])) return;
+  TmapBytes *dmaps = m->dalloc<TmapBytes>(maps.size());
+  const int kcols = (m->ctx.pro_cols + kKT - 1) / kKT * kKT;
+  uint8_t *act = m->dalloc<uint8_t>((size_t)kMmaM * kcols);
+  float *act_sx = m->dalloc<float>(kMaxSeqs);
+  if (!dmaps || !act || !act_sx) return;
+  if (cudaMemcpy(dmaps, maps.data(), maps.size() * sizeof(TmapBytes), cudaMemcpyHostToDevice) != cudaSuccess ||
+      cudaMemset(act, 0, (size_t)kMmaM * kcols) != cudaSuccess ||
+      cudaFuncSetAttribute(k_step_b<QT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)m->smem) != cudaSuccess) {
+    cudaGetLastError();
+    return;
+  }
+  int per_sm = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_step_b<QT>, kThreads, m->smem) != cudaSuccess ||
+      per_sm * m->sms < m->grid) {
+    cudaGetLastError();
+    return;
+  }
+  m->bw.tm = dmaps;
+  m->bw.act = act;
+  m->bw.act_sx = act_sx;
+  m->batched = true;
 }
 
 template <int QT>
@@ -504,7 +716,23 @@ int launch_step_q(ocrvl_model *m, int M, int any_logits, int do_embed, int feed)
   return OCRVL_OK;
 }
 
+template <int QT>
+int launch_step_b(ocrvl_model *m, int any_logits, int do_embed, int feed) {
+  Ctx c = m->ctx;
+  BatchedW bw = m->bw;
+  unsigned base = m->bar_base;
+  void *args[] = {&c, &bw, &any_logits, &do_embed, &feed, &base};
+  CK(cudaLaunchCooperativeKernel((void *)k_step_b<QT>, dim3(m->grid), dim3(kThreads), args, m->smem, m->stream));
+  m->bar_base += barriers_per_step_b(m->desc.num_layers, any_logits) * (unsigned)m->grid;
+  return OCRVL_OK;
+}
+
 int launch_step(ocrvl_model *m, int M, int any_logits, int do_embed, int feed = 0) {
+  if (M > kMaxBatch) {
+    if (!m->batched) return fail(OCRVL_E_INVALID, "batched step needs Q4 or Q6 weights");
+    if (m->qtype == QT_Q4) return launch_step_b<QT_Q4>(m, any_logits, do_embed, feed);
+    return launch_step_b<QT_Q6>(m, any_logits, do_embed, feed);
+  }
   if (m->qtype == QT_Q4) return launch_step_q<QT_Q4>(m, M, any_logits, do_embed, feed);
   if (m->qtype == QT_Q6) return launch_step_q<QT_Q6>(m, M, any_logits, do_embed, feed);
   return launch_step_q<QT_Q8>(m, M, any_logits, do_embed, feed);
@@ -781,6 +1009,8 @@ int ocrvl_finalize(ocrvl_model *m) {
              : m->qtype == QT_Q6 ? set_kernel_attrs<QT_Q6>(m) : set_kernel_attrs<QT_Q8>(m);
     if (rc) return rc;
   }
+  if (m->qtype == QT_Q4 && !getenv("OCRVL_NO_BATCHED")) setup_batched<QT_Q4>(m);
+  if (m->qtype == QT_Q6 && !getenv("OCRVL_NO_BATCHED")) setup_batched<QT_Q6>(m);
   if (getenv("OCRVL_TRACE")) {
     c.trace = m->dalloc<unsigned long long>(4 * 256);
     if (!c.trace) return fail(OCRVL_E_NOMEM, "trace buffer");
@@ -971,6 +1201,8 @@ int ocrvl_step(ocrvl_model *m, ocrvl_seq *const *seqs, int n, const int32_t *ids
     if (s->len % kPageTokens == 0 && (int)s->pages.size() <= s->len / kPageTokens) new_pages++;
   }
   if (new_pages > m->free_pages.size()) return fail(OCRVL_E_NOMEM, "KV page pool exhausted");
+  if (n > kMaxBatch && m->batched)
+    return step_group(m, seqs, n, ids, embeds, pos_thw, need_logits, out_ids, out_logits);
   // groups of kMaxBatch sequences, one launch each
   for (int g0 = 0; g0 < n; g0 += kMaxBatch) {
     const int gn = std::min(kMaxBatch, n - g0);
@@ -986,8 +1218,9 @@ void *ocrvl_model_stream(ocrvl_model *m) { return m ? (void *)m->stream : nullpt
 
 int ocrvl_step_io_bytes(const ocrvl_model *m, int n, int64_t *h2d, int64_t *d2h) {
   if (!m || !h2d || !d2h || n < 1 || n > kMaxSeqs) return fail(OCRVL_E_INVALID, "bad arguments");
-  const int groups = (n + kMaxBatch - 1) / kMaxBatch;
-  *h2d = (int64_t)(step_params_bytes(kMaxBatch) * (groups - 1) + step_params_bytes(n - (groups - 1) * kMaxBatch));
+  const int groups = m->batched ? 1 : (n + kMaxBatch - 1) / kMaxBatch;
+  *h2d = groups == 1 ? (int64_t)step_params_bytes(n)
+                     : (int64_t)(step_params_bytes(kMaxBatch) * (groups - 1) + step_params_bytes(n - (groups - 1) * kMaxBatch));
   *d2h = (int64_t)n * 4 + 4 * groups;  // ids + error word per launch
   return OCRVL_OK;
 }
@@ -1101,7 +1334,7 @@ int ocrvl_decode_greedy_device(ocrvl_model *m, ocrvl_seq *const *seqs, int n, co
   std::lock_guard<std::mutex> lk(m->mu);
   if (!m->finalized) return fail(OCRVL_E_INVALID, "model not finalized");
   if (int rc = set_device(m)) return rc;
-  if (n <= kMaxBatch) return decode_group(m, seqs, n, first_ids, steps, out_ids);
+  if (n <= kMaxBatch || m->batched) return decode_group(m, seqs, n, first_ids, steps, out_ids);
   // groups of kMaxBatch sequences run one after another; pages for all of
   // them are checked first so that no group starts when a later one cannot
   size_t new_pages = 0;

@@ -151,6 +151,70 @@ def test_many_sequences_step_equals_single(tiny_models, q):
         rt.step([rt.new_sequence(4) for _ in range(65)], ids=[1] * 65)
 
 
+@pytest.mark.parametrize("q", ["q4", "q6"])
+def test_batched_64_sequences_tensor_core_step(tiny_models, q):
+    """64 sequences with caches past one chunk (the batched kernel: int8
+    tensor-core GEMMs) give the same ids and logits, bit for bit, as each
+    sequence stepped alone, for three steps in a row."""
+    _need_gpu()
+    cfg, rt, _ = _pair(tiny_models[q], q)
+    n = 64
+    # one launch for all 64 (ids of 64 sequences + one status word come back)
+    assert rt.step_io_bytes(n)[1] == 4 * n + 4
+    lens = [33 + (j * 7) % 20 for j in range(n)]
+    prompts = [synth.random_prompt(lens[j], cfg.vocab_size, 500 + j) for j in range(n)]
+    seq_a = [rt.new_sequence(80) for _ in range(n)]
+    seq_b = [rt.new_sequence(80) for _ in range(n)]
+    toks = []
+    for j in range(n):
+        # prefill through the batched path too: all prompts of one length step together
+        for t in prompts[j][:-1]:
+            rt.step([seq_b[j]], ids=[t], need_logits=False)
+        toks.append(prompts[j][-1])
+    for p in range(max(lens) - 1):
+        live = [j for j in range(n) if p < lens[j] - 1]
+        rt.step([seq_a[j] for j in live], ids=[prompts[j][p] for j in live], need_logits=False)
+    for step in range(3):
+        ids_joint, logits_joint = rt.step(seq_a, ids=toks, return_logits=True)
+        for j in range(n):
+            ids1, logits1 = rt.step([seq_b[j]], ids=[toks[j]], return_logits=True)
+            assert int(ids1[0]) == int(ids_joint[j]), (step, j)
+            assert np.array_equal(logits1[0], logits_joint[j]), (step, j)
+        toks = [int(i) for i in ids_joint]
+
+
+@pytest.mark.parametrize("q", ["q4", "q8"])
+def test_long_caches_more_items_than_blocks(tiny_models, q):
+    """8 sequences whose chunked attention has more items than the grid has
+    blocks (each block then takes several items, with K/V copies started
+    before the phase), through prompt steps (append only in the last layer)
+    and full steps: ids and logits equal to each sequence stepped alone."""
+    _need_gpu()
+    cfg, rt, _ = _pair(tiny_models[q], q)
+    n = 8
+    lens = [150 + 9 * j for j in range(n)]
+    prompts = [synth.random_prompt(L, cfg.vocab_size, 900 + j) for j, L in enumerate(lens)]
+    seq_a = [rt.new_sequence(L + 8) for L in lens]
+    seq_b = [rt.new_sequence(L + 8) for L in lens]
+    for p in range(max(lens) - 1):
+        live = [j for j in range(n) if p < lens[j] - 1]
+        rt.step([seq_a[j] for j in live], ids=[prompts[j][p] for j in live], need_logits=False)
+    for j in range(n):
+        for t in prompts[j][:-1]:
+            rt.step([seq_b[j]], ids=[t], need_logits=False)
+    for j in range(n):
+        ka, va = seq_a[j].read_kv(1)
+        kb, vb = seq_b[j].read_kv(1)
+        assert np.array_equal(ka, kb) and np.array_equal(va, vb)
+    toks = [pr[-1] for pr in prompts]
+    for step in range(3):
+        ids_joint, logits_joint = rt.step(seq_a, ids=toks, return_logits=True)
+        for j in range(n):
+            ids1, logits1 = rt.step([seq_b[j]], ids=[toks[j]], return_logits=True)
+            assert int(ids1[0]) == int(ids_joint[j]) and np.array_equal(logits1[0], logits_joint[j]), (step, j)
+        toks = [int(i) for i in ids_joint]
+
+
 def test_embeds_and_mrope_positions(tiny_models):
     """Embedding input and distinct (T,H,W) positions (image-token prefill)."""
     _need_gpu()
