@@ -79,7 +79,7 @@ struct Ctx {
   float *part_t;                     // [B][QH][D] raw-score tail sums
   unsigned long long *argkey;        // [B]
   int *tok_out;                      // [B] ids, then the error word
-  int max_ctx, max_chunks;
+  int max_ctx;
   // step parameters: `sp` is read (inside the step kernels it points to a
   // shared-memory copy made at launch), `sp_w` is the global copy that the
   // device-fed loop advances for the next launch
@@ -1480,79 +1480,59 @@ __device__ float warp_softmax_weight(float v, int n) {
 // ---------------------------------------------------------------------------
 // Attention phase: RoPE, KV append, scores, softmax and value sums.
 //
-// Items: (sequence m, kv head g, chunk of tokens).  Caches of n <= 32
-// positions form one 32-token item per (m, g) that applies the reference
-// softmax exactly (incl. its small-n forms) and sums values in token order.
-// Longer caches are split into 16-token chunks (one KV page each): chunk c
-// keeps its max m_c, l_c = sum of exp_fma(s - m_c) and o_c = sum exp(...) v;
-// with nv = 16*floor(n/16) the last chunk holds the tokens at or above nv
-// (if n % 16 != 0), which the reference weights by their raw score
-// (expF32VecFMA leaves them unexponentiated, dot_amd64.s:6131-6168): that
-// chunk reports its max and the raw-weighted sum T instead.  Merge per query
-// head: head = (T + sum_c exp(m_c - M) o_c) / sum_c exp(m_c - M) l_c, M the
-// max over all scores.
+// Caches of n <= 32 positions form one 32-token item per (sequence m, kv
+// head g) that applies the reference softmax exactly (incl. its small-n
+// forms) and sums values in token order.  The item serves the G = QH/KVH
+// query heads of its kv head (GQA): warp h computes head h's scores, one
+// 128-wide dot per token split over the warp in the reference's 16-slot order
+// (lane = slot + 16*half, 4 products per lane, xor-16 pair, then the tree16
+// pairs by xor 8/4/2/1), so lane t ends holding token t's score.  K/V pages
+// arrive by TMA bulk copy into shared memory, issued before the grid barrier
+// that precedes the phase when the block's item is known (attn_prefetch);
+// the item takes the new token's k and v from the QKV output, rotates k and
+// appends both to the page (kvCache.append, model.go:5593-5612).
 //
-// Each item serves the G = QH/KVH query heads of its kv head (GQA): warp h
-// computes head h's scores, one 128-wide dot per token split over the warp in
-// the reference's 16-slot order (lane = slot + 16*half, 4 products per lane,
-// xor-16 pair, then the tree16 pairs by xor 8/4/2/1), so lane t ends holding
-// token t's score.  K/V pages arrive by TMA bulk copy into shared memory,
-// issued before the grid barrier that precedes the phase when the block's
-// item is known (attn_prefetch); the item holding the new token takes its k
-// and v from the QKV output, rotates k and appends both to the page
-// (kvCache.append, model.go:5593-5612).
-//
-// Merge: each item raises its (m, g) arrival counter.  When every item has a
-// block of its own, the last G arrivals each wait for the counter to be
-// complete (bounded) and merge one query head in parallel; otherwise the last
-// arrival merges all G heads.
+// Longer caches are streamed in page ranges with an online softmax per
+// segment and a merge per (m, g): phase_attn_range (attn_range.cuh), run in
+// the same phase after the block's short-cache items.
 // ---------------------------------------------------------------------------
-constexpr int kChunkTok = 16;  // tokens per chunk of a long cache (one KV page)
-
-__device__ __forceinline__ unsigned ld_acquire_u32(const unsigned *p) {
-  unsigned v;
-  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
-}
-
 struct AttnItem {
   int m, g, ch, t0, cnt, n, nch;
   bool exact;
 };
 
-// Item `it` of the step; false when it is past the last item.
+// Item `it` of the step (caches of n <= kAttnChunk positions, one item per
+// (sequence, kv head)); false when it is past the last item.
 __device__ __forceinline__ bool attn_item(const Ctx &c, const StepParams &sp, int it, AttnItem &I) {
   for (int m = 0; m < sp.M; m++) {
     const int n = sp.seq[m].len + 1;
-    const bool exact = n <= kAttnChunk;
-    const int ct = exact ? kAttnChunk : kChunkTok;
-    const int nch = (n + ct - 1) / ct;
-    const int cnt_items = c.KVH * nch;
-    if (it < cnt_items) {
+    if (n > kAttnChunk) continue;
+    if (it < c.KVH) {
       I.m = m;
-      I.g = it / nch;
-      I.ch = it % nch;
-      I.t0 = I.ch * ct;
-      I.cnt = min(n, I.t0 + ct) - I.t0;
+      I.g = it;
+      I.ch = 0;
+      I.t0 = 0;
+      I.cnt = n;
       I.n = n;
-      I.nch = nch;
-      I.exact = exact;
+      I.nch = 1;
+      I.exact = true;
       return true;
     }
-    it -= cnt_items;
+    it -= c.KVH;
   }
   return false;
 }
 
 __device__ __forceinline__ int attn_items_total(const Ctx &c, const StepParams &sp) {
   int total = 0;
-  for (int m = 0; m < sp.M; m++) {
-    const int n = sp.seq[m].len + 1;
-    const int ct = n <= kAttnChunk ? kAttnChunk : kChunkTok;
-    total += c.KVH * ((n + ct - 1) / ct);
-  }
+  for (int m = 0; m < sp.M; m++)
+    if (sp.seq[m].len + 1 <= kAttnChunk) total += c.KVH;
   return total;
 }
+
+}  // namespace ocrvl
+#include "attn_range.cuh"
+namespace ocrvl {
 
 // Per-block state of the K/V page loads, kept across phases of one launch.
 __shared__ __align__(8) uint64_t s_kv_bar;
@@ -1563,11 +1543,11 @@ __shared__ float s_rope_cs[kMaxBatch][kHeadDim / 2], s_rope_sn[kMaxBatch][kHeadD
 __shared__ int s_rope_ready;
 
 // Shared-memory layout of the attention phase (floats), from the base:
-//   q [G][D] | wt [G][32] | red [8][D] | scl [max_chunks]
+//   q [G][D] | wt [G][32]
 // and the K/V page buffers K [32][D] | V [32][D] (32 KB) in the last slot of
 // the GEMV stage ring, which the QKV phase before attention leaves unused.
-__host__ __device__ __forceinline__ size_t attn_smem_floats(int max_chunks) {
-  return (size_t)kMaxGroup * kHeadDim + (size_t)kMaxGroup * kAttnChunk + (size_t)8 * kHeadDim + (size_t)max_chunks;
+__host__ __device__ __forceinline__ size_t attn_smem_floats() {
+  return (size_t)kMaxGroup * kHeadDim + (size_t)kMaxGroup * kAttnChunk;
 }
 static_assert(2 * kAttnChunk * kHeadDim * 4 <= kStageBytes, "K/V buffers fit one ring slot");
 
@@ -1586,6 +1566,7 @@ __device__ __forceinline__ void attn_block_init() {
     s_kv_item = -1;
     s_rope_ready = 0;
   }
+  rg_block_init();
   __syncthreads();
 }
 
@@ -1645,14 +1626,42 @@ __device__ void attn_prefetch(const Ctx &c, int layer, float *smem, int lead) {
   s_kv_item = blockIdx.x;
 }
 
-// Waits for outstanding K/V loads (before the block leaves the kernel).
-__device__ void attn_drain(const Ctx &c) {
+// Waits for the outstanding K/V load of an n <= kAttnChunk item.
+__device__ __forceinline__ void attn_drain_item(const Ctx &c) {
   if (threadIdx.x == 0 && s_kv_item >= 0) {
     mbar_wait(&s_kv_bar, s_kv_parity, c.err);
     s_kv_parity ^= 1u;
     s_kv_item = -1;
   }
+}
+
+// Waits for every outstanding K/V load (before the block leaves the kernel).
+__device__ void attn_drain(const Ctx &c) {
+  attn_drain_item(c);
+  if (threadIdx.x == 0) rg_drain(c);
   __syncthreads();
+}
+
+// Thread `lead`, ahead of the attention phase of `layer`: the block's first
+// long-cache chunks (attn_range.cuh).  during_qkv: before the QKV phase,
+// whose weight stages then share the ring (single-sequence steps only, into
+// the slots the block's QKV slab leaves free).  A block with n <= kAttnChunk
+// items loads those first and skips this.
+__device__ void attn_range_prefetch(const Ctx &c, int layer, float *smem, int lead, bool during_qkv) {
+  const StepParams &sp = *c.sp;
+  if ((int)threadIdx.x != lead || attn_items_total(c, sp) > (int)blockIdx.x) return;
+  int upto = kRangeBufs;
+  if (during_qkv) {
+    if (sp.M > 1) return;
+    const DMat &A = c.layers[layer].qkv;
+    int lo, hi;
+    gemv_slab(0, A.rows, blockIdx.x, gridDim.x, lo, hi);
+    const int srows = kStageBytes / A.pitch;
+    upto = min(upto, kStagesM1 - (hi - lo + srows - 1) / srows);
+  }
+  RgCur r;
+  int i;
+  rg_issue_ahead(c, layer, smem, upto, r, i);
 }
 
 __device__ __noinline__ void phase_attn(const Ctx *cp, int layer, int append_only, int coop, float *smem) {
@@ -1664,34 +1673,27 @@ __device__ __noinline__ void phase_attn(const Ctx *cp, int layer, int append_onl
   float *Vs = Ks + kAttnChunk * D;                 // [32][D]
   float *qs = smem;                                // [G][D]
   float *wt = qs + kMaxGroup * D;                  // [G][32]
-  float *red = wt + kMaxGroup * kAttnChunk;        // [8][D]
-  float *scl = red + 8 * D;                        // [max_chunks]
   __shared__ float rcs_l[kHeadDim / 2], rsn_l[kHeadDim / 2];
-  __shared__ int merge_head;
-  __shared__ float mloc[kMaxGroup], lloc[kMaxGroup], dinv_s;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int items = attn_items_total(c, sp);
-  const bool multi = coop && items <= (int)gridDim.x;
   int tab_m = -1;  // sequence whose RoPE values rcs/rsn hold
   for (int it = blockIdx.x; it < items; it += gridDim.x) {
     AttnItem I;
     attn_item(c, sp, it, I);
     const int len = I.n - 1;
-    const bool has_new = I.t0 <= len && len < I.t0 + I.cnt;
     // one K/V copy in flight at a time: a copy started for another item (the
-    // one prefetched before the phase, when that item is skipped below or the
-    // block moves past it) completes before the buffers are reused
-    if (threadIdx.x == 0 && s_kv_item >= 0 && (s_kv_item != it || (append_only && !has_new))) {
+    // one prefetched before the phase, when the block moves past it)
+    // completes before the buffers are reused
+    if (threadIdx.x == 0 && s_kv_item >= 0 && (s_kv_item != it || append_only)) {
       mbar_wait(&s_kv_bar, s_kv_parity, c.err);
       s_kv_parity ^= 1u;
       s_kv_item = -1;
     }
-    if (append_only && !has_new) continue;
     const int *pos = sp.seq[I.m].pos;
     const bool has_rope = pos[0] != 0 || pos[1] != 0 || pos[2] != 0;
     const float *qkv = c.qkv + (size_t)I.m * qkvld;
     // ---- K/V pages (unless prefetched for this item), RoPE table of the position
-    if (threadIdx.x == 0 && s_kv_item != it) {
+    if (threadIdx.x == 0 && s_kv_item != it && !append_only) {
       attn_issue_kv(c, layer, I, Ks);
       s_kv_item = it;
     }
@@ -1719,8 +1721,7 @@ __device__ __noinline__ void phase_attn(const Ctx *cp, int layer, int append_onl
       }
     }
     float4 nk_a, nk_b, nv4;
-    const int tt_new = len - I.t0;
-    if (has_new && threadIdx.x < D4) {
+    if (threadIdx.x < D4) {
       if (threadIdx.x < H4) {
         const float4 *kn = (const float4 *)(qkv + (size_t)(c.QH + I.g) * D);
         nk_a = __ldcg(kn + threadIdx.x);
@@ -1733,25 +1734,25 @@ __device__ __noinline__ void phase_attn(const Ctx *cp, int layer, int append_onl
       nv4 = __ldcg((const float4 *)(qkv + (size_t)(c.QH + c.KVH + I.g) * D) + threadIdx.x);
       ((float4 *)kv_ptr(c, sp.seq[I.m].bt, layer, 1, I.g, len))[threadIdx.x] = nv4;
     }
+    if (append_only) {
+      __syncthreads();
+      continue;
+    }
     if (threadIdx.x == 0) {
       mbar_wait(&s_kv_bar, s_kv_parity, c.err);
       s_kv_parity ^= 1u;
       s_kv_item = -1;
     }
     __syncthreads();
-    if (has_new && threadIdx.x < D4) {
+    if (threadIdx.x < D4) {
       if (threadIdx.x < H4) {
-        ((float4 *)(Ks + (size_t)tt_new * D))[threadIdx.x] = nk_a;
-        ((float4 *)(Ks + (size_t)tt_new * D))[threadIdx.x + H4] = nk_b;
+        ((float4 *)(Ks + (size_t)len * D))[threadIdx.x] = nk_a;
+        ((float4 *)(Ks + (size_t)len * D))[threadIdx.x + H4] = nk_b;
       }
-      ((float4 *)(Vs + (size_t)tt_new * D))[threadIdx.x] = nv4;
-    }
-    if (append_only) {
-      __syncthreads();
-      continue;
+      ((float4 *)(Vs + (size_t)len * D))[threadIdx.x] = nv4;
     }
     __syncthreads();
-    // ---- scores (warp = head) and softmax / chunk statistics
+    // ---- scores (warp = head) and the reference softmax
     const int slot = lane & 15, half = lane >> 4;
     if (warp < G) {
       const float *q = qs + warp * D;
@@ -1775,25 +1776,8 @@ __device__ __noinline__ void phase_attn(const Ctx *cp, int layer, int append_onl
         r = __fadd_rn(r, __shfl_xor_sync(0xffffffffu, r, 1));
         if (lane == tt) mine = __fmul_rn(r, c.attn_scale);
       }
-      float w;
-      if (I.exact) {
-        w = warp_softmax_weight(mine, I.n);  // every lane takes part in the shuffles
-        if (lane >= I.cnt) w = 0.0f;
-      } else {
-        const int nv = I.n & ~15;
-        const bool tail = I.t0 >= nv;  // the whole chunk lies at or above nv
-        float mx = lane < I.cnt ? mine : -INFINITY;
-        for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-        float e = 0.0f;
-        if (lane < I.cnt) e = tail ? mine : exp_fma(__fsub_rn(mine, mx));
-        float l = tail ? 0.0f : e;
-        for (int o = 16; o > 0; o >>= 1) l = __fadd_rn(l, __shfl_xor_sync(0xffffffffu, l, o));
-        w = e;
-        if (lane == 0) {
-          mloc[warp] = mx;
-          lloc[warp] = l;
-        }
-      }
+      float w = warp_softmax_weight(mine, I.n);  // every lane takes part in the shuffles
+      if (lane >= I.cnt) w = 0.0f;
       wt[warp * kAttnChunk + lane] = w;
     }
     __syncthreads();
@@ -1802,17 +1786,10 @@ __device__ __noinline__ void phase_attn(const Ctx *cp, int layer, int append_onl
     for (int p = threadIdx.x; p < G * D4; p += kThreads) {
       const int hh = p / D4, d4 = p % D4;
       const float *w = wt + hh * kAttnChunk;
-      float4 acc;
-      int t = 0;
-      if (I.exact) {
-        const float4 v0 = ((const float4 *)Vs)[d4];
-        acc = make_float4(__fmul_rn(w[0], v0.x), __fmul_rn(w[0], v0.y), __fmul_rn(w[0], v0.z), __fmul_rn(w[0], v0.w));
-        t = 1;
-      } else {
-        acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-      }
+      const float4 v0 = ((const float4 *)Vs)[d4];
+      float4 acc = make_float4(__fmul_rn(w[0], v0.x), __fmul_rn(w[0], v0.y), __fmul_rn(w[0], v0.z), __fmul_rn(w[0], v0.w));
 #pragma unroll 4
-      for (; t < I.cnt; t++) {
+      for (int t = 1; t < I.cnt; t++) {
         const float4 v = ((const float4 *)(Vs + (size_t)t * D))[d4];
         const float wv = w[t];
         acc.x = __fmaf_rn(wv, v.x, acc.x);
@@ -1820,140 +1797,21 @@ __device__ __noinline__ void phase_attn(const Ctx *cp, int layer, int append_onl
         acc.z = __fmaf_rn(wv, v.z, acc.z);
         acc.w = __fmaf_rn(wv, v.w, acc.w);
       }
-      if (I.exact) {
-        ((float4 *)(c.head + (hbase + hh) * D))[d4] = acc;
-      } else {
-        const bool tail = I.t0 >= (I.n & ~15);
-        if (tail) {
-          ((float4 *)(c.part_t + (hbase + hh) * D))[d4] = acc;
-        } else {
-          ((float4 *)(c.part_o + ((size_t)it * G + hh) * D))[d4] = acc;
-        }
-        if (d4 == 0) {
-          float *ml = c.part_ml + ((size_t)it * G + hh) * 2;
-          ml[0] = mloc[hh];
-          ml[1] = lloc[hh];
-        }
-      }
-    }
-    if (I.exact) {
-      __syncthreads();
-      continue;
-    }
-    // ---- arrival (the barrier orders the block's partial writes before
-    // thread 0's fence and count); pick the merge work of this block
-    __syncthreads();
-    if (threadIdx.x == 0) {
-      unsigned *cnt = c.attn_count + 2 * (I.m * c.KVH + I.g);
-      // release: the block's partials (ordered before by the barrier) become
-      // visible with the count; acquire: a merger sees the others' partials
-      unsigned v;
-      asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(v) : "l"(cnt) : "memory");
-      const int nch = I.nch;
-      int mh = -1;
-      if (multi && nch >= G) {
-        if ((int)v >= nch - G) {
-          mh = (int)v - (nch - G);
-          // wait until every chunk of (m, g) has arrived (bounded)
-          unsigned long long spins = 0;
-          while (ld_acquire_u32(cnt) < (unsigned)nch) {
-            if (++spins > (1ull << 24) || *(volatile int *)c.err) {
-              atomicExch(c.err, 1);
-              mh = -2;
-              break;
-            }
-          }
-          if (mh >= 0 && atomicAdd(cnt + 1, 1u) == (unsigned)G - 1) {
-            // every merger has seen the complete count: reset for the next layer
-            cnt[1] = 0u;
-            cnt[0] = 0u;
-          }
-        }
-      } else if ((int)v == nch - 1) {
-        mh = G;  // all heads
-        cnt[0] = 0u;
-      }
-      merge_head = mh;
+      ((float4 *)(c.head + (hbase + hh) * D))[d4] = acc;
     }
     __syncthreads();
-    const int mh = merge_head;
-    if (mh < 0) continue;
-    const int h0 = mh == G ? 0 : mh, h1 = mh == G ? G : mh + 1;
-    const bool has_tail = (I.n & 15) != 0;
-    const int nfull = has_tail ? I.nch - 1 : I.nch;  // chunks with exponentiated weights
-#pragma unroll 1
-    for (int hh = h0; hh < h1; hh++) {
-      const size_t hq = hbase + hh;
-      // chunk k of (m, g) is item it0 + k; stride G heads per item
-      const size_t it0 = (size_t)(it - I.ch);
-      const float *ml = c.part_ml + (it0 * G + hh) * 2;
-      // this thread's first chunk partials, fetched while warp 0 works out
-      // the chunk scales
-      constexpr int kB = 4;
-      const int grp = threadIdx.x >> 5, d4 = threadIdx.x & 31;
-      const float4 *po = (const float4 *)(c.part_o + (it0 * G + hh) * D) + d4;
-      const size_t pstride = (size_t)G * D4;  // float4 per chunk
-      float4 v[kB];
-#pragma unroll
-      for (int u = 0; u < kB; u++)
-        if (grp + 8 * u < nfull && d4 < D4) v[u] = __ldcg(po + (size_t)(grp + 8 * u) * pstride);
-      if (warp == 0) {
-        float mx = -INFINITY;
-        for (int k = lane; k < I.nch; k += 32) mx = fmaxf(mx, __ldcg(ml + 2 * G * k));
-        for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-        float den = 0.0f;
-        for (int k = lane; k < nfull; k += 32) {
-          const float sk = exp_fma(__fsub_rn(__ldcg(ml + 2 * G * k), mx));
-          scl[k] = sk;
-          den = __fmaf_rn(sk, __ldcg(ml + 2 * G * k + 1), den);
-        }
-        for (int o = 16; o > 0; o >>= 1) den = __fadd_rn(den, __shfl_xor_sync(0xffffffffu, den, o));
-        if (lane == 0) dinv_s = __fdiv_rn(1.0f, den);
-      }
-      __syncthreads();
-      // 8 chunk groups x 32 float4 of dims; group sums, then in group order
-      {
-        float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-#pragma unroll 1
-        for (int k0 = grp; k0 < nfull; k0 += 8 * kB) {
-          if (k0 != grp) {
-#pragma unroll
-            for (int u = 0; u < kB; u++)
-              if (k0 + 8 * u < nfull && d4 < D4) v[u] = __ldcg(po + (size_t)(k0 + 8 * u) * pstride);
-          }
-#pragma unroll
-          for (int u = 0; u < kB; u++) {
-            if (k0 + 8 * u < nfull) {
-              const float sk = scl[k0 + 8 * u];
-              acc.x = __fmaf_rn(sk, v[u].x, acc.x);
-              acc.y = __fmaf_rn(sk, v[u].y, acc.y);
-              acc.z = __fmaf_rn(sk, v[u].z, acc.z);
-              acc.w = __fmaf_rn(sk, v[u].w, acc.w);
-            }
-          }
-        }
-        if (d4 < D4) ((float4 *)(red + grp * D))[d4] = acc;
-      }
-      __syncthreads();
-      if (threadIdx.x < D4) {
-        const int d4 = threadIdx.x;
-        float4 acc = has_tail ? __ldcg((const float4 *)(c.part_t + hq * D) + d4) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-#pragma unroll
-        for (int gq = 0; gq < 8; gq++) {
-          const float4 v = ((const float4 *)(red + gq * D))[d4];
-          acc.x = __fadd_rn(acc.x, v.x);
-          acc.y = __fadd_rn(acc.y, v.y);
-          acc.z = __fadd_rn(acc.z, v.z);
-          acc.w = __fadd_rn(acc.w, v.w);
-        }
-        const float di = dinv_s;
-        ((float4 *)(c.head + hq * D))[d4] =
-            make_float4(__fmul_rn(acc.x, di), __fmul_rn(acc.y, di), __fmul_rn(acc.z, di), __fmul_rn(acc.w, di));
-      }
-      __syncthreads();
-    }
   }
-  attn_drain(c);
+  attn_drain_item(c);
+  __syncthreads();
+  (void)coop;
+  // ---- caches of more than kAttnChunk positions
+  if (append_only) {
+    if (threadIdx.x == 0) rg_drain(c);
+    phase_append_long(c, layer);
+    __syncthreads();
+  } else {
+    phase_attn_range(cp, layer, smem);
+  }
 }
 
 // Normalised output of a fused AddRMSNorm (the normOut vector of

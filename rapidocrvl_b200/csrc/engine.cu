@@ -195,17 +195,26 @@ __device__ __forceinline__ bool is_gemv_phase(int phase) { return phase != 1; }
 // Work for phase (phase, layer) that needs nothing from other blocks, done by
 // threads kHelper.. while thread 0 waits at the grid barrier before it: the
 // GEMV arguments, the first weight stages and the staged scales / norm
-// weights; before a QKV phase also the K/V pages of the block's attention
-// item.  The block's next __syncthreads publishes the results.
+// weights; before a QKV phase also the K/V pages of the block's first
+// short-cache item or (single-sequence steps) of its first long-cache chunks,
+// and before the attention phase the remaining first chunks.  The block's
+// next __syncthreads publishes the results.
 constexpr int kHelper = 32;
 template <int QT>
 __device__ void prepare_phase(const Ctx &c, int phase, int layer, int M, int any_logits, int do_embed, int feed,
                               float *smem, int tidx) {
-  if (!is_gemv_phase(phase)) return;
+  const bool kv_only = layer == c.L - 1 && !any_logits;
+  if (!is_gemv_phase(phase)) {
+    if (phase == 1 && !kv_only) attn_range_prefetch(c, layer, smem, kHelper, false);
+    return;
+  }
   if (threadIdx.x == kHelper) build_args(c, phase, layer, any_logits, do_embed, feed, tidx);
   helpers_sync(kHelper);
   gemv_setup(QT, c, s_args, M, smem, kHelper, kThreads - kHelper);
-  if (phase == 0) attn_prefetch(c, layer, smem, kHelper);
+  if (phase == 0) {
+    attn_prefetch(c, layer, smem, kHelper);
+    if (!kv_only) attn_range_prefetch(c, layer, smem, kHelper, true);
+  }
   if (threadIdx.x == kHelper) s_ring_setup = 1;
 }
 
@@ -239,6 +248,16 @@ __device__ __forceinline__ void copy_words(void *dst, const void *src, int bytes
   for (int i = threadIdx.x; i < bytes / 4; i += kThreads) ((int *)dst)[i] = ((const int *)src)[i];
 }
 
+// Dynamic shared memory of the step kernels, from a 1024-byte boundary: TMA
+// tensor copies and tcgen05 operand tiles need 128-byte aligned destinations,
+// and where the dynamic area starts depends on the kernel's static shared
+// memory.  The launches reserve kSmemAlignSlack bytes for the shift.
+constexpr int kSmemAlignSlack = 1024;
+__device__ __forceinline__ float *align_dyn_smem(void *p) {
+  const uint32_t s = smem_u32(p);
+  return (float *)((uint8_t *)p + ((kSmemAlignSlack - (s & (kSmemAlignSlack - 1))) & (kSmemAlignSlack - 1)));
+}
+
 #define OCRVL_CTX_TO_SMEM(cv)                                                        \
   __shared__ Ctx sctx;                                                               \
   if (threadIdx.x == 0) sctx = cv;                                                   \
@@ -257,7 +276,7 @@ template <int QT>
 __global__ void __launch_bounds__(kThreads, 1)
     k_step(Ctx cv, int M, int any_logits, int do_embed, int feed, unsigned bar_base) {
   extern __shared__ float4 smem4[];
-  float *smem = (float *)smem4;
+  float *smem = align_dyn_smem(smem4);
   OCRVL_CTX_TO_SMEM(cv);
   attn_block_init();
   ring_init();
@@ -304,7 +323,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   attn_block_init();
   ring_init();
-  run_phase<QT>(c, phase, layer, M, any_logits, do_embed, feed, (float *)smem4, 0, 0, false);
+  run_phase<QT>(c, phase, layer, M, any_logits, do_embed, feed, align_dyn_smem(smem4), 0, 0, false);
 }
 
 template <int QT>
@@ -456,7 +475,7 @@ template <int QT>
 __global__ void __launch_bounds__(kThreads, 1)
     k_step_b(Ctx cv, BatchedW bwv, int any_logits, int do_embed, int feed, unsigned bar_base) {
   extern __shared__ float4 smem4[];
-  float *smem = (float *)smem4;
+  float *smem = align_dyn_smem(smem4);
   OCRVL_CTX_TO_SMEM(cv);
   __shared__ BatchedW sbw;
   __shared__ uint32_t s_tmem;
@@ -621,13 +640,13 @@ int upload_f32(ocrvl_model *m, float *&dst, int64_t n, const void *data) {
   return OCRVL_OK;
 }
 
-size_t smem_bytes(const ocrvl_model_desc &d, int qtype, int max_chunks) {
+size_t smem_bytes(const ocrvl_model_desc &d, int qtype) {
   int nmax = std::max(std::max(d.hidden_size, d.intermediate_size), d.num_heads * d.head_dim);
   size_t g1 = gemv_smem_total(qtype, 1, nmax, kStagesM1);
   size_t gb = gemv_smem_total(qtype, kMaxBatch, nmax, kStagesMB);
-  size_t attn = attn_smem_floats(max_chunks) * 4;
+  size_t attn = std::max(attn_smem_floats() * 4, rg_smem_bytes_multi());
   size_t bgemm = qtype == QT_Q8 ? 0 : gemm_b_smem_bytes();
-  return std::max(std::max(std::max(g1, gb), attn), bgemm) + 64;
+  return std::max(std::max(std::max(g1, gb), attn), bgemm) + 64 + kSmemAlignSlack;
 }
 
 typedef CUresult (*PfnEncodeTiled)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
@@ -963,7 +982,6 @@ int ocrvl_finalize(ocrvl_model *m) {
   c.kv_pool = m->kv_pool;
   c.page_floats = m->page_floats;
   c.max_ctx = d.max_position;
-  c.max_chunks = (c.max_ctx + kChunkTok - 1) / kChunkTok;
   int qkvld = (c.QH + 2 * c.KVH) * c.D;
   size_t B = kMaxSeqs;
   c.h = m->dalloc<float>(B * c.H);
@@ -1002,7 +1020,7 @@ int ocrvl_finalize(ocrvl_model *m) {
   CK(cudaHostAlloc((void **)&m->out_h, (B + 1) * 4, cudaHostAllocDefault));
   CK(cudaHostAlloc((void **)&m->bt_stage, B * 4, cudaHostAllocDefault));
   // launch geometry
-  m->smem = smem_bytes(d, m->qtype, c.max_chunks);
+  m->smem = smem_bytes(d, m->qtype);
   CK(cudaDeviceGetAttribute(&m->sms, cudaDevAttrMultiProcessorCount, m->device));
   {
     int rc = m->qtype == QT_Q4 ? set_kernel_attrs<QT_Q4>(m)
