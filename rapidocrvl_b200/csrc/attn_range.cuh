@@ -3,9 +3,8 @@
 // mbarrier and stage-ring helpers.
 //
 // Segments.  The np pages of a (sequence m, kv head g) pair split into
-// segments of S pages: S = 1 when np <= kSegMax, else the even number
-// 2 * ceil(np / (2 kSegMax)), so a pair has at most kSegMax segments and a
-// segment is a whole number of 32-token chunks.  The split depends on the
+// segments of S = 2 * ceil(np / (2 kSegMax)) pages, so a pair has at most
+// kSegMax segments and a segment is a whole number of 32-token chunks.  The split depends on the
 // cache length only: a sequence's result does not depend on the other
 // sequences of the step (a batched step equals the single steps bit for bit).
 //
@@ -58,7 +57,9 @@ constexpr int kRgW = kRgS + 256;                          // [32 tokens][8 heads
 constexpr int kRgAlpha = kRgW + 256;                      // [8] rescale factors
 constexpr int kRgRed = kRgAlpha + 32;                     // [8][128] o of token half 1
 constexpr int kRgT = kRgRed + 8 * 128;                    // [2 halves][8][128] raw-weighted tail sums
-constexpr int kRgFloats = kRgT + 2 * 8 * 128;
+constexpr int kRgMerges = 2 * kMaxSeqs;                   // pairs a block can complete in one phase
+constexpr int kRgMerge = kRgT + 2 * 8 * 128;              // count, then [kRgMerges][2] pairs to merge (ints)
+constexpr int kRgFloats = kRgMerge + 4 + 2 * kRgMerges;
 static_assert(kRgFloats * 4 <= kStageBytes, "small arrays fit one ring slot");
 static_assert(kRgPreLen % 4 == 0 && kRgPre % 4 == 0, "16-byte aligned prefetch buffers");
 
@@ -80,9 +81,7 @@ __device__ __forceinline__ float *rg_small(const Ctx &c, int M, float *smem) {
   return (float *)((uint8_t *)smem + (size_t)kRangeBufs * kStageBytes);
 }
 
-__host__ __device__ __forceinline__ int rg_seg_pages(int np) {
-  return np <= kSegMax ? 1 : 2 * ((np + 2 * kSegMax - 1) / (2 * kSegMax));
-}
+__host__ __device__ __forceinline__ int rg_seg_pages(int np) { return 2 * ((np + 2 * kSegMax - 1) / (2 * kSegMax)); }
 
 // Position in the step's stream of segments and chunks.
 struct RgCur {
@@ -92,10 +91,25 @@ struct RgCur {
   int pbase, sbase;    // pages and segments of the long caches before m
 };
 
-// Moves to the first long cache at or after sequence m (pbase / sbase are the
-// caller's).
+// Geometry of the step's long caches, fixed for a launch (the sequences and
+// their lengths do not change within it) and computed once at its start
+// (rg_launch_init): per sequence its pages (0 for a cache of n <= kAttnChunk
+// positions), pages per segment and segments; the prefix sums of pages and
+// segments over the sequences before it (kv heads included); this block's
+// first segment, the end of its page range and the pool pages of its range
+// (block-table entries, s_rg_pg[i] for the block's page i); the sequences
+// with caches of n <= kAttnChunk positions, in order.
+constexpr int kRgPgCap = 512;  // pool pages of a block's range held in shared memory
+__shared__ int s_rg_np[kMaxSeqs], s_rg_S[kMaxSeqs], s_rg_nseg[kMaxSeqs];
+__shared__ int s_rg_pbase[kMaxSeqs + 1], s_rg_sbase[kMaxSeqs + 1];
+__shared__ RgCur s_rg_first;
+__shared__ int s_rg_hi, s_rg_p0, s_rg_npg;
+__shared__ int s_rg_pg[kRgPgCap];
+__shared__ int s_ex_n, s_ex_m[kMaxSeqs];
+
+// Moves to the first long cache at or after sequence m.
 __device__ __forceinline__ void rg_load_seq(const StepParams &sp, RgCur &r, int m) {
-  while (m < sp.M && sp.seq[m].len + 1 <= kAttnChunk) m++;
+  while (m < sp.M && s_rg_np[m] == 0) m++;
   r.g = r.k = r.j = 0;
   if (m >= sp.M) {
     r.m = -1;
@@ -103,9 +117,11 @@ __device__ __forceinline__ void rg_load_seq(const StepParams &sp, RgCur &r, int 
   }
   r.m = m;
   r.n = sp.seq[m].len + 1;
-  r.np = (r.n + kPageTokens - 1) / kPageTokens;
-  r.S = rg_seg_pages(r.np);
-  r.nseg = (r.np + r.S - 1) / r.S;
+  r.np = s_rg_np[m];
+  r.S = s_rg_S[m];
+  r.nseg = s_rg_nseg[m];
+  r.pbase = s_rg_pbase[m];
+  r.sbase = s_rg_sbase[m];
 }
 
 __device__ __forceinline__ int rg_seg_np(const RgCur &r) { return min(r.np, (r.k + 1) * r.S) - r.k * r.S; }
@@ -118,8 +134,6 @@ __device__ __forceinline__ void rg_next_seg(const Ctx &c, const StepParams &sp, 
   if (++r.k < r.nseg) return;
   r.k = 0;
   if (++r.g < c.KVH) return;
-  r.pbase += c.KVH * r.np;
-  r.sbase += c.KVH * r.nseg;
   rg_load_seq(sp, r, r.m + 1);
 }
 
@@ -131,118 +145,193 @@ __device__ __forceinline__ void rg_next_chunk(const Ctx &c, const StepParams &sp
   rg_next_seg(c, sp, r);
 }
 
-__device__ __forceinline__ int rg_total_pages(const Ctx &c, const StepParams &sp) {
-  int P = 0;
-  for (int m = 0; m < sp.M; m++) {
-    const int n = sp.seq[m].len + 1;
-    if (n > kAttnChunk) P += c.KVH * ((n + kPageTokens - 1) / kPageTokens);
-  }
-  return P;
-}
-
 __device__ __forceinline__ int rg_bound(int P, int b, int nb) { return (int)(((long long)P * b + nb - 1) / nb); }
-
-// First segment whose first page is at or after page `lo` of the step.
-__device__ void rg_seek(const Ctx &c, const StepParams &sp, int lo, RgCur &r) {
-  r.pbase = r.sbase = 0;
-  rg_load_seq(sp, r, 0);
-  while (r.m >= 0) {
-    const int tot = c.KVH * r.np;
-    if (lo < r.pbase + tot) {
-      const int off = max(0, lo - r.pbase);
-      int g = off / r.np;
-      const int rem = off - g * r.np;
-      int k = (rem + r.S - 1) / r.S;
-      if (k >= r.nseg) {
-        k = 0;
-        g++;
-      }
-      if (g < c.KVH) {
-        r.g = g;
-        r.k = k;
-        r.j = 0;
-        return;
-      }
-    }
-    r.pbase += tot;
-    r.sbase += c.KVH * r.nseg;
-    rg_load_seq(sp, r, r.m + 1);
-  }
-}
 
 // Per-block state of the range loads, kept across the phases of a launch:
 // s_rg_full[j] completes when buffer j's copies land, s_rg_par bit j is the
-// parity of its next completion, s_rg_issued counts the chunks of the coming
-// attention phase already issued (into buffers 0 .. s_rg_issued-1).
+// parity of its next completion; s_rg_issued counts the chunks of the coming
+// (or running) attention phase issued so far (chunk i into buffer
+// i % kRangeBufs) and s_rg_icur is the next chunk to issue.
 __shared__ __align__(8) uint64_t s_rg_full[kRangeBufs];
-__shared__ uint32_t s_rg_par;
+__shared__ __align__(8) uint64_t s_rg_mbar;  // merge copies
+__shared__ uint32_t s_rg_par, s_rg_mpar;
 __shared__ int s_rg_issued;
+__shared__ RgCur s_rg_icur;
 
 __device__ __forceinline__ void rg_block_init() {
   if (threadIdx.x == 0) {
     for (int j = 0; j < kRangeBufs; j++) mbar_init(&s_rg_full[j], 1);
+    mbar_init(&s_rg_mbar, 1);
     mbar_fence_init();
     s_rg_par = 0;
+    s_rg_mpar = 0;
     s_rg_issued = 0;
   }
 }
 
+// All threads, once per launch (after the step parameters are in shared
+// memory and rg_block_init): the geometry tables, this block's range and its
+// pool pages.  The block takes the segments whose first page lies in
+// [ceil(P b / nb), ceil(P (b+1) / nb)).
+__device__ void rg_launch_init(const Ctx &c) {
+  const StepParams &sp = *c.sp;
+  for (int m = threadIdx.x; m < sp.M; m += kThreads) {
+    const int n = sp.seq[m].len + 1;
+    const int np = n > kAttnChunk ? (n + kPageTokens - 1) / kPageTokens : 0;
+    const int S = np ? rg_seg_pages(np) : 1;
+    s_rg_np[m] = np;
+    s_rg_S[m] = S;
+    s_rg_nseg[m] = np ? (np + S - 1) / S : 0;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int pb = 0, sb = 0, ne = 0, smax = 1;
+    for (int m = 0; m < sp.M; m++) {
+      s_rg_pbase[m] = pb;
+      s_rg_sbase[m] = sb;
+      pb += c.KVH * s_rg_np[m];
+      sb += c.KVH * s_rg_nseg[m];
+      smax = max(smax, s_rg_S[m]);
+      if (s_rg_np[m] == 0) s_ex_m[ne++] = m;
+    }
+    s_ex_n = ne;
+    s_rg_pbase[sp.M] = pb;
+    s_rg_sbase[sp.M] = sb;
+    const int lo = rg_bound(pb, blockIdx.x, gridDim.x);
+    const int hi = rg_bound(pb, blockIdx.x + 1, gridDim.x);
+    s_rg_hi = hi;
+    // first segment starting at or after page lo
+    RgCur r;
+    rg_load_seq(sp, r, 0);
+    while (r.m >= 0) {
+      const int tot = c.KVH * r.np;
+      if (lo < r.pbase + tot) {
+        const int off = max(0, lo - r.pbase);
+        int g = off / r.np;
+        const int rem = off - g * r.np;
+        int k = (rem + r.S - 1) / r.S;
+        if (k >= r.nseg) {
+          k = 0;
+          g++;
+        }
+        if (g < c.KVH) {
+          r.g = g;
+          r.k = k;
+          r.j = 0;
+          break;
+        }
+      }
+      rg_load_seq(sp, r, r.m + 1);
+    }
+    s_rg_first = r;
+    s_rg_icur = r;
+    // pages of the block's segments: from the first one's start to at most
+    // the largest segment past the end of the range
+    const int p0 = rg_in(r, hi) ? rg_start(r) : pb;
+    s_rg_p0 = p0;
+    s_rg_npg = min(kRgPgCap, max(0, min(pb, hi + smax) - p0));
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < s_rg_npg; i += kThreads) {
+    const int o = s_rg_p0 + i;
+    int lo = 0, hi = sp.M - 1;  // last sequence with pbase <= o (binary search)
+    while (lo < hi) {
+      const int mid = (lo + hi + 1) >> 1;
+      if (s_rg_pbase[mid] <= o) lo = mid;
+      else hi = mid - 1;
+    }
+    const int rem = o - s_rg_pbase[lo];
+    const int p = rem % s_rg_np[lo];
+    s_rg_pg[i] = __ldg(sp.seq[lo].bt + p);
+  }
+}
+
+// Per-block time stamp i (thread 0; the last layer's values remain):
+// 0 phase entry, 1 long-cache part entry, 2 first copies issued, 3 first
+// segment's rows landed, 4 q rotated, 5 first chunk landed, 6 its scores,
+// 7 first segment's chunks done, 8 arrival counted, 9 phase done; 10-13 the
+// second chunk: start, landed, scores, softmax; 14 chunks * 1000 + runs,
+// 15 merges * 1000 + their segments.
+__device__ __forceinline__ void rg_bmark(const Ctx &c, int i) {
+  if (c.trace && threadIdx.x == 0) c.trace[4 * kTraceRows + kTraceMarks * blockIdx.x + i] = gtimer();
+}
+
+// Pool page of the block's range page o (global page order), from the table
+// or the block table.
+__device__ __forceinline__ int rg_pool_page(const StepParams &sp, const RgCur &r, int o) {
+  const int i = o - s_rg_p0;
+  if (i >= 0 && i < s_rg_npg) return s_rg_pg[i];
+  return __ldg(sp.seq[r.m].bt + (o - r.pbase) % r.np);
+}
+
+// K rows then V rows of (layer, kv head g) in pool page `page`: 16 KB.
+__device__ __forceinline__ const float *rg_page_kv(const Ctx &c, int page, int layer, int g) {
+  return c.kv_pool + (size_t)page * c.page_floats + ((size_t)layer * c.KVH + g) * 2 * kPageTokens * c.D;
+}
+// Row of position t (0..31) of a chunk buffer: page t / 16 of the chunk at
+// 32 rows per page, K rows first.
+__device__ __forceinline__ float *rg_row(float *buf, int t, int kind) {
+  return buf + (size_t)(((t >> 4) * 2 + kind) * kPageTokens + (t & 15)) * kHeadDim;
+}
+
+// One thread: issues chunks while fewer than `upto` have been issued and the
+// block's range has more (chunk i into buffer i % kRangeBufs).
+__device__ void rg_issue_upto(const Ctx &c, int layer, float *smem, int upto) {
+  const StepParams &sp = *c.sp;
+  const int hi = s_rg_hi;
+  RgCur r = s_rg_icur;
+  int i = s_rg_issued;
+  if (i >= upto || !rg_in(r, hi)) return;
+  // before a phase's first copy: the buffers were last written by ordinary
+  // stores in earlier phases (later, the threads that patch a chunk fence
+  // their own stores; reads need no fence before a copy overwrites them)
+  if (i == 0) asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  constexpr uint32_t pb = 2u * kPageTokens * kHeadDim * 4;  // K and V rows of one page
+  for (; i < upto && rg_in(r, hi); i++) {
+    const int b = i % kRangeBufs;
+    float *buf = rg_buf(c, sp.M, smem, b);
+    const int o = rg_start(r) + 2 * r.j;
+    const bool two = r.k * r.S + rg_seg_np(r) - (r.k * r.S + 2 * r.j) >= 2;
+    const int pg0 = rg_pool_page(sp, r, o);
+    const int pg1 = two ? rg_pool_page(sp, r, o + 1) : 0;
+    uint64_t *bar = &s_rg_full[b];
+    if (i == 4) rg_bmark(c, 19);
+    mbar_expect_tx(bar, (two ? 2u : 1u) * pb);
+    if (i == 4) rg_bmark(c, 20);
+    bulk_g2s(buf, rg_page_kv(c, pg0, layer, r.g), pb, bar);
+    if (i == 4) rg_bmark(c, 21);
+    if (two) bulk_g2s(buf + 2 * kPageTokens * kHeadDim, rg_page_kv(c, pg1, layer, r.g), pb, bar);
+    if (i == 4) rg_bmark(c, 22);
+    rg_next_chunk(c, sp, r);
+  }
+  s_rg_icur = r;
+  s_rg_issued = i;
+}
+
 // Waits for range copies issued ahead of a phase that did not run (thread 0).
 __device__ __forceinline__ void rg_drain(const Ctx &c) {
-  for (int j = 0; j < s_rg_issued; j++) {
+  for (int j = 0; j < s_rg_issued && j < kRangeBufs; j++) {
     mbar_wait(&s_rg_full[j], (s_rg_par >> j) & 1u, c.err);
     s_rg_par ^= 1u << j;
   }
   s_rg_issued = 0;
+  s_rg_icur = s_rg_first;
 }
 
-// One thread: bulk copies of chunk r's K and V pages into buf.
-__device__ __forceinline__ void rg_issue(const Ctx &c, int layer, const RgCur &r, float *buf, uint64_t *bar) {
-  const int *bt = c.sp->seq[r.m].bt;
-  const int p = r.k * r.S + 2 * r.j;
-  const int pages = min(2, r.k * r.S + rg_seg_np(r) - p);
-  constexpr uint32_t pb = (uint32_t)kPageTokens * kHeadDim * 4;
-  mbar_expect_tx(bar, 2u * pages * pb);
-  for (int q = 0; q < pages; q++) {
-    bulk_g2s(buf + q * kPageTokens * kHeadDim, kv_ptr(c, bt, layer, 0, r.g, (p + q) * kPageTokens), pb, bar);
-    bulk_g2s(buf + (kRangeTok + q * kPageTokens) * kHeadDim, kv_ptr(c, bt, layer, 1, r.g, (p + q) * kPageTokens), pb,
-             bar);
-  }
-}
 
-// One thread: issues this block's chunks s_rg_issued .. upto-1 (chunk i into
-// buffer i); r is left at the next chunk to issue and i at its index.
-__device__ void rg_issue_ahead(const Ctx &c, int layer, float *smem, int upto, RgCur &r, int &i) {
-  const StepParams &sp = *c.sp;
-  const int P = rg_total_pages(c, sp);
-  i = 0;
-  r.m = -1;
-  if (P == 0) return;
-  const int hi = rg_bound(P, blockIdx.x + 1, gridDim.x);
-  rg_seek(c, sp, rg_bound(P, blockIdx.x, gridDim.x), r);
-  for (; i < s_rg_issued && rg_in(r, hi); i++) rg_next_chunk(c, sp, r);
-  // the buffers were last touched by ordinary loads and stores
-  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-  for (; i < upto && rg_in(r, hi); i++) {
-    rg_issue(c, layer, r, rg_buf(c, sp.M, smem, i), &s_rg_full[i]);
-    rg_next_chunk(c, sp, r);
-  }
-  s_rg_issued = i;
-}
-
-// All threads: cp.async copies of segment r's raw q (G heads), its new k and
-// v (last segment of the pair) and the cos / sin of the sequence's position.
-__device__ __forceinline__ void rg_prefetch_seg(const Ctx &c, const StepParams &sp, const RgCur &r, float *pre) {
+// All threads: cp.async copies of the raw q (G heads), new k and v of pair
+// (r.m, r.g) and the cos / sin of the sequence's position.
+__device__ __forceinline__ void rg_prefetch_run(const Ctx &c, const StepParams &sp, const RgCur &r, float *pre) {
   const int G = c.QH / c.KVH;
   const size_t qkvld = (size_t)(c.QH + 2 * c.KVH) * kHeadDim;
   const float *row = c.qkv + (size_t)r.m * qkvld;
   const int t = threadIdx.x;
   if (t < G * 32) cp_async16(pre + 4 * t, row + (size_t)r.g * G * kHeadDim + 4 * t);
-  if (r.k == r.nseg - 1 && t < 64) {
+  if (t < 64) {
     const int kind = t >> 5, i4 = t & 31;
     cp_async16(pre + 1024 + 128 * kind + 4 * i4, row + (size_t)(c.QH + kind * c.KVH + r.g) * kHeadDim + 4 * i4);
   }
-  if (t >= 128 && t < 256) {
+  if (t >= 128 && t < 256 && !(s_rope_ready && r.m < kMaxBatch)) {
     const int i = (t - 128) & 63;
     const int p = sp.seq[r.m].pos[c.sec_axis[i]];
     const float *tab = t < 192 ? c.rope_cos : c.rope_sin;
@@ -251,43 +340,61 @@ __device__ __forceinline__ void rg_prefetch_seg(const Ctx &c, const StepParams &
   asm volatile("cp.async.commit_group;" ::: "memory");
 }
 
-// Warps h < G of the block that completed (m, g): merge head h's segments.
-__device__ void rg_merge(const Ctx &c, int m, int g, int n, int sb, int nseg) {
+// All threads of the block that completed pair (m, g): its segments'
+// partials (o [nseg][G][128], maxima / sums [nseg][G][2], the tail sums
+// [G][128]) arrive by bulk copies in `stage` (nseg * 4 KB <= 128 KB) and
+// `aux`; warp h merges head h, lane dims 4 lane .. 4 lane + 3.
+__device__ __forceinline__ void rg_merge(const Ctx &c, int m, int g, int n, int sb, int nseg, float *stage, float *aux) {
   const int G = c.QH / c.KVH;
   const int h = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  if (h >= G) return;
-  const float *ml = c.part_ml + ((size_t)sb * G + h) * 2;  // segment k at + 2 G k
-  const float mk = lane < nseg ? __ldcg(ml + (size_t)2 * G * lane) : -INFINITY;
-  const float lk = lane < nseg ? __ldcg(ml + (size_t)2 * G * lane + 1) : 0.0f;
-  float mx = mk;
-  for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-  const float sk = lane < nseg ? exp_fma(__fsub_rn(mk, mx)) : 0.0f;
-  float den = __fmul_rn(sk, lk);
-  for (int o = 16; o > 0; o >>= 1) den = __fadd_rn(den, __shfl_xor_sync(0xffffffffu, den, o));
-  const size_t hq = (size_t)m * c.QH + (size_t)g * G + h;
-  float4 acc = (n & 15) ? __ldcg((const float4 *)(c.part_t + hq * kHeadDim) + lane) : make_float4(0.f, 0.f, 0.f, 0.f);
-  const float4 *po = (const float4 *)(c.part_o + ((size_t)sb * G + h) * kHeadDim) + lane;
-  const size_t pstride = (size_t)G * (kHeadDim / 4);  // float4 per segment
-#pragma unroll 1
-  for (int k0 = 0; k0 < nseg; k0 += 8) {
-    float4 v[8];
-#pragma unroll
-    for (int u = 0; u < 8; u++)
-      if (k0 + u < nseg) v[u] = __ldcg(po + (size_t)(k0 + u) * pstride);
-#pragma unroll
-    for (int u = 0; u < 8; u++) {
-      const float s = __shfl_sync(0xffffffffu, sk, (k0 + u) & 31);
-      if (k0 + u < nseg) {
-        acc.x = __fmaf_rn(s, v[u].x, acc.x);
-        acc.y = __fmaf_rn(s, v[u].y, acc.y);
-        acc.z = __fmaf_rn(s, v[u].z, acc.z);
-        acc.w = __fmaf_rn(s, v[u].w, acc.w);
-      }
-    }
+  const size_t hq0 = (size_t)m * c.QH + (size_t)g * G;
+  const bool tail = (n & 15) != 0;
+  float *mls = aux, *ts = aux + 2 * kSegMax * kMaxGroup;  // [nseg][G][2], [G][128]
+  if (threadIdx.x == 0) {
+    // partials of other blocks (released with their arrival counts, which
+    // this block acquired) are read through the async proxy
+    asm volatile("fence.proxy.async.global;" ::: "memory");
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    const uint32_t ob = (uint32_t)(nseg * G * kHeadDim * 4), mb = (uint32_t)(nseg * G * 8),
+                   tb = tail ? (uint32_t)(G * kHeadDim * 4) : 0u;
+    mbar_expect_tx(&s_rg_mbar, ob + mb + tb);
+    bulk_g2s(stage, c.part_o + (size_t)sb * G * kHeadDim, ob, &s_rg_mbar);
+    bulk_g2s(mls, c.part_ml + (size_t)sb * G * 2, mb, &s_rg_mbar);
+    if (tail) bulk_g2s(ts, c.part_t + hq0 * kHeadDim, tb, &s_rg_mbar);
   }
-  const float di = __fdiv_rn(1.0f, den);
-  ((float4 *)(c.head + hq * kHeadDim))[lane] =
-      make_float4(__fmul_rn(acc.x, di), __fmul_rn(acc.y, di), __fmul_rn(acc.z, di), __fmul_rn(acc.w, di));
+  mbar_wait(&s_rg_mbar, s_rg_mpar, c.err);
+  if (h < G) {
+    const float mk = lane < nseg ? mls[(lane * G + h) * 2] : -INFINITY;
+    const float lk = lane < nseg ? mls[(lane * G + h) * 2 + 1] : 0.0f;
+    float mx = mk;
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    const float sk = lane < nseg ? exp_fma(__fsub_rn(mk, mx)) : 0.0f;
+    float den = __fmul_rn(sk, lk);
+    for (int o = 16; o > 0; o >>= 1) den = __fadd_rn(den, __shfl_xor_sync(0xffffffffu, den, o));
+    float4 acc = tail ? ((const float4 *)(ts + h * kHeadDim))[lane] : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll 4
+    for (int u = 0; u < nseg; u++) {
+      const float s = __shfl_sync(0xffffffffu, sk, u);
+      const float4 v = ((const float4 *)(stage + ((size_t)u * G + h) * kHeadDim))[lane];
+      acc.x = __fmaf_rn(s, v.x, acc.x);
+      acc.y = __fmaf_rn(s, v.y, acc.y);
+      acc.z = __fmaf_rn(s, v.z, acc.z);
+      acc.w = __fmaf_rn(s, v.w, acc.w);
+    }
+    const float di = __fdiv_rn(1.0f, den);
+    ((float4 *)(c.head + (hq0 + h) * kHeadDim))[lane] =
+        make_float4(__fmul_rn(acc.x, di), __fmul_rn(acc.y, di), __fmul_rn(acc.z, di), __fmul_rn(acc.w, di));
+  }
+  // the stage is free again once every warp has read it
+  __syncthreads();
+  if (threadIdx.x == 0) s_rg_mpar ^= 1u;
+}
+
+// Trace (OCRVL_TRACE): latest time over the blocks at which their first
+// segment reached point i (0 q rotated, 1 chunks done, 2 arrival counted, 3
+// phase done), in trace row 200 + layer.
+__device__ __forceinline__ void rg_mark(const Ctx &c, int layer, int i) {
+  if (c.trace && threadIdx.x == 0 && layer < 26) atomicMax(c.trace + 4 * (200 + layer) + i, gtimer());
 }
 
 // Attention of the step's long caches (see the top of this file).
@@ -298,248 +405,312 @@ __device__ __noinline__ void phase_attn_range(const Ctx *cp, int layer, float *s
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int slot = lane & 15, grp = lane >> 4;
   const int d = threadIdx.x & 127, th = threadIdx.x >> 7;
-  const int P = rg_total_pages(c, sp);
-  if (P == 0) return;
-  const int hi = rg_bound(P, blockIdx.x + 1, gridDim.x);
+  rg_bmark(c, 1);
+  const int hi = s_rg_hi;
   float *sm = rg_small(c, sp.M, smem);
   float *qs = sm + kRgQs, *S = sm + kRgS, *W = sm + kRgW, *alph = sm + kRgAlpha, *red = sm + kRgRed;
   float *knew = sm + kRgKnew, *Tsm = sm + kRgT;
   __shared__ int s_merge;
-  RgCur cur;
-  rg_seek(c, sp, rg_bound(P, blockIdx.x, gridDim.x), cur);
+  RgCur cur = s_rg_first;
+  if (threadIdx.x == 0) ((int *)(sm + kRgMerge))[0] = 0;
   if (!rg_in(cur, hi)) return;
-  // thread 0: the issue cursor (next chunk to copy) and its index
-  RgCur icur;
-  int inext = 0;
-  if (threadIdx.x == 0) rg_issue_ahead(c, layer, smem, kRangeBufs, icur, inext);
-  rg_prefetch_seg(c, sp, cur, sm + kRgPre);
+  if (threadIdx.x == 0) rg_issue_upto(c, layer, smem, kRangeBufs);
+  rg_bmark(c, 2);
+  rg_prefetch_run(c, sp, cur, sm + kRgPre);
   int ci = 0;    // chunk index in the block's stream
-  int sidx = 0;  // segment index in the block's stream
+  int ridx = 0;  // run index in the block's stream
   while (rg_in(cur, hi)) {
-    // ---- segment start: rotated q (and new k) from the prefetched rows
-    const float *pre = sm + kRgPre + (sidx & 1) * kRgPreLen;
+    // ---- run start (the block's consecutive segments of one pair): rotated
+    // q and new k from the prefetched rows
+    const float *pre = sm + kRgPre + (ridx & 1) * kRgPreLen;
     asm volatile("cp.async.wait_all;" ::: "memory");
     __syncthreads();
+    if (ridx == 0) rg_bmark(c, 3);
     const int m = cur.m, g = cur.g, n = cur.n, len = n - 1, nv = n & ~15;
-    const bool last_seg = cur.k == cur.nseg - 1;
-    const int *pos = sp.seq[m].pos;
-    const bool has_rope = pos[0] != 0 || pos[1] != 0 || pos[2] != 0;
-    const float *rc = pre + 1280, *rs = pre + 1344;
-    for (int p = threadIdx.x; p < G * 16 + (last_seg ? 48 : 0); p += kThreads) {
-      if (p < G * 16) {
-        const int hh = p >> 4, i4 = p & 15;
-        float4 a = ((const float4 *)(pre + hh * kHeadDim))[i4], b = ((const float4 *)(pre + hh * kHeadDim + 64))[i4];
-        if (has_rope) rope4(a, b, rc + 4 * i4, rs + 4 * i4);
-        ((float4 *)(qs + hh * kHeadDim))[i4] = a;
-        ((float4 *)(qs + hh * kHeadDim + 64))[i4] = b;
-      } else if (p < G * 16 + 16) {
-        const int i4 = p - G * 16;
-        float4 a = ((const float4 *)(pre + 1024))[i4], b = ((const float4 *)(pre + 1024 + 64))[i4];
-        if (has_rope) rope4(a, b, rc + 4 * i4, rs + 4 * i4);
-        ((float4 *)knew)[i4] = a;
-        ((float4 *)knew)[i4 + 16] = b;
-      } else {
-        const int i4 = p - G * 16 - 16;
-        ((float4 *)(knew + 128))[i4] = ((const float4 *)(pre + 1152))[i4];
+    // segments k0 .. k1-1 of the pair are this block's (first page < hi)
+    const int k0 = cur.k;
+    const int k1 = min(cur.nseg, (hi - cur.pbase - g * cur.np + cur.S - 1) / cur.S);
+    {
+      const int *pos = sp.seq[m].pos;
+      const bool has_rope = pos[0] != 0 || pos[1] != 0 || pos[2] != 0;
+      const bool tab = s_rope_ready && m < kMaxBatch;  // the launch's RoPE tables hold sequence m
+      const float *rc = tab ? s_rope_cs[m] : pre + 1280, *rs = tab ? s_rope_sn[m] : pre + 1344;
+      for (int p = threadIdx.x; p < G * 16 + 48; p += kThreads) {
+        if (p < G * 16) {
+          const int hh = p >> 4, i4 = p & 15;
+          float4 a = ((const float4 *)(pre + hh * kHeadDim))[i4], b = ((const float4 *)(pre + hh * kHeadDim + 64))[i4];
+          if (has_rope) rope4(a, b, rc + 4 * i4, rs + 4 * i4);
+          ((float4 *)(qs + hh * kHeadDim))[i4] = a;
+          ((float4 *)(qs + hh * kHeadDim + 64))[i4] = b;
+        } else if (p < G * 16 + 16) {
+          const int i4 = p - G * 16;
+          float4 a = ((const float4 *)(pre + 1024))[i4], b = ((const float4 *)(pre + 1024 + 64))[i4];
+          if (has_rope) rope4(a, b, rc + 4 * i4, rs + 4 * i4);
+          ((float4 *)knew)[i4] = a;
+          ((float4 *)knew)[i4 + 16] = b;
+        } else {
+          const int i4 = p - G * 16 - 16;
+          ((float4 *)(knew + 128))[i4] = ((const float4 *)(pre + 1152))[i4];
+        }
       }
     }
     __syncthreads();
-    RgCur nxt = cur;
+    if (ridx == 0) {
+      rg_mark(c, layer, 0);
+      rg_bmark(c, 4);
+    }
+    RgCur nxt = cur;  // the next run: the first segment after this run
+    nxt.k = k1 - 1;
     rg_next_seg(c, sp, nxt);
-    if (rg_in(nxt, hi)) rg_prefetch_seg(c, sp, nxt, sm + kRgPre + ((sidx + 1) & 1) * kRgPreLen);
-    float qr[8][8];
-#pragma unroll
-    for (int h = 0; h < 8; h++)
-#pragma unroll
-      for (int jj = 0; jj < 8; jj++) qr[h][jj] = h < G ? qs[h * kHeadDim + 16 * (jj ^ grp) + slot] : 0.0f;
-    float m_run = -INFINITY, l_run = 0.0f;  // warp h < G: head h
-    float o[8];
-#pragma unroll
-    for (int h = 0; h < 8; h++) o[h] = 0.0f;
-    const int seg_np = rg_seg_np(cur);
-    const int nck = (seg_np + 1) / 2;
-    const int sp0 = cur.k * cur.S;  // first page of the segment
+    if (rg_in(nxt, hi)) rg_prefetch_run(c, sp, nxt, sm + kRgPre + ((ridx + 1) & 1) * kRgPreLen);
 #pragma unroll 1
-    for (int j = 0; j < nck; j++, ci++) {
-      const int b = ci % kRangeBufs;
-      float *Kb = rg_buf(c, sp.M, smem, b), *Vb = Kb + kRangeTok * kHeadDim;
-      const int p0 = sp0 + 2 * j;
-      const int t0 = p0 * kPageTokens;
-      const int cnt = min(min(2, sp0 + seg_np - p0) * kPageTokens, n - t0);
-      mbar_wait(&s_rg_full[b], (s_rg_par >> b) & 1u, c.err);
-      if (t0 <= len && len < t0 + cnt) {
-        // the new token: appended to the cache (kvCache.append,
-        // internal/model/model.go:5593-5612) and patched into the chunk
-        if (threadIdx.x < 64) {
-          const int kind = threadIdx.x >> 5, i4 = threadIdx.x & 31;
-          const float4 v = ((const float4 *)(knew + kind * 128))[i4];
-          ((float4 *)((kind ? Vb : Kb) + (size_t)(len - t0) * kHeadDim))[i4] = v;
-          ((float4 *)kv_ptr(c, sp.seq[m].bt, layer, kind, g, len))[i4] = v;
+    for (int k = k0; k < k1; k++) {
+      cur.k = k;
+      const bool last_seg = k == cur.nseg - 1;
+      float m_run = -INFINITY, l_run = 0.0f;  // warp h < G: head h
+      float o[8];
+#pragma unroll
+      for (int h = 0; h < 8; h++) o[h] = 0.0f;
+      const int seg_np = rg_seg_np(cur);
+      const int nck = (seg_np + 1) / 2;
+      const int sp0 = k * cur.S;  // first page of the segment
+#pragma unroll 1
+      for (int j = 0; j < nck; j++, ci++) {
+        const int b = ci % kRangeBufs;
+        float *Kb = rg_buf(c, sp.M, smem, b);  // rows by rg_row
+        const int p0 = sp0 + 2 * j;
+        const int t0 = p0 * kPageTokens;
+        const int cnt = min(min(2, sp0 + seg_np - p0) * kPageTokens, n - t0);
+        if (ci == 1) rg_bmark(c, 10);
+        mbar_wait(&s_rg_full[b], (s_rg_par >> b) & 1u, c.err);
+        if (ci == 0) rg_bmark(c, 5);
+        if (ci == 1) rg_bmark(c, 11);
+        if (t0 <= len && len < t0 + cnt) {
+          // the new token: appended to the cache (kvCache.append,
+          // internal/model/model.go:5593-5612) and patched into the chunk
+          if (threadIdx.x < 64) {
+            const int kind = threadIdx.x >> 5, i4 = threadIdx.x & 31;
+            const float4 v = ((const float4 *)(knew + kind * 128))[i4];
+            ((float4 *)rg_row(Kb, len - t0, kind))[i4] = v;
+            ((float4 *)kv_ptr(c, sp.seq[m].bt, layer, kind, g, len))[i4] = v;
+            // a later copy into this buffer must not overtake the store
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+          }
+          __syncthreads();
+        }
+        // ---- scores, heads in two groups of four: lane slot s of half grp
+        // holds dims s + 16 j of the group's q (j read as j ^ grp) and of the
+        // tokens 4 warp + 2 grp + {0, 1}; the reduce-scatter over the slots
+        // leaves value (token bit b3, head 2 b2 + b1) on the lane pair b0
+#pragma unroll
+        for (int hg = 0; hg < 2; hg++) {
+          float part[8];
+          float qr[4][8];
+#pragma unroll
+          for (int h4 = 0; h4 < 4; h4++)
+#pragma unroll
+            for (int jj = 0; jj < 8; jj++)
+              qr[h4][jj] = 4 * hg + h4 < G ? qs[(4 * hg + h4) * kHeadDim + 16 * (jj ^ grp) + slot] : 0.0f;
+#pragma unroll
+          for (int tl = 0; tl < 2; tl++) {
+            const float *kr = rg_row(Kb, 4 * warp + 2 * grp + tl, 0);
+            float kk[8];
+#pragma unroll
+            for (int jj = 0; jj < 8; jj++) kk[jj] = kr[16 * (jj ^ grp) + slot];
+#pragma unroll
+            for (int h4 = 0; h4 < 4; h4++) {
+              float pr[8];
+#pragma unroll
+              for (int jj = 0; jj < 8; jj++) pr[jj] = __fmul_rn(qr[h4][jj], kk[jj]);
+              part[tl * 4 + h4] = __fadd_rn(__fadd_rn(__fadd_rn(pr[0], pr[1]), __fadd_rn(pr[2], pr[3])),
+                                            __fadd_rn(__fadd_rn(pr[4], pr[5]), __fadd_rn(pr[6], pr[7])));
+            }
+          }
+#pragma unroll
+          for (int i = 0; i < 4; i++) {
+            const bool up = lane & 8;
+            const float send = up ? part[i] : part[4 + i];
+            part[i] = __fadd_rn(up ? part[4 + i] : part[i], __shfl_xor_sync(0xffffffffu, send, 8));
+          }
+#pragma unroll
+          for (int i = 0; i < 2; i++) {
+            const bool up = lane & 4;
+            const float send = up ? part[i] : part[2 + i];
+            part[i] = __fadd_rn(up ? part[2 + i] : part[i], __shfl_xor_sync(0xffffffffu, send, 4));
+          }
+          {
+            const bool up = lane & 2;
+            const float send = up ? part[0] : part[1];
+            part[0] = __fadd_rn(up ? part[1] : part[0], __shfl_xor_sync(0xffffffffu, send, 2));
+          }
+          const float r = __fadd_rn(part[0], __shfl_xor_sync(0xffffffffu, part[0], 1));
+          if (!(lane & 1))
+            S[(4 * hg + ((slot >> 1) & 3)) * 32 + 4 * warp + 2 * grp + (slot >> 3)] = __fmul_rn(r, c.attn_scale);
         }
         __syncthreads();
-      }
-      // ---- scores
-      {
-        float part[16];
-#pragma unroll
-        for (int tl = 0; tl < 2; tl++) {
-          const float *kr = Kb + (size_t)(4 * warp + 2 * grp + tl) * kHeadDim;
-          float kk[8];
-#pragma unroll
-          for (int jj = 0; jj < 8; jj++) kk[jj] = kr[16 * (jj ^ grp) + slot];
-#pragma unroll
-          for (int h = 0; h < 8; h++) {
-            float pr[8];
-#pragma unroll
-            for (int jj = 0; jj < 8; jj++) pr[jj] = __fmul_rn(qr[h][jj], kk[jj]);
-            part[tl * 8 + h] = __fadd_rn(__fadd_rn(__fadd_rn(pr[0], pr[1]), __fadd_rn(pr[2], pr[3])),
-                                         __fadd_rn(__fadd_rn(pr[4], pr[5]), __fadd_rn(pr[6], pr[7])));
-          }
+        if (ci == 0) rg_bmark(c, 6);
+        if (ci == 1) rg_bmark(c, 12);
+        if (threadIdx.x == 0) {
+          s_rg_par ^= 1u << b;
+          // every thread is past the previous chunk: its buffer takes the next copy
+          if (ci == 1) rg_bmark(c, 16);
+          rg_issue_upto(c, layer, smem, ci + kRangeBufs);
+          if (ci == 1) rg_bmark(c, 17);
         }
-        // reduce-scatter over the slots: lane keeps value (slot) = token
-        // half (slot >> 3), head (slot & 7)
-#pragma unroll
-        for (int i = 0; i < 8; i++) {
-          const bool up = lane & 8;
-          const float send = up ? part[i] : part[8 + i];
-          part[i] = __fadd_rn(up ? part[8 + i] : part[i], __shfl_xor_sync(0xffffffffu, send, 8));
+        // ---- online softmax, warp h = head h
+        if (warp < G) {
+          const float s = S[warp * 32 + lane];
+          const bool valid = lane < cnt;
+          float pm = valid ? s : -INFINITY;
+          for (int o2 = 16; o2 > 0; o2 >>= 1) pm = fmaxf(pm, __shfl_xor_sync(0xffffffffu, pm, o2));
+          const float m_new = fmaxf(m_run, pm);
+          const float alpha = m_run == -INFINITY ? 0.0f : exp_fma(__fsub_rn(m_run, m_new));
+          const bool raw = t0 + lane >= nv;
+          float e = 0.0f;
+          if (valid) e = raw ? s : exp_fma(__fsub_rn(s, m_new));
+          float le = valid && !raw ? e : 0.0f;
+          for (int o2 = 16; o2 > 0; o2 >>= 1) le = __fadd_rn(le, __shfl_xor_sync(0xffffffffu, le, o2));
+          l_run = __fadd_rn(__fmul_rn(l_run, alpha), le);
+          m_run = m_new;
+          W[lane * 8 + warp] = e;
+          if (lane == 0) alph[warp] = alpha;
         }
-#pragma unroll
-        for (int i = 0; i < 4; i++) {
-          const bool up = lane & 4;
-          const float send = up ? part[i] : part[4 + i];
-          part[i] = __fadd_rn(up ? part[4 + i] : part[i], __shfl_xor_sync(0xffffffffu, send, 4));
-        }
-#pragma unroll
-        for (int i = 0; i < 2; i++) {
-          const bool up = lane & 2;
-          const float send = up ? part[i] : part[2 + i];
-          part[i] = __fadd_rn(up ? part[2 + i] : part[i], __shfl_xor_sync(0xffffffffu, send, 2));
-        }
+        if (ci == 1) rg_bmark(c, 18);
+        __syncthreads();
+        if (ci == 1) rg_bmark(c, 13);
+        // ---- values: thread (d, th), tokens th*16 .. th*16+15 of the chunk
         {
-          const bool up = lane & 1;
-          const float send = up ? part[0] : part[1];
-          part[0] = __fadd_rn(up ? part[1] : part[0], __shfl_xor_sync(0xffffffffu, send, 1));
-        }
-        S[(slot & 7) * 32 + 4 * warp + 2 * grp + (slot >> 3)] = __fmul_rn(part[0], c.attn_scale);
-      }
-      __syncthreads();
-      if (threadIdx.x == 0) {
-        s_rg_par ^= 1u << b;
-        // every thread is past the previous chunk: its buffer takes the next copy
-        while (inext <= ci - 1 + kRangeBufs && rg_in(icur, hi)) {
-          asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-          const int bb = inext % kRangeBufs;
-          rg_issue(c, layer, icur, rg_buf(c, sp.M, smem, bb), &s_rg_full[bb]);
-          rg_next_chunk(c, sp, icur);
-          inext++;
-        }
-      }
-      // ---- online softmax, warp h = head h
-      if (warp < G) {
-        const float s = S[warp * 32 + lane];
-        const bool valid = lane < cnt;
-        float pm = valid ? s : -INFINITY;
-        for (int o2 = 16; o2 > 0; o2 >>= 1) pm = fmaxf(pm, __shfl_xor_sync(0xffffffffu, pm, o2));
-        const float m_new = fmaxf(m_run, pm);
-        const float alpha = m_run == -INFINITY ? 0.0f : exp_fma(__fsub_rn(m_run, m_new));
-        const bool raw = t0 + lane >= nv;
-        float e = 0.0f;
-        if (valid) e = raw ? s : exp_fma(__fsub_rn(s, m_new));
-        float le = valid && !raw ? e : 0.0f;
-        for (int o2 = 16; o2 > 0; o2 >>= 1) le = __fadd_rn(le, __shfl_xor_sync(0xffffffffu, le, o2));
-        l_run = __fadd_rn(__fmul_rn(l_run, alpha), le);
-        m_run = m_new;
-        W[lane * 8 + warp] = e;
-        if (lane == 0) alph[warp] = alpha;
-      }
-      __syncthreads();
-      // ---- values: thread (d, th), tokens th*16 .. th*16+15 of the chunk
-      {
-        float av[8];
+          float av[8];
 #pragma unroll
-        for (int h = 0; h < 8; h++) av[h] = h < G ? alph[h] : 0.0f;
+          for (int h = 0; h < 8; h++) av[h] = h < G ? alph[h] : 0.0f;
 #pragma unroll
-        for (int h = 0; h < 8; h++) o[h] = __fmul_rn(o[h], av[h]);
-        const int tb = th * 16, te = min(cnt, tb + 16);
-        const int tt = min(max(nv - t0, tb), te);  // [tb, tt) exponentiated, [tt, te) raw
+          for (int h = 0; h < 8; h++) o[h] = __fmul_rn(o[h], av[h]);
+          const int tb = th * 16, te = min(cnt, tb + 16);
+          const int tt = min(max(nv - t0, tb), te);  // [tb, tt) exponentiated, [tt, te) raw
+          const float *Vb = rg_row(Kb, tb, 1) - (size_t)tb * kHeadDim;  // row t of this half at Vb + t * D
 #pragma unroll 4
-        for (int t = tb; t < tt; t++) {
-          const float v = Vb[(size_t)t * kHeadDim + d];
-          const float4 w0 = ((const float4 *)(W + t * 8))[0], w1 = ((const float4 *)(W + t * 8))[1];
-          o[0] = __fmaf_rn(w0.x, v, o[0]);
-          o[1] = __fmaf_rn(w0.y, v, o[1]);
-          o[2] = __fmaf_rn(w0.z, v, o[2]);
-          o[3] = __fmaf_rn(w0.w, v, o[3]);
-          o[4] = __fmaf_rn(w1.x, v, o[4]);
-          o[5] = __fmaf_rn(w1.y, v, o[5]);
-          o[6] = __fmaf_rn(w1.z, v, o[6]);
-          o[7] = __fmaf_rn(w1.w, v, o[7]);
-        }
-        if (t0 + cnt > nv) {
-          // the chunk holding the positions at or above nv (the last one of
-          // the pair): this half's raw-weighted sums, zero when it has none
-          float ta[8];
-#pragma unroll
-          for (int h = 0; h < 8; h++) ta[h] = 0.0f;
-#pragma unroll 1
-          for (int t = tt; t < te; t++) {
+          for (int t = tb; t < tt; t++) {
             const float v = Vb[(size_t)t * kHeadDim + d];
             const float4 w0 = ((const float4 *)(W + t * 8))[0], w1 = ((const float4 *)(W + t * 8))[1];
-            ta[0] = __fmaf_rn(w0.x, v, ta[0]);
-            ta[1] = __fmaf_rn(w0.y, v, ta[1]);
-            ta[2] = __fmaf_rn(w0.z, v, ta[2]);
-            ta[3] = __fmaf_rn(w0.w, v, ta[3]);
-            ta[4] = __fmaf_rn(w1.x, v, ta[4]);
-            ta[5] = __fmaf_rn(w1.y, v, ta[5]);
-            ta[6] = __fmaf_rn(w1.z, v, ta[6]);
-            ta[7] = __fmaf_rn(w1.w, v, ta[7]);
+            o[0] = __fmaf_rn(w0.x, v, o[0]);
+            o[1] = __fmaf_rn(w0.y, v, o[1]);
+            o[2] = __fmaf_rn(w0.z, v, o[2]);
+            o[3] = __fmaf_rn(w0.w, v, o[3]);
+            o[4] = __fmaf_rn(w1.x, v, o[4]);
+            o[5] = __fmaf_rn(w1.y, v, o[5]);
+            o[6] = __fmaf_rn(w1.z, v, o[6]);
+            o[7] = __fmaf_rn(w1.w, v, o[7]);
           }
+          if (t0 + cnt > nv) {
+            // the chunk holding the positions at or above nv (the last one of
+            // the pair): this half's raw-weighted sums, zero when it has none
+            float ta[8];
 #pragma unroll
-          for (int h = 0; h < 8; h++) Tsm[th * 1024 + h * kHeadDim + d] = ta[h];
+            for (int h = 0; h < 8; h++) ta[h] = 0.0f;
+#pragma unroll 1
+            for (int t = tt; t < te; t++) {
+              const float v = Vb[(size_t)t * kHeadDim + d];
+              const float4 w0 = ((const float4 *)(W + t * 8))[0], w1 = ((const float4 *)(W + t * 8))[1];
+              ta[0] = __fmaf_rn(w0.x, v, ta[0]);
+              ta[1] = __fmaf_rn(w0.y, v, ta[1]);
+              ta[2] = __fmaf_rn(w0.z, v, ta[2]);
+              ta[3] = __fmaf_rn(w0.w, v, ta[3]);
+              ta[4] = __fmaf_rn(w1.x, v, ta[4]);
+              ta[5] = __fmaf_rn(w1.y, v, ta[5]);
+              ta[6] = __fmaf_rn(w1.z, v, ta[6]);
+              ta[7] = __fmaf_rn(w1.w, v, ta[7]);
+            }
+#pragma unroll
+            for (int h = 0; h < 8; h++) Tsm[th * 1024 + h * kHeadDim + d] = ta[h];
+          }
         }
       }
-    }
-    // ---- segment end: the partial (halves added in order), arrival, merge
-    const bool has_tail = last_seg && (n & 15) != 0;
-    const int seg = rg_seg_index(cur);
-    if (th == 1) {
+      // ---- segment end: the partial (halves added in order)
+      if (ridx == 0 && k == k0) {
+        rg_mark(c, layer, 1);
+        rg_bmark(c, 7);
+      }
+      const bool has_tail = last_seg && (n & 15) != 0;
+      const int seg = rg_seg_index(cur);
+      if (th == 1) {
 #pragma unroll
-      for (int h = 0; h < 8; h++)
-        if (h < G) red[h * kHeadDim + d] = o[h];
-    }
-    __syncthreads();
-    if (th == 0) {
+        for (int h = 0; h < 8; h++)
+          if (h < G) red[h * kHeadDim + d] = o[h];
+      }
+      __syncthreads();
+      if (th == 0) {
 #pragma unroll
-      for (int h = 0; h < 8; h++)
-        if (h < G) {
-          c.part_o[((size_t)seg * G + h) * kHeadDim + d] = __fadd_rn(o[h], red[h * kHeadDim + d]);
-          if (has_tail)
-            c.part_t[((size_t)m * c.QH + (size_t)g * G + h) * kHeadDim + d] =
-                __fadd_rn(Tsm[h * kHeadDim + d], Tsm[1024 + h * kHeadDim + d]);
-        }
+        for (int h = 0; h < 8; h++)
+          if (h < G) {
+            c.part_o[((size_t)seg * G + h) * kHeadDim + d] = __fadd_rn(o[h], red[h * kHeadDim + d]);
+            if (has_tail)
+              c.part_t[((size_t)m * c.QH + (size_t)g * G + h) * kHeadDim + d] =
+                  __fadd_rn(Tsm[h * kHeadDim + d], Tsm[1024 + h * kHeadDim + d]);
+          }
+      }
+      if (warp < G && lane == 0) {
+        c.part_ml[((size_t)seg * G + warp) * 2] = m_run;
+        c.part_ml[((size_t)seg * G + warp) * 2 + 1] = l_run;
+      }
+      // the merger reads the partials with bulk copies (async proxy)
+      asm volatile("fence.proxy.async.global;" ::: "memory");
     }
-    if (warp < G && lane == 0) {
-      c.part_ml[((size_t)seg * G + warp) * 2] = m_run;
-      c.part_ml[((size_t)seg * G + warp) * 2 + 1] = l_run;
-    }
+    // ---- run end: arrival of the run's segments, merge by the block that
+    // completes the pair
     __syncthreads();
     if (threadIdx.x == 0) {
       // release: the block's partials (ordered before by the barrier) become
       // visible with the count; acquire: the merger sees the others' partials
       unsigned *cntp = c.attn_count + 2 * (m * c.KVH + g);
       unsigned v;
-      asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(v) : "l"(cntp) : "memory");
-      s_merge = (int)v == cur.nseg - 1;
+      asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], %2;" : "=r"(v) : "l"(cntp), "r"(k1 - k0) : "memory");
+      s_merge = (int)v + (k1 - k0) == cur.nseg;
       if (s_merge) cntp[0] = 0u;
     }
     __syncthreads();
-    if (s_merge) rg_merge(c, m, g, n, cur.sbase + g * cur.nseg, cur.nseg);
+    if (ridx == 0) {
+      rg_mark(c, layer, 2);
+      rg_bmark(c, 8);
+    }
+    if (s_merge && threadIdx.x == 0) {
+      // merged after the phase (rg_merge_pending); a step has at most
+      // kRgMerges (sequence, kv head) pairs (checked on the host)
+      int *ml = (int *)(sm + kRgMerge);
+      const int q = ml[0];
+      ml[4 + 2 * q] = m | g << 8 | cur.nseg << 16;
+      ml[4 + 2 * q + 1] = cur.sbase + g * cur.nseg;
+      ml[0] = q + 1;
+      if (c.trace) c.trace[4 * kTraceRows + kTraceMarks * blockIdx.x + 15] += 1000 + cur.nseg;
+    }
     cur = nxt;
-    sidx++;
+    ridx++;
   }
-  if (threadIdx.x == 0) s_rg_issued = 0;
+  if (threadIdx.x == 0) {
+    s_rg_issued = 0;
+    s_rg_icur = s_rg_first;
+  }
   __syncthreads();
+  rg_mark(c, layer, 3);
+  rg_bmark(c, 9);
+  if (c.trace && threadIdx.x == 0) c.trace[4 * kTraceRows + kTraceMarks * blockIdx.x + 14] = (unsigned long long)ci * 1000 + ridx;
+}
+
+// All threads, after phase_attn_range: the merges of the pairs this block
+// completed, staged through the chunk buffers (contiguous: ring slots
+// 1 .. kRangeBufs for single-sequence steps, the first kRangeBufs slots
+// otherwise) and the small arrays before the list.
+__device__ __noinline__ void rg_merge_pending(const Ctx *cp, float *smem) {
+  const Ctx &c = *cp;
+  const StepParams &sp = *c.sp;
+  float *sm = rg_small(c, sp.M, smem);
+  const int *ml = (const int *)(sm + kRgMerge);
+  float *stage = rg_buf(c, sp.M, smem, sp.M <= 1 ? kRangeBufs - 1 : 0);
+  const int q = ml[0];
+  for (int i = 0; i < q; i++) {
+    const int a = ml[4 + 2 * i], sb = ml[4 + 2 * i + 1];
+    const int m = a & 255, g = (a >> 8) & 255, nseg = a >> 16;
+    rg_merge(c, m, g, sp.seq[m].len + 1, sb, nseg, stage, sm);
+  }
 }
 
 // KV append of the long caches without attention (the last layer of a step

@@ -102,6 +102,12 @@ __device__ __forceinline__ unsigned long long gtimer() {
   asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
   return t;
 }
+
+// Trace buffer (OCRVL_TRACE): 256 phase rows of 4 words, then kTraceMarks
+// per-block time stamps for each of up to 1024 blocks.
+constexpr int kTraceRows = 256;
+constexpr int kTraceMarks = 24;
+constexpr int kTraceWords = 4 * kTraceRows + kTraceMarks * 1024;
 // ---------------------------------------------------------------------------
 // Small block-level helpers
 // ---------------------------------------------------------------------------
@@ -1380,10 +1386,13 @@ __device__ __forceinline__ void phase_gemv(const Ctx *c, const GemvArgs *a, int 
 // ---------------------------------------------------------------------------
 // KV cache and RoPE helpers
 // ---------------------------------------------------------------------------
+// A KV page holds 16 positions of every layer and kv head:
+// [layer][kv head][K, V][16 positions][head_dim] floats, so the K and V rows
+// of one (layer, kv head) are one contiguous 16 KB block.
 __device__ __forceinline__ float *kv_ptr(const Ctx &c, const int *bt, int layer, int kind, int kvh, int t) {
   int page = bt[t / kPageTokens];
   return c.kv_pool + (size_t)page * c.page_floats +
-         ((((size_t)layer * 2 + kind) * c.KVH + kvh) * kPageTokens + (t % kPageTokens)) * c.D;
+         ((((size_t)layer * c.KVH + kvh) * 2 + kind) * kPageTokens + (t % kPageTokens)) * c.D;
 }
 
 // ropeFMA (internal/tensor/dot_amd64.s:5405-5440): a' = a*c - b*s,
@@ -1501,39 +1510,6 @@ struct AttnItem {
   bool exact;
 };
 
-// Item `it` of the step (caches of n <= kAttnChunk positions, one item per
-// (sequence, kv head)); false when it is past the last item.
-__device__ __forceinline__ bool attn_item(const Ctx &c, const StepParams &sp, int it, AttnItem &I) {
-  for (int m = 0; m < sp.M; m++) {
-    const int n = sp.seq[m].len + 1;
-    if (n > kAttnChunk) continue;
-    if (it < c.KVH) {
-      I.m = m;
-      I.g = it;
-      I.ch = 0;
-      I.t0 = 0;
-      I.cnt = n;
-      I.n = n;
-      I.nch = 1;
-      I.exact = true;
-      return true;
-    }
-    it -= c.KVH;
-  }
-  return false;
-}
-
-__device__ __forceinline__ int attn_items_total(const Ctx &c, const StepParams &sp) {
-  int total = 0;
-  for (int m = 0; m < sp.M; m++)
-    if (sp.seq[m].len + 1 <= kAttnChunk) total += c.KVH;
-  return total;
-}
-
-}  // namespace ocrvl
-#include "attn_range.cuh"
-namespace ocrvl {
-
 // Per-block state of the K/V page loads, kept across phases of one launch.
 __shared__ __align__(8) uint64_t s_kv_bar;
 __shared__ uint32_t s_kv_parity;
@@ -1541,6 +1517,30 @@ __shared__ int s_kv_item;  // item whose pages are in flight / loaded, -1 none
 // cos / sin of every RoPE frequency at each sequence's position of this step
 __shared__ float s_rope_cs[kMaxBatch][kHeadDim / 2], s_rope_sn[kMaxBatch][kHeadDim / 2];
 __shared__ int s_rope_ready;
+
+}  // namespace ocrvl
+#include "attn_range.cuh"
+namespace ocrvl {
+
+// Item `it` of the step (caches of n <= kAttnChunk positions, one item per
+// (sequence, kv head), from the launch's list of such sequences); false when
+// it is past the last item.
+__device__ __forceinline__ bool attn_item(const Ctx &c, const StepParams &sp, int it, AttnItem &I) {
+  if (it >= s_ex_n * c.KVH) return false;
+  const int m = s_ex_m[it / c.KVH];
+  const int n = sp.seq[m].len + 1;
+  I.m = m;
+  I.g = it % c.KVH;
+  I.ch = 0;
+  I.t0 = 0;
+  I.cnt = n;
+  I.n = n;
+  I.nch = 1;
+  I.exact = true;
+  return true;
+}
+
+__device__ __forceinline__ int attn_items_total(const Ctx &c, const StepParams &) { return s_ex_n * c.KVH; }
 
 // Shared-memory layout of the attention phase (floats), from the base:
 //   q [G][D] | wt [G][32]
@@ -1558,7 +1558,7 @@ __device__ __forceinline__ float *attn_kv_buf(const Ctx &c, int M, float *smem) 
 }
 
 // Called by every thread at the start of a launch that runs attention phases.
-__device__ __forceinline__ void attn_block_init() {
+__device__ __forceinline__ void attn_block_init(const Ctx &c) {
   if (threadIdx.x == 0) {
     mbar_init(&s_kv_bar, 1);
     mbar_fence_init();
@@ -1567,6 +1567,7 @@ __device__ __forceinline__ void attn_block_init() {
     s_rope_ready = 0;
   }
   rg_block_init();
+  rg_launch_init(c);
   __syncthreads();
 }
 
@@ -1659,13 +1660,12 @@ __device__ void attn_range_prefetch(const Ctx &c, int layer, float *smem, int le
     const int srows = kStageBytes / A.pitch;
     upto = min(upto, kStagesM1 - (hi - lo + srows - 1) / srows);
   }
-  RgCur r;
-  int i;
-  rg_issue_ahead(c, layer, smem, upto, r, i);
+  rg_issue_upto(c, layer, smem, upto);
 }
 
 __device__ __noinline__ void phase_attn(const Ctx *cp, int layer, int append_only, int coop, float *smem) {
   const Ctx &c = *cp;
+  rg_bmark(c, 0);
   const StepParams &sp = *c.sp;
   const int G = c.QH / c.KVH, D = c.D, D4 = D / 4, H4 = D / 8;
   const int qkvld = (c.QH + 2 * c.KVH) * D;
@@ -1811,6 +1811,7 @@ __device__ __noinline__ void phase_attn(const Ctx *cp, int layer, int append_onl
     __syncthreads();
   } else {
     phase_attn_range(cp, layer, smem);
+    rg_merge_pending(cp, smem);
   }
 }
 

@@ -278,7 +278,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   extern __shared__ float4 smem4[];
   float *smem = align_dyn_smem(smem4);
   OCRVL_CTX_TO_SMEM(cv);
-  attn_block_init();
+  attn_block_init(c);
   ring_init();
   unsigned k = 0;
   int t = 0;
@@ -321,7 +321,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   Ctx &cm = sctx;
   if (threadIdx.x == 0) cm.trace = nullptr;
   __syncthreads();
-  attn_block_init();
+  attn_block_init(c);
   ring_init();
   run_phase<QT>(c, phase, layer, M, any_logits, do_embed, feed, align_dyn_smem(smem4), 0, 0, false);
 }
@@ -373,7 +373,20 @@ __device__ void step_b_body(const Ctx &c, const BatchedW *bw, uint32_t tmem, int
                             unsigned bar_base, float *smem) {
   __shared__ GemmArgs sg;
   unsigned k = 0;
-  auto sync = [&]() { return grid_sync(c, bar_base + (++k) * gridDim.x); };
+  // trace (OCRVL_TRACE): per phase [start, 0, last block's end, barrier exit]
+  int t = 0;
+  if (c.trace && blockIdx.x == 0 && threadIdx.x == 0) c.trace[0] = gtimer();
+  auto sync = [&]() {
+    if (c.trace && threadIdx.x == 0 && t < 256) atomicMax(c.trace + 4 * t + 2, gtimer());
+    const bool ok = grid_sync(c, bar_base + (++k) * gridDim.x);
+    if (c.trace && blockIdx.x == 0 && threadIdx.x == 0 && t + 1 < 256) {
+      const unsigned long long now = gtimer();
+      c.trace[4 * t + 3] = now;
+      c.trace[4 * (t + 1)] = now;
+    }
+    t++;
+    return ok;
+  };
   auto gemm = [&](const GemmArgs &g) {
     if (threadIdx.x == 0) sg = g;
     __syncthreads();
@@ -469,6 +482,7 @@ __device__ void step_b_body(const Ctx &c, const BatchedW *bw, uint32_t tmem, int
   g.argmax_finish = 1;
   g.feed = feed;
   gemm(g);
+  if (c.trace && threadIdx.x == 0 && t < 256) atomicMax(c.trace + 4 * t + 2, gtimer());
 }
 
 template <int QT>
@@ -480,7 +494,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   __shared__ BatchedW sbw;
   __shared__ uint32_t s_tmem;
   if (threadIdx.x == 0) sbw = bwv;
-  attn_block_init();
+  attn_block_init(c);
   ring_init();
   if (threadIdx.x < 32) tmem_alloc(&s_tmem, kTmemCols);
   tc_fence_before();
@@ -681,6 +695,9 @@ void setup_batched(ocrvl_model *m) {
     return;
   }
   PfnEncodeTiled enc = (PfnEncodeTiled)fn;
+  // every (sequence, kv head) pair of a 64-sequence step must fit the
+  // attention phase's merge list
+  if (kMaxSeqs * m->desc.num_kv_heads > kRgMerges) return;
   const int L = m->desc.num_layers;
   std::vector<TmapBytes> maps((size_t)L * 5 + 1);
   for (int l = 0; l < L; l++) {
@@ -806,6 +823,8 @@ int ocrvl_init(int device, const ocrvl_model_desc *desc, ocrvl_model **out) {
   if (d.head_dim != kHeadDim) return fail(OCRVL_E_INVALID, "head_dim must be 128");
   if (d.num_heads % d.num_kv_heads != 0 || d.num_heads / d.num_kv_heads > 8)
     return fail(OCRVL_E_INVALID, "num_heads must be 1..8 x num_kv_heads");
+  if (kMaxBatch * d.num_kv_heads > kRgMerges)
+    return fail(OCRVL_E_INVALID, "num_kv_heads must be at most 16");
   int qrows = d.num_heads * d.head_dim;
   if (d.hidden_size % 128 || d.intermediate_size % 128 || qrows % 128)
     return fail(OCRVL_E_INVALID, "hidden, intermediate and heads*head_dim must be multiples of 128");
@@ -1030,9 +1049,9 @@ int ocrvl_finalize(ocrvl_model *m) {
   if (m->qtype == QT_Q4 && !getenv("OCRVL_NO_BATCHED")) setup_batched<QT_Q4>(m);
   if (m->qtype == QT_Q6 && !getenv("OCRVL_NO_BATCHED")) setup_batched<QT_Q6>(m);
   if (getenv("OCRVL_TRACE")) {
-    c.trace = m->dalloc<unsigned long long>(4 * 256);
+    c.trace = m->dalloc<unsigned long long>(kTraceWords);
     if (!c.trace) return fail(OCRVL_E_NOMEM, "trace buffer");
-    CK(cudaMemset(c.trace, 0, 4 * 256 * 8));
+    CK(cudaMemset(c.trace, 0, kTraceWords * 8));
   }
   const char *mode = getenv("OCRVL_STEP_MODE");
   m->persistent = !(mode && std::string(mode) == "phases");
@@ -1048,10 +1067,10 @@ int ocrvl_trace_read(ocrvl_model *m, uint64_t *out, int cap) {
   if (!m->ctx.trace) return 0;
   std::lock_guard<std::mutex> lk(m->mu);
   if (int rc = set_device(m)) return rc;
-  int n = std::min(cap, 4 * 256);
+  int n = std::min(cap, kTraceWords);
   CK(cudaStreamSynchronize(m->stream));
   CK(cudaMemcpy(out, m->ctx.trace, (size_t)n * 8, cudaMemcpyDeviceToHost));
-  CK(cudaMemset(m->ctx.trace, 0, 4 * 256 * 8));
+  CK(cudaMemset(m->ctx.trace, 0, kTraceWords * 8));
   return n;
 }
 
@@ -1121,7 +1140,7 @@ int ocrvl_seq_read_kv(ocrvl_seq *s, int layer, float *k, float *v) {
     for (int kind = 0; kind < 2; kind++)
       for (int g = 0; g < d.num_kv_heads; g++) {
         size_t off = (size_t)page * m->page_floats +
-                     ((((size_t)layer * 2 + kind) * d.num_kv_heads + g) * kPageTokens + t % kPageTokens) * d.head_dim;
+                     ((((size_t)layer * d.num_kv_heads + g) * 2 + kind) * kPageTokens + t % kPageTokens) * d.head_dim;
         float *dst = (kind == 0 ? k : v) + (size_t)t * kvd + (size_t)g * d.head_dim;
         CK(cudaMemcpy(dst, m->kv_pool + off, d.head_dim * 4, cudaMemcpyDeviceToHost));
       }
