@@ -111,6 +111,16 @@ int ocrvl_seq_len(const ocrvl_seq *s);
  * gathering through the sequence's block table. */
 int ocrvl_seq_read_kv(ocrvl_seq *s, int layer, float *k, float *v);
 
+/* Replaces the sequence's cache with n positions of K and V given for every
+ * layer ([num_layers][n][kv_heads*head_dim] f32 each, the layout
+ * ocrvl_seq_read_kv returns) and sets its length to n; the next step
+ * continues at position n.  No reference counterpart: it restores a cache
+ * saved with ocrvl_seq_read_kv (or built elsewhere) without replaying the
+ * prompt, e.g. to set up long contexts for profiling.  Invalid arguments
+ * leave the sequence unchanged; a later failure (page pool exhausted, copy
+ * error) leaves it empty. */
+int ocrvl_seq_import_kv(ocrvl_seq *s, int n, const float *k, const float *v);
+
 /* One decode step for n sequences (1 <= n <= 64) of the same model: the
  * batched form of Runtime.forwardEmbeddingForSampling
  * (internal/model/model.go:3475-3643).  Every sequence is validated before

@@ -61,6 +61,7 @@ SIGNATURES = {
     "ocrvl_seq_free": (None, [P]),
     "ocrvl_seq_len": (I, [P]),
     "ocrvl_seq_read_kv": (I, [P, I, P, P]),
+    "ocrvl_seq_import_kv": (I, [P, I, P, P]),
     "ocrvl_step": (I, [P, P, I, P, P, P, I, P, P]),
     "ocrvl_generate_greedy": (I, [P, P, I, I, P, I, P, I, C.POINTER(I)]),
     "ocrvl_decode_greedy_device": (I, [P, P, I, P, I, P]),

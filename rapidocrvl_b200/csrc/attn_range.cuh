@@ -268,6 +268,41 @@ __device__ __forceinline__ int rg_pool_page(const StepParams &sp, const RgCur &r
 __device__ __forceinline__ const float *rg_page_kv(const Ctx &c, int page, int layer, int g) {
   return c.kv_pool + (size_t)page * c.page_floats + ((size_t)layer * c.KVH + g) * 2 * kPageTokens * c.D;
 }
+// Pairs of floats in one 64-bit register pair and the sm_100 packed FP32
+// operations on them (each half rounded to nearest even, as the scalar
+// __fmul_rn / __fadd_rn / __fmaf_rn).
+typedef unsigned long long f2x;
+__device__ __forceinline__ f2x f2_pack(float a, float b) {
+  f2x r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+  return r;
+}
+__device__ __forceinline__ float f2_lo(f2x r) {
+  float a, b;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(r));
+  return a;
+}
+__device__ __forceinline__ float f2_hi(f2x r) {
+  float a, b;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(r));
+  return b;
+}
+__device__ __forceinline__ f2x f2_mul(f2x a, f2x b) {
+  f2x d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ f2x f2_add(f2x a, f2x b) {
+  f2x d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ f2x f2_fma(f2x a, f2x b, f2x c) {
+  f2x d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+
 // Row of position t (0..31) of a chunk buffer: page t / 16 of the chunk at
 // 32 rows per page, K rows first.
 __device__ __forceinline__ float *rg_row(float *buf, int t, int kind) {
@@ -468,9 +503,9 @@ __device__ __noinline__ void phase_attn_range(const Ctx *cp, int layer, float *s
       cur.k = k;
       const bool last_seg = k == cur.nseg - 1;
       float m_run = -INFINITY, l_run = 0.0f;  // warp h < G: head h
-      float o[8];
+      f2x o2[4];  // o of heads (2 p, 2 p + 1)
 #pragma unroll
-      for (int h = 0; h < 8; h++) o[h] = 0.0f;
+      for (int p = 0; p < 4; p++) o2[p] = 0ull;
       const int seg_np = rg_seg_np(cur);
       const int nck = (seg_np + 1) / 2;
       const int sp0 = k * cur.S;  // first page of the segment
@@ -505,25 +540,32 @@ __device__ __noinline__ void phase_attn_range(const Ctx *cp, int layer, float *s
 #pragma unroll
         for (int hg = 0; hg < 2; hg++) {
           float part[8];
-          float qr[4][8];
+          f2x qr[2][8];  // heads (4 hg + 2 p, 4 hg + 2 p + 1)
 #pragma unroll
-          for (int h4 = 0; h4 < 4; h4++)
+          for (int p = 0; p < 2; p++)
 #pragma unroll
-            for (int jj = 0; jj < 8; jj++)
-              qr[h4][jj] = 4 * hg + h4 < G ? qs[(4 * hg + h4) * kHeadDim + 16 * (jj ^ grp) + slot] : 0.0f;
+            for (int jj = 0; jj < 8; jj++) {
+              const int h0 = 4 * hg + 2 * p, idx = 16 * (jj ^ grp) + slot;
+              qr[p][jj] = f2_pack(h0 < G ? qs[h0 * kHeadDim + idx] : 0.0f, h0 + 1 < G ? qs[(h0 + 1) * kHeadDim + idx] : 0.0f);
+            }
 #pragma unroll
           for (int tl = 0; tl < 2; tl++) {
             const float *kr = rg_row(Kb, 4 * warp + 2 * grp + tl, 0);
-            float kk[8];
+            f2x kk[8];
 #pragma unroll
-            for (int jj = 0; jj < 8; jj++) kk[jj] = kr[16 * (jj ^ grp) + slot];
+            for (int jj = 0; jj < 8; jj++) {
+              const float kv = kr[16 * (jj ^ grp) + slot];
+              kk[jj] = f2_pack(kv, kv);
+            }
 #pragma unroll
-            for (int h4 = 0; h4 < 4; h4++) {
-              float pr[8];
+            for (int p = 0; p < 2; p++) {
+              f2x pr[8];
 #pragma unroll
-              for (int jj = 0; jj < 8; jj++) pr[jj] = __fmul_rn(qr[h4][jj], kk[jj]);
-              part[tl * 4 + h4] = __fadd_rn(__fadd_rn(__fadd_rn(pr[0], pr[1]), __fadd_rn(pr[2], pr[3])),
-                                            __fadd_rn(__fadd_rn(pr[4], pr[5]), __fadd_rn(pr[6], pr[7])));
+              for (int jj = 0; jj < 8; jj++) pr[jj] = f2_mul(qr[p][jj], kk[jj]);
+              const f2x sum = f2_add(f2_add(f2_add(pr[0], pr[1]), f2_add(pr[2], pr[3])),
+                                     f2_add(f2_add(pr[4], pr[5]), f2_add(pr[6], pr[7])));
+              part[tl * 4 + 2 * p] = f2_lo(sum);
+              part[tl * 4 + 2 * p + 1] = f2_hi(sum);
             }
           }
 #pragma unroll
@@ -580,26 +622,21 @@ __device__ __noinline__ void phase_attn_range(const Ctx *cp, int layer, float *s
         if (ci == 1) rg_bmark(c, 13);
         // ---- values: thread (d, th), tokens th*16 .. th*16+15 of the chunk
         {
-          float av[8];
 #pragma unroll
-          for (int h = 0; h < 8; h++) av[h] = h < G ? alph[h] : 0.0f;
-#pragma unroll
-          for (int h = 0; h < 8; h++) o[h] = __fmul_rn(o[h], av[h]);
+          for (int p = 0; p < 4; p++)
+            o2[p] = f2_mul(o2[p], f2_pack(2 * p < G ? alph[2 * p] : 0.0f, 2 * p + 1 < G ? alph[2 * p + 1] : 0.0f));
           const int tb = th * 16, te = min(cnt, tb + 16);
           const int tt = min(max(nv - t0, tb), te);  // [tb, tt) exponentiated, [tt, te) raw
           const float *Vb = rg_row(Kb, tb, 1) - (size_t)tb * kHeadDim;  // row t of this half at Vb + t * D
 #pragma unroll 4
           for (int t = tb; t < tt; t++) {
             const float v = Vb[(size_t)t * kHeadDim + d];
-            const float4 w0 = ((const float4 *)(W + t * 8))[0], w1 = ((const float4 *)(W + t * 8))[1];
-            o[0] = __fmaf_rn(w0.x, v, o[0]);
-            o[1] = __fmaf_rn(w0.y, v, o[1]);
-            o[2] = __fmaf_rn(w0.z, v, o[2]);
-            o[3] = __fmaf_rn(w0.w, v, o[3]);
-            o[4] = __fmaf_rn(w1.x, v, o[4]);
-            o[5] = __fmaf_rn(w1.y, v, o[5]);
-            o[6] = __fmaf_rn(w1.z, v, o[6]);
-            o[7] = __fmaf_rn(w1.w, v, o[7]);
+            const f2x vv = f2_pack(v, v);
+            const ulonglong2 wa = ((const ulonglong2 *)(W + t * 8))[0], wb = ((const ulonglong2 *)(W + t * 8))[1];
+            o2[0] = f2_fma(wa.x, vv, o2[0]);
+            o2[1] = f2_fma(wa.y, vv, o2[1]);
+            o2[2] = f2_fma(wb.x, vv, o2[2]);
+            o2[3] = f2_fma(wb.y, vv, o2[3]);
           }
           if (t0 + cnt > nv) {
             // the chunk holding the positions at or above nv (the last one of
@@ -632,6 +669,12 @@ __device__ __noinline__ void phase_attn_range(const Ctx *cp, int layer, float *s
       }
       const bool has_tail = last_seg && (n & 15) != 0;
       const int seg = rg_seg_index(cur);
+      float o[8];
+#pragma unroll
+      for (int p = 0; p < 4; p++) {
+        o[2 * p] = f2_lo(o2[p]);
+        o[2 * p + 1] = f2_hi(o2[p]);
+      }
       if (th == 1) {
 #pragma unroll
         for (int h = 0; h < 8; h++)

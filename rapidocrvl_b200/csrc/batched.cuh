@@ -24,9 +24,11 @@
 //             rows, unpacked by all threads to int8 in the K-major core-matrix
 //             layout (8 rows x 16 bytes contiguous; 8-row groups 1 KB apart)
 //     4 MMAs (K = 32 bytes each) issued by one thread into TMEM
-//   with two buffers per operand, so the copies and the unpacking of tile t+1
-//   overlap the tensor core's work on tile t; each MMA batch commits to an
-//   mbarrier that frees its buffers.  The epilogue reads D with tcgen05.ld
+//   through a ring of up to kGemmStages stages (A tile + packed B rows, as
+//   many as the shared memory holds), issued ahead so the copies of later K
+//   tiles overlap the unpacking and the tensor core's work; the unpacked int8
+//   tiles are double-buffered and each MMA batch commits to an mbarrier that
+//   frees its B buffer and its stage.  The epilogue reads D with tcgen05.ld
 //   (M = 64 puts sequence r in TMEM lane 32*(r/16) + r%16) and applies the
 //   same finalize and epilogue (store, residual, SwiGLU, argmax) as the
 //   single-sequence kernels.
@@ -48,6 +50,7 @@ struct BatchedW {
   const TmapBytes *tm;  // [L * 5 + 1]: per layer qkv, o, gate, up, down; then lm_head
   uint8_t *act;         // activation image [K tiles][64 rows][kKT]
   float *act_sx;        // [kMaxSeqs] activation scale per sequence
+  int smem_avail;       // dynamic shared memory of the step kernel (bytes, after alignment)
 };
 
 __device__ __forceinline__ const TmapBytes *bw_map(const BatchedW &bw, int layer, int which) {
@@ -146,6 +149,7 @@ struct GemmArgs {
   DMat A, B;
   int row_begin, row_end, K;     // output rows, input columns
   int nt;                        // rows per N tile = the maps' box height (multiple of 16, <= 256)
+  int u;                         // K tiles per copy (gemm_u): the maps' box width is u packed K tiles
   int epi;                       // EPI_*
   float *out;
   int ldo;
@@ -156,12 +160,27 @@ struct GemmArgs {
   int argmax_finish, feed;
 };
 
-// shared-memory layout of the GEMM phase (bytes)
-constexpr int kGemmA = kMmaM * kKT;              // 8 KB per A buffer
-constexpr int kGemmB = kMaxNT * kKT;             // 32 KB per B buffer (int8)
-constexpr int kGemmStage = kMaxNT * kKT * 3 / 4; // 24 KB per packed staging buffer (Q6 worst case)
+// K tiles per copy: N tiles of up to 64 rows move u K tiles per copy (one
+// 2-D TMA box of u * KP <= 256 bytes x nt rows, and one bulk copy of u A
+// tiles), so a phase issues few, large copies; wider N tiles (lm_head) one.
+__host__ __device__ __forceinline__ int gemm_u(int qt, int nt) {
+  return nt <= 64 ? (qt == QT_Q4 ? 4 : 2) : 1;
+}
+
+// shared-memory layout of the GEMM phase (bytes from the base):
+//   row scales [2][kMaxNT] f32 | row sums [2][kMaxNT] i32              4 KB
+//   unpacked B tiles [NB buffers][mats][nt][kKT] int8 (core-matrix layout)
+//   stages [S]: u A tiles (u * kGemmA) | packed rows [mats][nt][u * KP]
+//   (1 KB aligned)
+// NB = 8 when eight B buffers take at most a quarter of the memory, else 2;
+// S fills the rest (at most kGemmStages, at most the stages of K).
+constexpr int kGemmA = kMmaM * kKT;  // 8 KB per A tile
+constexpr int kGemmStages = 8;       // ring stages at most
+constexpr int kGemmBBufs = 8;        // unpacked B buffers at most
+constexpr int kGemmScl = 4 * kMaxNT * 4;
+// Least shared memory the phase needs (two stages of the largest tile).
 __host__ __device__ __forceinline__ size_t gemm_b_smem_bytes() {
-  return 2 * (size_t)kGemmA + 2 * (size_t)kGemmB + 2 * (size_t)kGemmStage * 2 + 4 * kMaxNT * 4 + 1024;
+  return (size_t)kGemmScl + 2 * (size_t)kMaxNT * kKT + 2 * ((size_t)kGemmA + (size_t)kMaxNT * kKT * 3 / 4);
 }
 
 template <int QT>
@@ -172,36 +191,50 @@ __device__ __noinline__ void phase_gemm_b(const Ctx *cp, const BatchedW *bwp, co
   const GemmArgs &a = *gp;
   constexpr int KP = QT == QT_Q4 ? kKT / 2 : kKT * 3 / 4;  // packed bytes per row per K tile
   const bool two = a.epi == EPI_SWIGLU;
+  const int mats = two ? 2 : 1;
   const int M = c.sp->M;
+  const int NT = a.nt, U = a.u;
   uint8_t *base = (uint8_t *)smem;
-  uint8_t *sA[2] = {base, base + kGemmA};
-  uint8_t *sB[2][2] = {{base + 2 * kGemmA, base + 2 * kGemmA + kGemmB}, {nullptr, nullptr}};
-  uint8_t *stg0 = base + 2 * kGemmA + 2 * kGemmB;
-  uint8_t *sStage[2][2] = {{stg0, stg0 + kGemmStage}, {stg0 + 2 * kGemmStage, stg0 + 3 * kGemmStage}};
-  float *s_scl = (float *)(stg0 + 4 * kGemmStage);  // [2][kMaxNT] scales, [2][kMaxNT] row sums
+  float *s_scl = (float *)base;  // [2][kMaxNT] scales, [2][kMaxNT] row sums
   int32_t *s_rs = (int32_t *)(s_scl + 2 * kMaxNT);
-  __shared__ __align__(8) uint64_t bar_ld[2], bar_mma[2];
-  __shared__ uint32_t par_ld, par_mma;
-  // SwiGLU keeps both weight tiles: B of the up matrix reuses the second
-  // buffer pair, so K tiles are single-buffered for it
+  uint8_t *sB0 = base + kGemmScl;                        // [NB][mats][NT][kKT]
+  const int sbytes = NT * kKT;
+  const int NB = kGemmBBufs * mats * sbytes * 4 <= bw.smem_avail - kGemmScl ? kGemmBBufs : 2;
+  uint8_t *stg = sB0 + (size_t)NB * mats * sbytes;       // stages
+  const int rowb = U * KP;                               // packed bytes per row per stage
+  const int stage_bytes = (U * kGemmA + mats * NT * rowb + 1023) / 1024 * 1024;
+  const int nk = a.K / kKT, nsu = (nk + U - 1) / U;
+  int S = (bw.smem_avail - (int)(stg - base)) / stage_bytes;
+  S = min(min(S, kGemmStages), max(nsu, 2));
+  __shared__ __align__(8) uint64_t bar_ld[kGemmStages], bar_su[kGemmStages], bar_mma[kGemmBBufs];
+  if (S < 2) {  // the host sizes the shared memory for two stages of the largest tile
+    if (threadIdx.x == 0) atomicExch(c.err, 1);
+    return;
+  }
   int lo, hi;
   gemv_slab(a.row_begin, a.row_end, blockIdx.x, gridDim.x, lo, hi);
-  const int nk = a.K / kKT;
   if (threadIdx.x == 0) {
-    for (int i = 0; i < 2; i++) {
+    for (int i = 0; i < kGemmStages; i++) {
       mbar_init(&bar_ld[i], 1);
-      mbar_init(&bar_mma[i], 1);
+      mbar_init(&bar_su[i], 1);
     }
+    for (int i = 0; i < kGemmBBufs; i++) mbar_init(&bar_mma[i], 1);
     mbar_fence_init();
-    par_ld = 0;
-    par_mma = 0;
   }
   __syncthreads();
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   unsigned long long best = 0ull;  // ARGMAX: lane's sequence best key
-  for (int n0 = lo; n0 < hi; n0 += a.nt) {
-    const int nrows = min(a.nt, hi - n0);
-    const int NT = a.nt;
+  // trace: per-block time stamps of the o projection (16 start, 17 first
+  // copies issued, 18-22 its third K tile: start, waits, unpack, barrier,
+  // MMAs issued, 23 end)
+  const bool mk = a.epi == EPI_RESID && a.resid_mode == RESID_ATTN;
+  if (mk) rg_bmark(c, 16);
+  // stage TU of the phase (over all N tiles) uses slot TU % S: bar_ld and
+  // bar_su complete once per use (use TU / S); K tile T uses B buffer T % NB
+  // and commits its MMAs to bar_mma[T % NB] (completion T / NB)
+  int T0 = 0, TU0 = 0;
+  for (int n0 = lo; n0 < hi; n0 += NT, T0 += nk, TU0 += nsu) {
+    const int nrows = min(NT, hi - n0);
     // scales / row sums of this N tile
     for (int i = threadIdx.x; i < nrows; i += kThreads) {
       s_scl[i] = __ldg(a.A.scale + n0 + i);
@@ -211,43 +244,51 @@ __device__ __noinline__ void phase_gemm_b(const Ctx *cp, const BatchedW *bwp, co
         s_rs[kMaxNT + i] = __ldg(a.B.rowsum + n0 + i);
       }
     }
-    const int nbuf = two ? 1 : 2;  // SwiGLU: one buffer per matrix
-    auto issue = [&](int t) {     // thread 0: copies of K tile t
-      const int b = t % nbuf;
-      const uint32_t bytes_b = (uint32_t)a.nt * KP;  // the whole box (rows past the matrix are zero-filled)
-      mbar_expect_tx(&bar_ld[b], kGemmA + (two ? 2 : 1) * bytes_b);
-      bulk_g2s(sA[b], bw.act + (size_t)t * kGemmA, kGemmA, &bar_ld[b]);
-      tma_2d(sStage[0][b], a.mapA, t * KP, n0, &bar_ld[b]);
-      if (two) tma_2d(sStage[1][0], a.mapB, t * KP, n0, &bar_ld[b]);
+    auto issue = [&](int su) {  // thread 0: copies of stage su (K tiles su*U ..)
+      const int slot = (TU0 + su) % S;
+      uint8_t *sa = stg + (size_t)slot * stage_bytes;
+      const uint32_t bytes_a = (uint32_t)min(U, nk - su * U) * kGemmA;
+      const uint32_t bytes_b = (uint32_t)NT * rowb;  // the whole box (past the matrix: zero-filled)
+      mbar_expect_tx(&bar_ld[slot], bytes_a + mats * bytes_b);
+      bulk_g2s(sa, bw.act + (size_t)su * U * kGemmA, bytes_a, &bar_ld[slot]);
+      tma_2d(sa + U * kGemmA, a.mapA, su * rowb, n0, &bar_ld[slot]);
+      if (two) tma_2d(sa + U * kGemmA + bytes_b, a.mapB, su * rowb, n0, &bar_ld[slot]);
     };
     if (threadIdx.x == 0) {
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-      for (int t = 0; t < nk && t < nbuf; t++) issue(t);
+      for (int su = 0; su < nsu && su < S; su++) issue(su);
     }
+    if (mk && n0 == lo) rg_bmark(c, 17);
     const uint32_t idesc = umma_idesc_i8(NT);
     for (int t = 0; t < nk; t++) {
-      const int b = t % nbuf;
-      // wait for the copies of tile t
-      if (!mbar_wait(&bar_ld[b], (par_ld >> b) & 1u, c.err)) break;
-      // unpack the packed weights to int8 in the core-matrix layout
-      for (int mi = 0; mi < (two ? 2 : 1); mi++) {
-        const uint8_t *stg = two ? sStage[mi][0] : sStage[0][b];
-        uint8_t *dstB = two ? sB[0][mi] : sB[0][b];
+      const int su = t / U, j = t - su * U, TU = TU0 + su, slot = TU % S;
+      const int T = T0 + t, bb = T % NB;
+      const uint8_t *sa = stg + (size_t)slot * stage_bytes;
+      const bool mt = mk && n0 == lo && t == 2;
+      if (mt) rg_bmark(c, 18);
+      if (j == 0) mbar_wait(&bar_ld[slot], (uint32_t)(TU / S) & 1u, c.err);
+      // the B buffer's previous MMAs (tile T - NB) are done before it is rewritten
+      if (t >= NB) mbar_wait(&bar_mma[bb], (uint32_t)(T / NB - 1) & 1u, c.err);
+      if (mt) rg_bmark(c, 19);
+      // unpack K tile j of the stage's packed rows to int8 in the core-matrix layout
+      for (int mi = 0; mi < mats; mi++) {
+        const uint8_t *pk_src = sa + U * kGemmA + (size_t)mi * NT * rowb + (size_t)j * KP;
+        uint8_t *dstB = sB0 + (size_t)(bb * mats + mi) * sbytes;
         if (QT == QT_Q4) {
           // 16 packed bytes -> 32 int8 = two 16-byte K chunks
           for (int task = threadIdx.x; task < NT * (KP / 16); task += kThreads) {
             const int r = task / (KP / 16), c4 = task % (KP / 16);
             uint4 pk = make_uint4(0, 0, 0, 0);
-            if (r < nrows) pk = *(const uint4 *)(stg + (size_t)r * KP + 16 * c4);
+            if (r < nrows) pk = *(const uint4 *)(pk_src + (size_t)r * rowb + 16 * c4);
             const uint32_t w4[4] = {pk.x, pk.y, pk.z, pk.w};
             uint32_t o[8];
 #pragma unroll
-            for (int j = 0; j < 4; j++) {
-              const uint32_t lo4 = w4[j] & 0x0F0F0F0Fu, hi4 = (w4[j] >> 4) & 0x0F0F0F0Fu;
+            for (int jq = 0; jq < 4; jq++) {
+              const uint32_t lo4 = w4[jq] & 0x0F0F0F0Fu, hi4 = (w4[jq] >> 4) & 0x0F0F0F0Fu;
               // bytes b0..b3 -> (lo0, hi0, lo1, hi1), (lo2, hi2, lo3, hi3); nibble - 8
               const uint32_t x0 = __byte_perm(lo4, hi4, 0x5140), x1 = __byte_perm(lo4, hi4, 0x7362);
-              o[2 * j] = __vsub4(x0, 0x08080808u);
-              o[2 * j + 1] = __vsub4(x1, 0x08080808u);
+              o[2 * jq] = __vsub4(x0, 0x08080808u);
+              o[2 * jq + 1] = __vsub4(x1, 0x08080808u);
             }
             *(uint4 *)(dstB + cm_off(r, 32 * c4)) = make_uint4(o[0], o[1], o[2], o[3]);
             *(uint4 *)(dstB + cm_off(r, 32 * c4 + 16)) = make_uint4(o[4], o[5], o[6], o[7]);
@@ -258,7 +299,7 @@ __device__ __noinline__ void phase_gemm_b(const Ctx *cp, const BatchedW *bwp, co
             const int r = task / (KP / 48), c3 = task % (KP / 48);
             uint32_t wd[12];
             if (r < nrows) {
-              const uint4 *s4 = (const uint4 *)(stg + (size_t)r * KP + 48 * c3);
+              const uint4 *s4 = (const uint4 *)(pk_src + (size_t)r * rowb + 48 * c3);
               const uint4 x = s4[0], y = s4[1], z = s4[2];
               const uint32_t t12[12] = {x.x, x.y, x.z, x.w, y.x, y.y, y.z, y.w, z.x, z.y, z.z, z.w};
 #pragma unroll
@@ -279,49 +320,42 @@ __device__ __noinline__ void phase_gemm_b(const Ctx *cp, const BatchedW *bwp, co
           }
         }
       }
+      if (mt) rg_bmark(c, 20);
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       tc_fence_before();
       __syncthreads();
       tc_fence_after();
+      if (mt) rg_bmark(c, 21);
       if (threadIdx.x == 0) {
-        par_ld ^= 1u << b;
         // MMAs of this K tile
-        for (int s = 0; s < kKT / 32; s++) {
-          const uint64_t da = umma_desc(sA[b] + s * 256);
-          const uint32_t acc = (t > 0 || s > 0) ? 1u : 0u;
-          if (two) {
-            umma_i8(tmem, da, umma_desc(sB[0][0] + s * 256), idesc, acc);
-            umma_i8(tmem + (uint32_t)NT, da, umma_desc(sB[0][1] + s * 256), idesc, acc);
-          } else {
-            umma_i8(tmem, da, umma_desc(sB[0][b] + s * 256), idesc, acc);
-          }
+        for (int s4 = 0; s4 < kKT / 32; s4++) {
+          const uint64_t da = umma_desc(sa + (size_t)j * kGemmA + s4 * 256);
+          const uint32_t acc = (t > 0 || s4 > 0) ? 1u : 0u;
+          for (int mi = 0; mi < mats; mi++)
+            umma_i8(tmem + (uint32_t)(mi * NT), da, umma_desc(sB0 + (size_t)(bb * mats + mi) * sbytes + s4 * 256), idesc,
+                    acc);
         }
-        umma_commit(&bar_mma[b]);
-      }
-      // refill: the buffers of the previous tile (two buffers) or of this
-      // tile (SwiGLU, one buffer) take tile t + 1 once their MMAs are done
-      const int tb = nbuf == 2 ? t - 1 : t;
-      if (tb >= 0) {
-        const int bb = tb % nbuf;
-        if (!mbar_wait(&bar_mma[bb], (par_mma >> bb) & 1u, c.err)) break;
-        tc_fence_after();
-        __syncthreads();
-        if (threadIdx.x == 0) {
-          par_mma ^= 1u << bb;
-          if (t + 1 < nk && (nbuf == 1 || t + 1 >= nbuf)) {
+        umma_commit(&bar_mma[bb]);
+        if (mt) rg_bmark(c, 22);
+        if (j == U - 1 || t == nk - 1) {
+          // the stage's MMAs are all issued: its slot frees once they are done
+          umma_commit(&bar_su[slot]);
+          // the previous stage's slot takes stage su - 1 + S
+          if (su >= 1 && su - 1 + S < nsu) {
+            const int pslot = (TU - 1) % S;
+            mbar_wait(&bar_su[pslot], (uint32_t)((TU - 1) / S) & 1u, c.err);
+            tc_fence_after();
             asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-            issue(t + 1);
+            issue(su - 1 + S);
           }
         }
       }
     }
-    // the last tile's MMAs (two buffers: not waited in the loop)
-    if (nbuf == 2 && nk > 0) {
-      const int bb = (nk - 1) % 2;
-      mbar_wait(&bar_mma[bb], (par_mma >> bb) & 1u, c.err);
+    // the last tile's MMAs
+    if (nk > 0) {
+      const int TL = T0 + nk - 1;
+      mbar_wait(&bar_mma[TL % NB], (uint32_t)(TL / NB) & 1u, c.err);
       tc_fence_after();
-      __syncthreads();
-      if (threadIdx.x == 0) par_mma ^= 1u << bb;
       __syncthreads();
     }
     // ---- epilogue: warps w and w+4 share TMEM lane quarter w (sequences
@@ -391,6 +425,7 @@ __device__ __noinline__ void phase_gemm_b(const Ctx *cp, const BatchedW *bwp, co
     }
   }
   __syncthreads();
+  if (mk) rg_bmark(c, 23);
 }
 
 }  // namespace ocrvl

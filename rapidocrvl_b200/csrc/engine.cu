@@ -406,6 +406,7 @@ __device__ void step_b_body(const Ctx &c, const BatchedW *bw, uint32_t tmem, int
       g.row_end = L.qkv.rows;
       g.K = c.H;
       g.nt = gemm_nt(L.qkv.rows, gridDim.x);
+      g.u = gemm_u(QT, g.nt);
       g.epi = EPI_STORE;
       g.out = c.qkv;
       g.ldo = qkvld;
@@ -424,6 +425,7 @@ __device__ void step_b_body(const Ctx &c, const BatchedW *bw, uint32_t tmem, int
       g.row_end = L.o.rows;
       g.K = c.QH * c.D;
       g.nt = gemm_nt(L.o.rows, gridDim.x);
+      g.u = gemm_u(QT, g.nt);
       g.epi = EPI_RESID;
       g.ldo = c.H;
       g.resid = c.h;
@@ -443,6 +445,7 @@ __device__ void step_b_body(const Ctx &c, const BatchedW *bw, uint32_t tmem, int
       g.row_end = L.gate.rows;
       g.K = c.H;
       g.nt = gemm_nt(L.gate.rows, gridDim.x);
+      g.u = gemm_u(QT, g.nt);
       g.epi = EPI_SWIGLU;
       g.out = c.g;
       g.ldo = c.I;
@@ -458,6 +461,7 @@ __device__ void step_b_body(const Ctx &c, const BatchedW *bw, uint32_t tmem, int
       g.row_end = L.down.rows;
       g.K = c.I;
       g.nt = gemm_nt(L.down.rows, gridDim.x);
+      g.u = gemm_u(QT, g.nt);
       g.epi = EPI_RESID;
       g.ldo = c.H;
       g.resid = c.h;
@@ -475,6 +479,7 @@ __device__ void step_b_body(const Ctx &c, const BatchedW *bw, uint32_t tmem, int
   g.row_end = c.lm_head.rows;
   g.K = c.H;
   g.nt = gemm_nt(c.lm_head.rows, gridDim.x);
+  g.u = gemm_u(QT, g.nt);
   g.epi = EPI_ARGMAX;
   g.ldo = c.V;
   g.argkey = c.argkey;
@@ -667,13 +672,15 @@ typedef CUresult (*PfnEncodeTiled)(CUtensorMap *, CUtensorMapDataType, cuuint32_
                                    const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
                                    CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
 
-// 2-D TMA map of a packed weight matrix: rows of `pitch` bytes; box = one
-// K tile of packed bytes x gemm_nt(rows, grid) rows (rows past the end read 0).
+// 2-D TMA map of a packed weight matrix: rows of `pitch` bytes; box =
+// gemm_u K tiles of packed bytes x gemm_nt(rows, grid) rows (rows and
+// columns past the end read 0).
 bool make_weight_map(PfnEncodeTiled enc, const DMat &A, int qtype, int grid, TmapBytes *out) {
   const int KP = qtype == QT_Q4 ? kKT / 2 : kKT * 3 / 4;
+  const int nt = gemm_nt(A.rows, grid);
   cuuint64_t dims[2] = {(cuuint64_t)A.pitch, (cuuint64_t)A.rows};
   cuuint64_t strides[1] = {(cuuint64_t)A.pitch};
-  cuuint32_t box[2] = {(cuuint32_t)KP, (cuuint32_t)gemm_nt(A.rows, grid)};
+  cuuint32_t box[2] = {(cuuint32_t)(gemm_u(qtype, nt) * KP), (cuuint32_t)nt};
   cuuint32_t es[2] = {1, 1};
   memset(out, 0, sizeof(*out));
   return enc((CUtensorMap *)out, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, (void *)A.w, dims, strides, box, es,
@@ -727,6 +734,7 @@ void setup_batched(ocrvl_model *m) {
   m->bw.tm = dmaps;
   m->bw.act = act;
   m->bw.act_sx = act_sx;
+  m->bw.smem_avail = (int)(m->smem - kSmemAlignSlack);
   m->batched = true;
 }
 
@@ -1125,6 +1133,55 @@ void ocrvl_seq_free(ocrvl_seq *s) {
 }
 
 int ocrvl_seq_len(const ocrvl_seq *s) { return s ? s->len : OCRVL_E_INVALID; }
+
+int ocrvl_seq_import_kv(ocrvl_seq *s, int n, const float *k, const float *v) {
+  if (!s) return fail(OCRVL_E_INVALID, "null seq");
+  if (n < 0 || n > s->max_tokens) return fail(OCRVL_E_INVALID, "n outside 0..max_tokens");
+  if (n > 0 && (!k || !v)) return fail(OCRVL_E_INVALID, "null K/V");
+  if (int rc = ocrvl_seq_reset(s)) return rc;
+  ocrvl_model *m = s->m;
+  std::lock_guard<std::mutex> lk(m->mu);
+  const ocrvl_model_desc &d = m->desc;
+  const int np = (n + kPageTokens - 1) / kPageTokens;
+  if ((size_t)np > m->free_pages.size()) return fail(OCRVL_E_NOMEM, "KV page pool exhausted");
+  if (int rc = set_device(m)) return rc;
+  CK(cudaStreamSynchronize(m->stream));
+  const int kvd = d.num_kv_heads * d.head_dim;
+  // one page at a time in the pool layout [layer][kv head][K, V][16][head_dim]
+  std::vector<float> page((size_t)m->page_floats);
+  std::vector<int> ids(np);
+  for (int p = 0; p < np; p++) {
+    ids[p] = m->free_pages.back();
+    m->free_pages.pop_back();
+    s->pages.push_back(ids[p]);
+    std::fill(page.begin(), page.end(), 0.0f);
+    for (int l = 0; l < d.num_layers; l++)
+      for (int g = 0; g < d.num_kv_heads; g++)
+        for (int kind = 0; kind < 2; kind++)
+          for (int r = 0; r < kPageTokens && p * kPageTokens + r < n; r++) {
+            const float *src = (kind ? v : k) + ((size_t)l * n + (size_t)p * kPageTokens + r) * kvd + (size_t)g * d.head_dim;
+            float *dst = page.data() + ((((size_t)l * d.num_kv_heads + g) * 2 + kind) * kPageTokens + r) * d.head_dim;
+            std::copy(src, src + d.head_dim, dst);
+          }
+    cudaError_t e = cudaMemcpy(m->kv_pool + (size_t)ids[p] * m->page_floats, page.data(), page.size() * 4,
+                               cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) {
+      for (int q : s->pages) m->free_pages.push_back(q);
+      s->pages.clear();
+      return fail(OCRVL_E_CUDA, std::string("cudaMemcpy: ") + cudaGetErrorString(e));
+    }
+  }
+  if (np > 0) {
+    cudaError_t e = cudaMemcpy(s->bt_d, ids.data(), (size_t)np * 4, cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) {
+      for (int q : s->pages) m->free_pages.push_back(q);
+      s->pages.clear();
+      return fail(OCRVL_E_CUDA, std::string("cudaMemcpy: ") + cudaGetErrorString(e));
+    }
+  }
+  s->len = n;
+  return OCRVL_OK;
+}
 
 int ocrvl_seq_read_kv(ocrvl_seq *s, int layer, float *k, float *v) {
   if (!s || !k || !v) return fail(OCRVL_E_INVALID, "null argument");

@@ -193,6 +193,17 @@ class Sequence_:
         _lib.check(self.rt._L.ocrvl_seq_read_kv(self._h, int(layer), _ptr(k), _ptr(v)))
         return k[:n], v[:n]
 
+    def import_kv(self, k, v) -> None:
+        """Replaces the cache with k, v of shape [num_layers][n][kv_heads *
+        head_dim] (f32) and sets the length to n (ocrvl_seq_import_kv)."""
+        c = self.rt.cfg
+        kvd = c.num_key_value_heads * c.head_dim
+        k = np.ascontiguousarray(k, np.float32)
+        v = np.ascontiguousarray(v, np.float32)
+        if k.shape != v.shape or k.ndim != 3 or k.shape[0] != c.num_hidden_layers or k.shape[2] != kvd:
+            raise ValueError(f"K/V must be [{c.num_hidden_layers}][n][{kvd}] f32, got {k.shape} / {v.shape}")
+        _lib.check(self.rt._L.ocrvl_seq_import_kv(self._h, int(k.shape[1]), _ptr(k), _ptr(v)))
+
 
 class Runtime:
     """Decoder runtime on one CUDA device (one process per GPU)."""

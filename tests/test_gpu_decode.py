@@ -275,3 +275,36 @@ def test_bench_model_greedy_32(q):
     got = rt.generate_with_options(ids, GenerateOptions(max_new_tokens=32, eos_token_ids=[]))
     want = orc.generate(ids, 32, eos=[])
     assert got.tokens == want
+
+
+def test_import_kv_restores_a_cache(tiny_models):
+    """ocrvl_seq_import_kv: the cache of a prefilled sequence, read back and
+    imported into a fresh sequence, reads back unchanged and gives the same
+    next step (ids and logits bit for bit); a length beyond the sequence's
+    capacity is rejected and leaves it unchanged."""
+    _need_gpu()
+    from rapidocrvl_b200 import _lib
+
+    cfg, rt, _ = _pair(tiny_models["q4"], "q4")
+    prompt = synth.random_prompt(41, cfg.vocab_size, 7)  # 40 cached positions: 3 pages, a long cache
+    a = rt.new_sequence(64)
+    b = rt.new_sequence(64)
+    for t in prompt[:-1]:
+        rt.step([a], ids=[t], need_logits=False)
+    L = cfg.num_hidden_layers
+    kv = [a.read_kv(layer) for layer in range(L)]
+    k = np.stack([x[0] for x in kv])
+    v = np.stack([x[1] for x in kv])
+    b.import_kv(k, v)
+    assert len(b) == len(a) == 40
+    for layer in range(L):
+        kb, vb = b.read_kv(layer)
+        assert np.array_equal(kb, k[layer]) and np.array_equal(vb, v[layer])
+    ida, la = rt.step([a], ids=[prompt[-1]], return_logits=True)
+    idb, lb = rt.step([b], ids=[prompt[-1]], return_logits=True)
+    assert int(ida[0]) == int(idb[0])
+    assert np.array_equal(la, lb)
+    too_long = np.zeros((L, 65, k.shape[2]), np.float32)
+    with pytest.raises(_lib.OcrvlError):
+        b.import_kv(too_long, too_long)
+    assert len(b) == 41  # rejected before any change
