@@ -24,11 +24,13 @@
 //             rows, unpacked by all threads to int8 in the K-major core-matrix
 //             layout (8 rows x 16 bytes contiguous; 8-row groups 1 KB apart)
 //     4 MMAs (K = 32 bytes each) issued by one thread into TMEM
-//   through a ring of up to kGemmStages stages (A tile + packed B rows, as
-//   many as the shared memory holds), issued ahead so the copies of later K
-//   tiles overlap the unpacking and the tensor core's work; the unpacked int8
-//   tiles are double-buffered and each MMA batch commits to an mbarrier that
-//   frees its B buffer and its stage.  The epilogue reads D with tcgen05.ld
+//   through a ring of up to kGemmStages stages of u K tiles (u A tiles in one
+//   bulk copy, the packed B rows of u tiles in one 2-D box), as many as the
+//   shared memory holds, issued ahead so later copies overlap the unpacking
+//   and the tensor core's work; per stage all threads unpack its u tiles into
+//   one of two groups of int8 buffers, one barrier, and one thread issues
+//   its 4u MMAs and commits them to mbarriers that free the group and the
+//   stage.  The epilogue reads D with tcgen05.ld
 //   (M = 64 puts sequence r in TMEM lane 32*(r/16) + r%16) and applies the
 //   same finalize and epilogue (store, residual, SwiGLU, argmax) as the
 //   single-sequence kernels.
@@ -65,6 +67,13 @@ __device__ __forceinline__ void tmem_alloc(uint32_t *dst_smem, uint32_t ncols) {
 }
 __device__ __forceinline__ void tmem_dealloc(uint32_t base, uint32_t ncols) {
   asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(base), "r"(ncols));
+}
+// One lane of the (converged) warp: the issuing lane for tcgen05 / TMA
+// instructions whose operands the whole warp computed (warp-uniform values).
+__device__ __forceinline__ bool elect_one_sync() {
+  uint32_t p;
+  asm volatile("{\n\t.reg .pred P;\n\telect.sync _|P, 0xffffffff;\n\tselp.b32 %0, 1, 0, P;\n\t}\n" : "=r"(p));
+  return p != 0;
 }
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
@@ -169,14 +178,12 @@ __host__ __device__ __forceinline__ int gemm_u(int qt, int nt) {
 
 // shared-memory layout of the GEMM phase (bytes from the base):
 //   row scales [2][kMaxNT] f32 | row sums [2][kMaxNT] i32              4 KB
-//   unpacked B tiles [NB buffers][mats][nt][kKT] int8 (core-matrix layout)
+//   unpacked B tiles [2 groups][u][mats][nt][kKT] int8 (core-matrix layout)
 //   stages [S]: u A tiles (u * kGemmA) | packed rows [mats][nt][u * KP]
 //   (1 KB aligned)
-// NB = 8 when eight B buffers take at most a quarter of the memory, else 2;
 // S fills the rest (at most kGemmStages, at most the stages of K).
 constexpr int kGemmA = kMmaM * kKT;  // 8 KB per A tile
 constexpr int kGemmStages = 8;       // ring stages at most
-constexpr int kGemmBBufs = 8;        // unpacked B buffers at most
 constexpr int kGemmScl = 4 * kMaxNT * 4;
 // Least shared memory the phase needs (two stages of the largest tile).
 __host__ __device__ __forceinline__ size_t gemm_b_smem_bytes() {
@@ -197,16 +204,16 @@ __device__ __noinline__ void phase_gemm_b(const Ctx *cp, const BatchedW *bwp, co
   uint8_t *base = (uint8_t *)smem;
   float *s_scl = (float *)base;  // [2][kMaxNT] scales, [2][kMaxNT] row sums
   int32_t *s_rs = (int32_t *)(s_scl + 2 * kMaxNT);
-  uint8_t *sB0 = base + kGemmScl;                        // [NB][mats][NT][kKT]
-  const int sbytes = NT * kKT;
-  const int NB = kGemmBBufs * mats * sbytes * 4 <= bw.smem_avail - kGemmScl ? kGemmBBufs : 2;
-  uint8_t *stg = sB0 + (size_t)NB * mats * sbytes;       // stages
+  uint8_t *sB0 = base + kGemmScl;                        // [2][U][mats][NT][kKT]
+  const int sbytes = NT * kKT;                           // one unpacked tile of one matrix
+  const int gbytes = U * mats * sbytes;                  // one group
+  uint8_t *stg = sB0 + 2 * (size_t)gbytes;               // stages
   const int rowb = U * KP;                               // packed bytes per row per stage
   const int stage_bytes = (U * kGemmA + mats * NT * rowb + 1023) / 1024 * 1024;
   const int nk = a.K / kKT, nsu = (nk + U - 1) / U;
   int S = (bw.smem_avail - (int)(stg - base)) / stage_bytes;
   S = min(min(S, kGemmStages), max(nsu, 2));
-  __shared__ __align__(8) uint64_t bar_ld[kGemmStages], bar_su[kGemmStages], bar_mma[kGemmBBufs];
+  __shared__ __align__(8) uint64_t bar_ld[kGemmStages], bar_su[kGemmStages], bar_grp[2];
   if (S < 2) {  // the host sizes the shared memory for two stages of the largest tile
     if (threadIdx.x == 0) atomicExch(c.err, 1);
     return;
@@ -218,22 +225,22 @@ __device__ __noinline__ void phase_gemm_b(const Ctx *cp, const BatchedW *bwp, co
       mbar_init(&bar_ld[i], 1);
       mbar_init(&bar_su[i], 1);
     }
-    for (int i = 0; i < kGemmBBufs; i++) mbar_init(&bar_mma[i], 1);
+    for (int i = 0; i < 2; i++) mbar_init(&bar_grp[i], 1);
     mbar_fence_init();
   }
   __syncthreads();
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   unsigned long long best = 0ull;  // ARGMAX: lane's sequence best key
   // trace: per-block time stamps of the o projection (16 start, 17 first
-  // copies issued, 18-22 its third K tile: start, waits, unpack, barrier,
-  // MMAs issued, 23 end)
+  // copies issued, 18 first stage's MMAs issued, 23 end)
   const bool mk = a.epi == EPI_RESID && a.resid_mode == RESID_ATTN;
   if (mk) rg_bmark(c, 16);
-  // stage TU of the phase (over all N tiles) uses slot TU % S: bar_ld and
-  // bar_su complete once per use (use TU / S); K tile T uses B buffer T % NB
-  // and commits its MMAs to bar_mma[T % NB] (completion T / NB)
-  int T0 = 0, TU0 = 0;
-  for (int n0 = lo; n0 < hi; n0 += NT, T0 += nk, TU0 += nsu) {
+  // stage TU of the phase (over all N tiles) uses slot TU % S (bar_ld and
+  // bar_su complete once per use, use TU / S) and unpacked group TU & 1
+  // (bar_grp[TU & 1] completes when the stage's MMAs are done, completion
+  // TU >> 1)
+  int TU0 = 0;
+  for (int n0 = lo; n0 < hi; n0 += NT, TU0 += nsu) {
     const int nrows = min(NT, hi - n0);
     // scales / row sums of this N tile
     for (int i = threadIdx.x; i < nrows; i += kThreads) {
@@ -260,101 +267,117 @@ __device__ __noinline__ void phase_gemm_b(const Ctx *cp, const BatchedW *bwp, co
     }
     if (mk && n0 == lo) rg_bmark(c, 17);
     const uint32_t idesc = umma_idesc_i8(NT);
-    for (int t = 0; t < nk; t++) {
-      const int su = t / U, j = t - su * U, TU = TU0 + su, slot = TU % S;
-      const int T = T0 + t, bb = T % NB;
+    for (int su = 0; su < nsu; su++) {
+      const int TU = TU0 + su, slot = TU % S, grp = TU & 1;
+      const int nt_here = min(U, nk - su * U);  // K tiles of this stage
       const uint8_t *sa = stg + (size_t)slot * stage_bytes;
-      const bool mt = mk && n0 == lo && t == 2;
-      if (mt) rg_bmark(c, 18);
-      if (j == 0) mbar_wait(&bar_ld[slot], (uint32_t)(TU / S) & 1u, c.err);
-      // the B buffer's previous MMAs (tile T - NB) are done before it is rewritten
-      if (t >= NB) mbar_wait(&bar_mma[bb], (uint32_t)(T / NB - 1) & 1u, c.err);
-      if (mt) rg_bmark(c, 19);
-      // unpack K tile j of the stage's packed rows to int8 in the core-matrix layout
-      for (int mi = 0; mi < mats; mi++) {
-        const uint8_t *pk_src = sa + U * kGemmA + (size_t)mi * NT * rowb + (size_t)j * KP;
-        uint8_t *dstB = sB0 + (size_t)(bb * mats + mi) * sbytes;
-        if (QT == QT_Q4) {
-          // 16 packed bytes -> 32 int8 = two 16-byte K chunks
-          for (int task = threadIdx.x; task < NT * (KP / 16); task += kThreads) {
-            const int r = task / (KP / 16), c4 = task % (KP / 16);
-            uint4 pk = make_uint4(0, 0, 0, 0);
-            if (r < nrows) pk = *(const uint4 *)(pk_src + (size_t)r * rowb + 16 * c4);
-            const uint32_t w4[4] = {pk.x, pk.y, pk.z, pk.w};
-            uint32_t o[8];
+      uint8_t *sg = sB0 + (size_t)grp * gbytes;
+      const bool ms = mk && n0 == lo && su == 2;
+      if (ms) rg_bmark(c, 19);
+      mbar_wait(&bar_ld[slot], (uint32_t)(TU / S) & 1u, c.err);
+      // the group's previous MMAs (stage TU - 2) are done before it is rewritten
+      if (su >= 2) mbar_wait(&bar_grp[grp], (uint32_t)((TU >> 1) - 1) & 1u, c.err);
+      if (ms) rg_bmark(c, 20);
+      // unpack the stage's K tiles to int8 in the core-matrix layout:
+      // tile j of matrix mi into sg + (j * mats + mi) * sbytes
+      if (QT == QT_Q4) {
+        // 16 packed bytes -> 32 int8 = two 16-byte K chunks
+        const int per = NT * (KP / 16);
+        for (int task = threadIdx.x; task < nt_here * mats * per; task += kThreads) {
+          const int jm = task / per, rc = task - jm * per;
+          const int j = jm / mats, mi = jm - j * mats;
+          const int r = rc / (KP / 16), c4 = rc % (KP / 16);
+          const uint8_t *pk_src = sa + U * kGemmA + (size_t)mi * NT * rowb + (size_t)j * KP;
+          uint8_t *dstB = sg + (size_t)(j * mats + mi) * sbytes;
+          uint4 pk = make_uint4(0, 0, 0, 0);
+          if (r < nrows) pk = *(const uint4 *)(pk_src + (size_t)r * rowb + 16 * c4);
+          const uint32_t w4[4] = {pk.x, pk.y, pk.z, pk.w};
+          uint32_t o[8];
 #pragma unroll
-            for (int jq = 0; jq < 4; jq++) {
-              const uint32_t lo4 = w4[jq] & 0x0F0F0F0Fu, hi4 = (w4[jq] >> 4) & 0x0F0F0F0Fu;
-              // bytes b0..b3 -> (lo0, hi0, lo1, hi1), (lo2, hi2, lo3, hi3); nibble - 8
-              const uint32_t x0 = __byte_perm(lo4, hi4, 0x5140), x1 = __byte_perm(lo4, hi4, 0x7362);
-              o[2 * jq] = __vsub4(x0, 0x08080808u);
-              o[2 * jq + 1] = __vsub4(x1, 0x08080808u);
-            }
-            *(uint4 *)(dstB + cm_off(r, 32 * c4)) = make_uint4(o[0], o[1], o[2], o[3]);
-            *(uint4 *)(dstB + cm_off(r, 32 * c4 + 16)) = make_uint4(o[4], o[5], o[6], o[7]);
+          for (int jq = 0; jq < 4; jq++) {
+            const uint32_t lo4 = w4[jq] & 0x0F0F0F0Fu, hi4 = (w4[jq] >> 4) & 0x0F0F0F0Fu;
+            // bytes b0..b3 -> (lo0, hi0, lo1, hi1), (lo2, hi2, lo3, hi3); nibble - 8
+            const uint32_t x0 = __byte_perm(lo4, hi4, 0x5140), x1 = __byte_perm(lo4, hi4, 0x7362);
+            o[2 * jq] = __vsub4(x0, 0x08080808u);
+            o[2 * jq + 1] = __vsub4(x1, 0x08080808u);
           }
-        } else {
-          // 48 packed bytes -> 64 int8 = four 16-byte K chunks
-          for (int task = threadIdx.x; task < NT * (KP / 48); task += kThreads) {
-            const int r = task / (KP / 48), c3 = task % (KP / 48);
-            uint32_t wd[12];
-            if (r < nrows) {
-              const uint4 *s4 = (const uint4 *)(pk_src + (size_t)r * rowb + 48 * c3);
-              const uint4 x = s4[0], y = s4[1], z = s4[2];
-              const uint32_t t12[12] = {x.x, x.y, x.z, x.w, y.x, y.y, y.z, y.w, z.x, z.y, z.z, z.w};
+          *(uint4 *)(dstB + cm_off(r, 32 * c4)) = make_uint4(o[0], o[1], o[2], o[3]);
+          *(uint4 *)(dstB + cm_off(r, 32 * c4 + 16)) = make_uint4(o[4], o[5], o[6], o[7]);
+        }
+      } else {
+        // 48 packed bytes -> 64 int8 = four 16-byte K chunks
+        const int per = NT * (KP / 48);
+        for (int task = threadIdx.x; task < nt_here * mats * per; task += kThreads) {
+          const int jm = task / per, rc = task - jm * per;
+          const int j = jm / mats, mi = jm - j * mats;
+          const int r = rc / (KP / 48), c3 = rc % (KP / 48);
+          const uint8_t *pk_src = sa + U * kGemmA + (size_t)mi * NT * rowb + (size_t)j * KP;
+          uint8_t *dstB = sg + (size_t)(j * mats + mi) * sbytes;
+          uint32_t wd[12];
+          if (r < nrows) {
+            const uint4 *s4 = (const uint4 *)(pk_src + (size_t)r * rowb + 48 * c3);
+            const uint4 x = s4[0], y = s4[1], z = s4[2];
+            const uint32_t t12[12] = {x.x, x.y, x.z, x.w, y.x, y.y, y.z, y.w, z.x, z.y, z.z, z.w};
 #pragma unroll
-              for (int i = 0; i < 12; i++) wd[i] = t12[i];
-            } else {
+            for (int i = 0; i < 12; i++) wd[i] = t12[i];
+          } else {
 #pragma unroll
-              for (int i = 0; i < 12; i++) wd[i] = 0u;
-            }
+            for (int i = 0; i < 12; i++) wd[i] = 0u;
+          }
 #pragma unroll
-            for (int g = 0; g < 4; g++) {
-              const uint32_t w0 = wd[3 * g], w1 = wd[3 * g + 1], w2 = wd[3 * g + 2];
-              uint32_t f[4] = {q6_spread(w0 & 0xFFFFFFu), q6_spread(__funnelshift_r(w0, w1, 24) & 0xFFFFFFu),
-                               q6_spread(__funnelshift_r(w1, w2, 16) & 0xFFFFFFu), q6_spread(w2 >> 8)};
+          for (int g = 0; g < 4; g++) {
+            const uint32_t w0 = wd[3 * g], w1 = wd[3 * g + 1], w2 = wd[3 * g + 2];
+            uint32_t f[4] = {q6_spread(w0 & 0xFFFFFFu), q6_spread(__funnelshift_r(w0, w1, 24) & 0xFFFFFFu),
+                             q6_spread(__funnelshift_r(w1, w2, 16) & 0xFFFFFFu), q6_spread(w2 >> 8)};
 #pragma unroll
-              for (int i = 0; i < 4; i++) f[i] = r < nrows ? __vsub4(f[i], 0x20202020u) : 0u;
-              *(uint4 *)(dstB + cm_off(r, 64 * c3 + 16 * g)) = make_uint4(f[0], f[1], f[2], f[3]);
-            }
+            for (int i = 0; i < 4; i++) f[i] = r < nrows ? __vsub4(f[i], 0x20202020u) : 0u;
+            *(uint4 *)(dstB + cm_off(r, 64 * c3 + 16 * g)) = make_uint4(f[0], f[1], f[2], f[3]);
           }
         }
       }
-      if (mt) rg_bmark(c, 20);
+      if (ms) rg_bmark(c, 21);
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       tc_fence_before();
       __syncthreads();
       tc_fence_after();
-      if (mt) rg_bmark(c, 21);
-      if (threadIdx.x == 0) {
-        // MMAs of this K tile
-        for (int s4 = 0; s4 < kKT / 32; s4++) {
-          const uint64_t da = umma_desc(sa + (size_t)j * kGemmA + s4 * 256);
-          const uint32_t acc = (t > 0 || s4 > 0) ? 1u : 0u;
-          for (int mi = 0; mi < mats; mi++)
-            umma_i8(tmem + (uint32_t)(mi * NT), da, umma_desc(sB0 + (size_t)(bb * mats + mi) * sbytes + s4 * 256), idesc,
-                    acc);
-        }
-        umma_commit(&bar_mma[bb]);
-        if (mt) rg_bmark(c, 22);
-        if (j == U - 1 || t == nk - 1) {
-          // the stage's MMAs are all issued: its slot frees once they are done
+      if (ms) rg_bmark(c, 22);
+      if (warp == 0) {
+        // MMAs of the stage's K tiles, in K order: warp 0 computes the
+        // descriptors, one elected lane issues
+        const bool leader = elect_one_sync();
+        for (int j = 0; j < nt_here; j++)
+          for (int s4 = 0; s4 < kKT / 32; s4++) {
+            const uint64_t da = umma_desc(sa + (size_t)j * kGemmA + s4 * 256);
+            const uint32_t acc = (su > 0 || j > 0 || s4 > 0) ? 1u : 0u;
+            for (int mi = 0; mi < mats; mi++) {
+              const uint64_t db = umma_desc(sg + (size_t)(j * mats + mi) * sbytes + s4 * 256);
+              if (leader) umma_i8(tmem + (uint32_t)(mi * NT), da, db, idesc, acc);
+            }
+          }
+        if (leader) {
+          umma_commit(&bar_grp[grp]);
           umma_commit(&bar_su[slot]);
-          // the previous stage's slot takes stage su - 1 + S
-          if (su >= 1 && su - 1 + S < nsu) {
-            const int pslot = (TU - 1) % S;
-            mbar_wait(&bar_su[pslot], (uint32_t)((TU - 1) / S) & 1u, c.err);
-            tc_fence_after();
+        }
+        __syncwarp();
+        if (mk && n0 == lo && su == 0) rg_bmark(c, 18);
+        if (ms) rg_bmark(c, 15);
+        // the previous stage's slot takes stage su - 1 + S once its MMAs are done
+        if (su >= 1 && su - 1 + S < nsu) {
+          const int pslot = (TU - 1) % S;
+          mbar_wait(&bar_su[pslot], (uint32_t)((TU - 1) / S) & 1u, c.err);
+          tc_fence_after();
+          if (leader) {
             asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
             issue(su - 1 + S);
           }
+          __syncwarp();
         }
       }
     }
-    // the last tile's MMAs
-    if (nk > 0) {
-      const int TL = T0 + nk - 1;
-      mbar_wait(&bar_mma[TL % NB], (uint32_t)(TL / NB) & 1u, c.err);
+    // the last stage's MMAs (commits complete in order: all are done)
+    if (nsu > 0) {
+      const int TL = TU0 + nsu - 1;
+      mbar_wait(&bar_grp[TL & 1], (uint32_t)(TL >> 1) & 1u, c.err);
       tc_fence_after();
       __syncthreads();
     }
