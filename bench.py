@@ -41,6 +41,8 @@ def parse():
     ap.add_argument("--prompt", type=int, default=PROMPT)
     ap.add_argument("--workload", default="configs1", choices=["configs1", "configs3"],
                     help="configs1: batch 1, 512-token prompt (headline); configs3: 64 sequences, contexts U[256, 4096]")
+    ap.add_argument("--ctx-hi", type=int, default=4096,
+                    help="configs3: contexts drawn U[256, ctx_hi] (4096 is the workload; smaller for profiling captures)")
     ap.add_argument("--kv", default="prefill", choices=["prefill", "synthetic"],
                     help="configs3 caches: prompt prefill through steps, or seeded K/V imported directly")
     return ap.parse_args()
@@ -342,7 +344,7 @@ def run_batched(args):
     cfg = config.load(d)
     n = 64
     rng = np.random.default_rng(2 + rank)
-    lens = rng.integers(256, 4097, size=n).tolist()
+    lens = rng.integers(256, args.ctx_hi + 1, size=n).tolist()
     total_new = args.warmup + args.steps + 1
     rt = Runtime.load(d, LoadOptions(quantization=args.quant, device=local, max_position=8192,
                                      kv_pool_bytes=int(sum(lens) + n * (total_new + 32)) * 36864 + (256 << 20)))
@@ -393,15 +395,25 @@ def run_batched(args):
         "metric": METRIC, "value": n * args.steps / (ms / 1e3), "unit": UNIT, "n_gpus": 1, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "i8/f32", "data": "synthetic (seeded weights; uniform prompt ids)",
-        "config": {"workload": f"configs[3]: {args.quant.upper()}, 64 sequences, contexts U[256,4096] (seed 2), "
+        "config": {"workload": f"configs[3]: {args.quant.upper()}, 64 sequences, contexts U[256,{args.ctx_hi}] (seed 2), "
                                f"16-token pages, {args.warmup}+{args.steps} steps of one token per sequence",
                    "kv": "prompt prefill" if args.kv == "prefill" else "seeded N(0,1) K/V imported",
                    "setup_s": round(t_pre, 1), "mean_context": float(np.mean(ctx0)) + args.steps / 2,
                    "l2": "no flush: per-step KV (~5.6 GB) + weights > 126 MB L2"},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                     "kernel": "k_step_b (one persistent launch per step)",
                      "algorithmic_bytes_per_step": bytes_per_step, "traffic": None},
         "gpu_launches": args.steps,
     }
+    traffic_path = os.path.join(ROOT, "profiles", "k_step_b_traffic.json")
+    if os.path.exists(traffic_path):
+        with open(traffic_path) as f:
+            tj = json.load(f)
+        if tj.get("quant") == args.quant:
+            # one ncu capture of a smaller case, scaled by the algorithmic bytes
+            # (the K/V stream dominates both)
+            line["roofline"]["traffic"] = tj["dram_bytes_per_step"] * bytes_per_step / tj["algorithmic_bytes_per_step"]
+            line["roofline"]["traffic_source"] = tj.get("source") + ", scaled by algorithmic bytes"
     rt.close()
     print(json.dumps(line), flush=True)
     return 0

@@ -823,7 +823,9 @@ __device__ void argmax_finish(const Ctx &c, int M, int feed) {
     c.tok_out[m] = id;
     c.argkey[m] = 0ull;
     if (feed) {
-      int step = *c.hist_pos;
+      // through L2: another block may have advanced it in an earlier step
+      // of the same launch (device-fed loop)
+      int step = __ldcg(c.hist_pos);
       c.hist[(size_t)step * M + m] = id;
       int len = sp.seq[m].len + 1;
       spw.seq[m].tok = id;
@@ -834,7 +836,7 @@ __device__ void argmax_finish(const Ctx &c, int M, int feed) {
   __syncthreads();
   if (threadIdx.x == 0) {
     if (feed) {
-      *c.hist_pos += 1;
+      atomicAdd(c.hist_pos, 1);  // at L2, like the read above
       spw.max_n = sp.max_n + 1;
     }
     *c.lm_count = 0u;

@@ -274,43 +274,67 @@ __device__ __forceinline__ float *align_dyn_smem(void *p) {
 
 template <int QT>
 __global__ void __launch_bounds__(kThreads, 1)
-    k_step(Ctx cv, int M, int any_logits, int do_embed, int feed, unsigned bar_base) {
+    k_step(Ctx cv, int M, int any_logits, int do_embed, int feed, unsigned bar_base, int nsteps) {
   extern __shared__ float4 smem4[];
   float *smem = align_dyn_smem(smem4);
   OCRVL_CTX_TO_SMEM(cv);
+  if (nsteps > 1) {  // the trace holds one step
+    Ctx &cm = sctx;
+    if (threadIdx.x == 0) cm.trace = nullptr;
+    __syncthreads();
+  }
   attn_block_init(c);
   ring_init();
   unsigned k = 0;
-  int t = 0;
-  if (threadIdx.x >= kHelper) prepare_phase<QT>(c, 0, 0, M, any_logits, do_embed, feed, smem, 0);
-  __syncthreads();
-  for (int l = 0; l < c.L; l++) {
-    const bool kv_only = l == c.L - 1 && !any_logits;
-    for (int ph = 0; ph < kLayerPhases; ph++, t++) {
-      run_phase<QT>(c, ph, l, M, any_logits, do_embed, feed, smem, t, 1, is_gemv_phase(ph));
-      if (kv_only && ph == 1) return;
+  for (int st = 0; st < nsteps; st++) {
+    if (st > 0) {
+      // the next device-fed step: the previous step's lm_head phase (its last
+      // block) wrote the step parameters; every block reloads them (from L2)
+      // and the per-launch attention geometry
       grid_arrive(c);
-      // while thread 0 waits for the other blocks, the helper threads set up
-      // the next phase and (once per launch) the RoPE values of this step
-      if (threadIdx.x >= kHelper) {
-        const bool more = ph + 1 < kLayerPhases || l + 1 < c.L || any_logits;
-        if (more) {
-          const int nph = ph + 1 < kLayerPhases ? ph + 1 : (l + 1 < c.L ? 0 : kPhaseLM);
-          const int nl = ph + 1 < kLayerPhases ? l : l + 1;
-          if (!(nl == c.L - 1 && !any_logits && nph > 1))
-            prepare_phase<QT>(c, nph, nl, M, any_logits, do_embed, feed, smem, t + 1);
-        }
-        if (l == 0 && ph == 0) attn_rope_tables(c, kHelper);
-      }
       if (!grid_wait(c, bar_base + (++k) * gridDim.x)) {
         attn_drain(c);
         gemv_drain(c);
         return;
       }
-      if (c.trace && blockIdx.x == 0 && threadIdx.x == 0) c.trace[4 * t + 3] = gtimer();
+      for (int i = threadIdx.x; i < (int)sizeof(StepParams) / 4; i += kThreads)
+        ((int *)&s_step_params)[i] = __ldcg((const int *)cv.sp + i);
+      if (threadIdx.x == 0) s_rope_ready = 0;
+      __syncthreads();
+      rg_launch_init(c);
+      __syncthreads();
     }
+    int t = 0;
+    if (threadIdx.x >= kHelper) prepare_phase<QT>(c, 0, 0, M, any_logits, do_embed, feed, smem, 0);
+    __syncthreads();
+    for (int l = 0; l < c.L; l++) {
+      const bool kv_only = l == c.L - 1 && !any_logits;
+      for (int ph = 0; ph < kLayerPhases; ph++, t++) {
+        run_phase<QT>(c, ph, l, M, any_logits, do_embed, feed, smem, t, 1, is_gemv_phase(ph));
+        if (kv_only && ph == 1) return;
+        grid_arrive(c);
+        // while thread 0 waits for the other blocks, the helper threads set up
+        // the next phase and (once per step) the RoPE values of this step
+        if (threadIdx.x >= kHelper) {
+          const bool more = ph + 1 < kLayerPhases || l + 1 < c.L || any_logits;
+          if (more) {
+            const int nph = ph + 1 < kLayerPhases ? ph + 1 : (l + 1 < c.L ? 0 : kPhaseLM);
+            const int nl = ph + 1 < kLayerPhases ? l : l + 1;
+            if (!(nl == c.L - 1 && !any_logits && nph > 1))
+              prepare_phase<QT>(c, nph, nl, M, any_logits, do_embed, feed, smem, t + 1);
+          }
+          if (l == 0 && ph == 0) attn_rope_tables(c, kHelper);
+        }
+        if (!grid_wait(c, bar_base + (++k) * gridDim.x)) {
+          attn_drain(c);
+          gemv_drain(c);
+          return;
+        }
+        if (c.trace && blockIdx.x == 0 && threadIdx.x == 0) c.trace[4 * t + 3] = gtimer();
+      }
+    }
+    if (any_logits) run_phase<QT>(c, kPhaseLM, c.L, M, any_logits, do_embed, feed, smem, t, 1, true);
   }
-  if (any_logits) run_phase<QT>(c, kPhaseLM, c.L, M, any_logits, do_embed, feed, smem, t, 1, true);
 }
 
 template <int QT>
@@ -739,15 +763,18 @@ void setup_batched(ocrvl_model *m) {
 }
 
 template <int QT>
-int launch_step_q(ocrvl_model *m, int M, int any_logits, int do_embed, int feed) {
+int launch_step_q(ocrvl_model *m, int M, int any_logits, int do_embed, int feed, int nsteps = 1) {
   Ctx c = m->ctx;
   if (m->persistent) {
     unsigned base = m->bar_base;
-    void *args[] = {&c, &M, &any_logits, &do_embed, &feed, &base};
+    void *args[] = {&c, &M, &any_logits, &do_embed, &feed, &base, &nsteps};
     CK(cudaLaunchCooperativeKernel((void *)k_step<QT>, dim3(m->grid), dim3(kThreads), args, m->smem, m->stream));
-    m->bar_base += barriers_per_step(m->desc.num_layers, any_logits) * (unsigned)m->grid;
+    // each step's barriers, and one between consecutive steps
+    m->bar_base += ((unsigned)nsteps * barriers_per_step(m->desc.num_layers, any_logits) + (unsigned)(nsteps - 1)) *
+                   (unsigned)m->grid;
     return OCRVL_OK;
   }
+  if (nsteps != 1) return fail(OCRVL_E_INVALID, "several steps per launch need the persistent step kernel");
   for (int l = 0; l < m->desc.num_layers; l++) {
     bool kv_only = l == m->desc.num_layers - 1 && !any_logits;
     for (int ph = 0; ph < kLayerPhases; ph++) {
@@ -1400,7 +1427,15 @@ int decode_group(ocrvl_model *m, ocrvl_seq *const *seqs, int n, const int32_t *f
   CK(cudaMemsetAsync(m->ctx.hist_pos, 0, 4, m->stream));
   CK(cudaMemcpyAsync(m->sp_d, &sp, step_params_bytes(n), cudaMemcpyHostToDevice, m->stream));
   int rc = OCRVL_OK;
-  for (int st = 0; st < steps && rc == OCRVL_OK; st++) rc = launch_step(m, n, 1, 1, 1);
+  if (n <= kMaxBatch && m->persistent) {
+    // every step in one persistent launch (the token feedback stays on the
+    // device; no launch between steps)
+    rc = m->qtype == QT_Q4   ? launch_step_q<QT_Q4>(m, n, 1, 1, 1, steps)
+         : m->qtype == QT_Q6 ? launch_step_q<QT_Q6>(m, n, 1, 1, 1, steps)
+                             : launch_step_q<QT_Q8>(m, n, 1, 1, 1, steps);
+  } else {
+    for (int st = 0; st < steps && rc == OCRVL_OK; st++) rc = launch_step(m, n, 1, 1, 1);
+  }
   m->ctx.hist = nullptr;
   if (rc == OCRVL_OK) {
     cudaError_t e1 = cudaMemcpyAsync(out_ids, hist, (size_t)steps * n * 4, cudaMemcpyDeviceToHost, m->stream);
