@@ -22,8 +22,8 @@
 //   T    sum of s v over the positions at or above nv, which the reference
 //        weights by their raw score (expF32VecFMA leaves the tail
 //        unexponentiated, internal/tensor/dot_amd64.s:6131-6168).
-// The block that completes the last segment of (m, g) merges, in segment
-// order: head = (T + sum_k exp(m_k - M) o_k) / sum_k exp(m_k - M) l_k with
+// The block holding the last segment of (m, g) merges, once every segment
+// has arrived, in segment order: head = (T + sum_k exp(m_k - M) o_k) / sum_k exp(m_k - M) l_k with
 // M = max_k m_k (the reference's max over all n scores and its 1/sum).
 //
 // Chunk work (256 threads).  Scores: warp w takes the chunk's tokens
@@ -375,7 +375,7 @@ __device__ __forceinline__ void rg_prefetch_run(const Ctx &c, const StepParams &
   asm volatile("cp.async.commit_group;" ::: "memory");
 }
 
-// All threads of the block that completed pair (m, g): its segments'
+// All threads of the block that merges pair (m, g): its segments'
 // partials (o [nseg][G][128], maxima / sums [nseg][G][2], the tail sums
 // [G][128]) arrive by bulk copies in `stage` (nseg * 4 KB <= 128 KB) and
 // `aux`; warp h merges head h, lane dims 4 lane .. 4 lane + 3.
@@ -445,7 +445,6 @@ __device__ __noinline__ void phase_attn_range(const Ctx *cp, int layer, float *s
   float *sm = rg_small(c, sp.M, smem);
   float *qs = sm + kRgQs, *S = sm + kRgS, *W = sm + kRgW, *alph = sm + kRgAlpha, *red = sm + kRgRed;
   float *knew = sm + kRgKnew, *Tsm = sm + kRgT;
-  __shared__ int s_merge;
   RgCur cur = s_rg_first;
   if (threadIdx.x == 0) ((int *)(sm + kRgMerge))[0] = 0;
   if (!rg_in(cur, hi)) return;
@@ -698,32 +697,28 @@ __device__ __noinline__ void phase_attn_range(const Ctx *cp, int layer, float *s
       // the merger reads the partials with bulk copies (async proxy)
       asm volatile("fence.proxy.async.global;" ::: "memory");
     }
-    // ---- run end: arrival of the run's segments, merge by the block that
-    // completes the pair
+    // ---- run end: arrival of the run's segments (no reply awaited); the
+    // block holding the pair's last segment merges it after its range work
     __syncthreads();
     if (threadIdx.x == 0) {
       // release: the block's partials (ordered before by the barrier) become
-      // visible with the count; acquire: the merger sees the others' partials
+      // visible with the count
       unsigned *cntp = c.attn_count + 2 * (m * c.KVH + g);
-      unsigned v;
-      asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], %2;" : "=r"(v) : "l"(cntp), "r"(k1 - k0) : "memory");
-      s_merge = (int)v + (k1 - k0) == cur.nseg;
-      if (s_merge) cntp[0] = 0u;
+      asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(cntp), "r"(k1 - k0) : "memory");
+      if (k1 == cur.nseg) {
+        // merged after the phase (rg_merge_pending); a step has at most
+        // kRgMerges (sequence, kv head) pairs (checked on the host)
+        int *ml = (int *)(sm + kRgMerge);
+        const int q = ml[0];
+        ml[4 + 2 * q] = m | g << 8 | cur.nseg << 16;
+        ml[4 + 2 * q + 1] = cur.sbase + g * cur.nseg;
+        ml[0] = q + 1;
+        if (c.trace) c.trace[4 * kTraceRows + kTraceMarks * blockIdx.x + 15] += 1000 + cur.nseg;
+      }
     }
-    __syncthreads();
     if (ridx == 0) {
       rg_mark(c, layer, 2);
       rg_bmark(c, 8);
-    }
-    if (s_merge && threadIdx.x == 0) {
-      // merged after the phase (rg_merge_pending); a step has at most
-      // kRgMerges (sequence, kv head) pairs (checked on the host)
-      int *ml = (int *)(sm + kRgMerge);
-      const int q = ml[0];
-      ml[4 + 2 * q] = m | g << 8 | cur.nseg << 16;
-      ml[4 + 2 * q + 1] = cur.sbase + g * cur.nseg;
-      ml[0] = q + 1;
-      if (c.trace) c.trace[4 * kTraceRows + kTraceMarks * blockIdx.x + 15] += 1000 + cur.nseg;
     }
     cur = nxt;
     ridx++;
@@ -738,8 +733,8 @@ __device__ __noinline__ void phase_attn_range(const Ctx *cp, int layer, float *s
   if (c.trace && threadIdx.x == 0) c.trace[4 * kTraceRows + kTraceMarks * blockIdx.x + 14] = (unsigned long long)ci * 1000 + ridx;
 }
 
-// All threads, after phase_attn_range: the merges of the pairs this block
-// completed, staged through the chunk buffers (contiguous: ring slots
+// All threads, after phase_attn_range: the merges of the pairs whose last
+// segment this block holds, staged through the chunk buffers (contiguous: ring slots
 // 1 .. kRangeBufs for single-sequence steps, the first kRangeBufs slots
 // otherwise) and the small arrays before the list.
 __device__ __noinline__ void rg_merge_pending(const Ctx *cp, float *smem) {
@@ -748,11 +743,32 @@ __device__ __noinline__ void rg_merge_pending(const Ctx *cp, float *smem) {
   float *sm = rg_small(c, sp.M, smem);
   const int *ml = (const int *)(sm + kRgMerge);
   float *stage = rg_buf(c, sp.M, smem, sp.M <= 1 ? kRangeBufs - 1 : 0);
+  __shared__ int s_ok;
   const int q = ml[0];
   for (int i = 0; i < q; i++) {
     const int a = ml[4 + 2 * i], sb = ml[4 + 2 * i + 1];
     const int m = a & 255, g = (a >> 8) & 255, nseg = a >> 16;
-    rg_merge(c, m, g, sp.seq[m].len + 1, sb, nseg, stage, sm);
+    if (threadIdx.x == 0) {
+      // every segment of the pair has arrived (bounded wait: every block
+      // posts all its arrivals before it waits for any)
+      unsigned *cntp = c.attn_count + 2 * (m * c.KVH + g);
+      long long spins = 0;
+      int ok = 1;
+      while (true) {
+        unsigned v;
+        asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(cntp) : "memory");
+        if ((int)v >= nseg) break;
+        if (++spins > kMbarSpins || *(volatile int *)c.err) {
+          atomicExch(c.err, 1);
+          ok = 0;
+          break;
+        }
+      }
+      if (ok) cntp[0] = 0u;  // for the next layer (its arrivals follow a grid barrier)
+      s_ok = ok;
+    }
+    __syncthreads();
+    if (s_ok) rg_merge(c, m, g, sp.seq[m].len + 1, sb, nseg, stage, sm);
   }
 }
 
