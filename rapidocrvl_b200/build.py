@@ -15,7 +15,6 @@ ROOT = os.path.dirname(HERE)
 CSRC = os.path.join(HERE, "csrc")
 LIB = os.path.join(HERE, "libocrvl_cuda.so")
 SOURCES = ["engine.cu"]
-DEPS = ["engine.cu", "decoder.cuh", "numerics.cuh"]
 
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",
@@ -36,7 +35,8 @@ def needs_build() -> bool:
     if not os.path.exists(LIB):
         return True
     t = os.path.getmtime(LIB)
-    files = [os.path.join(CSRC, f) for f in DEPS] + [os.path.join(ROOT, "include", "ocrvl_cuda.h")]
+    files = [os.path.join(CSRC, f) for f in os.listdir(CSRC) if f.endswith((".cu", ".cuh"))]
+    files.append(os.path.join(ROOT, "include", "ocrvl_cuda.h"))
     return any(os.path.getmtime(f) > t for f in files)
 
 

@@ -26,16 +26,20 @@
 // has arrived, in segment order: head = (T + sum_k exp(m_k - M) o_k) / sum_k exp(m_k - M) l_k with
 // M = max_k m_k (the reference's max over all n scores and its 1/sum).
 //
-// Chunk work (256 threads).  Scores: warp w takes the chunk's tokens
-// 4w .. 4w+3, lanes 0-15 the first two and lanes 16-31 the other two, for all
-// G query heads of the kv head.  Lane slot s multiplies dims s + 16 j
-// (j = 0..7) and sums them as ((p0+p1)+(p2+p3))+((p4+p5)+(p6+p7)); a
+// Chunk work (256 threads, each warp on its own).  Warp w takes the chunk's
+// tokens 4w .. 4w+3 for all G query heads of the kv head, with the run's q in
+// registers.  Scores: lanes 0-15 the first two tokens, lanes 16-31 the other
+// two; lane slot s multiplies dims s + 16 j (j = 0..7) and sums them as
+// ((p0+p1)+(p2+p3))+((p4+p5)+(p6+p7)) (packed in pairs (p_j, p_j+4)); a
 // reduce-scatter over the 16 slots (xor 8, 4, 2, 1) then leaves one
 // (token, head) score per lane.  That is the reference's dotF32 order (16
 // slot accumulators, the tree16 of the slots), so each score equals the
-// single-item path's bit for bit.  Softmax: warp h updates head h over the
-// chunk's 32 scores.  Values: thread (dim d, token half) accumulates d of all
-// G heads over its 16 tokens; the halves are added at the segment's end.
+// single-item path's bit for bit.  The warp keeps its own running max, sum
+// and o (lane dims 4 lane .. 4 lane + 3 of every head) over its tokens of the
+// segment, so a chunk needs no block barrier; at the segment's end the
+// warps' partials are combined in warp order through the buffer of the
+// segment's last chunk.  A warp done with a buffer counts itself out; the
+// last one issues the buffer's next chunk.
 
 namespace ocrvl {
 
@@ -48,20 +52,24 @@ static_assert(kMaxGroup == 8 && kHeadDim == 128, "score layout: 8 heads x 2 toke
 static_assert(kSegMax <= 32, "merge: one segment per lane");
 
 // Small arrays of the range phase (floats from their base).
-constexpr int kRgQs = 0;                                  // [8][128] rotated q
+// rotated q by lane: [half-warp grp][head][2][slot][4]: for lane slot s, the
+// dims (16 (j ^ grp) + s, +64) for j = 0, 1 then j = 2, 3
+constexpr int kRgQs = 0;
 constexpr int kRgPreLen = 8 * 128 + 128 + 128 + 64 + 64;  // raw q | new k | new v | cos | sin
-constexpr int kRgPre = kRgQs + 8 * 128;                   // two prefetch buffers
+constexpr int kRgPre = kRgQs + 2 * 8 * 128;               // two prefetch buffers
 constexpr int kRgKnew = kRgPre + 2 * kRgPreLen;           // [128] rotated new k, [128] new v
-constexpr int kRgS = kRgKnew + 256;                       // [8 heads][32 tokens] scores
-constexpr int kRgW = kRgS + 256;                          // [32 tokens][8 heads] weights
-constexpr int kRgAlpha = kRgW + 256;                      // [8] rescale factors
-constexpr int kRgRed = kRgAlpha + 32;                     // [8][128] o of token half 1
-constexpr int kRgT = kRgRed + 8 * 128;                    // [2 halves][8][128] raw-weighted tail sums
+constexpr int kRgWarps = kThreads / 32;                   // warps of the block
+// per warp: weights [4 tokens][8 heads] as (w, w) pairs | rescale factors [8]
+// as (a, a) pairs | raw weights [4 tokens][8 heads]
+constexpr int kRgWpW = 0, kRgWpA = 64, kRgWpRaw = 80, kRgWpLen = 112;
+constexpr int kRgWp = kRgKnew + 256;                      // [kRgWarps][kRgWpLen]
+constexpr int kRgMl = kRgWp + kRgWarps * kRgWpLen;        // [kRgWarps][8 heads][2] running max, sum
 constexpr int kRgMerges = 2 * kMaxSeqs;                   // pairs a block can complete in one phase
-constexpr int kRgMerge = kRgT + 2 * 8 * 128;              // count, then [kRgMerges][2] pairs to merge (ints)
+constexpr int kRgMerge = kRgMl + kRgWarps * 8 * 2;        // count, then [kRgMerges][2] pairs to merge (ints)
 constexpr int kRgFloats = kRgMerge + 4 + 2 * kRgMerges;
 static_assert(kRgFloats * 4 <= kStageBytes, "small arrays fit one ring slot");
-static_assert(kRgPreLen % 4 == 0 && kRgPre % 4 == 0, "16-byte aligned prefetch buffers");
+static_assert(kRgPreLen % 4 == 0 && kRgPre % 4 == 0 && kRgWp % 4 == 0 && kRgWpLen % 4 == 0, "16-byte aligned arrays");
+static_assert(kRgWarps * kMaxGroup * kHeadDim * 4 <= kStageBytes, "the warps' partials fit one chunk buffer");
 
 // Shared memory the range phase needs when M > 1 (its buffers then start at
 // the base of the dynamic shared memory; for M <= 1 they use ring slots
@@ -157,10 +165,14 @@ __shared__ __align__(8) uint64_t s_rg_mbar;  // merge copies
 __shared__ uint32_t s_rg_par, s_rg_mpar;
 __shared__ int s_rg_issued;
 __shared__ RgCur s_rg_icur;
+__shared__ unsigned s_rg_rel[kRangeBufs];  // warps done with each buffer's current chunk
 
 __device__ __forceinline__ void rg_block_init() {
   if (threadIdx.x == 0) {
-    for (int j = 0; j < kRangeBufs; j++) mbar_init(&s_rg_full[j], 1);
+    for (int j = 0; j < kRangeBufs; j++) {
+      mbar_init(&s_rg_full[j], 1);
+      s_rg_rel[j] = 0;
+    }
     mbar_init(&s_rg_mbar, 1);
     mbar_fence_init();
     s_rg_par = 0;
@@ -309,6 +321,22 @@ __device__ __forceinline__ float *rg_row(float *buf, int t, int kind) {
   return buf + (size_t)(((t >> 4) * 2 + kind) * kPageTokens + (t & 15)) * kHeadDim;
 }
 
+// One thread: the copies of the chunk at cursor r (its one or two pages, K
+// and V rows of each) into buffer b.
+__device__ __forceinline__ void rg_issue_chunk(const Ctx &c, int layer, float *smem, const RgCur &r, int b) {
+  const StepParams &sp = *c.sp;
+  constexpr uint32_t pb = 2u * kPageTokens * kHeadDim * 4;  // K and V rows of one page
+  float *buf = rg_buf(c, sp.M, smem, b);
+  const int o = rg_start(r) + 2 * r.j;
+  const bool two = rg_seg_np(r) - 2 * r.j >= 2;
+  const int pg0 = rg_pool_page(sp, r, o);
+  const int pg1 = two ? rg_pool_page(sp, r, o + 1) : 0;
+  uint64_t *bar = &s_rg_full[b];
+  mbar_expect_tx(bar, (two ? 2u : 1u) * pb);
+  bulk_g2s(buf, rg_page_kv(c, pg0, layer, r.g), pb, bar);
+  if (two) bulk_g2s(buf + 2 * kPageTokens * kHeadDim, rg_page_kv(c, pg1, layer, r.g), pb, bar);
+}
+
 // One thread: issues chunks while fewer than `upto` have been issued and the
 // block's range has more (chunk i into buffer i % kRangeBufs).
 __device__ void rg_issue_upto(const Ctx &c, int layer, float *smem, int upto) {
@@ -318,29 +346,33 @@ __device__ void rg_issue_upto(const Ctx &c, int layer, float *smem, int upto) {
   int i = s_rg_issued;
   if (i >= upto || !rg_in(r, hi)) return;
   // before a phase's first copy: the buffers were last written by ordinary
-  // stores in earlier phases (later, the threads that patch a chunk fence
-  // their own stores; reads need no fence before a copy overwrites them)
+  // stores in earlier phases (later, the threads that store into a buffer
+  // fence their own stores; reads need no fence before a copy overwrites them)
   if (i == 0) asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-  constexpr uint32_t pb = 2u * kPageTokens * kHeadDim * 4;  // K and V rows of one page
   for (; i < upto && rg_in(r, hi); i++) {
-    const int b = i % kRangeBufs;
-    float *buf = rg_buf(c, sp.M, smem, b);
-    const int o = rg_start(r) + 2 * r.j;
-    const bool two = r.k * r.S + rg_seg_np(r) - (r.k * r.S + 2 * r.j) >= 2;
-    const int pg0 = rg_pool_page(sp, r, o);
-    const int pg1 = two ? rg_pool_page(sp, r, o + 1) : 0;
-    uint64_t *bar = &s_rg_full[b];
-    if (i == 4) rg_bmark(c, 19);
-    mbar_expect_tx(bar, (two ? 2u : 1u) * pb);
-    if (i == 4) rg_bmark(c, 20);
-    bulk_g2s(buf, rg_page_kv(c, pg0, layer, r.g), pb, bar);
-    if (i == 4) rg_bmark(c, 21);
-    if (two) bulk_g2s(buf + 2 * kPageTokens * kHeadDim, rg_page_kv(c, pg1, layer, r.g), pb, bar);
-    if (i == 4) rg_bmark(c, 22);
+    rg_issue_chunk(c, layer, smem, r, i % kRangeBufs);
     rg_next_chunk(c, sp, r);
   }
   s_rg_icur = r;
   s_rg_issued = i;
+}
+
+// One lane of each warp, once the warp is done with the buffer of chunk ci
+// (cursor r): the last of the kRgWarps arrivals (atom.inc wraps the count
+// back to 0) issues the chunk kRangeBufs later in the block's range into the
+// same buffer.
+__device__ __forceinline__ void rg_release(const Ctx &c, int layer, float *smem, RgCur r, int ci) {
+  const int b = ci % kRangeBufs;
+  unsigned old;
+  asm volatile("atom.acq_rel.cta.shared::cta.inc.u32 %0, [%1], %2;"
+               : "=r"(old)
+               : "r"(smem_u32(&s_rg_rel[b])), "r"((unsigned)(kRgWarps - 1))
+               : "memory");
+  if (old != (unsigned)(kRgWarps - 1)) return;
+  const StepParams &sp = *c.sp;
+#pragma unroll 1
+  for (int i = 0; i < kRangeBufs && r.m >= 0; i++) rg_next_chunk(c, sp, r);
+  if (rg_in(r, s_rg_hi)) rg_issue_chunk(c, layer, smem, r, b);
 }
 
 // Waits for range copies issued ahead of a phase that did not run (thread 0).
@@ -439,16 +471,16 @@ __device__ __noinline__ void phase_attn_range(const Ctx *cp, int layer, float *s
   const int G = c.QH / c.KVH;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int slot = lane & 15, grp = lane >> 4;
-  const int d = threadIdx.x & 127, th = threadIdx.x >> 7;
   rg_bmark(c, 1);
   const int hi = s_rg_hi;
   float *sm = rg_small(c, sp.M, smem);
-  float *qs = sm + kRgQs, *S = sm + kRgS, *W = sm + kRgW, *alph = sm + kRgAlpha, *red = sm + kRgRed;
-  float *knew = sm + kRgKnew, *Tsm = sm + kRgT;
+  float *qs = sm + kRgQs, *knew = sm + kRgKnew, *mlw = sm + kRgMl;
+  float *wp = sm + kRgWp + warp * kRgWpLen;  // this warp's weights and rescale factors
   RgCur cur = s_rg_first;
   if (threadIdx.x == 0) ((int *)(sm + kRgMerge))[0] = 0;
   if (!rg_in(cur, hi)) return;
   if (threadIdx.x == 0) rg_issue_upto(c, layer, smem, kRangeBufs);
+  const uint32_t par0 = s_rg_par;  // parity of each buffer's next completion
   rg_bmark(c, 2);
   rg_prefetch_run(c, sp, cur, sm + kRgPre);
   int ci = 0;    // chunk index in the block's stream
@@ -474,8 +506,16 @@ __device__ __noinline__ void phase_attn_range(const Ctx *cp, int layer, float *s
           const int hh = p >> 4, i4 = p & 15;
           float4 a = ((const float4 *)(pre + hh * kHeadDim))[i4], b = ((const float4 *)(pre + hh * kHeadDim + 64))[i4];
           if (has_rope) rope4(a, b, rc + 4 * i4, rs + 4 * i4);
-          ((float4 *)(qs + hh * kHeadDim))[i4] = a;
-          ((float4 *)(qs + hh * kHeadDim + 64))[i4] = b;
+          const float av[4] = {a.x, a.y, a.z, a.w}, bv[4] = {b.x, b.y, b.z, b.w};
+#pragma unroll
+          for (int e = 0; e < 4; e++) {
+            const int d = 4 * i4 + e, jd = d >> 4, sd = d & 15;  // dims d and d + 64
+#pragma unroll
+            for (int gg = 0; gg < 2; gg++) {
+              const int jp = jd ^ gg;
+              *(float2 *)(qs + (((gg * 8 + hh) * 2 + (jp >> 1)) * 16 + sd) * 4 + (jp & 1) * 2) = make_float2(av[e], bv[e]);
+            }
+          }
         } else if (p < G * 16 + 16) {
           const int i4 = p - G * 16;
           float4 a = ((const float4 *)(pre + 1024))[i4], b = ((const float4 *)(pre + 1024 + 64))[i4];
@@ -493,6 +533,8 @@ __device__ __noinline__ void phase_attn_range(const Ctx *cp, int layer, float *s
       rg_mark(c, layer, 0);
       rg_bmark(c, 4);
     }
+    // this lane's q pairs of head h: qlane[2 h], qlane[2 h + 1]
+    const ulonglong2 *qlane = (const ulonglong2 *)qs + (grp * 8 * 2) * 16 + slot;
     RgCur nxt = cur;  // the next run: the first segment after this run
     nxt.k = k1 - 1;
     rg_next_seg(c, sp, nxt);
@@ -500,205 +542,215 @@ __device__ __noinline__ void phase_attn_range(const Ctx *cp, int layer, float *s
 #pragma unroll 1
     for (int k = k0; k < k1; k++) {
       cur.k = k;
-      const bool last_seg = k == cur.nseg - 1;
-      float m_run = -INFINITY, l_run = 0.0f;  // warp h < G: head h
-      f2x o2[4];  // o of heads (2 p, 2 p + 1)
+      // warp state over its tokens of the segment: running max and sum of
+      // head (lane & 7); o of head h at dims (4 lane, +1), (4 lane + 2, +3)
+      float m_run = -INFINITY, l_run = 0.0f;
+      f2x o2[8][2];
 #pragma unroll
-      for (int p = 0; p < 4; p++) o2[p] = 0ull;
+      for (int h = 0; h < 8; h++) o2[h][0] = o2[h][1] = 0ull;
       const int seg_np = rg_seg_np(cur);
       const int nck = (seg_np + 1) / 2;
       const int sp0 = k * cur.S;  // first page of the segment
 #pragma unroll 1
       for (int j = 0; j < nck; j++, ci++) {
+        cur.j = j;
         const int b = ci % kRangeBufs;
         float *Kb = rg_buf(c, sp.M, smem, b);  // rows by rg_row
-        const int p0 = sp0 + 2 * j;
-        const int t0 = p0 * kPageTokens;
-        const int cnt = min(min(2, sp0 + seg_np - p0) * kPageTokens, n - t0);
-        if (ci == 1) rg_bmark(c, 10);
-        mbar_wait(&s_rg_full[b], (s_rg_par >> b) & 1u, c.err);
+        const int t0 = (sp0 + 2 * j) * kPageTokens;
+        const int cnt = min(min(2, seg_np - 2 * j) * kPageTokens, n - t0);
+        mbar_wait(&s_rg_full[b], ((par0 >> b) ^ (uint32_t)(ci / kRangeBufs)) & 1u, c.err);
         if (ci == 0) rg_bmark(c, 5);
-        if (ci == 1) rg_bmark(c, 11);
-        if (t0 <= len && len < t0 + cnt) {
-          // the new token: appended to the cache (kvCache.append,
-          // internal/model/model.go:5593-5612) and patched into the chunk
-          if (threadIdx.x < 64) {
-            const int kind = threadIdx.x >> 5, i4 = threadIdx.x & 31;
-            const float4 v = ((const float4 *)(knew + kind * 128))[i4];
-            ((float4 *)rg_row(Kb, len - t0, kind))[i4] = v;
-            ((float4 *)kv_ptr(c, sp.seq[m].bt, layer, kind, g, len))[i4] = v;
-            // a later copy into this buffer must not overtake the store
-            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-          }
-          __syncthreads();
-        }
-        // ---- scores, heads in two groups of four: lane slot s of half grp
-        // holds dims s + 16 j of the group's q (j read as j ^ grp) and of the
-        // tokens 4 warp + 2 grp + {0, 1}; the reduce-scatter over the slots
-        // leaves value (token bit b3, head 2 b2 + b1) on the lane pair b0
-#pragma unroll
-        for (int hg = 0; hg < 2; hg++) {
-          float part[8];
-          f2x qr[2][8];  // heads (4 hg + 2 p, 4 hg + 2 p + 1)
-#pragma unroll
-          for (int p = 0; p < 2; p++)
-#pragma unroll
-            for (int jj = 0; jj < 8; jj++) {
-              const int h0 = 4 * hg + 2 * p, idx = 16 * (jj ^ grp) + slot;
-              qr[p][jj] = f2_pack(h0 < G ? qs[h0 * kHeadDim + idx] : 0.0f, h0 + 1 < G ? qs[(h0 + 1) * kHeadDim + idx] : 0.0f);
-            }
+        // ---- scores of the warp's tokens 4 warp .. 4 warp + 3: half grp
+        // takes tokens 4 warp + 2 grp + {0, 1}; the reduce-scatter over the
+        // 16 slots leaves (token lane >> 3, head lane & 7) on each lane
+        float v[16];
+        {
+          f2x kp[2][4];  // K of token (4 warp + 2 grp + tl) at dims (16 (j ^ grp) + slot, +64)
 #pragma unroll
           for (int tl = 0; tl < 2; tl++) {
-            const float *kr = rg_row(Kb, 4 * warp + 2 * grp + tl, 0);
-            f2x kk[8];
+            const int tok = 4 * warp + 2 * grp + tl;
+            const float *kr = t0 + tok == len ? knew : rg_row(Kb, tok, 0);
 #pragma unroll
-            for (int jj = 0; jj < 8; jj++) {
-              const float kv = kr[16 * (jj ^ grp) + slot];
-              kk[jj] = f2_pack(kv, kv);
-            }
-#pragma unroll
-            for (int p = 0; p < 2; p++) {
-              f2x pr[8];
-#pragma unroll
-              for (int jj = 0; jj < 8; jj++) pr[jj] = f2_mul(qr[p][jj], kk[jj]);
-              const f2x sum = f2_add(f2_add(f2_add(pr[0], pr[1]), f2_add(pr[2], pr[3])),
-                                     f2_add(f2_add(pr[4], pr[5]), f2_add(pr[6], pr[7])));
-              part[tl * 4 + 2 * p] = f2_lo(sum);
-              part[tl * 4 + 2 * p + 1] = f2_hi(sum);
+            for (int jj = 0; jj < 4; jj++) {
+              const int idx = 16 * (jj ^ grp) + slot;
+              kp[tl][jj] = f2_pack(kr[idx], kr[idx + 64]);
             }
           }
 #pragma unroll
-          for (int i = 0; i < 4; i++) {
-            const bool up = lane & 8;
-            const float send = up ? part[i] : part[4 + i];
-            part[i] = __fadd_rn(up ? part[4 + i] : part[i], __shfl_xor_sync(0xffffffffu, send, 8));
-          }
+          for (int h = 0; h < 8; h++) {
+            const ulonglong2 qa = qlane[(2 * h) * 16], qb = qlane[(2 * h + 1) * 16];
 #pragma unroll
-          for (int i = 0; i < 2; i++) {
-            const bool up = lane & 4;
-            const float send = up ? part[i] : part[2 + i];
-            part[i] = __fadd_rn(up ? part[2 + i] : part[i], __shfl_xor_sync(0xffffffffu, send, 4));
+            for (int tl = 0; tl < 2; tl++) {
+              // (p_j, p_j+4) pairs: ((p0+p1)+(p2+p3)) + ((p4+p5)+(p6+p7))
+              const f2x z = f2_add(f2_add(f2_mul(qa.x, kp[tl][0]), f2_mul(qa.y, kp[tl][1])),
+                                   f2_add(f2_mul(qb.x, kp[tl][2]), f2_mul(qb.y, kp[tl][3])));
+              v[tl * 8 + h] = h < G ? __fadd_rn(f2_lo(z), f2_hi(z)) : 0.0f;
+            }
           }
-          {
-            const bool up = lane & 2;
-            const float send = up ? part[0] : part[1];
-            part[0] = __fadd_rn(up ? part[1] : part[0], __shfl_xor_sync(0xffffffffu, send, 2));
-          }
-          const float r = __fadd_rn(part[0], __shfl_xor_sync(0xffffffffu, part[0], 1));
-          if (!(lane & 1))
-            S[(4 * hg + ((slot >> 1) & 3)) * 32 + 4 * warp + 2 * grp + (slot >> 3)] = __fmul_rn(r, c.attn_scale);
         }
-        __syncthreads();
-        if (ci == 0) rg_bmark(c, 6);
-        if (ci == 1) rg_bmark(c, 12);
-        if (threadIdx.x == 0) {
-          s_rg_par ^= 1u << b;
-          // every thread is past the previous chunk: its buffer takes the next copy
-          if (ci == 1) rg_bmark(c, 16);
-          rg_issue_upto(c, layer, smem, ci + kRangeBufs);
-          if (ci == 1) rg_bmark(c, 17);
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+          const bool up = lane & 8;
+          const float send = up ? v[i] : v[8 + i];
+          v[i] = __fadd_rn(up ? v[8 + i] : v[i], __shfl_xor_sync(0xffffffffu, send, 8));
         }
-        // ---- online softmax, warp h = head h
-        if (warp < G) {
-          const float s = S[warp * 32 + lane];
-          const bool valid = lane < cnt;
-          float pm = valid ? s : -INFINITY;
-          for (int o2 = 16; o2 > 0; o2 >>= 1) pm = fmaxf(pm, __shfl_xor_sync(0xffffffffu, pm, o2));
-          const float m_new = fmaxf(m_run, pm);
-          const float alpha = m_run == -INFINITY ? 0.0f : exp_fma(__fsub_rn(m_run, m_new));
-          const bool raw = t0 + lane >= nv;
-          float e = 0.0f;
-          if (valid) e = raw ? s : exp_fma(__fsub_rn(s, m_new));
-          float le = valid && !raw ? e : 0.0f;
-          for (int o2 = 16; o2 > 0; o2 >>= 1) le = __fadd_rn(le, __shfl_xor_sync(0xffffffffu, le, o2));
-          l_run = __fadd_rn(__fmul_rn(l_run, alpha), le);
-          m_run = m_new;
-          W[lane * 8 + warp] = e;
-          if (lane == 0) alph[warp] = alpha;
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+          const bool up = lane & 4;
+          const float send = up ? v[i] : v[4 + i];
+          v[i] = __fadd_rn(up ? v[4 + i] : v[i], __shfl_xor_sync(0xffffffffu, send, 4));
         }
-        if (ci == 1) rg_bmark(c, 18);
-        __syncthreads();
-        if (ci == 1) rg_bmark(c, 13);
-        // ---- values: thread (d, th), tokens th*16 .. th*16+15 of the chunk
+#pragma unroll
+        for (int i = 0; i < 2; i++) {
+          const bool up = lane & 2;
+          const float send = up ? v[i] : v[2 + i];
+          v[i] = __fadd_rn(up ? v[2 + i] : v[i], __shfl_xor_sync(0xffffffffu, send, 2));
+        }
+        float s;
         {
+          const bool up = lane & 1;
+          const float send = up ? v[0] : v[1];
+          s = __fmul_rn(__fadd_rn(up ? v[1] : v[0], __shfl_xor_sync(0xffffffffu, send, 1)), c.attn_scale);
+        }
+        if (ci == 0) rg_bmark(c, 6);
+        // ---- online softmax of the warp's tokens: head h on lanes h, h+8,
+        // h+16, h+24 (its four tokens)
+        const int tok = 4 * warp + (lane >> 3);
+        const bool valid = tok < cnt, raw = t0 + tok >= nv;
+        float pm = valid ? s : -INFINITY;
+        pm = fmaxf(pm, __shfl_xor_sync(0xffffffffu, pm, 8));
+        pm = fmaxf(pm, __shfl_xor_sync(0xffffffffu, pm, 16));
+        const float m_new = fmaxf(m_run, pm);
+        const float alpha = m_run == -INFINITY ? 0.0f : exp_fma(__fsub_rn(m_run, m_new));
+        float e = 0.0f;
+        if (valid) e = raw ? s : exp_fma(__fsub_rn(s, m_new));
+        float le = valid && !raw ? e : 0.0f;
+        le = __fadd_rn(le, __shfl_xor_sync(0xffffffffu, le, 8));
+        le = __fadd_rn(le, __shfl_xor_sync(0xffffffffu, le, 16));
+        l_run = __fadd_rn(__fmul_rn(l_run, alpha), le);
+        m_run = m_new;
+        {
+          const float w = valid && !raw ? e : 0.0f;
+          ((float2 *)(wp + kRgWpW))[lane] = make_float2(w, w);
+        }
+        if (lane < 8) ((float2 *)(wp + kRgWpA))[lane] = make_float2(alpha, alpha);
+        if (t0 + cnt > nv) wp[kRgWpRaw + lane] = valid && raw ? e : 0.0f;  // raw weights, for the tail sums
+        const bool rescale = !__all_sync(0xffffffffu, alpha == 1.0f);
+        __syncwarp();
+        // ---- values: lane dims 4 lane .. 4 lane + 3 of the G heads
+        if (rescale) {
 #pragma unroll
-          for (int p = 0; p < 4; p++)
-            o2[p] = f2_mul(o2[p], f2_pack(2 * p < G ? alph[2 * p] : 0.0f, 2 * p + 1 < G ? alph[2 * p + 1] : 0.0f));
-          const int tb = th * 16, te = min(cnt, tb + 16);
-          const int tt = min(max(nv - t0, tb), te);  // [tb, tt) exponentiated, [tt, te) raw
-          const float *Vb = rg_row(Kb, tb, 1) - (size_t)tb * kHeadDim;  // row t of this half at Vb + t * D
-#pragma unroll 4
-          for (int t = tb; t < tt; t++) {
-            const float v = Vb[(size_t)t * kHeadDim + d];
-            const f2x vv = f2_pack(v, v);
-            const ulonglong2 wa = ((const ulonglong2 *)(W + t * 8))[0], wb = ((const ulonglong2 *)(W + t * 8))[1];
-            o2[0] = f2_fma(wa.x, vv, o2[0]);
-            o2[1] = f2_fma(wa.y, vv, o2[1]);
-            o2[2] = f2_fma(wb.x, vv, o2[2]);
-            o2[3] = f2_fma(wb.y, vv, o2[3]);
-          }
-          if (t0 + cnt > nv) {
-            // the chunk holding the positions at or above nv (the last one of
-            // the pair): this half's raw-weighted sums, zero when it has none
-            float ta[8];
-#pragma unroll
-            for (int h = 0; h < 8; h++) ta[h] = 0.0f;
-#pragma unroll 1
-            for (int t = tt; t < te; t++) {
-              const float v = Vb[(size_t)t * kHeadDim + d];
-              const float4 w0 = ((const float4 *)(W + t * 8))[0], w1 = ((const float4 *)(W + t * 8))[1];
-              ta[0] = __fmaf_rn(w0.x, v, ta[0]);
-              ta[1] = __fmaf_rn(w0.y, v, ta[1]);
-              ta[2] = __fmaf_rn(w0.z, v, ta[2]);
-              ta[3] = __fmaf_rn(w0.w, v, ta[3]);
-              ta[4] = __fmaf_rn(w1.x, v, ta[4]);
-              ta[5] = __fmaf_rn(w1.y, v, ta[5]);
-              ta[6] = __fmaf_rn(w1.z, v, ta[6]);
-              ta[7] = __fmaf_rn(w1.w, v, ta[7]);
-            }
-#pragma unroll
-            for (int h = 0; h < 8; h++) Tsm[th * 1024 + h * kHeadDim + d] = ta[h];
+          for (int h2 = 0; h2 < 4; h2++) {
+            const ulonglong2 a = ((const ulonglong2 *)(wp + kRgWpA))[h2];
+            o2[2 * h2][0] = f2_mul(o2[2 * h2][0], a.x);
+            o2[2 * h2][1] = f2_mul(o2[2 * h2][1], a.x);
+            o2[2 * h2 + 1][0] = f2_mul(o2[2 * h2 + 1][0], a.y);
+            o2[2 * h2 + 1][1] = f2_mul(o2[2 * h2 + 1][1], a.y);
           }
         }
+        const int nvw = min(4, cnt - 4 * warp);
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+          if (i < nvw) {
+            const int tk = 4 * warp + i;
+            const float *vr = t0 + tk == len ? knew + kHeadDim : rg_row(Kb, tk, 1);
+            const ulonglong2 vq = ((const ulonglong2 *)vr)[lane];
+#pragma unroll
+            for (int h2 = 0; h2 < 4; h2++) {
+              const ulonglong2 w = ((const ulonglong2 *)(wp + kRgWpW + 16 * i))[h2];
+              o2[2 * h2][0] = f2_fma(w.x, vq.x, o2[2 * h2][0]);
+              o2[2 * h2][1] = f2_fma(w.x, vq.y, o2[2 * h2][1]);
+              o2[2 * h2 + 1][0] = f2_fma(w.y, vq.x, o2[2 * h2 + 1][0]);
+              o2[2 * h2 + 1][1] = f2_fma(w.y, vq.y, o2[2 * h2 + 1][1]);
+            }
+          }
+        }
+        if (t0 <= len && len < t0 + cnt && ((len - t0) >> 2) == warp) {
+          // the new token: appended to the cache (kvCache.append,
+          // internal/model/model.go:5593-5612)
+          ((float4 *)kv_ptr(c, sp.seq[m].bt, layer, 0, g, len))[lane] = ((const float4 *)knew)[lane];
+          ((float4 *)kv_ptr(c, sp.seq[m].bt, layer, 1, g, len))[lane] = ((const float4 *)(knew + kHeadDim))[lane];
+        }
+        __syncwarp();
+        // the warp is done with the chunk's rows (the segment's last chunk
+        // after the partials below)
+        if (j + 1 < nck && lane == 0) rg_release(c, layer, smem, cur, ci);
       }
-      // ---- segment end: the partial (halves added in order)
+      // ---- segment end: the warps' partials combined through the buffer of
+      // the segment's last chunk
       if (ridx == 0 && k == k0) {
         rg_mark(c, layer, 1);
         rg_bmark(c, 7);
       }
-      const bool has_tail = last_seg && (n & 15) != 0;
+      const int cl = ci - 1;
+      float *Kb = rg_buf(c, sp.M, smem, cl % kRangeBufs);
+      const int t0 = (sp0 + 2 * (nck - 1)) * kPageTokens;
+      const int cnt = min(min(2, seg_np - 2 * (nck - 1)) * kPageTokens, n - t0);
       const int seg = rg_seg_index(cur);
-      float o[8];
-#pragma unroll
-      for (int p = 0; p < 4; p++) {
-        o[2 * p] = f2_lo(o2[p]);
-        o[2 * p + 1] = f2_hi(o2[p]);
+      const size_t hq0 = (size_t)m * c.QH + (size_t)g * G;
+      __syncthreads();  // every warp is past the chunk's rows
+      if (t0 + cnt > nv) {
+        // the pair's last chunk holds the positions at or above nv: warp h
+        // sums head h's raw-weighted rows in position order
+        if (warp < G) {
+          float4 ta = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll 1
+          for (int t = max(nv - t0, 0); t < cnt; t++) {
+            const float w = sm[kRgWp + (t >> 2) * kRgWpLen + kRgWpRaw + (t & 3) * 8 + warp];
+            const float *vr = t0 + t == len ? knew + kHeadDim : rg_row(Kb, t, 1);
+            const float4 vv = ((const float4 *)vr)[lane];
+            ta.x = __fmaf_rn(w, vv.x, ta.x);
+            ta.y = __fmaf_rn(w, vv.y, ta.y);
+            ta.z = __fmaf_rn(w, vv.z, ta.z);
+            ta.w = __fmaf_rn(w, vv.w, ta.w);
+          }
+          ((float4 *)(c.part_t + (hq0 + warp) * kHeadDim))[lane] = ta;
+        }
+        __syncthreads();  // the rows are read before the partials overwrite them
       }
-      if (th == 1) {
+      {
+        ulonglong2 *cb = (ulonglong2 *)(Kb + (size_t)warp * kMaxGroup * kHeadDim);  // [warp][head][128]
 #pragma unroll
-        for (int h = 0; h < 8; h++)
-          if (h < G) red[h * kHeadDim + d] = o[h];
+        for (int h = 0; h < 8; h++) cb[h * (kHeadDim / 4) + lane] = make_ulonglong2(o2[h][0], o2[h][1]);
+        if (lane < 8) ((float2 *)mlw)[warp * 8 + lane] = make_float2(m_run, l_run);
+        // the buffer's next copy (async proxy) follows these stores
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       }
       __syncthreads();
-      if (th == 0) {
+      if (warp < G) {
+        // head h = warp: M = max over the warps, o and l summed over the
+        // warps in order, each scaled by exp(m_w - M)
+        const int h = warp;
+        const float2 ml = lane < 8 ? ((const float2 *)mlw)[lane * 8 + h] : make_float2(-INFINITY, 0.0f);
+        float mx = ml.x;
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
+        const float sc = lane < 8 && ml.x != -INFINITY ? exp_fma(__fsub_rn(ml.x, mx)) : 0.0f;
+        float l = __fmul_rn(sc, ml.y);
+        l = __fadd_rn(l, __shfl_xor_sync(0xffffffffu, l, 1));
+        l = __fadd_rn(l, __shfl_xor_sync(0xffffffffu, l, 2));
+        l = __fadd_rn(l, __shfl_xor_sync(0xffffffffu, l, 4));
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
-        for (int h = 0; h < 8; h++)
-          if (h < G) {
-            c.part_o[((size_t)seg * G + h) * kHeadDim + d] = __fadd_rn(o[h], red[h * kHeadDim + d]);
-            if (has_tail)
-              c.part_t[((size_t)m * c.QH + (size_t)g * G + h) * kHeadDim + d] =
-                  __fadd_rn(Tsm[h * kHeadDim + d], Tsm[1024 + h * kHeadDim + d]);
-          }
+        for (int w = 0; w < kRgWarps; w++) {
+          const float sw = __shfl_sync(0xffffffffu, sc, w);
+          const float4 ov = ((const float4 *)(Kb + (size_t)(w * kMaxGroup + h) * kHeadDim))[lane];
+          acc.x = __fmaf_rn(sw, ov.x, acc.x);
+          acc.y = __fmaf_rn(sw, ov.y, acc.y);
+          acc.z = __fmaf_rn(sw, ov.z, acc.z);
+          acc.w = __fmaf_rn(sw, ov.w, acc.w);
+        }
+        ((float4 *)(c.part_o + ((size_t)seg * G + h) * kHeadDim))[lane] = acc;
+        if (lane == 0) ((float2 *)c.part_ml)[(size_t)seg * G + h] = make_float2(mx, l);
       }
-      if (warp < G && lane == 0) {
-        c.part_ml[((size_t)seg * G + warp) * 2] = m_run;
-        c.part_ml[((size_t)seg * G + warp) * 2 + 1] = l_run;
-      }
-      // the merger reads the partials with bulk copies (async proxy)
-      asm volatile("fence.proxy.async.global;" ::: "memory");
+      __syncwarp();
+      if (lane == 0) rg_release(c, layer, smem, cur, cl);
     }
     // ---- run end: arrival of the run's segments (no reply awaited); the
-    // block holding the pair's last segment merges it after its range work
+    // block holding the pair's last segment merges it after its range work.
+    // The merger reads the partials with bulk copies (async proxy).
+    asm volatile("fence.proxy.async.global;" ::: "memory");
     __syncthreads();
     if (threadIdx.x == 0) {
       // release: the block's partials (ordered before by the barrier) become
@@ -708,11 +760,11 @@ __device__ __noinline__ void phase_attn_range(const Ctx *cp, int layer, float *s
       if (k1 == cur.nseg) {
         // merged after the phase (rg_merge_pending); a step has at most
         // kRgMerges (sequence, kv head) pairs (checked on the host)
-        int *ml = (int *)(sm + kRgMerge);
-        const int q = ml[0];
-        ml[4 + 2 * q] = m | g << 8 | cur.nseg << 16;
-        ml[4 + 2 * q + 1] = cur.sbase + g * cur.nseg;
-        ml[0] = q + 1;
+        int *mlist = (int *)(sm + kRgMerge);
+        const int q = mlist[0];
+        mlist[4 + 2 * q] = m | g << 8 | cur.nseg << 16;
+        mlist[4 + 2 * q + 1] = cur.sbase + g * cur.nseg;
+        mlist[0] = q + 1;
         if (c.trace) c.trace[4 * kTraceRows + kTraceMarks * blockIdx.x + 15] += 1000 + cur.nseg;
       }
     }
@@ -724,6 +776,9 @@ __device__ __noinline__ void phase_attn_range(const Ctx *cp, int layer, float *s
     ridx++;
   }
   if (threadIdx.x == 0) {
+    // chunk i completed a phase of buffer i % kRangeBufs
+    for (int b = 0; b < kRangeBufs; b++)
+      if (ci > b && (((ci - 1 - b) / kRangeBufs) & 1) == 0) s_rg_par ^= 1u << b;
     s_rg_issued = 0;
     s_rg_icur = s_rg_first;
   }
