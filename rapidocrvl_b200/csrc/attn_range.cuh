@@ -114,6 +114,13 @@ __shared__ RgCur s_rg_first;
 __shared__ int s_rg_hi, s_rg_p0, s_rg_npg;
 __shared__ int s_rg_pg[kRgPgCap];
 __shared__ int s_ex_n, s_ex_m[kMaxSeqs];
+// The block's chunks in stream order (pool page of each of their one or two
+// pages, -1 for none, and the kv head), when there are at most kRgChCap of
+// them (s_rg_nch their count, -1 otherwise): a buffer refill then reads its
+// chunk's copies from here instead of walking the cursor.
+constexpr int kRgChCap = 256;
+__shared__ int4 s_rg_ch[kRgChCap];
+__shared__ int s_rg_nch;
 
 // Moves to the first long cache at or after sequence m.
 __device__ __forceinline__ void rg_load_seq(const StepParams &sp, RgCur &r, int m) {
@@ -179,6 +186,14 @@ __device__ __forceinline__ void rg_block_init() {
     s_rg_mpar = 0;
     s_rg_issued = 0;
   }
+}
+
+// Pool page of the block's range page o (global page order), from the table
+// or the block table.
+__device__ __forceinline__ int rg_pool_page(const StepParams &sp, const RgCur &r, int o) {
+  const int i = o - s_rg_p0;
+  if (i >= 0 && i < s_rg_npg) return s_rg_pg[i];
+  return __ldg(sp.seq[r.m].bt + (o - r.pbase) % r.np);
 }
 
 // All threads, once per launch (after the step parameters are in shared
@@ -256,6 +271,18 @@ __device__ void rg_launch_init(const Ctx &c) {
     const int p = rem % s_rg_np[lo];
     s_rg_pg[i] = __ldg(sp.seq[lo].bt + p);
   }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    RgCur r = s_rg_first;
+    int i = 0;
+    for (; i < kRgChCap && rg_in(r, s_rg_hi); i++) {
+      const int o = rg_start(r) + 2 * r.j;
+      const bool two = rg_seg_np(r) - 2 * r.j >= 2;
+      s_rg_ch[i] = make_int4(rg_pool_page(sp, r, o), two ? rg_pool_page(sp, r, o + 1) : -1, r.g, 0);
+      rg_next_chunk(c, sp, r);
+    }
+    s_rg_nch = rg_in(r, s_rg_hi) ? -1 : i;
+  }
 }
 
 // Per-block time stamp i (thread 0; the last layer's values remain):
@@ -266,14 +293,6 @@ __device__ void rg_launch_init(const Ctx &c) {
 // 15 merges * 1000 + their segments.
 __device__ __forceinline__ void rg_bmark(const Ctx &c, int i) {
   if (c.trace && threadIdx.x == 0) c.trace[4 * kTraceRows + kTraceMarks * blockIdx.x + i] = gtimer();
-}
-
-// Pool page of the block's range page o (global page order), from the table
-// or the block table.
-__device__ __forceinline__ int rg_pool_page(const StepParams &sp, const RgCur &r, int o) {
-  const int i = o - s_rg_p0;
-  if (i >= 0 && i < s_rg_npg) return s_rg_pg[i];
-  return __ldg(sp.seq[r.m].bt + (o - r.pbase) % r.np);
 }
 
 // K rows then V rows of (layer, kv head g) in pool page `page`: 16 KB.
@@ -369,6 +388,19 @@ __device__ __forceinline__ void rg_release(const Ctx &c, int layer, float *smem,
                : "r"(smem_u32(&s_rg_rel[b])), "r"((unsigned)(kRgWarps - 1))
                : "memory");
   if (old != (unsigned)(kRgWarps - 1)) return;
+  const int nch = s_rg_nch;
+  if (nch >= 0) {
+    const int i = ci + kRangeBufs;
+    if (i >= nch) return;
+    constexpr uint32_t pb = 2u * kPageTokens * kHeadDim * 4;  // K and V rows of one page
+    const int4 d = s_rg_ch[i];
+    float *buf = rg_buf(c, c.sp->M, smem, b);
+    uint64_t *bar = &s_rg_full[b];
+    mbar_expect_tx(bar, (d.y >= 0 ? 2u : 1u) * pb);
+    bulk_g2s(buf, rg_page_kv(c, d.x, layer, d.z), pb, bar);
+    if (d.y >= 0) bulk_g2s(buf + 2 * kPageTokens * kHeadDim, rg_page_kv(c, d.y, layer, d.z), pb, bar);
+    return;
+  }
   const StepParams &sp = *c.sp;
 #pragma unroll 1
   for (int i = 0; i < kRangeBufs && r.m >= 0; i++) rg_next_chunk(c, sp, r);
