@@ -109,6 +109,19 @@ __device__ __forceinline__ void tmem_ld8(uint32_t addr, uint32_t (&v)[8]) {
                : "r"(addr));
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
+// 32 consecutive columns of this warp's TMEM lane quarter; the caller waits
+// with tmem_wait_ld before using the values.
+__device__ __forceinline__ void tmem_ld32_nowait(uint32_t addr, uint32_t (&v)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]), "=r"(v[8]),
+        "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15]), "=r"(v[16]),
+        "=r"(v[17]), "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]), "=r"(v[24]),
+        "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
+      : "r"(addr));
+}
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 // 2-D TMA tile copy (no multicast) of a box at (x bytes, y rows).
 __device__ __forceinline__ void tma_2d(void *dst, const TmapBytes *map, int x, int y, uint64_t *bar) {
   asm volatile(
@@ -267,6 +280,11 @@ __device__ __noinline__ void phase_gemm_b(const Ctx *cp, const BatchedW *bwp, co
     }
     if (mk && n0 == lo) rg_bmark(c, 17);
     const uint32_t idesc = umma_idesc_i8(NT);
+    // unpack tasks: CPR packed chunks per row, per = NT * CPR tasks per (tile, matrix)
+    constexpr int CPR = QT == QT_Q4 ? KP / 16 : KP / 48;
+    const int per = NT * CPR;
+    const int jm0 = threadIdx.x / per, rc0 = threadIdx.x - jm0 * per;
+    const int djm = kThreads / per, drc = kThreads - djm * per;
     for (int su = 0; su < nsu; su++) {
       const int TU = TU0 + su, slot = TU % S, grp = TU & 1;
       const int nt_here = min(U, nk - su * U);  // K tiles of this stage
@@ -280,13 +298,15 @@ __device__ __noinline__ void phase_gemm_b(const Ctx *cp, const BatchedW *bwp, co
       if (ms) rg_bmark(c, 20);
       // unpack the stage's K tiles to int8 in the core-matrix layout:
       // tile j of matrix mi into sg + (j * mats + mi) * sbytes
+      // task t = (tile j, matrix mi, row r, chunk) in that order; the
+      // thread's (jm = j * mats + mi, rc = row * CPR + chunk) advance by
+      // kThreads tasks a step without divisions
+      int jm = jm0, rc = rc0;
       if (QT == QT_Q4) {
         // 16 packed bytes -> 32 int8 = two 16-byte K chunks
-        const int per = NT * (KP / 16);
         for (int task = threadIdx.x; task < nt_here * mats * per; task += kThreads) {
-          const int jm = task / per, rc = task - jm * per;
-          const int j = jm / mats, mi = jm - j * mats;
-          const int r = rc / (KP / 16), c4 = rc % (KP / 16);
+          const int j = mats == 2 ? jm >> 1 : jm, mi = mats == 2 ? jm & 1 : 0;
+          const int r = rc / CPR, c4 = rc % CPR;
           const uint8_t *pk_src = sa + U * kGemmA + (size_t)mi * NT * rowb + (size_t)j * KP;
           uint8_t *dstB = sg + (size_t)(j * mats + mi) * sbytes;
           uint4 pk = make_uint4(0, 0, 0, 0);
@@ -303,14 +323,18 @@ __device__ __noinline__ void phase_gemm_b(const Ctx *cp, const BatchedW *bwp, co
           }
           *(uint4 *)(dstB + cm_off(r, 32 * c4)) = make_uint4(o[0], o[1], o[2], o[3]);
           *(uint4 *)(dstB + cm_off(r, 32 * c4 + 16)) = make_uint4(o[4], o[5], o[6], o[7]);
+          jm += djm;
+          rc += drc;
+          if (rc >= per) {
+            rc -= per;
+            jm++;
+          }
         }
       } else {
         // 48 packed bytes -> 64 int8 = four 16-byte K chunks
-        const int per = NT * (KP / 48);
         for (int task = threadIdx.x; task < nt_here * mats * per; task += kThreads) {
-          const int jm = task / per, rc = task - jm * per;
-          const int j = jm / mats, mi = jm - j * mats;
-          const int r = rc / (KP / 48), c3 = rc % (KP / 48);
+          const int j = mats == 2 ? jm >> 1 : jm, mi = mats == 2 ? jm & 1 : 0;
+          const int r = rc / CPR, c3 = rc % CPR;
           const uint8_t *pk_src = sa + U * kGemmA + (size_t)mi * NT * rowb + (size_t)j * KP;
           uint8_t *dstB = sg + (size_t)(j * mats + mi) * sbytes;
           uint32_t wd[12];
@@ -332,6 +356,12 @@ __device__ __noinline__ void phase_gemm_b(const Ctx *cp, const BatchedW *bwp, co
 #pragma unroll
             for (int i = 0; i < 4; i++) f[i] = r < nrows ? __vsub4(f[i], 0x20202020u) : 0u;
             *(uint4 *)(dstB + cm_off(r, 64 * c3 + 16 * g)) = make_uint4(f[0], f[1], f[2], f[3]);
+          }
+          jm += djm;
+          rc += drc;
+          if (rc >= per) {
+            rc -= per;
+            jm++;
           }
         }
       }
@@ -398,31 +428,39 @@ __device__ __noinline__ void phase_gemm_b(const Ctx *cp, const BatchedW *bwp, co
         }
       }
       const int ncol = (NT + 15) / 16 * 8;  // columns per half, multiple of 8
-      const int c_begin = half * ncol, c_end = min(NT, c_begin + ncol);
-      for (int c0 = c_begin; c0 < c_end; c0 += 8) {
-        uint32_t dv[8], uv[8];
-        tmem_ld8(tmem + ((uint32_t)(32 * quarter) << 16) + (uint32_t)c0, dv);
-        if (two) tmem_ld8(tmem + ((uint32_t)(32 * quarter) << 16) + (uint32_t)(NT + c0), uv);
+      const int c_begin = half * ncol, c_end = min(min(NT, c_begin + ncol), nrows);
+      const int epi = a.epi;
+      const size_t ldo = (size_t)a.ldo;
+      float *const outp = a.out, *const residp = a.resid, *const voutp = a.vout, *const logitsp = a.logits;
+      const uint32_t tq = tmem + ((uint32_t)(32 * quarter) << 16);
+      // 32 columns per load (columns < 2 NT + 32 <= kTmemCols: NT <= 256,
+      // multiple of 16, and c_begin a multiple of 8 below NT / 2 + 8)
+      for (int c0 = c_begin; c0 < c_end; c0 += 32) {
+        uint32_t dv[32], uv[32];
+        tmem_ld32_nowait(tq + (uint32_t)c0, dv);
+        if (two) tmem_ld32_nowait(tq + (uint32_t)(NT + c0), uv);
+        tmem_wait_ld();
         if (!live) continue;
+        const int nj = min(32, c_end - c0);
+        const size_t ob = (size_t)m * ldo + n0 + c0;
 #pragma unroll
-        for (int j = 0; j < 8; j++) {
+        for (int j = 0; j < 32; j++) {
+          if (j >= nj) break;
           const int cj = c0 + j;
-          if (cj >= nrows) break;
-          const int row = n0 + cj;
           const float v = vnni_finalize((int32_t)dv[j], s_rs[cj], sx, s_scl[cj]);
-          const size_t o = (size_t)m * a.ldo + row;
-          if (a.epi == EPI_STORE) {
-            a.out[o] = v;
-          } else if (a.epi == EPI_RESID) {
-            const float tt = __fadd_rn(__ldcg(a.resid + o), v);
-            a.vout[o] = tt;
-            if (in_place) a.resid[o] = tt;
-          } else if (a.epi == EPI_SWIGLU) {
+          const size_t o = ob + j;
+          if (epi == EPI_STORE) {
+            outp[o] = v;
+          } else if (epi == EPI_RESID) {
+            const float tt = __fadd_rn(__ldcg(residp + o), v);
+            voutp[o] = tt;
+            if (in_place) residp[o] = tt;
+          } else if (epi == EPI_SWIGLU) {
             const float u = vnni_finalize((int32_t)uv[j], s_rs[kMaxNT + cj], sx, s_scl[kMaxNT + cj]);
-            a.out[o] = silu_mul(v, u);
+            outp[o] = silu_mul(v, u);
           } else {
-            if (a.logits) a.logits[o] = v;
-            const unsigned long long k = argmax_key(v, row);
+            if (logitsp) logitsp[o] = v;
+            const unsigned long long k = argmax_key(v, n0 + cj);
             best = k > best ? k : best;
           }
         }

@@ -55,7 +55,7 @@ struct StepParams {
   int M;                   // sequences in this step
   int any_logits;          // some sequence needs lm_head this step
   int max_n;               // max over sequences of len+1
-  int pad;
+  int store_logits;        // write the full logits (the caller reads them), else argmax only
   SeqParams seq[kMaxSeqs];
 };
 __host__ __device__ __forceinline__ size_t step_params_bytes(int n) { return 16 + (size_t)n * sizeof(SeqParams); }

@@ -183,7 +183,7 @@ __device__ void build_args(const Ctx &c, int phase, int layer, int any_logits, i
         sa.epi = EPI_ARGMAX;
         sa.ldo = c.V;
         sa.argkey = c.argkey;
-        sa.logits = c.logits;
+        sa.logits = c.sp->store_logits ? c.logits : nullptr;
         sa.argmax_finish = 1;
         sa.feed = feed;
         break;
@@ -507,7 +507,7 @@ __device__ void step_b_body(const Ctx &c, const BatchedW *bw, uint32_t tmem, int
   g.epi = EPI_ARGMAX;
   g.ldo = c.V;
   g.argkey = c.argkey;
-  g.logits = c.logits;
+  g.logits = c.sp->store_logits ? c.logits : nullptr;
   g.argmax_finish = 1;
   g.feed = feed;
   gemm(g);
@@ -1245,7 +1245,7 @@ int step_group(ocrvl_model *m, ocrvl_seq *const *seqs, int n, const int32_t *ids
   StepParams &sp = *m->sp_h;
   sp.M = n;
   sp.any_logits = need_logits ? 1 : 0;
-  sp.pad = 0;
+  sp.store_logits = need_logits && out_logits ? 1 : 0;
   int max_n = 0;
   for (int i = 0; i < n; i++) {
     ocrvl_seq *s = seqs[i];
@@ -1356,7 +1356,7 @@ int decode_group(ocrvl_model *m, ocrvl_seq *const *seqs, int n, const int32_t *f
   const ocrvl_model_desc &d = m->desc;
   StepParams &sp = *m->sp_h;
   sp.M = n;
-  sp.pad = 0;
+  sp.store_logits = 0;
   sp.any_logits = 1;
   int max_n = 0;
   for (int i = 0; i < n; i++) {
