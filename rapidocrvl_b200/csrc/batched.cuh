@@ -259,6 +259,8 @@ __device__ __noinline__ void phase_gemm_b(const Ctx *cp, const BatchedW *bwp, co
     for (int i = threadIdx.x; i < nrows; i += kThreads) {
       s_scl[i] = __ldg(a.A.scale + n0 + i);
       s_rs[i] = __ldg(a.A.rowsum + n0 + i);
+      // argmax: 128 * rowsum of vnni_finalize, once per column (the B half is unused)
+      if (a.epi == EPI_ARGMAX) s_scl[kMaxNT + i] = __fmul_rn(128.0f, (float)s_rs[i]);
       if (two) {
         s_scl[kMaxNT + i] = __ldg(a.B.scale + n0 + i);
         s_rs[kMaxNT + i] = __ldg(a.B.rowsum + n0 + i);
@@ -418,6 +420,11 @@ __device__ __noinline__ void phase_gemm_b(const Ctx *cp, const BatchedW *bwp, co
       const int m = 16 * quarter + lane;
       const bool live = lane < 16 && m < M;
       const float sx = live ? __ldcg(bw.act_sx + m) : 0.0f;
+      // argmax only: lanes l and l + 16 share sequence 16 quarter + (l & 15),
+      // lane l + 16 taking the upper 16 of every 32 columns
+      const int ma = 16 * quarter + (lane & 15);
+      const bool alive = ma < M;
+      const float sxa = alive ? __ldcg(bw.act_sx + ma) : 0.0f;
       bool in_place = false;
       if (a.epi == EPI_RESID && live) {
         if (a.resid_mode == RESID_ALWAYS) {
@@ -440,8 +447,24 @@ __device__ __noinline__ void phase_gemm_b(const Ctx *cp, const BatchedW *bwp, co
         tmem_ld32_nowait(tq + (uint32_t)c0, dv);
         if (two) tmem_ld32_nowait(tq + (uint32_t)(NT + c0), uv);
         tmem_wait_ld();
-        if (!live) continue;
         const int nj = min(32, c_end - c0);
+        if (epi == EPI_ARGMAX && !logitsp) {
+          // vnni_finalize with the column's 128 * rowsum precomputed
+          const int hi16 = lane >> 4;
+#pragma unroll
+          for (int j = 0; j < 16; j++) {
+            const uint32_t up = __shfl_sync(0xffffffffu, dv[16 + j], lane & 15);
+            const int jj = j + 16 * hi16;
+            if (alive && jj < nj) {
+              const int cj = c0 + jj;
+              const float d = __fsub_rn((float)(int32_t)(hi16 ? up : dv[j]), s_scl[kMaxNT + cj]);
+              const unsigned long long k = argmax_key(__fmul_rn(__fmul_rn(d, sxa), s_scl[cj]), n0 + cj);
+              best = k > best ? k : best;
+            }
+          }
+          continue;
+        }
+        if (!live) continue;
         const size_t ob = (size_t)m * ldo + n0 + c0;
 #pragma unroll
         for (int j = 0; j < 32; j++) {
@@ -472,6 +495,11 @@ __device__ __noinline__ void phase_gemm_b(const Ctx *cp, const BatchedW *bwp, co
   }
   if (a.epi == EPI_ARGMAX) {
     const int m = 16 * (warp & 3) + lane;
+    {
+      // lanes l and l + 16 hold the same sequence's keys
+      const unsigned long long o = __shfl_xor_sync(0xffffffffu, best, 16);
+      best = o > best ? o : best;
+    }
     if (lane < 16 && m < M && best) atomicMax(a.argkey + m, best);
     if (a.argmax_finish) {
       __shared__ int is_last;
