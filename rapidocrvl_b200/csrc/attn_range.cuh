@@ -3,8 +3,9 @@
 // mbarrier and stage-ring helpers.
 //
 // Segments.  The np pages of a (sequence m, kv head g) pair split into
-// segments of S = 2 * ceil(np / (2 kSegMax)) pages, so a pair has at most
-// kSegMax segments and a segment is a whole number of 32-token chunks.  The split depends on the
+// segments of S = 2 ceil(np / 64) pages for np <= 64, S = 2 ceil(np / 32)
+// pages above (rg_seg_pages), so a pair has at most kSegMax segments and a
+// segment is a whole number of 32-token chunks.  The split depends on the
 // cache length only: a sequence's result does not depend on the other
 // sequences of the step (a batched step equals the single steps bit for bit).
 //
@@ -89,7 +90,14 @@ __device__ __forceinline__ float *rg_small(const Ctx &c, int M, float *smem) {
   return (float *)((uint8_t *)smem + (size_t)kRangeBufs * kStageBytes);
 }
 
-__host__ __device__ __forceinline__ int rg_seg_pages(int np) { return 2 * ((np + 2 * kSegMax - 1) / (2 * kSegMax)); }
+// Pages per segment: up to 2 kSegMax pages, 2-page segments (at most kSegMax
+// of them, for the parallelism of short steps); longer caches, whose pairs
+// carry more chunks each, half as many segments (each segment's end costs a
+// combine of the warps' partials and a partial for the merge).
+__host__ __device__ __forceinline__ int rg_seg_pages(int np) {
+  const int t = np <= 2 * kSegMax ? kSegMax : kSegMax / 2;  // target segments
+  return 2 * ((np + 2 * t - 1) / (2 * t));
+}
 
 // Position in the step's stream of segments and chunks.
 struct RgCur {

@@ -122,7 +122,7 @@ __device__ __forceinline__ void tmem_ld32_nowait(uint32_t addr, uint32_t (&v)[32
       : "r"(addr));
 }
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
-// 2-D TMA tile copy (no multicast) of a box at (x bytes, y rows).
+// 2-D TMA tile copy into this CTA only, of a box at (x bytes, y rows).
 __device__ __forceinline__ void tma_2d(void *dst, const TmapBytes *map, int x, int y, uint64_t *bar) {
   asm volatile(
       "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(

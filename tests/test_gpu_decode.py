@@ -308,3 +308,51 @@ def test_import_kv_restores_a_cache(tiny_models):
     with pytest.raises(_lib.OcrvlError):
         b.import_kv(too_long, too_long)
     assert len(b) == 41  # rejected before any change
+
+
+def test_caches_over_1024_positions(tiny_models):
+    """Caches of more than 64 pages (1,024 positions), which the long-cache
+    attention splits into half as many, longer segments: one sequence
+    prefilled to 1,100 positions token by token matches the oracle's logits
+    and argmax at its next step; 12 sequences of 900-2,100 cached positions
+    (seeded K/V imported) stepped together in one batched step get the ids
+    and logits of stepping each alone, bit for bit."""
+    _need_gpu()
+    import pyoracle
+
+    q = "q4"
+    cfg = config.load(tiny_models[q])
+    rt = Runtime.load(tiny_models[q], LoadOptions(quantization=q, max_position=4096, kv_pool_bytes=1 << 30))
+    orc = pyoracle.OracleModel(os.path.join(tiny_models[q], f"model-{q}.gguf"), cfg)
+    n0 = 1100
+    prompt = synth.random_prompt(n0 + 1, cfg.vocab_size, 31)
+    seq = rt.new_sequence(n0 + 8)
+    oseq = orc.new_seq(n0 + 8)
+    for p, t in enumerate(prompt[:-1]):
+        rt.step([seq], ids=[t], need_logits=False)
+        oseq.forward(orc.embed(t), p, need_logits=False)
+    ids, logits = rt.step([seq], ids=[prompt[-1]], return_logits=True)
+    otok, ologits, _ = oseq.forward(orc.embed(prompt[-1]), n0, need_logits=True, want_logits=True)
+    err = np.abs(logits[0] - ologits)
+    assert np.all(err <= LOGIT_ATOL + LOGIT_RTOL * np.abs(ologits)), f"max err {err.max()}"
+    assert int(ids[0]) == otok
+
+    rng = np.random.default_rng(5)
+    n = 12
+    lens = [900 + 109 * j for j in range(n)]
+    kvd = cfg.num_key_value_heads * cfg.head_dim
+    L = cfg.num_hidden_layers
+    seq_a = [rt.new_sequence(x + 8) for x in lens]
+    seq_b = [rt.new_sequence(x + 8) for x in lens]
+    for j, x in enumerate(lens):
+        k = (0.5 * rng.standard_normal((L, x, kvd))).astype(np.float32)
+        v = rng.standard_normal((L, x, kvd)).astype(np.float32)
+        seq_a[j].import_kv(k, v)
+        seq_b[j].import_kv(k, v)
+    toks = [int(t) for t in rng.integers(0, cfg.vocab_size, n)]
+    for step in range(2):
+        ids_joint, logits_joint = rt.step(seq_a, ids=toks, return_logits=True)
+        for j in range(n):
+            ids1, logits1 = rt.step([seq_b[j]], ids=[toks[j]], return_logits=True)
+            assert int(ids1[0]) == int(ids_joint[j]) and np.array_equal(logits1[0], logits_joint[j]), (step, j)
+        toks = [int(i) for i in ids_joint]
