@@ -52,8 +52,20 @@ struct BatchedW {
   const TmapBytes *tm;  // [L * 5 + 1]: per layer qkv, o, gate, up, down; then lm_head
   uint8_t *act;         // activation image [K tiles][64 rows][kKT]
   float *act_sx;        // [kMaxSeqs] activation scale per sequence
+  int32_t *part;        // split-K partial dots of the down projection [ks][64][H]
   int smem_avail;       // dynamic shared memory of the step kernel (bytes, after alignment)
 };
+
+// Split-K of the down projection (K = intermediate size, the longest K of a
+// layer): ks groups of CTAs each take 1/ks of the K tiles of a slab of rows
+// over gridDim.x / ks slabs, so a CTA issues ks times fewer MMAs of a wider N
+// tile; the int32 partial dots add exactly and a finalize phase applies the
+// epilogue.  At most kDownSplits groups, at least one K tile each.
+constexpr int kDownSplits = 6;
+__host__ __device__ __forceinline__ int down_splits(int K) {
+  const int nk = K / kKT;
+  return nk < kDownSplits ? (nk > 0 ? nk : 1) : kDownSplits;
+}
 
 __device__ __forceinline__ const TmapBytes *bw_map(const BatchedW &bw, int layer, int which) {
   return bw.tm + (size_t)layer * 5 + which;
@@ -180,6 +192,8 @@ struct GemmArgs {
   unsigned long long *argkey;
   float *logits;
   int argmax_finish, feed;
+  int ks;                        // > 1: split-K groups (raw int32 dots to `part`, no epilogue)
+  int32_t *part;                 // [ks][64][ldo]
 };
 
 // K tiles per copy: N tiles of up to 64 rows move u K tiles per copy (one
@@ -223,7 +237,11 @@ __device__ __noinline__ void phase_gemm_b(const Ctx *cp, const BatchedW *bwp, co
   uint8_t *stg = sB0 + 2 * (size_t)gbytes;               // stages
   const int rowb = U * KP;                               // packed bytes per row per stage
   const int stage_bytes = (U * kGemmA + mats * NT * rowb + 1023) / 1024 * 1024;
-  const int nk = a.K / kKT, nsu = (nk + U - 1) / U;
+  // split-K: CTA b takes K tiles [kt0, kt0 + nk) of slab b / ks (of
+  // gridDim.x / ks slabs); otherwise every K tile of slab b
+  const int ks = a.ks > 1 ? a.ks : 1, kg = blockIdx.x % ks, nslab = gridDim.x / ks;
+  const int kt0 = kg * (a.K / kKT) / ks;
+  const int nk = (kg + 1) * (a.K / kKT) / ks - kt0, nsu = (nk + U - 1) / U;
   int S = (bw.smem_avail - (int)(stg - base)) / stage_bytes;
   S = min(min(S, kGemmStages), max(nsu, 2));
   __shared__ __align__(8) uint64_t bar_ld[kGemmStages], bar_su[kGemmStages], bar_grp[2];
@@ -232,7 +250,8 @@ __device__ __noinline__ void phase_gemm_b(const Ctx *cp, const BatchedW *bwp, co
     return;
   }
   int lo, hi;
-  gemv_slab(a.row_begin, a.row_end, blockIdx.x, gridDim.x, lo, hi);
+  if ((int)blockIdx.x / ks < nslab) gemv_slab(a.row_begin, a.row_end, blockIdx.x / ks, nslab, lo, hi);
+  else lo = hi = a.row_end;
   if (threadIdx.x == 0) {
     for (int i = 0; i < kGemmStages; i++) {
       mbar_init(&bar_ld[i], 1);
@@ -272,9 +291,9 @@ __device__ __noinline__ void phase_gemm_b(const Ctx *cp, const BatchedW *bwp, co
       const uint32_t bytes_a = (uint32_t)min(U, nk - su * U) * kGemmA;
       const uint32_t bytes_b = (uint32_t)NT * rowb;  // the whole box (past the matrix: zero-filled)
       mbar_expect_tx(&bar_ld[slot], bytes_a + mats * bytes_b);
-      bulk_g2s(sa, bw.act + (size_t)su * U * kGemmA, bytes_a, &bar_ld[slot]);
-      tma_2d(sa + U * kGemmA, a.mapA, su * rowb, n0, &bar_ld[slot]);
-      if (two) tma_2d(sa + U * kGemmA + bytes_b, a.mapB, su * rowb, n0, &bar_ld[slot]);
+      bulk_g2s(sa, bw.act + (size_t)(kt0 + su * U) * kGemmA, bytes_a, &bar_ld[slot]);
+      tma_2d(sa + U * kGemmA, a.mapA, kt0 * KP + su * rowb, n0, &bar_ld[slot]);
+      if (two) tma_2d(sa + U * kGemmA + bytes_b, a.mapB, kt0 * KP + su * rowb, n0, &bar_ld[slot]);
     };
     if (threadIdx.x == 0) {
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -448,6 +467,15 @@ __device__ __noinline__ void phase_gemm_b(const Ctx *cp, const BatchedW *bwp, co
         if (two) tmem_ld32_nowait(tq + (uint32_t)(NT + c0), uv);
         tmem_wait_ld();
         const int nj = min(32, c_end - c0);
+        if (a.part) {
+          // split-K: the raw dots of this K range
+          if (!live) continue;
+          int32_t *pp = a.part + ((size_t)kg * kMmaM + m) * ldo + n0 + c0;
+#pragma unroll
+          for (int j = 0; j < 32; j++)
+            if (j < nj) pp[j] = (int32_t)dv[j];
+          continue;
+        }
         if (epi == EPI_ARGMAX && !logitsp) {
           // vnni_finalize with the column's 128 * rowsum precomputed
           const int hi16 = lane >> 4;
@@ -515,6 +543,32 @@ __device__ __noinline__ void phase_gemm_b(const Ctx *cp, const BatchedW *bwp, co
   }
   __syncthreads();
   if (mk) rg_bmark(c, 23);
+}
+
+// Split-K finalize of a residual GEMM (the down projection): for every
+// (sequence, row), the ks partial dots summed (exact int32), the same
+// finalize and residual epilogue as EPI_RESID.
+__device__ __noinline__ void phase_splitk_resid(const Ctx *cp, const BatchedW *bwp, const DMat *Ap, int ks, int rows,
+                                                float *resid, float *vout, int resid_mode) {
+  const Ctx &c = *cp;
+  const BatchedW &bw = *bwp;
+  const DMat &A = *Ap;
+  const int M = c.sp->M;
+  for (int i = blockIdx.x * kThreads + threadIdx.x; i < M * rows; i += gridDim.x * kThreads) {
+    const int m = i / rows, row = i - m * rows;
+    int32_t d = 0;
+    for (int g = 0; g < ks; g++) d += __ldcg(bw.part + ((size_t)g * kMmaM + m) * rows + row);
+    const float v = vnni_finalize(d, __ldg(A.rowsum + row), __ldcg(bw.act_sx + m), __ldg(A.scale + row));
+    bool in_place = resid_mode == RESID_ALWAYS;
+    if (resid_mode == RESID_ATTN) {
+      const int len = c.sp->seq[m].len;
+      in_place = len >= 1 && len + 1 <= 6;  // model.go:4043-4062
+    }
+    const size_t o = (size_t)m * rows + row;
+    const float tt = __fadd_rn(__ldcg(resid + o), v);
+    vout[o] = tt;
+    if (in_place) resid[o] = tt;
+  }
 }
 
 }  // namespace ocrvl

@@ -389,7 +389,9 @@ __host__ __device__ __forceinline__ int gemm_nt(int rows, int grid) {
   return nt < 256 ? nt : 256;  // kMaxNT
 }
 __host__ __device__ __forceinline__ unsigned barriers_per_step_b(int L, int any_logits) {
-  return any_logits ? (unsigned)(9 * L + 1) : (unsigned)(9 * (L - 1) + 2);
+  // per layer: 4 quantisation phases, 4 GEMMs, attention, the down
+  // projection's split-K finalize; then the final norm (and lm_head)
+  return any_logits ? (unsigned)(10 * L + 1) : (unsigned)(10 * (L - 1) + 2);
 }
 
 template <int QT>
@@ -484,15 +486,16 @@ __device__ void step_b_body(const Ctx &c, const BatchedW *bw, uint32_t tmem, int
       g.A = L.down;
       g.row_end = L.down.rows;
       g.K = c.I;
-      g.nt = gemm_nt(L.down.rows, gridDim.x);
+      g.ks = down_splits(L.down.cols);
+      g.nt = gemm_nt(L.down.rows, gridDim.x / g.ks);
       g.u = gemm_u(QT, g.nt);
       g.epi = EPI_RESID;
       g.ldo = c.H;
-      g.resid = c.h;
-      g.vout = c.vbuf;
-      g.resid_mode = last ? RESID_NEVER : RESID_ALWAYS;
+      g.part = bw->part;
       gemm(g);
     }
+    if (!sync()) return;
+    phase_splitk_resid(&c, bw, &L.down, down_splits(L.down.cols), c.H, c.h, c.vbuf, last ? RESID_NEVER : RESID_ALWAYS);
     if (!sync()) return;
   }
   phase_quant_b(&c, bw, c.vbuf, c.H, 0, c.H, PRO_ADDNORM, c.final_norm, nullptr, smem);
@@ -734,15 +737,19 @@ void setup_batched(ocrvl_model *m) {
   for (int l = 0; l < L; l++) {
     const LayerW &w = m->layers[l];
     const DMat *mats[5] = {&w.qkv, &w.o, &w.gate, &w.up, &w.down};
+    // the down projection's map: N tiles of its split-K slabs
     for (int i = 0; i < 5; i++)
-      if (!make_weight_map(enc, *mats[i], QT, m->grid, &maps[(size_t)l * 5 + i])) return;
+      if (!make_weight_map(enc, *mats[i], QT, i == 4 ? m->grid / down_splits(w.down.cols) : m->grid,
+                           &maps[(size_t)l * 5 + i]))
+        return;
   }
   if (!make_weight_map(enc, m->lm_head, QT, m->grid, &maps[(size_t)L * 5])) return;
   TmapBytes *dmaps = m->dalloc<TmapBytes>(maps.size());
   const int kcols = (m->ctx.pro_cols + kKT - 1) / kKT * kKT;
   uint8_t *act = m->dalloc<uint8_t>((size_t)kMmaM * kcols);
   float *act_sx = m->dalloc<float>(kMaxSeqs);
-  if (!dmaps || !act || !act_sx) return;
+  int32_t *part = m->dalloc<int32_t>((size_t)down_splits(m->desc.intermediate_size) * kMmaM * m->desc.hidden_size);
+  if (!dmaps || !act || !act_sx || !part) return;
   if (cudaMemcpy(dmaps, maps.data(), maps.size() * sizeof(TmapBytes), cudaMemcpyHostToDevice) != cudaSuccess ||
       cudaMemset(act, 0, (size_t)kMmaM * kcols) != cudaSuccess ||
       cudaFuncSetAttribute(k_step_b<QT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)m->smem) != cudaSuccess) {
@@ -758,6 +765,7 @@ void setup_batched(ocrvl_model *m) {
   m->bw.tm = dmaps;
   m->bw.act = act;
   m->bw.act_sx = act_sx;
+  m->bw.part = part;
   m->bw.smem_avail = (int)(m->smem - kSmemAlignSlack);
   m->batched = true;
 }
