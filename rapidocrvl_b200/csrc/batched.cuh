@@ -52,12 +52,13 @@ struct BatchedW {
   const TmapBytes *tm;  // [L * 5 + 1]: per layer qkv, o, gate, up, down; then lm_head
   uint8_t *act;         // activation image [K tiles][64 rows][kKT]
   float *act_sx;        // [kMaxSeqs] activation scale per sequence
-  int32_t *part;        // split-K partial dots of the down projection [ks][64][H]
+  int32_t *part;        // split-K partial dots of the o / down projection [ks][64][H]
   int smem_avail;       // dynamic shared memory of the step kernel (bytes, after alignment)
 };
 
-// Split-K of the down projection (K = intermediate size, the longest K of a
-// layer): ks groups of CTAs each take 1/ks of the K tiles of a slab of rows
+// Split-K of the residual projections (o and down, whose few output rows per
+// CTA would otherwise make K/32 MMAs of N = 16 per CTA): ks groups of CTAs
+// each take 1/ks of the K tiles of a slab of rows
 // over gridDim.x / ks slabs, so a CTA issues ks times fewer MMAs of a wider N
 // tile; the int32 partial dots add exactly and a finalize phase applies the
 // epilogue.  At most kDownSplits groups, at least one K tile each.
@@ -545,7 +546,7 @@ __device__ __noinline__ void phase_gemm_b(const Ctx *cp, const BatchedW *bwp, co
   if (mk) rg_bmark(c, 23);
 }
 
-// Split-K finalize of a residual GEMM (the down projection): for every
+// Split-K finalize of a residual GEMM (o or down projection): for every
 // (sequence, row), the ks partial dots summed (exact int32), the same
 // finalize and residual epilogue as EPI_RESID.
 __device__ __noinline__ void phase_splitk_resid(const Ctx *cp, const BatchedW *bwp, const DMat *Ap, int ks, int rows,

@@ -389,9 +389,9 @@ __host__ __device__ __forceinline__ int gemm_nt(int rows, int grid) {
   return nt < 256 ? nt : 256;  // kMaxNT
 }
 __host__ __device__ __forceinline__ unsigned barriers_per_step_b(int L, int any_logits) {
-  // per layer: 4 quantisation phases, 4 GEMMs, attention, the down
-  // projection's split-K finalize; then the final norm (and lm_head)
-  return any_logits ? (unsigned)(10 * L + 1) : (unsigned)(10 * (L - 1) + 2);
+  // per layer: 4 quantisation phases, 4 GEMMs, attention, the o and down
+  // projections' split-K finalize; then the final norm (and lm_head)
+  return any_logits ? (unsigned)(11 * L + 1) : (unsigned)(11 * (L - 1) + 2);
 }
 
 template <int QT>
@@ -450,15 +450,16 @@ __device__ void step_b_body(const Ctx &c, const BatchedW *bw, uint32_t tmem, int
       g.A = L.o;
       g.row_end = L.o.rows;
       g.K = c.QH * c.D;
-      g.nt = gemm_nt(L.o.rows, gridDim.x);
+      g.ks = down_splits(L.o.cols);
+      g.nt = gemm_nt(L.o.rows, gridDim.x / g.ks);
       g.u = gemm_u(QT, g.nt);
       g.epi = EPI_RESID;
       g.ldo = c.H;
-      g.resid = c.h;
-      g.vout = c.vbuf;
-      g.resid_mode = RESID_ATTN;
+      g.part = bw->part;
       gemm(g);
     }
+    if (!sync()) return;
+    phase_splitk_resid(&c, bw, &L.o, down_splits(L.o.cols), c.H, c.h, c.vbuf, RESID_ATTN);
     if (!sync()) return;
     phase_quant_b(&c, bw, c.vbuf, c.H, 0, c.H, PRO_ADDNORM, L.ln2, nullptr, smem);
     if (!sync()) return;
@@ -737,9 +738,9 @@ void setup_batched(ocrvl_model *m) {
   for (int l = 0; l < L; l++) {
     const LayerW &w = m->layers[l];
     const DMat *mats[5] = {&w.qkv, &w.o, &w.gate, &w.up, &w.down};
-    // the down projection's map: N tiles of its split-K slabs
+    // the o and down projections' maps: N tiles of their split-K slabs
     for (int i = 0; i < 5; i++)
-      if (!make_weight_map(enc, *mats[i], QT, i == 4 ? m->grid / down_splits(w.down.cols) : m->grid,
+      if (!make_weight_map(enc, *mats[i], QT, i == 1 || i == 4 ? m->grid / down_splits(mats[i]->cols) : m->grid,
                            &maps[(size_t)l * 5 + i]))
         return;
   }
@@ -748,7 +749,7 @@ void setup_batched(ocrvl_model *m) {
   const int kcols = (m->ctx.pro_cols + kKT - 1) / kKT * kKT;
   uint8_t *act = m->dalloc<uint8_t>((size_t)kMmaM * kcols);
   float *act_sx = m->dalloc<float>(kMaxSeqs);
-  int32_t *part = m->dalloc<int32_t>((size_t)down_splits(m->desc.intermediate_size) * kMmaM * m->desc.hidden_size);
+  int32_t *part = m->dalloc<int32_t>((size_t)kDownSplits * kMmaM * m->desc.hidden_size);
   if (!dmaps || !act || !act_sx || !part) return;
   if (cudaMemcpy(dmaps, maps.data(), maps.size() * sizeof(TmapBytes), cudaMemcpyHostToDevice) != cudaSuccess ||
       cudaMemset(act, 0, (size_t)kMmaM * kcols) != cudaSuccess ||
