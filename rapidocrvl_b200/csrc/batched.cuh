@@ -557,8 +557,10 @@ __device__ __noinline__ void phase_splitk_resid(const Ctx *cp, const BatchedW *b
   const int M = c.sp->M;
   for (int i = blockIdx.x * kThreads + threadIdx.x; i < M * rows; i += gridDim.x * kThreads) {
     const int m = i / rows, row = i - m * rows;
-    int32_t d = 0;
-    for (int g = 0; g < ks; g++) d += __ldcg(bw.part + ((size_t)g * kMmaM + m) * rows + row);
+    int32_t d = 0;  // the loads issued together; integer sums in any order are exact
+#pragma unroll
+    for (int g = 0; g < kDownSplits; g++)
+      if (g < ks) d += __ldcg(bw.part + ((size_t)g * kMmaM + m) * rows + row);
     const float v = vnni_finalize(d, __ldg(A.rowsum + row), __ldcg(bw.act_sx + m), __ldg(A.scale + row));
     bool in_place = resid_mode == RESID_ALWAYS;
     if (resid_mode == RESID_ATTN) {
