@@ -275,17 +275,6 @@ __device__ __noinline__ void phase_gemm_b(const Ctx *cp, const BatchedW *bwp, co
   int TU0 = 0;
   for (int n0 = lo; n0 < hi; n0 += NT, TU0 += nsu) {
     const int nrows = min(NT, hi - n0);
-    // scales / row sums of this N tile
-    for (int i = threadIdx.x; i < nrows; i += kThreads) {
-      s_scl[i] = __ldg(a.A.scale + n0 + i);
-      s_rs[i] = __ldg(a.A.rowsum + n0 + i);
-      // argmax: 128 * rowsum of vnni_finalize, once per column (the B half is unused)
-      if (a.epi == EPI_ARGMAX) s_scl[kMaxNT + i] = __fmul_rn(128.0f, (float)s_rs[i]);
-      if (two) {
-        s_scl[kMaxNT + i] = __ldg(a.B.scale + n0 + i);
-        s_rs[kMaxNT + i] = __ldg(a.B.rowsum + n0 + i);
-      }
-    }
     auto issue = [&](int su) {  // thread 0: copies of stage su (K tiles su*U ..)
       const int slot = (TU0 + su) % S;
       uint8_t *sa = stg + (size_t)slot * stage_bytes;
@@ -296,9 +285,22 @@ __device__ __noinline__ void phase_gemm_b(const Ctx *cp, const BatchedW *bwp, co
       tma_2d(sa + U * kGemmA, a.mapA, kt0 * KP + su * rowb, n0, &bar_ld[slot]);
       if (two) tma_2d(sa + U * kGemmA + bytes_b, a.mapB, kt0 * KP + su * rowb, n0, &bar_ld[slot]);
     };
+    // the first stages' copies first: the scales below are read only by the
+    // epilogue, so their load latency overlaps the copies and the MMAs
     if (threadIdx.x == 0) {
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       for (int su = 0; su < nsu && su < S; su++) issue(su);
+    }
+    // scales / row sums of this N tile
+    for (int i = threadIdx.x; i < nrows; i += kThreads) {
+      s_scl[i] = __ldg(a.A.scale + n0 + i);
+      s_rs[i] = __ldg(a.A.rowsum + n0 + i);
+      // argmax: 128 * rowsum of vnni_finalize, once per column (the B half is unused)
+      if (a.epi == EPI_ARGMAX) s_scl[kMaxNT + i] = __fmul_rn(128.0f, (float)s_rs[i]);
+      if (two) {
+        s_scl[kMaxNT + i] = __ldg(a.B.scale + n0 + i);
+        s_rs[kMaxNT + i] = __ldg(a.B.rowsum + n0 + i);
+      }
     }
     if (mk && n0 == lo) rg_bmark(c, 17);
     const uint32_t idesc = umma_idesc_i8(NT);
