@@ -97,6 +97,17 @@ int ocrvl_quant_type(const ocrvl_model *m);
  * tracing is off). */
 int ocrvl_trace_read(ocrvl_model *m, uint64_t *out, int cap);
 
+/* Copies up to `count` floats of one of the step's work buffers, as the
+ * last step left them, to host memory (no reference counterpart: a
+ * debugging aid for comparing a step's intermediates with a CPU run).
+ * which: 0 residual h [n][hidden], 1 residual + projection [n][hidden], 2 q|k|v
+ * before RoPE [n][(heads + 2 kv_heads) head_dim], 3 attention output
+ * [n][heads head_dim], 4 SwiGLU output [n][intermediate], 5 long-cache
+ * attention scores (per sequence [kv head][head][positions], sequences in
+ * order); each for the last layer the step ran.  Returns the number of floats
+ * copied. */
+int ocrvl_debug_read(ocrvl_model *m, int which, float *out, int64_t count);
+
 void ocrvl_free(ocrvl_model *m);
 
 /* A decode sequence owning paged KV for up to max_tokens positions.

@@ -670,8 +670,10 @@ void append_kv(Seq &s, int li, const float *k, const float *v) {
 
 // forwardEmbeddingForSampling, CPU branches (model.go:3475-3643, 3850-4066,
 // 5714-5800).  Returns 0 or <0 on a shape error.
+// dump (nullable): per layer [h_in H | norm1 H | q, k, v before RoPE | head
+// QH*D | h + o H | norm2 H | g I] (orc_dump_floats per layer).
 int forward(Model &m, Seq &s, const float *emb, int T, int H, int W, bool need_logits,
-            int *token, float *logits, float *final_out) {
+            int *token, float *logits, float *final_out, float *dump = nullptr) {
   const orc_config &c = m.cfg;
   int hid = c.hidden_size, D = c.head_dim;
   int qrows = c.num_heads * D, kvrows = c.num_kv_heads * D;
@@ -685,7 +687,10 @@ int forward(Model &m, Seq &s, const float *emb, int T, int H, int W, bool need_l
   for (int li = 0; li < c.num_layers; li++) {
     Layer &L = m.layers[li];
     bool last = li + 1 == c.num_layers;
+    float *dl = dump ? dump + (size_t)li * (4 * hid + 2 * qrows + 2 * kvrows + qrows + c.intermediate_size) : nullptr;
+    if (dl) memcpy(dl, h.data(), sizeof(float) * hid);
     rmsnorm(h.data(), L.ln1.data(), hid, c.rms_norm_eps, norm.data());
+    if (dl) memcpy(dl + hid, norm.data(), sizeof(float) * hid);
     if (last && !need_logits) {
       // attentionCacheOnly (model.go:3650-3668)
       matvec(L.k, norm.data(), k.data());
@@ -709,6 +714,11 @@ int forward(Model &m, Seq &s, const float *emb, int T, int H, int W, bool need_l
       matvec(L.q, norm.data(), q.data());
       matvec(L.k, norm.data(), k.data());
       matvec(L.v, norm.data(), v.data());
+      if (dl) {
+        memcpy(dl + 2 * hid, q.data(), sizeof(float) * qrows);
+        memcpy(dl + 2 * hid + qrows, k.data(), sizeof(float) * kvrows);
+        memcpy(dl + 2 * hid + qrows + kvrows, v.data(), sizeof(float) * kvrows);
+      }
       if (has_rope) {
         rope(q.data(), c.num_heads, D, cs.data(), sn.data());
         rope(k.data(), c.num_kv_heads, D, cs.data(), sn.data());
@@ -720,9 +730,18 @@ int forward(Model &m, Seq &s, const float *emb, int T, int H, int W, bool need_l
       // longer caches -> Q8 in place, Q4/Q6 ...OutOnly (model.go:4043-4062).
       in_place = n <= 6 || !vnni;
     }
-    if (!matvec_add_rmsnorm(L.o, head.data(), h.data(), L.ln2.data(), c.rms_norm_eps, in_place, norm.data()))
+    if (dl) memcpy(dl + 2 * hid + qrows + 2 * kvrows, head.data(), sizeof(float) * qrows);
+    // v = h + o and its fused-order norm; h takes v only in the in-place form
+    std::vector<float> vo(h);
+    if (!matvec_add_rmsnorm(L.o, head.data(), vo.data(), L.ln2.data(), c.rms_norm_eps, true, norm.data()))
       return -2;
+    if (in_place) h = vo;
+    if (dl) {
+      memcpy(dl + 2 * hid + 2 * qrows + 2 * kvrows, vo.data(), sizeof(float) * hid);
+      memcpy(dl + 3 * hid + 2 * qrows + 2 * kvrows, norm.data(), sizeof(float) * hid);
+    }
     swiglu(L.gate, L.up, norm.data(), g.data());
+    if (dl) memcpy(dl + 4 * hid + 2 * qrows + 2 * kvrows, g.data(), sizeof(float) * c.intermediate_size);
     if (!last) {
       if (!matvec_add_rmsnorm(L.down, g.data(), h.data(), m.layers[li + 1].ln1.data(), c.rms_norm_eps, true, scratch.data()))
         return -2;
@@ -802,6 +821,17 @@ void *orc_load(const char *path, const orc_config *cfg, char *err, int errlen) {
 }
 
 void orc_free(void *model) { delete (Model *)model; }
+int orc_set_threads(int n) {
+  // the CPU baseline runs on every host core whatever OMP_NUM_THREADS a
+  // launcher (torchrun sets 1 for multi-process jobs) put in the environment
+#ifdef _OPENMP
+  if (n > 0) omp_set_num_threads(n);
+  return omp_get_max_threads();
+#else
+  (void)n;
+  return 1;
+#endif
+}
 int orc_quant_type(void *model) { return ((Model *)model)->qtype; }
 
 void *orc_seq_new(void *model, int max_tokens) {
@@ -816,6 +846,26 @@ void *orc_seq_new(void *model, int max_tokens) {
 }
 void orc_seq_free(void *seq) { delete (Seq *)seq; }
 int orc_seq_len(void *seq) { return ((Seq *)seq)->len; }
+int orc_seq_import_kv(void *seq, int n, const float *k, const float *v) {
+  // the cache a prompt of n tokens would leave (kvCache contents,
+  // model.go:373-379), given as [layer][n][kv_heads*head_dim]
+  Seq *s = (Seq *)seq;
+  if (n < 0 || (n > 0 && (!k || !v))) return -1;
+  int kvd = s->m->cfg.num_kv_heads * s->m->cfg.head_dim;
+  if (n > s->cap) {
+    for (size_t l = 0; l < s->k.size(); l++) {
+      s->k[l].resize((size_t)n * kvd);
+      s->v[l].resize((size_t)n * kvd);
+    }
+    s->cap = n;
+  }
+  for (size_t l = 0; l < s->k.size(); l++) {
+    memcpy(s->k[l].data(), k + l * (size_t)n * kvd, (size_t)n * kvd * 4);
+    memcpy(s->v[l].data(), v + l * (size_t)n * kvd, (size_t)n * kvd * 4);
+  }
+  s->len = n;
+  return 0;
+}
 int orc_seq_kv(void *seq, int layer, float *k, float *v) {
   Seq *s = (Seq *)seq;
   if (layer < 0 || layer >= (int)s->k.size()) return -1;
@@ -828,6 +878,11 @@ int orc_seq_kv(void *seq, int layer, float *k, float *v) {
 int orc_forward(void *model, void *seq, const float *emb, int pT, int pH, int pW, int need_logits,
                 int *token, float *logits, float *final_norm) {
   return forward(*(Model *)model, *(Seq *)seq, emb, pT, pH, pW, need_logits != 0, token, logits, final_norm);
+}
+
+int orc_forward_dump(void *model, void *seq, const float *emb, int pT, int pH, int pW, int *token, float *logits,
+                     float *dump) {
+  return forward(*(Model *)model, *(Seq *)seq, emb, pT, pH, pW, true, token, logits, nullptr, dump);
 }
 
 int orc_embed(void *model, int id, float *out) {

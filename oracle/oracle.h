@@ -40,12 +40,18 @@ enum { ORC_F32 = 0, ORC_Q8 = 1000, ORC_Q4 = 1001, ORC_Q6 = 1002 };
 /* ---- model / sequence --------------------------------------------------- */
 void *orc_load(const char *gguf_path, const orc_config *cfg, char *err, int errlen);
 void orc_free(void *model);
+/* OpenMP threads of the oracle's parallel loops (n > 0 sets them); returns
+ * the count in effect.  The CPU baseline sets every host core. */
+int orc_set_threads(int n);
 int orc_quant_type(void *model);
 void *orc_seq_new(void *model, int max_tokens);
 void orc_seq_free(void *seq);
 int orc_seq_len(void *seq);
 /* Copies layer `layer`'s K and V caches ([len][kv_heads*head_dim] f32). */
 int orc_seq_kv(void *seq, int layer, float *k, float *v);
+/* Replaces the cache with n positions given for every layer
+ * ([num_layers][n][kv_heads*head_dim] f32 each) and sets the length to n. */
+int orc_seq_import_kv(void *seq, int n, const float *k, const float *v);
 
 /* One decode step (Runtime.forwardEmbeddingForSampling, model.go:3475-3643).
  * emb: hidden_size f32.  pos: (T,H,W).  If need_logits, writes the argmax id to
@@ -53,6 +59,12 @@ int orc_seq_kv(void *seq, int layer, float *k, float *v);
  * final_norm (nullable) receives the lm_head input vector. */
 int orc_forward(void *model, void *seq, const float *emb, int pT, int pH, int pW,
                 int need_logits, int *token, float *logits, float *final_norm);
+
+/* orc_forward with need_logits, also writing the intermediates of every
+ * layer to dump: [h_in H | norm1 H | q QH*D | k KVH*D | v KVH*D (before RoPE)
+ * | head QH*D | h + o H | norm2 H | g I] per layer (debugging aid). */
+int orc_forward_dump(void *model, void *seq, const float *emb, int pT, int pH, int pW, int *token,
+                     float *logits, float *dump);
 
 /* Greedy generation (Runtime.GenerateWithOptions, model.go:1492-1572) with
  * temperature 0.  out receives prompt + generated ids; returns count or <0. */

@@ -46,13 +46,16 @@ def lib():
         L.orc_load.restype = P
         L.orc_load.argtypes = [C.c_char_p, C.POINTER(OrcConfig), C.c_char_p, I]
         L.orc_free.argtypes = [P]
+        L.orc_set_threads.argtypes = [I]
         L.orc_quant_type.argtypes = [P]
         L.orc_seq_new.restype = P
         L.orc_seq_new.argtypes = [P, I]
         L.orc_seq_free.argtypes = [P]
         L.orc_seq_len.argtypes = [P]
         L.orc_seq_kv.argtypes = [P, I, P, P]
+        L.orc_seq_import_kv.argtypes = [P, I, P, P]
         L.orc_forward.argtypes = [P, P, P, I, I, I, I, P, P, P]
+        L.orc_forward_dump.argtypes = [P, P, P, I, I, I, P, P, P]
         L.orc_generate.argtypes = [P, P, I, I, P, I, P, I]
         L.orc_decode_steps.argtypes = [P, P, I, I, I]
         L.orc_embed.argtypes = [P, I, P]
@@ -82,6 +85,11 @@ def lib():
         L.orc_argmax_matvec.argtypes = [I, I, I, P, P, P, P]
         _lib = L
     return _lib
+
+
+def set_threads(n: int) -> int:
+    """OpenMP threads of the oracle (n > 0 sets them); returns the count in effect."""
+    return int(lib().orc_set_threads(int(n)))
 
 
 def ptr(a: np.ndarray):
@@ -170,6 +178,32 @@ class OracleSeq:
             raise RuntimeError(f"oracle forward failed ({rc})")
         return tok.value, logits, fin
 
+    def forward_dump(self, emb, pos):
+        """orc_forward_dump: (token, logits, per-layer dict of intermediates)."""
+        c = self.m.cfg
+        H, I = c.hidden_size, c.intermediate_size
+        qr, kr = c.num_attention_heads * c.head_dim, c.num_key_value_heads * c.head_dim
+        per = 4 * H + 2 * qr + 2 * kr + I
+        dump = np.zeros(c.num_hidden_layers * per, np.float32)
+        logits = np.zeros(c.vocab_size, np.float32)
+        tok = C.c_int(-1)
+        t, h, w = pos if isinstance(pos, (tuple, list)) else (pos, pos, pos)
+        rc = lib().orc_forward_dump(self.m.h, self.h, ptr(np.ascontiguousarray(emb, np.float32)), t, h, w,
+                                    C.byref(tok), ptr(logits), ptr(dump))
+        if rc != 0:
+            raise RuntimeError(f"oracle forward failed ({rc})")
+        layers = []
+        for li in range(c.num_hidden_layers):
+            d = dump[li * per:(li + 1) * per]
+            o = 0
+            rec = {}
+            for name, size in (("h_in", H), ("norm1", H), ("q", qr), ("k", kr), ("v", kr), ("head", qr),
+                               ("vo", H), ("norm2", H), ("g", I)):
+                rec[name] = d[o:o + size].copy()
+                o += size
+            layers.append(rec)
+        return tok.value, logits, layers
+
     def kv(self, layer):
         c = self.m.cfg
         n = len(self)
@@ -178,6 +212,15 @@ class OracleSeq:
         v = np.zeros((max(n, 1), kvd), np.float32)
         lib().orc_seq_kv(self.h, layer, ptr(k), ptr(v))
         return k[:n], v[:n]
+
+    def import_kv(self, k, v):
+        """Cache of n positions, k and v [num_layers][n][kv_heads*head_dim] f32."""
+        k = np.ascontiguousarray(k, np.float32)
+        v = np.ascontiguousarray(v, np.float32)
+        if k.shape != v.shape or k.ndim != 3:
+            raise ValueError("K/V must be [num_layers][n][kvd]")
+        if lib().orc_seq_import_kv(self.h, int(k.shape[1]), ptr(k), ptr(v)) != 0:
+            raise RuntimeError("oracle import_kv failed")
 
     def decode_steps(self, tok, pos, steps):
         return lib().orc_decode_steps(self.m.h, self.h, int(tok), int(pos), int(steps))

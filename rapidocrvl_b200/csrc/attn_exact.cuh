@@ -1,0 +1,581 @@
+// Attention over long caches (more than kAttnChunk positions) in the
+// reference's exact arithmetic, as two phases separated by a grid barrier.
+// Included by decoder.cuh after the KV, RoPE, mbarrier and stage-ring
+// helpers.
+//
+// The reference (cacheAttentionScores, SoftmaxInPlace, weightedCacheValueSum;
+// internal/model/model.go:4623-4795, 5201-5591, internal/tensor/ops.go:
+// 1199-1363) computes, per query head h over the n cached positions:
+//   s_t = dotF32(q_h, k_t) * 1/sqrt(D)      (16-slot order + tree16)
+//   M   = max_t s_t
+//   e_t = exp_fma(s_t - M) for t < nv = 16 floor(n / 16); the positions at or
+//         above nv keep their raw score (expF32VecFMA leaves the tail,
+//         internal/tensor/dot_amd64.s:6131-6168)
+//   sum = tree16 of 16 lane chains, lane l adding e_l, e_{l+16}, ... in order
+//   w_t = e_t * (1 / sum)                    (the tail: s_t * (1 / sum))
+//   o   = w_0 v_0, then o = fma(w_t, v_t, o) for t = 1 .. n-1
+// Both phases restate these steps in the same order, so the head outputs
+// are bit-identical to the reference's.
+//
+// Phase 1 (scores).  The long caches' positions split into chunks of 32
+// (two KV pages) per (sequence m, kv head g); the step's chunks, in (m, g,
+// chunk) order, go to the blocks in contiguous ranges of equal count.  A
+// block streams its chunks' K rows (one 8 KB bulk copy per page) through
+// kAxKBufs buffers, the first ones issued before the phase, and writes the
+// G scores of every position to the score scratch (c.att_s, per sequence
+// [kv head][head][n rounded up to 4]).  The chunk holding the new position scores it with the
+// new key (rotated) and appends the new K and V rows to the cache.
+//
+// Phase 2 (softmax and values).  One item per (m, g, half of the head dims):
+// warp h reads head h's scores, takes M, the lane chains and 1/sum (every
+// item of a pair recomputes them: 8 n exponentials), then lane i of warp h
+// runs the value chains of dims (64 half + 2 i, +1) over all n positions in
+// order, with V rows staged through shared memory 32 positions at a time.
+namespace ocrvl {
+
+constexpr int kAxTok = 32;                            // positions per score chunk (two pages)
+constexpr int kAxKBufs = 4;                           // K chunk buffers per block
+constexpr int kAxKBytes = kAxTok * kHeadDim * 4;      // K rows of one chunk: 16 KB
+constexpr int kAxVTok = 32;                           // positions per value step
+constexpr int kAxVBytes = kAxVTok * (kHeadDim / 2) * 4;  // half-dim V rows of one step: 8 KB
+static_assert(2 * kAxKBytes == kStageBytes, "two K chunks per ring slot");
+static_assert(kMaxGroup == 8 && kHeadDim == 128, "score layout: 8 heads x 2 tokens per half-warp");
+
+// Small arrays of the score phase (floats from their base): rotated q by lane
+// [half-warp grp][head][2][slot][4] (dims (16 (j ^ grp) + slot, +64)), the
+// new key (rotated) and value, cos / sin of the sequence's position.
+constexpr int kAxQs = 0;
+constexpr int kAxKnew = kAxQs + 2 * 8 * 128;  // [128] rotated new k, [128] new v
+constexpr int kAxCos = kAxKnew + 256;         // [64] cos, [64] sin
+constexpr int kAxSmallFloats = kAxCos + 128;
+static_assert(kAxSmallFloats * 4 <= kStageBytes, "small arrays fit one ring slot");
+
+// Shared memory the attention phases need when M > 1 (their buffers start at
+// the base of the dynamic shared memory; for M <= 1 the K buffers use ring
+// slots kStagesM1-1 and kStagesM1-2 and the small arrays ring slot 0; the
+// value phase uses the base of the shared memory for every M).
+__host__ __device__ __forceinline__ size_t ax_smem_bytes_multi() {
+  return (size_t)kAxKBufs * kAxKBytes + (size_t)kAxSmallFloats * 4;
+}
+
+__device__ __forceinline__ float *ax_kbuf(const Ctx &c, int M, float *smem, int j) {
+  if (M <= 1)
+    return (float *)((uint8_t *)smem + gemv_prologue_bytes(c.qtype, 1, c.pro_cols) +
+                     (size_t)(kStagesM1 - 1 - j / 2) * kStageBytes + (size_t)(j & 1) * kAxKBytes);
+  return (float *)((uint8_t *)smem + (size_t)j * kAxKBytes);
+}
+__device__ __forceinline__ float *ax_small(const Ctx &c, int M, float *smem) {
+  if (M <= 1) return (float *)((uint8_t *)smem + gemv_prologue_bytes(c.qtype, 1, c.pro_cols));
+  return (float *)((uint8_t *)smem + (size_t)kAxKBufs * kAxKBytes);
+}
+// Geometry of the step's caches, fixed for a launch and computed at its start
+// (ax_launch_init): per sequence its positions n (0 for a cache of at most
+// kAttnChunk positions, handled by the short path), the prefix of its chunks
+// over (sequence, kv head) and of its scores; the long caches (longest
+// first) and the short ones (in order); this block's chunk range.
+__shared__ int s_ax_n[kMaxSeqs], s_ax_cb[kMaxSeqs + 1], s_ax_sb[kMaxSeqs];
+__shared__ int s_ax_nl, s_ax_long[kMaxSeqs];
+__shared__ int s_ex_n, s_ex_m[kMaxSeqs];
+__shared__ int s_ax_lo, s_ax_hi;
+
+// Per-block state of the K chunk loads, kept across the phases of a launch:
+// s_ax_full[j] completes when buffer j's copies land, s_ax_par bit j is the
+// parity of its next completion, s_ax_issued counts the chunks of the coming
+// (or running) score phase issued so far (chunk lo + i into buffer i %
+// kAxKBufs).
+__shared__ __align__(8) uint64_t s_ax_full[kAxKBufs];
+__shared__ uint32_t s_ax_par;
+__shared__ int s_ax_issued;
+
+__device__ __forceinline__ void ax_block_init() {
+  if (threadIdx.x == 0) {
+    for (int j = 0; j < kAxKBufs; j++) mbar_init(&s_ax_full[j], 1);
+    mbar_fence_init();
+    s_ax_par = 0;
+    s_ax_issued = 0;
+  }
+}
+
+// Row stride of a head's scores: n rounded up to 4 floats, so every row starts
+// on a 16-byte boundary (bulk and cp.async copies of whole rows).
+__host__ __device__ __forceinline__ int ax_stride(int n) { return (n + 3) & ~3; }
+
+__device__ __forceinline__ int ax_bound(int P, int b, int nb) { return (int)(((long long)P * b + nb - 1) / nb); }
+
+// All threads, once per launch (after the step parameters are in shared
+// memory and ax_block_init).
+__device__ void ax_launch_init(const Ctx &c) {
+  const StepParams &sp = *c.sp;
+  if (threadIdx.x == 0) {
+    int cb = 0, sb = 0, ne = 0, nl = 0;
+    for (int m = 0; m < sp.M; m++) {
+      const int n = sp.seq[m].len + 1;
+      const bool lng = n > kAttnChunk;
+      s_ax_n[m] = lng ? n : 0;
+      s_ax_cb[m] = cb;
+      s_ax_sb[m] = sb;
+      if (lng) {
+        cb += c.KVH * ((n + kAxTok - 1) / kAxTok);
+        sb += c.QH * ax_stride(n);
+        s_ax_long[nl++] = m;
+      } else {
+        s_ex_m[ne++] = m;
+      }
+    }
+    s_ax_cb[sp.M] = cb;
+    s_ex_n = ne;
+    s_ax_nl = nl;
+    // value items go to the blocks longest cache first (stable insertion sort)
+    for (int i = 1; i < nl; i++) {
+      const int m = s_ax_long[i];
+      int j = i - 1;
+      while (j >= 0 && s_ax_n[s_ax_long[j]] < s_ax_n[m]) {
+        s_ax_long[j + 1] = s_ax_long[j];
+        j--;
+      }
+      s_ax_long[j + 1] = m;
+    }
+    s_ax_lo = ax_bound(cb, blockIdx.x, gridDim.x);
+    s_ax_hi = ax_bound(cb, blockIdx.x + 1, gridDim.x);
+  }
+}
+
+// Chunk ci of the step: its sequence, kv head and first position.
+struct AxChunk {
+  int m, g, t0;
+};
+__device__ __forceinline__ AxChunk ax_chunk(const Ctx &c, const StepParams &sp, int ci) {
+  int lo = 0, hi = sp.M - 1;  // last sequence with s_ax_cb <= ci
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (s_ax_cb[mid] <= ci) lo = mid;
+    else hi = mid - 1;
+  }
+  const int nch = (s_ax_n[lo] + kAxTok - 1) / kAxTok;
+  const int r = ci - s_ax_cb[lo];
+  AxChunk k;
+  k.m = lo;
+  k.g = r / nch;
+  k.t0 = (r - k.g * nch) * kAxTok;
+  return k;
+}
+
+// K rows of (layer, kv head g) in pool page `page`: 8 KB (the V rows follow).
+__device__ __forceinline__ const float *ax_page_k(const Ctx &c, int page, int layer, int g) {
+  return c.kv_pool + (size_t)page * c.page_floats + ((size_t)layer * c.KVH + g) * 2 * kPageTokens * c.D;
+}
+
+// One thread: the K copies of the block's chunk lo + i into buffer i % kAxKBufs.
+__device__ __forceinline__ void ax_issue(const Ctx &c, int layer, float *smem, int i) {
+  const StepParams &sp = *c.sp;
+  const AxChunk k = ax_chunk(c, sp, s_ax_lo + i);
+  const int n = s_ax_n[k.m];
+  const int *bt = sp.seq[k.m].bt;
+  const bool two = k.t0 + kPageTokens < n;
+  constexpr uint32_t pb = kPageTokens * kHeadDim * 4;
+  const int b = i % kAxKBufs;
+  float *buf = ax_kbuf(c, sp.M, smem, b);
+  uint64_t *bar = &s_ax_full[b];
+  mbar_expect_tx(bar, (two ? 2u : 1u) * pb);
+  bulk_g2s(buf, ax_page_k(c, __ldg(bt + k.t0 / kPageTokens), layer, k.g), pb, bar);
+  if (two) bulk_g2s(buf + kPageTokens * kHeadDim, ax_page_k(c, __ldg(bt + k.t0 / kPageTokens + 1), layer, k.g), pb, bar);
+}
+
+// One thread: issues the block's chunks while fewer than `upto` (at most
+// kAxKBufs) are in flight or done for the coming phase.
+__device__ void ax_issue_upto(const Ctx &c, int layer, float *smem, int upto) {
+  int i = s_ax_issued;
+  const int nch = s_ax_hi - s_ax_lo;
+  if (upto > kAxKBufs) upto = kAxKBufs;
+  if (i >= upto || i >= nch) return;
+  // the buffers were last written by ordinary stores (or read) in earlier
+  // phases: order those before the async copies
+  if (i == 0) asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  for (; i < upto && i < nch; i++) ax_issue(c, layer, smem, i);
+  s_ax_issued = i;
+}
+
+// Waits for chunk copies issued ahead of a score phase that did not run
+// (thread 0).
+__device__ __forceinline__ void ax_drain(const Ctx &c) {
+  for (int j = 0; j < s_ax_issued && j < kAxKBufs; j++) {
+    mbar_wait(&s_ax_full[j], (s_ax_par >> j) & 1u, c.err);
+    s_ax_par ^= 1u << j;
+  }
+  s_ax_issued = 0;
+}
+
+// Per-block time stamp i (thread 0; the last layer's values remain).
+__device__ __forceinline__ void rg_bmark(const Ctx &c, int i) {
+  if (c.trace && threadIdx.x == 0) c.trace[4 * kTraceRows + kTraceMarks * blockIdx.x + i] = gtimer();
+}
+
+// Pairs of floats in one 64-bit register pair and the sm_100 packed FP32
+// operations on them (each half rounded to nearest even, as the scalar
+// __fmul_rn / __fadd_rn / __fmaf_rn).  A packed multiply whose result feeds a
+// packed add is contracted into an FMA by ptxas (measured on B200 even with
+// the explicit .rn), so no exact path uses that pair.
+typedef unsigned long long f2x;
+__device__ __forceinline__ f2x f2_pack(float a, float b) {
+  f2x r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+  return r;
+}
+__device__ __forceinline__ float f2_lo(f2x r) { return __uint_as_float((uint32_t)(r & 0xFFFFFFFFull)); }
+__device__ __forceinline__ float f2_hi(f2x r) { return __uint_as_float((uint32_t)(r >> 32)); }
+__device__ __forceinline__ f2x f2_mul(f2x a, f2x b) {
+  f2x d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ f2x f2_add(f2x a, f2x b) {
+  f2x d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ f2x f2_fma(f2x a, f2x b, f2x c) {
+  f2x d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+
+// All threads: rotated q of pair (m, g) into the lane layout, the new key
+// (rotated) and value.
+__device__ void ax_load_q(const Ctx &c, const StepParams &sp, int m, int g, float *sm) {
+  const int G = c.QH / c.KVH;
+  const size_t qkvld = (size_t)(c.QH + 2 * c.KVH) * kHeadDim;
+  const float *row = c.qkv + (size_t)m * qkvld;
+  float *qs = sm + kAxQs, *knew = sm + kAxKnew;
+  const int *pos = sp.seq[m].pos;
+  const bool has_rope = pos[0] != 0 || pos[1] != 0 || pos[2] != 0;
+  const bool tab = s_rope_ready && m < kMaxBatch;  // the launch's RoPE tables hold sequence m
+  float *cs = sm + kAxCos;
+  if (!tab && threadIdx.x < kHeadDim) {
+    const int i = threadIdx.x & 63;
+    const int p = pos[c.sec_axis[i]];
+    cs[threadIdx.x] = __ldg((threadIdx.x < 64 ? c.rope_cos : c.rope_sin) + (size_t)p * (kHeadDim / 2) + i);
+  }
+  __syncthreads();
+  const float *rc = tab ? s_rope_cs[m] : cs, *rs = tab ? s_rope_sn[m] : cs + 64;
+  for (int p = threadIdx.x; p < G * 16 + 48; p += kThreads) {
+    if (p < G * 16) {
+      const int hh = p >> 4, i4 = p & 15;
+      const float *qh = row + (size_t)(g * G + hh) * kHeadDim;
+      float4 a = __ldcg((const float4 *)qh + i4), b = __ldcg((const float4 *)(qh + 64) + i4);
+      if (has_rope) rope4(a, b, rc + 4 * i4, rs + 4 * i4);
+      const float av[4] = {a.x, a.y, a.z, a.w}, bv[4] = {b.x, b.y, b.z, b.w};
+#pragma unroll
+      for (int e = 0; e < 4; e++) {
+        const int d = 4 * i4 + e, jd = d >> 4, sd = d & 15;  // dims d and d + 64
+#pragma unroll
+        for (int gg = 0; gg < 2; gg++) {
+          const int jp = jd ^ gg;
+          *(float2 *)(qs + (((gg * 8 + hh) * 2 + (jp >> 1)) * 16 + sd) * 4 + (jp & 1) * 2) = make_float2(av[e], bv[e]);
+        }
+      }
+    } else if (p < G * 16 + 16) {
+      const int i4 = p - G * 16;
+      const float *kn = row + (size_t)(c.QH + g) * kHeadDim;
+      float4 a = __ldcg((const float4 *)kn + i4), b = __ldcg((const float4 *)(kn + 64) + i4);
+      if (has_rope) rope4(a, b, rc + 4 * i4, rs + 4 * i4);
+      ((float4 *)knew)[i4] = a;
+      ((float4 *)knew)[i4 + 16] = b;
+    } else {
+      const int i4 = p - G * 16 - 16;
+      ((float4 *)(knew + 128))[i4] = __ldcg((const float4 *)(row + (size_t)(c.QH + c.KVH + g) * kHeadDim) + i4);
+    }
+  }
+  __syncthreads();
+}
+
+// Phase 1: scores of the block's chunks (see the top of this file).
+__device__ __noinline__ void phase_attn_scores(const Ctx *cp, int layer, float *smem) {
+  const Ctx &c = *cp;
+  const StepParams &sp = *c.sp;
+  const int G = c.QH / c.KVH;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int slot = lane & 15, grp = lane >> 4;
+  const int lo = s_ax_lo, nch = s_ax_hi - s_ax_lo;
+  if (nch <= 0) return;
+  rg_bmark(c, 1);
+  float *sm = ax_small(c, sp.M, smem);
+  if (threadIdx.x == 0) ax_issue_upto(c, layer, smem, kAxKBufs);
+  const uint32_t par0 = s_ax_par;  // parity of each buffer's next completion
+  int qm = -1, qg = -1;
+#pragma unroll 1
+  for (int i = 0; i < nch; i++) {
+    const AxChunk k = ax_chunk(c, sp, lo + i);
+    const int n = s_ax_n[k.m], len = n - 1;
+    if (k.m != qm || k.g != qg) {
+      ax_load_q(c, sp, k.m, k.g, sm);
+      qm = k.m;
+      qg = k.g;
+    }
+    const int b = i % kAxKBufs;
+    const float *Kb = ax_kbuf(c, sp.M, smem, b);
+    const float *knew = sm + kAxKnew;
+    mbar_wait(&s_ax_full[b], ((par0 >> b) ^ (uint32_t)(i / kAxKBufs)) & 1u, c.err);
+    if (i == 0) rg_bmark(c, 2);
+    // ---- scores of the warp's tokens 4 warp .. 4 warp + 3: half grp takes
+    // tokens 4 warp + 2 grp + {0, 1}; lane slot s multiplies dims s + 16 j
+    // (j = 0..7) and sums them as ((p0+p1)+(p2+p3))+((p4+p5)+(p6+p7)) (packed
+    // in pairs (p_j, p_j+4)); the reduce-scatter over the 16 slots (xor 8, 4,
+    // 2, 1: the reference's tree16) leaves (token lane >> 3, head lane & 7) on
+    // each lane
+    const ulonglong2 *qlane = (const ulonglong2 *)(sm + kAxQs) + (grp * 8 * 2) * 16 + slot;
+    float v[16];
+    {
+      f2x kp[2][4];
+#pragma unroll
+      for (int tl = 0; tl < 2; tl++) {
+        const int tok = 4 * warp + 2 * grp + tl;
+        const float *kr = k.t0 + tok == len ? knew : Kb + (size_t)tok * kHeadDim;
+#pragma unroll
+        for (int jj = 0; jj < 4; jj++) {
+          const int idx = 16 * (jj ^ grp) + slot;
+          kp[tl][jj] = f2_pack(kr[idx], kr[idx + 64]);
+        }
+      }
+      // products as the reference forms them, fmaf(q, k, +0) (its slot
+      // accumulators start at zero): a packed FMA whose zero addend is read at
+      // run time.  ptxas contracts a packed multiply followed by a packed add
+      // into an FMA even with explicit .rn, and folds a constant zero addend,
+      // either of which changes the sums' rounding.
+      const f2x z0 = f2_pack(c.fzero, c.fzero);
+#pragma unroll
+      for (int h = 0; h < 8; h++) {
+        const ulonglong2 qa = qlane[(2 * h) * 16], qb = qlane[(2 * h + 1) * 16];
+#pragma unroll
+        for (int tl = 0; tl < 2; tl++) {
+          const f2x z = f2_add(f2_add(f2_fma(qa.x, kp[tl][0], z0), f2_fma(qa.y, kp[tl][1], z0)),
+                               f2_add(f2_fma(qb.x, kp[tl][2], z0), f2_fma(qb.y, kp[tl][3], z0)));
+          v[tl * 8 + h] = h < G ? __fadd_rn(f2_lo(z), f2_hi(z)) : 0.0f;
+        }
+      }
+    }
+#pragma unroll
+    for (int q = 0; q < 8; q++) {
+      const bool up = lane & 8;
+      const float send = up ? v[q] : v[8 + q];
+      v[q] = __fadd_rn(up ? v[8 + q] : v[q], __shfl_xor_sync(0xffffffffu, send, 8));
+    }
+#pragma unroll
+    for (int q = 0; q < 4; q++) {
+      const bool up = lane & 4;
+      const float send = up ? v[q] : v[4 + q];
+      v[q] = __fadd_rn(up ? v[4 + q] : v[q], __shfl_xor_sync(0xffffffffu, send, 4));
+    }
+#pragma unroll
+    for (int q = 0; q < 2; q++) {
+      const bool up = lane & 2;
+      const float send = up ? v[q] : v[2 + q];
+      v[q] = __fadd_rn(up ? v[2 + q] : v[q], __shfl_xor_sync(0xffffffffu, send, 2));
+    }
+    float s;
+    {
+      const bool up = lane & 1;
+      const float send = up ? v[0] : v[1];
+      s = __fmul_rn(__fadd_rn(up ? v[1] : v[0], __shfl_xor_sync(0xffffffffu, send, 1)), c.attn_scale);
+    }
+    {
+      const int t = k.t0 + 4 * warp + (lane >> 3), h = lane & 7;
+      if (t < n && h < G) __stcg(c.att_s + s_ax_sb[k.m] + (size_t)(k.g * G + h) * ax_stride(n) + t, s);
+    }
+    if (k.t0 <= len && len < k.t0 + kAxTok && ((len - k.t0) >> 2) == warp) {
+      // the new position: appended to the cache (kvCache.append,
+      // internal/model/model.go:5593-5612)
+      ((float4 *)kv_ptr(c, sp.seq[k.m].bt, layer, 0, k.g, len))[lane] = ((const float4 *)knew)[lane];
+      ((float4 *)kv_ptr(c, sp.seq[k.m].bt, layer, 1, k.g, len))[lane] = ((const float4 *)(knew + kHeadDim))[lane];
+    }
+    // every warp is done with buffer b (and, at a pair change, with q)
+    __syncthreads();
+    if (threadIdx.x == 0 && i + kAxKBufs < nch) ax_issue(c, layer, smem, i + kAxKBufs);
+  }
+  if (threadIdx.x == 0) {
+    // chunk i completed a phase of buffer i % kAxKBufs
+    for (int b = 0; b < kAxKBufs; b++)
+      if (nch > b && (((nch - 1 - b) / kAxKBufs) & 1) == 0) s_ax_par ^= 1u << b;
+    s_ax_issued = 0;
+  }
+  rg_bmark(c, 3);
+  __syncthreads();
+}
+
+// Value phase shared memory, from the base of the dynamic shared memory (the
+// phase runs alone: no copies of other phases are in flight during it):
+// a ring of value-step buffers (V rows of 32 positions, half the head dims:
+// 8 KB each, kAxVRing steps in flight, the first ones issued before the
+// softmax statistics are formed), then the item's scores ([G][stride] floats)
+// when they fit in the rest (c.dyn_smem bytes in all), else they are read
+// from the scratch.
+constexpr int kAxVRing = 8;
+constexpr int kAxVRingBytes = kAxVRing * kAxVBytes;
+
+__device__ __forceinline__ float *ax_vbuf(float *smem, int j) { return (float *)((uint8_t *)smem + (size_t)j * kAxVBytes); }
+
+// Every thread's cp.async copies of value step st (positions 32 st .. +31,
+// dims 64 half .. +63) of pair (m, g) into ring buffer st % kAxVRing: 32 rows
+// of 256 bytes; one commit group per step (empty past the last step).
+__device__ __forceinline__ void ax_issue_v(const Ctx &c, const int *bt, int layer, int g, int half, int st, int n,
+                                           float *smem) {
+  const int t0 = st * kAxVTok;
+  if (t0 < n) {
+    float *vb = ax_vbuf(smem, st % kAxVRing);
+    for (int q = threadIdx.x; q < kAxVTok * 16; q += kThreads) {
+      const int r = q >> 4, c16 = q & 15, t = t0 + r;
+      if (t < n) {
+        const float *src = c.kv_pool + (size_t)__ldg(bt + t / kPageTokens) * c.page_floats +
+                           ((((size_t)layer * c.KVH + g) * 2 + 1) * kPageTokens + (t % kPageTokens)) * kHeadDim +
+                           64 * half + 4 * c16;
+        cp_async16(vb + r * 64 + 4 * c16, src);
+      }
+    }
+  }
+  asm volatile("cp.async.commit_group;" ::: "memory");
+}
+
+// Phase 2: softmax and value chains of the step's long caches.
+__device__ __noinline__ void phase_attn_values(const Ctx *cp, int layer, float *smem) {
+  const Ctx &c = *cp;
+  const StepParams &sp = *c.sp;
+  const int G = c.QH / c.KVH;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int items = s_ax_nl * c.KVH * 2;
+  __shared__ float s_mx[kMaxGroup], s_inv[kMaxGroup];
+  float *ssc = (float *)((uint8_t *)smem + kAxVRingBytes);  // the item's scores, when they fit
+  for (int it = blockIdx.x; it < items; it += gridDim.x) {
+    const int m = s_ax_long[it / (2 * c.KVH)], g = (it >> 1) % c.KVH, half = it & 1;
+    const int n = s_ax_n[m], nv = n & ~15, ld = ax_stride(n);
+    const int *bt = sp.seq[m].bt;
+    const float *Sg = c.att_s + s_ax_sb[m] + (size_t)g * G * ld;
+    const bool staged = (size_t)G * ld * 4 + kAxVRingBytes <= (size_t)c.dyn_smem;
+    // the item's scores (one group), then the first value steps
+    if (staged)
+      for (int q = threadIdx.x; q < G * ld / 4; q += kThreads) cp_async16(ssc + 4 * q, Sg + 4 * q);
+    asm volatile("cp.async.commit_group;" ::: "memory");
+    for (int st = 0; st < kAxVRing - 1; st++) ax_issue_v(c, bt, layer, g, half, st, n, smem);
+    // the scores' group is complete once at most kAxVRing - 1 (the value
+    // steps') are pending
+    asm volatile("cp.async.wait_group %0;" ::"n"(kAxVRing - 1) : "memory");
+    __syncthreads();
+    const float *S = staged ? ssc : Sg;
+    if (warp < G) {
+      const float *Sh = S + (size_t)warp * ld;
+      float mx = -INFINITY;
+#pragma unroll 8
+      for (int t = lane; t < n; t += 32) mx = fmaxf(mx, staged ? Sh[t] : __ldcg(Sh + t));
+      for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+      // lane chains: lane l (< 16) adds e_l, e_{l+16}, e_{l+32}, ... in order
+      // (lane l + 16 computes the odd 16-blocks' exponentials); scores are
+      // loaded four 32-blocks ahead of their use
+      float acc = 0.0f;
+#pragma unroll 1
+      for (int t0 = 0; t0 < nv; t0 += 128) {
+        float sv[4];
+#pragma unroll
+        for (int u = 0; u < 4; u++) {
+          const int t = t0 + 32 * u + lane;
+          sv[u] = t < nv ? (staged ? Sh[t] : __ldcg(Sh + t)) : 0.0f;
+        }
+#pragma unroll
+        for (int u = 0; u < 4; u++) {
+          const int b0 = t0 + 32 * u;
+          if (b0 < nv) {
+            const float e = b0 + lane < nv ? exp_fma(__fsub_rn(sv[u], mx)) : 0.0f;
+            const float hi = __shfl_down_sync(0xffffffffu, e, 16);
+            acc = __fadd_rn(acc, e);
+            if (b0 + 16 < nv) acc = __fadd_rn(acc, hi);
+          }
+        }
+      }
+      // tree16 of lanes 0..15: (l, l+8), (l, l+4), then (0+2)+(1+3)
+      float a = __fadd_rn(acc, __shfl_down_sync(0xffffffffu, acc, 8));
+      a = __fadd_rn(a, __shfl_down_sync(0xffffffffu, a, 4));
+      a = __fadd_rn(a, __shfl_down_sync(0xffffffffu, a, 2));
+      a = __fadd_rn(a, __shfl_down_sync(0xffffffffu, a, 1));
+      if (lane == 0) {
+        s_mx[warp] = mx;
+        s_inv[warp] = __fdiv_rn(1.0f, a);
+      }
+    }
+    __syncthreads();
+    // ---- value chains: warp h, dims 64 half + 2 lane, +1
+    const int h = warp;
+    const float mx = h < G ? s_mx[h] : 0.0f, inv = h < G ? s_inv[h] : 0.0f;
+    const float *Sh = S + (size_t)(h < G ? h : 0) * ld;
+    f2x o = 0ull;
+    const int nst = (n + kAxVTok - 1) / kAxVTok;
+    // scores of positions 32 st + lane, loaded ahead (two steps) when read
+    // from the scratch
+    float s1 = h < G && lane < n ? (staged ? Sh[lane] : __ldcg(Sh + lane)) : 0.0f;
+    float s2 = h < G && lane + kAxVTok < n ? (staged ? Sh[lane + kAxVTok] : __ldcg(Sh + lane + kAxVTok)) : 0.0f;
+#pragma unroll 1
+    for (int st = 0; st < nst; st++) {
+      const int t0 = st * kAxVTok, t = t0 + lane;
+      const float sv = s1;
+      s1 = s2;
+      s2 = h < G && t + 2 * kAxVTok < n ? (staged ? Sh[t + 2 * kAxVTok] : __ldcg(Sh + t + 2 * kAxVTok)) : 0.0f;
+      float w = 0.0f;
+      if (h < G && t < n) w = __fmul_rn(t < nv ? exp_fma(__fsub_rn(sv, mx)) : sv, inv);
+      // step st's copies: all but the kAxVRing - 2 newest groups are complete
+      asm volatile("cp.async.wait_group %0;" ::"n"(kAxVRing - 2) : "memory");
+      __syncthreads();  // every thread's rows of step st landed; step st-1's buffer is free
+      ax_issue_v(c, bt, layer, g, half, st + kAxVRing - 1, n, smem);
+      const float *vb = ax_vbuf(smem, st % kAxVRing);
+      const int cnt = min(kAxVTok, n - t0);
+      if (h < G) {
+        int i0 = 0;
+        if (st == 0) {
+          const float w0 = __shfl_sync(0xffffffffu, w, 0);
+          o = f2_mul(f2_pack(w0, w0), *(const f2x *)(vb + 2 * lane));
+          i0 = 1;
+        }
+#pragma unroll 8
+        for (int i = i0; i < cnt; i++) {
+          const float wi = __shfl_sync(0xffffffffu, w, i);
+          o = f2_fma(f2_pack(wi, wi), *(const f2x *)(vb + i * 64 + 2 * lane), o);
+        }
+      }
+    }
+    asm volatile("cp.async.wait_group 0;" ::: "memory");
+    if (h < G) {
+      float2 r;
+      r.x = f2_lo(o);
+      r.y = f2_hi(o);
+      *(float2 *)(c.head + ((size_t)m * c.QH + (size_t)g * G + h) * kHeadDim + 64 * half + 2 * lane) = r;
+    }
+    __syncthreads();  // the ring and the score copy are free for the next item
+  }
+}
+
+// KV append of the long caches without attention (the last layer of a step
+// that needs no logits): one warp per (sequence, kv head).
+__device__ void phase_append_long(const Ctx &c, int layer) {
+  const StepParams &sp = *c.sp;
+  const size_t qkvld = (size_t)(c.QH + 2 * c.KVH) * kHeadDim;
+  const int lane = threadIdx.x & 31;
+  const int nw = gridDim.x * (kThreads / 32);
+  for (int p = blockIdx.x * (kThreads / 32) + (threadIdx.x >> 5); p < sp.M * c.KVH; p += nw) {
+    const int m = p / c.KVH, g = p % c.KVH;
+    const int len = sp.seq[m].len;
+    if (len + 1 <= kAttnChunk) continue;
+    const float *row = c.qkv + (size_t)m * qkvld;
+    const int *pos = sp.seq[m].pos;
+    if (lane < 16) {
+      const float4 *kn = (const float4 *)(row + (size_t)(c.QH + g) * kHeadDim);
+      float4 a = __ldcg(kn + lane), b = __ldcg(kn + lane + 16);
+      if (pos[0] != 0 || pos[1] != 0 || pos[2] != 0) {
+        float cs[4], sn[4];
+        rope_cs4(c, pos, lane, cs, sn);
+        rope4(a, b, cs, sn);
+      }
+      float4 *kd = (float4 *)kv_ptr(c, sp.seq[m].bt, layer, 0, g, len);
+      kd[lane] = a;
+      kd[lane + 16] = b;
+    }
+    ((float4 *)kv_ptr(c, sp.seq[m].bt, layer, 1, g, len))[lane] =
+        __ldcg((const float4 *)(row + (size_t)(c.QH + c.KVH + g) * kHeadDim) + lane);
+  }
+}
+
+}  // namespace ocrvl

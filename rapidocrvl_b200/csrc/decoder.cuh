@@ -64,6 +64,8 @@ static_assert(sizeof(SeqParams) == 32, "SeqParams is 32 bytes");
 struct Ctx {
   int qtype, H, I, L, QH, KVH, D, V;
   float eps, attn_scale;
+  float fzero;                       // 0.0f, read at run time (an FMA addend the compiler cannot fold)
+  int dyn_smem;                      // usable dynamic shared memory of the step kernels (bytes, after alignment)
   const float *embed, *final_norm;
   const LayerW *layers;
   DMat lm_head;
@@ -74,9 +76,7 @@ struct Ctx {
   long long page_floats;
   // step work buffers
   float *h, *vbuf, *qkv, *head, *g, *logits;
-  float *part_o;                     // [item][G][D] attention chunk sums (item = (sequence, kv head, chunk))
-  float *part_ml;                    // [item][G][2] chunk max / sum
-  float *part_t;                     // [B][QH][D] raw-score tail sums
+  float *att_s;                      // long-cache attention scores: per sequence [kv head][head][positions]
   unsigned long long *argkey;        // [B]
   int *tok_out;                      // [B] ids, then the error word
   int max_ctx;
@@ -86,7 +86,6 @@ struct Ctx {
   const StepParams *sp;
   StepParams *sp_w;
   int pro_cols;                      // widest GEMV input: fixes the stage-ring offset (0: per phase)
-  unsigned *attn_count;              // [B][KVH][2] chunk arrivals, finished mergers
   unsigned *lm_count;                // lm_head block arrivals
   int *hist, *hist_pos;              // device-side greedy loop: ids [steps][M], write index
   // persistent-kernel barrier: monotonic arrival counter and error word
@@ -1001,105 +1000,87 @@ __device__ __noinline__ void phase_gemv_t(const Ctx *cp, const GemvArgs *ap, int
 // does not change results.
 // ---------------------------------------------------------------------------
 // Input prologue of the single-sequence int8-activation GEMV (xs path), with
-// two block barriers: the gather, then the quantised vector.  Every warp
-// computes the norm's sum of squares in the reference order and the largest
-// |value| itself, so no barrier is spent on those reductions.
-//   PRO_RMSNORM: 64 FMA slot chains (sumSquaresF32FMA), lane L owning slots L
-//     and L+32; slots folded as (s[l]+s[l+16]) + (s[l+32]+s[l+48]) by xor-16
-//     shuffles, then tree16 by xor 8/4/2/1.
-//   PRO_ADDNORM: the fused kernels' 8 workers of n/8 rows, each 16 lanes of
-//     unfused square-adds + tree16 (VNNI finalize); lane L (l = L%16, h =
-//     L/16) runs workers h, h+2, h+4, h+6; worker partials added in order.
-//   The largest |normalised value| is fl(max|fl(x*w)| * scale), rounding
-//   being monotone and sign-symmetric.
+// three block barriers: the gather, the reductions, the quantised vector.
+// The reductions are split over the 8 warps and combined in the reference's
+// order after one barrier:
+//   largest |value|: warp w takes elements [w n/8, (w+1) n/8) (|x| for
+//     PRO_PLAIN, |fl(x*w)| otherwise); the largest |normalised value| is
+//     fl(max|fl(x*w)| * scale), rounding being monotone and sign-symmetric;
+//   PRO_RMSNORM: the 64 FMA slot chains of sumSquaresF32FMA (slot s over
+//     elements s, s+64, ... in order), lane l < 8 of warp w running slot
+//     8w + l; slots folded as (s[l]+s[l+16]) + (s[l+32]+s[l+48]), then tree16;
+//   PRO_ADDNORM: the fused kernels' 8 workers of n/8 rows, worker w on warp w:
+//     16 lanes of unfused square-adds + tree16 (VNNI finalize); worker partials
+//     added in order.
 // Writes the uint8 activations (Q4: even columns then odd) to the x area and
 // returns the activation scale sx (the same value in every thread).
 __device__ __noinline__ float xs_prologue(int qt, const float *src, int n, int mode, const float *w, bool w_global,
-                                          float eps, float *smem) {
+                                          float eps, float *smem, unsigned long long *mk = nullptr) {
+  float *red = smem;  // [0..7] warp maxima, [16..79] slot / worker sums
   float *tmp = smem + 320;
   uint8_t *q = (uint8_t *)(tmp + n);
   g2s_f32(tmp, src, n);
   cp_async_wait_all();
   __syncthreads();
-  const int lane = threadIdx.x & 31;
+  if (mk) mk[17] = gtimer();
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   auto wv = [&](int i) { return w_global ? __ldg(w + i) : w[i]; };
-  float ss = 0.0f, M = 0.0f;
-  // largest |x| (PLAIN) or |fl(x*w)| over the whole vector, float4 at a time
-  if (mode == PRO_PLAIN || !w_global) {
-#pragma unroll 4
-    for (int i = lane; i < n / 4; i += 32) {
+  {
+    // largest |x| (PLAIN) or |fl(x*w)| over the warp's share, float4 at a time
+    const int per4 = n / 4 / kFusedWorkers, b4 = warp * per4;
+    float M = 0.0f;
+    for (int i = b4 + lane; i < b4 + per4; i += 32) {
       const float4 x = ((const float4 *)tmp)[i];
       if (mode == PRO_PLAIN) {
         M = fmaxf(M, fmaxf(fmaxf(fabsf(x.x), fabsf(x.y)), fmaxf(fabsf(x.z), fabsf(x.w))));
       } else {
-        const float4 ww = ((const float4 *)w)[i];
+        const float4 ww = w_global ? __ldg((const float4 *)w + i) : ((const float4 *)w)[i];
         M = fmaxf(M, fmaxf(fmaxf(fabsf(__fmul_rn(x.x, ww.x)), fabsf(__fmul_rn(x.y, ww.y))),
                            fmaxf(fabsf(__fmul_rn(x.z, ww.z)), fabsf(__fmul_rn(x.w, ww.w)))));
       }
     }
-  } else {
-    for (int i = lane; i < n; i += 32) M = fmaxf(M, fabsf(__fmul_rn(tmp[i], __ldg(w + i))));
+    for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+    if (lane == 0) red[warp] = M;
   }
   if (mode == PRO_RMSNORM) {
-    // two slot chains per lane; loads batched ahead of the FMAs
-    float a0 = 0.0f, a1 = 0.0f;
-    constexpr int U = 8;
-#pragma unroll 1
-    for (int c0 = 0; c0 < n; c0 += 64 * U) {
-      float x0[U], x1[U];
-#pragma unroll
-      for (int u = 0; u < U; u++) {
-        const int c = c0 + 64 * u;
-        x0[u] = c < n ? tmp[c + lane] : 0.0f;
-        x1[u] = c < n ? tmp[c + 32 + lane] : 0.0f;
-      }
-#pragma unroll
-      for (int u = 0; u < U; u++) {
-        if (c0 + 64 * u < n) {
-          a0 = __fmaf_rn(x0[u], x0[u], a0);
-          a1 = __fmaf_rn(x1[u], x1[u], a1);
-        }
-      }
+    if (lane < 8) {
+      const int sl = 8 * warp + lane;
+      float a = 0.0f;
+#pragma unroll 4
+      for (int c = sl; c < n; c += 64) a = __fmaf_rn(tmp[c], tmp[c], a);
+      red[16 + sl] = a;
     }
-    float r = __fadd_rn(__fadd_rn(a0, __shfl_xor_sync(0xffffffffu, a0, 16)),
-                        __fadd_rn(a1, __shfl_xor_sync(0xffffffffu, a1, 16)));
-    r = __fadd_rn(r, __shfl_xor_sync(0xffffffffu, r, 8));
-    r = __fadd_rn(r, __shfl_xor_sync(0xffffffffu, r, 4));
-    r = __fadd_rn(r, __shfl_xor_sync(0xffffffffu, r, 2));
-    ss = __fadd_rn(r, __shfl_xor_sync(0xffffffffu, r, 1));
   } else if (mode == PRO_ADDNORM) {
-    // four worker chains per lane, interleaved; loads batched ahead
-    const int chunk = n / kFusedWorkers, l = lane & 15, h = lane >> 4;
-    float part[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-    constexpr int U = 4;
-#pragma unroll 1
-    for (int k0 = 0; k0 < chunk; k0 += 16 * U) {
-      float v[4][U];
-#pragma unroll
-      for (int j = 0; j < 4; j++)
-#pragma unroll
-        for (int u = 0; u < U; u++) {
-          const int k = k0 + 16 * u;
-          v[j][u] = k < chunk ? tmp[(h + 2 * j) * chunk + k + l] : 0.0f;
-        }
-#pragma unroll
-      for (int u = 0; u < U; u++)
-#pragma unroll
-        for (int j = 0; j < 4; j++)
-          if (k0 + 16 * u < chunk) part[j] = __fadd_rn(part[j], __fmul_rn(v[j][u], v[j][u]));
+    const int chunk = n / kFusedWorkers, l = lane & 15;
+    float a = 0.0f;
+    if (lane < 16) {
+#pragma unroll 4
+      for (int k = l; k < chunk; k += 16) {
+        const float x = tmp[warp * chunk + k];
+        a = __fadd_rn(a, __fmul_rn(x, x));
+      }
     }
-#pragma unroll
-    for (int j = 0; j < 4; j++) {
-      float a = part[j];
-      a = __fadd_rn(a, __shfl_xor_sync(0xffffffffu, a, 8));
-      a = __fadd_rn(a, __shfl_xor_sync(0xffffffffu, a, 4));
-      a = __fadd_rn(a, __shfl_xor_sync(0xffffffffu, a, 2));
-      part[j] = __fadd_rn(a, __shfl_xor_sync(0xffffffffu, a, 1));
-    }
-#pragma unroll
-    for (int wk = 0; wk < kFusedWorkers; wk++) ss = __fadd_rn(ss, __shfl_sync(0xffffffffu, part[wk >> 1], (wk & 1) * 16));
+    // tree16 of lanes 0..15
+    a = __fadd_rn(a, __shfl_down_sync(0xffffffffu, a, 8));
+    a = __fadd_rn(a, __shfl_down_sync(0xffffffffu, a, 4));
+    a = __fadd_rn(a, __shfl_down_sync(0xffffffffu, a, 2));
+    a = __fadd_rn(a, __shfl_down_sync(0xffffffffu, a, 1));
+    if (lane == 0) red[16 + warp] = a;
   }
-  for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+  __syncthreads();
+  float M = red[0];
+#pragma unroll
+  for (int i = 1; i < kFusedWorkers; i++) M = fmaxf(M, red[i]);
+  float ss = 0.0f;
+  if (mode == PRO_RMSNORM) {
+    float r[16];
+#pragma unroll
+    for (int l = 0; l < 16; l++) r[l] = __fadd_rn(__fadd_rn(red[16 + l], red[32 + l]), __fadd_rn(red[48 + l], red[64 + l]));
+    ss = tree16(r);
+  } else if (mode == PRO_ADDNORM) {
+#pragma unroll
+    for (int wk = 0; wk < kFusedWorkers; wk++) ss = __fadd_rn(ss, red[16 + wk]);
+  }
   float scale = 1.0f, mx = M;
   if (mode != PRO_PLAIN) {
     scale = fast_rsqrt(__fadd_rn(__fdiv_rn(ss, (float)n), eps));
@@ -1110,6 +1091,7 @@ __device__ __noinline__ float xs_prologue(int qt, const float *src, int n, int m
     sx = __fdiv_rn(mx, 127.0f);
     inv = __fdiv_rn(1.0f, sx);
   }
+  if (mk) mk[18] = gtimer();
   const int half = qt == QT_Q4 ? n / 2 : 0;
   for (int i = threadIdx.x; i < n; i += kThreads) {
     float v = tmp[i];
@@ -1119,6 +1101,7 @@ __device__ __noinline__ float xs_prologue(int qt, const float *src, int n, int m
     q[half ? (i & 1) * half + (i >> 1) : i] = (uint8_t)b;
   }
   __syncthreads();
+  if (mk) mk[19] = gtimer();
   return sx;
 }
 
@@ -1215,6 +1198,12 @@ __device__ __noinline__ void phase_gemv_xs(const Ctx *cp, const GemvArgs *ap, fl
   const int lpr = g.lpr;
   const int rpw = 32 / lpr, li = lane & (lpr - 1), sub = lane / lpr;
   const int pass = (kThreads / 32) * rpw;  // rows one pass of the block covers per RB slot
+  // trace marks 16-23 of the block (QKV phases; the last layer's remain):
+  // entry, input gathered, reductions done, input quantised, activations in
+  // registers, first stage landed, dots done, exit
+  unsigned long long *mk =
+      c.trace && EPI == EPI_STORE && threadIdx.x == 0 ? c.trace + 4 * kTraceRows + kTraceMarks * blockIdx.x : nullptr;
+  if (mk) mk[16] = gtimer();
   // residual values of this lane's rows of a one-stage slab, fetched now so
   // their latency hides behind the prologue
   float rpre[RB];
@@ -1227,7 +1216,7 @@ __device__ __noinline__ void phase_gemv_xs(const Ctx *cp, const GemvArgs *ap, fl
     }
   }
   const float *src = a.src + (a.src_tok ? (size_t)c.sp->seq[0].tok * a.ld : 0);
-  const float sx = xs_prologue(QT, src, n, a.mode, nw_staged ? nw_s : a.norm_w, !nw_staged, c.eps, smem);
+  const float sx = xs_prologue(QT, src, n, a.mode, nw_staged ? nw_s : a.norm_w, !nw_staged, c.eps, smem, mk);
   const uint8_t *xq = (const uint8_t *)(smem + 320 + n);
   if (a.copy_src && blockIdx.x == 0) {
     // layer 0: the embedding row the prologue gathered becomes the residual
@@ -1251,16 +1240,21 @@ __device__ __noinline__ void phase_gemv_xs(const Ctx *cp, const GemvArgs *ap, fl
       }
     }
   }
+  // the sum of all activations: the lpr lanes of a row group hold every
+  // chunk once (zero past the row's end)
   uint32_t qsum = 0;
-  for (int i = lane; i < n / 16; i += 32) {
-    const uint4 v = lds16(xq + 16 * i);
-    qsum = __dp4a(v.x, 0x01010101u, qsum);
-    qsum = __dp4a(v.y, 0x01010101u, qsum);
-    qsum = __dp4a(v.z, 0x01010101u, qsum);
-    qsum = __dp4a(v.w, 0x01010101u, qsum);
-  }
-  for (int o = 16; o > 0; o >>= 1) qsum += __shfl_xor_sync(0xffffffffu, qsum, o);
+#pragma unroll
+  for (int j = 0; j < T::XMAX; j++)
+#pragma unroll
+    for (int t = 0; t < T::XW; t++) {
+      qsum = __dp4a(xr[j][t].x, 0x01010101u, qsum);
+      qsum = __dp4a(xr[j][t].y, 0x01010101u, qsum);
+      qsum = __dp4a(xr[j][t].z, 0x01010101u, qsum);
+      qsum = __dp4a(xr[j][t].w, 0x01010101u, qsum);
+    }
+  for (int o = lpr >> 1; o > 0; o >>= 1) qsum += __shfl_xor_sync(0xffffffffu, qsum, o);
   const int32_t corr = T::OFF * (int32_t)qsum;
+  if (mk) mk[20] = gtimer();
   bool in_place = false;
   if (EPI == EPI_RESID) {
     if (a.resid_mode == RESID_ALWAYS) {
@@ -1282,6 +1276,7 @@ __device__ __noinline__ void phase_gemv_xs(const Ctx *cp, const GemvArgs *ap, fl
     const int r0 = lo + st * srows, nr = min(srows, hi - r0);
     const uint8_t *buf = g.stage + (size_t)(st % g.kSt) * kStageBytes;
     if (!gemv_wait(c, g, st)) ok = false;
+    if (mk && st == 0) mk[21] = gtimer();
 #pragma unroll 1
     for (int base = warp * rpw; ok && base < nr; base += pass * RB) {
       int lr[RB];
@@ -1330,6 +1325,7 @@ __device__ __noinline__ void phase_gemv_xs(const Ctx *cp, const GemvArgs *ap, fl
     __syncthreads();  // stage buffer free
     gemv_retire(a, g, st);
   }
+  if (mk) mk[22] = gtimer();
   if (threadIdx.x == 0) s_ring_setup = 0;
   if constexpr (EPI == EPI_ARGMAX) {
     for (int o = 16; o > 0; o >>= 1) {
@@ -1350,6 +1346,7 @@ __device__ __noinline__ void phase_gemv_xs(const Ctx *cp, const GemvArgs *ap, fl
     }
   }
   __syncthreads();
+  if (mk) mk[23] = gtimer();
 }
 
 // Single sequence: the x-stationary path for Q4/Q6 (when the rows are narrow
@@ -1503,9 +1500,9 @@ __device__ float warp_softmax_weight(float v, int n) {
 // the item takes the new token's k and v from the QKV output, rotates k and
 // appends both to the page (kvCache.append, model.go:5593-5612).
 //
-// Longer caches are streamed in page ranges with an online softmax per
-// segment and a merge per (m, g): phase_attn_range (attn_range.cuh), run in
-// the same phase after the block's short-cache items.
+// Longer caches take two phases in the reference's exact order
+// (attn_exact.cuh): the scores, run in this phase after the block's
+// short-cache items, then the softmax and value sums.
 // ---------------------------------------------------------------------------
 struct AttnItem {
   int m, g, ch, t0, cnt, n, nch;
@@ -1521,7 +1518,7 @@ __shared__ float s_rope_cs[kMaxBatch][kHeadDim / 2], s_rope_sn[kMaxBatch][kHeadD
 __shared__ int s_rope_ready;
 
 }  // namespace ocrvl
-#include "attn_range.cuh"
+#include "attn_exact.cuh"
 namespace ocrvl {
 
 // Item `it` of the step (caches of n <= kAttnChunk positions, one item per
@@ -1568,8 +1565,8 @@ __device__ __forceinline__ void attn_block_init(const Ctx &c) {
     s_kv_item = -1;
     s_rope_ready = 0;
   }
-  rg_block_init();
-  rg_launch_init(c);
+  ax_block_init();
+  ax_launch_init(c);
   __syncthreads();
 }
 
@@ -1641,28 +1638,29 @@ __device__ __forceinline__ void attn_drain_item(const Ctx &c) {
 // Waits for every outstanding K/V load (before the block leaves the kernel).
 __device__ void attn_drain(const Ctx &c) {
   attn_drain_item(c);
-  if (threadIdx.x == 0) rg_drain(c);
+  if (threadIdx.x == 0) ax_drain(c);
   __syncthreads();
 }
 
-// Thread `lead`, ahead of the attention phase of `layer`: the block's first
-// long-cache chunks (attn_range.cuh).  during_qkv: before the QKV phase,
-// whose weight stages then share the ring (single-sequence steps only, into
-// the slots the block's QKV slab leaves free).  A block with n <= kAttnChunk
-// items loads those first and skips this.
+// Thread `lead`, ahead of the attention phase of `layer`: the K copies of
+// the block's first long-cache chunks (attn_exact.cuh).  during_qkv: before
+// the QKV phase, whose weight stages then share the ring (single-sequence
+// steps only, two chunk buffers in each ring slot the block's QKV slab leaves
+// free at the top).  A block with n <= kAttnChunk items loads those first and
+// skips this.
 __device__ void attn_range_prefetch(const Ctx &c, int layer, float *smem, int lead, bool during_qkv) {
   const StepParams &sp = *c.sp;
   if ((int)threadIdx.x != lead || attn_items_total(c, sp) > (int)blockIdx.x) return;
-  int upto = kRangeBufs;
+  int upto = kAxKBufs;
   if (during_qkv) {
     if (sp.M > 1) return;
     const DMat &A = c.layers[layer].qkv;
     int lo, hi;
     gemv_slab(0, A.rows, blockIdx.x, gridDim.x, lo, hi);
     const int srows = kStageBytes / A.pitch;
-    upto = min(upto, kStagesM1 - (hi - lo + srows - 1) / srows);
+    upto = min(upto, 2 * (kStagesM1 - (hi - lo + srows - 1) / srows));
   }
-  rg_issue_upto(c, layer, smem, upto);
+  ax_issue_upto(c, layer, smem, upto);
 }
 
 __device__ __noinline__ void phase_attn(const Ctx *cp, int layer, int append_only, int coop, float *smem) {
@@ -1806,14 +1804,14 @@ __device__ __noinline__ void phase_attn(const Ctx *cp, int layer, int append_onl
   attn_drain_item(c);
   __syncthreads();
   (void)coop;
-  // ---- caches of more than kAttnChunk positions
+  // ---- caches of more than kAttnChunk positions: their scores (the
+  // softmax and value sums follow in phase_attn_values after a grid barrier)
   if (append_only) {
-    if (threadIdx.x == 0) rg_drain(c);
+    if (threadIdx.x == 0) ax_drain(c);
     phase_append_long(c, layer);
     __syncthreads();
   } else {
-    phase_attn_range(cp, layer, smem);
-    rg_merge_pending(cp, smem);
+    phase_attn_scores(cp, layer, smem);
   }
 }
 

@@ -102,8 +102,10 @@ __device__ bool grid_sync(const Ctx &c, unsigned target) {
   return grid_wait(c, target);
 }
 
-constexpr int kLayerPhases = 5;  // qkv, attention, o, gate/up, down
-constexpr int kPhaseLM = 5;      // lm_head argmax (after the last layer)
+// qkv, attention (short caches; long caches' scores), long caches' softmax
+// and values, o, gate/up, down
+constexpr int kLayerPhases = 6;
+constexpr int kPhaseLM = 6;      // lm_head argmax (after the last layer)
 
 __host__ __device__ __forceinline__ unsigned barriers_per_step(int L, int any_logits) {
   return any_logits ? (unsigned)(kLayerPhases * L) : (unsigned)(kLayerPhases * (L - 1) + 1);
@@ -137,7 +139,7 @@ __device__ void build_args(const Ctx &c, int phase, int layer, int any_logits, i
         sa.out = c.qkv;
         sa.ldo = (c.QH + 2 * c.KVH) * c.D;
         break;
-      case 2:  // o projection + residual
+      case 3:  // o projection + residual
         sa.A = L.o;
         sa.row_end = L.o.rows;
         sa.src = c.head;
@@ -149,7 +151,7 @@ __device__ void build_args(const Ctx &c, int phase, int layer, int any_logits, i
         sa.vout = c.vbuf;
         sa.resid_mode = RESID_ATTN;
         break;
-      case 3:  // gate/up with the post-attention AddRMSNorm as prologue
+      case 4:  // gate/up with the post-attention AddRMSNorm as prologue
         sa.A = L.gate;
         sa.B = L.up;
         sa.row_end = L.gate.rows;
@@ -161,7 +163,7 @@ __device__ void build_args(const Ctx &c, int phase, int layer, int any_logits, i
         sa.out = c.g;
         sa.ldo = c.I;
         break;
-      case 4:  // down projection + residual (last layer: out-only)
+      case 5:  // down projection + residual (last layer: out-only)
         sa.A = L.down;
         sa.row_end = L.down.rows;
         sa.src = c.g;
@@ -190,7 +192,7 @@ __device__ void build_args(const Ctx &c, int phase, int layer, int any_logits, i
     }
 }
 
-__device__ __forceinline__ bool is_gemv_phase(int phase) { return phase != 1; }
+__device__ __forceinline__ bool is_gemv_phase(int phase) { return phase != 1 && phase != 2; }
 
 // Work for phase (phase, layer) that needs nothing from other blocks, done by
 // threads kHelper.. while thread 0 waits at the grid barrier before it: the
@@ -227,6 +229,8 @@ __device__ void run_phase(const Ctx &c, int phase, int layer, int M, int any_log
   const bool last = layer == c.L - 1;
   if (phase == 1) {
     phase_attn(&c, layer, last && !any_logits, coop, smem);
+  } else if (phase == 2) {
+    phase_attn_values(&c, layer, smem);
   } else {
     if (!prepared) {
       if (threadIdx.x == 0) build_args(c, phase, layer, any_logits, do_embed, feed, tidx);
@@ -301,7 +305,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         ((int *)&s_step_params)[i] = __ldcg((const int *)cv.sp + i);
       if (threadIdx.x == 0) s_rope_ready = 0;
       __syncthreads();
-      rg_launch_init(c);
+      ax_launch_init(c);
       __syncthreads();
     }
     int t = 0;
@@ -389,9 +393,10 @@ __host__ __device__ __forceinline__ int gemm_nt(int rows, int grid) {
   return nt < 256 ? nt : 256;  // kMaxNT
 }
 __host__ __device__ __forceinline__ unsigned barriers_per_step_b(int L, int any_logits) {
-  // per layer: 4 quantisation phases, 4 GEMMs, attention, the o and down
-  // projections' split-K finalize; then the final norm (and lm_head)
-  return any_logits ? (unsigned)(11 * L + 1) : (unsigned)(11 * (L - 1) + 2);
+  // per layer: 4 quantisation phases, 4 GEMMs, the two attention phases, the
+  // o and down projections' split-K finalize; then the final norm (and
+  // lm_head)
+  return any_logits ? (unsigned)(12 * L + 1) : (unsigned)(12 * (L - 1) + 2);
 }
 
 template <int QT>
@@ -441,6 +446,8 @@ __device__ void step_b_body(const Ctx &c, const BatchedW *bw, uint32_t tmem, int
     if (!sync()) return;
     phase_attn(&c, l, kv_only, 1, smem);
     if (kv_only) return;
+    if (!sync()) return;
+    phase_attn_values(&c, l, smem);
     if (!sync()) return;
     phase_quant_b(&c, bw, c.head, c.QH * c.D, 0, c.QH * c.D, PRO_PLAIN, nullptr, nullptr, smem);
     if (!sync()) return;
@@ -691,7 +698,7 @@ size_t smem_bytes(const ocrvl_model_desc &d, int qtype) {
   int nmax = std::max(std::max(d.hidden_size, d.intermediate_size), d.num_heads * d.head_dim);
   size_t g1 = gemv_smem_total(qtype, 1, nmax, kStagesM1);
   size_t gb = gemv_smem_total(qtype, kMaxBatch, nmax, kStagesMB);
-  size_t attn = std::max(attn_smem_floats() * 4, rg_smem_bytes_multi());
+  size_t attn = std::max(attn_smem_floats() * 4, ax_smem_bytes_multi());
   size_t bgemm = qtype == QT_Q8 ? 0 : gemm_b_smem_bytes();
   return std::max(std::max(std::max(g1, gb), attn), bgemm) + 64 + kSmemAlignSlack;
 }
@@ -730,9 +737,6 @@ void setup_batched(ocrvl_model *m) {
     return;
   }
   PfnEncodeTiled enc = (PfnEncodeTiled)fn;
-  // every (sequence, kv head) pair of a 64-sequence step must fit the
-  // attention phase's merge list
-  if (kMaxSeqs * m->desc.num_kv_heads > kRgMerges) return;
   const int L = m->desc.num_layers;
   std::vector<TmapBytes> maps((size_t)L * 5 + 1);
   for (int l = 0; l < L; l++) {
@@ -836,7 +840,6 @@ void reset_after_timeout(ocrvl_model *m) {
   int zero = 0;
   cudaMemcpy(m->ctx.err, &zero, 4, cudaMemcpyHostToDevice);
   cudaMemset(m->ctx.bar_count, 0, 4);
-  cudaMemset(m->ctx.attn_count, 0, (size_t)2 * kMaxSeqs * m->ctx.KVH * 4);
   cudaMemset(m->ctx.lm_count, 0, 4);
   cudaMemset(m->ctx.argkey, 0, kMaxSeqs * 8);
   m->bar_base = 0;
@@ -867,8 +870,7 @@ int ocrvl_init(int device, const ocrvl_model_desc *desc, ocrvl_model **out) {
   if (d.head_dim != kHeadDim) return fail(OCRVL_E_INVALID, "head_dim must be 128");
   if (d.num_heads % d.num_kv_heads != 0 || d.num_heads / d.num_kv_heads > 8)
     return fail(OCRVL_E_INVALID, "num_heads must be 1..8 x num_kv_heads");
-  if (kMaxBatch * d.num_kv_heads > kRgMerges)
-    return fail(OCRVL_E_INVALID, "num_kv_heads must be at most 16");
+  if (d.num_kv_heads > 16) return fail(OCRVL_E_INVALID, "num_kv_heads must be at most 16");
   int qrows = d.num_heads * d.head_dim;
   if (d.hidden_size % 128 || d.intermediate_size % 128 || qrows % 128)
     return fail(OCRVL_E_INVALID, "hidden, intermediate and heads*head_dim must be multiples of 128");
@@ -1034,6 +1036,7 @@ int ocrvl_finalize(ocrvl_model *m) {
   c.V = d.vocab_size;
   c.eps = d.rms_norm_eps;
   c.attn_scale = (float)(1.0 / std::sqrt((double)d.head_dim));
+  c.fzero = 0.0f;
   c.embed = m->embed;
   c.final_norm = m->final_norm;
   c.layers = m->layers_d;
@@ -1052,23 +1055,19 @@ int ocrvl_finalize(ocrvl_model *m) {
   c.qkv = m->dalloc<float>(B * qkvld);
   c.head = m->dalloc<float>(B * c.QH * c.D);
   c.g = m->dalloc<float>(B * c.I);
-  // attention chunk partials, one slot per item: a step has at most one item
-  // per (kv head, KV page), i.e. kv_heads * pages of the pool
-  const size_t max_items = (size_t)c.KVH * m->num_pages + (size_t)2 * kMaxSeqs * c.KVH;
-  const size_t G = (size_t)(c.QH / c.KVH);
-  c.part_o = m->dalloc<float>(max_items * G * c.D);
-  c.part_ml = m->dalloc<float>(max_items * G * 2);
-  c.part_t = m->dalloc<float>(B * c.QH * (size_t)c.D);
+  // long-cache attention scores: every position of a step's caches lies in a
+  // page of the pool (the new position's page is taken before the step)
+  // (rows padded to 4 floats: at most 3 more per (sequence, head))
+  c.att_s = m->dalloc<float>(((size_t)m->num_pages * kPageTokens + 4 * kMaxSeqs) * c.QH);
   c.logits = m->dalloc<float>(B * (size_t)c.V);
   c.argkey = m->dalloc<unsigned long long>(B);
   c.tok_out = m->dalloc<int>(B + 1);
-  c.bar_count = m->dalloc<unsigned>(2 + 2 * B * c.KVH);
+  c.bar_count = m->dalloc<unsigned>(2);
   c.lm_count = c.bar_count + 1;
-  c.attn_count = c.bar_count + 2;
   c.hist_pos = m->dalloc<int>(1);
   if (!c.hist_pos) return fail(OCRVL_E_NOMEM, "history counter");
   StepParams *spd = m->dalloc<StepParams>(1);
-  if (!c.h || !c.vbuf || !c.qkv || !c.head || !c.g || !c.part_o || !c.part_ml || !c.part_t || !c.logits || !c.argkey ||
+  if (!c.h || !c.vbuf || !c.qkv || !c.head || !c.g || !c.att_s || !c.logits || !c.argkey ||
       !c.tok_out || !c.bar_count || !spd)
     return fail(OCRVL_E_NOMEM, "work buffer allocation failed");
   c.err = c.tok_out + B;
@@ -1078,12 +1077,13 @@ int ocrvl_finalize(ocrvl_model *m) {
   c.pro_cols = std::max(std::max(d.hidden_size, d.intermediate_size), d.num_heads * d.head_dim);
   CK(cudaMemset(c.argkey, 0, B * 8));
   CK(cudaMemset(c.tok_out, 0, (B + 1) * 4));
-  CK(cudaMemset(c.bar_count, 0, (2 + 2 * B * c.KVH) * 4));
+  CK(cudaMemset(c.bar_count, 0, 2 * 4));
   CK(cudaHostAlloc((void **)&m->sp_h, sizeof(StepParams), cudaHostAllocDefault));
   CK(cudaHostAlloc((void **)&m->out_h, (B + 1) * 4, cudaHostAllocDefault));
   CK(cudaHostAlloc((void **)&m->bt_stage, B * 4, cudaHostAllocDefault));
   // launch geometry
   m->smem = smem_bytes(d, m->qtype);
+  c.dyn_smem = (int)(m->smem - kSmemAlignSlack - 64);
   CK(cudaDeviceGetAttribute(&m->sms, cudaDevAttrMultiProcessorCount, m->device));
   {
     int rc = m->qtype == QT_Q4 ? set_kernel_attrs<QT_Q4>(m)
@@ -1116,6 +1116,29 @@ int ocrvl_trace_read(ocrvl_model *m, uint64_t *out, int cap) {
   CK(cudaMemcpy(out, m->ctx.trace, (size_t)n * 8, cudaMemcpyDeviceToHost));
   CK(cudaMemset(m->ctx.trace, 0, kTraceWords * 8));
   return n;
+}
+
+int ocrvl_debug_read(ocrvl_model *m, int which, float *out, int64_t count) {
+  if (!m || !out || count < 0) return fail(OCRVL_E_INVALID, "bad arguments");
+  std::lock_guard<std::mutex> lk(m->mu);
+  if (!m->finalized) return fail(OCRVL_E_INVALID, "model not finalized");
+  if (int rc = set_device(m)) return rc;
+  const Ctx &c = m->ctx;
+  const float *src = nullptr;
+  int64_t n = 0;
+  switch (which) {
+    case 0: src = c.h; n = (int64_t)kMaxSeqs * c.H; break;
+    case 1: src = c.vbuf; n = (int64_t)kMaxSeqs * c.H; break;
+    case 2: src = c.qkv; n = (int64_t)kMaxSeqs * (c.QH + 2 * c.KVH) * c.D; break;
+    case 3: src = c.head; n = (int64_t)kMaxSeqs * c.QH * c.D; break;
+    case 4: src = c.g; n = (int64_t)kMaxSeqs * c.I; break;
+    case 5: src = c.att_s; n = ((int64_t)m->num_pages * kPageTokens + 4 * kMaxSeqs) * c.QH; break;
+    default: return fail(OCRVL_E_INVALID, "which must be 0..5");
+  }
+  n = std::min(n, count);
+  CK(cudaStreamSynchronize(m->stream));
+  CK(cudaMemcpy(out, src, (size_t)n * 4, cudaMemcpyDeviceToHost));
+  return (int)n;
 }
 
 void ocrvl_free(ocrvl_model *m) {

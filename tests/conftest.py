@@ -16,7 +16,9 @@ def pytest_configure(config):
 
 @pytest.fixture(scope="session")
 def tiny_models():
-    """Seeded tiny decoders (same head geometry as the benchmark model) in q8/q6/q4."""
+    """Seeded tiny decoders in q8/q6/q4: head_dim 128 like the benchmark model,
+    but 4 q heads over 2 kv heads (GQA group 2; the benchmark model has group 8,
+    covered by tests/test_gpu_bench_shapes.py)."""
     from rapidocrvl_b200 import synth
 
     return {q: synth.ensure("tiny", q) for q in ("q8", "q6", "q4")}
