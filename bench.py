@@ -1,16 +1,33 @@
-"""Decode-step benchmark (Q4, batch 1, 512-token
-prompt, 256 greedy new tokens, context 512 -> 768).
+"""Decode-step benchmark of the B200 engine against BASELINE.json's metric
+("decode tokens/s (bs=1 and bs=64, Q4/Q8) and quant-GEMV HBM GB/s").
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl cuda|reference]
 
-A step is one greedy decode token.  ``value`` is device-timed (CUDA events on
-the engine's stream around K steps of the device-fed decode loop, inputs
-resident in HBM); ``e2e`` times the same K-token workload through the
+One JSON line.  Its headline (``value``, ``e2e``, ``roofline``,
+``cpu_baseline``) is configs[1]: the Q4 decoder, batch 1, a 512-token prompt
+and K greedy decode tokens (a step is one token).  ``value`` is device-timed
+(CUDA events on the engine's stream around K steps of the device-fed decode
+loop, inputs resident in HBM); ``e2e`` times the same K tokens through the
 reference-facing C ABI (ocrvl_step with host buffers: token in, token out,
-one call per token).  Under torchrun each rank decodes its own request on its
-own GPU (request-parallel replicas, no collective on the data path); the
-reported time is the max over ranks.  ``--impl reference`` times the CPU
-restatement of the reference's decode path on the host cores instead.
+one call per token).  Under torchrun each rank decodes its own configs[1]
+request on its own GPU (request-parallel replicas, no collective on the data
+path); the reported time is the max over ranks.
+
+Further keys of the same line carry the metric's other configurations, each
+with its own ms_per_step, roofline and e2e:
+  configs0  Q8, batch 1, 32-token prompt, 64 new tokens (1 GPU runs only);
+  configs3  Q4, 64 sequences with contexts U[256, 4096] (seed 2), 128 steps
+            of one token per sequence (1 GPU runs only);
+  configs4  Q8, 512 requests with prompts U[1024, 8192] (seed 3) and 256 new
+            tokens each, partitioned over the N GPUs (no collective), each GPU
+            running a continuous batch of up to 64 live sequences; value =
+            all requests' tokens / max over ranks of the summed step times.
+Prompt caches of configs3 and configs4 are seeded synthetic K/V written on the
+device (the decode time does not depend on the cached values; the reference
+prefills token by token, untimed here).
+
+``--impl reference`` times the CPU restatement of the reference's decode path
+(oracle/, all host threads) on configs[1] instead.
 """
 from __future__ import annotations
 
@@ -39,12 +56,10 @@ def parse():
     ap.add_argument("--impl", default="cuda", choices=["cuda", "reference"])
     ap.add_argument("--quant", default="q4", choices=["q4", "q6", "q8"])
     ap.add_argument("--prompt", type=int, default=PROMPT)
-    ap.add_argument("--workload", default="configs1", choices=["configs1", "configs3"],
-                    help="configs1: batch 1, 512-token prompt (headline); configs3: 64 sequences, contexts U[256, 4096]")
-    ap.add_argument("--ctx-hi", type=int, default=4096,
-                    help="configs3: contexts drawn U[256, ctx_hi] (4096 is the workload; smaller for profiling captures)")
-    ap.add_argument("--kv", default="prefill", choices=["prefill", "synthetic"],
-                    help="configs3 caches: prompt prefill through steps, or seeded K/V imported directly")
+    ap.add_argument("--workload", default="all", choices=["all", "configs1", "configs0", "configs3", "configs4"],
+                    help="all: configs1 headline plus the other configurations' keys; otherwise one of them alone")
+    ap.add_argument("--ctx-hi", type=int, default=4096, help="configs3: contexts U[256, ctx_hi] (profiling: smaller)")
+    ap.add_argument("--requests", type=int, default=512, help="configs4: requests over all GPUs")
     return ap.parse_args()
 
 
@@ -52,11 +67,22 @@ def dist_env():
     return int(os.environ.get("RANK", 0)), int(os.environ.get("WORLD_SIZE", 1)), int(os.environ.get("LOCAL_RANK", 0))
 
 
+def host_threads() -> int:
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
+def model_desc(cfg):
+    return (f"hidden {cfg.hidden_size}, {cfg.num_hidden_layers} layers, {cfg.num_attention_heads}q/"
+            f"{cfg.num_key_value_heads}kv heads, head_dim {cfg.head_dim}, SwiGLU {cfg.intermediate_size}, "
+            f"vocab {cfg.vocab_size}")
+
+
 def workload_config(args, cfg):
     return {
-        "workload": f"configs[1]: {args.quant.upper()} decoder (hidden {cfg.hidden_size}, {cfg.num_hidden_layers} layers, "
-                    f"{cfg.num_attention_heads}q/{cfg.num_key_value_heads}kv heads, head_dim {cfg.head_dim}, "
-                    f"SwiGLU {cfg.intermediate_size}, vocab {cfg.vocab_size}), batch 1 per GPU, {args.prompt}-token "
+        "workload": f"configs[1]: {args.quant.upper()} decoder ({model_desc(cfg)}), batch 1 per GPU, {args.prompt}-token "
                     f"prompt, {args.warmup}+{args.steps} greedy decode tokens",
         "quant": args.quant,
         "batch_per_gpu": 1,
@@ -68,9 +94,9 @@ def workload_config(args, cfg):
 
 
 def algorithmic_bytes(model_dir, quant, cfg):
-    """Weight bytes streamed per token: rows*(packed row + f32
-    scale) for every quantized matrix incl. lm_head, the 2L+1 f32 norm
-    vectors and one f32 embedding row."""
+    """Bytes one decode token streams: rows * (packed row + f32 scale) of every
+    quantized matrix incl. lm_head, the 2L+1 f32 norm vectors and one f32
+    embedding row; plus K and V (f32, every layer) per attended position."""
     from rapidocrvl_b200 import gguf
 
     g = gguf.GGUFFile(os.path.join(model_dir, f"model-{quant}.gguf"))
@@ -83,6 +109,21 @@ def algorithmic_bytes(model_dir, quant, cfg):
     w += cfg.hidden_size * 4  # embedding row
     kv_tok = cfg.num_hidden_layers * 2 * cfg.num_key_value_heads * cfg.head_dim * 4
     return w, kv_tok
+
+
+def hbm_peak():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            return float(json.load(f)["hbm_gbs"]), "measured (MEASURED_PEAKS.json hbm_gbs)"
+    return 6650.0, "fallback"
+
+
+def roofline(bytes_per_step, ms_per_step, kernel):
+    peak, src = hbm_peak()
+    achieved = bytes_per_step / (ms_per_step / 1e3) / 1e9
+    return {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+            "peak_source": src, "kernel": kernel, "algorithmic_bytes_per_step": bytes_per_step, "traffic": None}
 
 
 class ClockSampler:
@@ -137,13 +178,27 @@ class ClockSampler:
                 "reasons": reasons, "samples": len(self.rows)}
 
 
-def cpu_reference_decode(model_dir, quant, cfg, prompt, steps, warmup, seed_kv=None, budget_s=None):
+def visible_bus_ids(local):
+    try:
+        r = subprocess.run(["nvidia-smi", "--query-gpu=pci.bus_id", "--format=csv,noheader"], capture_output=True,
+                           text=True, timeout=20)
+        allb = [x.strip() for x in r.stdout.splitlines() if x.strip()]
+        vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+        idx = [int(v) for v in vis.split(",")] if vis else list(range(len(allb)))
+        return [allb[idx[local]]] if local < len(idx) and idx[local] < len(allb) else allb[:1]
+    except Exception:
+        return []
+
+
+# ---- CPU baseline (the oracle: C++ restatement of the reference CPU path) ---
+def cpu_reference_decode(model_dir, quant, cfg, prompt, steps, warmup, budget_s=None):
     """Times the CPU restatement of the reference decode path (oracle/) on all
-    host threads.  With seed_kv (GPU prefill K/V) the prompt is not recomputed."""
+    host threads (set explicitly: torchrun sets OMP_NUM_THREADS=1 for its
+    workers).  Returns (steps, seconds, prefill seconds, threads)."""
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
-    import numpy as np
     import pyoracle
 
+    threads = pyoracle.set_threads(host_threads())
     om = pyoracle.OracleModel(os.path.join(model_dir, f"model-{quant}.gguf"), cfg)
     seq = om.new_seq(len(prompt) + warmup + steps + 8)
     t_pre = time.time()
@@ -164,7 +219,7 @@ def cpu_reference_decode(model_dir, quant, cfg, prompt, steps, warmup, seed_kv=N
     seq.decode_steps(tok, pos, steps)
     dt = time.time() - t0
     om.close()
-    return steps, dt, t_pre
+    return steps, dt, t_pre, threads
 
 
 def run_reference(args):
@@ -176,50 +231,44 @@ def run_reference(args):
     d = synth.ensure("bench", args.quant)
     cfg = config.load(d)
     prompt = synth.random_prompt(args.prompt, cfg.vocab_size, 0)
-    steps, dt, t_pre = cpu_reference_decode(d, args.quant, cfg, prompt, args.steps, args.warmup)
+    steps, dt, t_pre, threads = cpu_reference_decode(d, args.quant, cfg, prompt, args.steps, args.warmup)
     v = steps / dt
-    cores = os.cpu_count()
     line = {
         "impl": "reference", "metric": METRIC, "value": v, "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": 1e3 * dt / steps, "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "i8/f32", "data": "synthetic (seeded N(0,0.02) BF16 weights -> GGUF; uniform prompt ids)",
+        "vs_baseline": None, "dtype": "i8/f32",
+        "data": "synthetic (seeded N(0,0.02) BF16 weights -> GGUF; uniform prompt ids)",
         "config": workload_config(args, cfg),
-        "cpu_baseline": {"value": v, "unit": UNIT, "cores": cores, "kind": "port",
+        "cpu_baseline": {"value": v, "unit": UNIT, "cores": threads, "kind": "port",
                          "sample": f"{steps} greedy decode steps at context {args.prompt + args.warmup}+ after a "
                                    f"{args.prompt}-token CPU prefill ({t_pre:.1f} s, untimed); C++ restatement of the "
-                                   f"reference Go CPU path (no Go toolchain on this image), all host threads"},
+                                   f"reference Go CPU path (no Go toolchain on this image), {threads} OpenMP threads"},
         "e2e": {"value": v, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
     return 0
 
 
-def run_cuda(args):
-    import numpy as np
+# ---- GPU workloads -----------------------------------------------------------
+def events():
     import torch
 
-    rank, world, local = dist_env()
-    torch.cuda.set_device(local)
-    pg = None
-    if world > 1:
-        import datetime
+    return torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
 
-        import torch.distributed as dist
 
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600))
-        pg = dist
+def bs1_workload(quant, prompt_len, steps, warmup, rank, device, label, clocks_for=None):
+    """Batch-1 greedy decode: device-fed loop (value) and one C-ABI call per
+    token with host buffers (e2e)."""
+    import torch
+
     from rapidocrvl_b200 import LoadOptions, Runtime, config, synth
 
-    if rank == 0:
-        d = synth.ensure("bench", args.quant)
-    if pg:
-        pg.barrier()
-    d = synth.ensure("bench", args.quant)
+    d = synth.ensure("bench", quant)
     cfg = config.load(d)
-    total = args.prompt + args.warmup + 2 * args.steps + 8
-    rt = Runtime.load(d, LoadOptions(quantization=args.quant, device=local, max_position=max(4096, total),
+    total = prompt_len + warmup + 2 * steps + 8
+    rt = Runtime.load(d, LoadOptions(quantization=quant, device=device, max_position=max(4096, total),
                                      kv_pool_bytes=2 << 30))
-    prompt = synth.random_prompt(args.prompt, cfg.vocab_size, rank)
+    prompt = synth.random_prompt(prompt_len, cfg.vocab_size, rank)
 
     def prefill():
         s = rt.new_sequence(total)
@@ -232,95 +281,270 @@ def run_cuda(args):
     seq_dev, tok_dev = prefill()
     seq_e2e, tok_e2e = prefill()
     stream = torch.cuda.ExternalStream(rt.stream_handle)
-    # warm-up (device loop and host-call path)
-    out = rt.decode_device([seq_dev], [tok_dev], args.warmup)
+    out = rt.decode_device([seq_dev], [tok_dev], warmup)
     tok_dev = int(out[-1, 0])
-    for _ in range(args.warmup):
+    for _ in range(warmup):
         ids, _ = rt.step([seq_e2e], ids=[tok_e2e])
         tok_e2e = int(ids[0])
-    bus_ids = []
-    try:
-        r = subprocess.run(["nvidia-smi", "--query-gpu=pci.bus_id", "--format=csv,noheader"], capture_output=True,
-                           text=True, timeout=20)
-        allb = [x.strip() for x in r.stdout.splitlines() if x.strip()]
-        vis = os.environ.get("CUDA_VISIBLE_DEVICES")
-        idx = [int(v) for v in vis.split(",")] if vis else list(range(len(allb)))
-        bus_ids = [allb[idx[local]]] if local < len(idx) and idx[local] < len(allb) else allb[:1]
-    except Exception:
-        bus_ids = []
-    # ---- device-timed value ----
-    if pg:
-        pg.barrier()
     torch.cuda.synchronize()
-    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(bus_ids) as clocks:
+    res = {}
+    ev0, ev1 = events()
+    sampler = ClockSampler(clocks_for) if clocks_for is not None else None
+    if sampler:
+        sampler.__enter__()
+    try:
         ev0.record(stream)
-        out = rt.decode_device([seq_dev], [tok_dev], args.steps)
+        rt.decode_device([seq_dev], [tok_dev], steps)
         ev1.record(stream)
         torch.cuda.synchronize()
         ms = ev0.elapsed_time(ev1)
-        # ---- e2e through the C ABI, host buffers, one call per token ----
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0, e1 = events()
         e0.record(stream)
-        for _ in range(args.steps):
+        for _ in range(steps):
             ids, _ = rt.step([seq_e2e], ids=[tok_e2e])
             tok_e2e = int(ids[0])
         e1.record(stream)
         torch.cuda.synchronize()
         ms_e2e = e0.elapsed_time(e1)
-    if pg:
-        t = torch.tensor([ms, ms_e2e], device="cuda")
-        pg.all_reduce(t, op=pg.ReduceOp.MAX)
-        ms, ms_e2e = float(t[0]), float(t[1])
-        pg.barrier()
-    w_bytes, kv_tok = algorithmic_bytes(d, args.quant, cfg)
-    ctx0 = args.prompt + args.warmup
-    # step i attends ctx0+i+1 positions and appends one
-    kv_read = sum((ctx0 + i + 1) * kv_tok for i in range(args.steps))
-    bytes_per_step = w_bytes + (kv_read + args.steps * kv_tok) / args.steps
-    step_s = ms / 1e3 / args.steps
-    peaks_path = os.path.join(ROOT, "MEASURED_PEAKS.json")
-    peak, peak_src = 6650.0, "fallback"
-    if os.path.exists(peaks_path):
-        with open(peaks_path) as f:
-            peak, peak_src = float(json.load(f)["hbm_gbs"]), "measured"
-    achieved = bytes_per_step / step_s / 1e9
-    h2d, d2h = rt.step_io_bytes(1)
-    value = world * args.steps / (ms / 1e3)
-    line = {
-        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-        "dtype": "i8/f32" if args.quant != "q8" else "f32",
-        "data": "synthetic (seeded N(0,0.02) BF16 weights converted to GGUF; uniform random prompt ids)",
-        "config": workload_config(args, cfg),
-        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
-                     "peak_source": f"{peak_src} (MEASURED_PEAKS.json hbm_gbs)" if peak_src == "measured" else "fallback",
-                     "kernel": "k_step (one persistent launch per token)",
-                     "algorithmic_bytes_per_step": bytes_per_step, "traffic": None},
-        "e2e": {"value": world * args.steps / (ms_e2e / 1e3), "unit": UNIT, "h2d_bytes_per_step": h2d,
-                "d2h_bytes_per_step": d2h},
-        "gpu_launches": args.steps,
-        "clocks": clocks.summary(),
-    }
-    traffic_path = os.path.join(ROOT, "profiles", "k_step_traffic.json")
-    if os.path.exists(traffic_path):
-        with open(traffic_path) as f:
-            tj = json.load(f)
-        if tj.get("quant") == args.quant:
-            # one ncu capture at a fixed context, moved to this run's mean
-            # context by the K/V bytes per position (traffic grows with it)
-            mean_ctx = ctx0 + (args.steps + 1) / 2
-            line["roofline"]["traffic"] = (tj["dram_bytes_per_step"]
-                                           + (mean_ctx - tj["context"]) * tj["kv_bytes_per_position"])
-            line["roofline"]["traffic_source"] = tj.get("source")
-    if rank == 0 and world == 1 and os.environ.get("OCRVL_BENCH_NO_CPU") is None:
-        steps, dt, t_pre = cpu_reference_decode(d, args.quant, cfg, prompt, args.steps, 0, budget_s=15.0)
-        line["cpu_baseline"] = {
-            "value": steps / dt, "unit": UNIT, "cores": os.cpu_count(), "kind": "port",
-            "sample": f"{steps} greedy decode steps at context {args.prompt}+ after a {args.prompt}-token CPU "
-                      f"prefill ({t_pre:.1f} s, untimed); C++ restatement of the reference Go CPU path, all host "
-                      f"threads (OpenMP)"}
+    finally:
+        if sampler:
+            sampler.__exit__()
+    w_bytes, kv_tok = algorithmic_bytes(d, quant, cfg)
+    ctx0 = prompt_len + warmup
+    kv = sum((ctx0 + i + 1) * kv_tok for i in range(steps)) + steps * kv_tok  # read + append
+    res["bytes_per_step"] = w_bytes + kv / steps
+    res["ms"], res["ms_e2e"] = ms, ms_e2e
+    res["io"] = rt.step_io_bytes(1)
+    res["clocks"] = sampler.summary() if sampler else None
+    res["cfg"] = cfg
+    res["dir"] = d
+    res["prompt"] = prompt
     rt.close()
+    return res
+
+
+def batched_workload(quant, n, ctx_hi, steps, warmup, rank, device):
+    """configs3: n sequences with contexts U[256, ctx_hi] (seed 2), seeded
+    synthetic caches, one token per sequence per step; value through the
+    device-fed loop, e2e through ocrvl_step with host buffers."""
+    import numpy as np
+    import torch
+
+    from rapidocrvl_b200 import LoadOptions, Runtime, config, synth
+
+    d = synth.ensure("bench", quant)
+    cfg = config.load(d)
+    rng = np.random.default_rng(2 + rank)
+    lens = rng.integers(256, ctx_hi + 1, size=n).tolist()
+    total_new = warmup + 2 * steps + 2
+    _, kv_tok = algorithmic_bytes(d, quant, cfg)
+    rt = Runtime.load(d, LoadOptions(quantization=quant, device=device, max_position=ctx_hi + total_new + 64,
+                                     kv_pool_bytes=int(sum(lens) + n * (total_new + 32)) * kv_tok + (256 << 20)))
+    seqs = [rt.new_sequence(L + total_new + 8) for L in lens]
+    t0 = time.time()
+    for j, L in enumerate(lens):
+        seqs[j].fill_synthetic(L, 1000 * rank + j)
+    t_setup = time.time() - t0
+    first = [int(t) for t in rng.integers(0, cfg.vocab_size, size=n)]
+    out = rt.decode_device(seqs, first, warmup)
+    toks = [int(i) for i in out[-1]]
+    stream = torch.cuda.ExternalStream(rt.stream_handle)
+    torch.cuda.synchronize()
+    ev0, ev1 = events()
+    ev0.record(stream)
+    out = rt.decode_device(seqs, toks, steps)
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    ms = ev0.elapsed_time(ev1)
+    toks = [int(i) for i in out[-1]]
+    e0, e1 = events()
+    e0.record(stream)
+    for _ in range(steps):
+        ids, _ = rt.step(seqs, ids=toks)
+        toks = [int(i) for i in ids]
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms_e2e = e0.elapsed_time(e1)
+    w_bytes, kv_tok = algorithmic_bytes(d, quant, cfg)
+    ctx0 = [L + warmup for L in lens]
+    kv = sum(sum((c + i + 1) * kv_tok for c in ctx0) for i in range(steps)) + steps * n * kv_tok
+    res = {"ms": ms, "ms_e2e": ms_e2e, "bytes_per_step": w_bytes + kv / steps, "io": rt.step_io_bytes(n),
+           "setup_s": t_setup, "mean_context": float(np.mean(ctx0)) + steps / 2, "cfg": cfg}
+    rt.close()
+    return res
+
+
+def sweep_workload(n_requests, rank, world, device, new_tokens=256, max_live=64):
+    """configs4: Q8, n_requests requests (prompts U[1024, 8192], seed 3),
+    new_tokens greedy tokens each, partitioned over the ranks by predicted KV
+    bytes; each rank runs a continuous batch of up to max_live sequences."""
+    import numpy as np
+    import torch
+
+    from rapidocrvl_b200 import LoadOptions, Runtime, config, partition, scheduler, synth
+
+    d = synth.ensure("bench", "q8")
+    cfg = config.load(d)
+    rng = np.random.default_rng(3)
+    prompts = rng.integers(1024, 8193, size=n_requests).tolist()
+    firsts = rng.integers(0, cfg.vocab_size, size=n_requests).tolist()
+    costs = [partition.request_cost(cfg, p, new_tokens) for p in prompts]
+    mine = partition.shard(costs, rank, world)
+    w_bytes, kv_tok = algorithmic_bytes(d, "q8", cfg)
+    # live sequences at their longest, plus a margin for the one joining
+    live_peak = sorted((prompts[i] + new_tokens + 16 for i in mine), reverse=True)[:max_live + 1]
+    rt = Runtime.load(d, LoadOptions(quantization="q8", device=device, max_position=8192 + new_tokens + 64,
+                                     kv_pool_bytes=int(sum(live_peak) * kv_tok) + (512 << 20)))
+    reqs = [scheduler.Request(i, prompts[i], new_tokens, int(firsts[i])) for i in mine]
+    stream = torch.cuda.ExternalStream(rt.stream_handle)
+    fill_s = [0.0]
+
+    def prefill(seq, r):
+        t0 = time.time()
+        seq.fill_synthetic(r.prompt_tokens, 7919 * r.index + 1)
+        fill_s[0] += time.time() - t0
+
+    stats = scheduler.run(rt, reqs, prefill, max_live=max_live, stream=stream)
+    bytes_total = stats.steps * w_bytes + stats.kv_positions_read * kv_tok + stats.tokens * kv_tok
+    res = {"ms": stats.step_ms, "steps": stats.steps, "tokens": stats.tokens, "requests": len(mine),
+           "bytes_total": bytes_total, "mean_batch": stats.tokens / max(1, stats.steps), "fill_s": fill_s[0],
+           "io": rt.step_io_bytes(min(max_live, max(1, len(mine))))}
+    rt.close()
+    return res
+
+
+def run_cuda(args):
+    import torch
+
+    rank, world, local = dist_env()
+    torch.cuda.set_device(local)
+    pg = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=900))
+        pg = dist
+    from rapidocrvl_b200 import synth
+
+    if rank == 0:
+        for q in ("q4", "q8"):
+            synth.ensure("bench", q)
+    if pg:
+        pg.barrier()
+
+    def max_over_ranks(vals):
+        if not pg:
+            return vals
+        t = torch.tensor(vals, device="cuda", dtype=torch.float64)
+        pg.all_reduce(t, op=pg.ReduceOp.MAX)
+        return [float(x) for x in t]
+
+    def sum_over_ranks(vals):
+        if not pg:
+            return vals
+        t = torch.tensor(vals, device="cuda", dtype=torch.float64)
+        pg.all_reduce(t, op=pg.ReduceOp.SUM)
+        return [float(x) for x in t]
+
+    want = args.workload
+    line = None
+    if want in ("all", "configs1"):
+        if pg:
+            pg.barrier()
+        r = bs1_workload(args.quant, args.prompt, args.steps, args.warmup, rank, local, "configs1",
+                         clocks_for=visible_bus_ids(local))
+        ms, ms_e2e = max_over_ranks([r["ms"], r["ms_e2e"]])
+        cfg = r["cfg"]
+        h2d, d2h = r["io"]
+        line = {
+            "metric": METRIC, "value": world * args.steps / (ms / 1e3), "unit": UNIT, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "i8/f32" if args.quant != "q8" else "f32",
+            "data": "synthetic (seeded N(0,0.02) BF16 weights converted to GGUF; uniform random prompt ids)",
+            "config": workload_config(args, cfg),
+            "roofline": roofline(r["bytes_per_step"], ms / args.steps, "k_step (one persistent launch per token)"),
+            "e2e": {"value": world * args.steps / (ms_e2e / 1e3), "unit": UNIT, "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": d2h},
+            "gpu_launches": 1,
+            "gpu_launches_note": "value: the device-fed loop runs all K steps in one persistent k_step launch; "
+                                 "e2e: one k_step launch per token",
+            "clocks": r["clocks"],
+        }
+        traffic_path = os.path.join(ROOT, "profiles", "k_step_traffic.json")
+        if os.path.exists(traffic_path):
+            with open(traffic_path) as f:
+                tj = json.load(f)
+            if tj.get("quant") == args.quant:
+                # one ncu capture at a fixed context, moved to this run's mean
+                # context by the K/V bytes per position (traffic grows with it)
+                mean_ctx = args.prompt + args.warmup + (args.steps + 1) / 2
+                line["roofline"]["traffic"] = (tj["dram_bytes_per_step"]
+                                               + (mean_ctx - tj["context"]) * tj["kv_bytes_per_position"])
+                line["roofline"]["traffic_source"] = tj.get("source")
+        if rank == 0 and world == 1 and os.environ.get("OCRVL_BENCH_NO_CPU") is None:
+            steps, dt, t_pre, threads = cpu_reference_decode(r["dir"], args.quant, cfg, r["prompt"], args.steps, 0,
+                                                             budget_s=15.0)
+            line["cpu_baseline"] = {
+                "value": steps / dt, "unit": UNIT, "cores": threads, "kind": "port",
+                "sample": f"{steps} greedy decode steps at context {args.prompt}+ after a {args.prompt}-token CPU "
+                          f"prefill ({t_pre:.1f} s, untimed); C++ restatement of the reference Go CPU path, "
+                          f"{threads} OpenMP threads"}
+    extra = {}
+    if world == 1 and want in ("all", "configs0"):
+        r = bs1_workload("q8", 32, 64, 8, rank, local, "configs0")
+        extra["configs0"] = {
+            "workload": "configs[0]: Q8 decoder, batch 1, 32-token prompt, 8+64 greedy decode tokens",
+            "value": 64 / (r["ms"] / 1e3), "unit": UNIT, "ms_per_step": r["ms"] / 64,
+            "roofline": roofline(r["bytes_per_step"], r["ms"] / 64, "k_step (one persistent launch per token)"),
+            "e2e": {"value": 64 / (r["ms_e2e"] / 1e3), "unit": UNIT, "h2d_bytes_per_step": r["io"][0],
+                    "d2h_bytes_per_step": r["io"][1]}}
+    if world == 1 and want in ("all", "configs3"):
+        steps3 = 128 if want == "all" else args.steps
+        warm3 = 4 if want == "all" else args.warmup
+        r = batched_workload("q4", 64, args.ctx_hi, steps3, warm3, rank, local)
+        extra["configs3"] = {
+            "workload": f"configs[3]: Q4 decoder, 64 sequences, contexts U[256,{args.ctx_hi}] (seed 2), 16-token "
+                        f"pages, {warm3}+{steps3} steps of one token per sequence",
+            "value": 64 * steps3 / (r["ms"] / 1e3), "unit": UNIT, "ms_per_step": r["ms"] / steps3,
+            "mean_context": r["mean_context"], "setup_s": round(r["setup_s"], 1),
+            "kv": "seeded synthetic K/V written on the device (ocrvl_seq_fill_synthetic)",
+            "roofline": roofline(r["bytes_per_step"], r["ms"] / steps3, "k_step_b (one persistent launch per step)"),
+            "e2e": {"value": 64 * steps3 / (r["ms_e2e"] / 1e3), "unit": UNIT, "h2d_bytes_per_step": r["io"][0],
+                    "d2h_bytes_per_step": r["io"][1]},
+            "gpu_launches": steps3}
+    if want in ("all", "configs4"):
+        if pg:
+            pg.barrier()
+        r = sweep_workload(args.requests, rank, world, local)
+        ms_max, = max_over_ranks([r["ms"]])
+        tokens, bytes_total = sum_over_ranks([float(r["tokens"]), float(r["bytes_total"])])
+        peak, src = hbm_peak()
+        extra["configs4"] = {
+            "workload": f"configs[4]: Q8 decoder, {args.requests} requests with prompts U[1024, 8192] (seed 3), 256 "
+                        f"greedy tokens each, partitioned over {world} GPU(s) by predicted KV bytes, continuous "
+                        f"batching of up to 64 live sequences per GPU",
+            "value": tokens / (ms_max / 1e3), "unit": UNIT, "n_gpus": world, "scaling": "strong",
+            "ms_max_over_ranks": ms_max, "rank0": {k: r[k] for k in ("steps", "tokens", "requests", "mean_batch")},
+            "prefill": "seeded synthetic K/V written on the device, untimed",
+            "roofline_per_gpu": {"bound": "hbm", "achieved": bytes_total / world / (ms_max / 1e3) / 1e9, "peak": peak,
+                                 "unit": "GB/s", "frac": bytes_total / world / (ms_max / 1e3) / 1e9 / peak,
+                                 "peak_source": src},
+            "e2e": {"value": tokens / (ms_max / 1e3), "unit": UNIT, "h2d_bytes_per_step": r["io"][0],
+                    "d2h_bytes_per_step": r["io"][1],
+                    "note": "every step is a C-ABI ocrvl_step with host ids in and out"}}
+    if line is None:
+        # a single non-headline workload: its object is the line
+        (name, obj), = extra.items()
+        line = {"metric": METRIC, "value": obj["value"], "unit": UNIT, "n_gpus": world, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": obj.get("ms_per_step", obj.get("ms_max_over_ranks")),
+                "higher_is_better": True, "scaling": obj.get("scaling", "weak"), "vs_baseline": None,
+                "dtype": "i8/f32", "data": "synthetic", "config": {"workload": obj["workload"]},
+                "roofline": obj.get("roofline", obj.get("roofline_per_gpu")), "e2e": obj["e2e"],
+                "gpu_launches": obj.get("gpu_launches")}
+    else:
+        line.update(extra)
     if rank == 0:
         print(json.dumps(line), flush=True)
     if pg:
@@ -329,102 +553,10 @@ def run_cuda(args):
     return 0
 
 
-def run_batched(args):
-    """64 sequences, contexts drawn U[256, 4096] (seed 2), one new
-    token per sequence per step; the projections run as int8 tensor-core
-    GEMMs (Q4).  Value = generated tokens/s of the device-fed loop."""
-    import numpy as np
-    import torch
-
-    from rapidocrvl_b200 import LoadOptions, Runtime, config, synth
-
-    rank, world, local = dist_env()
-    torch.cuda.set_device(local)
-    d = synth.ensure("bench", args.quant)
-    cfg = config.load(d)
-    n = 64
-    rng = np.random.default_rng(2 + rank)
-    lens = rng.integers(256, args.ctx_hi + 1, size=n).tolist()
-    total_new = args.warmup + args.steps + 1
-    rt = Runtime.load(d, LoadOptions(quantization=args.quant, device=local, max_position=8192,
-                                     kv_pool_bytes=int(sum(lens) + n * (total_new + 32)) * 36864 + (256 << 20)))
-    seqs = [rt.new_sequence(L + total_new + 8) for L in lens]
-    prompts = [synth.random_prompt(L, cfg.vocab_size, 1000 * rank + j) for j, L in enumerate(lens)]
-    t0 = time.time()
-    if args.kv == "synthetic":
-        # seeded K/V imported straight into the caches (ocrvl_seq_import_kv):
-        # the decode timing does not depend on the cached values, and setting
-        # up takes one call per sequence instead of max(lens) prefill launches
-        kvd = cfg.num_key_value_heads * cfg.head_dim
-        krng = np.random.default_rng(5 + rank)
-        shape = (cfg.num_hidden_layers, max(lens), kvd)
-        kpool = krng.standard_normal(shape, dtype=np.float32)
-        vpool = krng.standard_normal(shape, dtype=np.float32)
-        for j, L in enumerate(lens):  # sequence j: positions j .. j+L-2 of the pools (wrapping)
-            idx = (np.arange(L - 1) + j) % shape[1]
-            seqs[j].import_kv(kpool[:, idx], vpool[:, idx])
-    else:
-        for p in range(max(lens) - 1):
-            live = [j for j in range(n) if p < lens[j] - 1]
-            rt.step([seqs[j] for j in live], ids=[prompts[j][p] for j in live], need_logits=False)
-    ids, _ = rt.step(seqs, ids=[pr[-1] for pr in prompts])
-    t_pre = time.time() - t0
-    first = [int(i) for i in ids]
-    out = rt.decode_device(seqs, first, args.warmup)
-    first = [int(i) for i in out[-1]]
-    stream = torch.cuda.ExternalStream(rt.stream_handle)
-    torch.cuda.synchronize()
-    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    ev0.record(stream)
-    out = rt.decode_device(seqs, first, args.steps)
-    ev1.record(stream)
-    torch.cuda.synchronize()
-    ms = ev0.elapsed_time(ev1)
-    w_bytes, kv_tok = algorithmic_bytes(d, args.quant, cfg)
-    ctx0 = [L + args.warmup for L in lens]
-    kv_read = sum(sum((c + i + 1) * kv_tok for c in ctx0) for i in range(args.steps))
-    bytes_per_step = w_bytes + (kv_read + args.steps * n * kv_tok) / args.steps
-    step_s = ms / 1e3 / args.steps
-    peaks_path = os.path.join(ROOT, "MEASURED_PEAKS.json")
-    peak = 6650.0
-    if os.path.exists(peaks_path):
-        with open(peaks_path) as f:
-            peak = float(json.load(f)["hbm_gbs"])
-    achieved = bytes_per_step / step_s / 1e9
-    line = {
-        "metric": METRIC, "value": n * args.steps / (ms / 1e3), "unit": UNIT, "n_gpus": 1, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "i8/f32", "data": "synthetic (seeded weights; uniform prompt ids)",
-        "config": {"workload": f"configs[3]: {args.quant.upper()}, 64 sequences, contexts U[256,{args.ctx_hi}] (seed 2), "
-                               f"16-token pages, {args.warmup}+{args.steps} steps of one token per sequence",
-                   "kv": "prompt prefill" if args.kv == "prefill" else "seeded N(0,1) K/V imported",
-                   "setup_s": round(t_pre, 1), "mean_context": float(np.mean(ctx0)) + args.steps / 2,
-                   "l2": "no flush: per-step KV (~5.6 GB) + weights > 126 MB L2"},
-        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
-                     "kernel": "k_step_b (one persistent launch per step)",
-                     "algorithmic_bytes_per_step": bytes_per_step, "traffic": None},
-        "gpu_launches": args.steps,
-    }
-    traffic_path = os.path.join(ROOT, "profiles", "k_step_b_traffic.json")
-    if os.path.exists(traffic_path):
-        with open(traffic_path) as f:
-            tj = json.load(f)
-        if tj.get("quant") == args.quant:
-            # one ncu capture of a smaller case, scaled by the algorithmic bytes
-            # (the K/V stream dominates both)
-            line["roofline"]["traffic"] = tj["dram_bytes_per_step"] * bytes_per_step / tj["algorithmic_bytes_per_step"]
-            line["roofline"]["traffic_source"] = tj.get("source") + ", scaled by algorithmic bytes"
-    rt.close()
-    print(json.dumps(line), flush=True)
-    return 0
-
-
 def main():
     args = parse()
     if args.impl == "reference":
         return run_reference(args)
-    if args.workload == "configs3":
-        return run_batched(args)
     return run_cuda(args)
 
 

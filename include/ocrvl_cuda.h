@@ -132,6 +132,14 @@ int ocrvl_seq_read_kv(ocrvl_seq *s, int layer, float *k, float *v);
  * error) leaves it empty. */
 int ocrvl_seq_import_kv(ocrvl_seq *s, int n, const float *k, const float *v);
 
+/* Sets the sequence's cache to n positions of seeded pseudo-random K and V
+ * generated on the device (K uniform in [-0.5, 0.5), V in [-1, 1), a hash of
+ * seed, position, layer, kv head and dim) and its length to n.  No reference
+ * counterpart: it stands in for a prompt's prefill when only the decode steps
+ * after it are measured (long-prompt benchmarks), without a host copy of the
+ * cache.  Errors leave the sequence empty. */
+int ocrvl_seq_fill_synthetic(ocrvl_seq *s, int n, uint64_t seed);
+
 /* One decode step for n sequences (1 <= n <= 64) of the same model: the
  * batched form of Runtime.forwardEmbeddingForSampling
  * (internal/model/model.go:3475-3643).  Every sequence is validated before

@@ -63,6 +63,7 @@ SIGNATURES = {
     "ocrvl_seq_len": (I, [P]),
     "ocrvl_seq_read_kv": (I, [P, I, P, P]),
     "ocrvl_seq_import_kv": (I, [P, I, P, P]),
+    "ocrvl_seq_fill_synthetic": (I, [P, I, C.c_uint64]),
     "ocrvl_step": (I, [P, P, I, P, P, P, I, P, P]),
     "ocrvl_generate_greedy": (I, [P, P, I, I, P, I, P, I, C.POINTER(I)]),
     "ocrvl_decode_greedy_device": (I, [P, P, I, P, I, P]),

@@ -36,8 +36,10 @@ namespace ocrvl {
 constexpr int kAxTok = 32;                            // positions per score chunk (two pages)
 constexpr int kAxKBufs = 4;                           // K chunk buffers per block
 constexpr int kAxKBytes = kAxTok * kHeadDim * 4;      // K rows of one chunk: 16 KB
+constexpr int kAxVRing = 8;                           // value-step buffers in flight
 constexpr int kAxVTok = 32;                           // positions per value step
 constexpr int kAxVBytes = kAxVTok * (kHeadDim / 2) * 4;  // half-dim V rows of one step: 8 KB
+constexpr int kAxVRingBytes = kAxVRing * kAxVBytes;
 static_assert(2 * kAxKBytes == kStageBytes, "two K chunks per ring slot");
 static_assert(kMaxGroup == 8 && kHeadDim == 128, "score layout: 8 heads x 2 tokens per half-warp");
 
@@ -75,8 +77,13 @@ __device__ __forceinline__ float *ax_small(const Ctx &c, int M, float *smem) {
 // first) and the short ones (in order); this block's chunk range.
 __shared__ int s_ax_n[kMaxSeqs], s_ax_cb[kMaxSeqs + 1], s_ax_sb[kMaxSeqs];
 __shared__ int s_ax_nl, s_ax_long[kMaxSeqs];
+__shared__ int s_ax_hg;  // head groups per value item (the longest cache's scores of G / hg heads fit shared memory)
 __shared__ int s_ex_n, s_ex_m[kMaxSeqs];
 __shared__ int s_ax_lo, s_ax_hi;
+// Pool pages of the block's first kAxPgCap chunks (the second -1 when the
+// chunk has one page), so a refill needs no block-table load.
+constexpr int kAxPgCap = 256;
+__shared__ int2 s_ax_pg[kAxPgCap];
 
 // Per-block state of the K chunk loads, kept across the phases of a launch:
 // s_ax_full[j] completes when buffer j's copies land, s_ax_par bit j is the
@@ -101,6 +108,26 @@ __device__ __forceinline__ void ax_block_init() {
 __host__ __device__ __forceinline__ int ax_stride(int n) { return (n + 3) & ~3; }
 
 __device__ __forceinline__ int ax_bound(int P, int b, int nb) { return (int)(((long long)P * b + nb - 1) / nb); }
+
+// Chunk ci of the step: its sequence, kv head and first position.
+struct AxChunk {
+  int m, g, t0;
+};
+__device__ __forceinline__ AxChunk ax_chunk(const Ctx &c, const StepParams &sp, int ci) {
+  int lo = 0, hi = sp.M - 1;  // last sequence with s_ax_cb <= ci
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (s_ax_cb[mid] <= ci) lo = mid;
+    else hi = mid - 1;
+  }
+  const int nch = (s_ax_n[lo] + kAxTok - 1) / kAxTok;
+  const int r = ci - s_ax_cb[lo];
+  AxChunk k;
+  k.m = lo;
+  k.g = r / nch;
+  k.t0 = (r - k.g * nch) * kAxTok;
+  return k;
+}
 
 // All threads, once per launch (after the step parameters are in shared
 // memory and ax_block_init).
@@ -137,27 +164,20 @@ __device__ void ax_launch_init(const Ctx &c) {
     }
     s_ax_lo = ax_bound(cb, blockIdx.x, gridDim.x);
     s_ax_hi = ax_bound(cb, blockIdx.x + 1, gridDim.x);
+    const int G = c.QH / c.KVH;
+    int hg = 1;
+    if (nl > 0)
+      while (hg < G && (size_t)(G / hg) * ax_stride(s_ax_n[s_ax_long[0]]) * 4 + kAxVRingBytes > (size_t)c.dyn_smem)
+        hg *= 2;
+    s_ax_hg = hg;
   }
-}
-
-// Chunk ci of the step: its sequence, kv head and first position.
-struct AxChunk {
-  int m, g, t0;
-};
-__device__ __forceinline__ AxChunk ax_chunk(const Ctx &c, const StepParams &sp, int ci) {
-  int lo = 0, hi = sp.M - 1;  // last sequence with s_ax_cb <= ci
-  while (lo < hi) {
-    const int mid = (lo + hi + 1) >> 1;
-    if (s_ax_cb[mid] <= ci) lo = mid;
-    else hi = mid - 1;
+  __syncthreads();
+  for (int i = threadIdx.x; i < s_ax_hi - s_ax_lo && i < kAxPgCap; i += kThreads) {
+    const AxChunk k = ax_chunk(c, sp, s_ax_lo + i);
+    const int *bt = sp.seq[k.m].bt;
+    s_ax_pg[i] = make_int2(__ldg(bt + k.t0 / kPageTokens),
+                           k.t0 + kPageTokens < s_ax_n[k.m] ? __ldg(bt + k.t0 / kPageTokens + 1) : -1);
   }
-  const int nch = (s_ax_n[lo] + kAxTok - 1) / kAxTok;
-  const int r = ci - s_ax_cb[lo];
-  AxChunk k;
-  k.m = lo;
-  k.g = r / nch;
-  k.t0 = (r - k.g * nch) * kAxTok;
-  return k;
 }
 
 // K rows of (layer, kv head g) in pool page `page`: 8 KB (the V rows follow).
@@ -169,16 +189,21 @@ __device__ __forceinline__ const float *ax_page_k(const Ctx &c, int page, int la
 __device__ __forceinline__ void ax_issue(const Ctx &c, int layer, float *smem, int i) {
   const StepParams &sp = *c.sp;
   const AxChunk k = ax_chunk(c, sp, s_ax_lo + i);
-  const int n = s_ax_n[k.m];
-  const int *bt = sp.seq[k.m].bt;
-  const bool two = k.t0 + kPageTokens < n;
+  int2 pg;
+  if (i < kAxPgCap) {
+    pg = s_ax_pg[i];
+  } else {
+    const int *bt = sp.seq[k.m].bt;
+    pg = make_int2(__ldg(bt + k.t0 / kPageTokens),
+                   k.t0 + kPageTokens < s_ax_n[k.m] ? __ldg(bt + k.t0 / kPageTokens + 1) : -1);
+  }
   constexpr uint32_t pb = kPageTokens * kHeadDim * 4;
   const int b = i % kAxKBufs;
   float *buf = ax_kbuf(c, sp.M, smem, b);
   uint64_t *bar = &s_ax_full[b];
-  mbar_expect_tx(bar, (two ? 2u : 1u) * pb);
-  bulk_g2s(buf, ax_page_k(c, __ldg(bt + k.t0 / kPageTokens), layer, k.g), pb, bar);
-  if (two) bulk_g2s(buf + kPageTokens * kHeadDim, ax_page_k(c, __ldg(bt + k.t0 / kPageTokens + 1), layer, k.g), pb, bar);
+  mbar_expect_tx(bar, (pg.y >= 0 ? 2u : 1u) * pb);
+  bulk_g2s(buf, ax_page_k(c, pg.x, layer, k.g), pb, bar);
+  if (pg.y >= 0) bulk_g2s(buf + kPageTokens * kHeadDim, ax_page_k(c, pg.y, layer, k.g), pb, bar);
 }
 
 // One thread: issues the block's chunks while fewer than `upto` (at most
@@ -402,149 +427,197 @@ __device__ __noinline__ void phase_attn_scores(const Ctx *cp, int layer, float *
 }
 
 // Value phase shared memory, from the base of the dynamic shared memory (the
-// phase runs alone: no copies of other phases are in flight during it):
-// a ring of value-step buffers (V rows of 32 positions, half the head dims:
-// 8 KB each, kAxVRing steps in flight, the first ones issued before the
-// softmax statistics are formed), then the item's scores ([G][stride] floats)
-// when they fit in the rest (c.dyn_smem bytes in all), else they are read
-// from the scratch.
-constexpr int kAxVRing = 8;
-constexpr int kAxVRingBytes = kAxVRing * kAxVBytes;
+// phase runs alone: no copies of other phases are in flight during it): a
+// ring of kAxVRing value-step buffers (V rows of 32 positions, half the head
+// dims: 8 KB each; per page one 2-D TMA box of 64 dims x 16 rows from the
+// pool map), then the item's scores (G / hg heads x stride floats, one bulk
+// copy), which the item turns into exponentials and then weights in place.
+__shared__ __align__(8) uint64_t s_av_bar[kAxVRing + 1];  // value steps, then the scores
+__shared__ uint32_t s_av_par;                             // parity of each barrier's next completion
+constexpr int kAvPgCap = 576;                             // pages of an item held in shared memory (9,216 positions)
+__shared__ int s_av_pg[kAvPgCap];
 
 __device__ __forceinline__ float *ax_vbuf(float *smem, int j) { return (float *)((uint8_t *)smem + (size_t)j * kAxVBytes); }
 
-// Every thread's cp.async copies of value step st (positions 32 st .. +31,
-// dims 64 half .. +63) of pair (m, g) into ring buffer st % kAxVRing: 32 rows
-// of 256 bytes; one commit group per step (empty past the last step).
-__device__ __forceinline__ void ax_issue_v(const Ctx &c, const int *bt, int layer, int g, int half, int st, int n,
-                                           float *smem) {
-  const int t0 = st * kAxVTok;
-  if (t0 < n) {
-    float *vb = ax_vbuf(smem, st % kAxVRing);
-    for (int q = threadIdx.x; q < kAxVTok * 16; q += kThreads) {
-      const int r = q >> 4, c16 = q & 15, t = t0 + r;
-      if (t < n) {
-        const float *src = c.kv_pool + (size_t)__ldg(bt + t / kPageTokens) * c.page_floats +
-                           ((((size_t)layer * c.KVH + g) * 2 + 1) * kPageTokens + (t % kPageTokens)) * kHeadDim +
-                           64 * half + 4 * c16;
-        cp_async16(vb + r * 64 + 4 * c16, src);
-      }
-    }
+__device__ __forceinline__ void av_block_init() {
+  if (threadIdx.x == 0) {
+    for (int j = 0; j <= kAxVRing; j++) mbar_init(&s_av_bar[j], 1);
+    mbar_fence_init();
+    s_av_par = 0;
   }
-  asm volatile("cp.async.commit_group;" ::: "memory");
 }
 
-// Phase 2: softmax and value chains of the step's long caches.
+// One thread: the copies of value step st (positions 32 st .. +31, dims
+// 64 half .. +63) of pair (m, g) into ring buffer st % kAxVRing.
+__device__ __forceinline__ void av_issue(const Ctx &c, const int *bt, int layer, int g, int half, int st, int n,
+                                         float *smem) {
+  const int t0 = st * kAxVTok;
+  if (t0 >= n) return;
+  const int b = st % kAxVRing;
+  float *vb = ax_vbuf(smem, b);
+  const int np = t0 + kPageTokens < n ? 2 : 1;
+  mbar_expect_tx(&s_av_bar[b], (uint32_t)np * kPageTokens * 64 * 4);
+  for (int p = 0; p < np; p++) {
+    // pool row of (page, layer, kv head g, V, position 0 of the page)
+    const int pi = t0 / kPageTokens + p;
+    const int page = pi < kAvPgCap ? s_av_pg[pi] : __ldg(bt + pi);
+    const int row = (((page * c.L + layer) * c.KVH + g) * 2 + 1) * kPageTokens;
+    tma_2d(vb + p * kPageTokens * 64, c.kv_map, 64 * half, row, &s_av_bar[b]);
+  }
+}
+
+__device__ __forceinline__ float4 lds_f4(const float *p) {
+  float4 v;
+  asm volatile("ld.shared.v4.f32 {%0,%1,%2,%3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "r"(smem_u32(p)) : "memory");
+  return v;
+}
+__device__ __forceinline__ f2x lds_f2x(const float *p) {
+  f2x v;
+  asm volatile("ld.shared.b64 %0, [%1];" : "=l"(v) : "r"(smem_u32(p)) : "memory");
+  return v;
+}
+__device__ __forceinline__ float lds_f1(const float *p) {
+  float v;
+  asm volatile("ld.shared.f32 %0, [%1];" : "=f"(v) : "r"(smem_u32(p)) : "memory");
+  return v;
+}
+
+// Phase 2: softmax and value chains of the step's long caches.  Items are
+// (sequence, kv head, half of the dims, group of G / hg heads), longest cache
+// first.
 __device__ __noinline__ void phase_attn_values(const Ctx *cp, int layer, float *smem) {
   const Ctx &c = *cp;
   const StepParams &sp = *c.sp;
-  const int G = c.QH / c.KVH;
+  const int G = c.QH / c.KVH, hg = s_ax_hg, Gs = G / hg;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int items = s_ax_nl * c.KVH * 2;
-  __shared__ float s_mx[kMaxGroup], s_inv[kMaxGroup];
-  float *ssc = (float *)((uint8_t *)smem + kAxVRingBytes);  // the item's scores, when they fit
+  const int per_pair = 2 * hg;
+  const int items = s_ax_nl * c.KVH * per_pair;
+  float *ssc = (float *)((uint8_t *)smem + kAxVRingBytes);  // the item's scores
+  if ((int)blockIdx.x >= items) return;
+  // trace marks 4-15 of the block's first item (SM clock cycles): entry,
+  // scores landed, weights formed, then (landed, chain done) of steps 0, 1,
+  // 8 and the last, exit
+  unsigned long long *mk = c.trace && threadIdx.x == 0 ? c.trace + 4 * kTraceRows + kTraceMarks * blockIdx.x : nullptr;
+  if (mk) mk[4] = clock64();
+  if (threadIdx.x == 0) {
+    // the ring's buffers were last written by ordinary stores in earlier
+    // phases; the scores and the new V rows were written by other blocks'
+    // ordinary stores (ordered by the grid barrier) and are read by the
+    // async proxy
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    asm volatile("fence.proxy.async.global;" ::: "memory");
+  }
   for (int it = blockIdx.x; it < items; it += gridDim.x) {
-    const int m = s_ax_long[it / (2 * c.KVH)], g = (it >> 1) % c.KVH, half = it & 1;
+    const int pair = it / per_pair, sub = it % per_pair;
+    const int m = s_ax_long[pair / c.KVH], g = pair % c.KVH, half = sub & 1, h0 = (sub >> 1) * Gs;
     const int n = s_ax_n[m], nv = n & ~15, ld = ax_stride(n);
     const int *bt = sp.seq[m].bt;
-    const float *Sg = c.att_s + s_ax_sb[m] + (size_t)g * G * ld;
-    const bool staged = (size_t)G * ld * 4 + kAxVRingBytes <= (size_t)c.dyn_smem;
-    // the item's scores (one group), then the first value steps
-    if (staged)
-      for (int q = threadIdx.x; q < G * ld / 4; q += kThreads) cp_async16(ssc + 4 * q, Sg + 4 * q);
-    asm volatile("cp.async.commit_group;" ::: "memory");
-    for (int st = 0; st < kAxVRing - 1; st++) ax_issue_v(c, bt, layer, g, half, st, n, smem);
-    // the scores' group is complete once at most kAxVRing - 1 (the value
-    // steps') are pending
-    asm volatile("cp.async.wait_group %0;" ::"n"(kAxVRing - 1) : "memory");
+    const float *Sg = c.att_s + s_ax_sb[m] + ((size_t)g * G + h0) * ld;
+    const int nst = (n + kAxVTok - 1) / kAxVTok;
+    const uint32_t par = s_av_par;
+    for (int i = threadIdx.x; i < (n + kPageTokens - 1) / kPageTokens && i < kAvPgCap; i += kThreads)
+      s_av_pg[i] = __ldg(bt + i);
     __syncthreads();
-    const float *S = staged ? ssc : Sg;
-    if (warp < G) {
-      const float *Sh = S + (size_t)warp * ld;
+    if (threadIdx.x == 0) {
+      mbar_expect_tx(&s_av_bar[kAxVRing], (uint32_t)(Gs * ld * 4));
+      bulk_g2s(ssc, Sg, (uint32_t)(Gs * ld * 4), &s_av_bar[kAxVRing]);
+      for (int st = 0; st < kAxVRing && st < nst; st++) av_issue(c, bt, layer, g, half, st, n, smem);
+    }
+    mbar_wait(&s_av_bar[kAxVRing], (par >> kAxVRing) & 1u, c.err);
+    if (mk && it == (int)blockIdx.x) mk[5] = clock64();
+    // ---- softmax of head h0 + warp (warps < Gs), in place: scores ->
+    // exponentials (positions below nv) -> weights (times 1/sum, all n)
+    float *W = ssc + (size_t)(warp < Gs ? warp : 0) * ld;
+    if (warp < Gs) {
       float mx = -INFINITY;
-#pragma unroll 8
-      for (int t = lane; t < n; t += 32) mx = fmaxf(mx, staged ? Sh[t] : __ldcg(Sh + t));
+      for (int i4 = lane; i4 < ld / 4; i4 += 32) {
+        const float4 v = lds_f4(W + 4 * i4);
+        const int t = 4 * i4;
+        mx = fmaxf(mx, t < n ? v.x : -INFINITY);
+        mx = fmaxf(mx, t + 1 < n ? v.y : -INFINITY);
+        mx = fmaxf(mx, t + 2 < n ? v.z : -INFINITY);
+        mx = fmaxf(mx, t + 3 < n ? v.w : -INFINITY);
+      }
       for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-      // lane chains: lane l (< 16) adds e_l, e_{l+16}, e_{l+32}, ... in order
-      // (lane l + 16 computes the odd 16-blocks' exponentials); scores are
-      // loaded four 32-blocks ahead of their use
+      for (int t = lane; t < nv; t += 32) W[t] = exp_fma(__fsub_rn(W[t], mx));
+      __syncwarp();
+      // lane chains: lane l (< 16) adds e_l, e_{l+16}, ... in order
       float acc = 0.0f;
-#pragma unroll 1
-      for (int t0 = 0; t0 < nv; t0 += 128) {
-        float sv[4];
-#pragma unroll
-        for (int u = 0; u < 4; u++) {
-          const int t = t0 + 32 * u + lane;
-          sv[u] = t < nv ? (staged ? Sh[t] : __ldcg(Sh + t)) : 0.0f;
-        }
-#pragma unroll
-        for (int u = 0; u < 4; u++) {
-          const int b0 = t0 + 32 * u;
-          if (b0 < nv) {
-            const float e = b0 + lane < nv ? exp_fma(__fsub_rn(sv[u], mx)) : 0.0f;
-            const float hi = __shfl_down_sync(0xffffffffu, e, 16);
-            acc = __fadd_rn(acc, e);
-            if (b0 + 16 < nv) acc = __fadd_rn(acc, hi);
-          }
-        }
+      if (lane < 16) {
+#pragma unroll 8
+        for (int t = lane; t < nv; t += 16) acc = __fadd_rn(acc, lds_f1(W + t));
       }
       // tree16 of lanes 0..15: (l, l+8), (l, l+4), then (0+2)+(1+3)
       float a = __fadd_rn(acc, __shfl_down_sync(0xffffffffu, acc, 8));
       a = __fadd_rn(a, __shfl_down_sync(0xffffffffu, a, 4));
       a = __fadd_rn(a, __shfl_down_sync(0xffffffffu, a, 2));
       a = __fadd_rn(a, __shfl_down_sync(0xffffffffu, a, 1));
-      if (lane == 0) {
-        s_mx[warp] = mx;
-        s_inv[warp] = __fdiv_rn(1.0f, a);
-      }
+      const float inv = __shfl_sync(0xffffffffu, __fdiv_rn(1.0f, a), 0);
+      // weights: exponential (or the tail's raw score) times 1/sum
+      for (int t = lane; t < n; t += 32) W[t] = __fmul_rn(W[t], inv);
+      __syncwarp();
     }
-    __syncthreads();
+    if (mk && it == (int)blockIdx.x) mk[6] = clock64();
     // ---- value chains: warp h, dims 64 half + 2 lane, +1
-    const int h = warp;
-    const float mx = h < G ? s_mx[h] : 0.0f, inv = h < G ? s_inv[h] : 0.0f;
-    const float *Sh = S + (size_t)(h < G ? h : 0) * ld;
     f2x o = 0ull;
-    const int nst = (n + kAxVTok - 1) / kAxVTok;
-    // scores of positions 32 st + lane, loaded ahead (two steps) when read
-    // from the scratch
-    float s1 = h < G && lane < n ? (staged ? Sh[lane] : __ldcg(Sh + lane)) : 0.0f;
-    float s2 = h < G && lane + kAxVTok < n ? (staged ? Sh[lane + kAxVTok] : __ldcg(Sh + lane + kAxVTok)) : 0.0f;
 #pragma unroll 1
     for (int st = 0; st < nst; st++) {
-      const int t0 = st * kAxVTok, t = t0 + lane;
-      const float sv = s1;
-      s1 = s2;
-      s2 = h < G && t + 2 * kAxVTok < n ? (staged ? Sh[t + 2 * kAxVTok] : __ldcg(Sh + t + 2 * kAxVTok)) : 0.0f;
-      float w = 0.0f;
-      if (h < G && t < n) w = __fmul_rn(t < nv ? exp_fma(__fsub_rn(sv, mx)) : sv, inv);
-      // step st's copies: all but the kAxVRing - 2 newest groups are complete
-      asm volatile("cp.async.wait_group %0;" ::"n"(kAxVRing - 2) : "memory");
-      __syncthreads();  // every thread's rows of step st landed; step st-1's buffer is free
-      ax_issue_v(c, bt, layer, g, half, st + kAxVRing - 1, n, smem);
-      const float *vb = ax_vbuf(smem, st % kAxVRing);
+      const int t0 = st * kAxVTok;
+      const int b = st % kAxVRing;
+      // step st's rows (use st / kAxVRing of buffer b)
+      mbar_wait(&s_av_bar[b], ((par >> b) ^ (uint32_t)(st / kAxVRing)) & 1u, c.err);
+      const int mi = st == 0 ? 7 : st == 1 ? 9 : st == 8 ? 11 : st == nst - 1 ? 13 : 0;
+      if (mk && mi && it == (int)blockIdx.x) mk[mi] = clock64();
+      const float *vb = ax_vbuf(smem, b) + 2 * lane;
+      const float *wt = W + t0;
       const int cnt = min(kAxVTok, n - t0);
-      if (h < G) {
-        int i0 = 0;
+      if (warp < Gs) {
+        int i = 0;
         if (st == 0) {
-          const float w0 = __shfl_sync(0xffffffffu, w, 0);
-          o = f2_mul(f2_pack(w0, w0), *(const f2x *)(vb + 2 * lane));
-          i0 = 1;
+          const float w0 = lds_f1(wt);
+          o = f2_mul(f2_pack(w0, w0), lds_f2x(vb));
+          i = 1;
+          for (; i < 4 && i < cnt; i++) {
+            const float wi = lds_f1(wt + i);
+            o = f2_fma(f2_pack(wi, wi), lds_f2x(vb + i * 64), o);
+          }
         }
-#pragma unroll 8
-        for (int i = i0; i < cnt; i++) {
-          const float wi = __shfl_sync(0xffffffffu, w, i);
-          o = f2_fma(f2_pack(wi, wi), *(const f2x *)(vb + i * 64 + 2 * lane), o);
+#pragma unroll 2
+        for (; i + 4 <= cnt; i += 4) {
+          const float4 w4 = lds_f4(wt + i);
+          const f2x v0 = lds_f2x(vb + i * 64), v1 = lds_f2x(vb + (i + 1) * 64);
+          const f2x v2 = lds_f2x(vb + (i + 2) * 64), v3 = lds_f2x(vb + (i + 3) * 64);
+          o = f2_fma(f2_pack(w4.x, w4.x), v0, o);
+          o = f2_fma(f2_pack(w4.y, w4.y), v1, o);
+          o = f2_fma(f2_pack(w4.z, w4.z), v2, o);
+          o = f2_fma(f2_pack(w4.w, w4.w), v3, o);
+        }
+        for (; i < cnt; i++) {
+          const float wi = lds_f1(wt + i);
+          o = f2_fma(f2_pack(wi, wi), lds_f2x(vb + i * 64), o);
         }
       }
+      if (mk && mi && it == (int)blockIdx.x) mk[mi + 1] = clock64();
+      // every warp is done with buffer b: it takes step st + kAxVRing
+      __syncthreads();
+      if (threadIdx.x == 0 && st + kAxVRing < nst) av_issue(c, bt, layer, g, half, st + kAxVRing, n, smem);
     }
-    asm volatile("cp.async.wait_group 0;" ::: "memory");
-    if (h < G) {
+    if (warp < Gs) {
       float2 r;
       r.x = f2_lo(o);
       r.y = f2_hi(o);
-      *(float2 *)(c.head + ((size_t)m * c.QH + (size_t)g * G + h) * kHeadDim + 64 * half + 2 * lane) = r;
+      *(float2 *)(c.head + ((size_t)m * c.QH + (size_t)g * G + h0 + warp) * kHeadDim + 64 * half + 2 * lane) = r;
     }
-    __syncthreads();  // the ring and the score copy are free for the next item
+    if (threadIdx.x == 0) {
+      // step i completed a phase of buffer i % kAxVRing; the scores one
+      uint32_t p = par;
+      for (int j = 0; j < kAxVRing; j++)
+        if (nst > j && (((nst - 1 - j) / kAxVRing) & 1) == 0) p ^= 1u << j;
+      p ^= 1u << kAxVRing;
+      s_av_par = p;
+    }
+    __syncthreads();  // the scores' copy and s_av_par are settled for the next item
+    if (mk && it == (int)blockIdx.x) mk[15] = clock64();
   }
 }
 

@@ -43,10 +43,6 @@ constexpr int kMmaM = 64;         // A rows (sequences) per MMA
 constexpr int kMaxNT = 256;       // output rows per N tile
 constexpr int kTmemCols = 512;    // TMEM columns a block allocates
 
-// TMA descriptor of one packed weight matrix (CUtensorMap, 128 bytes).
-struct __align__(64) TmapBytes {
-  unsigned char b[128];
-};
 
 struct BatchedW {
   const TmapBytes *tm;  // [L * 5 + 1]: per layer qkv, o, gate, up, down; then lm_head
@@ -135,14 +131,6 @@ __device__ __forceinline__ void tmem_ld32_nowait(uint32_t addr, uint32_t (&v)[32
       : "r"(addr));
 }
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
-// 2-D TMA tile copy into this CTA only, of a box at (x bytes, y rows).
-__device__ __forceinline__ void tma_2d(void *dst, const TmapBytes *map, int x, int y, uint64_t *bar) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
-          smem_u32(dst)),
-      "l"(map), "r"(x), "r"(y), "r"(smem_u32(bar))
-      : "memory");
-}
 
 // Offset of (row r, byte k) in a K-major core-matrix tile of kKT bytes per row.
 __host__ __device__ __forceinline__ int cm_off(int r, int k) {

@@ -61,6 +61,11 @@ struct StepParams {
 __host__ __device__ __forceinline__ size_t step_params_bytes(int n) { return 16 + (size_t)n * sizeof(SeqParams); }
 static_assert(sizeof(SeqParams) == 32, "SeqParams is 32 bytes");
 
+// TMA descriptor (CUtensorMap, 128 bytes) as the kernels receive it.
+struct __align__(64) TmapBytes {
+  unsigned char b[128];
+};
+
 struct Ctx {
   int qtype, H, I, L, QH, KVH, D, V;
   float eps, attn_scale;
@@ -72,7 +77,8 @@ struct Ctx {
   const float *rope_cos, *rope_sin;  // [rope_max][D/2]
   int rope_max;
   const int *sec_axis;               // [D/2] M-RoPE axis of each frequency
-  float *kv_pool;                    // pages of [L][2][KVH][16][D] f32
+  float *kv_pool;                    // pages of [L][KVH][2 (K, V)][16][D] f32
+  const TmapBytes *kv_map;           // 2-D map of the pool: rows of D floats, box 64 floats x 16 rows
   long long page_floats;
   // step work buffers
   float *h, *vbuf, *qkv, *head, *g, *logits;
@@ -371,6 +377,15 @@ __device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t by
                    smem_u32(dst)),
                "l"(src), "r"(bytes), "r"(smem_u32(bar))
                : "memory");
+}
+// 2-D TMA tile copy into this CTA only, of a box at (x elements, y rows); x
+// times the element size is a multiple of 16 bytes at every call site.
+__device__ __forceinline__ void tma_2d(void *dst, const TmapBytes *map, int x, int y, uint64_t *bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+          smem_u32(dst)),
+      "l"(map), "r"(x), "r"(y), "r"(smem_u32(bar))
+      : "memory");
 }
 // Bounded wait for phase `parity` of an mbarrier.  On timeout the error word
 // is set and false returned.
@@ -999,78 +1014,83 @@ __device__ __noinline__ void phase_gemv_t(const Ctx *cp, const GemvArgs *ap, int
 // at once with two dp4a chains per row; the int32 sums are exact, so the split
 // does not change results.
 // ---------------------------------------------------------------------------
-// Input prologue of the single-sequence int8-activation GEMV (xs path), with
-// three block barriers: the gather, the reductions, the quantised vector.
-// The reductions are split over the 8 warps and combined in the reference's
-// order after one barrier:
-//   largest |value|: warp w takes elements [w n/8, (w+1) n/8) (|x| for
-//     PRO_PLAIN, |fl(x*w)| otherwise); the largest |normalised value| is
-//     fl(max|fl(x*w)| * scale), rounding being monotone and sign-symmetric;
-//   PRO_RMSNORM: the 64 FMA slot chains of sumSquaresF32FMA (slot s over
-//     elements s, s+64, ... in order), lane l < 8 of warp w running slot
-//     8w + l; slots folded as (s[l]+s[l+16]) + (s[l+32]+s[l+48]), then tree16;
-//   PRO_ADDNORM: the fused kernels' 8 workers of n/8 rows, worker w on warp w:
-//     16 lanes of unfused square-adds + tree16 (VNNI finalize); worker partials
-//     added in order.
-// Writes the uint8 activations (Q4: even columns then odd) to the x area and
-// returns the activation scale sx (the same value in every thread).
+// Input prologue of the single-sequence int8-activation GEMV (xs path).
+// Every thread loads float4 groups t, t + 256, ... of the input from L2 into
+// registers (the norm modes also into shared memory, where the reduction
+// chains read them), the chains are reduced in the reference's order and
+// combined after a barrier, and every thread quantises the elements it holds:
+//   PRO_RMSNORM (sumSquaresF32FMA): thread s < 64 runs slot s's FMA chain over
+//     elements s, s+64, ... in order; slots folded as (s[l]+s[l+16]) +
+//     (s[l+32]+s[l+48]), then tree16;
+//   PRO_ADDNORM (the fused kernels' 8 workers of n/8 rows, VNNI finalize):
+//     thread 16 w + l runs worker w's lane l (rows w n/8 + l + 16 k,
+//     unfused square-adds), tree16 over the half-warp, workers added in order;
+//   PRO_PLAIN: only the largest |x|.
+// The largest |normalised value| is fl(max|fl(x*w)| * scale), rounding being
+// monotone and sign-symmetric.  Barriers: 3 (norm modes) or 2 (plain).  Writes
+// the uint8 activations (Q4: even columns then odd) to the x area and returns
+// the activation scale sx (the same value in every thread).
+constexpr int kXsMaxPer = 16;  // elements a thread holds (n <= 4096)
 __device__ __noinline__ float xs_prologue(int qt, const float *src, int n, int mode, const float *w, bool w_global,
                                           float eps, float *smem, unsigned long long *mk = nullptr) {
-  float *red = smem;  // [0..7] warp maxima, [16..79] slot / worker sums
+  float *red = smem;  // [16..79] slot / worker sums, [96..103] warp maxima
   float *tmp = smem + 320;
   uint8_t *q = (uint8_t *)(tmp + n);
-  g2s_f32(tmp, src, n);
-  cp_async_wait_all();
-  __syncthreads();
-  if (mk) mk[17] = gtimer();
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  auto wv = [&](int i) { return w_global ? __ldg(w + i) : w[i]; };
-  {
-    // largest |x| (PLAIN) or |fl(x*w)| over the warp's share, float4 at a time
-    const int per4 = n / 4 / kFusedWorkers, b4 = warp * per4;
-    float M = 0.0f;
-    for (int i = b4 + lane; i < b4 + per4; i += 32) {
-      const float4 x = ((const float4 *)tmp)[i];
-      if (mode == PRO_PLAIN) {
-        M = fmaxf(M, fmaxf(fmaxf(fabsf(x.x), fabsf(x.y)), fmaxf(fabsf(x.z), fabsf(x.w))));
-      } else {
-        const float4 ww = w_global ? __ldg((const float4 *)w + i) : ((const float4 *)w)[i];
-        M = fmaxf(M, fmaxf(fmaxf(fabsf(__fmul_rn(x.x, ww.x)), fabsf(__fmul_rn(x.y, ww.y))),
-                           fmaxf(fabsf(__fmul_rn(x.z, ww.z)), fabsf(__fmul_rn(x.w, ww.w)))));
-      }
-    }
-    for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
-    if (lane == 0) red[warp] = M;
-  }
-  if (mode == PRO_RMSNORM) {
-    if (lane < 8) {
-      const int sl = 8 * warp + lane;
-      float a = 0.0f;
-#pragma unroll 4
-      for (int c = sl; c < n; c += 64) a = __fmaf_rn(tmp[c], tmp[c], a);
-      red[16 + sl] = a;
-    }
-  } else if (mode == PRO_ADDNORM) {
-    const int chunk = n / kFusedWorkers, l = lane & 15;
-    float a = 0.0f;
-    if (lane < 16) {
-#pragma unroll 4
-      for (int k = l; k < chunk; k += 16) {
-        const float x = tmp[warp * chunk + k];
-        a = __fadd_rn(a, __fmul_rn(x, x));
-      }
-    }
-    // tree16 of lanes 0..15
-    a = __fadd_rn(a, __shfl_down_sync(0xffffffffu, a, 8));
-    a = __fadd_rn(a, __shfl_down_sync(0xffffffffu, a, 4));
-    a = __fadd_rn(a, __shfl_down_sync(0xffffffffu, a, 2));
-    a = __fadd_rn(a, __shfl_down_sync(0xffffffffu, a, 1));
-    if (lane == 0) red[16 + warp] = a;
-  }
-  __syncthreads();
-  float M = red[0];
+  const int t = threadIdx.x, lane = t & 31, warp = t >> 5, n4 = n / 4;
+  float4 xv[kXsMaxPer / 4];
 #pragma unroll
-  for (int i = 1; i < kFusedWorkers; i++) M = fmaxf(M, red[i]);
+  for (int k = 0; k < kXsMaxPer / 4; k++) {
+    const int g = t + kThreads * k;
+    xv[k] = g < n4 ? __ldcg((const float4 *)src + g) : make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+  float M = 0.0f;
+#pragma unroll
+  for (int k = 0; k < kXsMaxPer / 4; k++) {
+    const int g = t + kThreads * k;
+    if (g < n4) {
+      const float4 v = xv[k];
+      if (mode == PRO_PLAIN) {
+        M = fmaxf(M, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
+      } else {
+        ((float4 *)tmp)[g] = v;
+        const float4 ww = w_global ? __ldg((const float4 *)w + g) : ((const float4 *)w)[g];
+        M = fmaxf(M, fmaxf(fmaxf(fabsf(__fmul_rn(v.x, ww.x)), fabsf(__fmul_rn(v.y, ww.y))),
+                           fmaxf(fabsf(__fmul_rn(v.z, ww.z)), fabsf(__fmul_rn(v.w, ww.w)))));
+      }
+    }
+  }
+  for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+  if (lane == 0) red[96 + warp] = M;
+  if (mode != PRO_PLAIN) {
+    __syncthreads();
+    if (mode == PRO_RMSNORM) {
+      if (t < 64) {
+        float a = 0.0f;
+#pragma unroll 4
+        for (int c = t; c < n; c += 64) a = __fmaf_rn(tmp[c], tmp[c], a);
+        red[16 + t] = a;
+      }
+    } else {
+      const int chunk = n / kFusedWorkers;
+      float a = 0.0f;
+      if (t < 16 * kFusedWorkers) {
+        const float *r = tmp + (t >> 4) * chunk;
+#pragma unroll 4
+        for (int k = t & 15; k < chunk; k += 16) a = __fadd_rn(a, __fmul_rn(r[k], r[k]));
+      }
+      // tree16 of each half-warp (one worker)
+      a = __fadd_rn(a, __shfl_down_sync(0xffffffffu, a, 8));
+      a = __fadd_rn(a, __shfl_down_sync(0xffffffffu, a, 4));
+      a = __fadd_rn(a, __shfl_down_sync(0xffffffffu, a, 2));
+      a = __fadd_rn(a, __shfl_down_sync(0xffffffffu, a, 1));
+      if ((t & 15) == 0 && t < 16 * kFusedWorkers) red[16 + (t >> 4)] = a;
+    }
+  }
+  __syncthreads();
+  if (mk) mk[17] = clock64();
+  M = red[96];
+#pragma unroll
+  for (int i = 1; i < kThreads / 32; i++) M = fmaxf(M, red[96 + i]);
   float ss = 0.0f;
   if (mode == PRO_RMSNORM) {
     float r[16];
@@ -1091,18 +1111,43 @@ __device__ __noinline__ float xs_prologue(int qt, const float *src, int n, int m
     sx = __fdiv_rn(mx, 127.0f);
     inv = __fdiv_rn(1.0f, sx);
   }
-  if (mk) mk[18] = gtimer();
+  if (mk) mk[18] = clock64();
   const int half = qt == QT_Q4 ? n / 2 : 0;
-  for (int i = threadIdx.x; i < n; i += kThreads) {
-    float v = tmp[i];
-    if (mode != PRO_PLAIN) v = __fmul_rn(__fmul_rn(v, wv(i)), scale);
-    const float f = __fadd_rn(rintf(__fmul_rn(v, inv)), 128.0f);
-    const int b = mx != 0.0f ? (int)fminf(fmaxf(f, 0.0f), 255.0f) : 128;
-    q[half ? (i & 1) * half + (i >> 1) : i] = (uint8_t)b;
+#pragma unroll
+  for (int k = 0; k < kXsMaxPer / 4; k++) {
+    const int g = t + kThreads * k;
+    if (g < n4) {
+      float v4[4] = {xv[k].x, xv[k].y, xv[k].z, xv[k].w};
+      float4 ww = make_float4(1.f, 1.f, 1.f, 1.f);
+      if (mode != PRO_PLAIN) ww = w_global ? __ldg((const float4 *)w + g) : ((const float4 *)w)[g];
+      const float w4[4] = {ww.x, ww.y, ww.z, ww.w};
+      uint32_t packed = 0;
+#pragma unroll
+      for (int e = 0; e < 4; e++) {
+        const float v = mode != PRO_PLAIN ? __fmul_rn(__fmul_rn(v4[e], w4[e]), scale) : v4[e];
+        const float f = __fadd_rn(rintf(__fmul_rn(v, inv)), 128.0f);
+        const int b = mx != 0.0f ? (int)fminf(fmaxf(f, 0.0f), 255.0f) : 128;
+        packed |= (uint32_t)b << (8 * e);
+      }
+      const int i = 4 * g;
+      if (half) {
+        // Q4: even columns to the first half, odd ones to the second
+        ((uint16_t *)q)[i >> 2] = (uint16_t)((packed & 0xFFu) | ((packed >> 8) & 0xFF00u));
+        ((uint16_t *)(q + half))[i >> 2] = (uint16_t)(((packed >> 8) & 0xFFu) | ((packed >> 16) & 0xFF00u));
+      } else {
+        *(uint32_t *)(q + i) = packed;
+      }
+    }
   }
   __syncthreads();
-  if (mk) mk[19] = gtimer();
+  if (mk) mk[19] = clock64();
   return sx;
+}
+
+// Input widths xs_prologue takes (kXsMaxPer elements a thread).
+__host__ __device__ __forceinline__ bool xs_prologue_fits(int mode, int n) {
+  return mode == PRO_RMSNORM ? n <= 64 * kXsMaxPer : mode == PRO_ADDNORM ? n <= 16 * kFusedWorkers * kXsMaxPer
+                                                                         : n <= 4 * kThreads * (kXsMaxPer / 4);
 }
 
 template <int QT>
@@ -1198,12 +1243,12 @@ __device__ __noinline__ void phase_gemv_xs(const Ctx *cp, const GemvArgs *ap, fl
   const int lpr = g.lpr;
   const int rpw = 32 / lpr, li = lane & (lpr - 1), sub = lane / lpr;
   const int pass = (kThreads / 32) * rpw;  // rows one pass of the block covers per RB slot
-  // trace marks 16-23 of the block (QKV phases; the last layer's remain):
-  // entry, input gathered, reductions done, input quantised, activations in
-  // registers, first stage landed, dots done, exit
+  // trace marks 16-23 of the block (QKV phases; the last layer's remain), SM
+  // clock cycles: entry, reductions posted, scale formed, input quantised,
+  // activations in registers, first stage landed, dots done, exit
   unsigned long long *mk =
       c.trace && EPI == EPI_STORE && threadIdx.x == 0 ? c.trace + 4 * kTraceRows + kTraceMarks * blockIdx.x : nullptr;
-  if (mk) mk[16] = gtimer();
+  if (mk) mk[16] = clock64();
   // residual values of this lane's rows of a one-stage slab, fetched now so
   // their latency hides behind the prologue
   float rpre[RB];
@@ -1254,7 +1299,7 @@ __device__ __noinline__ void phase_gemv_xs(const Ctx *cp, const GemvArgs *ap, fl
     }
   for (int o = lpr >> 1; o > 0; o >>= 1) qsum += __shfl_xor_sync(0xffffffffu, qsum, o);
   const int32_t corr = T::OFF * (int32_t)qsum;
-  if (mk) mk[20] = gtimer();
+  if (mk) mk[20] = clock64();
   bool in_place = false;
   if (EPI == EPI_RESID) {
     if (a.resid_mode == RESID_ALWAYS) {
@@ -1276,7 +1321,7 @@ __device__ __noinline__ void phase_gemv_xs(const Ctx *cp, const GemvArgs *ap, fl
     const int r0 = lo + st * srows, nr = min(srows, hi - r0);
     const uint8_t *buf = g.stage + (size_t)(st % g.kSt) * kStageBytes;
     if (!gemv_wait(c, g, st)) ok = false;
-    if (mk && st == 0) mk[21] = gtimer();
+    if (mk && st == 0) mk[21] = clock64();
 #pragma unroll 1
     for (int base = warp * rpw; ok && base < nr; base += pass * RB) {
       int lr[RB];
@@ -1325,7 +1370,7 @@ __device__ __noinline__ void phase_gemv_xs(const Ctx *cp, const GemvArgs *ap, fl
     __syncthreads();  // stage buffer free
     gemv_retire(a, g, st);
   }
-  if (mk) mk[22] = gtimer();
+  if (mk) mk[22] = clock64();
   if (threadIdx.x == 0) s_ring_setup = 0;
   if constexpr (EPI == EPI_ARGMAX) {
     for (int o = 16; o > 0; o >>= 1) {
@@ -1346,7 +1391,7 @@ __device__ __noinline__ void phase_gemv_xs(const Ctx *cp, const GemvArgs *ap, fl
     }
   }
   __syncthreads();
-  if (mk) mk[23] = gtimer();
+  if (mk) mk[23] = clock64();
 }
 
 // Single sequence: the x-stationary path for Q4/Q6 (when the rows are narrow
@@ -1357,7 +1402,7 @@ __device__ __forceinline__ void phase_gemv_q(const Ctx *c, const GemvArgs *a, in
   constexpr int R1 = 2;
   if (M <= 1) {
     if constexpr (QT != QT_Q8) {
-      if (xs_fits<QT>(a->A.pitch)) {
+      if (xs_fits<QT>(a->A.pitch) && xs_prologue_fits(a->mode, a->A.cols)) {
         // one instance per epilogue keeps each stage loop's code small
         switch (a->epi) {
           case EPI_STORE: phase_gemv_xs<QT, 2, EPI_STORE>(c, a, smem); break;
@@ -1566,6 +1611,7 @@ __device__ __forceinline__ void attn_block_init(const Ctx &c) {
     s_rope_ready = 0;
   }
   ax_block_init();
+  av_block_init();
   ax_launch_init(c);
   __syncthreads();
 }

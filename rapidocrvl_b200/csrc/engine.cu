@@ -548,6 +548,42 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (threadIdx.x < 32) tmem_dealloc(s_tmem, kTmemCols);
 }
 
+// Seeded pseudo-random K/V for positions [0, n) of the pages listed in
+// `pages` (np of them): K uniform in [-0.5, 0.5), V in [-1, 1), a hash of
+// (seed, position, layer, kv head, K|V, dim).  Grid-stride over float4s of
+// the pages.
+__global__ void k_fill_kv(float *pool, long long page_floats, const int *pages, int np, int n, int L, int KVH, int D,
+                          unsigned long long seed) {
+  const long long per4 = page_floats / 4, total = per4 * np;
+  for (long long q = (long long)blockIdx.x * blockDim.x + threadIdx.x; q < total;
+       q += (long long)gridDim.x * blockDim.x) {
+    const int p = (int)(q / per4);
+    const long long r = (q - (long long)p * per4) * 4;  // float offset within the page
+    const int d = (int)(r % D), row = (int)((r / D) % kPageTokens);
+    const long long blk = r / ((long long)D * kPageTokens);  // (layer, kv head, K|V)
+    const int kind = (int)(blk & 1);
+    const int pos = p * kPageTokens + row;
+    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (pos < n) {
+      float e[4];
+      for (int j = 0; j < 4; j++) {
+        unsigned long long h = seed ^ ((unsigned long long)pos << 32) ^ ((unsigned long long)blk << 12) ^ (d + j);
+        h ^= h >> 33;
+        h *= 0xff51afd7ed558ccdull;
+        h ^= h >> 33;
+        h *= 0xc4ceb9fe1a85ec53ull;
+        h ^= h >> 33;
+        const float u = (float)(h >> 40) * (1.0f / 16777216.0f);  // [0, 1)
+        e[j] = kind ? 2.0f * u - 1.0f : u - 0.5f;
+      }
+      v = make_float4(e[0], e[1], e[2], e[3]);
+    }
+    ((float4 *)(pool + (size_t)pages[p] * page_floats))[r / 4] = v;
+  }
+  (void)L;
+  (void)KVH;
+}
+
 // Per-row sum of unpacked int8 weights; one warp per row.
 __global__ void k_rowsum(int type, const uint8_t *w, int rows, int cols, int pitch, int32_t *out) {
   int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
@@ -723,6 +759,38 @@ bool make_weight_map(PfnEncodeTiled enc, const DMat &A, int qtype, int grid, Tma
              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// 2-D TMA map of the KV pool for the attention value phase: rows of head_dim
+// floats (every (page, layer, kv head, K|V, position) is one row), boxes of
+// 64 floats x 16 rows (half a head's dims over one page).
+int make_kv_map(ocrvl_model *m) {
+  void *fn = nullptr;
+  cudaDriverEntryPointQueryResult q;
+  if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) != cudaSuccess || !fn ||
+      q != cudaDriverEntryPointSuccess) {
+    cudaGetLastError();
+    return fail(OCRVL_E_CUDA, "cuTensorMapEncodeTiled is unavailable (driver too old for the attention path)");
+  }
+  PfnEncodeTiled enc = (PfnEncodeTiled)fn;
+  const ocrvl_model_desc &d = m->desc;
+  const long long rows = (long long)m->num_pages * d.num_layers * d.num_kv_heads * 2 * kPageTokens;
+  if (rows >= (1ll << 31)) return fail(OCRVL_E_INVALID, "kv_pool_bytes too large for the attention map");
+  cuuint64_t dims[2] = {(cuuint64_t)d.head_dim, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)d.head_dim * 4};
+  cuuint32_t box[2] = {64, (cuuint32_t)kPageTokens};
+  cuuint32_t es[2] = {1, 1};
+  TmapBytes map;
+  memset(&map, 0, sizeof(map));
+  if (enc((CUtensorMap *)&map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, (void *)m->kv_pool, dims, strides, box, es,
+          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+    return fail(OCRVL_E_CUDA, "cuTensorMapEncodeTiled failed for the KV pool");
+  TmapBytes *dmap = m->dalloc<TmapBytes>(1);
+  if (!dmap) return fail(OCRVL_E_NOMEM, "KV map");
+  CK(cudaMemcpy(dmap, &map, sizeof(map), cudaMemcpyHostToDevice));
+  m->ctx.kv_map = dmap;
+  return OCRVL_OK;
+}
+
 // Sets up the batched step for Q4 / Q6 models: weight maps, activation image,
 // kernel attributes.  Leaves m->batched false (steps of more than kMaxBatch
 // sequences then run as groups) when any part is unavailable.
@@ -737,6 +805,11 @@ void setup_batched(ocrvl_model *m) {
     return;
   }
   PfnEncodeTiled enc = (PfnEncodeTiled)fn;
+  // the quantisation phases hold each thread's inputs in registers
+  const ocrvl_model_desc &dd = m->desc;
+  if (!xs_prologue_fits(PRO_RMSNORM, dd.hidden_size) ||
+      !xs_prologue_fits(PRO_PLAIN, std::max(dd.num_heads * dd.head_dim, dd.intermediate_size)))
+    return;
   const int L = m->desc.num_layers;
   std::vector<TmapBytes> maps((size_t)L * 5 + 1);
   for (int l = 0; l < L; l++) {
@@ -1047,6 +1120,7 @@ int ocrvl_finalize(ocrvl_model *m) {
   c.sec_axis = m->sec_axis;
   c.kv_pool = m->kv_pool;
   c.page_floats = m->page_floats;
+  if (int rc = make_kv_map(m)) return rc;
   c.max_ctx = d.max_position;
   int qkvld = (c.QH + 2 * c.KVH) * c.D;
   size_t B = kMaxSeqs;
@@ -1238,6 +1312,45 @@ int ocrvl_seq_import_kv(ocrvl_seq *s, int n, const float *k, const float *v) {
       return fail(OCRVL_E_CUDA, std::string("cudaMemcpy: ") + cudaGetErrorString(e));
     }
   }
+  s->len = n;
+  return OCRVL_OK;
+}
+
+int ocrvl_seq_fill_synthetic(ocrvl_seq *s, int n, uint64_t seed) {
+  if (!s) return fail(OCRVL_E_INVALID, "null seq");
+  if (n < 0 || n > s->max_tokens) return fail(OCRVL_E_INVALID, "n outside 0..max_tokens");
+  if (int rc = ocrvl_seq_reset(s)) return rc;
+  ocrvl_model *m = s->m;
+  std::lock_guard<std::mutex> lk(m->mu);
+  const ocrvl_model_desc &d = m->desc;
+  const int np = (n + kPageTokens - 1) / kPageTokens;
+  if ((size_t)np > m->free_pages.size()) return fail(OCRVL_E_NOMEM, "KV page pool exhausted");
+  if (int rc = set_device(m)) return rc;
+  if (np == 0) {
+    s->len = 0;
+    return OCRVL_OK;
+  }
+  CK(cudaStreamSynchronize(m->stream));  // the pinned staging may feed an earlier copy
+  std::vector<int> ids(np);
+  for (int p = 0; p < np; p++) {
+    ids[p] = m->free_pages.back();
+    m->free_pages.pop_back();
+    s->pages.push_back(ids[p]);
+  }
+  auto undo = [&](cudaError_t e) {
+    for (int q : s->pages) m->free_pages.push_back(q);
+    s->pages.clear();
+    return fail(OCRVL_E_CUDA, std::string("fill: ") + cudaGetErrorString(e));
+  };
+  cudaError_t e = cudaMemcpy(s->bt_d, ids.data(), (size_t)np * 4, cudaMemcpyHostToDevice);
+  if (e != cudaSuccess) return undo(e);
+  const long long total4 = m->page_floats / 4 * np;
+  const int blocks = (int)std::min<long long>((total4 + 255) / 256, (long long)m->sms * 16);
+  k_fill_kv<<<blocks, 256, 0, m->stream>>>(m->kv_pool, m->page_floats, s->bt_d, np, n, d.num_layers, d.num_kv_heads,
+                                           d.head_dim, (unsigned long long)seed);
+  e = cudaGetLastError();
+  if (e == cudaSuccess) e = cudaStreamSynchronize(m->stream);
+  if (e != cudaSuccess) return undo(e);
   s->len = n;
   return OCRVL_OK;
 }

@@ -193,6 +193,12 @@ class Sequence_:
         _lib.check(self.rt._L.ocrvl_seq_read_kv(self._h, int(layer), _ptr(k), _ptr(v)))
         return k[:n], v[:n]
 
+    def fill_synthetic(self, n: int, seed: int) -> None:
+        """Sets the cache to n positions of seeded device-generated K/V
+        (ocrvl_seq_fill_synthetic): the stand-in for a long prompt's prefill
+        when only the decode steps after it are timed."""
+        _lib.check(self.rt._L.ocrvl_seq_fill_synthetic(self._h, int(n), int(seed) & 0xFFFFFFFFFFFFFFFF))
+
     def import_kv(self, k, v) -> None:
         """Replaces the cache with k, v of shape [num_layers][n][kv_heads *
         head_dim] (f32) and sets the length to n (ocrvl_seq_import_kv)."""

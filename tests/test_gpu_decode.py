@@ -356,3 +356,31 @@ def test_caches_over_1024_positions(tiny_models):
             ids1, logits1 = rt.step([seq_b[j]], ids=[toks[j]], return_logits=True)
             assert int(ids1[0]) == int(ids_joint[j]) and np.array_equal(logits1[0], logits_joint[j]), (step, j)
         toks = [int(i) for i in ids_joint]
+
+
+def test_fill_synthetic_cache_steps_like_the_oracle(tiny_models):
+    """ocrvl_seq_fill_synthetic: seeded device-generated K/V (the same seed
+    gives the same cache, values in K [-0.5, 0.5) / V [-1, 1)); the cache read
+    back and imported into the oracle gives the engine's next-step logits bit
+    for bit, and a refill with another length replaces it."""
+    _need_gpu()
+    cfg, rt, orc = _pair(tiny_models["q4"], "q4")
+    a, b = rt.new_sequence(720), rt.new_sequence(720)
+    a.fill_synthetic(700, 99)
+    b.fill_synthetic(700, 99)
+    L = cfg.num_hidden_layers
+    kv = [a.read_kv(layer) for layer in range(L)]
+    for layer in range(L):
+        kb, vb = b.read_kv(layer)
+        assert np.array_equal(kb, kv[layer][0]) and np.array_equal(vb, kv[layer][1])
+    k = np.stack([x[0] for x in kv])
+    v = np.stack([x[1] for x in kv])
+    assert k.shape == (L, 700, cfg.num_key_value_heads * cfg.head_dim)
+    assert np.all(np.abs(k) <= 0.5) and np.all(np.abs(v) <= 1.0) and np.std(v) > 0.3
+    o = orc.new_seq(720)
+    o.import_kv(k, v)
+    ids, logits = rt.step([a], ids=[17], return_logits=True)
+    otok, olog, _ = o.forward(orc.embed(17), 700, need_logits=True, want_logits=True)
+    assert int(ids[0]) == otok and np.array_equal(logits[0], olog)
+    a.fill_synthetic(40, 1)
+    assert len(a) == 40
