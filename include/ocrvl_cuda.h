@@ -97,6 +97,16 @@ int ocrvl_quant_type(const ocrvl_model *m);
  * tracing is off). */
 int ocrvl_trace_read(ocrvl_model *m, uint64_t *out, int cap);
 
+/* Polls a block of the step kernel makes at a grid barrier before it gives up
+ * (0 restores the default, about 4 million).  A step whose barrier wait runs
+ * out returns OCRVL_E_TIMEOUT, leaves its sequences as they were (no position
+ * appended) and resets the device barrier state, so the next step runs
+ * normally.  No reference counterpart: the reference detects failures by op
+ * error returns (internal/model/model.go:7235-7285); this bounds the device
+ * waits that replace them, and a small limit lets a test exercise the
+ * timeout path without faulting the GPU. */
+int ocrvl_set_wait_limit(ocrvl_model *m, int64_t barrier_polls);
+
 /* Copies up to `count` floats of one of the step's work buffers, as the
  * last step left them, to host memory (no reference counterpart: a
  * debugging aid for comparing a step's intermediates with a CPU run).

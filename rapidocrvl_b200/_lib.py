@@ -55,6 +55,7 @@ SIGNATURES = {
     "ocrvl_finalize": (I, [P]),
     "ocrvl_quant_type": (I, [P]),
     "ocrvl_trace_read": (I, [P, P, I]),
+    "ocrvl_set_wait_limit": (I, [P, I64]),
     "ocrvl_debug_read": (I, [P, I, P, I64]),
     "ocrvl_free": (None, [P]),
     "ocrvl_seq_create": (I, [P, I, C.POINTER(P)]),

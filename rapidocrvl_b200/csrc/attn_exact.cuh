@@ -314,7 +314,9 @@ __device__ void ax_load_q(const Ctx &c, const StepParams &sp, int m, int g, floa
 }
 
 // Phase 1: scores of the block's chunks (see the top of this file).
-__device__ __noinline__ void phase_attn_scores(const Ctx *cp, int layer, float *smem) {
+__device__ __noinline__ void phase_attn_scores(const Ctx *cp, int layer, float *smem_arg) {
+  float *const smem = dyn_smem();  // == smem_arg (the aligned dynamic base)
+  (void)smem_arg;
   const Ctx &c = *cp;
   const StepParams &sp = *c.sp;
   const int G = c.QH / c.KVH;
@@ -466,26 +468,16 @@ __device__ __forceinline__ void av_issue(const Ctx &c, const int *bt, int layer,
   }
 }
 
-__device__ __forceinline__ float4 lds_f4(const float *p) {
-  float4 v;
-  asm volatile("ld.shared.v4.f32 {%0,%1,%2,%3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "r"(smem_u32(p)) : "memory");
-  return v;
-}
-__device__ __forceinline__ f2x lds_f2x(const float *p) {
-  f2x v;
-  asm volatile("ld.shared.b64 %0, [%1];" : "=l"(v) : "r"(smem_u32(p)) : "memory");
-  return v;
-}
-__device__ __forceinline__ float lds_f1(const float *p) {
-  float v;
-  asm volatile("ld.shared.f32 %0, [%1];" : "=f"(v) : "r"(smem_u32(p)) : "memory");
-  return v;
-}
+__device__ __forceinline__ float4 lds_f4(const float *p) { return *(const float4 *)p; }
+__device__ __forceinline__ f2x lds_f2x(const float *p) { return *(const f2x *)p; }
+__device__ __forceinline__ float lds_f1(const float *p) { return *p; }
 
 // Phase 2: softmax and value chains of the step's long caches.  Items are
 // (sequence, kv head, half of the dims, group of G / hg heads), longest cache
 // first.
-__device__ __noinline__ void phase_attn_values(const Ctx *cp, int layer, float *smem) {
+__device__ __noinline__ void phase_attn_values(const Ctx *cp, int layer, float *smem_arg) {
+  float *const smem = dyn_smem();  // == smem_arg (the aligned dynamic base)
+  (void)smem_arg;
   const Ctx &c = *cp;
   const StepParams &sp = *c.sp;
   const int G = c.QH / c.KVH, hg = s_ax_hg, Gs = G / hg;
@@ -539,13 +531,26 @@ __device__ __noinline__ void phase_attn_values(const Ctx *cp, int layer, float *
         mx = fmaxf(mx, t + 3 < n ? v.w : -INFINITY);
       }
       for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-      for (int t = lane; t < nv; t += 32) W[t] = exp_fma(__fsub_rn(W[t], mx));
+      // exponentials, four independent ones per lane at a time
+      for (int t0 = 4 * lane; t0 < nv; t0 += 128) {
+        const float4 v = lds_f4(W + t0);  // nv is a multiple of 16: t0 + 3 < nv
+        *(float4 *)(W + t0) = make_float4(exp_fma(__fsub_rn(v.x, mx)), exp_fma(__fsub_rn(v.y, mx)),
+                                          exp_fma(__fsub_rn(v.z, mx)), exp_fma(__fsub_rn(v.w, mx)));
+      }
       __syncwarp();
-      // lane chains: lane l (< 16) adds e_l, e_{l+16}, ... in order
+      // lane chains: lane l (< 16) adds e_l, e_{l+16}, ... in order; loads
+      // eight steps ahead of the adds
       float acc = 0.0f;
       if (lane < 16) {
-#pragma unroll 8
-        for (int t = lane; t < nv; t += 16) acc = __fadd_rn(acc, lds_f1(W + t));
+        int t = lane;
+        for (; t + 7 * 16 < nv; t += 8 * 16) {
+          float e[8];
+#pragma unroll
+          for (int u = 0; u < 8; u++) e[u] = W[t + 16 * u];
+#pragma unroll
+          for (int u = 0; u < 8; u++) acc = __fadd_rn(acc, e[u]);
+        }
+        for (; t < nv; t += 16) acc = __fadd_rn(acc, W[t]);
       }
       // tree16 of lanes 0..15: (l, l+8), (l, l+4), then (0+2)+(1+3)
       float a = __fadd_rn(acc, __shfl_down_sync(0xffffffffu, acc, 8));
@@ -553,8 +558,13 @@ __device__ __noinline__ void phase_attn_values(const Ctx *cp, int layer, float *
       a = __fadd_rn(a, __shfl_down_sync(0xffffffffu, a, 2));
       a = __fadd_rn(a, __shfl_down_sync(0xffffffffu, a, 1));
       const float inv = __shfl_sync(0xffffffffu, __fdiv_rn(1.0f, a), 0);
-      // weights: exponential (or the tail's raw score) times 1/sum
-      for (int t = lane; t < n; t += 32) W[t] = __fmul_rn(W[t], inv);
+      // weights: exponential (or the tail's raw score) times 1/sum (the
+      // stride's padding past n is scaled too and never read)
+      for (int t0 = 4 * lane; t0 < ld; t0 += 128) {
+        const float4 v = lds_f4(W + t0);
+        *(float4 *)(W + t0) = make_float4(__fmul_rn(v.x, inv), __fmul_rn(v.y, inv), __fmul_rn(v.z, inv),
+                                          __fmul_rn(v.w, inv));
+      }
       __syncwarp();
     }
     if (mk && it == (int)blockIdx.x) mk[6] = clock64();
@@ -572,29 +582,27 @@ __device__ __noinline__ void phase_attn_values(const Ctx *cp, int layer, float *
       const float *wt = W + t0;
       const int cnt = min(kAxVTok, n - t0);
       if (warp < Gs) {
+        // the chain o = fma(w_t, v_t, o) is sequential; a full step is
+        // unrolled so that the compiler issues its shared loads ahead of the
+        // FMAs (the chain then waits on the FMA latency, not on the loads)
         int i = 0;
         if (st == 0) {
-          const float w0 = lds_f1(wt);
-          o = f2_mul(f2_pack(w0, w0), lds_f2x(vb));
+          const float w0 = wt[0];
+          o = f2_mul(f2_pack(w0, w0), *(const f2x *)vb);
           i = 1;
-          for (; i < 4 && i < cnt; i++) {
-            const float wi = lds_f1(wt + i);
-            o = f2_fma(f2_pack(wi, wi), lds_f2x(vb + i * 64), o);
+        }
+        if (cnt == kAxVTok && i == 0) {
+#pragma unroll
+          for (int u = 0; u < kAxVTok; u++) {
+            const float wu = wt[u];
+            o = f2_fma(f2_pack(wu, wu), *(const f2x *)(vb + u * 64), o);
           }
-        }
-#pragma unroll 2
-        for (; i + 4 <= cnt; i += 4) {
-          const float4 w4 = lds_f4(wt + i);
-          const f2x v0 = lds_f2x(vb + i * 64), v1 = lds_f2x(vb + (i + 1) * 64);
-          const f2x v2 = lds_f2x(vb + (i + 2) * 64), v3 = lds_f2x(vb + (i + 3) * 64);
-          o = f2_fma(f2_pack(w4.x, w4.x), v0, o);
-          o = f2_fma(f2_pack(w4.y, w4.y), v1, o);
-          o = f2_fma(f2_pack(w4.z, w4.z), v2, o);
-          o = f2_fma(f2_pack(w4.w, w4.w), v3, o);
-        }
-        for (; i < cnt; i++) {
-          const float wi = lds_f1(wt + i);
-          o = f2_fma(f2_pack(wi, wi), lds_f2x(vb + i * 64), o);
+        } else {
+#pragma unroll 8
+          for (; i < cnt; i++) {
+            const float wi = wt[i];
+            o = f2_fma(f2_pack(wi, wi), *(const f2x *)(vb + i * 64), o);
+          }
         }
       }
       if (mk && mi && it == (int)blockIdx.x) mk[mi + 1] = clock64();

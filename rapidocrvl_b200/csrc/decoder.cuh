@@ -94,9 +94,11 @@ struct Ctx {
   int pro_cols;                      // widest GEMV input: fixes the stage-ring offset (0: per phase)
   unsigned *lm_count;                // lm_head block arrivals
   int *hist, *hist_pos;              // device-side greedy loop: ids [steps][M], write index
-  // persistent-kernel barrier: monotonic arrival counter and error word
+  // persistent-kernel barrier: monotonic arrival counter, error word and the
+  // polls a block makes before it gives up (the step then fails with a timeout)
   unsigned *bar_count;
   int *err;
+  unsigned long long bar_spins;
   // optional step trace: per phase [start, prologue end, phase end (max over
   // blocks), barrier exit] in %globaltimer ns
   unsigned long long *trace;
@@ -106,6 +108,20 @@ __device__ __forceinline__ unsigned long long gtimer() {
   unsigned long long t;
   asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
   return t;
+}
+
+// Dynamic shared memory of the kernels that run the phases below, from a
+// 1024-byte boundary: TMA tensor copies and tcgen05 operand tiles need
+// 128-byte aligned destinations, and where the dynamic area starts depends on
+// the kernel's static shared memory (launches reserve kSmemAlignSlack bytes
+// for the shift).  The phases derive their pointers from this address inside
+// the function, so the compiler knows they point to shared memory and emits
+// shared-memory loads (a pointer passed in from the caller is generic).
+constexpr int kSmemAlignSlack = 1024;
+__device__ __forceinline__ float *dyn_smem() {
+  extern __shared__ float4 ocrvl_dyn_smem[];
+  const uint32_t s = (uint32_t)__cvta_generic_to_shared(ocrvl_dyn_smem);
+  return (float *)((uint8_t *)ocrvl_dyn_smem + ((kSmemAlignSlack - (s & (kSmemAlignSlack - 1))) & (kSmemAlignSlack - 1)));
 }
 
 // Trace buffer (OCRVL_TRACE): 256 phase rows of 4 words, then kTraceMarks
@@ -387,35 +403,39 @@ __device__ __forceinline__ void tma_2d(void *dst, const TmapBytes *map, int x, i
       "l"(map), "r"(x), "r"(y), "r"(smem_u32(bar))
       : "memory");
 }
-// Bounded wait for phase `parity` of an mbarrier.  On timeout the error word
-// is set and false returned.
+// Bounded wait for phase `parity` of an mbarrier: at most kMbarSpins polls
+// and kMbarWaitNs of elapsed time (a poll may suspend the thread for a while).
+// On timeout the error word is set and false returned.
 constexpr long long kMbarSpins = 1ll << 24;
+constexpr unsigned long long kMbarWaitNs = 2000000000ull;
 __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, int *err) {
   uint32_t done = 0;
   long long spins = 0;
+  unsigned long long t0 = 0;
   while (true) {
     asm volatile("{ .reg .pred p; mbarrier.try_wait.parity.shared.b64 p, [%1], %2; selp.u32 %0, 1, 0, p; }"
                  : "=r"(done)
                  : "r"(smem_u32(bar)), "r"(parity)
                  : "memory");
     if (done) return true;
-    if (++spins > kMbarSpins) {
+    ++spins;
+    if ((spins & 255) == 1) {
+      const unsigned long long now = gtimer();
+      if (spins == 1) t0 = now;
+      else if (now - t0 > kMbarWaitNs) spins = kMbarSpins + 1;
+    }
+    if (spins > kMbarSpins) {
       if (err) atomicExch(err, 1);
       return false;
     }
   }
 }
 
-__device__ __forceinline__ uint4 lds16(const void *p) {
-  uint4 v;
-  asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(smem_u32(p)));
-  return v;
-}
-__device__ __forceinline__ uint32_t lds4(const void *p) {
-  uint32_t v;
-  asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(smem_u32(p)));
-  return v;
-}
+// Shared-memory loads as ordinary dereferences: the compiler orders them
+// against barriers and the mbarrier waits (asm with a memory clobber) but is
+// free to issue them early, ahead of the arithmetic that consumes them.
+__device__ __forceinline__ uint4 lds16(const void *p) { return *(const uint4 *)p; }
+__device__ __forceinline__ uint32_t lds4(const void *p) { return *(const uint32_t *)p; }
 
 // ---------------------------------------------------------------------------
 // Row dot products over a batch of RB rows whose packed weights are staged in
@@ -858,7 +878,9 @@ __device__ void argmax_finish(const Ctx &c, int M, int feed) {
 }
 
 template <int QT, int M_, int RB>
-__device__ __noinline__ void phase_gemv_t(const Ctx *cp, const GemvArgs *ap, int M, float *smem) {
+__device__ __noinline__ void phase_gemv_t(const Ctx *cp, const GemvArgs *ap, int M, float *smem_arg) {
+  float *const smem = dyn_smem();  // == smem_arg (the aligned dynamic base)
+  (void)smem_arg;
   const Ctx &c = *cp;
   const GemvArgs &a = *ap;
   const int qt = QT;
@@ -1103,7 +1125,10 @@ __device__ __noinline__ float xs_prologue(int qt, const float *src, int n, int m
   }
   float scale = 1.0f, mx = M;
   if (mode != PRO_PLAIN) {
-    scale = fast_rsqrt(__fadd_rn(__fdiv_rn(ss, (float)n), eps));
+    // ss / n: a power-of-two n divides exactly as a multiply by 1/n
+    const float mean = (n & (n - 1)) == 0 ? __fmul_rn(ss, __uint_as_float((uint32_t)(127 - (31 - __clz(n))) << 23))
+                                          : __fdiv_rn(ss, (float)n);
+    scale = fast_rsqrt(__fadd_rn(mean, eps));
     mx = __fmul_rn(M, scale);
   }
   float sx = 1.0f, inv = 0.0f;
@@ -1221,7 +1246,9 @@ __device__ __forceinline__ uint32_t xs_row_dot(const uint8_t *w, const uint4 (*x
 }
 
 template <int QT, int RB, int EPI>
-__device__ __noinline__ void phase_gemv_xs(const Ctx *cp, const GemvArgs *ap, float *smem) {
+__device__ __noinline__ void phase_gemv_xs(const Ctx *cp, const GemvArgs *ap, float *smem_arg) {
+  float *const smem = dyn_smem();  // == smem_arg (the aligned dynamic base)
+  (void)smem_arg;
   using T = XsTraits<QT>;
   const Ctx &c = *cp;
   const GemvArgs &a = *ap;
@@ -1709,7 +1736,9 @@ __device__ void attn_range_prefetch(const Ctx &c, int layer, float *smem, int le
   ax_issue_upto(c, layer, smem, upto);
 }
 
-__device__ __noinline__ void phase_attn(const Ctx *cp, int layer, int append_only, int coop, float *smem) {
+__device__ __noinline__ void phase_attn(const Ctx *cp, int layer, int append_only, int coop, float *smem_arg) {
+  float *const smem = dyn_smem();  // == smem_arg (the aligned dynamic base)
+  (void)smem_arg;
   const Ctx &c = *cp;
   rg_bmark(c, 0);
   const StepParams &sp = *c.sp;

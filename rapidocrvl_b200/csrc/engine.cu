@@ -3,8 +3,7 @@
 // A decode step runs as ONE persistent cooperative kernel (k_step): every
 // block walks the phases of decoder.cuh for all layers, separated by a grid
 // barrier whose waits are bounded (a timed-out wait sets an error word and
-// every block returns).  OCRVL_STEP_MODE=phases runs the same phases as
-// separate launches instead (used to cross-check the barrier path).
+// every block returns).
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -71,7 +70,7 @@ __device__ __forceinline__ void red_add_release(unsigned *p, unsigned v) {
 // across launches).  Waits are bounded: after kBarrierSpins polls the block
 // records an error and leaves; waiting blocks also leave once any block has
 // recorded one.  Returns false on error.
-constexpr unsigned long long kBarrierSpins = 1ull << 22;
+constexpr unsigned long long kBarrierSpins = 1ull << 22;  // default poll limit (Ctx::bar_spins)
 __shared__ int s_grid_ok;
 // Arrival half: after the block's phase work (all threads), thread 0 adds 1.
 __device__ __forceinline__ void grid_arrive(const Ctx &c) {
@@ -86,7 +85,7 @@ __device__ bool grid_wait(const Ctx &c, unsigned target) {
     unsigned long long spins = 0;
     while ((int)(ld_acquire(c.bar_count) - target) < 0) {
       ++spins;
-      if (spins > kBarrierSpins || ((spins & 1023) == 0 && *(volatile int *)c.err)) {
+      if (spins > c.bar_spins || ((spins & 1023) == 0 && *(volatile int *)c.err)) {
         atomicExch(c.err, 1);
         ok = 0;
         break;
@@ -252,15 +251,7 @@ __device__ __forceinline__ void copy_words(void *dst, const void *src, int bytes
   for (int i = threadIdx.x; i < bytes / 4; i += kThreads) ((int *)dst)[i] = ((const int *)src)[i];
 }
 
-// Dynamic shared memory of the step kernels, from a 1024-byte boundary: TMA
-// tensor copies and tcgen05 operand tiles need 128-byte aligned destinations,
-// and where the dynamic area starts depends on the kernel's static shared
-// memory.  The launches reserve kSmemAlignSlack bytes for the shift.
-constexpr int kSmemAlignSlack = 1024;
-__device__ __forceinline__ float *align_dyn_smem(void *p) {
-  const uint32_t s = smem_u32(p);
-  return (float *)((uint8_t *)p + ((kSmemAlignSlack - (s & (kSmemAlignSlack - 1))) & (kSmemAlignSlack - 1)));
-}
+__device__ __forceinline__ float *align_dyn_smem(void *) { return dyn_smem(); }
 
 #define OCRVL_CTX_TO_SMEM(cv)                                                        \
   __shared__ Ctx sctx;                                                               \
@@ -342,19 +333,6 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 template <int QT>
-__global__ void __launch_bounds__(kThreads, 1)
-    k_phase(Ctx cv, int phase, int layer, int M, int any_logits, int do_embed, int feed) {
-  extern __shared__ float4 smem4[];
-  OCRVL_CTX_TO_SMEM(cv);
-  Ctx &cm = sctx;
-  if (threadIdx.x == 0) cm.trace = nullptr;
-  __syncthreads();
-  attn_block_init(c);
-  ring_init();
-  run_phase<QT>(c, phase, layer, M, any_logits, do_embed, feed, align_dyn_smem(smem4), 0, 0, false);
-}
-
-template <int QT>
 __global__ void __launch_bounds__(kThreads) k_gemv(Ctx cv, GemvArgs av, int M) {
   extern __shared__ float4 smem4[];
   OCRVL_CTX_TO_SMEM(cv);
@@ -362,7 +340,7 @@ __global__ void __launch_bounds__(kThreads) k_gemv(Ctx cv, GemvArgs av, int M) {
   __shared__ GemvArgs sa;
   if (threadIdx.x == 0) sa = av;
   __syncthreads();
-  phase_gemv_q<QT>(&c, &sa, M, (float *)smem4);
+  phase_gemv_q<QT>(&c, &sa, M, dyn_smem());
 }
 
 __global__ void __launch_bounds__(kThreads) k_addnorm_out(Ctx c, const float *v, int n, int M, const float *w,
@@ -643,7 +621,6 @@ struct ocrvl_model {
   int *bt_stage = nullptr;
   int grid = 0;
   size_t smem = 0;
-  bool persistent = true;
   unsigned bar_base = 0;  // value of the barrier counter before the next launch
   int sms = 0;
   // device-fed decode loop: id history and pinned staging for block-table
@@ -851,25 +828,12 @@ void setup_batched(ocrvl_model *m) {
 template <int QT>
 int launch_step_q(ocrvl_model *m, int M, int any_logits, int do_embed, int feed, int nsteps = 1) {
   Ctx c = m->ctx;
-  if (m->persistent) {
-    unsigned base = m->bar_base;
-    void *args[] = {&c, &M, &any_logits, &do_embed, &feed, &base, &nsteps};
-    CK(cudaLaunchCooperativeKernel((void *)k_step<QT>, dim3(m->grid), dim3(kThreads), args, m->smem, m->stream));
-    // each step's barriers, and one between consecutive steps
-    m->bar_base += ((unsigned)nsteps * barriers_per_step(m->desc.num_layers, any_logits) + (unsigned)(nsteps - 1)) *
-                   (unsigned)m->grid;
-    return OCRVL_OK;
-  }
-  if (nsteps != 1) return fail(OCRVL_E_INVALID, "several steps per launch need the persistent step kernel");
-  for (int l = 0; l < m->desc.num_layers; l++) {
-    bool kv_only = l == m->desc.num_layers - 1 && !any_logits;
-    for (int ph = 0; ph < kLayerPhases; ph++) {
-      k_phase<QT><<<m->grid, kThreads, m->smem, m->stream>>>(c, ph, l, M, any_logits, do_embed, feed);
-      if (kv_only && ph == 1) break;
-    }
-  }
-  if (any_logits) k_phase<QT><<<m->grid, kThreads, m->smem, m->stream>>>(c, kPhaseLM, m->desc.num_layers, M, any_logits, do_embed, feed);
-  CK(cudaGetLastError());
+  unsigned base = m->bar_base;
+  void *args[] = {&c, &M, &any_logits, &do_embed, &feed, &base, &nsteps};
+  CK(cudaLaunchCooperativeKernel((void *)k_step<QT>, dim3(m->grid), dim3(kThreads), args, m->smem, m->stream));
+  // each step's barriers, and one between consecutive steps
+  m->bar_base += ((unsigned)nsteps * barriers_per_step(m->desc.num_layers, any_logits) + (unsigned)(nsteps - 1)) *
+                 (unsigned)m->grid;
   return OCRVL_OK;
 }
 
@@ -898,13 +862,10 @@ int launch_step(ocrvl_model *m, int M, int any_logits, int do_embed, int feed = 
 template <int QT>
 int set_kernel_attrs(ocrvl_model *m) {
   CK(cudaFuncSetAttribute(k_step<QT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)m->smem));
-  CK(cudaFuncSetAttribute(k_phase<QT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)m->smem));
   int per_sm = 0;
   CK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_step<QT>, kThreads, m->smem));
   if (per_sm <= 0) return fail(OCRVL_E_CUDA, "step kernel does not fit on an SM");
-  int want = 1;
-  if (const char *e = getenv("OCRVL_BLOCKS_PER_SM")) want = std::max(1, std::atoi(e));
-  m->grid = m->sms * std::min(per_sm, want);
+  m->grid = m->sms;  // one block per SM (the kernel holds ~200 KB of shared memory)
   return OCRVL_OK;
 }
 
@@ -1110,6 +1071,7 @@ int ocrvl_finalize(ocrvl_model *m) {
   c.eps = d.rms_norm_eps;
   c.attn_scale = (float)(1.0 / std::sqrt((double)d.head_dim));
   c.fzero = 0.0f;
+  c.bar_spins = kBarrierSpins;
   c.embed = m->embed;
   c.final_norm = m->final_norm;
   c.layers = m->layers_d;
@@ -1164,15 +1126,13 @@ int ocrvl_finalize(ocrvl_model *m) {
              : m->qtype == QT_Q6 ? set_kernel_attrs<QT_Q6>(m) : set_kernel_attrs<QT_Q8>(m);
     if (rc) return rc;
   }
-  if (m->qtype == QT_Q4 && !getenv("OCRVL_NO_BATCHED")) setup_batched<QT_Q4>(m);
-  if (m->qtype == QT_Q6 && !getenv("OCRVL_NO_BATCHED")) setup_batched<QT_Q6>(m);
+  if (m->qtype == QT_Q4) setup_batched<QT_Q4>(m);
+  if (m->qtype == QT_Q6) setup_batched<QT_Q6>(m);
   if (getenv("OCRVL_TRACE")) {
     c.trace = m->dalloc<unsigned long long>(kTraceWords);
     if (!c.trace) return fail(OCRVL_E_NOMEM, "trace buffer");
     CK(cudaMemset(c.trace, 0, kTraceWords * 8));
   }
-  const char *mode = getenv("OCRVL_STEP_MODE");
-  m->persistent = !(mode && std::string(mode) == "phases");
   CK(cudaStreamSynchronize(m->stream));
   m->finalized = true;
   return OCRVL_OK;
@@ -1190,6 +1150,14 @@ int ocrvl_trace_read(ocrvl_model *m, uint64_t *out, int cap) {
   CK(cudaMemcpy(out, m->ctx.trace, (size_t)n * 8, cudaMemcpyDeviceToHost));
   CK(cudaMemset(m->ctx.trace, 0, kTraceWords * 8));
   return n;
+}
+
+int ocrvl_set_wait_limit(ocrvl_model *m, int64_t barrier_polls) {
+  if (!m || barrier_polls < 0) return fail(OCRVL_E_INVALID, "bad arguments");
+  std::lock_guard<std::mutex> lk(m->mu);
+  if (!m->finalized) return fail(OCRVL_E_INVALID, "model not finalized");
+  m->ctx.bar_spins = barrier_polls == 0 ? kBarrierSpins : (unsigned long long)barrier_polls;
+  return OCRVL_OK;
 }
 
 int ocrvl_debug_read(ocrvl_model *m, int which, float *out, int64_t count) {
@@ -1572,7 +1540,7 @@ int decode_group(ocrvl_model *m, ocrvl_seq *const *seqs, int n, const int32_t *f
   CK(cudaMemsetAsync(m->ctx.hist_pos, 0, 4, m->stream));
   CK(cudaMemcpyAsync(m->sp_d, &sp, step_params_bytes(n), cudaMemcpyHostToDevice, m->stream));
   int rc = OCRVL_OK;
-  if (n <= kMaxBatch && m->persistent) {
+  if (n <= kMaxBatch) {
     // every step in one persistent launch (the token feedback stays on the
     // device; no launch between steps)
     rc = m->qtype == QT_Q4   ? launch_step_q<QT_Q4>(m, n, 1, 1, 1, steps)
@@ -1809,7 +1777,7 @@ template <int QT>
 int op_gemv_q(const Ctx &c, const GemvArgs &a, int m, cudaStream_t st) {
   // the batched form (m > 1) keeps kMaxBatch input vectors in shared memory
   size_t smem = (m > 1 ? gemv_smem_total(QT, kMaxBatch, a.A.cols, kStagesMB)
-                       : gemv_smem_total(QT, 1, a.A.cols, kStagesM1)) + 64;
+                       : gemv_smem_total(QT, 1, a.A.cols, kStagesM1)) + 64 + kSmemAlignSlack;
   CK(cudaFuncSetAttribute(k_gemv<QT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   k_gemv<QT><<<op_grid(a.A.rows), kThreads, smem, st>>>(c, a, m);
   CK(cudaGetLastError());
