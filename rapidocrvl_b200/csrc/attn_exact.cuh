@@ -20,11 +20,15 @@
 // Phase 1 (scores).  The long caches' positions split into chunks of 32
 // (two KV pages) per (sequence m, kv head g); the step's chunks, in (m, g,
 // chunk) order, go to the blocks in contiguous ranges of equal count.  A
-// block streams its chunks' K rows (one 8 KB bulk copy per page) through
-// kAxKBufs buffers, the first ones issued before the phase, and writes the
+// block streams its chunks' K rows (one 8 KB bulk copy per page) through a
+// ring of K buffers, the first ones issued before the phase, and writes the
 // G scores of every position to the score scratch (c.att_s, per sequence
-// [kv head][head][n rounded up to 4]).  The chunk holding the new position scores it with the
-// new key (rotated) and appends the new K and V rows to the cache.
+// [kv head][head][n rounded up to 4]).  Chunk descriptors (sequence, kv head,
+// first position, pool pages) come from a per-launch table, and two chunks of
+// one pair are scored per iteration (independent work for the warps between
+// block barriers); refills are issued from two warps (one thread issues bulk
+// copies at about 24 GB/s).  The chunk holding the new position scores it
+// with the new key (rotated) and appends the new K and V rows to the cache.
 //
 // Phase 2 (softmax and values).  One item per (m, g, half of the head dims):
 // warp h reads head h's scores, takes M, the lane chains and 1/sum (every
@@ -34,7 +38,8 @@
 namespace ocrvl {
 
 constexpr int kAxTok = 32;                            // positions per score chunk (two pages)
-constexpr int kAxKBufs = 4;                           // K chunk buffers per block
+constexpr int kAxKBufs = 8;                           // K chunk buffers per block (M > 1)
+constexpr int kAxKBufsM1 = 4;                         // K chunk buffers per block (M <= 1: GEMV ring slots)
 constexpr int kAxKBytes = kAxTok * kHeadDim * 4;      // K rows of one chunk: 16 KB
 constexpr int kAxVRing = 8;                           // value-step buffers in flight
 constexpr int kAxVTok = 32;                           // positions per value step
@@ -42,6 +47,8 @@ constexpr int kAxVBytes = kAxVTok * (kHeadDim / 2) * 4;  // half-dim V rows of o
 constexpr int kAxVRingBytes = kAxVRing * kAxVBytes;
 static_assert(2 * kAxKBytes == kStageBytes, "two K chunks per ring slot");
 static_assert(kMaxGroup == 8 && kHeadDim == 128, "score layout: 8 heads x 2 tokens per half-warp");
+
+__host__ __device__ __forceinline__ int ax_nbufs(int M) { return M <= 1 ? kAxKBufsM1 : kAxKBufs; }
 
 // Small arrays of the score phase (floats from their base): rotated q by lane
 // [half-warp grp][head][2][slot][4] (dims (16 (j ^ grp) + slot, +64)), the
@@ -80,16 +87,17 @@ __shared__ int s_ax_nl, s_ax_long[kMaxSeqs];
 __shared__ int s_ax_hg;  // head groups per value item (the longest cache's scores of G / hg heads fit shared memory)
 __shared__ int s_ex_n, s_ex_m[kMaxSeqs];
 __shared__ int s_ax_lo, s_ax_hi;
-// Pool pages of the block's first kAxPgCap chunks (the second -1 when the
-// chunk has one page), so a refill needs no block-table load.
-constexpr int kAxPgCap = 256;
-__shared__ int2 s_ax_pg[kAxPgCap];
+// Descriptors of the block's first kAxTabCap chunks: x = m | g << 8, y = first
+// position, z / w = pool pages (w = -1 when the chunk has one page), so that
+// neither a chunk's scoring nor its refill searches the chunk list.
+constexpr int kAxTabCap = 256;
+__shared__ int4 s_ax_tab[kAxTabCap];
 
 // Per-block state of the K chunk loads, kept across the phases of a launch:
 // s_ax_full[j] completes when buffer j's copies land, s_ax_par bit j is the
 // parity of its next completion, s_ax_issued counts the chunks of the coming
 // (or running) score phase issued so far (chunk lo + i into buffer i %
-// kAxKBufs).
+// nbufs).
 __shared__ __align__(8) uint64_t s_ax_full[kAxKBufs];
 __shared__ uint32_t s_ax_par;
 __shared__ int s_ax_issued;
@@ -172,12 +180,22 @@ __device__ void ax_launch_init(const Ctx &c) {
     s_ax_hg = hg;
   }
   __syncthreads();
-  for (int i = threadIdx.x; i < s_ax_hi - s_ax_lo && i < kAxPgCap; i += kThreads) {
+  for (int i = threadIdx.x; i < s_ax_hi - s_ax_lo && i < kAxTabCap; i += kThreads) {
     const AxChunk k = ax_chunk(c, sp, s_ax_lo + i);
     const int *bt = sp.seq[k.m].bt;
-    s_ax_pg[i] = make_int2(__ldg(bt + k.t0 / kPageTokens),
-                           k.t0 + kPageTokens < s_ax_n[k.m] ? __ldg(bt + k.t0 / kPageTokens + 1) : -1);
+    s_ax_tab[i] = make_int4(k.m | (k.g << 8), k.t0, __ldg(bt + k.t0 / kPageTokens),
+                            k.t0 + kPageTokens < s_ax_n[k.m] ? __ldg(bt + k.t0 / kPageTokens + 1) : -1);
   }
+}
+
+// Descriptor of the block's chunk lo + i (from the table, or computed for the
+// chunks past its end).
+__device__ __forceinline__ int4 ax_desc(const Ctx &c, const StepParams &sp, int i) {
+  if (i < kAxTabCap) return s_ax_tab[i];
+  const AxChunk k = ax_chunk(c, sp, s_ax_lo + i);
+  const int *bt = sp.seq[k.m].bt;
+  return make_int4(k.m | (k.g << 8), k.t0, __ldg(bt + k.t0 / kPageTokens),
+                   k.t0 + kPageTokens < s_ax_n[k.m] ? __ldg(bt + k.t0 / kPageTokens + 1) : -1);
 }
 
 // K rows of (layer, kv head g) in pool page `page`: 8 KB (the V rows follow).
@@ -185,33 +203,27 @@ __device__ __forceinline__ const float *ax_page_k(const Ctx &c, int page, int la
   return c.kv_pool + (size_t)page * c.page_floats + ((size_t)layer * c.KVH + g) * 2 * kPageTokens * c.D;
 }
 
-// One thread: the K copies of the block's chunk lo + i into buffer i % kAxKBufs.
+// One thread: the K copies of the block's chunk lo + i into buffer i % nbufs.
 __device__ __forceinline__ void ax_issue(const Ctx &c, int layer, float *smem, int i) {
   const StepParams &sp = *c.sp;
-  const AxChunk k = ax_chunk(c, sp, s_ax_lo + i);
-  int2 pg;
-  if (i < kAxPgCap) {
-    pg = s_ax_pg[i];
-  } else {
-    const int *bt = sp.seq[k.m].bt;
-    pg = make_int2(__ldg(bt + k.t0 / kPageTokens),
-                   k.t0 + kPageTokens < s_ax_n[k.m] ? __ldg(bt + k.t0 / kPageTokens + 1) : -1);
-  }
+  const int4 d = ax_desc(c, sp, i);
+  const int g = d.x >> 8;
   constexpr uint32_t pb = kPageTokens * kHeadDim * 4;
-  const int b = i % kAxKBufs;
+  const int b = i % ax_nbufs(sp.M);
   float *buf = ax_kbuf(c, sp.M, smem, b);
   uint64_t *bar = &s_ax_full[b];
-  mbar_expect_tx(bar, (pg.y >= 0 ? 2u : 1u) * pb);
-  bulk_g2s(buf, ax_page_k(c, pg.x, layer, k.g), pb, bar);
-  if (pg.y >= 0) bulk_g2s(buf + kPageTokens * kHeadDim, ax_page_k(c, pg.y, layer, k.g), pb, bar);
+  mbar_expect_tx(bar, (d.w >= 0 ? 2u : 1u) * pb);
+  bulk_g2s(buf, ax_page_k(c, d.z, layer, g), pb, bar);
+  if (d.w >= 0) bulk_g2s(buf + kPageTokens * kHeadDim, ax_page_k(c, d.w, layer, g), pb, bar);
 }
 
 // One thread: issues the block's chunks while fewer than `upto` (at most
-// kAxKBufs) are in flight or done for the coming phase.
+// nbufs) are in flight or done for the coming phase.
 __device__ void ax_issue_upto(const Ctx &c, int layer, float *smem, int upto) {
   int i = s_ax_issued;
   const int nch = s_ax_hi - s_ax_lo;
-  if (upto > kAxKBufs) upto = kAxKBufs;
+  const int nb = ax_nbufs(c.sp->M);
+  if (upto > nb) upto = nb;
   if (i >= upto || i >= nch) return;
   // the buffers were last written by ordinary stores (or read) in earlier
   // phases: order those before the async copies
@@ -223,7 +235,7 @@ __device__ void ax_issue_upto(const Ctx &c, int layer, float *smem, int upto) {
 // Waits for chunk copies issued ahead of a score phase that did not run
 // (thread 0).
 __device__ __forceinline__ void ax_drain(const Ctx &c) {
-  for (int j = 0; j < s_ax_issued && j < kAxKBufs; j++) {
+  for (int j = 0; j < s_ax_issued && j < ax_nbufs(c.sp->M); j++) {
     mbar_wait(&s_ax_full[j], (s_ax_par >> j) & 1u, c.err);
     s_ax_par ^= 1u << j;
   }
@@ -313,6 +325,81 @@ __device__ void ax_load_q(const Ctx &c, const StepParams &sp, int m, int g, floa
   __syncthreads();
 }
 
+// Scores of the warp's tokens 4 warp .. 4 warp + 3 of NC chunks of one pair
+// (K rows in Kb[k], first positions t0[k]; the new position len takes the
+// rotated key knew): half grp takes tokens 4 warp + 2 grp + {0, 1}; lane slot
+// s multiplies dims s + 16 j (j = 0..7) and sums them as
+// ((p0+p1)+(p2+p3))+((p4+p5)+(p6+p7)) (packed in pairs (p_j, p_j+4)); the
+// reduce-scatter over the 16 slots (xor 8, 4, 2, 1: the reference's tree16)
+// leaves (token lane >> 3, head lane & 7) on each lane, returned in out[k]
+// times the attention scale.
+template <int NC>
+__device__ __forceinline__ void ax_score_chunks(const Ctx &c, const float *sm, const float *const *Kb, const int *t0,
+                                                int len, int G, float *out) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int slot = lane & 15, grp = lane >> 4;
+  const ulonglong2 *qlane = (const ulonglong2 *)(sm + kAxQs) + (grp * 8 * 2) * 16 + slot;
+  const float *knew = sm + kAxKnew;
+  float v[NC][16];
+  f2x kp[NC][2][4];
+#pragma unroll
+  for (int k = 0; k < NC; k++) {
+#pragma unroll
+    for (int tl = 0; tl < 2; tl++) {
+      const int tok = 4 * warp + 2 * grp + tl;
+      const float *kr = t0[k] + tok == len ? knew : Kb[k] + (size_t)tok * kHeadDim;
+#pragma unroll
+      for (int jj = 0; jj < 4; jj++) {
+        const int idx = 16 * (jj ^ grp) + slot;
+        kp[k][tl][jj] = f2_pack(kr[idx], kr[idx + 64]);
+      }
+    }
+  }
+  // products as the reference forms them, fmaf(q, k, +0) (its slot
+  // accumulators start at zero): a packed FMA whose zero addend is read at
+  // run time.  ptxas contracts a packed multiply followed by a packed add
+  // into an FMA even with explicit .rn, and folds a constant zero addend,
+  // either of which changes the sums' rounding.
+  const f2x z0 = f2_pack(c.fzero, c.fzero);
+#pragma unroll
+  for (int h = 0; h < 8; h++) {
+    const ulonglong2 qa = qlane[(2 * h) * 16], qb = qlane[(2 * h + 1) * 16];
+#pragma unroll
+    for (int k = 0; k < NC; k++) {
+#pragma unroll
+      for (int tl = 0; tl < 2; tl++) {
+        const f2x z = f2_add(f2_add(f2_fma(qa.x, kp[k][tl][0], z0), f2_fma(qa.y, kp[k][tl][1], z0)),
+                             f2_add(f2_fma(qb.x, kp[k][tl][2], z0), f2_fma(qb.y, kp[k][tl][3], z0)));
+        v[k][tl * 8 + h] = h < G ? __fadd_rn(f2_lo(z), f2_hi(z)) : 0.0f;
+      }
+    }
+  }
+#pragma unroll
+  for (int k = 0; k < NC; k++) {
+#pragma unroll
+    for (int q = 0; q < 8; q++) {
+      const bool up = lane & 8;
+      const float send = up ? v[k][q] : v[k][8 + q];
+      v[k][q] = __fadd_rn(up ? v[k][8 + q] : v[k][q], __shfl_xor_sync(0xffffffffu, send, 8));
+    }
+#pragma unroll
+    for (int q = 0; q < 4; q++) {
+      const bool up = lane & 4;
+      const float send = up ? v[k][q] : v[k][4 + q];
+      v[k][q] = __fadd_rn(up ? v[k][4 + q] : v[k][q], __shfl_xor_sync(0xffffffffu, send, 4));
+    }
+#pragma unroll
+    for (int q = 0; q < 2; q++) {
+      const bool up = lane & 2;
+      const float send = up ? v[k][q] : v[k][2 + q];
+      v[k][q] = __fadd_rn(up ? v[k][2 + q] : v[k][q], __shfl_xor_sync(0xffffffffu, send, 2));
+    }
+    const bool up = lane & 1;
+    const float send = up ? v[k][0] : v[k][1];
+    out[k] = __fmul_rn(__fadd_rn(up ? v[k][1] : v[k][0], __shfl_xor_sync(0xffffffffu, send, 1)), c.attn_scale);
+  }
+}
+
 // Phase 1: scores of the block's chunks (see the top of this file).
 __device__ __noinline__ void phase_attn_scores(const Ctx *cp, int layer, float *smem_arg) {
   float *const smem = dyn_smem();  // == smem_arg (the aligned dynamic base)
@@ -321,107 +408,63 @@ __device__ __noinline__ void phase_attn_scores(const Ctx *cp, int layer, float *
   const StepParams &sp = *c.sp;
   const int G = c.QH / c.KVH;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int slot = lane & 15, grp = lane >> 4;
-  const int lo = s_ax_lo, nch = s_ax_hi - s_ax_lo;
+  const int nch = s_ax_hi - s_ax_lo;
   if (nch <= 0) return;
+  const int M = sp.M, nb = ax_nbufs(M);
   rg_bmark(c, 1);
-  float *sm = ax_small(c, sp.M, smem);
-  if (threadIdx.x == 0) ax_issue_upto(c, layer, smem, kAxKBufs);
+  float *sm = ax_small(c, M, smem);
+  if (threadIdx.x == 0) ax_issue_upto(c, layer, smem, nb);
   const uint32_t par0 = s_ax_par;  // parity of each buffer's next completion
-  int qm = -1, qg = -1;
+  int qpair = -1;
 #pragma unroll 1
-  for (int i = 0; i < nch; i++) {
-    const AxChunk k = ax_chunk(c, sp, lo + i);
-    const int n = s_ax_n[k.m], len = n - 1;
-    if (k.m != qm || k.g != qg) {
-      ax_load_q(c, sp, k.m, k.g, sm);
-      qm = k.m;
-      qg = k.g;
+  for (int i = 0; i < nch;) {
+    const int4 d0 = ax_desc(c, sp, i);
+    const int4 d1 = i + 1 < nch ? ax_desc(c, sp, i + 1) : make_int4(-1, 0, 0, 0);
+    const int nc = d1.x == d0.x ? 2 : 1;  // two chunks of one pair
+    const int m = d0.x & 255, g = d0.x >> 8;
+    const int n = s_ax_n[m], len = n - 1;
+    if (d0.x != qpair) {
+      ax_load_q(c, sp, m, g, sm);
+      qpair = d0.x;
     }
-    const int b = i % kAxKBufs;
-    const float *Kb = ax_kbuf(c, sp.M, smem, b);
-    const float *knew = sm + kAxKnew;
-    mbar_wait(&s_ax_full[b], ((par0 >> b) ^ (uint32_t)(i / kAxKBufs)) & 1u, c.err);
+    const float *Kb[2];
+    const int t0[2] = {d0.y, d1.y};
+    for (int k = 0; k < nc; k++) {
+      const int b = (i + k) % nb;
+      Kb[k] = ax_kbuf(c, M, smem, b);
+      mbar_wait(&s_ax_full[b], ((par0 >> b) ^ (uint32_t)((i + k) / nb)) & 1u, c.err);
+    }
     if (i == 0) rg_bmark(c, 2);
-    // ---- scores of the warp's tokens 4 warp .. 4 warp + 3: half grp takes
-    // tokens 4 warp + 2 grp + {0, 1}; lane slot s multiplies dims s + 16 j
-    // (j = 0..7) and sums them as ((p0+p1)+(p2+p3))+((p4+p5)+(p6+p7)) (packed
-    // in pairs (p_j, p_j+4)); the reduce-scatter over the 16 slots (xor 8, 4,
-    // 2, 1: the reference's tree16) leaves (token lane >> 3, head lane & 7) on
-    // each lane
-    const ulonglong2 *qlane = (const ulonglong2 *)(sm + kAxQs) + (grp * 8 * 2) * 16 + slot;
-    float v[16];
-    {
-      f2x kp[2][4];
-#pragma unroll
-      for (int tl = 0; tl < 2; tl++) {
-        const int tok = 4 * warp + 2 * grp + tl;
-        const float *kr = k.t0 + tok == len ? knew : Kb + (size_t)tok * kHeadDim;
-#pragma unroll
-        for (int jj = 0; jj < 4; jj++) {
-          const int idx = 16 * (jj ^ grp) + slot;
-          kp[tl][jj] = f2_pack(kr[idx], kr[idx + 64]);
-        }
-      }
-      // products as the reference forms them, fmaf(q, k, +0) (its slot
-      // accumulators start at zero): a packed FMA whose zero addend is read at
-      // run time.  ptxas contracts a packed multiply followed by a packed add
-      // into an FMA even with explicit .rn, and folds a constant zero addend,
-      // either of which changes the sums' rounding.
-      const f2x z0 = f2_pack(c.fzero, c.fzero);
-#pragma unroll
-      for (int h = 0; h < 8; h++) {
-        const ulonglong2 qa = qlane[(2 * h) * 16], qb = qlane[(2 * h + 1) * 16];
-#pragma unroll
-        for (int tl = 0; tl < 2; tl++) {
-          const f2x z = f2_add(f2_add(f2_fma(qa.x, kp[tl][0], z0), f2_fma(qa.y, kp[tl][1], z0)),
-                               f2_add(f2_fma(qb.x, kp[tl][2], z0), f2_fma(qb.y, kp[tl][3], z0)));
-          v[tl * 8 + h] = h < G ? __fadd_rn(f2_lo(z), f2_hi(z)) : 0.0f;
-        }
+    float sc[2];
+    if (nc == 2) {
+      ax_score_chunks<2>(c, sm, Kb, t0, len, G, sc);
+    } else {
+      Kb[1] = Kb[0];
+      ax_score_chunks<1>(c, sm, Kb, t0, len, G, sc);
+    }
+    const int ld = ax_stride(n), h = lane & 7;
+    float *srow = c.att_s + s_ax_sb[m] + (size_t)g * G * ld;
+    for (int k = 0; k < nc; k++) {
+      const int t = t0[k] + 4 * warp + (lane >> 3);
+      if (t < n && h < G) __stcg(srow + (size_t)h * ld + t, sc[k]);
+      if (t0[k] <= len && len < t0[k] + kAxTok && ((len - t0[k]) >> 2) == warp) {
+        // the new position: appended to the cache (kvCache.append,
+        // internal/model/model.go:5593-5612)
+        const float *knew = sm + kAxKnew;
+        ((float4 *)kv_ptr(c, sp.seq[m].bt, layer, 0, g, len))[lane] = ((const float4 *)knew)[lane];
+        ((float4 *)kv_ptr(c, sp.seq[m].bt, layer, 1, g, len))[lane] = ((const float4 *)(knew + kHeadDim))[lane];
       }
     }
-#pragma unroll
-    for (int q = 0; q < 8; q++) {
-      const bool up = lane & 8;
-      const float send = up ? v[q] : v[8 + q];
-      v[q] = __fadd_rn(up ? v[8 + q] : v[q], __shfl_xor_sync(0xffffffffu, send, 8));
-    }
-#pragma unroll
-    for (int q = 0; q < 4; q++) {
-      const bool up = lane & 4;
-      const float send = up ? v[q] : v[4 + q];
-      v[q] = __fadd_rn(up ? v[4 + q] : v[q], __shfl_xor_sync(0xffffffffu, send, 4));
-    }
-#pragma unroll
-    for (int q = 0; q < 2; q++) {
-      const bool up = lane & 2;
-      const float send = up ? v[q] : v[2 + q];
-      v[q] = __fadd_rn(up ? v[2 + q] : v[q], __shfl_xor_sync(0xffffffffu, send, 2));
-    }
-    float s;
-    {
-      const bool up = lane & 1;
-      const float send = up ? v[0] : v[1];
-      s = __fmul_rn(__fadd_rn(up ? v[1] : v[0], __shfl_xor_sync(0xffffffffu, send, 1)), c.attn_scale);
-    }
-    {
-      const int t = k.t0 + 4 * warp + (lane >> 3), h = lane & 7;
-      if (t < n && h < G) __stcg(c.att_s + s_ax_sb[k.m] + (size_t)(k.g * G + h) * ax_stride(n) + t, s);
-    }
-    if (k.t0 <= len && len < k.t0 + kAxTok && ((len - k.t0) >> 2) == warp) {
-      // the new position: appended to the cache (kvCache.append,
-      // internal/model/model.go:5593-5612)
-      ((float4 *)kv_ptr(c, sp.seq[k.m].bt, layer, 0, k.g, len))[lane] = ((const float4 *)knew)[lane];
-      ((float4 *)kv_ptr(c, sp.seq[k.m].bt, layer, 1, k.g, len))[lane] = ((const float4 *)(knew + kHeadDim))[lane];
-    }
-    // every warp is done with buffer b (and, at a pair change, with q)
+    // every warp is done with the chunks' buffers (and, at a pair change,
+    // with q); the refills go out from two warps
     __syncthreads();
-    if (threadIdx.x == 0 && i + kAxKBufs < nch) ax_issue(c, layer, smem, i + kAxKBufs);
+    if (lane == 0 && warp < nc && i + warp + nb < nch) ax_issue(c, layer, smem, i + warp + nb);
+    i += nc;
   }
   if (threadIdx.x == 0) {
-    // chunk i completed a phase of buffer i % kAxKBufs
-    for (int b = 0; b < kAxKBufs; b++)
-      if (nch > b && (((nch - 1 - b) / kAxKBufs) & 1) == 0) s_ax_par ^= 1u << b;
+    // chunk i completed a phase of buffer i % nb
+    for (int b = 0; b < nb; b++)
+      if (nch > b && (((nch - 1 - b) / nb) & 1) == 0) s_ax_par ^= 1u << b;
     s_ax_issued = 0;
   }
   rg_bmark(c, 3);
@@ -491,11 +534,11 @@ __device__ __noinline__ void phase_attn_values(const Ctx *cp, int layer, float *
   // 8 and the last, exit
   unsigned long long *mk = c.trace && threadIdx.x == 0 ? c.trace + 4 * kTraceRows + kTraceMarks * blockIdx.x : nullptr;
   if (mk) mk[4] = clock64();
-  if (threadIdx.x == 0) {
+  if (lane == 0) {
     // the ring's buffers were last written by ordinary stores in earlier
     // phases; the scores and the new V rows were written by other blocks'
     // ordinary stores (ordered by the grid barrier) and are read by the
-    // async proxy
+    // async proxy (every warp's lane 0 issues copies)
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     asm volatile("fence.proxy.async.global;" ::: "memory");
   }
@@ -510,11 +553,14 @@ __device__ __noinline__ void phase_attn_values(const Ctx *cp, int layer, float *
     for (int i = threadIdx.x; i < (n + kPageTokens - 1) / kPageTokens && i < kAvPgCap; i += kThreads)
       s_av_pg[i] = __ldg(bt + i);
     __syncthreads();
+    // the scores by one bulk copy; the V steps from every warp (one thread
+    // issues bulk copies at about 24 GB/s): step st from warp st % 8
     if (threadIdx.x == 0) {
       mbar_expect_tx(&s_av_bar[kAxVRing], (uint32_t)(Gs * ld * 4));
       bulk_g2s(ssc, Sg, (uint32_t)(Gs * ld * 4), &s_av_bar[kAxVRing]);
-      for (int st = 0; st < kAxVRing && st < nst; st++) av_issue(c, bt, layer, g, half, st, n, smem);
     }
+    if (lane == 0)
+      for (int st = warp; st < kAxVRing && st < nst; st += kThreads / 32) av_issue(c, bt, layer, g, half, st, n, smem);
     mbar_wait(&s_av_bar[kAxVRing], (par >> kAxVRing) & 1u, c.err);
     if (mk && it == (int)blockIdx.x) mk[5] = clock64();
     // ---- softmax of head h0 + warp (warps < Gs), in place: scores ->
@@ -608,7 +654,8 @@ __device__ __noinline__ void phase_attn_values(const Ctx *cp, int layer, float *
       if (mk && mi && it == (int)blockIdx.x) mk[mi + 1] = clock64();
       // every warp is done with buffer b: it takes step st + kAxVRing
       __syncthreads();
-      if (threadIdx.x == 0 && st + kAxVRing < nst) av_issue(c, bt, layer, g, half, st + kAxVRing, n, smem);
+      if (lane == 0 && warp == st % (kThreads / 32) && st + kAxVRing < nst)
+        av_issue(c, bt, layer, g, half, st + kAxVRing, n, smem);
     }
     if (warp < Gs) {
       float2 r;
