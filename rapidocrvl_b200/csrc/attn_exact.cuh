@@ -84,7 +84,8 @@ __device__ __forceinline__ float *ax_small(const Ctx &c, int M, float *smem) {
 // first) and the short ones (in order); this block's chunk range.
 __shared__ int s_ax_n[kMaxSeqs], s_ax_cb[kMaxSeqs + 1], s_ax_sb[kMaxSeqs];
 __shared__ int s_ax_nl, s_ax_long[kMaxSeqs];
-__shared__ int s_ax_hg;  // head groups per value item (the longest cache's scores of G / hg heads fit shared memory)
+__shared__ int s_ax_hg;  // head groups per value item (the longest cache's scores of G / hg heads fit shared memory;
+                         // more groups when there are few long caches)
 __shared__ int s_ex_n, s_ex_m[kMaxSeqs];
 __shared__ int s_ax_lo, s_ax_hi;
 // Descriptors of the block's first kAxTabCap chunks: x = m | g << 8, y = first
@@ -177,6 +178,9 @@ __device__ void ax_launch_init(const Ctx &c) {
     if (nl > 0)
       while (hg < G && (size_t)(G / hg) * ax_stride(s_ax_n[s_ax_long[0]]) * 4 + kAxVRingBytes > (size_t)c.dyn_smem)
         hg *= 2;
+    // few long caches (single-sequence steps): more, smaller items (fewer
+    // heads each) spread over the blocks
+    while (hg < G && nl * c.KVH * 2 * hg * 2 <= (int)gridDim.x) hg *= 2;
     s_ax_hg = hg;
   }
   __syncthreads();
@@ -477,7 +481,11 @@ __device__ __noinline__ void phase_attn_scores(const Ctx *cp, int layer, float *
 // dims: 8 KB each; per page one 2-D TMA box of 64 dims x 16 rows from the
 // pool map), then the item's scores (G / hg heads x stride floats, one bulk
 // copy), which the item turns into exponentials and then weights in place.
-__shared__ __align__(8) uint64_t s_av_bar[kAxVRing + 1];  // value steps, then the scores
+// An item whose whole V half (all its pages) and scores fit shared memory
+// loads all pages at once instead ("whole" items: the boxes are requested from
+// every warp against one barrier, and the chains then run without a block
+// barrier per step).
+__shared__ __align__(8) uint64_t s_av_bar[kAxVRing + 2];  // value steps, the scores, an item's whole V
 __shared__ uint32_t s_av_par;                             // parity of each barrier's next completion
 constexpr int kAvPgCap = 576;                             // pages of an item held in shared memory (9,216 positions)
 __shared__ int s_av_pg[kAvPgCap];
@@ -486,7 +494,7 @@ __device__ __forceinline__ float *ax_vbuf(float *smem, int j) { return (float *)
 
 __device__ __forceinline__ void av_block_init() {
   if (threadIdx.x == 0) {
-    for (int j = 0; j <= kAxVRing; j++) mbar_init(&s_av_bar[j], 1);
+    for (int j = 0; j <= kAxVRing + 1; j++) mbar_init(&s_av_bar[j], 1);
     mbar_fence_init();
     s_av_par = 0;
   }
@@ -549,23 +557,38 @@ __device__ __noinline__ void phase_attn_values(const Ctx *cp, int layer, float *
     const int *bt = sp.seq[m].bt;
     const float *Sg = c.att_s + s_ax_sb[m] + ((size_t)g * G + h0) * ld;
     const int nst = (n + kAxVTok - 1) / kAxVTok;
+    const int npg = (n + kPageTokens - 1) / kPageTokens;
+    const bool whole = npg <= kAvPgCap && (size_t)npg * kPageTokens * 256 + (size_t)Gs * ld * 4 <= (size_t)c.dyn_smem;
+    float *ssc_i = whole ? smem + (size_t)npg * kPageTokens * 64 : ssc;
     const uint32_t par = s_av_par;
     for (int i = threadIdx.x; i < (n + kPageTokens - 1) / kPageTokens && i < kAvPgCap; i += kThreads)
       s_av_pg[i] = __ldg(bt + i);
     __syncthreads();
     // the scores by one bulk copy; the V steps from every warp (one thread
     // issues bulk copies at about 24 GB/s): step st from warp st % 8
+    // (the previous item wrote its weights over its scores with ordinary
+    // stores; the copies below reuse that memory)
+    if (lane == 0) asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     if (threadIdx.x == 0) {
       mbar_expect_tx(&s_av_bar[kAxVRing], (uint32_t)(Gs * ld * 4));
-      bulk_g2s(ssc, Sg, (uint32_t)(Gs * ld * 4), &s_av_bar[kAxVRing]);
+      bulk_g2s(ssc_i, Sg, (uint32_t)(Gs * ld * 4), &s_av_bar[kAxVRing]);
+      if (whole) mbar_expect_tx(&s_av_bar[kAxVRing + 1], (uint32_t)npg * kPageTokens * 64 * 4);
     }
-    if (lane == 0)
+    if (whole) {
+      __syncthreads();  // the expected bytes are registered before any box lands
+      if (lane == 0)
+        for (int p = warp; p < npg; p += kThreads / 32) {
+          const int row = (((s_av_pg[p] * c.L + layer) * c.KVH + g) * 2 + 1) * kPageTokens;
+          tma_2d(smem + (size_t)p * kPageTokens * 64, c.kv_map, 64 * half, row, &s_av_bar[kAxVRing + 1]);
+        }
+    } else if (lane == 0) {
       for (int st = warp; st < kAxVRing && st < nst; st += kThreads / 32) av_issue(c, bt, layer, g, half, st, n, smem);
+    }
     mbar_wait(&s_av_bar[kAxVRing], (par >> kAxVRing) & 1u, c.err);
     if (mk && it == (int)blockIdx.x) mk[5] = clock64();
     // ---- softmax of head h0 + warp (warps < Gs), in place: scores ->
     // exponentials (positions below nv) -> weights (times 1/sum, all n)
-    float *W = ssc + (size_t)(warp < Gs ? warp : 0) * ld;
+    float *W = ssc_i + (size_t)(warp < Gs ? warp : 0) * ld;
     if (warp < Gs) {
       float mx = -INFINITY;
       for (int i4 = lane; i4 < ld / 4; i4 += 32) {
@@ -616,8 +639,32 @@ __device__ __noinline__ void phase_attn_values(const Ctx *cp, int layer, float *
     if (mk && it == (int)blockIdx.x) mk[6] = clock64();
     // ---- value chains: warp h, dims 64 half + 2 lane, +1
     f2x o = 0ull;
+    if (whole) {
+      mbar_wait(&s_av_bar[kAxVRing + 1], (par >> (kAxVRing + 1)) & 1u, c.err);
+      if (warp < Gs) {
+        // o = w_0 v_0, then batches of 16 positions: their V pairs and
+        // weights loaded, then the FMAs in position order
+        const float *vb = smem + 2 * lane;
+        o = f2_mul(f2_pack(W[0], W[0]), *(const f2x *)vb);
+        int t = 1;
 #pragma unroll 1
-    for (int st = 0; st < nst; st++) {
+        for (; t + 16 <= n; t += 16) {
+          f2x v[16];
+          float w[16];
+#pragma unroll
+          for (int u = 0; u < 16; u++) {
+            v[u] = *(const f2x *)(vb + (t + u) * 64);
+            w[u] = W[t + u];
+          }
+#pragma unroll
+          for (int u = 0; u < 16; u++) o = f2_fma(f2_pack(w[u], w[u]), v[u], o);
+        }
+#pragma unroll 1
+        for (; t < n; t++) o = f2_fma(f2_pack(W[t], W[t]), *(const f2x *)(vb + t * 64), o);
+      }
+    }
+#pragma unroll 1
+    for (int st = 0; st < (whole ? 0 : nst); st++) {
       const int t0 = st * kAxVTok;
       const int b = st % kAxVRing;
       // step st's rows (use st / kAxVRing of buffer b)
@@ -666,8 +713,12 @@ __device__ __noinline__ void phase_attn_values(const Ctx *cp, int layer, float *
     if (threadIdx.x == 0) {
       // step i completed a phase of buffer i % kAxVRing; the scores one
       uint32_t p = par;
-      for (int j = 0; j < kAxVRing; j++)
-        if (nst > j && (((nst - 1 - j) / kAxVRing) & 1) == 0) p ^= 1u << j;
+      if (whole) {
+        p ^= 1u << (kAxVRing + 1);
+      } else {
+        for (int j = 0; j < kAxVRing; j++)
+          if (nst > j && (((nst - 1 - j) / kAxVRing) & 1) == 0) p ^= 1u << j;
+      }
       p ^= 1u << kAxVRing;
       s_av_par = p;
     }
