@@ -486,6 +486,7 @@ __device__ __noinline__ void phase_attn_scores(const Ctx *cp, int layer, float *
 // every warp against one barrier, and the chains then run without a block
 // barrier per step).
 __shared__ __align__(8) uint64_t s_av_bar[kAxVRing + 2];  // value steps, the scores, an item's whole V
+__shared__ __align__(8) uint64_t s_av_free[kAxVRing];     // value step buffers released by every warp
 __shared__ uint32_t s_av_par;                             // parity of each barrier's next completion
 constexpr int kAvPgCap = 576;                             // pages of an item held in shared memory (9,216 positions)
 __shared__ int s_av_pg[kAvPgCap];
@@ -495,6 +496,7 @@ __device__ __forceinline__ float *ax_vbuf(float *smem, int j) { return (float *)
 __device__ __forceinline__ void av_block_init() {
   if (threadIdx.x == 0) {
     for (int j = 0; j <= kAxVRing + 1; j++) mbar_init(&s_av_bar[j], 1);
+    for (int j = 0; j < kAxVRing; j++) mbar_init(&s_av_free[j], kThreads / 32);
     mbar_fence_init();
     s_av_par = 0;
   }
@@ -663,21 +665,24 @@ __device__ __noinline__ void phase_attn_values(const Ctx *cp, int layer, float *
         for (; t < n; t++) o = f2_fma(f2_pack(W[t], W[t]), *(const f2x *)(vb + t * 64), o);
       }
     }
+    // ring: buffer b serves steps b, b + kAxVRing, ...; every warp releases a
+    // step's buffer (s_av_free, whose completions pair with the buffer's
+    // loads, so one parity serves both) and the step one behind is refilled
+    // by the warp whose turn it is, so no block barrier runs per step
 #pragma unroll 1
     for (int st = 0; st < (whole ? 0 : nst); st++) {
       const int t0 = st * kAxVTok;
       const int b = st % kAxVRing;
-      // step st's rows (use st / kAxVRing of buffer b)
+      // step st's rows (use st / kAxVRing of buffer b); every warp waits for
+      // them, so that no warp's release of a later use of the buffer can
+      // count toward this one
       mbar_wait(&s_av_bar[b], ((par >> b) ^ (uint32_t)(st / kAxVRing)) & 1u, c.err);
-      const int mi = st == 0 ? 7 : st == 1 ? 9 : st == 8 ? 11 : st == nst - 1 ? 13 : 0;
-      if (mk && mi && it == (int)blockIdx.x) mk[mi] = clock64();
-      const float *vb = ax_vbuf(smem, b) + 2 * lane;
-      const float *wt = W + t0;
-      const int cnt = min(kAxVTok, n - t0);
       if (warp < Gs) {
-        // the chain o = fma(w_t, v_t, o) is sequential; a full step is
-        // unrolled so that the compiler issues its shared loads ahead of the
-        // FMAs (the chain then waits on the FMA latency, not on the loads)
+        const float *vb = ax_vbuf(smem, b) + 2 * lane;
+        const float *wt = W + t0;  // 16-byte aligned: rows start on 4-float boundaries, t0 % 32 == 0
+        const int cnt = min(kAxVTok, n - t0);
+        // the chain o = fma(w_t, v_t, o) is sequential; four weights per
+        // shared load, a batch's loads ahead of its FMAs
         int i = 0;
         if (st == 0) {
           const float w0 = wt[0];
@@ -686,9 +691,14 @@ __device__ __noinline__ void phase_attn_values(const Ctx *cp, int layer, float *
         }
         if (cnt == kAxVTok && i == 0) {
 #pragma unroll
-          for (int u = 0; u < kAxVTok; u++) {
-            const float wu = wt[u];
-            o = f2_fma(f2_pack(wu, wu), *(const f2x *)(vb + u * 64), o);
+          for (int u0 = 0; u0 < kAxVTok; u0 += 8) {
+            const float4 wa = *(const float4 *)(wt + u0), wb = *(const float4 *)(wt + u0 + 4);
+            const float w[8] = {wa.x, wa.y, wa.z, wa.w, wb.x, wb.y, wb.z, wb.w};
+            f2x v[8];
+#pragma unroll
+            for (int u = 0; u < 8; u++) v[u] = *(const f2x *)(vb + (u0 + u) * 64);
+#pragma unroll
+            for (int u = 0; u < 8; u++) o = f2_fma(f2_pack(w[u], w[u]), v[u], o);
           }
         } else {
 #pragma unroll 8
@@ -698,11 +708,16 @@ __device__ __noinline__ void phase_attn_values(const Ctx *cp, int layer, float *
           }
         }
       }
-      if (mk && mi && it == (int)blockIdx.x) mk[mi + 1] = clock64();
-      // every warp is done with buffer b: it takes step st + kAxVRing
-      __syncthreads();
-      if (lane == 0 && warp == st % (kThreads / 32) && st + kAxVRing < nst)
-        av_issue(c, bt, layer, g, half, st + kAxVRing, n, smem);
+      __syncwarp();
+      if (lane == 0) {
+        asm volatile("mbarrier.arrive.shared.b64 _, [%0];" ::"r"(smem_u32(&s_av_free[b])) : "memory");
+        const int rs = st - 1 + kAxVRing;  // the next step of the previous step's buffer
+        if (st >= 1 && rs < nst && warp == (st - 1) % (kThreads / 32)) {
+          const int bp = (st - 1) % kAxVRing;
+          mbar_wait(&s_av_free[bp], ((par >> bp) ^ (uint32_t)((st - 1) / kAxVRing)) & 1u, c.err, true);
+          av_issue(c, bt, layer, g, half, rs, n, smem);
+        }
+      }
     }
     if (warp < Gs) {
       float2 r;

@@ -405,10 +405,13 @@ __device__ __forceinline__ void tma_2d(void *dst, const TmapBytes *map, int x, i
 }
 // Bounded wait for phase `parity` of an mbarrier: at most kMbarSpins polls
 // and kMbarWaitNs of elapsed time (a poll may suspend the thread for a while).
-// On timeout the error word is set and false returned.
+// On timeout the error word is set and false returned.  `bail`: the wait also
+// ends once another thread has set the error word (for waits on other
+// threads' arrivals; a wait on the block's own copies runs until they land,
+// so that no copy is in flight when the block leaves).
 constexpr long long kMbarSpins = 1ll << 24;
 constexpr unsigned long long kMbarWaitNs = 2000000000ull;
-__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, int *err) {
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, int *err, bool bail = false) {
   uint32_t done = 0;
   long long spins = 0;
   unsigned long long t0 = 0;
@@ -422,7 +425,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, int *e
     if ((spins & 255) == 1) {
       const unsigned long long now = gtimer();
       if (spins == 1) t0 = now;
-      else if (now - t0 > kMbarWaitNs) spins = kMbarSpins + 1;
+      else if (now - t0 > kMbarWaitNs || (bail && err && *(volatile int *)err)) spins = kMbarSpins + 1;
     }
     if (spins > kMbarSpins) {
       if (err) atomicExch(err, 1);
