@@ -552,7 +552,12 @@ __device__ __noinline__ void phase_attn_values(const Ctx *cp, int layer, float *
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     asm volatile("fence.proxy.async.global;" ::: "memory");
   }
-  for (int it = blockIdx.x; it < items; it += gridDim.x) {
+  // items in rows of gridDim.x, longest first; even rows left to right over
+  // the blocks, odd rows right to left, so a block's items balance
+#pragma unroll 1
+  for (int row = 0; row * (int)gridDim.x < items; row++) {
+    const int it = row * gridDim.x + ((row & 1) ? gridDim.x - 1 - blockIdx.x : blockIdx.x);
+    if (it >= items) continue;
     const int pair = it / per_pair, sub = it % per_pair;
     const int m = s_ax_long[pair / c.KVH], g = pair % c.KVH, half = sub & 1, h0 = (sub >> 1) * Gs;
     const int n = s_ax_n[m], nv = n & ~15, ld = ax_stride(n);
@@ -587,7 +592,7 @@ __device__ __noinline__ void phase_attn_values(const Ctx *cp, int layer, float *
       for (int st = warp; st < kAxVRing && st < nst; st += kThreads / 32) av_issue(c, bt, layer, g, half, st, n, smem);
     }
     mbar_wait(&s_av_bar[kAxVRing], (par >> kAxVRing) & 1u, c.err);
-    if (mk && it == (int)blockIdx.x) mk[5] = clock64();
+    if (mk && row == 0) mk[5] = clock64();
     // ---- softmax of head h0 + warp (warps < Gs), in place: scores ->
     // exponentials (positions below nv) -> weights (times 1/sum, all n)
     float *W = ssc_i + (size_t)(warp < Gs ? warp : 0) * ld;
@@ -638,7 +643,7 @@ __device__ __noinline__ void phase_attn_values(const Ctx *cp, int layer, float *
       }
       __syncwarp();
     }
-    if (mk && it == (int)blockIdx.x) mk[6] = clock64();
+    if (mk && row == 0) mk[6] = clock64();
     // ---- value chains: warp h, dims 64 half + 2 lane, +1
     f2x o = 0ull;
     if (whole) {
@@ -738,7 +743,7 @@ __device__ __noinline__ void phase_attn_values(const Ctx *cp, int layer, float *
       s_av_par = p;
     }
     __syncthreads();  // the scores' copy and s_av_par are settled for the next item
-    if (mk && it == (int)blockIdx.x) mk[15] = clock64();
+    if (mk && row == 0) mk[15] = clock64();
   }
 }
 
