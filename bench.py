@@ -21,7 +21,12 @@ with its own ms_per_step, roofline and e2e:
   configs4  Q8, 512 requests with prompts U[1024, 8192] (seed 3) and 256 new
             tokens each, partitioned over the N GPUs (no collective), each GPU
             running a continuous batch of up to 64 live sequences; value =
-            all requests' tokens / max over ranks of the summed step times.
+            all requests' tokens / max over ranks of the summed step times;
+  gemv      quant-GEMV HBM GB/s: the op-level matvec kernel (k_gemv) on
+            lm_head-sized matrices (103,424 x 1,024, one input vector) for
+            Q4/Q6/Q8 and the row-sum kernel (k_rowsum), each call on another
+            of several weight copies (together over twice the L2), CUDA events
+            around 20 calls (1 GPU runs only).
 Prompt caches of configs3 and configs4 are seeded synthetic K/V written on the
 device (the decode time does not depend on the cached values; the reference
 prefills token by token, untimed here).
@@ -56,7 +61,7 @@ def parse():
     ap.add_argument("--impl", default="cuda", choices=["cuda", "reference"])
     ap.add_argument("--quant", default="q4", choices=["q4", "q6", "q8"])
     ap.add_argument("--prompt", type=int, default=PROMPT)
-    ap.add_argument("--workload", default="all", choices=["all", "configs1", "configs0", "configs3", "configs4"],
+    ap.add_argument("--workload", default="all", choices=["all", "configs1", "configs0", "configs3", "configs4", "gemv"],
                     help="all: configs1 headline plus the other configurations' keys; otherwise one of them alone")
     ap.add_argument("--ctx-hi", type=int, default=4096, help="configs3: contexts U[256, ctx_hi] (profiling: smaller)")
     ap.add_argument("--requests", type=int, default=512, help="configs4: requests over all GPUs")
@@ -374,6 +379,72 @@ def batched_workload(quant, n, ctx_hi, steps, warmup, rank, device):
     return res
 
 
+def gemv_workload(reps=20):
+    """Quant-GEMV bandwidth of the op-level kernels: ocrvl_op_matvec (k_gemv)
+    on lm_head-sized matrices with one input vector, per quantization type, and
+    ocrvl_op_rowsum (k_rowsum).  Weight bytes are random (every byte pattern is
+    a valid Q4/Q6/Q8 row); successive calls use different copies so that the
+    weights stream from HBM.  Algorithmic bytes per call: packed rows + f32
+    scales (+ int32 row sums for the int8-activation types) + input + output."""
+    import ctypes as C
+
+    import torch
+
+    from rapidocrvl_b200 import _lib, gguf
+
+    L = _lib.load()
+    rows, cols = 103424, 1024
+    stream = torch.cuda.current_stream()
+    sh = C.c_void_p(stream.cuda_stream)
+    ptr = lambda t: C.c_void_p(t.data_ptr())  # noqa: E731
+    peak, src = hbm_peak()
+    res = {}
+    g = torch.Generator(device="cuda").manual_seed(5)
+    for name, typ in (("q4", gguf.Q4_ROW), ("q6", gguf.Q6_ROW), ("q8", gguf.Q8_ROW)):
+        pitch = gguf.packed_row_bytes(typ, cols)
+        copies = max(2, -(-300_000_000 // (rows * pitch)))
+        ws = [torch.randint(0, 256, (rows, pitch), dtype=torch.uint8, device="cuda", generator=g) for _ in range(copies)]
+        sc = torch.rand(rows, device="cuda", generator=g) * 1e-3 + 1e-4
+        rs = [torch.empty(rows, dtype=torch.int32, device="cuda") for _ in range(copies)]
+        x = torch.randn(cols, device="cuda", generator=g)
+        out = torch.empty(rows, device="cuda")
+        for i in range(copies):
+            _lib.check(L.ocrvl_op_rowsum(typ, rows, cols, ptr(ws[i]), ptr(rs[i]), sh))
+        for i in range(3):  # warm-up
+            _lib.check(L.ocrvl_op_matvec(typ, rows, cols, ptr(ws[i % copies]), ptr(sc), ptr(rs[i % copies]), 1, ptr(x),
+                                         None, 0.0, ptr(out), sh))
+        ev0, ev1 = events()
+        torch.cuda.synchronize()
+        ev0.record(stream)
+        for i in range(reps):
+            _lib.check(L.ocrvl_op_matvec(typ, rows, cols, ptr(ws[i % copies]), ptr(sc), ptr(rs[i % copies]), 1, ptr(x),
+                                         None, 0.0, ptr(out), sh))
+        ev1.record(stream)
+        torch.cuda.synchronize()
+        us = ev0.elapsed_time(ev1) * 1e3 / reps
+        nbytes = rows * (pitch + 4 + (4 if typ != gguf.Q8_ROW else 0)) + cols * 4 + rows * 4
+        gbs = nbytes / (us * 1e-6) / 1e9
+        res[name] = {"kernel": "k_gemv", "us_per_call": us, "algorithmic_bytes": nbytes, "achieved_gbs": gbs,
+                     "frac": gbs / peak}
+        if name == "q4":
+            e0, e1 = events()
+            e0.record(stream)
+            for i in range(reps):
+                _lib.check(L.ocrvl_op_rowsum(typ, rows, cols, ptr(ws[i % copies]), ptr(rs[i % copies]), sh))
+            e1.record(stream)
+            torch.cuda.synchronize()
+            us_r = e0.elapsed_time(e1) * 1e3 / reps
+            rb = rows * (pitch + 4)
+            res["rowsum_q4"] = {"kernel": "k_rowsum", "us_per_call": us_r, "algorithmic_bytes": rb,
+                                "achieved_gbs": rb / (us_r * 1e-6) / 1e9, "frac": rb / (us_r * 1e-6) / 1e9 / peak}
+        del ws, rs
+        torch.cuda.empty_cache()
+    res["peak_gbs"] = peak
+    res["peak_source"] = src
+    res["shape"] = f"{rows} x {cols}, one input vector, {reps} calls over rotating weight copies (> 2x L2)"
+    return res
+
+
 def sweep_workload(n_requests, rank, world, device, new_tokens=256, max_live=64):
     """configs4: Q8, n_requests requests (prompts U[1024, 8192], seed 3),
     new_tokens greedy tokens each, partitioned over the ranks by predicted KV
@@ -514,6 +585,8 @@ def run_cuda(args):
             "e2e": {"value": 64 * steps3 / (r["ms_e2e"] / 1e3), "unit": UNIT, "h2d_bytes_per_step": r["io"][0],
                     "d2h_bytes_per_step": r["io"][1]},
             "gpu_launches": steps3}
+    if world == 1 and want in ("all", "gemv"):
+        extra["gemv"] = gemv_workload()
     if want in ("all", "configs4"):
         if pg:
             pg.barrier()
@@ -534,7 +607,13 @@ def run_cuda(args):
             "e2e": {"value": tokens / (ms_max / 1e3), "unit": UNIT, "h2d_bytes_per_step": r["io"][0],
                     "d2h_bytes_per_step": r["io"][1],
                     "note": "every step is a C-ABI ocrvl_step with host ids in and out"}}
-    if line is None:
+    if line is None and want == "gemv":
+        obj = extra["gemv"]
+        line = {"metric": METRIC, "value": obj["q4"]["achieved_gbs"], "unit": "GB/s", "n_gpus": world,
+                "steps": 20, "warmup": 3, "ms_per_step": obj["q4"]["us_per_call"] / 1e3, "higher_is_better": True,
+                "scaling": "weak", "vs_baseline": None, "dtype": "i8/f32", "data": "synthetic random weights",
+                "config": {"workload": "quant-GEMV (k_gemv) Q4, " + obj["shape"]}, "gemv": obj}
+    elif line is None:
         # a single non-headline workload: its object is the line
         (name, obj), = extra.items()
         line = {"metric": METRIC, "value": obj["value"], "unit": UNIT, "n_gpus": world, "steps": args.steps,
