@@ -328,7 +328,7 @@ def is_quantized_text_tensor(name: str, shape, cfg) -> bool:
     return want is not None and tuple(int(d) for d in shape) == want
 
 
-def _metadata(cfg, quant: str, n_tensors: int, n_f32: int, n_quant: int):
+def _metadata(cfg, quant: str, n_tensors: int, n_f32: int, n_quant: int, n_shards: int = 1):
     file_type = {"q8": 7, "q6": 6, "q4": 3}.get(quant, 0)
     kvs = [
         ("general.architecture", META_STR, "paddleocrvl"),
@@ -338,7 +338,7 @@ def _metadata(cfg, quant: str, n_tensors: int, n_f32: int, n_quant: int):
         ("paddleocrvl.gguf_version", META_U32, VERSION),
         ("paddleocrvl.quantization", META_STR, quant or "f32"),
         ("paddleocrvl.source_tensors", META_U64, n_tensors),
-        ("paddleocrvl.source_shards", META_U64, 1),
+        ("paddleocrvl.source_shards", META_U64, n_shards),
         ("paddleocrvl.f32_tensors", META_U64, n_f32),
         ("paddleocrvl.quantized_tensors", META_U64, n_quant),
     ]
@@ -357,9 +357,12 @@ def _pack_str(s: str) -> bytes:
     return struct.pack("<Q", len(b)) + b
 
 
-def convert(tensors, dst: str, cfg, quantization: str = "q8") -> None:
+def convert(tensors, dst: str, cfg, quantization: str = "q8", shards: int = 1, progress=None) -> None:
     """Write ``tensors`` (name -> float32 ndarray, or an object with ``shape``
-    and ``materialize()``, materialized in sorted name order) as a GGUF file."""
+    and ``materialize()``, materialized in sorted name order) as a GGUF file.
+    ``shards``: the source checkpoint's file count (metadata); ``progress``:
+    called as progress(done, total, name, type_name) before each tensor and
+    once at the end (ConvertOptions.Progress, internal/gguf/convert.go:37-40)."""
     quant = (quantization or "f32").strip().lower()
     if quant not in ("f32", "q8", "q6", "q4"):
         raise ValueError(f"unsupported quantization {quantization!r}")
@@ -381,7 +384,7 @@ def convert(tensors, dst: str, cfg, quantization: str = "q8") -> None:
         off += tensor_bytes(typ, shape)
     hdr = bytearray()
     hdr += MAGIC + struct.pack("<I", VERSION)
-    kvs = _metadata(cfg, quant, len(names), n_f32, n_q)
+    kvs = _metadata(cfg, quant, len(names), n_f32, n_q, shards)
     hdr += struct.pack("<QQ", len(infos), len(kvs))
     for key, typ, val in kvs:
         hdr += _pack_str(key) + struct.pack("<I", typ)
@@ -401,7 +404,9 @@ def convert(tensors, dst: str, cfg, quantization: str = "q8") -> None:
     with open(tmp, "wb") as f:
         f.write(hdr)
         cur = 0
-        for name, shape, typ, o in infos:
+        for i, (name, shape, typ, o) in enumerate(infos):
+            if progress is not None:
+                progress(i, len(infos), name, TYPE_NAMES.get(typ, str(typ)))
             if cur < o:
                 f.write(b"\0" * (o - cur))
                 cur = o
@@ -414,4 +419,6 @@ def convert(tensors, dst: str, cfg, quantization: str = "q8") -> None:
                 b = sc.astype(np.float32).tobytes() + packed.tobytes()
             f.write(b)
             cur += len(b)
+    if progress is not None:
+        progress(len(infos), len(infos), "", "")
     os.replace(tmp, dst)
