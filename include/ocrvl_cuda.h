@@ -171,6 +171,30 @@ int ocrvl_step(ocrvl_model *m, ocrvl_seq *const *seqs, int n, const int32_t *ids
 int ocrvl_generate_greedy(ocrvl_model *m, const int32_t *ids, int n_ids, int max_new, const int32_t *eos,
                           int n_eos, int32_t *out, int out_cap, int *n_out);
 
+/* One decode step (as ocrvl_step with need_logits = 1) whose next ids are
+ * drawn by the reference's generation-loop sampler on its CPU backend
+ * (Runtime.GenerateWithOptions' sampling, internal/model/model.go:1536-1544,
+ * 3611-3642, 7202-7233), on the device from the step's logits:
+ *   temperature <= 0 or top_k == 1  argmax (ocrvl_step's greedy id, no draw)
+ *   2 <= top_k < vocab_size         the top_k logits, ties to the lower id,
+ *       in descending order (MatVecTopK*WithWork, internal/tensor/topk.go:
+ *       326-347), drawn by sampleCandidateScoresScratch (model.go:1929-1976);
+ *       top_k <= 4096
+ *   top_k == 0 or >= vocab_size     the full logits (sampleFullLogitsScratch,
+ *       model.go:2215-2307); vocab_size must be a multiple of 16
+ * rng_state: n fastRNG states (model.go:1829-1852), one per sequence, each
+ * advanced by one draw per sampled token; NULL only for argmax.  A negative
+ * temperature counts as 0 (the reference validates it before generation). */
+int ocrvl_step_sample(ocrvl_model *m, ocrvl_seq *const *seqs, int n, const int32_t *ids, const float *embeds,
+                      const int32_t *pos_thw, double temperature, int top_k, uint64_t *rng_state, int32_t *out_ids);
+
+/* Runtime.GenerateWithOptions (internal/model/model.go:1492-1572): greedy as
+ * ocrvl_generate_greedy when temperature <= 0 or top_k == 1, else sampled
+ * through ocrvl_step_sample with one RNG started at uint64(seed)
+ * (samplingRNGInto, model.go:1846-1852). */
+int ocrvl_generate(ocrvl_model *m, const int32_t *ids, int n_ids, int max_new, const int32_t *eos, int n_eos,
+                   double temperature, int top_k, int64_t seed, int32_t *out, int out_cap, int *n_out);
+
 /* Greedy decode of `steps` tokens for n sequences with the token feedback
  * kept on the device (the decode loop of GenerateWithOptions,
  * internal/model/model.go:1538-1568, without the per-token EOS check): the
@@ -238,6 +262,14 @@ int ocrvl_op_argmax(int type, int rows, int cols, const void *w, const float *sc
  * must be ordered by the caller. */
 int ocrvl_op_argmax_noalloc(int type, int rows, int cols, const void *w, const float *scale,
                             const int32_t *rowsum, int m, const float *x, int32_t *ids, void *stream);
+
+/* The sampler of ocrvl_step_sample on m rows of logits ([m][vocab] device
+ * floats): out_ids[m], rng_state[m] (device uint64, advanced), optional
+ * cand_ids / cand_scores ([m][top_k], top-k path only: the candidates in the
+ * order sampleCandidateScoresScratch sees them), work ([m][vocab] floats,
+ * full-vocabulary path only).  No allocation. */
+int ocrvl_op_sample(int m, int vocab, const float *logits, double temperature, int top_k, uint64_t *rng_state,
+                    int32_t *out_ids, int32_t *cand_ids, float *cand_scores, float *work, void *stream);
 
 /* out = RMSNorm(x, w, eps) for m vectors of n (tensor.RMSNorm). */
 int ocrvl_op_rmsnorm(int n, int m, const float *x, const float *w, float eps, float *out, void *stream);

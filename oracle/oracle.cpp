@@ -511,6 +511,225 @@ int argmax_matvec(const QMat &m, const float *x, float *best) {
 }
 
 // ---------------------------------------------------------------------------
+// Sampling (internal/model/model.go:1821-2828; internal/tensor/topk.go,
+// cumsum.go, weighted_sum.go:314-328 -> dot_amd64.s:6886-6996).  The
+// generation loop's CPU path (model.go:1536-1544, 3632-3642): top_k in
+// [2, vocab) takes the lm_head top-k candidates (MatVecTopK*WithWork) and
+// sampleCandidateScoresScratch; top_k <= 0 or >= vocab samples the full
+// logits (sampleTokenScratch -> sampleFullLogitsScratch) with a weight
+// scratch; temperature <= 0 or top_k == 1 is the argmax.  One RNG draw per
+// sampled token.
+// ---------------------------------------------------------------------------
+
+// fastRNG.Float64 (model.go:1833-1840): splitmix64 step, top 53 bits.
+double rng_float64(uint64_t &state) {
+  state += 0x9e3779b97f4a7c15ull;
+  uint64_t z = state;
+  z = (z ^ (z >> 30)) * 0xbf58476d1ce4e5b9ull;
+  z = (z ^ (z >> 27)) * 0x94d049bb133111ebull;
+  z ^= z >> 31;
+  return (double)(z >> 11) * (1.0 / 9007199254740992.0);
+}
+
+// topKSelectWithWork (topk.go:326-347): partial selection sort, the k
+// highest scores with ties to the lower id, in descending order.
+void topk_select(const float *logits, int n, int k, int *ids, float *scores) {
+  if (k > n) k = n;
+  std::vector<int> id(n);
+  std::vector<float> sc(logits, logits + n);
+  for (int i = 0; i < n; i++) id[i] = i;
+  for (int i = 0; i < k; i++) {
+    int best = i;
+    for (int j = i + 1; j < n; j++)
+      if (sc[j] > sc[best] || (sc[j] == sc[best] && id[j] < id[best])) best = j;
+    if (best != i) {
+      std::swap(sc[i], sc[best]);
+      std::swap(id[i], id[best]);
+    }
+  }
+  for (int i = 0; i < k; i++) {
+    ids[i] = id[i];
+    scores[i] = sc[i];
+  }
+}
+
+inline float max32_local(float a, float b) { return b > a ? b : a; }  // model.go:2468-2473
+
+// sampleCandidateScoresSmall (model.go:1978-2034), temperature != 1, <= 4 candidates.
+int sample_small(const int *ids, const float *s, int k, float inv, float mx, uint64_t &rng) {
+  if (k == 0) return 0;
+  if (k == 1) return ids[0];
+  if (k == 2) {
+    float s0 = s[0] * inv, s1 = s[1] * inv;
+    if (s0 >= s1) {
+      double w1 = fast_exp(s1 - s0);
+      return rng_float64(rng) * (1 + w1) <= 1 ? ids[0] : ids[1];
+    }
+    double w0 = fast_exp(s0 - s1);
+    return rng_float64(rng) * (w0 + 1) <= w0 ? ids[0] : ids[1];
+  }
+  double w[4];
+  for (int i = 0; i < k; i++) w[i] = fast_exp(s[i] * inv - mx);
+  double pick = rng_float64(rng) * (k == 3 ? (w[0] + w[1]) + w[2] : (w[0] + w[1]) + (w[2] + w[3]));
+  double acc = w[0];
+  if (pick <= acc) return ids[0];
+  acc += w[1];
+  if (pick <= acc) return ids[1];
+  if (k == 3) return ids[2];
+  acc += w[2];
+  if (pick <= acc) return ids[2];
+  return ids[3];
+}
+
+// sampleCandidateScoresTemp1Small (model.go:2140-2209), <= 4 candidates.
+int sample_temp1_small(const int *ids, const float *s, int k, float mx, uint64_t &rng) {
+  if (k == 0) return 0;
+  if (k == 1) return ids[0];
+  if (k == 2) {
+    float s0 = s[0], s1 = s[1];
+    if (s0 >= s1) {
+      double w1 = fast_exp(s1 - s0);
+      return rng_float64(rng) * (1 + w1) <= 1 ? ids[0] : ids[1];
+    }
+    double w0 = fast_exp(s0 - s1);
+    return rng_float64(rng) * (w0 + 1) <= w0 ? ids[0] : ids[1];
+  }
+  float w[4];
+  for (int i = 0; i < k; i++) w[i] = fast_exp(s[i] - mx);
+  if (k == 3) {
+    float pick = (float)rng_float64(rng) * ((w[0] + w[1]) + w[2]);
+    if (pick <= w[0]) return ids[0];
+    if (pick <= w[0] + w[1]) return ids[1];
+    return ids[2];
+  }
+  float pick = (float)rng_float64(rng) * ((w[0] + w[1]) + (w[2] + w[3]));
+  float acc = w[0];
+  if (pick <= acc) return ids[0];
+  acc += w[1];
+  if (pick <= acc) return ids[1];
+  acc += w[2];
+  if (pick <= acc) return ids[2];
+  return ids[3];
+}
+
+// sampleCandidateScoresScratch (model.go:1929-1976) with a weight scratch:
+// temperature 1 -> float32 weights and sums (sampleCandidateScoresTemp1Scratch
+// + pickWeightedRawFloat32, model.go:2036-2061, 2418-2462); otherwise float32
+// weights summed in float64 (pickWeightedFloat32, model.go:2342-2416).
+int sample_candidates(const int *ids, const float *s, int k, double temp, uint64_t &rng) {
+  if (k == 0) return 0;
+  if (temp == 1) {
+    float mx = s[0];
+    for (int i = 1; i < k; i++) mx = max32_local(mx, s[i]);
+    if (k <= 4) return sample_temp1_small(ids, s, k, mx, rng);
+    std::vector<float> w(k);
+    float sum = 0;
+    for (int i = 0; i < k; i++) {
+      w[i] = fast_exp(s[i] - mx);
+      sum += w[i];
+    }
+    float pick = (float)rng_float64(rng) * sum;
+    float acc = 0;
+    for (int i = 0; i < k; i++) {
+      acc += w[i];
+      if (pick <= acc) return ids[i];
+    }
+    return ids[k - 1];
+  }
+  float inv = (float)(1 / temp);
+  float raw = s[0];
+  for (int i = 1; i < k; i++) raw = max32_local(raw, s[i]);
+  float mx = raw * inv;
+  if (k <= 4) return sample_small(ids, s, k, inv, mx, rng);
+  std::vector<float> w(k);
+  double sum = 0;
+  for (int i = 0; i < k; i++) {
+    w[i] = fast_exp(s[i] * inv - mx);
+    sum += (double)w[i];
+  }
+  double pick = rng_float64(rng) * sum;
+  double acc = 0;
+  for (int i = 0; i < k; i++) {
+    acc += (double)w[i];
+    if (pick <= acc) return ids[i];
+  }
+  return ids[k - 1];
+}
+
+// sampleFullLogitsScratch / sampleFullLogitsTemp1Scratch with a weight
+// scratch (model.go:2215-2307): weights = ExpScaledVec(logits, 1/temp,
+// -max*inv) (expScaledVecFMA: x*scale, + bias, vector exp; 16 lane sums,
+// tree16), CumulativeSum (cumsum.go:9-58: one chain below 4096, else four
+// blocks of ceil(n/4) with the earlier blocks' sums added), pick =
+// float32(u) * sum, pickCumulativeFloat32's binary search (model.go:
+// 2326-2340).  The vector kernel processes whole 16-float blocks only and
+// leaves the last n % 16 weights unset (stale scratch), so only n % 16 == 0
+// is restated; returns -2 otherwise.
+int sample_full(const float *logits, int n, float temp, uint64_t &rng) {
+  if (n < 16 || n % 16 != 0) return -2;
+  float inv = temp == 1 ? 1.0f : 1.0f / temp;
+  float mx = logits[0];
+  for (int i = 1; i < n; i++) mx = std::max(mx, logits[i]);
+  float bias = -(mx * inv);
+  std::vector<float> w(n);
+  float lanes[16] = {0};
+  for (int i = 0; i < n; i += 16)
+    for (int l = 0; l < 16; l++) {
+      w[i + l] = exp_fma(logits[i + l] * inv + bias);
+      lanes[l] = lanes[l] + w[i + l];
+    }
+  float sum = tree16(lanes);
+  if (n < 4096) {
+    float cs = 0;
+    for (int i = 0; i < n; i++) w[i] = cs = cs + w[i];
+  } else {
+    int bs = (n + 3) / 4;
+    float bsum[4] = {0, 0, 0, 0};
+    for (int b = 0; b < 4; b++) {
+      int st = b * bs, en = std::min(n, st + bs);
+      float cs = 0;
+      for (int i = st; i < en; i++) w[i] = cs = cs + w[i];
+      if (st < en) bsum[b] = cs;
+    }
+    float off = bsum[0];
+    for (int b = 1; b < 4; b++) {
+      int st = b * bs, en = std::min(n, st + bs);
+      for (int i = st; i < en; i++) w[i] = w[i] + off;
+      off = off + bsum[b];
+    }
+  }
+  float pick = (float)rng_float64(rng) * sum;
+  int lo = 0, hi = n;
+  while (lo < hi) {
+    int mid = (int)((unsigned)(lo + hi) >> 1);
+    if (pick <= w[mid]) hi = mid;
+    else lo = mid + 1;
+  }
+  return lo < n ? lo : n - 1;
+}
+
+// First index of the maximum (the greedy path's tie rule).
+int argmax_first(const float *x, int n) {
+  int bi = 0;
+  for (int i = 1; i < n; i++)
+    if (x[i] > x[bi]) bi = i;
+  return bi;
+}
+
+// The generation loop's choice of sampler (model.go:1536-1544, 1854-1868,
+// 3611-3642, 7202-7205): <0 unsupported.
+int sample_token(const float *logits, int n, double temperature, int top_k, uint64_t &rng) {
+  if (temperature <= 0 || top_k == 1) return argmax_first(logits, n);
+  if (top_k > 1 && top_k < n) {
+    std::vector<int> ids(top_k);
+    std::vector<float> sc(top_k);
+    topk_select(logits, n, top_k, ids.data(), sc.data());
+    return sample_candidates(ids.data(), sc.data(), top_k, temperature, rng);
+  }
+  return sample_full(logits, n, (float)temperature, rng);
+}
+
+// ---------------------------------------------------------------------------
 // GGUF reader (internal/gguf/gguf.go:111-251, 435-569)
 // ---------------------------------------------------------------------------
 struct TensorMeta {
@@ -925,6 +1144,46 @@ int orc_generate(void *model, const int *ids, int n_ids, int max_new, const int 
   return rc == 0 ? n : rc;
 }
 
+// Sampled generation (Runtime.GenerateWithOptions, model.go:1492-1572): the
+// RNG state starts at uint64(seed) (samplingRNGInto, model.go:1846-1852) and
+// each generated token is drawn by sample_token from the full logits.
+int orc_generate_sampled(void *model, const int *ids, int n_ids, int max_new, const int *eos, int n_eos,
+                         double temperature, int top_k, int64_t seed, int *out, int out_cap) {
+  Model *m = (Model *)model;
+  if (max_new < 0) return -1;
+  for (int i = 0; i < n_ids; i++)
+    if (ids[i] < 0 || ids[i] >= m->cfg.vocab_size) return -1;
+  if (out_cap < n_ids) return -1;
+  for (int i = 0; i < n_ids; i++) out[i] = ids[i];
+  if (max_new == 0) return n_ids;
+  if (n_ids == 0) return -1;
+  static const int def_eos[1] = {2};
+  if (!eos) { eos = def_eos; n_eos = 1; }
+  const int V = m->cfg.vocab_size;
+  uint64_t rng = (uint64_t)seed;
+  Seq *s = (Seq *)orc_seq_new(model, n_ids + max_new);
+  std::vector<float> emb(m->cfg.hidden_size), logits(V);
+  int tok = 0, n = n_ids, rc = 0;
+  for (int p = 0; p < n_ids && rc == 0; p++) {
+    orc_embed(model, ids[p], emb.data());
+    rc = forward(*m, *s, emb.data(), p, p, p, p == n_ids - 1, &tok, logits.data(), nullptr);
+  }
+  for (int i = 0; rc == 0 && i < max_new; i++) {
+    if (n >= out_cap) { rc = -1; break; }
+    tok = sample_token(logits.data(), V, temperature, top_k, rng);
+    if (tok < 0) { rc = tok; break; }
+    out[n++] = tok;
+    bool stop = false;
+    for (int j = 0; j < n_eos; j++) stop |= tok == eos[j];
+    if (stop || i + 1 >= max_new) break;
+    orc_embed(model, tok, emb.data());
+    int p = n - 1;
+    rc = forward(*m, *s, emb.data(), p, p, p, 1, &tok, logits.data(), nullptr);
+  }
+  orc_seq_free(s);
+  return rc == 0 ? n : rc;
+}
+
 int orc_decode_steps(void *model, void *seq, int tok, int pos, int steps) {
   Model *m = (Model *)model;
   Seq *s = (Seq *)seq;
@@ -1021,6 +1280,19 @@ void orc_softmax(float *x, int n) { softmax(x, n); }
 void orc_attention(const float *q, const float *kc, const float *vc, int n, int heads, int kvh, int dim,
                    float *out) {
   attention(q, kc, vc, n, heads, kvh, dim, out);
+}
+double orc_rng_float64(uint64_t *state) { return rng_float64(*state); }
+void orc_topk_select(const float *logits, int n, int k, int *ids, float *scores) {
+  topk_select(logits, n, k, ids, scores);
+}
+int orc_sample_candidates(const int *ids, const float *scores, int k, double temperature, uint64_t *state) {
+  return sample_candidates(ids, scores, k, temperature, *state);
+}
+int orc_sample_full(const float *logits, int n, float temperature, uint64_t *state) {
+  return sample_full(logits, n, temperature, *state);
+}
+int orc_sample_token(const float *logits, int n, double temperature, int top_k, uint64_t *state) {
+  return sample_token(logits, n, temperature, top_k, *state);
 }
 int orc_argmax_matvec(int type, int rows, int cols, const float *scales, const void *data, const float *x,
                       float *best) {

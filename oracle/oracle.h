@@ -115,6 +115,23 @@ void orc_attention(const float *q, const float *kc, const float *vc, int n, int 
                    int kv_heads, int dim, float *head_out);
 int orc_argmax_matvec(int type, int rows, int cols, const float *scales, const void *data,
                       const float *x, float *best_score);
+/* ---- sampling (model.go:1821-2828, topk.go, cumsum.go) ------------------ */
+/* fastRNG.Float64 (model.go:1833-1840): advances *state, returns [0, 1). */
+double orc_rng_float64(uint64_t *state);
+/* topKSelectWithWork (topk.go:326-347): the k highest scores (ties -> lower
+ * id), descending. */
+void orc_topk_select(const float *logits, int n, int k, int *ids, float *scores);
+/* sampleCandidateScoresScratch (model.go:1929-1976) on k candidates. */
+int orc_sample_candidates(const int *ids, const float *scores, int k, double temperature, uint64_t *state);
+/* sampleFullLogitsScratch with a weight scratch (model.go:2215-2307);
+ * -2 unless n is a multiple of 16 (>= 16). */
+int orc_sample_full(const float *logits, int n, float temperature, uint64_t *state);
+/* The generation loop's sampler: argmax for temperature <= 0 or top_k == 1,
+ * top-k candidates for 2 <= top_k < n, else the full logits. */
+int orc_sample_token(const float *logits, int n, double temperature, int top_k, uint64_t *state);
+/* GenerateWithOptions with sampling; the RNG starts at uint64(seed). */
+int orc_generate_sampled(void *model, const int *ids, int n_ids, int max_new, const int *eos, int n_eos,
+                         double temperature, int top_k, int64_t seed, int *out, int out_cap);
 
 #ifdef __cplusplus
 }

@@ -39,7 +39,8 @@ def build() -> str:
 def lib():
     global _lib
     if _lib is None:
-        if not os.path.exists(_LIB_PATH):
+        srcs = [os.path.join(_HERE, f) for f in ("oracle.cpp", "oracle.h")]
+        if not os.path.exists(_LIB_PATH) or os.path.getmtime(_LIB_PATH) < max(map(os.path.getmtime, srcs)):
             build()
         L = C.CDLL(_LIB_PATH)
         P, I, F, D = C.c_void_p, C.c_int, C.c_float, C.c_double
@@ -83,6 +84,14 @@ def lib():
         L.orc_softmax.argtypes = [P, I]
         L.orc_attention.argtypes = [P, P, P, I, I, I, I, P]
         L.orc_argmax_matvec.argtypes = [I, I, I, P, P, P, P]
+        U64P = C.POINTER(C.c_uint64)
+        L.orc_rng_float64.restype = D
+        L.orc_rng_float64.argtypes = [U64P]
+        L.orc_topk_select.argtypes = [P, I, I, P, P]
+        L.orc_sample_candidates.argtypes = [P, P, I, D, U64P]
+        L.orc_sample_full.argtypes = [P, I, F, U64P]
+        L.orc_sample_token.argtypes = [P, I, D, I, U64P]
+        L.orc_generate_sampled.argtypes = [P, P, I, I, P, I, D, I, C.c_int64, P, I]
         _lib = L
     return _lib
 
@@ -90,6 +99,53 @@ def lib():
 def set_threads(n: int) -> int:
     """OpenMP threads of the oracle (n > 0 sets them); returns the count in effect."""
     return int(lib().orc_set_threads(int(n)))
+
+
+def _seed64(seed: int) -> int:
+    """The int64 whose two's-complement bits are uint64(seed)."""
+    u = int(seed) & 0xFFFFFFFFFFFFFFFF
+    return u - (1 << 64) if u >= 1 << 63 else u
+
+
+class RNG:
+    """fastRNG (model.go:1829-1852) held in a uint64; ``state`` is readable."""
+
+    def __init__(self, seed: int):
+        self._s = C.c_uint64(int(seed) & 0xFFFFFFFFFFFFFFFF)
+
+    @property
+    def state(self) -> int:
+        return int(self._s.value)
+
+    def float64(self) -> float:
+        return float(lib().orc_rng_float64(C.byref(self._s)))
+
+
+def topk_select(logits, k):
+    """topKSelectWithWork: (ids, scores) of the k best, descending, ties -> lower id."""
+    x = np.ascontiguousarray(logits, np.float32)
+    k = min(int(k), len(x))
+    ids = np.zeros(k, np.int32)
+    sc = np.zeros(k, np.float32)
+    lib().orc_topk_select(ptr(x), len(x), k, ptr(ids), ptr(sc))
+    return ids, sc
+
+
+def sample_candidates(ids, scores, temperature, rng: RNG) -> int:
+    i = np.ascontiguousarray(ids, np.int32)
+    s = np.ascontiguousarray(scores, np.float32)
+    return int(lib().orc_sample_candidates(ptr(i), ptr(s), len(i), float(temperature), C.byref(rng._s)))
+
+
+def sample_full(logits, temperature, rng: RNG) -> int:
+    x = np.ascontiguousarray(logits, np.float32)
+    return int(lib().orc_sample_full(ptr(x), len(x), float(temperature), C.byref(rng._s)))
+
+
+def sample_token(logits, temperature, top_k, rng: RNG) -> int:
+    """The generation loop's sampler on one row of logits (-2: unsupported vocab)."""
+    x = np.ascontiguousarray(logits, np.float32)
+    return int(lib().orc_sample_token(ptr(x), len(x), float(temperature), int(top_k), C.byref(rng._s)))
 
 
 def ptr(a: np.ndarray):
@@ -137,6 +193,18 @@ class OracleModel:
         e = None if eos is None else np.asarray(eos, dtype=np.int32)
         n = lib().orc_generate(self.h, ptr(ids), len(ids), max_new, None if e is None else ptr(e),
                                0 if e is None else len(e), ptr(out), len(out))
+        if n < 0:
+            raise RuntimeError(f"oracle generate failed ({n})")
+        return out[:n].tolist()
+
+    def generate_sampled(self, ids, max_new, temperature, top_k, seed, eos=None):
+        """GenerateWithOptions with temperature / top_k / seed (orc_generate_sampled)."""
+        ids = np.asarray(ids, dtype=np.int32)
+        out = np.zeros(len(ids) + max_new + 1, dtype=np.int32)
+        e = None if eos is None else np.asarray(eos, dtype=np.int32)
+        n = lib().orc_generate_sampled(self.h, ptr(ids), len(ids), max_new, None if e is None else ptr(e),
+                                       0 if e is None else len(e), float(temperature), int(top_k),
+                                       _seed64(seed), ptr(out), len(out))
         if n < 0:
             raise RuntimeError(f"oracle generate failed ({n})")
         return out[:n].tolist()

@@ -66,6 +66,8 @@ SIGNATURES = {
     "ocrvl_seq_import_kv": (I, [P, I, P, P]),
     "ocrvl_seq_fill_synthetic": (I, [P, I, C.c_uint64]),
     "ocrvl_step": (I, [P, P, I, P, P, P, I, P, P]),
+    "ocrvl_step_sample": (I, [P, P, I, P, P, P, C.c_double, I, P, P]),
+    "ocrvl_generate": (I, [P, P, I, I, P, I, C.c_double, I, C.c_int64, P, I, C.POINTER(I)]),
     "ocrvl_generate_greedy": (I, [P, P, I, I, P, I, P, I, C.POINTER(I)]),
     "ocrvl_decode_greedy_device": (I, [P, P, I, P, I, P]),
     "ocrvl_model_stream": (P, [P]),
@@ -76,6 +78,7 @@ SIGNATURES = {
     "ocrvl_op_swiglu": (I, [I, I, I, P, P, P, P, P, P, I, P, P, P]),
     "ocrvl_op_argmax": (I, [I, I, I, P, P, P, I, P, P, P]),
     "ocrvl_op_argmax_noalloc": (I, [I, I, I, P, P, P, I, P, P, P]),
+    "ocrvl_op_sample": (I, [I, I, P, C.c_double, I, P, P, P, P, P, P]),
     "ocrvl_op_rmsnorm": (I, [I, I, P, P, F, P, P]),
 }
 

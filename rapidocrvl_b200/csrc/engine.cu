@@ -21,6 +21,7 @@
 #include "../../include/ocrvl_cuda.h"
 #include "decoder.cuh"
 #include "batched.cuh"
+#include "sample.cuh"
 
 using namespace ocrvl;
 
@@ -633,6 +634,10 @@ struct ocrvl_model {
   // and the activation image
   bool batched = false;
   BatchedW bw{};
+  // sampling: per-sequence fastRNG states (device + pinned staging) and the
+  // full-vocabulary cumulative-sum scratch (allocated on first use)
+  unsigned long long *rng_d = nullptr, *rng_h = nullptr;
+  float *samp_work = nullptr;
 
   template <typename T>
   T *dalloc(size_t n) {
@@ -1117,6 +1122,10 @@ int ocrvl_finalize(ocrvl_model *m) {
   CK(cudaHostAlloc((void **)&m->sp_h, sizeof(StepParams), cudaHostAllocDefault));
   CK(cudaHostAlloc((void **)&m->out_h, (B + 1) * 4, cudaHostAllocDefault));
   CK(cudaHostAlloc((void **)&m->bt_stage, B * 4, cudaHostAllocDefault));
+  CK(cudaHostAlloc((void **)&m->rng_h, B * 8, cudaHostAllocDefault));
+  m->rng_d = m->dalloc<unsigned long long>(B);
+  if (!m->rng_d) return fail(OCRVL_E_NOMEM, "sampler state");
+  CK(cudaFuncSetAttribute(k_sample, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sample_smem_max()));
   // launch geometry
   m->smem = smem_bytes(d, m->qtype);
   c.dyn_smem = (int)(m->smem - kSmemAlignSlack - 64);
@@ -1191,6 +1200,7 @@ void ocrvl_free(ocrvl_model *m) {
   if (m->sp_h) cudaFreeHost(m->sp_h);
   if (m->out_h) cudaFreeHost(m->out_h);
   if (m->bt_stage) cudaFreeHost(m->bt_stage);
+  if (m->rng_h) cudaFreeHost(m->rng_h);
   if (m->hist_d) cudaFree(m->hist_d);
   if (m->pin_pages) cudaFreeHost(m->pin_pages);
   if (m->stream) cudaStreamDestroy(m->stream);
@@ -1349,16 +1359,70 @@ int ocrvl_seq_read_kv(ocrvl_seq *s, int layer, float *k, float *v) {
 
 namespace {
 
+// The generation loop's choice of sampler for GenerateOptions
+// (internal/model/model.go:1536-1544, 1854-1868, 3611-3642, 7202-7205).
+struct SamplePlan {
+  int mode = SAMPLE_ARGMAX, k = 0, temp1 = 0;
+  float inv = 1.0f;
+};
+
+int plan_sampling(double temperature, int top_k, int vocab, SamplePlan *p) {
+  if (std::isnan(temperature) || std::isinf(temperature)) return fail(OCRVL_E_INVALID, "temperature must be finite");
+  if (top_k < 0) return fail(OCRVL_E_INVALID, "top_k must be >= 0");
+  *p = SamplePlan{};
+  if (temperature <= 0 || top_k == 1) return OCRVL_OK;
+  if (top_k > 1 && top_k < vocab) {
+    if (top_k > kSampleMaxTopK) return fail(OCRVL_E_INVALID, "top_k above 4096 is not supported by the device sampler");
+    p->mode = SAMPLE_TOPK;
+    p->k = top_k;
+    p->temp1 = temperature == 1.0 ? 1 : 0;
+    p->inv = (float)(1.0 / temperature);
+    return OCRVL_OK;
+  }
+  // expScaledVecFMA leaves the last vocab % 16 weights unset, so the full
+  // path is restated for whole 16-float blocks only
+  if (vocab < 16 || vocab % 16 != 0)
+    return fail(OCRVL_E_INVALID, "full-vocabulary sampling needs vocab_size to be a multiple of 16");
+  p->mode = SAMPLE_FULL;
+  const float t = (float)temperature;
+  p->inv = t == 1.0f ? 1.0f : 1.0f / t;
+  return OCRVL_OK;
+}
+
+int launch_sample(const SamplePlan &p, int rows, int vocab, const float *logits, long long ld,
+                  unsigned long long *rng, int *out, int *cand_ids, float *cand_scores, float *work,
+                  cudaStream_t stream) {
+  SampleArgs a{};
+  a.logits = logits;
+  a.ld = ld;
+  a.V = vocab;
+  a.mode = p.mode;
+  a.k = p.k;
+  a.temp1 = p.temp1;
+  a.inv = p.inv;
+  a.rng = rng;
+  a.out = out;
+  a.cand_ids = cand_ids;
+  a.cand_scores = cand_scores;
+  a.work = work;
+  const size_t smem = p.mode == SAMPLE_TOPK ? sample_smem_topk(p.k) : p.mode == SAMPLE_FULL ? sample_smem_full() : 0;
+  k_sample<<<rows, kSampleThreads, smem, stream>>>(a);
+  CK(cudaGetLastError());
+  return OCRVL_OK;
+}
+
 // One launch of the step kernel for n <= kMaxBatch sequences that ocrvl_step
 // has validated (model lock held): page allocation, parameter upload,
 // launch, results.
 int step_group(ocrvl_model *m, ocrvl_seq *const *seqs, int n, const int32_t *ids, const float *embeds,
-               const int32_t *pos_thw, int need_logits, int32_t *out_ids, float *out_logits) {
+               const int32_t *pos_thw, int need_logits, int32_t *out_ids, float *out_logits,
+               const SamplePlan *smp = nullptr, uint64_t *rng_state = nullptr) {
   const ocrvl_model_desc &d = m->desc;
+  const bool draw = need_logits && smp && smp->mode != SAMPLE_ARGMAX;
   StepParams &sp = *m->sp_h;
   sp.M = n;
   sp.any_logits = need_logits ? 1 : 0;
-  sp.store_logits = need_logits && out_logits ? 1 : 0;
+  sp.store_logits = need_logits && (out_logits || draw) ? 1 : 0;
   int max_n = 0;
   for (int i = 0; i < n; i++) {
     ocrvl_seq *s = seqs[i];
@@ -1387,7 +1451,18 @@ int step_group(ocrvl_model *m, ocrvl_seq *const *seqs, int n, const int32_t *ids
   }
   CK(cudaMemcpyAsync(m->sp_d, &sp, step_params_bytes(n), cudaMemcpyHostToDevice, m->stream));
   if (embeds) CK(cudaMemcpyAsync(m->ctx.h, embeds, (size_t)n * d.hidden_size * 4, cudaMemcpyHostToDevice, m->stream));
+  if (draw) {
+    memcpy(m->rng_h, rng_state, (size_t)n * 8);
+    CK(cudaMemcpyAsync(m->rng_d, m->rng_h, (size_t)n * 8, cudaMemcpyHostToDevice, m->stream));
+  }
   if (int rc = launch_step(m, n, sp.any_logits, embeds ? 0 : 1)) return rc;
+  if (draw) {
+    // the draw replaces the greedy ids in tok_out (same stream, after the step)
+    if (int rc = launch_sample(*smp, n, d.vocab_size, m->ctx.logits, d.vocab_size, m->rng_d, m->ctx.tok_out, nullptr,
+                               nullptr, m->samp_work, m->stream))
+      return rc;
+    CK(cudaMemcpyAsync(m->rng_h, m->rng_d, (size_t)n * 8, cudaMemcpyDeviceToHost, m->stream));
+  }
   CK(cudaMemcpyAsync(m->out_h, m->ctx.tok_out, (size_t)n * 4, cudaMemcpyDeviceToHost, m->stream));
   CK(cudaMemcpyAsync(m->out_h + kMaxSeqs, m->ctx.err, 4, cudaMemcpyDeviceToHost, m->stream));
   if (out_logits && need_logits)
@@ -1396,6 +1471,11 @@ int step_group(ocrvl_model *m, ocrvl_seq *const *seqs, int n, const int32_t *ids
   if (m->out_h[kMaxSeqs]) {
     reset_after_timeout(m);
     return fail(OCRVL_E_TIMEOUT, "device grid barrier timed out");
+  }
+  if (draw) {
+    for (int i = 0; i < n; i++)
+      if (m->out_h[i] < 0) return fail(OCRVL_E_CUDA, "device sampler: candidate count mismatch");
+    memcpy(rng_state, m->rng_h, (size_t)n * 8);
   }
   for (int i = 0; i < n; i++) {
     seqs[i]->len++;
@@ -1408,8 +1488,15 @@ int step_group(ocrvl_model *m, ocrvl_seq *const *seqs, int n, const int32_t *ids
 
 extern "C" {
 
-int ocrvl_step(ocrvl_model *m, ocrvl_seq *const *seqs, int n, const int32_t *ids, const float *embeds,
-               const int32_t *pos_thw, int need_logits, int32_t *out_ids, float *out_logits) {
+}  // extern "C"
+
+namespace {
+
+// ocrvl_step / ocrvl_step_sample: validation of every sequence, then one
+// step_group per launch.
+int step_impl(ocrvl_model *m, ocrvl_seq *const *seqs, int n, const int32_t *ids, const float *embeds,
+              const int32_t *pos_thw, int need_logits, int32_t *out_ids, float *out_logits, const SamplePlan *smp,
+              uint64_t *rng_state) {
   if (!m || !seqs) return fail(OCRVL_E_INVALID, "null argument");
   if (n < 1 || n > kMaxSeqs) return fail(OCRVL_E_INVALID, "batch must be 1..64 sequences");
   if (!ids && !embeds) return fail(OCRVL_E_INVALID, "ids or embeds required");
@@ -1435,17 +1522,40 @@ int ocrvl_step(ocrvl_model *m, ocrvl_seq *const *seqs, int n, const int32_t *ids
     if (s->len % kPageTokens == 0 && (int)s->pages.size() <= s->len / kPageTokens) new_pages++;
   }
   if (new_pages > m->free_pages.size()) return fail(OCRVL_E_NOMEM, "KV page pool exhausted");
+  if (smp && smp->mode == SAMPLE_FULL && !m->samp_work) {
+    m->samp_work = m->dalloc<float>((size_t)kMaxSeqs * d.vocab_size);
+    if (!m->samp_work) return fail(OCRVL_E_NOMEM, "sampler scratch");
+  }
   if (n > kMaxBatch && m->batched)
-    return step_group(m, seqs, n, ids, embeds, pos_thw, need_logits, out_ids, out_logits);
+    return step_group(m, seqs, n, ids, embeds, pos_thw, need_logits, out_ids, out_logits, smp, rng_state);
   // groups of kMaxBatch sequences, one launch each
   for (int g0 = 0; g0 < n; g0 += kMaxBatch) {
     const int gn = std::min(kMaxBatch, n - g0);
     int rc = step_group(m, seqs + g0, gn, ids ? ids + g0 : nullptr, embeds ? embeds + (size_t)g0 * d.hidden_size : nullptr,
                         pos_thw ? pos_thw + 3 * g0 : nullptr, need_logits, out_ids ? out_ids + g0 : nullptr,
-                        out_logits ? out_logits + (size_t)g0 * d.vocab_size : nullptr);
+                        out_logits ? out_logits + (size_t)g0 * d.vocab_size : nullptr, smp,
+                        rng_state ? rng_state + g0 : nullptr);
     if (rc) return rc;
   }
   return OCRVL_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int ocrvl_step(ocrvl_model *m, ocrvl_seq *const *seqs, int n, const int32_t *ids, const float *embeds,
+               const int32_t *pos_thw, int need_logits, int32_t *out_ids, float *out_logits) {
+  return step_impl(m, seqs, n, ids, embeds, pos_thw, need_logits, out_ids, out_logits, nullptr, nullptr);
+}
+
+int ocrvl_step_sample(ocrvl_model *m, ocrvl_seq *const *seqs, int n, const int32_t *ids, const float *embeds,
+                      const int32_t *pos_thw, double temperature, int top_k, uint64_t *rng_state, int32_t *out_ids) {
+  if (!m || !out_ids) return fail(OCRVL_E_INVALID, "null argument");
+  SamplePlan p;
+  if (int rc = plan_sampling(temperature, top_k, m->desc.vocab_size, &p)) return rc;
+  if (p.mode != SAMPLE_ARGMAX && !rng_state) return fail(OCRVL_E_INVALID, "rng_state required when sampling");
+  return step_impl(m, seqs, n, ids, embeds, pos_thw, 1, out_ids, nullptr, &p, rng_state);
 }
 
 void *ocrvl_model_stream(ocrvl_model *m) { return m ? (void *)m->stream : nullptr; }
@@ -1625,6 +1735,43 @@ int ocrvl_generate_greedy(ocrvl_model *m, const int32_t *ids, int n_ids, int max
     if (stop || i + 1 >= max_new) break;
     int32_t cur = tok;
     rc = ocrvl_step(m, &s, 1, &cur, nullptr, nullptr, 1, &tok, nullptr);
+  }
+  ocrvl_seq_free(s);
+  *n_out = n;
+  return rc;
+}
+
+int ocrvl_generate(ocrvl_model *m, const int32_t *ids, int n_ids, int max_new, const int32_t *eos, int n_eos,
+                   double temperature, int top_k, int64_t seed, int32_t *out, int out_cap, int *n_out) {
+  if (!m || !out || !n_out || (n_ids > 0 && !ids)) return fail(OCRVL_E_INVALID, "null argument");
+  SamplePlan p;
+  if (int rc = plan_sampling(temperature, top_k, m->desc.vocab_size, &p)) return rc;
+  if (p.mode == SAMPLE_ARGMAX) return ocrvl_generate_greedy(m, ids, n_ids, max_new, eos, n_eos, out, out_cap, n_out);
+  if (max_new < 0) return fail(OCRVL_E_INVALID, "max_new_tokens must be >= 0");
+  for (int i = 0; i < n_ids; i++)
+    if (ids[i] < 0) return fail(OCRVL_E_INVALID, "input tokens must not contain negative ids");
+  if (max_new > 0 && n_ids == 0) return fail(OCRVL_E_INVALID, "input tokens must not be empty when max_new_tokens > 0");
+  if (out_cap < n_ids + max_new) return fail(OCRVL_E_INVALID, "output buffer too small");
+  static const int32_t kDefaultEOS[1] = {2};
+  if (!eos) { eos = kDefaultEOS; n_eos = 1; }
+  for (int i = 0; i < n_ids; i++) out[i] = ids[i];
+  *n_out = n_ids;
+  if (max_new == 0) return OCRVL_OK;
+  ocrvl_seq *s = nullptr;
+  int rc = ocrvl_seq_create(m, n_ids + max_new, &s);
+  if (rc) return rc;
+  uint64_t rng = (uint64_t)seed;  // samplingRNGInto (model.go:1846-1852)
+  int32_t tok = -1;
+  for (int q = 0; q + 1 < n_ids && rc == 0; q++) rc = ocrvl_step(m, &s, 1, &ids[q], nullptr, nullptr, 0, &tok, nullptr);
+  if (rc == 0) rc = ocrvl_step_sample(m, &s, 1, &ids[n_ids - 1], nullptr, nullptr, temperature, top_k, &rng, &tok);
+  int n = n_ids;
+  for (int i = 0; rc == 0 && i < max_new; i++) {
+    out[n++] = tok;
+    bool stop = false;
+    for (int j = 0; j < n_eos; j++) stop |= tok == eos[j];
+    if (stop || i + 1 >= max_new) break;
+    int32_t cur = tok;
+    rc = ocrvl_step_sample(m, &s, 1, &cur, nullptr, nullptr, temperature, top_k, &rng, &tok);
   }
   ocrvl_seq_free(s);
   *n_out = n;
@@ -1986,6 +2133,21 @@ int ocrvl_op_argmax_noalloc(int type, int rows, int cols, const void *w, const f
   k_argmax_ids<<<1, 32, 0, st>>>(keys, m, ids);
   CK(cudaGetLastError());
   return OCRVL_OK;
+}
+
+int ocrvl_op_sample(int m, int vocab, const float *logits, double temperature, int top_k, uint64_t *rng_state,
+                    int32_t *out_ids, int32_t *cand_ids, float *cand_scores, float *work, void *stream) {
+  if (m < 1 || m > 65535) return fail(OCRVL_E_INVALID, "m must be 1..65535 rows");
+  if (vocab < 2) return fail(OCRVL_E_INVALID, "vocab must be >= 2");
+  if (!logits || !out_ids) return fail(OCRVL_E_INVALID, "null argument");
+  SamplePlan p;
+  if (int rc = plan_sampling(temperature, top_k, vocab, &p)) return rc;
+  if (p.mode != SAMPLE_ARGMAX && !rng_state) return fail(OCRVL_E_INVALID, "rng_state required when sampling");
+  if (p.mode == SAMPLE_FULL && !work) return fail(OCRVL_E_INVALID, "work (m * vocab floats) required for full-vocabulary sampling");
+  if (p.mode != SAMPLE_TOPK && (cand_ids || cand_scores))
+    return fail(OCRVL_E_INVALID, "candidates are only produced by top-k sampling");
+  return launch_sample(p, m, vocab, logits, vocab, (unsigned long long *)rng_state, out_ids, cand_ids, cand_scores,
+                       work, (cudaStream_t)stream);
 }
 
 }  // extern "C"

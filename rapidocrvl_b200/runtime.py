@@ -68,6 +68,22 @@ def validate_generate_options(opts: GenerateOptions) -> None:
         raise ValueError("eos_token_ids must not contain negative ids")
 
 
+def generation_needs_sampling(opts: GenerateOptions) -> bool:
+    """generationNeedsSamplingScratch (model.go:1854-1856): an RNG is used."""
+    return opts.max_new_tokens > 0 and opts.temperature > 0 and opts.top_k != 1
+
+
+def generation_uses_argmax(opts: GenerateOptions) -> bool:
+    """generationUsesArgmaxSampling (model.go:1858-1860)."""
+    return opts.temperature <= 0 or opts.top_k == 1
+
+
+def sampling_rng_state(opts: GenerateOptions) -> Optional[int]:
+    """samplingRNGInto (model.go:1846-1852): the fastRNG state uint64(seed),
+    or None when generation draws nothing."""
+    return (int(opts.seed) & 0xFFFFFFFFFFFFFFFF) if generation_needs_sampling(opts) else None
+
+
 def validate_generation_input(ids: Sequence[int], opts: GenerateOptions) -> None:
     """validateInputTokenIDs + validateGenerationInput (model.go:472-490)."""
     if any(i < 0 for i in ids):
@@ -314,6 +330,26 @@ class Runtime:
                                       _ptr(out), _ptr(logits)))
         return out, logits
 
+    def step_sample(self, seqs, ids=None, embeds=None, positions=None, temperature=0.0, top_k=0, rng_states=None):
+        """One decode step whose next ids are drawn on the device by the
+        reference's generation-loop sampler (``ocrvl_step_sample``).
+        ``rng_states``: one fastRNG state per sequence (a uint64 numpy array,
+        advanced in place); unused for argmax.  Returns the ids."""
+        n = len(seqs)
+        arr = (C.c_void_p * n)(*[s._h for s in seqs])
+        ids_a = None if ids is None else _i32(ids)
+        emb = None if embeds is None else np.ascontiguousarray(embeds, dtype=np.float32)
+        pos = None if positions is None else _i32(positions).reshape(n, 3)
+        st = None
+        if rng_states is not None:
+            st = rng_states
+            if not (isinstance(st, np.ndarray) and st.dtype == np.uint64 and st.flags.c_contiguous and st.size == n):
+                raise ValueError("rng_states must be a contiguous uint64 array with one state per sequence")
+        out = np.zeros(n, np.int32)
+        _lib.check(self._L.ocrvl_step_sample(self._h, arr, n, _ptr(ids_a), _ptr(emb), _ptr(pos), float(temperature),
+                                             int(top_k), _ptr(st), _ptr(out)))
+        return out
+
     def decode_device(self, seqs, first_ids, steps: int) -> np.ndarray:
         """Greedy decode of ``steps`` tokens per sequence with device-side
         token feedback (no host round trip per token).  Returns [steps, n] ids."""
@@ -339,8 +375,6 @@ class Runtime:
     def generate_with_options(self, ids: Sequence[int], opts: GenerateOptions) -> GenerateResult:
         validate_generate_options(opts)
         validate_generation_input(ids, opts)
-        if opts.temperature > 0:
-            raise NotImplementedError("sampled generation (temperature > 0) is not on the CUDA path yet")
         eos = DEFAULT_EOS_TOKEN_IDS if opts.eos_token_ids is None else list(opts.eos_token_ids)
         ids_a = _i32(list(ids))
         if opts.max_new_tokens == 0:
@@ -352,21 +386,22 @@ class Runtime:
         n = C.c_int(0)
         # an explicit empty list means "no EOS" (only None selects the default)
         eos_a = _i32(eos) if eos else np.zeros(1, np.int32)
-        _lib.check(self._L.ocrvl_generate_greedy(self._h, _ptr(ids_a), len(ids_a), int(opts.max_new_tokens),
-                                                 _ptr(eos_a), len(eos), _ptr(out),
-                                                 len(out), C.byref(n)))
+        seed = int(opts.seed) & 0xFFFFFFFFFFFFFFFF
+        seed = seed - (1 << 64) if seed >= 1 << 63 else seed
+        _lib.check(self._L.ocrvl_generate(self._h, _ptr(ids_a), len(ids_a), int(opts.max_new_tokens),
+                                          _ptr(eos_a), len(eos), float(opts.temperature), int(opts.top_k), seed,
+                                          _ptr(out), len(out), C.byref(n)))
         return GenerateResult(tokens=out[: n.value].tolist(), prompt_tokens=len(ids_a))
 
     def generate_with_image_embeds(self, ids: Sequence[int], image_embeds, image_grid,
                                    opts: GenerateOptions) -> GenerateResult:
-        """GenerateWithImageEmbeds (model.go:1582-1707) with temperature 0:
-        image placeholders take the given embeddings (one row each, in order),
-        M-RoPE positions come from :func:`multimodal_positions`, and generated
-        tokens sit at len(out) - 1 + rope delta.  One ``ocrvl_step`` per token."""
+        """GenerateWithImageEmbeds (model.go:1582-1707): image placeholders
+        take the given embeddings (one row each, in order), M-RoPE positions
+        come from :func:`multimodal_positions`, and generated tokens sit at
+        len(out) - 1 + rope delta.  One ``ocrvl_step`` per token, or
+        ``ocrvl_step_sample`` when the options sample."""
         validate_generate_options(opts)
         validate_generation_input(ids, opts)
-        if opts.temperature > 0:
-            raise NotImplementedError("sampled generation (temperature > 0) is not on the CUDA path yet")
         if opts.max_new_tokens == 0:
             return GenerateResult(tokens=list(ids), prompt_tokens=len(ids))
         c = self.cfg
@@ -379,6 +414,16 @@ class Runtime:
             raise ValueError(f"too many image placeholder tokens: need {len(emb)}")
         if n_img < len(emb):
             raise ValueError(f"not enough image placeholder tokens: got {n_img} need {len(emb)}")
+        state = sampling_rng_state(opts)
+        rng = None if state is None else np.array([state], np.uint64)
+
+        def step(ids=None, embeds=None, pos=None, last=True):
+            if last and rng is not None:
+                return int(self.step_sample([seq], ids=ids, embeds=embeds, positions=[pos],
+                                            temperature=opts.temperature, top_k=opts.top_k, rng_states=rng)[0])
+            r, _ = self.step([seq], ids=ids, embeds=embeds, positions=[pos], need_logits=last)
+            return int(r[0])
+
         seq = self.new_sequence(len(inp) + opts.max_new_tokens)
         try:
             cursor = 0
@@ -386,19 +431,17 @@ class Runtime:
             for i, t in enumerate(inp):
                 last = i == len(inp) - 1
                 if t == c.image_token_id:
-                    r, _ = self.step([seq], embeds=emb[cursor:cursor + 1], positions=[positions[i]], need_logits=last)
+                    nxt = step(embeds=emb[cursor:cursor + 1], pos=positions[i], last=last)
                     cursor += 1
                 else:
-                    r, _ = self.step([seq], ids=[t], positions=[positions[i]], need_logits=last)
-                nxt = int(r[0])
+                    nxt = step(ids=[t], pos=positions[i], last=last)
             out = list(inp)
             for i in range(opts.max_new_tokens):
                 out.append(nxt)
                 if nxt in eos or i + 1 >= opts.max_new_tokens:
                     break
                 p = len(out) - 1 + delta
-                r, _ = self.step([seq], ids=[nxt], positions=[(p, p, p)], need_logits=True)
-                nxt = int(r[0])
+                nxt = step(ids=[nxt], pos=(p, p, p))
             return GenerateResult(tokens=out, prompt_tokens=len(inp))
         finally:
             seq.close()

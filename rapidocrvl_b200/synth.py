@@ -103,10 +103,17 @@ def cache_root() -> str:
     return os.environ.get("OCRVL_MODEL_CACHE", os.path.join("/tmp", "ocrvl_models"))
 
 
+# The tiny decoder with a vocabulary that is a multiple of 16 (the
+# full-vocabulary sampler's whole 16-float blocks).
+TINY_V1024_CONFIG = dict(TINY_CONFIG, vocab_size=1024)
+
+KINDS = {"bench": BENCH_CONFIG, "tiny": TINY_CONFIG, "tiny-v1024": TINY_V1024_CONFIG}
+
+
 def ensure(kind: str, quantization: str, seed: int = 0) -> str:
-    """Return a model directory holding the seeded ``kind`` ('bench'|'tiny')
+    """Return a model directory holding the seeded ``kind`` (a key of KINDS)
     decoder in ``quantization``, building it on first use."""
-    kw = BENCH_CONFIG if kind == "bench" else TINY_CONFIG
+    kw = KINDS[kind]
     c = make_config(**kw)
     key = hashlib.sha1(json.dumps([kw, seed, 1], sort_keys=True).encode()).hexdigest()[:10]
     d = os.path.join(cache_root(), f"{kind}-{key}")
