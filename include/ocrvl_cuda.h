@@ -267,7 +267,8 @@ int ocrvl_op_argmax_noalloc(int type, int rows, int cols, const void *w, const f
  * floats): out_ids[m], rng_state[m] (device uint64, advanced), optional
  * cand_ids / cand_scores ([m][top_k], top-k path only: the candidates in the
  * order sampleCandidateScoresScratch sees them), work ([m][vocab] floats,
- * full-vocabulary path only).  No allocation. */
+ * full-vocabulary path only; logits and work 16-byte aligned there).  No
+ * allocation. */
 int ocrvl_op_sample(int m, int vocab, const float *logits, double temperature, int top_k, uint64_t *rng_state,
                     int32_t *out_ids, int32_t *cand_ids, float *cand_scores, float *work, void *stream);
 

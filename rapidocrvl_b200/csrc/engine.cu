@@ -1125,7 +1125,6 @@ int ocrvl_finalize(ocrvl_model *m) {
   CK(cudaHostAlloc((void **)&m->rng_h, B * 8, cudaHostAllocDefault));
   m->rng_d = m->dalloc<unsigned long long>(B);
   if (!m->rng_d) return fail(OCRVL_E_NOMEM, "sampler state");
-  CK(cudaFuncSetAttribute(k_sample, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sample_smem_max()));
   // launch geometry
   m->smem = smem_bytes(d, m->qtype);
   c.dyn_smem = (int)(m->smem - kSmemAlignSlack - 64);
@@ -1406,6 +1405,17 @@ int launch_sample(const SamplePlan &p, int rows, int vocab, const float *logits,
   a.cand_scores = cand_scores;
   a.work = work;
   const size_t smem = p.mode == SAMPLE_TOPK ? sample_smem_topk(p.k) : p.mode == SAMPLE_FULL ? sample_smem_full() : 0;
+  if (smem > 48 * 1024) {
+    // more than the default dynamic shared memory: opt in once per device
+    static std::atomic<unsigned long long> opted{0};
+    int dev = 0;
+    CK(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= 64) return fail(OCRVL_E_INVALID, "device index out of range");
+    if (!(opted.load() & (1ull << dev))) {
+      CK(cudaFuncSetAttribute(k_sample, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sample_smem_max()));
+      opted.fetch_or(1ull << dev);
+    }
+  }
   k_sample<<<rows, kSampleThreads, smem, stream>>>(a);
   CK(cudaGetLastError());
   return OCRVL_OK;
@@ -2144,6 +2154,8 @@ int ocrvl_op_sample(int m, int vocab, const float *logits, double temperature, i
   if (int rc = plan_sampling(temperature, top_k, vocab, &p)) return rc;
   if (p.mode != SAMPLE_ARGMAX && !rng_state) return fail(OCRVL_E_INVALID, "rng_state required when sampling");
   if (p.mode == SAMPLE_FULL && !work) return fail(OCRVL_E_INVALID, "work (m * vocab floats) required for full-vocabulary sampling");
+  if (p.mode == SAMPLE_FULL && ((reinterpret_cast<uintptr_t>(logits) | reinterpret_cast<uintptr_t>(work)) & 15))
+    return fail(OCRVL_E_INVALID, "logits and work must be 16-byte aligned for full-vocabulary sampling");
   if (p.mode != SAMPLE_TOPK && (cand_ids || cand_scores))
     return fail(OCRVL_E_INVALID, "candidates are only produced by top-k sampling");
   return launch_sample(p, m, vocab, logits, vocab, (unsigned long long *)rng_state, out_ids, cand_ids, cand_scores,

@@ -29,6 +29,9 @@ constexpr int kSampleThreads = 1024;
 constexpr int kSampleMaxTopK = 4096;
 constexpr int kFullTile = 1024;          // block-chain floats per round
 constexpr int kFullLaneSlab = 4096;      // lane-sum floats per round (16 lanes x 256)
+constexpr int kTopkBins = 4096;          // top-k first digit: the top 12 bits of the order key
+constexpr int kTopkCap = 8192;           // top-k candidates the in-shared-memory sort holds
+constexpr int kTopkRankMax = 384;        // up to this many candidates: rank sort, else bitonic
 
 enum { SAMPLE_ARGMAX = 0, SAMPLE_TOPK = 1, SAMPLE_FULL = 2 };
 
@@ -47,11 +50,17 @@ struct SampleArgs {
   float *work;              // [rows][ld] cumulative sums (SAMPLE_FULL)
 };
 
-__host__ __device__ constexpr size_t sample_smem_topk(int k) { return (size_t)k * 28 + 16; }
+__host__ __device__ constexpr size_t sample_smem_topk(int k) {
+  return (size_t)kTopkCap * 8 + (size_t)kTopkBins * 4 + (size_t)k * 20;
+}
 __host__ __device__ constexpr size_t sample_smem_full() { return 2 * (4 * (kFullTile + 1) + kFullLaneSlab) * 4; }
 __host__ __device__ constexpr size_t sample_smem_max() {
   return sample_smem_topk(kSampleMaxTopK) > sample_smem_full() ? sample_smem_topk(kSampleMaxTopK) : sample_smem_full();
 }
+
+// Round-to-nearest sum in the accumulator's precision.
+__device__ __forceinline__ float sum_rn(float a, float b) { return __fadd_rn(a, b); }
+__device__ __forceinline__ double sum_rn(double a, float b) { return __dadd_rn(a, (double)b); }
 
 // fastRNG.Float64 (model.go:1833-1840).
 __device__ __forceinline__ double rng_float64(unsigned long long &s) {
@@ -161,18 +170,173 @@ __device__ int sample_small(const float *ss, const int *sid, int k, bool temp1, 
   return pick <= acc ? sid[2] : sid[3];
 }
 
-// Top-k candidates and the draw for one row.
-__device__ void sample_topk_row(const SampleArgs &a, int row, unsigned char *dsm) {
+// Calls f(i, x[i]) for every i < V of one row; 16-byte loads, four a
+// thread in flight, when the row is 16-byte aligned.  f runs under
+// divergence (no warp-synchronous intrinsics).  Each thread visits its
+// indices in increasing order.  kReadOnly: x is not written during the
+// kernel (read-only data path); otherwise the loads go through L2.
+template <bool kReadOnly = true, typename F>
+__device__ __forceinline__ void for_each_logit(const float *x, int V, F f) {
+  const int tid = threadIdx.x, bd = blockDim.x;
+  int i0 = 0;
+  if ((reinterpret_cast<uintptr_t>(x) & 15) == 0) {
+    const float4 *x4 = reinterpret_cast<const float4 *>(x);
+    const int V4 = V >> 2;
+    int j = tid;
+    for (; j + 3 * bd < V4; j += 4 * bd) {
+      float4 v[4];
+#pragma unroll
+      for (int u = 0; u < 4; u++) v[u] = kReadOnly ? __ldg(x4 + j + u * bd) : __ldcg(x4 + j + u * bd);
+#pragma unroll
+      for (int u = 0; u < 4; u++) {
+        const int i = 4 * (j + u * bd);
+        f(i, v[u].x);
+        f(i + 1, v[u].y);
+        f(i + 2, v[u].z);
+        f(i + 3, v[u].w);
+      }
+    }
+    for (; j < V4; j += bd) {
+      const float4 v = kReadOnly ? __ldg(x4 + j) : __ldcg(x4 + j);
+      f(4 * j, v.x);
+      f(4 * j + 1, v.y);
+      f(4 * j + 2, v.z);
+      f(4 * j + 3, v.w);
+    }
+    i0 = 4 * V4;
+  }
+  for (int i = i0 + tid; i < V; i += bd) f(i, kReadOnly ? __ldg(x + i) : __ldcg(x + i));
+}
+
+// Block-wide exclusive scan of one value a thread (blockDim.x a multiple of
+// 32, at most 1024); returns the exclusive prefix, *total the block sum.
+__device__ __forceinline__ unsigned block_exclusive_scan(unsigned v, unsigned *warp_sums, unsigned *total) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  unsigned incl = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const unsigned t = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += t;
+  }
+  if (lane == 31) warp_sums[warp] = incl;
+  __syncthreads();
+  if (warp == 0) {
+    const unsigned w = lane < nw ? warp_sums[lane] : 0u;
+    unsigned wi = w;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const unsigned t = __shfl_up_sync(0xffffffffu, wi, o);
+      if (lane >= o) wi += t;
+    }
+    if (lane < nw) warp_sums[lane] = wi - w;
+    if (lane == 31) warp_sums[32] = wi;
+  }
+  __syncthreads();
+  const unsigned r = warp_sums[warp] + incl - v;
+  *total = warp_sums[32];
+  __syncthreads();
+  return r;
+}
+
+// Candidate key: the order key above, the complement of the id below, so
+// that a larger key is a higher score or, on equal scores, a lower id.
+__device__ __forceinline__ unsigned long long cand_key(unsigned key, int i) {
+  return ((unsigned long long)key << 32) | (unsigned long long)(0xFFFFFFFFu - (unsigned)i);
+}
+
+// Fast path: one 12-bit histogram pass finds the bin that holds the k-th
+// largest key; every logit at or above that bin's lower edge (normally a few
+// hundred beyond k) is gathered into shared memory and sorted there (a rank
+// count for a few hundred, else a bitonic network).
+// Returns false (nothing written) when more than kTopkCap logits qualify.
+__device__ bool topk_fast(const float *x, int V, int k, unsigned char *dsm, float *ss, int *sid) {
+  __shared__ unsigned warp_sums[33];
+  __shared__ unsigned s_bin, s_above, s_cnt, s_n;
+  unsigned long long *buf = (unsigned long long *)dsm;
+  unsigned *hist = (unsigned *)(dsm + (size_t)kTopkCap * 8);
+  const int tid = threadIdx.x, bd = blockDim.x;
+  for (int b = tid; b < kTopkBins; b += bd) hist[b] = 0;
+  if (tid == 0) s_bin = s_above = s_cnt = 0;
+  __syncthreads();
+  for_each_logit(x, V, [&](int, float v) { atomicAdd(&hist[order_key(v) >> 20], 1u); });
+  __syncthreads();
+  // bins from the top, kTopkBins / blockDim.x consecutive bins a thread
+  const int per = kTopkBins / bd;
+  unsigned local = 0;
+  for (int j = 0; j < per; j++) local += hist[kTopkBins - 1 - (tid * per + j)];
+  unsigned total;
+  unsigned run = block_exclusive_scan(local, warp_sums, &total);
+  if (run < (unsigned)k && (unsigned)k <= run + local) {
+    for (int j = 0; j < per; j++) {
+      const int b = kTopkBins - 1 - (tid * per + j);
+      if (run + hist[b] >= (unsigned)k) {
+        s_bin = b;
+        s_above = run;
+        s_cnt = hist[b];
+        break;
+      }
+      run += hist[b];
+    }
+  }
+  __syncthreads();
+  const unsigned C = s_above + s_cnt;
+  if (C > (unsigned)kTopkCap) return false;  // uniform: read after a barrier
+  const unsigned lower = s_bin << 20;
+  if (tid == 0) s_n = 0;
+  __syncthreads();
+  for_each_logit(x, V, [&](int i, float v) {
+    const unsigned key = order_key(v);
+    if (key >= lower) {
+      const unsigned p = atomicAdd(&s_n, 1u);
+      if (p < C) buf[p] = cand_key(key, i);
+    }
+  });
+  __syncthreads();
+  if (C <= (unsigned)kTopkRankMax) {
+    // few candidates: each one's place is the number of larger keys (only
+    // the warps that hold a candidate run the count)
+    if (tid < (int)C) {
+      const unsigned long long mine = buf[tid];
+      int place = 0;
+      for (int j = 0; j < (int)C; j++) place += buf[j] > mine;
+      if (place < k) sid[place] = (int)(0xFFFFFFFFu - (unsigned)(mine & 0xFFFFFFFFull));
+    }
+    __syncthreads();
+  } else {
+    int N = 2;
+    while (N < (int)C) N <<= 1;
+    for (int i = C + tid; i < N; i += bd) buf[i] = 0ull;  // below every real key
+    __syncthreads();
+    // bitonic sort, descending
+    for (int size = 2; size <= N; size <<= 1) {
+      for (int stride = size >> 1; stride > 0; stride >>= 1) {
+        for (int t = tid; t < (N >> 1); t += bd) {
+          const int lo = 2 * t - (t & (stride - 1)), hi = lo + stride;
+          const unsigned long long u = buf[lo], w = buf[hi];
+          if ((u < w) == ((lo & size) == 0)) {
+            buf[lo] = w;
+            buf[hi] = u;
+          }
+        }
+        __syncthreads();
+      }
+    }
+    for (int c = tid; c < k; c += bd) sid[c] = (int)(0xFFFFFFFFu - (unsigned)(buf[c] & 0xFFFFFFFFull));
+    __syncthreads();
+  }
+  for (int c = tid; c < k; c += bd) ss[c] = x[sid[c]];  // the logit's own bits (the key folds -0 into +0)
+  __syncthreads();
+  return true;
+}
+
+// General path: 8-bit radix select of the k-th largest key, then the k-th
+// smallest id among the logits equal to it, a gather of exactly k
+// candidates and a rank sort.  Returns false on a candidate count mismatch.
+__device__ bool topk_radix(const float *x, int V, int k, unsigned char *dsm, float *ss, int *sid) {
   __shared__ unsigned hist[256];
   __shared__ unsigned sel[3];
   __shared__ unsigned s_cnt;
-  __shared__ int s_first;
-  __shared__ float s_pickf;
-  __shared__ double s_pickd;
-  const float *x = a.logits + (long long)row * a.ld;
-  const int V = a.V, k = a.k, tid = threadIdx.x, lane = tid & 31;
-
-  // (1) radix select of the k-th largest order key T, 8 bits a pass
+  const int tid = threadIdx.x, lane = tid & 31;
   unsigned prefix = 0, mask = 0, need = (unsigned)k, ties = 0;
   for (int shift = 24; shift >= 0; shift -= 8) {
     for (int i = tid; i < 256; i += blockDim.x) hist[i] = 0;
@@ -191,8 +355,6 @@ __device__ void sample_topk_row(const SampleArgs &a, int row, unsigned char *dsm
     ties = sel[2];
     __syncthreads();
   }
-  // (2) when more logits equal T than are needed, the need-th smallest id
-  //     among them bounds the ones taken (ties go to the lower id)
   unsigned idcut = 0xFFFFFFFFu;
   if (ties > need) {
     unsigned ip = 0, im = 0, n2 = need;
@@ -214,23 +376,16 @@ __device__ void sample_topk_row(const SampleArgs &a, int row, unsigned char *dsm
     }
     idcut = ip;
   }
-  // (3) collect the k candidates (unordered)
   unsigned long long *ck = (unsigned long long *)dsm;
-  float *cs = (float *)(ck + k);
-  int *cid = (int *)(cs + k);
-  float *ss = (float *)(cid + k);
-  int *sid = (int *)(ss + k);
-  float *w = (float *)(sid + k);
+  int *cid = (int *)(ck + k);
   if (tid == 0) s_cnt = 0;
   __syncthreads();
   for (int base = tid & ~31; base < V; base += blockDim.x) {
     const int i = base + lane;
-    float v = 0.0f;
     unsigned key = 0;
     bool take = false;
     if (i < V) {
-      v = x[i];
-      key = order_key(v);
+      key = order_key(x[i]);
       take = key > prefix || (key == prefix && (unsigned)i <= idcut);
     }
     const unsigned b = __ballot_sync(0xffffffffu, take);
@@ -240,26 +395,65 @@ __device__ void sample_topk_row(const SampleArgs &a, int row, unsigned char *dsm
     if (take) {
       const unsigned p = p0 + __popc(b & ((1u << lane) - 1u));
       if (p < (unsigned)k) {
-        ck[p] = ((unsigned long long)key << 32) | (unsigned long long)(0xFFFFFFFFu - (unsigned)i);
-        cs[p] = v;
+        ck[p] = cand_key(key, i);
         cid[p] = i;
       }
     }
   }
   __syncthreads();
-  if (s_cnt != (unsigned)k) {
-    if (tid == 0) a.out[row] = -1;
-    return;
-  }
-  // (4) descending order by (score, lower id): rank of each candidate
+  if (s_cnt != (unsigned)k) return false;
   for (int c = tid; c < k; c += blockDim.x) {
     const unsigned long long me = ck[c];
     int r = 0;
     for (int j = 0; j < k; j++) r += ck[j] > me;
-    ss[r] = cs[c];
     sid[r] = cid[c];
+    ss[r] = x[cid[c]];
   }
   __syncthreads();
+  return true;
+}
+
+// acc += p[0], p[stride], ... (n terms, in order), each partial sum written
+// back in place when kStore.  Loads run a batch of 8 ahead of the dependent
+// adds, so the chain is bound by the add latency.
+template <bool kStore, typename T, typename P>
+__device__ __forceinline__ void chain_sum(T &acc, const float *src, P *dst, int stride, int n) {
+  float cur[8], nxt[8];
+#pragma unroll
+  for (int u = 0; u < 8; u++) nxt[u] = u < n ? src[u * stride] : 0.0f;
+  for (int j0 = 0; j0 < n; j0 += 8) {
+#pragma unroll
+    for (int u = 0; u < 8; u++) cur[u] = nxt[u];
+#pragma unroll
+    for (int u = 0; u < 8; u++) nxt[u] = j0 + 8 + u < n ? src[(j0 + 8 + u) * stride] : 0.0f;
+#pragma unroll
+    for (int u = 0; u < 8; u++)
+      if (j0 + u < n) {
+        acc = sum_rn(acc, cur[u]);
+        if (kStore) dst[(j0 + u) * stride] = acc;
+      }
+  }
+}
+
+// Top-k candidates and the draw for one row.  Shared memory: kTopkCap
+// 8-byte candidate keys, kTopkBins counters, then the running sums (k
+// doubles), ss, sid and w (k each).
+__device__ void sample_topk_row(const SampleArgs &a, int row, unsigned char *dsm) {
+  __shared__ int s_first;
+  __shared__ float s_pickf;
+  __shared__ double s_pickd;
+  const float *x = a.logits + (long long)row * a.ld;
+  const int V = a.V, k = a.k, tid = threadIdx.x;
+  unsigned char *tail = dsm + (size_t)kTopkCap * 8 + (size_t)kTopkBins * 4;
+  double *partd = (double *)tail;
+  float *partf = (float *)tail;
+  float *ss = (float *)(partd + k);
+  int *sid = (int *)(ss + k);
+  float *w = (float *)(sid + k);
+  if (!topk_fast(x, V, k, dsm, ss, sid) && !topk_radix(x, V, k, dsm, ss, sid)) {
+    if (tid == 0) a.out[row] = -1;
+    return;
+  }
   for (int c = tid; c < k; c += blockDim.x) {
     if (a.cand_ids) a.cand_ids[(long long)row * k + c] = sid[c];
     if (a.cand_scores) a.cand_scores[(long long)row * k + c] = ss[c];
@@ -273,32 +467,22 @@ __device__ void sample_topk_row(const SampleArgs &a, int row, unsigned char *dsm
     }
     return;
   }
-  // (5) weights; the maximum of the sorted candidates is the first
+  // weights; the maximum of the sorted candidates is the first
   const float mx = temp1 ? ss[0] : __fmul_rn(ss[0], a.inv);
   for (int c = tid; c < k; c += blockDim.x)
     w[c] = temp1 ? fast_exp(__fsub_rn(ss[c], mx)) : fast_exp(__fsub_rn(__fmul_rn(ss[c], a.inv), mx));
   __syncthreads();
-  // (6) the running sums (one chain in the reference's order; the pick scan
-  //     of pickWeighted*Float32 compares against the same partial sums)
-  double *partd = (double *)ck;
-  float *partf = cs;
+  // the running sums (one chain in the reference's order; the pick scan of
+  // pickWeighted*Float32 compares against the same partial sums)
   if (tid == 0) {
     unsigned long long st = a.rng[row];
     if (temp1) {
       float acc = 0.0f;
-#pragma unroll 8
-      for (int c = 0; c < k; c++) {
-        acc = __fadd_rn(acc, w[c]);
-        partf[c] = acc;
-      }
+      chain_sum<true>(acc, w, partf, 1, k);
       s_pickf = __fmul_rn(__double2float_rn(rng_float64(st)), acc);
     } else {
       double acc = 0.0;
-#pragma unroll 8
-      for (int c = 0; c < k; c++) {
-        acc = __dadd_rn(acc, (double)w[c]);
-        partd[c] = acc;
-      }
+      chain_sum<true>(acc, w, partd, 1, k);
       s_pickd = __dmul_rn(rng_float64(st), acc);
     }
     a.rng[row] = st;
@@ -313,7 +497,8 @@ __device__ void sample_topk_row(const SampleArgs &a, int row, unsigned char *dsm
   if (tid == 0) a.out[row] = sid[s_first < k ? s_first : k - 1];
 }
 
-// Full-vocabulary draw for one row (V a multiple of 16).
+// Full-vocabulary draw for one row (V a multiple of 16, so every 16-byte
+// group of four logits lies inside one CumulativeSum block and one round).
 __device__ void sample_full_row(const SampleArgs &a, int row, unsigned char *dsm) {
   __shared__ float red[32];
   __shared__ float s_bs[4];
@@ -326,7 +511,7 @@ __device__ void sample_full_row(const SampleArgs &a, int row, unsigned char *dsm
 
   // (1) maximum (tensor.Max), bias = -(max * inv)
   float m = -INFINITY;
-  for (int i = tid; i < V; i += blockDim.x) m = fmaxf(m, x[i]);
+  for_each_logit(x, V, [&](int, float v) { m = fmaxf(m, v); });
   for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
   if (lane == 0) red[warp] = m;
   __syncthreads();
@@ -338,30 +523,66 @@ __device__ void sample_full_row(const SampleArgs &a, int row, unsigned char *dsm
   __syncthreads();
   const float inv = a.inv;
   const float bias = -__fmul_rn(red[0], inv);
+  auto weight = [&](float v) { return exp_fma(__fadd_rn(__fmul_rn(v, inv), bias)); };
 
   // (2) weights staged through shared memory, two buffers a round: 4 block
-  //     sub-tiles for the CumulativeSum chains (warp 1, lanes 0..nb-1) and a
-  //     16-lane slab for the 16 lane sums of expScaledVecFMA (warp 0).
-  //     Warps 2.. produce the next round while warps 0-1 consume this one.
+  //     sub-tiles of kFullTile for the CumulativeSum chains (warp 1, lanes
+  //     0..nb-1, which leave the running sums in place) and a slab of
+  //     kFullLaneSlab for the 16 lane sums of expScaledVecFMA (warp 0, lanes
+  //     0..15).  Warps 2.. load and weigh the next round, and copy the
+  //     round before this one's running sums out to cdf, while warps 0-1
+  //     consume this round.  Work items are groups of four floats: items
+  //     [0, kFullTile) are the chain sub-tiles, [kFullTile, 2 kFullTile)
+  //     the lane slab.
   const int nb = V < 4096 ? 1 : 4;
-  const int bs = V < 4096 ? V : (V + 3) / 4;
+  const int bs = V < 4096 ? V : V / 4;
   const int rounds = (bs + kFullTile - 1) / kFullTile;
   const int lrounds = (V + kFullLaneSlab - 1) / kFullLaneSlab;
   const int R = rounds > lrounds ? rounds : lrounds;
   float *buf = (float *)dsm;
   const int bufsz = 4 * (kFullTile + 1) + kFullLaneSlab;
-  auto produce = [&](int r, float *dst) {
-    const int pt = tid - 64, np = blockDim.x - 64;
-    for (int e = pt; e < 4 * kFullTile; e += np) {
-      const int b = e / kFullTile, j = e % kFullTile;
+  constexpr int kItems = 2 * kFullTile;  // groups of four floats a round
+  const int pt = tid - 64, np = (int)blockDim.x - 64;
+  // first logit of item q in round r (and its slot in a buffer), or -1
+  auto item = [&](int q, int r, int *slot) {
+    if (q < kFullTile) {
+      const int b = q / (kFullTile / 4), j = 4 * (q % (kFullTile / 4));
+      *slot = b * (kFullTile + 1) + j;
       const int i = b * bs + r * kFullTile + j;
-      if (b < nb && r * kFullTile + j < bs && i < V)
-        dst[b * (kFullTile + 1) + j] = exp_fma(__fadd_rn(__fmul_rn(x[i], inv), bias));
+      return (b < nb && r * kFullTile + j < bs && i < V) ? i : -1;
     }
-    for (int e = pt; e < kFullLaneSlab; e += np) {
-      const int i = r * kFullLaneSlab + e;
-      if (i < V) dst[4 * (kFullTile + 1) + e] = exp_fma(__fadd_rn(__fmul_rn(x[i], inv), bias));
+    const int e = 4 * (q - kFullTile);
+    *slot = 4 * (kFullTile + 1) + e;
+    const int i = r * kFullLaneSlab + e;
+    return i < V ? i : -1;
+  };
+  auto flush = [&](int r, const float *src, int t0, int nt) {
+    for (int q = t0; q < kFullTile; q += nt) {
+      int slot;
+      const int i = item(q, r, &slot);
+      if (i >= 0) *(float4 *)(cdf + i) = make_float4(src[slot], src[slot + 1], src[slot + 2], src[slot + 3]);
     }
+  };
+  constexpr int kPer = (kItems + 959) / 960;  // items a producer thread takes (960 producers)
+  auto produce = [&](int r, float *dst) {
+    float4 v[kPer];
+    int at[kPer], slot[kPer];
+#pragma unroll
+    for (int u = 0; u < kPer; u++) {  // loads first, so that they are all in flight
+      const int q = pt + u * np;
+      at[u] = q < kItems ? item(q, r, &slot[u]) : -1;
+      if (at[u] >= 0) v[u] = __ldg((const float4 *)(x + at[u]));
+    }
+    if (r >= 2) flush(r - 2, dst, pt, np);
+#pragma unroll
+    for (int u = 0; u < kPer; u++)
+      if (at[u] >= 0) {
+        float *d = dst + slot[u];
+        d[0] = weight(v[u].x);
+        d[1] = weight(v[u].y);
+        d[2] = weight(v[u].z);
+        d[3] = weight(v[u].w);
+      }
   };
   if (warp >= 2) produce(0, buf);
   __syncthreads();
@@ -370,25 +591,19 @@ __device__ void sample_full_row(const SampleArgs &a, int row, unsigned char *dsm
     float *cur = buf + (r & 1) * bufsz;
     if (warp >= 2) {
       if (r + 1 < R) produce(r + 1, buf + ((r + 1) & 1) * bufsz);
+      else if (r >= 1) flush(r - 1, buf + ((r + 1) & 1) * bufsz, pt, np);
     } else if (warp == 0) {
       if (lane < 16) {
-        const float *src = cur + 4 * (kFullTile + 1);
-        const int lim = min(kFullLaneSlab, V - r * kFullLaneSlab);
-#pragma unroll 8
-        for (int e = lane; e < lim; e += 16) acc = __fadd_rn(acc, src[e]);
+        const int n = max(0, min(kFullLaneSlab, V - r * kFullLaneSlab)) / 16;  // this lane's terms
+        chain_sum<false>(acc, cur + 4 * (kFullTile + 1) + lane, (float *)nullptr, 16, n);
       }
     } else if (lane < nb) {
-      const float *src = cur + lane * (kFullTile + 1);
-      const int st = lane * bs + r * kFullTile;
-      const int lim = min(kFullTile, min(bs - r * kFullTile, V - st));
-#pragma unroll 8
-      for (int j = 0; j < lim; j++) {
-        acc = __fadd_rn(acc, src[j]);
-        cdf[st + j] = acc;
-      }
+      float *src = cur + lane * (kFullTile + 1);
+      chain_sum<true>(acc, src, src, 1, max(0, min(kFullTile, bs - r * kFullTile)));
     }
     __syncthreads();
   }
+  flush(R - 1, buf + ((R - 1) & 1) * bufsz, tid, blockDim.x);
   if (warp == 0) {  // tree16 of the 16 lane sums
     float v = acc;
     v = __fadd_rn(v, __shfl_down_sync(0xffffffffu, v, 8));
@@ -397,7 +612,7 @@ __device__ void sample_full_row(const SampleArgs &a, int row, unsigned char *dsm
     v = __fadd_rn(v, __shfl_down_sync(0xffffffffu, v, 1));
     if (lane == 0) s_sum = v;
   } else if (warp == 1 && lane < 4) {
-    s_bs[lane] = (lane < nb && lane * bs < V) ? acc : 0.0f;
+    s_bs[lane] = lane < nb ? acc : 0.0f;
   }
   __syncthreads();
   // (3) block offsets (cumsum.go:46-57), the pick, pickCumulativeFloat32
@@ -413,15 +628,15 @@ __device__ void sample_full_row(const SampleArgs &a, int row, unsigned char *dsm
   }
   __syncthreads();
   const float pick = s_pick;
-  auto cdf_at = [&](int i) {
+  auto cdf_of = [&](int i, float c) {
     const int b = nb == 1 ? 0 : i / bs;
-    return b == 0 ? cdf[i] : __fadd_rn(cdf[i], b == 1 ? off1 : b == 2 ? off2 : off3);
+    return b == 0 ? c : __fadd_rn(c, b == 1 ? off1 : b == 2 ? off2 : off3);
   };
   int first = V, lastfalse = -1;
-  for (int i = tid; i < V; i += blockDim.x) {
-    if (pick <= cdf_at(i)) first = min(first, i);
+  for_each_logit<false>(cdf, V, [&](int i, float c) {
+    if (pick <= cdf_of(i, c)) first = min(first, i);
     else lastfalse = max(lastfalse, i);
-  }
+  });
   for (int o = 16; o; o >>= 1) {
     first = min(first, __shfl_xor_sync(0xffffffffu, first, o));
     lastfalse = max(lastfalse, __shfl_xor_sync(0xffffffffu, lastfalse, o));
@@ -439,7 +654,7 @@ __device__ void sample_full_row(const SampleArgs &a, int row, unsigned char *dsm
       int lo = 0, hi = V;
       while (lo < hi) {
         const int mid = (int)((unsigned)(lo + hi) >> 1);
-        if (pick <= cdf_at(mid)) hi = mid;
+        if (pick <= cdf_of(mid, __ldcg(cdf + mid))) hi = mid;
         else lo = mid + 1;
       }
       res = lo;
@@ -456,17 +671,28 @@ __device__ void sample_argmax_row(const SampleArgs &a, int row) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   float bv = -INFINITY;
   int bi = a.V;
-  for (int i = tid; i < a.V; i += blockDim.x)
-    if (x[i] > bv || bi == a.V) { bv = x[i]; bi = i; }
+  // each thread visits its indices in increasing order: its first maximum
+  for_each_logit(x, a.V, [&](int i, float v) {
+    if (bi == a.V || v > bv) {
+      bv = v;
+      bi = i;
+    }
+  });
   auto merge = [&](float ov, int oi) {
-    if (oi < a.V && (bi == a.V || ov > bv || (ov == bv && oi < bi))) { bv = ov; bi = oi; }
+    if (oi < a.V && (bi == a.V || ov > bv || (ov == bv && oi < bi))) {
+      bv = ov;
+      bi = oi;
+    }
   };
   for (int o = 16; o; o >>= 1) {
     const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
     const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
     merge(ov, oi);
   }
-  if (lane == 0) { sv[warp] = bv; si[warp] = bi; }
+  if (lane == 0) {
+    sv[warp] = bv;
+    si[warp] = bi;
+  }
   __syncthreads();
   if (tid == 0) {
     for (int w = 1; w < (int)(blockDim.x >> 5); w++) merge(sv[w], si[w]);
