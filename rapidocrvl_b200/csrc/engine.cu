@@ -1382,6 +1382,8 @@ int plan_sampling(double temperature, int top_k, int vocab, SamplePlan *p) {
   // path is restated for whole 16-float blocks only
   if (vocab < 16 || vocab % 16 != 0)
     return fail(OCRVL_E_INVALID, "full-vocabulary sampling needs vocab_size to be a multiple of 16");
+  if (vocab > kFullMaxVocab)
+    return fail(OCRVL_E_INVALID, "full-vocabulary sampling supports vocab_size up to 262144");
   p->mode = SAMPLE_FULL;
   const float t = (float)temperature;
   p->inv = t == 1.0f ? 1.0f : 1.0f / t;
@@ -1404,7 +1406,7 @@ int launch_sample(const SamplePlan &p, int rows, int vocab, const float *logits,
   a.cand_ids = cand_ids;
   a.cand_scores = cand_scores;
   a.work = work;
-  const size_t smem = p.mode == SAMPLE_TOPK ? sample_smem_topk(p.k) : p.mode == SAMPLE_FULL ? sample_smem_full() : 0;
+  const size_t smem = p.mode == SAMPLE_TOPK ? sample_smem_topk(p.k) : p.mode == SAMPLE_FULL ? sample_smem_full(vocab) : 0;
   if (smem > 48 * 1024) {
     // more than the default dynamic shared memory: opt in once per device
     static std::atomic<unsigned long long> opted{0};
@@ -1484,7 +1486,7 @@ int step_group(ocrvl_model *m, ocrvl_seq *const *seqs, int n, const int32_t *ids
   }
   if (draw) {
     for (int i = 0; i < n; i++)
-      if (m->out_h[i] < 0) return fail(OCRVL_E_CUDA, "device sampler: candidate count mismatch");
+      if (m->out_h[i] < 0) return fail(OCRVL_E_CUDA, "device sampler: internal failure (candidate count or bounded wait)");
     memcpy(rng_state, m->rng_h, (size_t)n * 8);
   }
   for (int i = 0; i < n; i++) {

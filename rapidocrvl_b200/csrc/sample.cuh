@@ -20,6 +20,7 @@
 #pragma once
 #include <cstdint>
 
+#include "decoder.cuh"  // mbarriers and bulk copies
 #include "numerics.cuh"
 
 using ocrvl::exp_fma;
@@ -27,8 +28,12 @@ using ocrvl::fast_exp;
 
 constexpr int kSampleThreads = 1024;
 constexpr int kSampleMaxTopK = 4096;
-constexpr int kFullTile = 1024;          // block-chain floats per round
-constexpr int kFullLaneSlab = 4096;      // lane-sum floats per round (16 lanes x 256)
+constexpr int kFullTile = 1024;          // block-chain floats a round (per CumulativeSum block)
+constexpr int kFullLaneSlab = 4096;      // lane-sum floats a round (16 lanes x 256)
+constexpr int kFullStages = 4;           // rounds in flight in the shared-memory ring
+constexpr int kFullTileStride = kFullTile + 4;  // 16-byte aligned, the 4 chain lanes on different banks
+constexpr int kFullStage = 4 * kFullTileStride + kFullLaneSlab;  // floats a ring stage
+constexpr int kFullMaxVocab = 262144;    // checkpoints (vocab / 16) held in shared memory
 constexpr int kTopkBins = 4096;          // top-k first digit: the top 12 bits of the order key
 constexpr int kTopkCap = 8192;           // top-k candidates the in-shared-memory sort holds
 constexpr int kTopkRankMax = 384;        // up to this many candidates: rank sort, else bitonic
@@ -44,7 +49,7 @@ struct SampleArgs {
   int temp1;            // top-k: temperature == 1 (float64 compare)
   float inv;            // top-k: float32(1/temp); full: 1/float32(temp)
   unsigned long long *rng;  // [rows] fastRNG states (in/out)
-  int *out;                 // [rows] sampled ids (-1: candidate count mismatch)
+  int *out;                 // [rows] sampled ids (-1: internal failure)
   int *cand_ids;            // [rows][k] or null
   float *cand_scores;       // [rows][k] or null
   float *work;              // [rows][ld] cumulative sums (SAMPLE_FULL)
@@ -53,14 +58,30 @@ struct SampleArgs {
 __host__ __device__ constexpr size_t sample_smem_topk(int k) {
   return (size_t)kTopkCap * 8 + (size_t)kTopkBins * 4 + (size_t)k * 20;
 }
-__host__ __device__ constexpr size_t sample_smem_full() { return 2 * (4 * (kFullTile + 1) + kFullLaneSlab) * 4; }
+// checkpoint floats: one every 16 logits of each block plus the blocks'
+// partial ends, rounded to an even count (the mbarriers after them are 8-byte)
+__host__ __device__ constexpr int sample_full_ckpts(int V) { return (V / 16 + 9) & ~1; }
+// ring, checkpoints, full / empty mbarriers
+__host__ __device__ constexpr size_t sample_smem_full(int V) {
+  return (size_t)kFullStages * kFullStage * 4 + (size_t)sample_full_ckpts(V) * 4 + 2 * kFullStages * 8;
+}
 __host__ __device__ constexpr size_t sample_smem_max() {
-  return sample_smem_topk(kSampleMaxTopK) > sample_smem_full() ? sample_smem_topk(kSampleMaxTopK) : sample_smem_full();
+  return sample_smem_topk(kSampleMaxTopK) > sample_smem_full(kFullMaxVocab) ? sample_smem_topk(kSampleMaxTopK)
+                                                                           : sample_smem_full(kFullMaxVocab);
 }
 
 // Round-to-nearest sum in the accumulator's precision.
 __device__ __forceinline__ float sum_rn(float a, float b) { return __fadd_rn(a, b); }
 __device__ __forceinline__ double sum_rn(double a, float b) { return __dadd_rn(a, (double)b); }
+
+// Four consecutive running sums (dst 16-byte aligned).
+__device__ __forceinline__ void store4(float *d, float a, float b, float c, float e) {
+  *reinterpret_cast<float4 *>(d) = make_float4(a, b, c, e);
+}
+__device__ __forceinline__ void store4(double *d, double a, double b, double c, double e) {
+  reinterpret_cast<double2 *>(d)[0] = make_double2(a, b);
+  reinterpret_cast<double2 *>(d)[1] = make_double2(c, e);
+}
 
 // fastRNG.Float64 (model.go:1833-1840).
 __device__ __forceinline__ double rng_float64(unsigned long long &s) {
@@ -413,25 +434,65 @@ __device__ bool topk_radix(const float *x, int V, int k, unsigned char *dsm, flo
   return true;
 }
 
-// acc += p[0], p[stride], ... (n terms, in order), each partial sum written
-// back in place when kStore.  Loads run a batch of 8 ahead of the dependent
-// adds, so the chain is bound by the add latency.
-template <bool kStore, typename T, typename P>
-__device__ __forceinline__ void chain_sum(T &acc, const float *src, P *dst, int stride, int n) {
-  float cur[8], nxt[8];
+// acc += src[0], src[1], ... src[n-1] in order (src 16-byte aligned), each
+// partial sum stored to dst[j] when kStore (dst may be src).  16-byte loads
+// run four to eight ahead of the dependent adds, so the chain is bound by
+// the add latency rather than by shared-memory latency.
+template <bool kStore, typename T>
+__device__ __forceinline__ void chain4(T &acc, const float *src, T *dst, int n) {
+  const float4 *s4 = reinterpret_cast<const float4 *>(src);
+  const int n4 = n >> 2;
+  const float4 z = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+  float4 b[4];
 #pragma unroll
-  for (int u = 0; u < 8; u++) nxt[u] = u < n ? src[u * stride] : 0.0f;
-  for (int j0 = 0; j0 < n; j0 += 8) {
+  for (int u = 0; u < 4; u++) b[u] = u < n4 ? s4[u] : z;
+  for (int q0 = 0; q0 < n4; q0 += 4) {
+    float4 nb[4];
 #pragma unroll
-    for (int u = 0; u < 8; u++) cur[u] = nxt[u];
+    for (int u = 0; u < 4; u++) nb[u] = q0 + 4 + u < n4 ? s4[q0 + 4 + u] : z;
 #pragma unroll
-    for (int u = 0; u < 8; u++) nxt[u] = j0 + 8 + u < n ? src[(j0 + 8 + u) * stride] : 0.0f;
-#pragma unroll
-    for (int u = 0; u < 8; u++)
-      if (j0 + u < n) {
-        acc = sum_rn(acc, cur[u]);
-        if (kStore) dst[(j0 + u) * stride] = acc;
+    for (int u = 0; u < 4; u++) {
+      if (q0 + u < n4) {
+        const T r0 = acc = sum_rn(acc, b[u].x);
+        const T r1 = acc = sum_rn(acc, b[u].y);
+        const T r2 = acc = sum_rn(acc, b[u].z);
+        const T r3 = acc = sum_rn(acc, b[u].w);
+        if (kStore) store4(dst + 4 * (q0 + u), r0, r1, r2, r3);
       }
+    }
+#pragma unroll
+    for (int u = 0; u < 4; u++) b[u] = nb[u];
+  }
+  for (int j = 4 * n4; j < n; j++) {
+    acc = sum_rn(acc, src[j]);
+    if (kStore) dst[j] = acc;
+  }
+}
+
+// chain4<false> over n4 float4 of src, also storing the running sum after
+// every fourth float4 (16 logits) to ck[0], ck[1], ...
+__device__ __forceinline__ void chain_ckpt(float &acc, const float *src, int n4, float *ck) {
+  const float4 *s4 = reinterpret_cast<const float4 *>(src);
+  const float4 z = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+  float4 b[4];
+#pragma unroll
+  for (int u = 0; u < 4; u++) b[u] = u < n4 ? s4[u] : z;
+  for (int q0 = 0; q0 < n4; q0 += 4) {
+    float4 nb[4];
+#pragma unroll
+    for (int u = 0; u < 4; u++) nb[u] = q0 + 4 + u < n4 ? s4[q0 + 4 + u] : z;
+#pragma unroll
+    for (int u = 0; u < 4; u++) {
+      if (q0 + u < n4) {
+        acc = __fadd_rn(acc, b[u].x);
+        acc = __fadd_rn(acc, b[u].y);
+        acc = __fadd_rn(acc, b[u].z);
+        acc = __fadd_rn(acc, b[u].w);
+      }
+    }
+    if (q0 + 3 < n4) ck[q0 >> 2] = acc;
+#pragma unroll
+    for (int u = 0; u < 4; u++) b[u] = nb[u];
   }
 }
 
@@ -478,11 +539,11 @@ __device__ void sample_topk_row(const SampleArgs &a, int row, unsigned char *dsm
     unsigned long long st = a.rng[row];
     if (temp1) {
       float acc = 0.0f;
-      chain_sum<true>(acc, w, partf, 1, k);
+      chain4<true>(acc, w, partf, k);
       s_pickf = __fmul_rn(__double2float_rn(rng_float64(st)), acc);
     } else {
       double acc = 0.0;
-      chain_sum<true>(acc, w, partd, 1, k);
+      chain4<true>(acc, w, partd, k);
       s_pickd = __dmul_rn(rng_float64(st), acc);
     }
     a.rng[row] = st;
@@ -497,19 +558,70 @@ __device__ void sample_topk_row(const SampleArgs &a, int row, unsigned char *dsm
   if (tid == 0) a.out[row] = sid[s_first < k ? s_first : k - 1];
 }
 
-// Full-vocabulary draw for one row (V a multiple of 16, so every 16-byte
-// group of four logits lies inside one CumulativeSum block and one round).
+// Bounded mbarrier wait that sleeps between polls: for the warps that run
+// ahead of the cumulative-sum chains, so that their polling leaves the
+// shared-memory pipe to the chains.  Gives up (error word set) after about
+// two seconds or, with bail (waits on other threads' arrivals, not on this
+// block's own copies), once another thread has set the error word.
+__device__ __forceinline__ bool wait_backoff(uint64_t *bar, uint32_t parity, int *err, bool bail) {
+  const unsigned long long t0 = ocrvl::gtimer();
+  for (long long i = 0; i < (1ll << 24); i++) {
+    uint32_t done;
+    asm volatile("{ .reg .pred p; mbarrier.try_wait.parity.shared.b64 p, [%1], %2; selp.u32 %0, 1, 0, p; }"
+                 : "=r"(done)
+                 : "r"(ocrvl::smem_u32(bar)), "r"(parity)
+                 : "memory");
+    if (done) return true;
+    __nanosleep(256);
+    if ((i & 63) == 63 && (ocrvl::gtimer() - t0 > ocrvl::kMbarWaitNs || (bail && *(volatile int *)err))) break;
+  }
+  atomicExch(err, 1);
+  return false;
+}
+
+// Full-vocabulary draw for one row (V a multiple of 16, at most
+// kFullMaxVocab).  Phases:
+//   (1) maximum (tensor.Max) and bias = -(max * inv);
+//   (2) every weight exp(x * inv + bias) to work[] (all threads), noting any
+//       weight with its sign bit set or NaN;
+//   (3) the sequential sums: warp 1 lanes 0..nb-1 run the CumulativeSum
+//       block chains and keep the running sum at the end of every 16-logit
+//       group (checkpoints, in shared memory); warp 0 lanes 0..15 run the 16
+//       lane sums of expScaledVecFMA.  The weights reach shared memory by
+//       bulk copies (cp.async.bulk) into a ring of kFullStages rounds that
+//       warp 2 lane 0 refills as the consumers release stages.
+//   (4) the pick and pickCumulativeFloat32: with no negative or NaN weight
+//       the cumulative sums never decrease, so the binary search's answer is
+//       the first index whose sum reaches the pick: the first group whose end
+//       does, then one group re-summed from its checkpoint.  Otherwise the
+//       binary search itself runs, each probe re-summed from a checkpoint.
 __device__ void sample_full_row(const SampleArgs &a, int row, unsigned char *dsm) {
   __shared__ float red[32];
   __shared__ float s_bs[4];
   __shared__ float s_sum, s_pick;
-  __shared__ int s_first, s_lastfalse;
+  __shared__ int s_neg, s_err, s_first;
   const float *x = a.logits + (long long)row * a.ld;
-  float *cdf = a.work + (long long)row * a.ld;
+  float *wk = a.work + (long long)row * a.ld;
   const int V = a.V, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int nwarps = blockDim.x >> 5;
+  const int nb = V < 4096 ? 1 : 4;
+  const int bs = V < 4096 ? V : V / 4;
+  const int ngrp = (bs + 15) / 16;  // checkpoint groups a block
+  float *ring = (float *)dsm;
+  float *ck = ring + (size_t)kFullStages * kFullStage;
+  uint64_t *full = (uint64_t *)(ck + sample_full_ckpts(V));
+  uint64_t *empty = full + kFullStages;
 
-  // (1) maximum (tensor.Max), bias = -(max * inv)
+  // (1)
+  if (tid == 0) {
+    s_neg = 0;
+    s_err = 0;
+    for (int st = 0; st < kFullStages; st++) {
+      ocrvl::mbar_init(&full[st], 1);
+      ocrvl::mbar_init(&empty[st], 2);
+    }
+    ocrvl::mbar_fence_init();
+  }
   float m = -INFINITY;
   for_each_logit(x, V, [&](int, float v) { m = fmaxf(m, v); });
   for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
@@ -525,85 +637,79 @@ __device__ void sample_full_row(const SampleArgs &a, int row, unsigned char *dsm
   const float bias = -__fmul_rn(red[0], inv);
   auto weight = [&](float v) { return exp_fma(__fadd_rn(__fmul_rn(v, inv), bias)); };
 
-  // (2) weights staged through shared memory, two buffers a round: 4 block
-  //     sub-tiles of kFullTile for the CumulativeSum chains (warp 1, lanes
-  //     0..nb-1, which leave the running sums in place) and a slab of
-  //     kFullLaneSlab for the 16 lane sums of expScaledVecFMA (warp 0, lanes
-  //     0..15).  Warps 2.. load and weigh the next round, and copy the
-  //     round before this one's running sums out to cdf, while warps 0-1
-  //     consume this round.  Work items are groups of four floats: items
-  //     [0, kFullTile) are the chain sub-tiles, [kFullTile, 2 kFullTile)
-  //     the lane slab.
-  const int nb = V < 4096 ? 1 : 4;
-  const int bs = V < 4096 ? V : V / 4;
+  // (2) V % 16 == 0 and 16-byte aligned rows: whole float4 groups
+  {
+    bool neg = false;
+    const float4 *x4 = reinterpret_cast<const float4 *>(x);
+    float4 *w4 = reinterpret_cast<float4 *>(wk);
+    for (int q = tid; q < V / 4; q += blockDim.x) {
+      const float4 v = __ldg(x4 + q);
+      const float4 w = make_float4(weight(v.x), weight(v.y), weight(v.z), weight(v.w));
+      neg |= (__float_as_uint(w.x) | __float_as_uint(w.y) | __float_as_uint(w.z) | __float_as_uint(w.w)) >> 31;
+      neg |= isnan(w.x) || isnan(w.y) || isnan(w.z) || isnan(w.w);
+      w4[q] = w;
+    }
+    if (__any_sync(0xffffffffu, neg) && lane == 0) s_neg = 1;
+    // the bulk copies (async proxy) read what these stores wrote
+    asm volatile("fence.proxy.async.global;" ::: "memory");
+  }
+  __syncthreads();
+
+  // (3)
   const int rounds = (bs + kFullTile - 1) / kFullTile;
   const int lrounds = (V + kFullLaneSlab - 1) / kFullLaneSlab;
   const int R = rounds > lrounds ? rounds : lrounds;
-  float *buf = (float *)dsm;
-  const int bufsz = 4 * (kFullTile + 1) + kFullLaneSlab;
-  constexpr int kItems = 2 * kFullTile;  // groups of four floats a round
-  const int pt = tid - 64, np = (int)blockDim.x - 64;
-  // first logit of item q in round r (and its slot in a buffer), or -1
-  auto item = [&](int q, int r, int *slot) {
-    if (q < kFullTile) {
-      const int b = q / (kFullTile / 4), j = 4 * (q % (kFullTile / 4));
-      *slot = b * (kFullTile + 1) + j;
-      const int i = b * bs + r * kFullTile + j;
-      return (b < nb && r * kFullTile + j < bs && i < V) ? i : -1;
+  float acc = 0.0f;
+  if (warp == 2 && lane == 0) {
+    for (int r = 0; r < R; r++) {
+      const int st = r % kFullStages;
+      if (r >= kFullStages && !wait_backoff(&empty[st], (r / kFullStages - 1) & 1, &s_err, true)) break;
+      float *dst = ring + (size_t)st * kFullStage;
+      const int cl = max(0, min(kFullTile, bs - r * kFullTile));
+      const int ll = max(0, min(kFullLaneSlab, V - r * kFullLaneSlab));
+      ocrvl::mbar_expect_tx(&full[st], (uint32_t)(4 * (nb * cl + ll)));
+      if (cl > 0)
+        for (int b = 0; b < nb; b++)
+          ocrvl::bulk_g2s(dst + b * kFullTileStride, wk + (size_t)b * bs + (size_t)r * kFullTile, 4u * cl, &full[st]);
+      if (ll > 0) ocrvl::bulk_g2s(dst + 4 * kFullTileStride, wk + (size_t)r * kFullLaneSlab, 4u * ll, &full[st]);
     }
-    const int e = 4 * (q - kFullTile);
-    *slot = 4 * (kFullTile + 1) + e;
-    const int i = r * kFullLaneSlab + e;
-    return i < V ? i : -1;
-  };
-  auto flush = [&](int r, const float *src, int t0, int nt) {
-    for (int q = t0; q < kFullTile; q += nt) {
-      int slot;
-      const int i = item(q, r, &slot);
-      if (i >= 0) *(float4 *)(cdf + i) = make_float4(src[slot], src[slot + 1], src[slot + 2], src[slot + 3]);
-    }
-  };
-  constexpr int kPer = (kItems + 959) / 960;  // items a producer thread takes (960 producers)
-  auto produce = [&](int r, float *dst) {
-    float4 v[kPer];
-    int at[kPer], slot[kPer];
+  } else if (warp == 0 && lane < 16) {
+    for (int r = 0; r < R; r++) {
+      const int st = r % kFullStages;
+      if (!wait_backoff(&full[st], (r / kFullStages) & 1, &s_err, false)) break;
+      const float *src = ring + (size_t)st * kFullStage + 4 * kFullTileStride + lane;
+      const int n = max(0, min(kFullLaneSlab, V - r * kFullLaneSlab)) / 16;  // this lane's terms
+      float nxt[8];
 #pragma unroll
-    for (int u = 0; u < kPer; u++) {  // loads first, so that they are all in flight
-      const int q = pt + u * np;
-      at[u] = q < kItems ? item(q, r, &slot[u]) : -1;
-      if (at[u] >= 0) v[u] = __ldg((const float4 *)(x + at[u]));
-    }
-    if (r >= 2) flush(r - 2, dst, pt, np);
+      for (int u = 0; u < 8; u++) nxt[u] = u < n ? src[16 * u] : 0.0f;
+      for (int t0 = 0; t0 < n; t0 += 8) {
+        float cur[8];
 #pragma unroll
-    for (int u = 0; u < kPer; u++)
-      if (at[u] >= 0) {
-        float *d = dst + slot[u];
-        d[0] = weight(v[u].x);
-        d[1] = weight(v[u].y);
-        d[2] = weight(v[u].z);
-        d[3] = weight(v[u].w);
+        for (int u = 0; u < 8; u++) cur[u] = nxt[u];
+#pragma unroll
+        for (int u = 0; u < 8; u++) nxt[u] = t0 + 8 + u < n ? src[16 * (t0 + 8 + u)] : 0.0f;
+#pragma unroll
+        for (int u = 0; u < 8; u++)
+          if (t0 + u < n) acc = __fadd_rn(acc, cur[u]);
       }
-  };
-  if (warp >= 2) produce(0, buf);
-  __syncthreads();
-  float acc = 0.0f;  // warp 0: lane sum; warp 1: block chain
-  for (int r = 0; r < R; r++) {
-    float *cur = buf + (r & 1) * bufsz;
-    if (warp >= 2) {
-      if (r + 1 < R) produce(r + 1, buf + ((r + 1) & 1) * bufsz);
-      else if (r >= 1) flush(r - 1, buf + ((r + 1) & 1) * bufsz, pt, np);
-    } else if (warp == 0) {
-      if (lane < 16) {
-        const int n = max(0, min(kFullLaneSlab, V - r * kFullLaneSlab)) / 16;  // this lane's terms
-        chain_sum<false>(acc, cur + 4 * (kFullTile + 1) + lane, (float *)nullptr, 16, n);
-      }
-    } else if (lane < nb) {
-      float *src = cur + lane * (kFullTile + 1);
-      chain_sum<true>(acc, src, src, 1, max(0, min(kFullTile, bs - r * kFullTile)));
+      __syncwarp(0xffffu);
+      if (lane == 0) asm volatile("mbarrier.arrive.shared.b64 _, [%0];" ::"r"(ocrvl::smem_u32(&empty[st])) : "memory");
     }
-    __syncthreads();
+  } else if (warp == 1 && lane < nb) {
+    const unsigned cmask = (1u << nb) - 1u;
+    float *ckb = ck + lane * ngrp;
+    for (int r = 0; r < R; r++) {
+      const int st = r % kFullStages;
+      if (!ocrvl::mbar_wait(&full[st], (r / kFullStages) & 1, &s_err)) break;
+      const float4 *s4 = reinterpret_cast<const float4 *>(ring + (size_t)st * kFullStage + lane * kFullTileStride);
+      const int n4 = max(0, min(kFullTile, bs - r * kFullTile)) / 4;
+      // the running sum after every 16 logits, and at the block's end
+      chain_ckpt(acc, reinterpret_cast<const float *>(s4), n4, ckb + r * (kFullTile / 16));
+      if (r * kFullTile + 4 * n4 == bs && (bs & 15)) ckb[(bs - 1) >> 4] = acc;
+      __syncwarp(cmask);
+      if (lane == 0) asm volatile("mbarrier.arrive.shared.b64 _, [%0];" ::"r"(ocrvl::smem_u32(&empty[st])) : "memory");
+    }
   }
-  flush(R - 1, buf + ((R - 1) & 1) * bufsz, tid, blockDim.x);
   if (warp == 0) {  // tree16 of the 16 lane sums
     float v = acc;
     v = __fadd_rn(v, __shfl_down_sync(0xffffffffu, v, 8));
@@ -615,51 +721,60 @@ __device__ void sample_full_row(const SampleArgs &a, int row, unsigned char *dsm
     s_bs[lane] = lane < nb ? acc : 0.0f;
   }
   __syncthreads();
-  // (3) block offsets (cumsum.go:46-57), the pick, pickCumulativeFloat32
+  if (s_err) {
+    if (tid == 0) a.out[row] = -1;
+    return;
+  }
+
+  // (4) block offsets (cumsum.go:46-57), the pick, pickCumulativeFloat32
   const float off1 = s_bs[0];
   const float off2 = __fadd_rn(off1, s_bs[1]);
   const float off3 = __fadd_rn(off2, s_bs[2]);
+  auto with_off = [&](int b, float c) { return b == 0 ? c : __fadd_rn(c, b == 1 ? off1 : b == 2 ? off2 : off3); };
+  // block-local running sum at j, re-summed from the checkpoint before it
+  auto cs_at = [&](int b, int j) {
+    const int g = j >> 4;
+    float c = g == 0 ? 0.0f : ck[b * ngrp + g - 1];
+    for (int e = g * 16; e <= j; e++) c = __fadd_rn(c, __ldcg(wk + (size_t)b * bs + e));
+    return c;
+  };
   if (tid == 0) {
-    unsigned long long st = a.rng[row];
-    s_pick = __fmul_rn(__double2float_rn(rng_float64(st)), s_sum);
-    a.rng[row] = st;
-    s_first = V;
-    s_lastfalse = -1;
+    unsigned long long stt = a.rng[row];
+    s_pick = __fmul_rn(__double2float_rn(rng_float64(stt)), s_sum);
+    a.rng[row] = stt;
+    s_first = nb * ngrp;
   }
   __syncthreads();
   const float pick = s_pick;
-  auto cdf_of = [&](int i, float c) {
-    const int b = nb == 1 ? 0 : i / bs;
-    return b == 0 ? c : __fadd_rn(c, b == 1 ? off1 : b == 2 ? off2 : off3);
-  };
-  int first = V, lastfalse = -1;
-  for_each_logit<false>(cdf, V, [&](int i, float c) {
-    if (pick <= cdf_of(i, c)) first = min(first, i);
-    else lastfalse = max(lastfalse, i);
-  });
-  for (int o = 16; o; o >>= 1) {
-    first = min(first, __shfl_xor_sync(0xffffffffu, first, o));
-    lastfalse = max(lastfalse, __shfl_xor_sync(0xffffffffu, lastfalse, o));
-  }
-  if (lane == 0) {
-    atomicMin(&s_first, first);
-    atomicMax(&s_lastfalse, lastfalse);
-  }
-  __syncthreads();
-  if (tid == 0) {
-    int res;
-    if (s_lastfalse < s_first) {
-      res = s_first;  // the predicate is monotone: the binary search's answer
-    } else {
-      int lo = 0, hi = V;
-      while (lo < hi) {
-        const int mid = (int)((unsigned)(lo + hi) >> 1);
-        if (pick <= cdf_of(mid, __ldcg(cdf + mid))) hi = mid;
-        else lo = mid + 1;
+  if (!s_neg) {
+    for (int G = tid; G < nb * ngrp; G += blockDim.x)
+      if (pick <= with_off(G / ngrp, ck[G])) atomicMin(&s_first, G);
+    __syncthreads();
+    if (tid == 0) {
+      int res = V - 1;
+      if (s_first < nb * ngrp) {
+        const int b = s_first / ngrp, g = s_first % ngrp;
+        float c = g == 0 ? 0.0f : ck[b * ngrp + g - 1];
+        const int end = min(bs, (g + 1) * 16);
+        for (int e = g * 16; e < end; e++) {
+          c = __fadd_rn(c, __ldcg(wk + (size_t)b * bs + e));
+          if (pick <= with_off(b, c)) {
+            res = b * bs + e;
+            break;
+          }
+        }
       }
-      res = lo;
+      a.out[row] = res;
     }
-    a.out[row] = res < V ? res : V - 1;
+  } else if (tid == 0) {
+    int lo = 0, hi = V;
+    while (lo < hi) {
+      const int mid = (int)((unsigned)(lo + hi) >> 1);
+      const int b = mid / bs;
+      if (pick <= with_off(b, cs_at(b, mid - b * bs))) hi = mid;
+      else lo = mid + 1;
+    }
+    a.out[row] = lo < V ? lo : V - 1;
   }
 }
 
