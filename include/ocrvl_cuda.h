@@ -160,7 +160,11 @@ int ocrvl_seq_fill_synthetic(ocrvl_seq *s, int n, uint64_t seed);
  *   pos_thw   n*3 M-RoPE positions, or NULL for (len, len, len)
  *   need_logits  0: prompt token (K/V only in the last layer), 1: full step
  *   out_ids   n greedy ids (lm_head argmax, ties -> lowest id), may be NULL
- *   out_logits  n*vocab_size f32 logits, may be NULL                      */
+ *   out_logits  n*vocab_size f32 logits, may be NULL
+ * When the step runs as several launches (Q8, or more than 8 sequences
+ * without the batched kernel) and a later launch fails (timeout or CUDA
+ * error), the sequences of the earlier launches have already taken the step:
+ * ocrvl_seq_len tells the caller which ones advanced. */
 int ocrvl_step(ocrvl_model *m, ocrvl_seq *const *seqs, int n, const int32_t *ids, const float *embeds,
                const int32_t *pos_thw, int need_logits, int32_t *out_ids, float *out_logits);
 
