@@ -61,7 +61,7 @@ def parse():
     ap.add_argument("--impl", default="cuda", choices=["cuda", "reference"])
     ap.add_argument("--quant", default="q4", choices=["q4", "q6", "q8"])
     ap.add_argument("--prompt", type=int, default=PROMPT)
-    ap.add_argument("--workload", default="all", choices=["all", "configs1", "configs0", "configs3", "configs4", "gemv"],
+    ap.add_argument("--workload", default="all", choices=["all", "configs1", "configs0", "configs3", "configs4", "gemv", "sample"],
                     help="all: configs1 headline plus the other configurations' keys; otherwise one of them alone")
     ap.add_argument("--ctx-hi", type=int, default=4096, help="configs3: contexts U[256, ctx_hi] (profiling: smaller)")
     ap.add_argument("--requests", type=int, default=512, help="configs4: requests over all GPUs")
@@ -445,6 +445,51 @@ def gemv_workload(reps=20):
     return res
 
 
+def sample_workload(reps=20):
+    """The device sampler (ocrvl_op_sample, k_sample) on rows of vocab
+    103,424 logits (randn * 2): top-k 50 at temperature 0.8 and the full
+    vocabulary at temperature 1.0, for 1 and 64 rows, device-timed over
+    `reps` calls after 3 warm-up calls (the rows stay in L2: the sampler
+    reads each row once or twice and is bound by its sequential sums and one
+    SM's issue rate, not by HBM)."""
+    import ctypes as C
+
+    import torch
+
+    from rapidocrvl_b200 import _lib
+
+    L = _lib.load()
+    V = 103424
+    stream = torch.cuda.current_stream()
+    sh = C.c_void_p(stream.cuda_stream)
+    ptr = lambda t: C.c_void_p(t.data_ptr())  # noqa: E731
+    g = torch.Generator(device="cuda").manual_seed(11)
+    res = {}
+    for m in (1, 64):
+        x = torch.randn(m, V, device="cuda", generator=g) * 2
+        st = torch.arange(m, dtype=torch.int64, device="cuda")
+        out = torch.empty(m, dtype=torch.int32, device="cuda")
+        work = torch.empty(m, V, device="cuda")
+        for name, temp, k in (("top_k50", 0.8, 50), ("full_vocab", 1.0, 0)):
+            wk = ptr(work) if k == 0 else None
+
+            def call():
+                _lib.check(L.ocrvl_op_sample(m, V, ptr(x), temp, k, ptr(st), ptr(out), None, None, wk, sh))
+
+            for _ in range(3):
+                call()
+            ev0, ev1 = events()
+            torch.cuda.synchronize()
+            ev0.record(stream)
+            for _ in range(reps):
+                call()
+            ev1.record(stream)
+            torch.cuda.synchronize()
+            res[f"{name}_rows{m}_us"] = ev0.elapsed_time(ev1) * 1e3 / reps
+    res["shape"] = f"vocab {V}, randn*2 logits, {reps} calls per case"
+    return res
+
+
 def sweep_workload(n_requests, rank, world, device, new_tokens=256, max_live=64):
     """configs4: Q8, n_requests requests (prompts U[1024, 8192], seed 3),
     new_tokens greedy tokens each, partitioned over the ranks by predicted KV
@@ -587,6 +632,8 @@ def run_cuda(args):
             "gpu_launches": steps3}
     if world == 1 and want in ("all", "gemv"):
         extra["gemv"] = gemv_workload()
+    if world == 1 and want in ("all", "sample"):
+        extra["sample"] = sample_workload(reps=max(1, args.steps) if want == "sample" else 20)
     if want in ("all", "configs4"):
         if pg:
             pg.barrier()
@@ -613,6 +660,13 @@ def run_cuda(args):
                 "steps": 20, "warmup": 3, "ms_per_step": obj["q4"]["us_per_call"] / 1e3, "higher_is_better": True,
                 "scaling": "weak", "vs_baseline": None, "dtype": "i8/f32", "data": "synthetic random weights",
                 "config": {"workload": "quant-GEMV (k_gemv) Q4, " + obj["shape"]}, "gemv": obj}
+    elif line is None and want == "sample":
+        obj = extra["sample"]
+        line = {"metric": "device sampler time per call (vocab 103424, top-k 50, one row)",
+                "value": obj["top_k50_rows1_us"], "unit": "us", "n_gpus": world, "steps": max(1, args.steps),
+                "warmup": 3, "ms_per_step": obj["top_k50_rows1_us"] / 1e3, "higher_is_better": False,
+                "scaling": "weak", "vs_baseline": None, "dtype": "f32/f64", "data": "synthetic logits",
+                "config": {"workload": "k_sample, " + obj["shape"]}, "sample": obj}
     elif line is None:
         # a single non-headline workload: its object is the line
         (name, obj), = extra.items()
