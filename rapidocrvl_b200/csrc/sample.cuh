@@ -469,30 +469,47 @@ __device__ __forceinline__ void chain4(T &acc, const float *src, T *dst, int n) 
   }
 }
 
-// chain4<false> over n4 float4 of src, also storing the running sum after
-// every fourth float4 (16 logits) to ck[0], ck[1], ...
+// acc += the 4 * n4 floats of src in order, storing the running sum after
+// every 16 (each whole group of four float4) to ck[0], ck[1], ...  The main
+// loop has no per-element guards: the next group's loads are issued, then
+// this group's 16 dependent adds run.
 __device__ __forceinline__ void chain_ckpt(float &acc, const float *src, int n4, float *ck) {
   const float4 *s4 = reinterpret_cast<const float4 *>(src);
-  const float4 z = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-  float4 b[4];
-#pragma unroll
-  for (int u = 0; u < 4; u++) b[u] = u < n4 ? s4[u] : z;
-  for (int q0 = 0; q0 < n4; q0 += 4) {
-    float4 nb[4];
-#pragma unroll
-    for (int u = 0; u < 4; u++) nb[u] = q0 + 4 + u < n4 ? s4[q0 + 4 + u] : z;
-#pragma unroll
-    for (int u = 0; u < 4; u++) {
-      if (q0 + u < n4) {
-        acc = __fadd_rn(acc, b[u].x);
-        acc = __fadd_rn(acc, b[u].y);
-        acc = __fadd_rn(acc, b[u].z);
-        acc = __fadd_rn(acc, b[u].w);
-      }
+  const int nf = n4 & ~3;  // float4 in whole groups
+  float4 b0, b1, b2, b3;
+  if (nf > 0) {
+    b0 = s4[0];
+    b1 = s4[1];
+    b2 = s4[2];
+    b3 = s4[3];
+  }
+  for (int q0 = 0; q0 < nf; q0 += 4) {
+    float4 n0, n1, n2, n3;
+    const bool more = q0 + 4 < nf;
+    if (more) {
+      n0 = s4[q0 + 4];
+      n1 = s4[q0 + 5];
+      n2 = s4[q0 + 6];
+      n3 = s4[q0 + 7];
     }
-    if (q0 + 3 < n4) ck[q0 >> 2] = acc;
-#pragma unroll
-    for (int u = 0; u < 4; u++) b[u] = nb[u];
+    acc = __fadd_rn(acc, b0.x); acc = __fadd_rn(acc, b0.y); acc = __fadd_rn(acc, b0.z); acc = __fadd_rn(acc, b0.w);
+    acc = __fadd_rn(acc, b1.x); acc = __fadd_rn(acc, b1.y); acc = __fadd_rn(acc, b1.z); acc = __fadd_rn(acc, b1.w);
+    acc = __fadd_rn(acc, b2.x); acc = __fadd_rn(acc, b2.y); acc = __fadd_rn(acc, b2.z); acc = __fadd_rn(acc, b2.w);
+    acc = __fadd_rn(acc, b3.x); acc = __fadd_rn(acc, b3.y); acc = __fadd_rn(acc, b3.z); acc = __fadd_rn(acc, b3.w);
+    ck[q0 >> 2] = acc;
+    if (more) {
+      b0 = n0;
+      b1 = n1;
+      b2 = n2;
+      b3 = n3;
+    }
+  }
+  for (int q = nf; q < n4; q++) {  // a partial last group (its end is the block's, stored by the caller)
+    const float4 v = s4[q];
+    acc = __fadd_rn(acc, v.x);
+    acc = __fadd_rn(acc, v.y);
+    acc = __fadd_rn(acc, v.z);
+    acc = __fadd_rn(acc, v.w);
   }
 }
 
