@@ -153,9 +153,10 @@ def test_full_vocabulary_generation_needs_whole_blocks():
         rt.generate_with_options([5, 6], GenerateOptions(max_new_tokens=3, temperature=1.0, top_k=0))
 
 
-@pytest.mark.parametrize("q,n", [("q8", 3), ("q4", 10)])
+@pytest.mark.parametrize("q,n", [("q8", 3), ("q4", 10), ("q8", 10)])
 def test_step_sample_batch_matches_oracle(q, n):
-    """n sequences, each with its own RNG; n > 8 crosses the batched step."""
+    """n sequences, each with its own RNG; n > 8 is one batched launch for
+    Q4 and two launches (8 + 2, each drawing with its own RNG states) for Q8."""
     _torch()
     cfg, rt, orc = _pair("tiny", q)
     seqs = [rt.new_sequence(64) for _ in range(n)]
