@@ -18,6 +18,10 @@ Files
                       positions, RMSNorm
   tiny_greedy.json    greedy ids of the seeded tiny decoders (q8/q6/q4) and
                       the sha256 of each GGUF file the ids came from
+  sampling.npz        logits rows with, per (temperature, top_k), the sampled
+                      id and the advanced fastRNG state of each row's seed
+                      (top-k candidates, full vocabulary in one and in four
+                      cumulative-sum blocks, argmax)
 """
 from __future__ import annotations
 
@@ -142,6 +146,33 @@ def misc_fixture() -> dict:
     return f
 
 
+# (temperature, top_k) cases of the sampling fixture; top_k 0 = full vocabulary
+SAMPLE_CASES = [(0.0, 0), (0.8, 1), (1.0, 2), (0.7, 3), (1.0, 4), (1.3, 5), (1.0, 40), (0.6, 200), (1.0, 0), (0.5, 0),
+                (1.7, 0)]
+
+
+def sampling_fixture() -> dict:
+    rng = np.random.default_rng(33)
+    f = {"cases": np.array(SAMPLE_CASES, np.float64)}
+    for V in (2048, 4160):
+        x = _f32(rng, (6, V), 2.0)
+        x[1] = np.round(x[1] * 2) / 2  # ties
+        x[2, : V // 2] = -30.0
+        seeds = rng.integers(-(1 << 62), 1 << 62, 6, dtype=np.int64)
+        f[f"logits_{V}"] = x
+        f[f"seeds_{V}"] = seeds
+        ids = np.zeros((len(SAMPLE_CASES), 6), np.int32)
+        states = np.zeros((len(SAMPLE_CASES), 6), np.uint64)
+        for c, (t, k) in enumerate(SAMPLE_CASES):
+            for r in range(6):
+                st = pyoracle.RNG(int(seeds[r]))
+                ids[c, r] = pyoracle.sample_token(x[r], t, k, st)
+                states[c, r] = st.state
+        f[f"ids_{V}"] = ids
+        f[f"states_{V}"] = states
+    return f
+
+
 def file_sha256(path: str) -> str:
     h = hashlib.sha256()
     with open(path, "rb") as fh:
@@ -170,6 +201,7 @@ def main():
     for q in QTYPES:
         np.savez_compressed(os.path.join(HERE, f"ops_{q}.npz"), **ops_fixture(q))
     np.savez_compressed(os.path.join(HERE, "misc.npz"), **misc_fixture())
+    np.savez_compressed(os.path.join(HERE, "sampling.npz"), **sampling_fixture())
     with open(os.path.join(HERE, "tiny_greedy.json"), "w") as fh:
         json.dump(greedy_fixture(), fh)
         fh.write("\n")

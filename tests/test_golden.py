@@ -101,3 +101,14 @@ def test_tiny_greedy_fixture(tiny_models):
         ids = om.generate(g["prompt"], g["max_new"], eos=[])
         om.close()
         assert ids == g["models"][q]["ids"]
+
+
+def test_sampling_fixture():
+    f = _load("sampling.npz")
+    for V in (2048, 4160):
+        x, seeds = f[f"logits_{V}"], f[f"seeds_{V}"]
+        for c, (t, k) in enumerate(f["cases"]):
+            for r in range(x.shape[0]):
+                st = pyoracle.RNG(int(seeds[r]))
+                assert pyoracle.sample_token(x[r], float(t), int(k), st) == f[f"ids_{V}"][c, r], (V, t, k, r)
+                assert st.state == int(f[f"states_{V}"][c, r])

@@ -168,3 +168,24 @@ def test_image_embeds_generation_matches_oracle(tiny_models, q):
         rt.generate_with_image_embeds([5, 999, 999, 6], emb[:3], [1, 4, 4], GenerateOptions(max_new_tokens=2))
     orc.close()
     rt.close()
+
+
+def test_sampling_fixture_on_device():
+    """ocrvl_op_sample on the fixture's logits rows: the oracle's ids and RNG
+    states for every (temperature, top_k) case."""
+    torch = _torch()
+    L = _lib.load()
+    f = np.load(os.path.join(GOLDEN, "sampling.npz"))
+    for V in (2048, 4160):
+        x = torch.from_numpy(np.ascontiguousarray(f[f"logits_{V}"])).cuda()
+        m = x.shape[0]
+        work = torch.zeros((m, V), dtype=torch.float32, device="cuda")
+        for c, (t, k) in enumerate(f["cases"]):
+            st = torch.from_numpy(f[f"seeds_{V}"].copy()).cuda()
+            out = torch.full((m,), -1, dtype=torch.int32, device="cuda")
+            full = t > 0 and k != 1 and not (1 < k < V)
+            _lib.check(L.ocrvl_op_sample(m, V, _p(x), float(t), int(k), _p(st), _p(out), None, None,
+                                         _p(work) if full else None, None))
+            torch.cuda.synchronize()
+            assert out.cpu().numpy().tolist() == f[f"ids_{V}"][c].tolist(), (V, t, k)
+            assert st.cpu().numpy().view(np.uint64).tolist() == f[f"states_{V}"][c].tolist(), (V, t, k)
