@@ -656,6 +656,18 @@ int sample_candidates(const int *ids, const float *s, int k, double temp, uint64
   return ids[k - 1];
 }
 
+// pickCumulativeFloat32 (model.go:2326-2340): binary search for the first
+// cdf entry >= pick; -1 past the end.
+int pick_cumulative(const float *cdf, int n, float pick) {
+  int lo = 0, hi = n;
+  while (lo < hi) {
+    int mid = (int)((unsigned)(lo + hi) >> 1);
+    if (pick <= cdf[mid]) hi = mid;
+    else lo = mid + 1;
+  }
+  return lo < n ? lo : -1;
+}
+
 // sampleFullLogitsScratch / sampleFullLogitsTemp1Scratch with a weight
 // scratch (model.go:2215-2307): weights = ExpScaledVec(logits, 1/temp,
 // -max*inv) (expScaledVecFMA: x*scale, + bias, vector exp; 16 lane sums,
@@ -699,13 +711,8 @@ int sample_full(const float *logits, int n, float temp, uint64_t &rng) {
     }
   }
   float pick = (float)rng_float64(rng) * sum;
-  int lo = 0, hi = n;
-  while (lo < hi) {
-    int mid = (int)((unsigned)(lo + hi) >> 1);
-    if (pick <= w[mid]) hi = mid;
-    else lo = mid + 1;
-  }
-  return lo < n ? lo : n - 1;
+  int idx = pick_cumulative(w.data(), n, pick);
+  return idx >= 0 ? idx : n - 1;
 }
 
 // First index of the maximum (the greedy path's tie rule).
@@ -1288,6 +1295,7 @@ void orc_topk_select(const float *logits, int n, int k, int *ids, float *scores)
 int orc_sample_candidates(const int *ids, const float *scores, int k, double temperature, uint64_t *state) {
   return sample_candidates(ids, scores, k, temperature, *state);
 }
+int orc_pick_cumulative(const float *cdf, int n, float pick) { return pick_cumulative(cdf, n, pick); }
 int orc_sample_full(const float *logits, int n, float temperature, uint64_t *state) {
   return sample_full(logits, n, temperature, *state);
 }

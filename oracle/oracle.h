@@ -123,6 +123,9 @@ double orc_rng_float64(uint64_t *state);
 void orc_topk_select(const float *logits, int n, int k, int *ids, float *scores);
 /* sampleCandidateScoresScratch (model.go:1929-1976) on k candidates. */
 int orc_sample_candidates(const int *ids, const float *scores, int k, double temperature, uint64_t *state);
+/* pickCumulativeFloat32 (model.go:2326-2340): first index with pick <=
+ * cdf[i] by binary search, or -1. */
+int orc_pick_cumulative(const float *cdf, int n, float pick);
 /* sampleFullLogitsScratch with a weight scratch (model.go:2215-2307);
  * -2 unless n is a multiple of 16 (>= 16). */
 int orc_sample_full(const float *logits, int n, float temperature, uint64_t *state);

@@ -90,6 +90,7 @@ def lib():
         L.orc_topk_select.argtypes = [P, I, I, P, P]
         L.orc_sample_candidates.argtypes = [P, P, I, D, U64P]
         L.orc_sample_full.argtypes = [P, I, F, U64P]
+        L.orc_pick_cumulative.argtypes = [P, I, F]
         L.orc_sample_token.argtypes = [P, I, D, I, U64P]
         L.orc_generate_sampled.argtypes = [P, P, I, I, P, I, D, I, C.c_int64, P, I]
         _lib = L
@@ -135,6 +136,12 @@ def sample_candidates(ids, scores, temperature, rng: RNG) -> int:
     i = np.ascontiguousarray(ids, np.int32)
     s = np.ascontiguousarray(scores, np.float32)
     return int(lib().orc_sample_candidates(ptr(i), ptr(s), len(i), float(temperature), C.byref(rng._s)))
+
+
+def pick_cumulative(cdf, pick) -> int:
+    """pickCumulativeFloat32: first index with pick <= cdf[i], or -1."""
+    c = np.ascontiguousarray(cdf, np.float32)
+    return int(lib().orc_pick_cumulative(ptr(c), len(c), float(pick)))
 
 
 def sample_full(logits, temperature, rng: RNG) -> int:

@@ -59,6 +59,14 @@ def test_topk_sorts_all_and_breaks_ties_by_id():
     assert ids.tolist() == [1, 2, 5, 0, 3, 4]
 
 
+def test_pick_cumulative_float32():
+    # TestPickCumulativeFloat32
+    cdf = [0.25, 0.75, 1.0]
+    for pick, want in ((0.01, 0), (0.25, 0), (0.26, 1), (0.75, 1), (0.90, 2)):
+        assert pyoracle.pick_cumulative(cdf, pick) == want
+    assert pyoracle.pick_cumulative(cdf, 1.1) == -1
+
+
 def test_top_k_one_and_zero_temperature_use_argmax():
     # TestSampleTopKOneUsesArgmax
     r = pyoracle.RNG(1)
